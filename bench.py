@@ -1,0 +1,503 @@
+"""Benchmark of the B200 attention inference path (one JSON line on rank 0).
+
+Headline: causal self-attention prefill, per GPU batch 8 x
+seq 4096 x 16 heads x head_dim 128, bf16 in / fp32 accumulate, per-sequence
+key padding with valid lengths ~U[2048, 4096] -> TFLOP/s of useful attention
+FLOPs (4 * D * H * sum_b P_b, P_b = L(L+1)/2 + (S - L) * L). Weak scaling:
+every rank runs its own batch of 8 sequences (partitioned by batch x head, no
+collective); value = all ranks' FLOPs / max-over-ranks device time.
+
+Also measured in the same run (sub-objects of the line):
+  decode_cfg3  -- KV-cache decode B64 H32 D128 ctx 8192, 128 steps with a
+                  K3 append each step (HBM GB/s, tokens/s), batch rows split
+                  across ranks.
+  longctx_cfg5 -- split-KV decode B4 H32 D128 over a 262144-token cache
+                  sharded by sequence across ranks; per-GPU (out, LSE)
+                  partials all-gathered over NCCL and LSE-merged.
+
+Run: python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+Multi-GPU: torchrun --nproc-per-node N bench.py --gpus N ...
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import platform
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "attn prefill TFLOP/s (causal, key-padded, bf16)"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+CFG2 = dict(B=8, S=4096, H=16, D=128, lo=2048, hi=4096)
+CFG3 = dict(B=64, H=32, D=128, ctx=8192, steps=128)
+CFG5 = dict(B=4, H=32, D=128, ctx=262144, steps=16)
+
+
+def load_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def cfg2_lengths(rank: int):
+    import numpy as np
+    return np.random.RandomState(2 + rank).randint(CFG2["lo"], CFG2["hi"] + 1, size=CFG2["B"])
+
+
+def cfg2_flops(lengths) -> float:
+    S, H, D = CFG2["S"], CFG2["H"], CFG2["D"]
+    pairs = sum(L * (L + 1) / 2 + (S - L) * L for L in (int(x) for x in lengths))
+    return 4.0 * D * H * pairs
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples taken while the timed
+    region runs (20 ms period)."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.samples = []
+        self.proc = None
+        self.windows = []
+        self._thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "20", "-i", str(self.device_index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+            return
+        self._thread = threading.Thread(target=self._read, daemon=True)
+        self._thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append((time.time(), line.strip()))
+
+    def mark(self, t0, t1):
+        self.windows.append((t0, t1))
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self._thread is not None:
+            self._thread.join(timeout=2)
+
+    def summary(self):
+        def parse(line):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                return None
+            try:
+                return dict(sm=float(parts[1]), smax=float(parts[2]),
+                            hw=parts[5], hwt=parts[6], swt=parts[7], pcap=parts[8])
+            except ValueError:
+                return None
+        inside = [parse(l) for t, l in self.samples
+                  if any(a - 0.05 <= t <= b + 0.05 for a, b in self.windows)]
+        inside = [s for s in inside if s]
+        if not inside:
+            inside = [s for s in (parse(l) for _, l in self.samples) if s]
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        reasons = set()
+        for s in inside:
+            for key, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"),
+                              ("swt", "sw_thermal_slowdown"), ("pcap", "sw_power_cap")):
+                if s[key].lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(s["sm"] for s in inside),
+                "sm_max_mhz": max(s["smax"] for s in inside),
+                "reasons": sorted(reasons), "samples": len(inside)}
+
+
+# ------------------------------------------------------------ dist helpers
+class Dist:
+    def __init__(self, n_gpus: int):
+        import torch
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        if self.world != n_gpus:
+            raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={self.world}")
+        torch.cuda.set_device(self.local_rank)
+        self.device = torch.device("cuda", self.local_rank)
+        self.pg = None
+        if self.world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=self.device)
+            self.pg = dist
+
+    def barrier(self):
+        import torch
+        torch.cuda.synchronize()
+        if self.pg:
+            self.pg.barrier()
+        torch.cuda.synchronize()
+
+    def max(self, value: float) -> float:
+        import torch
+        if not self.pg:
+            return value
+        t = torch.tensor([value], dtype=torch.float64, device=self.device)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, value: float) -> float:
+        import torch
+        if not self.pg:
+            return value
+        t = torch.tensor([value], dtype=torch.float64, device=self.device)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.SUM)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.barrier()
+            self.pg.destroy_process_group()
+
+
+def timed(dist: Dist, clocks: ClockSampler, fn, steps: int) -> float:
+    """Run fn() `steps` times between CUDA events on the current stream,
+    bracketed by barrier + synchronize; return max-over-ranks milliseconds."""
+    import torch
+    dist.barrier()
+    t0 = time.time()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        fn()
+    end.record()
+    torch.cuda.synchronize()
+    t1 = time.time()
+    dist.barrier()
+    clocks.mark(t0, t1)
+    return dist.max(start.elapsed_time(end))
+
+
+# ------------------------------------------------------------- workloads
+def bench_prefill(dist: Dist, clocks: ClockSampler, steps: int, warmup: int):
+    import torch
+    from enilnets_b200 import kernels, _native
+    B, S, H, D = CFG2["B"], CFG2["S"], CFG2["H"], CFG2["D"]
+    g = torch.Generator(device=dist.device).manual_seed(1000 + dist.rank)
+    q, k, v = (torch.randn((B, S, H, D), generator=g, device=dist.device).to(torch.bfloat16)
+               for _ in range(3))
+    lengths = cfg2_lengths(dist.rank)
+    lens = torch.tensor(lengths, dtype=torch.int32, device=dist.device)
+    out = torch.empty((B, S, H, D), dtype=torch.bfloat16, device=dist.device)
+
+    def step():
+        kernels.attention_prefill(q, k, v, causal=True, kv_valid_len=lens,
+                                  mask_mode="additive", out=out)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    _native.raise_on_device_error()
+    ms = timed(dist, clocks, step, steps)
+    flops_rank = cfg2_flops(lengths)
+    flops_total = dist.sum(flops_rank)
+    ms_step = ms / steps
+    value = flops_total / (ms_step * 1e-3) / 1e12
+
+    # End to end: host (pinned) inputs -> H2D -> kernel -> D2H of the output,
+    # through the same public call, every step.
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    dq, dk, dv = (torch.empty_like(t) for t in (q, k, v))
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        kernels.attention_prefill(dq, dk, dv, causal=True, kv_valid_len=lens,
+                                  mask_mode="additive", out=out)
+        hout.copy_(out, non_blocking=True)
+
+    e2e_steps = max(3, min(steps, 20))
+    for _ in range(2):
+        e2e_step()
+    ms_e2e = timed(dist, clocks, e2e_step, e2e_steps) / e2e_steps
+    h2d = 3 * q.numel() * q.element_size()
+    d2h = out.numel() * out.element_size()
+    e2e = {"value": flops_total / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
+           "ms_per_step": ms_e2e, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+    return dict(value=value, ms_step=ms_step, flops_rank=flops_rank, flops_total=flops_total,
+                e2e=e2e, lengths=[int(x) for x in lengths], per_launch_ms=ms_step)
+
+
+def bench_decode_cfg3(dist: Dist, clocks: ClockSampler, warmup: int):
+    """Batch rows split across ranks (64 / N per GPU)."""
+    import torch
+    from enilnets_b200 import kernels, _native
+    Btot, H, D, ctx, T = CFG3["B"], CFG3["H"], CFG3["D"], CFG3["ctx"], CFG3["steps"]
+    if Btot % dist.world:
+        return {"skipped": f"batch {Btot} not divisible by {dist.world} ranks"}
+    B = Btot // dist.world
+    cap = ctx + T
+    g = torch.Generator(device=dist.device).manual_seed(3 + dist.rank)
+    kc = torch.empty((B, H, cap, D), dtype=torch.bfloat16, device=dist.device)
+    vc = torch.empty_like(kc)
+    kc[:, :, :ctx].normal_(generator=g)
+    vc[:, :, :ctx].normal_(generator=g)
+    qs = torch.randn((T, B, H, D), generator=g, device=dist.device).to(torch.bfloat16)
+    kn = torch.randn((T, B, 1, H, D), generator=g, device=dist.device).to(torch.bfloat16)
+    vn = torch.randn((T, B, 1, H, D), generator=g, device=dist.device).to(torch.bfloat16)
+    out = torch.empty((B, H, D), dtype=torch.bfloat16, device=dist.device)
+    state = {"t": 0}
+
+    def step():
+        t = state["t"]
+        kernels.kv_append(kc, kn[t], ctx + t)
+        kernels.kv_append(vc, vn[t], ctx + t)
+        kernels.attention_decode(qs[t], kc, vc, slot_begin=0, slot_end=ctx + t + 1,
+                                 pos_slot0=0, q_pos=ctx + t, out=out)
+        state["t"] = (t + 1) % T
+
+    for _ in range(max(warmup, 3)):
+        step()
+    state["t"] = 0
+    torch.cuda.synchronize()
+    _native.raise_on_device_error()
+    # Decode-only timing of the same kernel on a fixed context, for the roofline.
+    ms_all = timed(dist, clocks, step, T)
+    bytes_rank = 0
+    for t in range(T):
+        n = ctx + t + 1
+        bytes_rank += 2 * B * H * D * 2 * n + 2 * B * H * D * 2 + 2 * B * H * D * 2
+    bytes_total = dist.sum(bytes_rank)
+    gbs = bytes_total / (ms_all * 1e-3) / 1e9
+    state["t"] = 0
+    ms_dec = timed(dist, clocks, lambda: kernels.attention_decode(
+        qs[0], kc, vc, slot_begin=0, slot_end=ctx + 1, pos_slot0=0, q_pos=ctx, out=out), T)
+    dec_bytes = 2 * B * H * D * 2 * (ctx + 1) + 2 * B * H * D * 2
+    dec_gbs = dist.sum(dec_bytes) / (ms_dec / T * 1e-3) / 1e9
+    return {"GB_s": gbs, "tokens_s": Btot * T / (ms_all * 1e-3), "ms_per_step": ms_all / T,
+            "decode_kernel_GB_s": dec_gbs, "decode_kernel_ms": ms_dec / T,
+            "splits": kernels.decode_auto_splits(B, H, ctx + 1),
+            "config": f"B{Btot} H{H} D{D} ctx {ctx}+{T} steps, append each step, "
+                      f"{B} rows per GPU"}
+
+
+def bench_longctx_cfg5(dist: Dist, clocks: ClockSampler, warmup: int):
+    """Sequence-sharded split-KV decode with an NCCL all-gather of (out, LSE)."""
+    import torch
+    from enilnets_b200 import kernels, _native
+    B, H, D, ctx, T = CFG5["B"], CFG5["H"], CFG5["D"], CFG5["ctx"], CFG5["steps"]
+    N = dist.world
+    shard = ctx // N
+    tail = dist.rank == N - 1
+    cap = shard + (T if tail else 0)
+    g = torch.Generator(device=dist.device).manual_seed(5 + dist.rank)
+    kc = torch.empty((B, H, cap, D), dtype=torch.bfloat16, device=dist.device)
+    vc = torch.empty_like(kc)
+    kc[:, :, :shard].normal_(generator=g)
+    vc[:, :, :shard].normal_(generator=g)
+    gq = torch.Generator(device=dist.device).manual_seed(55)  # same query on every rank
+    qs = torch.randn((T, B, H, D), generator=gq, device=dist.device).to(torch.bfloat16)
+    kn = torch.randn((T, B, 1, H, D), generator=gq, device=dist.device).to(torch.bfloat16)
+    vn = torch.randn((T, B, 1, H, D), generator=gq, device=dist.device).to(torch.bfloat16)
+    part = torch.empty((B, H, D + 1), dtype=torch.float32, device=dist.device)
+    gathered = torch.empty((N, B, H, D + 1), dtype=torch.float32, device=dist.device)
+    out = torch.empty((B, H, D), dtype=torch.bfloat16, device=dist.device)
+    state = {"t": 0}
+
+    def step():
+        t = state["t"]
+        pos = ctx + t
+        if tail:
+            kernels.kv_append(kc, kn[t], shard + t)
+            kernels.kv_append(vc, vn[t], shard + t)
+        n_live = shard + (t + 1 if tail else 0)
+        o_loc, lse_loc = kernels.attention_decode(
+            qs[t], kc, vc, slot_begin=0, slot_end=n_live, pos_slot0=dist.rank * shard,
+            q_pos=pos, out_dtype=torch.float32, return_lse=True)
+        if N == 1:
+            out.copy_(o_loc)
+        else:
+            part[..., :D].copy_(o_loc)
+            part[..., D].copy_(lse_loc)
+            dist.pg.all_gather_into_tensor(gathered, part)
+            kernels.lse_merge(gathered[..., :D].contiguous(), gathered[..., D].contiguous(),
+                              out=out)
+        state["t"] = (t + 1) % T
+
+    for _ in range(max(warmup, 3)):
+        step()
+    state["t"] = 0
+    torch.cuda.synchronize()
+    _native.raise_on_device_error()
+    ms = timed(dist, clocks, step, T)
+    bytes_total = sum(2 * B * H * D * 2 * (ctx + t + 1) for t in range(T))
+    return {"GB_s": bytes_total / (ms * 1e-3) / 1e9, "tokens_s": B * T / (ms * 1e-3),
+            "ms_per_step": ms / T, "shard_tokens_per_gpu": shard,
+            "collective": "none" if N == 1 else "ncclAllGather of fp32 (out, LSE) + LSE merge"}
+
+
+# ------------------------------------------------------------- CPU baseline
+def cpu_sample_tflops(heads: int = 16, repeats: int = 1):
+    """The reference's streaming softmax (oracle port of
+    nn/flash_attention.py:42-80, float64, block 512) on one full-length
+    causal sequence x `heads` heads of config 2; useful causal FLOPs / s."""
+    import numpy as np
+    from oracle.attention_ref import flash_attention_ref
+    S, D = CFG2["S"], CFG2["D"]
+    rng = np.random.RandomState(0)
+    Q, K, V = (rng.standard_normal((1, heads, S, D)) for _ in range(3))
+    times = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        flash_attention_ref(Q, K, V, 512, causal=True)
+        times.append(time.perf_counter() - t0)
+    flops = 4.0 * D * heads * S * (S + 1) / 2
+    t = statistics.mean(times)
+    return flops / t / 1e12, t, f"1 sequence x {heads} heads, S={S}, D={D}, causal, float64"
+
+
+def cpu_info():
+    model = platform.processor()
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return model, os.cpu_count()
+
+
+def run_reference(args):
+    """--impl reference: the reference algorithm (NumPy float64 port) on the
+    host cores, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    model, cores = cpu_info()
+    for _ in range(args.warmup):
+        cpu_sample_tflops(heads=2)
+    vals = []
+    t_total = 0.0
+    for _ in range(args.steps):
+        v, t, sample = cpu_sample_tflops(heads=2)
+        vals.append(v)
+        t_total += t
+    value = statistics.mean(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000 * t_total / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": "cfg2 causal prefill sample (reference flash path)",
+                       "cpu": model},
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--skip-sub", action="store_true", help="headline only")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    from enilnets_b200 import _native
+    _native.load()
+    dist = Dist(args.gpus)
+    clocks = ClockSampler(dist.local_rank)
+    clocks.start()
+    try:
+        pre = bench_prefill(dist, clocks, args.steps, args.warmup)
+        sub = {}
+        if not args.skip_sub:
+            sub["decode_cfg3"] = bench_decode_cfg3(dist, clocks, args.warmup)
+            sub["longctx_cfg5"] = bench_longctx_cfg5(dist, clocks, args.warmup)
+    finally:
+        clocks.stop()
+    peaks, peak_kind = load_peaks()
+    if dist.rank == 0:
+        achieved = pre["flops_rank"] / (pre["per_launch_ms"] * 1e-3) / 1e12
+        peak = float(peaks["bf16_tflops"])
+        roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                    "frac": achieved / peak, "traffic": None,
+                    "peak_source": f"{peak_kind} bf16 burst (MEASURED_PEAKS.json)"
+                    if peak_kind == "measured" else "fallback 1590 TFLOP/s"}
+        prof = REPO / "profiles" / "prefill_traffic.json"
+        if prof.exists():
+            roofline["traffic"] = json.loads(prof.read_text()).get("bytes_per_launch")
+        hbm = float(peaks["hbm_gbs"])
+        for key in ("decode_cfg3", "longctx_cfg5"):
+            if key in sub and "GB_s" in sub[key]:
+                per_gpu = sub[key]["GB_s"] / dist.world
+                sub[key]["frac_of_hbm_per_gpu"] = per_gpu / hbm
+        if "decode_cfg3" in sub and "decode_kernel_GB_s" in sub["decode_cfg3"]:
+            sub["decode_cfg3"]["decode_kernel_frac_of_hbm"] = \
+                sub["decode_cfg3"]["decode_kernel_GB_s"] / dist.world / hbm
+        cpu = None
+        if not args.no_cpu_baseline:
+            model, cores = cpu_info()
+            v, t, sample = cpu_sample_tflops(heads=16)
+            cpu = {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                   "sample": sample + f" ({t:.1f} s, numpy/BLAS on all host threads, {model})"}
+        line = {
+            "metric": METRIC, "value": pre["value"], "unit": "TFLOP/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": pre["ms_step"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic N(0,1) activations, seeded",
+            "config": {"workload": "cfg2 causal prefill B8/GPU S4096 H16 D128, key padding "
+                                   "L~U[2048,4096]",
+                       "global_batch": CFG2["B"] * args.gpus, "seq_len": CFG2["S"],
+                       "parallelism": f"batch x head over {args.gpus} GPU(s), no collective",
+                       "l2": "inputs 402 MB per GPU > 126 MB L2 (no flush needed)",
+                       "lengths_rank0": pre["lengths"]},
+            "e2e": pre["e2e"],
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "gpu_launches": args.steps,
+            "clocks": clocks.summary(),
+            **sub,
+        }
+        print(json.dumps(line))
+    dist.close()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,144 @@
+"""ctypes binding of libenl_b200.so (the C ABI declared in include/enl_attn.h).
+
+There is no fallback: if the library is missing or cannot be loaded, every
+entry point raises. Status codes map to the reference's error conventions:
+argument problems raise ValueError (as the reference's layer builders do,
+nn/layers.py:210-327), CUDA and device-side failures raise RuntimeError (as
+core/backend.py:106-113 does for device problems).
+"""
+from __future__ import annotations
+
+import ctypes
+from ctypes import (POINTER, Structure, c_char_p, c_float, c_int32, c_int64, c_size_t,
+                    c_void_p)
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libenl_b200.so"
+
+ENL_OK = 0
+ENL_ERR_INVALID = 1
+ENL_ERR_UNSUPPORTED = 2
+ENL_ERR_CUDA = 3
+ENL_ERR_DEVICE = 4
+
+ENL_DTYPE_BF16 = 0
+ENL_DTYPE_FP32 = 1
+
+ENL_MASK_EXCLUDE = 0
+ENL_MASK_ADDITIVE = 1
+
+DEVICE_ERRORS = {1: "an mbarrier wait exceeded its time budget",
+                 2: "an index was out of range",
+                 3: "a launch-time shape invariant was violated"}
+
+
+class PrefillArgs(Structure):
+    """Mirror of enl_prefill_args (field order and types match the header)."""
+    _fields_ = [
+        ("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("o", c_void_p),
+        ("lse", c_void_p),
+        ("batch", c_int32), ("num_heads", c_int32), ("num_kv_heads", c_int32),
+        ("seq_q", c_int32), ("seq_kv", c_int32), ("head_dim", c_int32),
+        ("q_stride_b", c_int64), ("q_stride_s", c_int64), ("q_stride_h", c_int64),
+        ("k_stride_b", c_int64), ("k_stride_s", c_int64), ("k_stride_h", c_int64),
+        ("v_stride_b", c_int64), ("v_stride_s", c_int64), ("v_stride_h", c_int64),
+        ("o_stride_b", c_int64), ("o_stride_s", c_int64), ("o_stride_h", c_int64),
+        ("in_dtype", c_int32), ("out_dtype", c_int32),
+        ("causal", c_int32), ("window", c_int32), ("mask_mode", c_int32),
+        ("kv_valid_len", c_void_p), ("alibi_slopes", c_void_p),
+        ("q_pos0", c_int64), ("k_pos0", c_int64),
+        ("scale", c_float),
+    ]
+
+
+class DecodeArgs(Structure):
+    """Mirror of enl_decode_args."""
+    _fields_ = [
+        ("q", c_void_p), ("q_stride_b", c_int64), ("q_stride_h", c_int64),
+        ("k_cache", c_void_p), ("v_cache", c_void_p),
+        ("cache_stride_b", c_int64), ("cache_stride_h", c_int64), ("cache_stride_s", c_int64),
+        ("o", c_void_p), ("o_stride_b", c_int64), ("o_stride_h", c_int64),
+        ("lse", c_void_p),
+        ("batch", c_int32), ("num_heads", c_int32), ("num_kv_heads", c_int32),
+        ("head_dim", c_int32),
+        ("slot_begin", c_int32), ("slot_end", c_int32),
+        ("pos_slot0", c_int64), ("q_pos", c_int64),
+        ("window", c_int32), ("alibi_slopes", c_void_p), ("scale", c_float),
+        ("in_dtype", c_int32), ("out_dtype", c_int32), ("n_splits", c_int32),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+    ]
+
+
+# Exported symbol -> (argtypes, restype). Kept in sync with include/enl_attn.h
+# (a CPU test checks every declared symbol is exported and bound here).
+SIGNATURES = {
+    "enl_attn_prefill": ([POINTER(PrefillArgs), c_void_p], c_int32),
+    "enl_attn_decode": ([POINTER(DecodeArgs), c_void_p], c_int32),
+    "enl_decode_auto_splits": ([c_int32, c_int32, c_int32], c_int32),
+    "enl_decode_workspace_bytes": ([c_int32, c_int32, c_int32, c_int32], c_size_t),
+    "enl_lse_merge": ([c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p,
+                       c_int64, c_int64, c_int32, c_void_p, c_void_p], c_int32),
+    "enl_kv_append": ([c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64,
+                       c_int64, c_int32, c_int32, c_int32, c_int32, c_int32, c_int64, c_int64,
+                       c_void_p], c_int32),
+    "enl_kv_gather": ([c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64,
+                       c_int64, c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32,
+                       c_int32, c_void_p], c_int32),
+    "enl_rope_apply": ([c_void_p, c_int64, c_int64, c_int64, c_int32, c_int32, c_int32,
+                        c_int32, c_int32, c_void_p, c_void_p, c_int64, c_int64, c_void_p],
+                       c_int32),
+    "enl_device_error": ([POINTER(c_int32), POINTER(c_int32), c_int32], c_int32),
+    "enl_last_error": ([], c_char_p),
+    "enl_abi_version": ([], c_int32),
+}
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the library once; raise a clear error when it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise RuntimeError(
+            f"{LIB_PATH.name} is not built (expected at {LIB_PATH}). Build it with "
+            "`python -m enilnets_b200.build`; there is no CPU fallback for the attention path.")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    for name, (argtypes, restype) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = argtypes
+        fn.restype = restype
+    _lib = lib
+    return lib
+
+
+def last_error() -> str:
+    msg = load().enl_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(status: int, what: str) -> None:
+    """Raise the reference-style exception for a non-zero ABI status."""
+    if status == ENL_OK:
+        return
+    msg = f"{what}: {last_error()}"
+    if status in (ENL_ERR_INVALID, ENL_ERR_UNSUPPORTED):
+        raise ValueError(msg)
+    raise RuntimeError(msg)
+
+
+def device_error(clear: bool = True) -> tuple[int, int]:
+    """(code, info) of the device error word; synchronises the device."""
+    code, info = c_int32(0), c_int32(0)
+    check(load().enl_device_error(ctypes.byref(code), ctypes.byref(info), int(clear)),
+          "enl_device_error")
+    return code.value, info.value
+
+
+def raise_on_device_error() -> None:
+    code, info = device_error(clear=True)
+    if code:
+        raise RuntimeError(
+            f"enilnets_b200 kernel reported device error {code} "
+            f"({DEVICE_ERRORS.get(code, 'unknown')}), info={info}")

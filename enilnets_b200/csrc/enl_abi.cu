@@ -1,0 +1,389 @@
+// C-ABI entry points of libenl_b200.so (declared in include/enl_attn.h):
+// argument validation, TMA tensor-map construction and kernel launches.
+#include <cstdio>
+#include <cstdarg>
+#include <string>
+
+#include "enl_attn.h"
+#include "enl_common.cuh"
+#include "enl_kernels.h"
+
+namespace enl {
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  return fail(ENL_ERR_CUDA, "%s: %s (%s)", where, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 4-D bf16 map over (head_dim, seq, heads, batch) with 128-byte swizzled
+// boxes of 64 x 128 elements: exactly the K-major SW128 layout the UMMA
+// descriptors in enl_prefill.cu expect.
+int make_qkv_map(CUtensorMap* map, const void* base, int D, int S, int H, int B, int64_t ss,
+                 int64_t sh, int64_t sb, const char* name) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(ENL_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)ss * 2, (cuuint64_t)sh * 2, (cuuint64_t)sb * 2};
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims,
+                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(ENL_ERR_INVALID, "cuTensorMapEncodeTiled(%s) failed with CUresult %d", name,
+                (int)r);
+  return ENL_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_strides_16B(const char* name, int64_t sb, int64_t ss, int64_t sh, int elem_bytes) {
+  const int64_t v[3] = {sb, ss, sh};
+  for (int i = 0; i < 3; ++i)
+    if (v[i] < 0 || (v[i] * elem_bytes) % 16 != 0)
+      return fail(ENL_ERR_INVALID,
+                  "%s strides (%lld, %lld, %lld) must be non-negative multiples of 16 bytes",
+                  name, (long long)sb, (long long)ss, (long long)sh);
+  return ENL_OK;
+}
+
+}  // namespace
+}  // namespace enl
+
+using namespace enl;
+
+extern "C" {
+
+const char* enl_last_error(void) { return t_last_error.c_str(); }
+
+int enl_abi_version(void) { return ENL_ABI_VERSION; }
+
+int enl_device_error(int32_t* code, int32_t* info, int32_t clear) {
+  int c = 0, i = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "enl_device_error: cudaDeviceSynchronize");
+  e = cudaMemcpyFromSymbol(&c, g_device_error, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&i, g_device_error_info, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail(e, "enl_device_error: read");
+  if (clear) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_device_error_info, &zero, sizeof(int));
+    if (e != cudaSuccess) return cuda_fail(e, "enl_device_error: clear");
+  }
+  if (code) *code = c;
+  if (info) *info = i;
+  return ENL_OK;
+}
+
+int enl_attn_prefill(const enl_prefill_args* a, void* stream) {
+  if (!a) return fail(ENL_ERR_INVALID, "enl_attn_prefill: args is NULL");
+  if (!a->q || !a->k || !a->v || !a->o)
+    return fail(ENL_ERR_INVALID, "enl_attn_prefill: q, k, v and o must be non-NULL");
+  if (a->batch < 1 || a->num_heads < 1 || a->num_kv_heads < 1 || a->seq_q < 1 || a->seq_kv < 1)
+    return fail(ENL_ERR_INVALID,
+                "enl_attn_prefill: batch=%d num_heads=%d num_kv_heads=%d seq_q=%d seq_kv=%d "
+                "must all be >= 1",
+                a->batch, a->num_heads, a->num_kv_heads, a->seq_q, a->seq_kv);
+  if (a->num_heads % a->num_kv_heads != 0)
+    return fail(ENL_ERR_INVALID, "enl_attn_prefill: num_kv_heads=%d must divide num_heads=%d",
+                a->num_kv_heads, a->num_heads);
+  if (a->head_dim != 64 && a->head_dim != 128)
+    return fail(ENL_ERR_UNSUPPORTED, "enl_attn_prefill: head_dim=%d (supported: 64, 128)",
+                a->head_dim);
+  if (a->in_dtype != ENL_DTYPE_BF16)
+    return fail(ENL_ERR_UNSUPPORTED, "enl_attn_prefill: in_dtype=%d (supported: bf16)",
+                a->in_dtype);
+  if (a->out_dtype != ENL_DTYPE_BF16 && a->out_dtype != ENL_DTYPE_FP32)
+    return fail(ENL_ERR_INVALID, "enl_attn_prefill: out_dtype=%d", a->out_dtype);
+  if (a->mask_mode != ENL_MASK_EXCLUDE && a->mask_mode != ENL_MASK_ADDITIVE)
+    return fail(ENL_ERR_INVALID, "enl_attn_prefill: mask_mode=%d", a->mask_mode);
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->o))
+    return fail(ENL_ERR_INVALID, "enl_attn_prefill: q, k, v, o must be 16-byte aligned");
+  int st;
+  if ((st = check_strides_16B("q", a->q_stride_b, a->q_stride_s, a->q_stride_h, 2))) return st;
+  if ((st = check_strides_16B("k", a->k_stride_b, a->k_stride_s, a->k_stride_h, 2))) return st;
+  if ((st = check_strides_16B("v", a->v_stride_b, a->v_stride_s, a->v_stride_h, 2))) return st;
+  if ((st = check_strides_16B("o", a->o_stride_b, a->o_stride_s, a->o_stride_h,
+                              a->out_dtype == ENL_DTYPE_FP32 ? 4 : 2)))
+    return st;
+  if ((long long)((a->seq_q + 255) / 256) > 65535)
+    return fail(ENL_ERR_UNSUPPORTED, "enl_attn_prefill: seq_q=%d too long", a->seq_q);
+
+  const int D = a->head_dim;
+  CUtensorMap tq, tk, tv;
+  if ((st = make_qkv_map(&tq, a->q, D, a->seq_q, a->num_heads, a->batch, a->q_stride_s,
+                         a->q_stride_h, a->q_stride_b, "q")))
+    return st;
+  if ((st = make_qkv_map(&tk, a->k, D, a->seq_kv, a->num_kv_heads, a->batch, a->k_stride_s,
+                         a->k_stride_h, a->k_stride_b, "k")))
+    return st;
+  if ((st = make_qkv_map(&tv, a->v, D, a->seq_kv, a->num_kv_heads, a->batch, a->v_stride_s,
+                         a->v_stride_h, a->v_stride_b, "v")))
+    return st;
+
+  PrefillParams p;
+  p.B = a->batch;
+  p.H = a->num_heads;
+  p.Hkv = a->num_kv_heads;
+  p.Sq = a->seq_q;
+  p.Skv = a->seq_kv;
+  p.o = a->o;
+  p.o_sb = a->o_stride_b;
+  p.o_ss = a->o_stride_s;
+  p.o_sh = a->o_stride_h;
+  p.out_fp32 = a->out_dtype == ENL_DTYPE_FP32;
+  p.lse = a->lse;
+  p.causal = a->causal != 0;
+  p.window = a->window < 0 ? -1 : a->window;
+  p.additive = a->mask_mode == ENL_MASK_ADDITIVE;
+  p.kv_len = a->kv_valid_len;
+  p.alibi = a->alibi_slopes;
+  p.q_pos0 = a->q_pos0;
+  p.k_pos0 = a->k_pos0;
+  p.scale_log2 = a->scale * 1.4426950408889634f;
+
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e = (D == 128) ? launch_prefill<128>(tq, tk, tv, p, s)
+                             : launch_prefill<64>(tq, tk, tv, p, s);
+  if (e != cudaSuccess) return cuda_fail(e, "enl_attn_prefill launch");
+  return ENL_OK;
+}
+
+int enl_decode_auto_splits(int32_t batch, int32_t num_kv_heads, int32_t n_slots) {
+  if (batch < 1 || num_kv_heads < 1 || n_slots < 1) return 1;
+  const long long units = (long long)batch * num_kv_heads;
+  const long long target_ctas = 148ll * 32;  // enough CTAs to balance 148 SMs
+  long long splits = (target_ctas + units - 1) / units;
+  const long long max_splits = (n_slots + 511) / 512;  // keep >= ~512 slots per split
+  if (splits > max_splits) splits = max_splits;
+  if (splits < 1) splits = 1;
+  if (splits > 1024) splits = 1024;
+  return (int)splits;
+}
+
+size_t enl_decode_workspace_bytes(int32_t batch, int32_t num_heads, int32_t head_dim,
+                                  int32_t n_splits) {
+  if (n_splits <= 1) return 0;
+  return (size_t)n_splits * batch * num_heads * (head_dim + 1) * sizeof(float);
+}
+
+int enl_attn_decode(const enl_decode_args* a, void* stream) {
+  if (!a) return fail(ENL_ERR_INVALID, "enl_attn_decode: args is NULL");
+  if (!a->q || !a->k_cache || !a->v_cache || !a->o)
+    return fail(ENL_ERR_INVALID, "enl_attn_decode: q, k_cache, v_cache and o must be non-NULL");
+  if (a->batch < 1 || a->num_heads < 1 || a->num_kv_heads < 1)
+    return fail(ENL_ERR_INVALID, "enl_attn_decode: batch/num_heads/num_kv_heads must be >= 1");
+  if (a->num_heads % a->num_kv_heads != 0)
+    return fail(ENL_ERR_INVALID, "enl_attn_decode: num_kv_heads=%d must divide num_heads=%d",
+                a->num_kv_heads, a->num_heads);
+  const int G = a->num_heads / a->num_kv_heads;
+  if (G != 1 && G != 2 && G != 4 && G != 8)
+    return fail(ENL_ERR_UNSUPPORTED,
+                "enl_attn_decode: num_heads/num_kv_heads=%d (supported: 1, 2, 4, 8)", G);
+  if (a->head_dim != 64 && a->head_dim != 128)
+    return fail(ENL_ERR_UNSUPPORTED, "enl_attn_decode: head_dim=%d (supported: 64, 128)",
+                a->head_dim);
+  if (a->in_dtype != ENL_DTYPE_BF16)
+    return fail(ENL_ERR_UNSUPPORTED, "enl_attn_decode: in_dtype=%d (supported: bf16)",
+                a->in_dtype);
+  if (a->out_dtype != ENL_DTYPE_BF16 && a->out_dtype != ENL_DTYPE_FP32)
+    return fail(ENL_ERR_INVALID, "enl_attn_decode: out_dtype=%d", a->out_dtype);
+  if (a->slot_begin < 0 || a->slot_end < a->slot_begin)
+    return fail(ENL_ERR_INVALID, "enl_attn_decode: slot range [%d, %d) is invalid",
+                a->slot_begin, a->slot_end);
+  if (!aligned16(a->q) || !aligned16(a->k_cache) || !aligned16(a->v_cache))
+    return fail(ENL_ERR_INVALID, "enl_attn_decode: q and caches must be 16-byte aligned");
+  int st;
+  if ((st = check_strides_16B("q", a->q_stride_b, 0, a->q_stride_h, 2))) return st;
+  if ((st = check_strides_16B("cache", a->cache_stride_b, a->cache_stride_s, a->cache_stride_h,
+                              2)))
+    return st;
+
+  // Narrow the slot range by causality (keys after the query are invisible)
+  // and by the sliding window, so the kernel only streams what it attends.
+  long long lo = a->slot_begin, hi = a->slot_end;
+  const long long q_slot = a->q_pos - a->pos_slot0;  // slot holding the query position
+  if (hi > q_slot + 1) hi = q_slot + 1;
+  if (a->window >= 0 && lo < q_slot - a->window) lo = q_slot - a->window;
+  if (hi < lo) hi = lo;
+  const int n_slots = (int)(hi - lo);
+
+  int splits = a->n_splits > 0 ? a->n_splits : enl_decode_auto_splits(a->batch, a->num_kv_heads,
+                                                                      n_slots > 0 ? n_slots : 1);
+  if (n_slots <= 1) splits = 1;
+  int split_len = (n_slots + splits - 1) / splits;
+  if (split_len < 1) split_len = 1;
+  splits = (n_slots + split_len - 1) / split_len;
+  if (splits < 1) splits = 1;
+  if (splits > 1) {
+    const size_t need = enl_decode_workspace_bytes(a->batch, a->num_heads, a->head_dim, splits);
+    if (!a->workspace || a->workspace_bytes < need)
+      return fail(ENL_ERR_INVALID,
+                  "enl_attn_decode: %d splits need a %zu-byte workspace (got %zu)", splits, need,
+                  a->workspace_bytes);
+  }
+
+  DecodeParams p;
+  p.B = a->batch;
+  p.H = a->num_heads;
+  p.Hkv = a->num_kv_heads;
+  p.q = a->q;
+  p.q_sb = a->q_stride_b;
+  p.q_sh = a->q_stride_h;
+  p.k = a->k_cache;
+  p.v = a->v_cache;
+  p.k_sb = p.v_sb = a->cache_stride_b;
+  p.k_sh = p.v_sh = a->cache_stride_h;
+  p.k_ss = p.v_ss = a->cache_stride_s;
+  p.slot_begin = (int)lo;
+  p.slot_end = (int)hi;
+  p.q_minus_k0 = q_slot;
+  p.alibi = a->alibi_slopes;
+  p.scale_log2 = a->scale * 1.4426950408889634f;
+  p.n_splits = splits;
+  p.split_len = split_len;
+  p.o = a->o;
+  p.o_sb = a->o_stride_b;
+  p.o_sh = a->o_stride_h;
+  p.out_fp32 = a->out_dtype == ENL_DTYPE_FP32;
+  p.lse = a->lse;
+  p.part_o = reinterpret_cast<float*>(a->workspace);
+  p.part_lse = p.part_o ? p.part_o + (size_t)splits * a->batch * a->num_heads * a->head_dim
+                        : nullptr;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e = (a->head_dim == 128) ? launch_decode<128>(p, s) : launch_decode<64>(p, s);
+  if (e != cudaSuccess) return cuda_fail(e, "enl_attn_decode launch");
+  return ENL_OK;
+}
+
+int enl_lse_merge(const float* part_o, const float* part_lse, int32_t n_parts, int32_t batch,
+                  int32_t num_heads, int32_t head_dim, void* o, int64_t o_stride_b,
+                  int64_t o_stride_h, int32_t out_dtype, float* lse, void* stream) {
+  if (!part_o || !part_lse || !o)
+    return fail(ENL_ERR_INVALID, "enl_lse_merge: part_o, part_lse and o must be non-NULL");
+  if (n_parts < 1 || batch < 1 || num_heads < 1 || head_dim < 1)
+    return fail(ENL_ERR_INVALID, "enl_lse_merge: sizes must be >= 1");
+  if (out_dtype != ENL_DTYPE_BF16 && out_dtype != ENL_DTYPE_FP32)
+    return fail(ENL_ERR_INVALID, "enl_lse_merge: out_dtype=%d", out_dtype);
+  cudaError_t e = launch_lse_merge(part_o, part_lse, n_parts, (long long)batch * num_heads * head_dim,
+                                   (long long)batch * num_heads, batch, num_heads, head_dim, o,
+                                   o_stride_b, o_stride_h, out_dtype == ENL_DTYPE_FP32, lse,
+                                   reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "enl_lse_merge launch");
+  return ENL_OK;
+}
+
+int enl_kv_append(void* cache, int64_t cache_stride_b, int64_t cache_stride_h,
+                  int64_t cache_stride_s, const void* src, int64_t src_stride_b,
+                  int64_t src_stride_t, int64_t src_stride_h, int32_t batch,
+                  int32_t num_kv_heads, int32_t n_new, int32_t head_dim, int32_t dtype,
+                  int64_t slot0, int64_t capacity, void* stream) {
+  if (!cache || !src) return fail(ENL_ERR_INVALID, "enl_kv_append: cache and src must be non-NULL");
+  if (dtype != ENL_DTYPE_BF16 && dtype != ENL_DTYPE_FP32)
+    return fail(ENL_ERR_INVALID, "enl_kv_append: dtype=%d", dtype);
+  const int eb = dtype == ENL_DTYPE_FP32 ? 4 : 2;
+  if (batch < 0 || num_kv_heads < 1 || n_new < 0 || head_dim < 1)
+    return fail(ENL_ERR_INVALID, "enl_kv_append: bad sizes");
+  if ((head_dim * eb) % 16 != 0)
+    return fail(ENL_ERR_INVALID, "enl_kv_append: head_dim * element size must be a multiple of 16");
+  if (slot0 < 0 || slot0 + n_new > capacity)
+    return fail(ENL_ERR_INVALID, "enl_kv_append: slots [%lld, %lld) exceed capacity %lld",
+                (long long)slot0, (long long)(slot0 + n_new), (long long)capacity);
+  if (!aligned16(cache) || !aligned16(src))
+    return fail(ENL_ERR_INVALID, "enl_kv_append: buffers must be 16-byte aligned");
+  int st;
+  if ((st = check_strides_16B("cache", cache_stride_b, cache_stride_s, cache_stride_h, eb)))
+    return st;
+  if ((st = check_strides_16B("src", src_stride_b, src_stride_t, src_stride_h, eb))) return st;
+  cudaError_t e = launch_kv_append(cache, cache_stride_b, cache_stride_h, cache_stride_s, src,
+                                   src_stride_b, src_stride_t, src_stride_h, batch, num_kv_heads,
+                                   n_new, head_dim, eb, slot0,
+                                   reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "enl_kv_append launch");
+  return ENL_OK;
+}
+
+int enl_kv_gather(void* dst, int64_t dst_stride_b, int64_t dst_stride_h, int64_t dst_stride_s,
+                  const void* src, int64_t src_stride_b, int64_t src_stride_h,
+                  int64_t src_stride_s, const int64_t* index, int32_t batch_out,
+                  int32_t batch_src, int32_t num_kv_heads, int32_t slot_begin, int32_t slot_end,
+                  int32_t head_dim, int32_t dtype, void* stream) {
+  if (!dst || !src || !index)
+    return fail(ENL_ERR_INVALID, "enl_kv_gather: dst, src and index must be non-NULL");
+  if (dst == src) return fail(ENL_ERR_INVALID, "enl_kv_gather: dst must not alias src");
+  if (dtype != ENL_DTYPE_BF16 && dtype != ENL_DTYPE_FP32)
+    return fail(ENL_ERR_INVALID, "enl_kv_gather: dtype=%d", dtype);
+  const int eb = dtype == ENL_DTYPE_FP32 ? 4 : 2;
+  if (batch_out < 0 || batch_src < 1 || num_kv_heads < 1 || slot_begin < 0 ||
+      slot_end < slot_begin || (head_dim * eb) % 16 != 0)
+    return fail(ENL_ERR_INVALID, "enl_kv_gather: bad sizes");
+  if (!aligned16(dst) || !aligned16(src))
+    return fail(ENL_ERR_INVALID, "enl_kv_gather: buffers must be 16-byte aligned");
+  int st;
+  if ((st = check_strides_16B("dst", dst_stride_b, dst_stride_s, dst_stride_h, eb))) return st;
+  if ((st = check_strides_16B("src", src_stride_b, src_stride_s, src_stride_h, eb))) return st;
+  cudaError_t e = launch_kv_gather(dst, dst_stride_b, dst_stride_h, dst_stride_s, src,
+                                   src_stride_b, src_stride_h, src_stride_s,
+                                   reinterpret_cast<const long long*>(index), batch_out,
+                                   batch_src, num_kv_heads, slot_begin, slot_end, head_dim, eb,
+                                   reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "enl_kv_gather launch");
+  return ENL_OK;
+}
+
+int enl_rope_apply(void* x, int64_t stride_b, int64_t stride_s, int64_t stride_h, int32_t batch,
+                   int32_t seq, int32_t num_heads, int32_t head_dim, int32_t dtype,
+                   const float* cos_table, const float* sin_table, int64_t table_row0,
+                   int64_t table_rows, void* stream) {
+  if (!x || !cos_table || !sin_table)
+    return fail(ENL_ERR_INVALID, "enl_rope_apply: x and tables must be non-NULL");
+  if (head_dim < 2 || head_dim % 2 != 0)
+    return fail(ENL_ERR_INVALID, "enl_rope_apply: head_dim=%d must be even", head_dim);
+  if (dtype != ENL_DTYPE_BF16 && dtype != ENL_DTYPE_FP32)
+    return fail(ENL_ERR_INVALID, "enl_rope_apply: dtype=%d", dtype);
+  if (batch < 0 || seq < 0 || num_heads < 1)
+    return fail(ENL_ERR_INVALID, "enl_rope_apply: bad sizes");
+  if (table_row0 < 0 || table_row0 + seq > table_rows)
+    return fail(ENL_ERR_INVALID, "enl_rope_apply: table rows [%lld, %lld) exceed %lld",
+                (long long)table_row0, (long long)(table_row0 + seq), (long long)table_rows);
+  cudaError_t e = launch_rope(x, stride_b, stride_s, stride_h, batch, seq, num_heads, head_dim,
+                              dtype == ENL_DTYPE_FP32 ? 4 : 2, cos_table, sin_table, table_row0,
+                              table_rows, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "enl_rope_apply launch");
+  return ENL_OK;
+}
+
+}  // extern "C"

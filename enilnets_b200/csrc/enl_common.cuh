@@ -1,0 +1,286 @@
+// Shared device helpers for the Enilnets B200 attention kernels (sm_100a only).
+//
+// Everything here is a thin inline-PTX wrapper around one Blackwell feature:
+// mbarriers, TMA tensor/bulk copies (never with cluster multicast), tcgen05
+// tensor-memory allocation / MMA / loads / stores, plus the device error word
+// that every bounded wait reports into instead of trapping.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda.h>
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "enilnets_b200 kernels are written for sm_100a only"
+#endif
+
+namespace enl {
+
+// ---------------------------------------------------------------------------
+// Device error word. Kernels never trap: a failed bound check or a wait that
+// ran out of time records a code here (first writer wins) and the kernel
+// returns. The host reads and clears it through enl_device_error().
+// ---------------------------------------------------------------------------
+enum DeviceError : int {
+  kDevOk = 0,
+  kDevWaitTimeout = 1,     // an mbarrier wait exceeded its time budget
+  kDevBadIndex = 2,        // an index (slot, gather row) was out of range
+  kDevBadShape = 3,        // launch-time shape invariants violated
+};
+
+// Defined here: the library is built as a single translation unit (enl_lib.cu).
+__device__ int g_device_error = 0;
+__device__ int g_device_error_info = 0;
+
+__device__ __forceinline__ void report_error(int code, int info) {
+  if (atomicCAS(&g_device_error, 0, code) == 0) {
+    g_device_error_info = info;
+  }
+}
+
+// Wait budget for every spin on an mbarrier: about one second of wall time.
+constexpr uint64_t kWaitBudgetNs = 1000ull * 1000ull * 1000ull;
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(
+                   smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait on `parity`. Returns false (after recording kDevWaitTimeout and
+// raising *abort) when the budget runs out or when another role already
+// aborted; the caller then stops issuing work and drains.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          volatile int* abort_flag, int site) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+      report_error(kDevWaitTimeout, site);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// TMA (tensor copies global -> shared, no multicast) and bulk copies.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2),
+      "r"(c3)
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05: tensor memory, MMA, loads and stores.
+// ---------------------------------------------------------------------------
+template <uint32_t kCols>
+__device__ __forceinline__ void tmem_alloc(uint32_t* smem_result) {
+  static_assert(kCols >= 32 && (kCols & (kCols - 1)) == 0 && kCols <= 512, "TMEM columns");
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(smem_result)),
+               "n"(kCols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+template <uint32_t kCols>
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "n"(kCols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (bf16 in, fp32 acc).
+__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc], kind::f16. A lives in tensor memory.
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` once every tcgen05.mma issued so far by this thread is done.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+// 32 lanes x 32 bit, 32 consecutive columns: thread i of the warp receives
+// lane (base_lane + i), columns [col, col + 32). The array is indexed with a
+// compile-time offset so it stays in registers.
+#define ENL_R32(a, o)                                                                        \
+  "=r"(a[(o) + 0]), "=r"(a[(o) + 1]), "=r"(a[(o) + 2]), "=r"(a[(o) + 3]), "=r"(a[(o) + 4]),  \
+      "=r"(a[(o) + 5]), "=r"(a[(o) + 6]), "=r"(a[(o) + 7]), "=r"(a[(o) + 8]),                \
+      "=r"(a[(o) + 9]), "=r"(a[(o) + 10]), "=r"(a[(o) + 11]), "=r"(a[(o) + 12]),             \
+      "=r"(a[(o) + 13]), "=r"(a[(o) + 14]), "=r"(a[(o) + 15]), "=r"(a[(o) + 16]),            \
+      "=r"(a[(o) + 17]), "=r"(a[(o) + 18]), "=r"(a[(o) + 19]), "=r"(a[(o) + 20]),            \
+      "=r"(a[(o) + 21]), "=r"(a[(o) + 22]), "=r"(a[(o) + 23]), "=r"(a[(o) + 24]),            \
+      "=r"(a[(o) + 25]), "=r"(a[(o) + 26]), "=r"(a[(o) + 27]), "=r"(a[(o) + 28]),            \
+      "=r"(a[(o) + 29]), "=r"(a[(o) + 30]), "=r"(a[(o) + 31])
+#define ENL_W32(a, o)                                                                        \
+  "r"(a[(o) + 0]), "r"(a[(o) + 1]), "r"(a[(o) + 2]), "r"(a[(o) + 3]), "r"(a[(o) + 4]),       \
+      "r"(a[(o) + 5]), "r"(a[(o) + 6]), "r"(a[(o) + 7]), "r"(a[(o) + 8]), "r"(a[(o) + 9]),   \
+      "r"(a[(o) + 10]), "r"(a[(o) + 11]), "r"(a[(o) + 12]), "r"(a[(o) + 13]),                \
+      "r"(a[(o) + 14]), "r"(a[(o) + 15]), "r"(a[(o) + 16]), "r"(a[(o) + 17]),                \
+      "r"(a[(o) + 18]), "r"(a[(o) + 19]), "r"(a[(o) + 20]), "r"(a[(o) + 21]),                \
+      "r"(a[(o) + 22]), "r"(a[(o) + 23]), "r"(a[(o) + 24]), "r"(a[(o) + 25]),                \
+      "r"(a[(o) + 26]), "r"(a[(o) + 27]), "r"(a[(o) + 28]), "r"(a[(o) + 29]),                \
+      "r"(a[(o) + 30]), "r"(a[(o) + 31])
+
+// Loads carry their own tcgen05.wait::ld inside the same asm statement: the
+// compiler treats asm outputs as ready when the statement ends, so a separate
+// wait could let it schedule uses of the registers before the data lands.
+#define ENL_TMEM_LD32(taddr, a, o)                                                           \
+  asm volatile(                                                                              \
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"                       \
+      "tcgen05.wait::ld.sync.aligned;"                                                       \
+      : ENL_R32(a, o)                                                                        \
+      : "r"(taddr)                                                                           \
+      : "memory")
+
+// 128 consecutive columns in one instruction (a full 128-key score row).
+#define ENL_TMEM_LD128(taddr, a)                                                             \
+  asm volatile(                                                                              \
+      "tcgen05.ld.sync.aligned.32x32b.x128.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63, %64, %65, %66, %67, %68, %69, %70, %71, %72, %73, %74, %75, %76, %77, %78, %79, %80, %81, %82, %83, %84, %85, %86, %87, %88, %89, %90, %91, %92, %93, %94, %95, %96, %97, %98, %99, %100, %101, %102, %103, %104, %105, %106, %107, %108, %109, %110, %111, %112, %113, %114, %115, %116, %117, %118, %119, %120, %121, %122, %123, %124, %125, %126, %127}, [%128];\n\t"                     \
+      "tcgen05.wait::ld.sync.aligned;"                                                       \
+      : ENL_R32(a, 0), ENL_R32(a, 32), ENL_R32(a, 64), ENL_R32(a, 96)                        \
+      : "r"(taddr)                                                                           \
+      : "memory")
+
+#define ENL_TMEM_ST32(taddr, a, o)                                                           \
+  asm volatile(                                                                              \
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "                                        \
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "            \
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"   \
+      ::"r"(taddr),                                                                          \
+      ENL_W32(a, o)                                                                          \
+      : "memory")
+
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// UMMA descriptors (tcgen05 shared-memory matrix descriptor, version 1).
+//   bits  0-13 start address >> 4     bits 16-29 leading byte offset >> 4
+//   bits 32-45 stride byte offset >> 4 bits 46-47 version (1 on sm_100)
+//   bits 49-51 base offset (0: tiles are 1024-byte aligned)
+//   bits 61-63 layout (2 = 128-byte swizzle)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo_bytes,
+                                                    uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
+// Instruction descriptor, kind::f16 with bf16 A/B and fp32 accumulation.
+//   bits 4-5 D format (1 = f32); 7-9 A format (1 = bf16); 10-12 B format;
+//   bit 15 A major (0 = K); bit 16 B major (1 = MN); 17-22 N >> 3; 24-28 M >> 4.
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(uint32_t M, uint32_t N, bool b_mn_major) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+         ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+
+// ---------------------------------------------------------------------------
+// Small numeric helpers.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+__device__ __forceinline__ float bf16lo_to_f32(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi_to_f32(uint32_t w) {
+  return __uint_as_float(w & 0xFFFF0000u);
+}
+
+}  // namespace enl

@@ -1,0 +1,279 @@
+// K2: bandwidth-bound split-KV decode, plus the log-sum-exp merge.
+//
+// Replaces the one-token attention of the reference's cached step,
+// nn/kvcache.py:198-213 (scores / sqrt(Dh), ALiBi at absolute positions,
+// softmax, attn @ V). The reference re-concatenates and re-reads the whole
+// cache each step; here the cache is a preallocated device buffer
+// (B, Hkv, capacity, D) and each step streams the live slots exactly once.
+//
+// Grid: (n_splits, B * Hkv). A CTA owns one contiguous slot range of one
+// (batch, kv head) and all H/Hkv query heads that share it (GQA group-major:
+// query head h reads kv head h / (H/Hkv), nn/forward.py:165-171), so every K/V
+// byte is read once per step whatever the group size. D/8 lanes share a key
+// row: each lane loads 16 contiguous bytes (128-bit, L1 no-allocate), so a
+// warp reads whole 256-byte rows back to back. Scores reduce across the lane
+// group with xor-shuffles; the softmax runs online in the log2 domain.
+#include "enl_common.cuh"
+#include "enl_kernels.h"
+
+namespace enl {
+
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ void unpack8(const uint4& w, float (&f)[8]) {
+  f[0] = bf16lo_to_f32(w.x);
+  f[1] = bf16hi_to_f32(w.x);
+  f[2] = bf16lo_to_f32(w.y);
+  f[3] = bf16hi_to_f32(w.y);
+  f[4] = bf16lo_to_f32(w.z);
+  f[5] = bf16hi_to_f32(w.z);
+  f[6] = bf16lo_to_f32(w.w);
+  f[7] = bf16hi_to_f32(w.w);
+}
+
+template <int D, int G>
+struct DecodeCfg {
+  static constexpr int kThreads = 128;
+  static constexpr int kLanesPerKey = D / 8;
+  static constexpr int kKeysPerWarp = 32 / kLanesPerKey;
+  static constexpr int kGroups = (kThreads / 32) * kKeysPerWarp;  // key groups per CTA
+  static constexpr int kUnroll = (G >= 4) ? 2 : 4;  // bounded by registers at large G
+};
+
+template <int D, int G>
+__global__ void __launch_bounds__(128) attn_decode_kernel(const DecodeParams p) {
+  using Cfg = DecodeCfg<D, G>;
+  constexpr int LPK = Cfg::kLanesPerKey;
+  constexpr int NG = Cfg::kGroups;
+  constexpr int U = Cfg::kUnroll;
+
+  const int split = blockIdx.x;
+  const int bkv = blockIdx.y;
+  const int b = bkv / p.Hkv;
+  const int hkv = bkv % p.Hkv;
+  const int lane = threadIdx.x % 32;
+  const int warp = threadIdx.x / 32;
+  const int sub = lane % LPK;                        // which 8-element slice of D
+  const int group = warp * Cfg::kKeysPerWarp + lane / LPK;
+
+  const int s_begin = p.slot_begin + split * p.split_len;
+  const int s_end = min(p.slot_end, s_begin + p.split_len);
+
+  // Queries of the GQA group, pre-scaled into the log2 domain.
+  float q[G][8];
+  float slope2[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const int h = hkv * G + g;
+    const uint4 w = *reinterpret_cast<const uint4*>(
+        reinterpret_cast<const __nv_bfloat16*>(p.q) + (long long)b * p.q_sb +
+        (long long)h * p.q_sh + sub * 8);
+    unpack8(w, q[g]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) q[g][i] *= p.scale_log2;
+    slope2[g] = p.alibi ? p.alibi[h] * 1.4426950408889634f : 0.0f;
+  }
+
+  float m[G], l[G], acc[G][8];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[g][i] = 0.0f;
+  }
+
+  const __nv_bfloat16* kbase = reinterpret_cast<const __nv_bfloat16*>(p.k) +
+                               (long long)b * p.k_sb + (long long)hkv * p.k_sh + sub * 8;
+  const __nv_bfloat16* vbase = reinterpret_cast<const __nv_bfloat16*>(p.v) +
+                               (long long)b * p.v_sb + (long long)hkv * p.v_sh + sub * 8;
+
+  // The loop bound is warp-uniform (the shuffles below need the whole warp);
+  // each lane group masks its own slots past the end of the split.
+  const int group_in_warp = lane / LPK;
+  for (int sw = s_begin + warp * Cfg::kKeysPerWarp; sw < s_end; sw += NG * U) {
+    const int s0 = sw + group_in_warp;
+    uint4 kr[U], vr[U];
+    bool valid[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int slot = s0 + u * NG;
+      valid[u] = slot < s_end;
+      if (valid[u]) {
+        kr[u] = ld_stream(kbase + (long long)slot * p.k_ss);
+        vr[u] = ld_stream(vbase + (long long)slot * p.v_ss);
+      } else {
+        kr[u] = make_uint4(0, 0, 0, 0);
+        vr[u] = make_uint4(0, 0, 0, 0);
+      }
+    }
+    float kf[U][8], vf[U][8];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      unpack8(kr[u], kf[u]);
+      unpack8(vr[u], vf[u]);
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float s[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        float d = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) d = fmaf(q[g][i], kf[u][i], d);
+#pragma unroll
+        for (int off = LPK / 2; off > 0; off /= 2) d += __shfl_xor_sync(0xffffffffu, d, off);
+        if (slope2[g] != 0.0f) {
+          // ALiBi at absolute positions: -slope * (pos_q - pos_k), nn/kvcache.py:199-203.
+          const float dist = (float)(p.q_minus_k0 - (long long)(s0 + u * NG));
+          d = fmaf(-slope2[g], dist, d);
+        }
+        s[u] = valid[u] ? d : -INFINITY;
+      }
+      float mx = m[g];
+#pragma unroll
+      for (int u = 0; u < U; ++u) mx = fmaxf(mx, s[u]);
+      if (mx != -INFINITY) {
+        const float corr = fast_exp2(m[g] - mx);  // exp2(-inf) == 0 on the first keys
+        l[g] *= corr;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[g][i] *= corr;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const float pu = fast_exp2(s[u] - mx);
+          l[g] += pu;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[g][i] = fmaf(pu, vf[u][i], acc[g][i]);
+        }
+        m[g] = mx;
+      }
+    }
+  }
+
+  // Merge the NG key groups of this CTA through shared memory.
+  __shared__ float sm_m[G][NG];
+  __shared__ float sm_l[G][NG];
+  __shared__ float sm_acc[G][NG][D];
+  if (sub == 0) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      sm_m[g][group] = m[g];
+      sm_l[g][group] = l[g];
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sm_acc[g][group][sub * 8 + i] = acc[g][i];
+  __syncthreads();
+
+  for (int idx = threadIdx.x; idx < G * D; idx += Cfg::kThreads) {
+    const int g = idx / D;
+    const int d = idx % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < NG; ++k) M = fmaxf(M, sm_m[g][k]);
+    float L = 0.0f, O = 0.0f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int k = 0; k < NG; ++k) {
+        const float w = fast_exp2(sm_m[g][k] - M);
+        L = fmaf(w, sm_l[g][k], L);
+        O = fmaf(w, sm_acc[g][k][d], O);
+      }
+    }
+    const int h = hkv * G + g;
+    const float lse = (M == -INFINITY) ? -INFINITY : (M + log2f(L)) * 0.6931471805599453f;
+    if (p.n_splits == 1) {
+      const float val = O / L;  // 0/0 -> NaN when no key was visible
+      if (p.out_fp32) {
+        reinterpret_cast<float*>(p.o)[(long long)b * p.o_sb + (long long)h * p.o_sh + d] = val;
+      } else {
+        reinterpret_cast<__nv_bfloat16*>(p.o)[(long long)b * p.o_sb + (long long)h * p.o_sh + d] =
+            __float2bfloat16_rn(val);
+      }
+      if (d == 0 && p.lse) p.lse[(long long)b * p.H + h] = lse;
+    } else {
+      const long long row = ((long long)split * p.B + b) * p.H + h;
+      p.part_o[row * D + d] = (L > 0.0f) ? O / L : 0.0f;
+      if (d == 0) p.part_lse[row] = lse;
+    }
+  }
+}
+
+template <int D, int G>
+static cudaError_t launch_decode_g(const DecodeParams& p, cudaStream_t stream) {
+  dim3 grid(p.n_splits, p.B * p.Hkv);
+  attn_decode_kernel<D, G><<<grid, DecodeCfg<D, G>::kThreads, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+template <int D>
+cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream) {
+  const int G = p.H / p.Hkv;
+  cudaError_t e;
+  switch (G) {
+    case 1: e = launch_decode_g<D, 1>(p, stream); break;
+    case 2: e = launch_decode_g<D, 2>(p, stream); break;
+    case 4: e = launch_decode_g<D, 4>(p, stream); break;
+    case 8: e = launch_decode_g<D, 8>(p, stream); break;
+    default: return cudaErrorInvalidValue;
+  }
+  if (e != cudaSuccess || p.n_splits == 1) return e;
+  return launch_lse_merge(p.part_o, p.part_lse, p.n_splits, (long long)p.B * p.H * D,
+                          (long long)p.B * p.H, p.B, p.H, D, p.o, p.o_sb, p.o_sh, p.out_fp32,
+                          p.lse, stream);
+}
+
+template cudaError_t launch_decode<64>(const DecodeParams&, cudaStream_t);
+template cudaError_t launch_decode<128>(const DecodeParams&, cudaStream_t);
+
+// out = sum_i e^{lse_i - lse*} o_i / sum_i e^{lse_i - lse*}; parts whose
+// lse is -inf (no visible key) carry no weight.
+__global__ void lse_merge_kernel(const float* __restrict__ part_o,
+                                 const float* __restrict__ part_lse, int n_parts,
+                                 long long stride_o, long long stride_lse, int B, int H, int D,
+                                 void* o, long long o_sb, long long o_sh, int out_fp32,
+                                 float* lse_out) {
+  const int bh = blockIdx.x;
+  const int b = bh / H, h = bh % H;
+  float M = -INFINITY;
+  for (int i = 0; i < n_parts; ++i) M = fmaxf(M, part_lse[i * stride_lse + bh]);
+  float W = 0.0f;
+  if (M != -INFINITY)
+    for (int i = 0; i < n_parts; ++i) W += __expf(part_lse[i * stride_lse + bh] - M);
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.0f;
+    if (M != -INFINITY) {
+      for (int i = 0; i < n_parts; ++i) {
+        const float li = part_lse[i * stride_lse + bh];
+        if (li != -INFINITY) acc += __expf(li - M) * part_o[i * stride_o + (long long)bh * D + d];
+      }
+    }
+    const float val = acc / W;  // NaN when nothing was visible, like the reference
+    if (out_fp32)
+      reinterpret_cast<float*>(o)[(long long)b * o_sb + (long long)h * o_sh + d] = val;
+    else
+      reinterpret_cast<__nv_bfloat16*>(o)[(long long)b * o_sb + (long long)h * o_sh + d] =
+          __float2bfloat16_rn(val);
+  }
+  if (threadIdx.x == 0 && lse_out) lse_out[bh] = (M == -INFINITY) ? M : M + logf(W);
+}
+
+cudaError_t launch_lse_merge(const float* part_o, const float* part_lse, int n_parts,
+                             long long part_stride_o, long long part_stride_lse, int B, int H,
+                             int D, void* o, long long o_sb, long long o_sh, int out_fp32,
+                             float* lse, cudaStream_t stream) {
+  lse_merge_kernel<<<B * H, 128, 0, stream>>>(part_o, part_lse, n_parts, part_stride_o,
+                                              part_stride_lse, B, H, D, o, o_sb, o_sh, out_fp32,
+                                              lse);
+  return cudaGetLastError();
+}
+
+}  // namespace enl

@@ -1,0 +1,84 @@
+// Internal launch interface between the C-ABI layer (enl_abi.cu) and the
+// kernels. Not installed; the public surface is include/enl_attn.h.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace enl {
+
+// K1 prefill. Q is (B, Sq, H, D), K/V (B, Skv, Hkv, D) with arbitrary b/s/h
+// strides (head dim contiguous) described by the tensor maps; O has the same
+// logical shape as Q. Query row r sits at absolute position q_pos0 + r, key j
+// at k_pos0 + j.
+struct PrefillParams {
+  int B, H, Hkv, Sq, Skv;
+  void* o;
+  long long o_sb, o_ss, o_sh;  // element strides of O
+  int out_fp32;                // 0: bf16 output, 1: fp32 output
+  float* lse;                  // (B, H, Sq) natural-log LSE, or null
+  int causal;                  // key j allowed only if pos_k <= pos_q
+  int window;                  // < 0: none; else |pos_q - pos_k| <= window
+  int additive;                // 1: graph/sequence.py -1e9 additive rule; 0: -inf exclusion
+  const int* kv_len;           // (B) valid key prefix per batch row, or null
+  const float* alibi;          // (H) ALiBi slopes (natural-log units), or null
+  long long q_pos0, k_pos0;
+  float scale_log2;            // softmax scale * log2(e)
+};
+
+template <int D>
+cudaError_t launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                           const PrefillParams& p, cudaStream_t stream);
+
+// K2 split-KV decode: one query token per (b, h) against cached slots.
+struct DecodeParams {
+  int B, H, Hkv;
+  const void* q;  // bf16 q[b, h, :]
+  long long q_sb, q_sh;
+  const void* k;  // bf16 cache[b, hkv, slot, :]
+  const void* v;
+  long long k_sb, k_sh, k_ss;
+  long long v_sb, v_sh, v_ss;
+  int slot_begin, slot_end;  // key slots to read, already narrowed by the window
+  long long q_minus_k0;      // q position minus the position of slot 0
+  const float* alibi;        // (H) or null
+  float scale_log2;
+  int n_splits, split_len;
+  void* o;  // final output o[b, h, :] (n_splits == 1)
+  long long o_sb, o_sh;
+  int out_fp32;
+  float* lse;       // (B, H) or null (n_splits == 1)
+  float* part_o;    // (n_splits, B, H, D) fp32 normalised partials
+  float* part_lse;  // (n_splits, B, H)
+};
+
+template <int D>
+cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream);
+
+// LSE merge of n_parts normalised partials (o_i, lse_i) into one output.
+cudaError_t launch_lse_merge(const float* part_o, const float* part_lse, int n_parts,
+                             long long part_stride_o, long long part_stride_lse, int B, int H,
+                             int D, void* o, long long o_sb, long long o_sh, int out_fp32,
+                             float* lse, cudaStream_t stream);
+
+// K3 cache append: cache[b, h, slot0 + t, :] = src[b, t, h, :].
+cudaError_t launch_kv_append(void* cache, long long c_sb, long long c_sh, long long c_ss,
+                             const void* src, long long s_sb, long long s_st, long long s_sh,
+                             int B, int Hkv, int n_new, int D, int elem_bytes, long long slot0,
+                             cudaStream_t stream);
+
+// Batch-axis gather of cache rows: dst[i, h, s, :] = src[index[i], h, s, :]
+// for s in [slot_begin, slot_end).
+cudaError_t launch_kv_gather(void* dst, long long d_sb, long long d_sh, long long d_ss,
+                             const void* src, long long s_sb, long long s_sh, long long s_ss,
+                             const long long* index, int B_out, int B_src, int Hkv,
+                             int slot_begin, int slot_end, int D, int elem_bytes,
+                             cudaStream_t stream);
+
+// RoPE rotate-half in place on x[b, s, h, :] using a (n_pos, D/2) cos/sin table.
+cudaError_t launch_rope(void* x, long long x_sb, long long x_ss, long long x_sh, int B, int S,
+                        int H, int D, int elem_bytes, const float* cos_t, const float* sin_t,
+                        long long table_row0, long long n_rows, cudaStream_t stream);
+
+}  // namespace enl

@@ -1,0 +1,7 @@
+// Single translation unit of libenl_b200.so: the kernels share one device
+// error word, so they are compiled together rather than with relocatable
+// device code.
+#include "enl_abi.cu"
+#include "enl_prefill.cu"
+#include "enl_decode.cu"
+#include "enl_kvcache.cu"

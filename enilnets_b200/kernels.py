@@ -1,0 +1,261 @@
+"""Tensor-level wrappers over the C ABI: one Python function per entry point.
+
+Tensors are torch CUDA tensors (device memory and streams are plumbing; the
+math runs in libenl_b200.so). Every function launches on the current torch
+stream and returns without synchronising, like the ABI itself.
+
+Shapes follow the reference's head-split convention
+(nn/forward.py:433-435): queries (B, S, H, D) and keys/values (B, S, Hkv, D)
+as strided views of the projection outputs, KV caches (B, Hkv, S, D)
+(nn/kvcache.py:27-30).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Optional
+
+import torch
+
+from . import _native as nat
+
+_DTYPES = {torch.bfloat16: nat.ENL_DTYPE_BF16, torch.float32: nat.ENL_DTYPE_FP32}
+_MASK_MODES = {"exclude": nat.ENL_MASK_EXCLUDE, "additive": nat.ENL_MASK_ADDITIVE}
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _require_cuda(name: str, t: torch.Tensor, dtype=None, last_contiguous=True) -> None:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (got {type(t).__name__})")
+    if dtype is not None and t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype} (got {t.dtype})")
+    if last_contiguous and t.stride(-1) != 1:
+        raise ValueError(f"{name} must have a contiguous last (head) dimension")
+
+
+def attention_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
+                      causal: bool = False, window: Optional[int] = None,
+                      kv_valid_len: Optional[torch.Tensor] = None,
+                      alibi_slopes: Optional[torch.Tensor] = None,
+                      q_pos0: int = 0, k_pos0: int = 0, mask_mode: str = "exclude",
+                      scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
+                      out_dtype: torch.dtype = torch.bfloat16,
+                      return_lse: bool = False):
+    """softmax(q k^T * scale + alibi + mask) v via the K1 tcgen05 kernel.
+
+    q: (B, Sq, H, D) bf16; k, v: (B, Skv, Hkv, D) bf16; H % Hkv == 0 and query
+    head h reads kv head h // (H // Hkv) (nn/forward.py:165-171).
+    kv_valid_len: int32 (B,) -- keys [0, len_b) are real (graph/sequence.py:23-29).
+    mask_mode: "exclude" (-inf, the nn/ path) or "additive" (-1e9 per violated
+    mask term, graph/sequence.py:162-176).
+    Returns out (B, Sq, H, D) [and lse (B, H, Sq) fp32].
+    """
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _require_cuda(name, t, torch.bfloat16)
+        if t.dim() != 4:
+            raise ValueError(f"{name} must be 4-D (batch, seq, heads, head_dim)")
+    B, Sq, H, D = q.shape
+    Bk, Skv, Hkv, Dk = k.shape
+    if tuple(v.shape) != (Bk, Skv, Hkv, Dk) or Bk != B or Dk != D:
+        raise ValueError(f"shape mismatch: q {tuple(q.shape)}, k {tuple(k.shape)}, "
+                         f"v {tuple(v.shape)}")
+    if mask_mode not in _MASK_MODES:
+        raise ValueError(f"mask_mode must be one of {sorted(_MASK_MODES)}, got {mask_mode!r}")
+    if out is None:
+        out = torch.empty((B, Sq, H, D), device=q.device, dtype=out_dtype)
+    _require_cuda("out", out)
+    if tuple(out.shape) != (B, Sq, H, D) or out.dtype not in _DTYPES:
+        raise ValueError(f"out must be ({B}, {Sq}, {H}, {D}) bf16/fp32")
+    lse = torch.empty((B, H, Sq), device=q.device, dtype=torch.float32) if return_lse else None
+    if kv_valid_len is not None:
+        _require_cuda("kv_valid_len", kv_valid_len, torch.int32, last_contiguous=False)
+        if tuple(kv_valid_len.shape) != (B,) or not kv_valid_len.is_contiguous():
+            raise ValueError(f"kv_valid_len must be a contiguous int32 ({B},) tensor")
+    if alibi_slopes is not None:
+        _require_cuda("alibi_slopes", alibi_slopes, torch.float32, last_contiguous=False)
+        if tuple(alibi_slopes.shape) != (H,) or not alibi_slopes.is_contiguous():
+            raise ValueError(f"alibi_slopes must be a contiguous float32 ({H},) tensor")
+    a = nat.PrefillArgs()
+    a.q, a.k, a.v, a.o, a.lse = q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), _ptr(lse)
+    a.batch, a.num_heads, a.num_kv_heads = B, H, Hkv
+    a.seq_q, a.seq_kv, a.head_dim = Sq, Skv, D
+    a.q_stride_b, a.q_stride_s, a.q_stride_h = q.stride(0), q.stride(1), q.stride(2)
+    a.k_stride_b, a.k_stride_s, a.k_stride_h = k.stride(0), k.stride(1), k.stride(2)
+    a.v_stride_b, a.v_stride_s, a.v_stride_h = v.stride(0), v.stride(1), v.stride(2)
+    a.o_stride_b, a.o_stride_s, a.o_stride_h = out.stride(0), out.stride(1), out.stride(2)
+    a.in_dtype = nat.ENL_DTYPE_BF16
+    a.out_dtype = _DTYPES[out.dtype]
+    a.causal = int(bool(causal))
+    a.window = -1 if window is None else int(window)
+    a.mask_mode = _MASK_MODES[mask_mode]
+    a.kv_valid_len = _ptr(kv_valid_len)
+    a.alibi_slopes = _ptr(alibi_slopes)
+    a.q_pos0, a.k_pos0 = int(q_pos0), int(k_pos0)
+    a.scale = 1.0 / math.sqrt(D) if scale is None else float(scale)
+    nat.check(nat.load().enl_attn_prefill(ctypes.byref(a), _stream()), "enl_attn_prefill")
+    return (out, lse) if return_lse else out
+
+
+_workspaces: dict = {}
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    key = (device.index if device.index is not None else torch.cuda.current_device())
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _workspaces[key] = ws
+    return ws
+
+
+def decode_workspace_bytes(batch: int, num_heads: int, head_dim: int, n_splits: int) -> int:
+    return int(nat.load().enl_decode_workspace_bytes(batch, num_heads, head_dim, n_splits))
+
+
+def decode_auto_splits(batch: int, num_kv_heads: int, n_slots: int) -> int:
+    return int(nat.load().enl_decode_auto_splits(batch, num_kv_heads, max(1, n_slots)))
+
+
+def attention_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, *,
+                     slot_begin: int, slot_end: int, pos_slot0: int, q_pos: int,
+                     window: Optional[int] = None,
+                     alibi_slopes: Optional[torch.Tensor] = None,
+                     scale: Optional[float] = None, n_splits: int = 0,
+                     out: Optional[torch.Tensor] = None,
+                     out_dtype: torch.dtype = torch.bfloat16,
+                     workspace: Optional[torch.Tensor] = None,
+                     return_lse: bool = False):
+    """One-token decode via the K2 split-KV kernel.
+
+    q: (B, H, D) bf16; k_cache/v_cache: (B, Hkv, capacity, D) bf16 with equal
+    strides; live slots [slot_begin, slot_end), slot s at absolute position
+    pos_slot0 + s; the query sits at q_pos (keys after it are invisible).
+    Returns out (B, H, D) [and lse (B, H) fp32].
+    """
+    _require_cuda("q", q, torch.bfloat16)
+    _require_cuda("k_cache", k_cache, torch.bfloat16)
+    _require_cuda("v_cache", v_cache, torch.bfloat16)
+    if q.dim() != 3 or k_cache.dim() != 4:
+        raise ValueError("q must be (B, H, D) and caches (B, Hkv, capacity, D)")
+    if k_cache.shape != v_cache.shape or k_cache.stride() != v_cache.stride():
+        raise ValueError("k_cache and v_cache must have the same shape and strides")
+    B, H, D = q.shape
+    Bc, Hkv, cap, Dc = k_cache.shape
+    if Bc != B or Dc != D:
+        raise ValueError(f"shape mismatch: q {tuple(q.shape)} vs cache {tuple(k_cache.shape)}")
+    if not (0 <= slot_begin <= slot_end <= cap):
+        raise ValueError(f"slot range [{slot_begin}, {slot_end}) outside capacity {cap}")
+    if out is None:
+        out = torch.empty((B, H, D), device=q.device, dtype=out_dtype)
+    _require_cuda("out", out)
+    if tuple(out.shape) != (B, H, D) or out.dtype not in _DTYPES:
+        raise ValueError(f"out must be ({B}, {H}, {D}) bf16/fp32")
+    lse = torch.empty((B, H), device=q.device, dtype=torch.float32) if return_lse else None
+    if alibi_slopes is not None:
+        _require_cuda("alibi_slopes", alibi_slopes, torch.float32, last_contiguous=False)
+    n_slots = max(1, slot_end - slot_begin)
+    splits = n_splits if n_splits > 0 else decode_auto_splits(B, Hkv, n_slots)
+    need = decode_workspace_bytes(B, H, D, splits)
+    if workspace is None and need > 0:
+        workspace = _workspace(q.device, need)
+    a = nat.DecodeArgs()
+    a.q, a.q_stride_b, a.q_stride_h = q.data_ptr(), q.stride(0), q.stride(1)
+    a.k_cache, a.v_cache = k_cache.data_ptr(), v_cache.data_ptr()
+    a.cache_stride_b, a.cache_stride_h, a.cache_stride_s = (k_cache.stride(0), k_cache.stride(1),
+                                                            k_cache.stride(2))
+    a.o, a.o_stride_b, a.o_stride_h = out.data_ptr(), out.stride(0), out.stride(1)
+    a.lse = _ptr(lse)
+    a.batch, a.num_heads, a.num_kv_heads, a.head_dim = B, H, Hkv, D
+    a.slot_begin, a.slot_end = int(slot_begin), int(slot_end)
+    a.pos_slot0, a.q_pos = int(pos_slot0), int(q_pos)
+    a.window = -1 if window is None else int(window)
+    a.alibi_slopes = _ptr(alibi_slopes)
+    a.scale = 1.0 / math.sqrt(D) if scale is None else float(scale)
+    a.in_dtype, a.out_dtype = nat.ENL_DTYPE_BF16, _DTYPES[out.dtype]
+    a.n_splits = int(splits)
+    a.workspace = _ptr(workspace)
+    a.workspace_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    nat.check(nat.load().enl_attn_decode(ctypes.byref(a), _stream()), "enl_attn_decode")
+    return (out, lse) if return_lse else out
+
+
+def lse_merge(part_o: torch.Tensor, part_lse: torch.Tensor, *,
+              out: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.bfloat16,
+              return_lse: bool = False):
+    """Merge (n_parts, B, H, D) fp32 partials by their (n_parts, B, H) LSEs."""
+    _require_cuda("part_o", part_o, torch.float32)
+    _require_cuda("part_lse", part_lse, torch.float32, last_contiguous=False)
+    if not part_o.is_contiguous() or not part_lse.is_contiguous():
+        raise ValueError("partials must be contiguous")
+    P, B, H, D = part_o.shape
+    if tuple(part_lse.shape) != (P, B, H):
+        raise ValueError("part_lse must be (n_parts, B, H)")
+    if out is None:
+        out = torch.empty((B, H, D), device=part_o.device, dtype=out_dtype)
+    lse = torch.empty((B, H), device=part_o.device, dtype=torch.float32) if return_lse else None
+    nat.check(nat.load().enl_lse_merge(part_o.data_ptr(), part_lse.data_ptr(), P, B, H, D,
+                                       out.data_ptr(), out.stride(0), out.stride(1),
+                                       _DTYPES[out.dtype], _ptr(lse), _stream()),
+              "enl_lse_merge")
+    return (out, lse) if return_lse else out
+
+
+def kv_append(cache: torch.Tensor, src: torch.Tensor, slot0: int) -> None:
+    """cache[b, h, slot0 + t] = src[b, t, h] for a (B, Hkv, cap, D) cache and a
+    (B, n_new, Hkv, D) source (the head-split projection output)."""
+    _require_cuda("cache", cache)
+    _require_cuda("src", src)
+    if cache.dtype != src.dtype or cache.dtype not in _DTYPES:
+        raise ValueError("cache and src must share a bf16/fp32 dtype")
+    B, Hkv, cap, D = cache.shape
+    Bs, n_new, Hs, Ds = src.shape
+    if (Bs, Hs, Ds) != (B, Hkv, D):
+        raise ValueError(f"src {tuple(src.shape)} does not match cache {tuple(cache.shape)}")
+    nat.check(nat.load().enl_kv_append(cache.data_ptr(), cache.stride(0), cache.stride(1),
+                                       cache.stride(2), src.data_ptr(), src.stride(0),
+                                       src.stride(1), src.stride(2), B, Hkv, n_new, D,
+                                       _DTYPES[cache.dtype], int(slot0), cap, _stream()),
+              "enl_kv_append")
+
+
+def kv_gather(dst: torch.Tensor, src: torch.Tensor, index: torch.Tensor, slot_begin: int,
+              slot_end: int) -> None:
+    """dst[i, :, s] = src[index[i], :, s] for s in [slot_begin, slot_end)."""
+    _require_cuda("dst", dst)
+    _require_cuda("src", src)
+    _require_cuda("index", index, torch.int64, last_contiguous=False)
+    if dst.dtype != src.dtype or dst.shape[1:] != src.shape[1:]:
+        raise ValueError("dst and src must agree in dtype and (Hkv, cap, D)")
+    if tuple(index.shape) != (dst.shape[0],) or not index.is_contiguous():
+        raise ValueError("index must be a contiguous int64 (B_out,) tensor")
+    nat.check(nat.load().enl_kv_gather(dst.data_ptr(), dst.stride(0), dst.stride(1),
+                                       dst.stride(2), src.data_ptr(), src.stride(0),
+                                       src.stride(1), src.stride(2), index.data_ptr(),
+                                       dst.shape[0], src.shape[0], src.shape[1], int(slot_begin),
+                                       int(slot_end), src.shape[3], _DTYPES[src.dtype],
+                                       _stream()),
+              "enl_kv_gather")
+
+
+def rope_(x: torch.Tensor, cos_table: torch.Tensor, sin_table: torch.Tensor,
+          row0: int) -> torch.Tensor:
+    """Rotate x (B, S, H, D) in place; sequence row s uses table row row0 + s."""
+    _require_cuda("x", x)
+    _require_cuda("cos_table", cos_table, torch.float32)
+    _require_cuda("sin_table", sin_table, torch.float32)
+    B, S, H, D = x.shape
+    if cos_table.shape != sin_table.shape or cos_table.shape[1] != D // 2:
+        raise ValueError("cos/sin tables must both be (rows, head_dim/2)")
+    nat.check(nat.load().enl_rope_apply(x.data_ptr(), x.stride(0), x.stride(1), x.stride(2), B, S,
+                                        H, D, _DTYPES[x.dtype], cos_table.data_ptr(),
+                                        sin_table.data_ptr(), int(row0), cos_table.shape[0],
+                                        _stream()),
+              "enl_rope_apply")
+    return x

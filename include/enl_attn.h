@@ -1,0 +1,164 @@
+/*
+ * enl_attn.h -- C ABI of libenl_b200.so, the B200 (sm_100a) attention
+ * inference path behind the Enilnets attention layers.
+ *
+ * Plain C: pointers, fixed-width integers and sizes only. Every entry point
+ * returns an int status (ENL_OK == 0); on failure enl_last_error() returns a
+ * thread-local message. Launches are asynchronous on the caller's stream
+ * (a cudaStream_t passed as void*, NULL = legacy default stream). Device
+ * pointers are caller-owned; the library never allocates device memory.
+ *
+ * Layout conventions: every tensor has a contiguous head dimension; the
+ * other axes are described by element strides, so projection outputs of
+ * shape (batch, seq, heads * head_dim) are consumed in place.
+ */
+#ifndef ENL_ATTN_H_
+#define ENL_ATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ENL_ABI_VERSION 1
+
+/* Status codes. The Python binding maps INVALID/UNSUPPORTED to ValueError
+ * (the reference raises ValueError for bad layer configurations,
+ * nn/layers.py:210-327) and CUDA/DEVICE to RuntimeError (core/backend.py:106-113). */
+enum {
+  ENL_OK = 0,
+  ENL_ERR_INVALID = 1,     /* bad argument: shape, stride, alignment, null pointer */
+  ENL_ERR_UNSUPPORTED = 2, /* valid request outside what the kernels cover */
+  ENL_ERR_CUDA = 3,        /* CUDA runtime / driver error */
+  ENL_ERR_DEVICE = 4       /* a kernel recorded an error in the device error word */
+};
+
+enum { ENL_DTYPE_BF16 = 0, ENL_DTYPE_FP32 = 1 };
+
+/* How masked scores are treated.
+ * EXCLUDE : masked scores are -inf (nn/forward.py:102-117, the nn/ layers).
+ * ADDITIVE: each violated mask term adds -1e9 (graph/sequence.py:162-176);
+ *           a row whose every key is masked keeps the keys with the fewest
+ *           violations, exactly as the float64 reference does. */
+enum { ENL_MASK_EXCLUDE = 0, ENL_MASK_ADDITIVE = 1 };
+
+/* ---------------------------------------------------------------- prefill */
+typedef struct enl_prefill_args {
+  const void* q; /* (batch, seq_q, num_heads, head_dim) */
+  const void* k; /* (batch, seq_kv, num_kv_heads, head_dim) */
+  const void* v; /* (batch, seq_kv, num_kv_heads, head_dim) */
+  void* o;       /* (batch, seq_q, num_heads, head_dim), out_dtype */
+  float* lse;    /* (batch, num_heads, seq_q) natural-log LSE, or NULL */
+  int32_t batch, num_heads, num_kv_heads, seq_q, seq_kv, head_dim;
+  int64_t q_stride_b, q_stride_s, q_stride_h; /* element strides */
+  int64_t k_stride_b, k_stride_s, k_stride_h;
+  int64_t v_stride_b, v_stride_s, v_stride_h;
+  int64_t o_stride_b, o_stride_s, o_stride_h;
+  int32_t in_dtype;  /* ENL_DTYPE_BF16 */
+  int32_t out_dtype; /* ENL_DTYPE_BF16 or ENL_DTYPE_FP32 */
+  int32_t causal;    /* key allowed only when pos_k <= pos_q */
+  int32_t window;    /* < 0: none; else |pos_q - pos_k| <= window */
+  int32_t mask_mode; /* ENL_MASK_EXCLUDE or ENL_MASK_ADDITIVE */
+  const int32_t* kv_valid_len; /* device (batch,): keys [0, len) are real; NULL = all */
+  const float* alibi_slopes;   /* device (num_heads,): ALiBi slopes; NULL = none */
+  int64_t q_pos0;              /* absolute position of query row 0 */
+  int64_t k_pos0;              /* absolute position of key row 0 */
+  float scale;                 /* softmax scale, normally 1/sqrt(head_dim) */
+} enl_prefill_args;
+
+/* Fused attention prefill: softmax(Q K^T * scale + bias + mask) V.
+ * Replaces the score/softmax/context math of nn/forward.py:525-551 (MHA),
+ * nn/flash_attention.py:42-80 (tiled softmax), nn/forward.py:578-586 (cross
+ * attention), the cached multi-token step nn/kvcache.py:198-213, and the
+ * key-padding rule of graph/sequence.py:159-183. head_dim 64 or 128. */
+int enl_attn_prefill(const enl_prefill_args* args, void* stream);
+
+/* ----------------------------------------------------------------- decode */
+typedef struct enl_decode_args {
+  const void* q; /* (batch, num_heads, head_dim): one query token per row */
+  int64_t q_stride_b, q_stride_h;
+  const void* k_cache; /* (batch, num_kv_heads, capacity, head_dim) */
+  const void* v_cache;
+  int64_t cache_stride_b, cache_stride_h, cache_stride_s; /* shared by K and V */
+  void* o; /* (batch, num_heads, head_dim), out_dtype */
+  int64_t o_stride_b, o_stride_h;
+  float* lse; /* (batch, num_heads) natural-log LSE, or NULL */
+  int32_t batch, num_heads, num_kv_heads, head_dim;
+  int32_t slot_begin, slot_end; /* live cache slots [slot_begin, slot_end) */
+  int64_t pos_slot0;            /* absolute position of cache slot 0 */
+  int64_t q_pos;                /* absolute position of the query token */
+  int32_t window;               /* < 0: none */
+  const float* alibi_slopes;    /* device (num_heads,) or NULL */
+  float scale;
+  int32_t in_dtype, out_dtype;
+  int32_t n_splits; /* KV splits per (batch, kv head); 0 = choose automatically */
+  void* workspace;  /* device scratch, >= enl_decode_workspace_bytes(); may be NULL if 1 split */
+  size_t workspace_bytes;
+} enl_decode_args;
+
+/* Split-KV single-token decode with log-sum-exp merge of the splits.
+ * Replaces the attention half of nn/kvcache.py:_attention_step (lines
+ * 198-213) for one new token; head_dim 64 or 128, num_heads/num_kv_heads in
+ * {1, 2, 4, 8}. */
+int enl_attn_decode(const enl_decode_args* args, void* stream);
+
+/* The split count enl_attn_decode uses for n_splits == 0. */
+int enl_decode_auto_splits(int32_t batch, int32_t num_kv_heads, int32_t n_slots);
+
+/* Scratch bytes enl_attn_decode needs for a given split count. */
+size_t enl_decode_workspace_bytes(int32_t batch, int32_t num_heads, int32_t head_dim,
+                                  int32_t n_splits);
+
+/* Merge n_parts normalised partial outputs (part_o: (n_parts, batch, heads,
+ * head_dim) fp32; part_lse: (n_parts, batch, heads)) by log-sum-exp. Used
+ * after an NCCL all-gather of per-GPU partials in sequence-sharded decode.
+ * No reference counterpart: the reference never splits the KV sequence. */
+int enl_lse_merge(const float* part_o, const float* part_lse, int32_t n_parts, int32_t batch,
+                  int32_t num_heads, int32_t head_dim, void* o, int64_t o_stride_b,
+                  int64_t o_stride_h, int32_t out_dtype, float* lse, void* stream);
+
+/* -------------------------------------------------------------- KV cache */
+/* cache[b, h, slot0 + t, :] = src[b, t, h, :] for t < n_new. Replaces the
+ * whole-cache np.concatenate of nn/kvcache.py:156-162. Fails with
+ * ENL_ERR_INVALID when slot0 + n_new > capacity. */
+int enl_kv_append(void* cache, int64_t cache_stride_b, int64_t cache_stride_h,
+                  int64_t cache_stride_s, const void* src, int64_t src_stride_b,
+                  int64_t src_stride_t, int64_t src_stride_h, int32_t batch,
+                  int32_t num_kv_heads, int32_t n_new, int32_t head_dim, int32_t dtype,
+                  int64_t slot0, int64_t capacity, void* stream);
+
+/* dst[i, h, s, :] = src[index[i], h, s, :] for s in [slot_begin, slot_end).
+ * Replaces KVCache.reorder / expand (nn/kvcache.py:42-66) on device. index is
+ * a device int64 array of batch_out entries; out-of-range entries set the
+ * device error word and are skipped. dst must not alias src. */
+int enl_kv_gather(void* dst, int64_t dst_stride_b, int64_t dst_stride_h, int64_t dst_stride_s,
+                  const void* src, int64_t src_stride_b, int64_t src_stride_h,
+                  int64_t src_stride_s, const int64_t* index, int32_t batch_out,
+                  int32_t batch_src, int32_t num_kv_heads, int32_t slot_begin, int32_t slot_end,
+                  int32_t head_dim, int32_t dtype, void* stream);
+
+/* In-place rotate-half RoPE on x[b, s, h, :] (nn/forward.py:80-88) with
+ * float32 tables cos/sin of shape (table_rows, head_dim/2) computed as
+ * nn/forward.py:46-55 does; sequence row s uses table row table_row0 + s. */
+int enl_rope_apply(void* x, int64_t stride_b, int64_t stride_s, int64_t stride_h, int32_t batch,
+                   int32_t seq, int32_t num_heads, int32_t head_dim, int32_t dtype,
+                   const float* cos_table, const float* sin_table, int64_t table_row0,
+                   int64_t table_rows, void* stream);
+
+/* ------------------------------------------------------------- utilities */
+/* Read (and with clear != 0 reset) the device error word of the current
+ * device. Synchronises the device. *code == 0 means no kernel reported. */
+int enl_device_error(int32_t* code, int32_t* info, int32_t clear);
+
+/* Message for the last failing call on this thread ("" if none). */
+const char* enl_last_error(void);
+
+int enl_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ENL_ATTN_H_ */

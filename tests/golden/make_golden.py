@@ -1,0 +1,289 @@
+"""Generate the golden vectors that pin the oracle (and the kernels) to the
+reference, by running the reference itself.
+
+Run in a container that has the reference checked out:
+
+    PYTHONPATH=/path/to/reference python tests/golden/make_golden.py
+
+(the default path is the reference mount of the build container). Writes
+tests/golden/*.npz. The reference must never be imported at test time; the
+committed .npz files are all the tests use.
+
+Every case runs the reference in float64 (``use_float64(True)``). To expose
+the attention core through the reference's own layer code, the projection
+weights are set to identity and the biases to zero, so a layer's output is
+exactly the concatenated per-head context (nn/forward.py:428-551,
+graph/sequence.py:144-183, nn/kvcache.py:123-214). Inputs of the larger,
+kernel-shaped cases are regenerated from their seeds by
+``oracle.attention_ref.seeded_normal`` and are therefore not stored.
+"""
+from __future__ import annotations
+
+import json
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+sys.path.insert(0, str(REPO))
+REF = os.environ.get("ENILNETS_REFERENCE", "/root/reference")
+sys.path.insert(0, REF)
+
+from oracle.attention_ref import seeded_normal  # noqa: E402
+
+import Enilnets  # noqa: E402
+from Enilnets import NeuralNet  # noqa: E402
+from Enilnets.core import backend  # noqa: E402
+from Enilnets.nn import flash_attention as fa  # noqa: E402
+from Enilnets.nn import kvcache as kvc  # noqa: E402
+from Enilnets.graph import MultiHeadAttention, Tensor, lengths_to_mask  # noqa: E402
+
+backend.use_float64(True)
+
+
+def identity_layer(layer: dict) -> None:
+    E = layer["embed_dim"]
+    kv = layer["num_kv_heads"] * layer["head_dim"]
+    layer["Wq"] = np.eye(E)
+    layer["Wo"] = np.eye(E)
+    layer["Wk"] = np.eye(kv, E)
+    layer["Wv"] = np.eye(kv, E)
+    for b, n in (("bq", E), ("bk", kv), ("bv", kv), ("bo", E)):
+        layer[b] = np.zeros(n)
+
+
+def flash_cases():
+    """nn/flash_attention.py:42-80 on random (B, H, S, D) inputs."""
+    out = {}
+    meta = []
+    rng = np.random.RandomState(1234)
+    i = 0
+    for causal in (False, True):
+        for window in (None, 3):
+            for alibi in (False, True):
+                Q, K, V = (rng.standard_normal((2, 4, 11, 8)) for _ in range(3))
+                slopes = Enilnets.nn.forward._alibi_slopes(4) if alibi else None
+                o, cache = fa.flash_attention_forward(Q, K, V, 4, causal, window, slopes)
+                out[f"q{i}"], out[f"k{i}"], out[f"v{i}"], out[f"o{i}"] = Q, K, V, o
+                out[f"rowmax{i}"], out[f"rowsum{i}"] = cache[4], cache[5]
+                meta.append({"causal": causal, "window": window, "alibi": alibi, "block": 4})
+                i += 1
+    out["meta"] = np.array(json.dumps(meta))
+    np.savez_compressed(HERE / "flash_attention.npz", **out)
+
+
+def mha_layer_cases():
+    """Full MHA layers (nn/forward.py:423-556) with random weights, float64."""
+    out = {}
+    meta = []
+    i = 0
+    configs = [
+        dict(embed_dim=16, num_heads=4, causal=True),
+        dict(embed_dim=16, num_heads=4, causal=False),
+        dict(embed_dim=16, num_heads=4, causal=True, window_size=2),
+        dict(embed_dim=16, num_heads=4, causal=True, positional_scheme="rope"),
+        dict(embed_dim=16, num_heads=4, causal=False, positional_scheme="alibi"),
+        dict(embed_dim=16, num_heads=4, causal=True, positional_scheme="alibi"),
+        dict(embed_dim=16, num_heads=4, causal=True, num_kv_heads=2),
+        dict(embed_dim=16, num_heads=4, causal=True, num_kv_heads=1, window_size=3,
+             positional_scheme="rope"),
+    ]
+    for cfg in configs:
+        Enilnets.core.utils.set_seed(100 + i)
+        m = NeuralNet()
+        m.add_multihead_attention(**cfg)
+        x = np.random.RandomState(200 + i).standard_normal((2, 9, 16))
+        y = m.Forward(x, training=False)
+        layer = m.layers[0]
+        for key in ("Wq", "bq", "Wk", "bk", "Wv", "bv", "Wo", "bo"):
+            out[f"{key}{i}"] = layer[key]
+        out[f"x{i}"], out[f"y{i}"] = x, y
+        meta.append(cfg)
+        i += 1
+    out["meta"] = np.array(json.dumps(meta))
+    np.savez_compressed(HERE / "mha_layer.npz", **out)
+
+
+def graph_padding_cases():
+    """graph.MultiHeadAttention with key_padding_mask (graph/sequence.py:144-183)."""
+    out = {}
+    meta = []
+    i = 0
+    for causal in (False, True):
+        for window in (None, 2):
+            for lengths in ([9, 5, 1], [9, 4, 0]):
+                Enilnets.core.utils.set_seed(300 + i)
+                g = MultiHeadAttention(16, 4, causal=causal, window_size=window)
+                x = np.random.RandomState(400 + i).standard_normal((3, 9, 16))
+                mask = np.asarray(lengths_to_mask(lengths, 9))
+                y = g(Tensor(x), key_padding_mask=mask).data
+                for key in ("Wq", "bq", "Wk", "bk", "Wv", "bv", "Wo", "bo"):
+                    out[f"{key}{i}"] = getattr(g, key).data
+                out[f"x{i}"], out[f"y{i}"], out[f"len{i}"] = x, y, np.array(lengths)
+                meta.append({"causal": causal, "window_size": window, "embed_dim": 16,
+                             "num_heads": 4, "lengths": lengths})
+                i += 1
+    out["meta"] = np.array(json.dumps(meta))
+    np.savez_compressed(HERE / "graph_padding.npz", **out)
+
+
+def cross_cases():
+    """cross_attention layers (nn/forward.py:557-591): Q from a dense layer's
+    output, K/V from the raw network input."""
+    out = {}
+    meta = []
+    for i, hkv in enumerate((None, 2)):
+        Enilnets.core.utils.set_seed(500 + i)
+        m = NeuralNet()
+        m.add_dense(16, 16, activation="linear")
+        m.add_cross_attention(kv_source_index=-1, embed_dim=16, num_heads=4, num_kv_heads=hkv)
+        x = np.random.RandomState(600 + i).standard_normal((2, 7, 16))
+        y = m.Forward(x, training=False)
+        q_in = m.outputs[1]
+        layer = m.layers[1]
+        for key in ("Wq", "bq", "Wk", "bk", "Wv", "bv", "Wo", "bo"):
+            out[f"{key}{i}"] = layer[key]
+        out[f"x{i}"], out[f"qin{i}"], out[f"y{i}"] = x, q_in, y
+        meta.append({"num_kv_heads": hkv, "embed_dim": 16, "num_heads": 4})
+    out["meta"] = np.array(json.dumps(meta))
+    np.savez_compressed(HERE / "cross_layer.npz", **out)
+
+
+def kernel_prefill_cases():
+    """Attention core at kernel shapes (head_dim 64/128), produced by the
+    reference's own layers with identity projections. Inputs come from
+    seeded_normal(seed, (B, S, E)) and are not stored."""
+    out = {}
+    meta = []
+    cases = [
+        dict(kind="nn", B=1, S=160, H=2, D=64, causal=True, window=None, scheme="absolute"),
+        dict(kind="nn", B=1, S=160, H=2, D=64, causal=False, window=None, scheme="absolute"),
+        dict(kind="nn", B=1, S=200, H=1, D=128, causal=True, window=None, scheme="absolute"),
+        dict(kind="nn", B=1, S=160, H=2, D=64, causal=True, window=40, scheme="alibi"),
+        dict(kind="nn", B=1, S=130, H=2, D=64, causal=False, window=None, scheme="alibi"),
+        dict(kind="graph", B=2, S=150, H=2, D=64, causal=True, window=None,
+             lengths=[150, 70]),
+        dict(kind="graph", B=2, S=150, H=2, D=64, causal=False, window=None,
+             lengths=[131, 0]),
+        dict(kind="graph", B=2, S=150, H=2, D=64, causal=True, window=20,
+             lengths=[150, 90]),
+    ]
+    for i, c in enumerate(cases):
+        seed = 700 + i
+        E = c["H"] * c["D"]
+        x = seeded_normal(seed, (c["B"], c["S"], E))
+        if c["kind"] == "nn":
+            m = NeuralNet()
+            m.add_multihead_attention(embed_dim=E, num_heads=c["H"], causal=c["causal"],
+                                      window_size=c["window"], positional_scheme=c["scheme"])
+            identity_layer(m.layers[0])
+            y = m.Forward(x, training=False)
+        else:
+            g = MultiHeadAttention(E, c["H"], causal=c["causal"], window_size=c["window"])
+            for name, n_out in (("Wq", E), ("Wk", E), ("Wv", E), ("Wo", E)):
+                getattr(g, name).data = np.eye(n_out, E)
+                getattr(g, "b" + name[1:].lower()).data = np.zeros(n_out)
+            mask = np.asarray(lengths_to_mask(c["lengths"], c["S"]))
+            y = g(Tensor(x), key_padding_mask=mask).data
+        out[f"y{i}"] = y.astype(np.float32)
+        meta.append(dict(c, seed=seed))
+    out["meta"] = np.array(json.dumps(meta))
+    np.savez_compressed(HERE / "kernel_prefill.npz", **out)
+
+
+def kernel_decode_cases():
+    """One-token cached steps through nn/kvcache.py:_attention_step at kernel
+    shapes, identity projections: the new token's q = k = v = x, the cache is
+    seeded N(0,1) (bf16-rounded) K/V."""
+    out = {}
+    meta = []
+    cases = [
+        dict(B=2, H=2, Hkv=2, D=64, ctx=300, scheme="absolute", window=None),
+        dict(B=2, H=4, Hkv=2, D=64, ctx=257, scheme="alibi", window=None),
+        dict(B=1, H=2, Hkv=2, D=128, ctx=200, scheme="absolute", window=64),
+        dict(B=2, H=4, Hkv=1, D=64, ctx=129, scheme="absolute", window=None),
+    ]
+    for i, c in enumerate(cases):
+        seed = 800 + i
+        B, H, Hkv, D, ctx = c["B"], c["H"], c["Hkv"], c["D"], c["ctx"]
+        E = H * D
+        m = NeuralNet()
+        m.add_multihead_attention(embed_dim=E, num_heads=H, causal=True, num_kv_heads=Hkv,
+                                  window_size=c["window"], positional_scheme=c["scheme"])
+        layer = m.layers[0]
+        identity_layer(layer)
+        Kc = seeded_normal(seed, (B, Hkv, ctx, D))
+        Vc = seeded_normal(seed + 1000, (B, Hkv, ctx, D))
+        x = seeded_normal(seed + 2000, (B, 1, E))
+        cache = kvc.KVCache()
+        cache.kv[0] = (Kc, Vc, 0)
+        y = kvc._attention_step(layer, x, 0, cache, B, 1, ctx)
+        out[f"y{i}"] = y.astype(np.float32)
+        out[f"start{i}"] = np.array(cache.kv[0][2])
+        out[f"len{i}"] = np.array(cache.kv[0][0].shape[2])
+        meta.append(dict(c, seed=seed))
+    out["meta"] = np.array(json.dumps(meta))
+    np.savez_compressed(HERE / "kernel_decode.npz", **out)
+
+
+def kvcache_cases():
+    """Token-by-token and primed stepping through cached_forward_step of a
+    small causal stack (nn/kvcache.py:69-120) against its full Forward."""
+    out = {}
+    meta = []
+    i = 0
+    for scheme in ("absolute", "rope", "alibi"):
+        for hkv, window in ((None, None), (1, 2)):
+            Enilnets.core.utils.set_seed(900 + i)
+            m = NeuralNet()
+            m.add_embedding(vocab_size=17, embed_dim=8)
+            if scheme == "absolute":
+                m.add_positional_encoding(max_seq_len=32, learnable=False)
+            m.add_transformer_block(8, num_heads=2, causal=True, positional_scheme=scheme,
+                                    num_kv_heads=hkv, window_size=window)
+            m.add_layernorm()
+            m.add_dense(n_out=17, activation="linear")
+            toks = np.random.RandomState(950 + i).randint(0, 17, size=(3, 6))
+            full = m.Forward(toks, training=False)
+            cache = kvc.KVCache()
+            pieces = [kvc.cached_forward_step(m, toks[:, :4], cache)]
+            pieces += [kvc.cached_forward_step(m, toks[:, j:j + 1], cache) for j in (4, 5)]
+            stepped = np.concatenate(pieces, axis=1)
+            out[f"toks{i}"], out[f"full{i}"], out[f"stepped{i}"] = toks, full, stepped
+            attn_idx = [j for j, l in enumerate(m.layers) if l["type"] == "multihead_attention"][0]
+            out[f"kshape{i}"] = np.array(cache.kv[attn_idx][0].shape)
+            out[f"start{i}"] = np.array(cache.kv[attn_idx][2])
+            layers = []
+            for j, l in enumerate(m.layers):
+                rec = {k: v for k, v in l.items() if not isinstance(v, np.ndarray)
+                       and k not in ("sparse_pattern",) and not k.startswith("_")
+                       and isinstance(v, (int, float, str, bool, type(None), tuple, list))}
+                rec["_pos_type"] = l.get("_pos_type")
+                layers.append(rec)
+                for k, v in l.items():
+                    if isinstance(v, np.ndarray):
+                        out[f"L{i}_{j}_{k}"] = v
+            meta.append({"scheme": scheme, "num_kv_heads": hkv, "window_size": window,
+                         "layers": layers})
+            i += 1
+    out["meta"] = np.array(json.dumps(meta, default=str))
+    np.savez_compressed(HERE / "kvcache_stepping.npz", **out)
+
+
+def main():
+    flash_cases()
+    mha_layer_cases()
+    graph_padding_cases()
+    cross_cases()
+    kernel_prefill_cases()
+    kernel_decode_cases()
+    kvcache_cases()
+    for p in sorted(HERE.glob("*.npz")):
+        print(p.name, p.stat().st_size)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,102 @@
+"""C-ABI checks that need no GPU: the library loads, exports every function
+include/enl_attn.h declares, the ctypes binding covers them all, the ctypes
+struct layouts match the C compiler's, and argument validation rejects bad
+calls before anything is launched."""
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from enilnets_b200 import _native
+
+REPO = Path(__file__).resolve().parent.parent
+HEADER = REPO / "include" / "enl_attn.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(enl_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_expected_entry_points():
+    names = declared_functions()
+    for must in ("enl_attn_prefill", "enl_attn_decode", "enl_kv_append", "enl_kv_gather",
+                 "enl_lse_merge", "enl_rope_apply", "enl_last_error", "enl_device_error"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _native.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} declared in enl_attn.h but not exported"
+        assert name in _native.SIGNATURES, f"{name} has no ctypes signature"
+    assert lib.enl_abi_version() == 1
+
+
+def test_nm_shows_c_linkage():
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_native.LIB_PATH)],
+                         capture_output=True, text=True, check=True).stdout
+    exported = set(re.findall(r" T (enl_\w+)$", out, flags=re.M))
+    assert set(declared_functions()) <= exported
+
+
+def _c_offsets(struct, fields):
+    src = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(){"]
+    src.append(f'printf("%zu\\n", sizeof({struct}));')
+    for f in fields:
+        src.append(f'printf("%zu\\n", offsetof({struct}, {f}));')
+    src.append("return 0;}")
+    tmp = Path(subprocess.run(["mktemp", "-d"], capture_output=True, text=True).stdout.strip())
+    c = tmp / "layout.c"
+    c.write_text("\n".join(src))
+    subprocess.run(["gcc", "-o", str(tmp / "layout"), str(c)], check=True)
+    vals = [int(x) for x in subprocess.run([str(tmp / "layout")], capture_output=True,
+                                           text=True, check=True).stdout.split()]
+    return vals[0], vals[1:]
+
+
+@pytest.mark.parametrize("cls,cname", [(_native.PrefillArgs, "enl_prefill_args"),
+                                       (_native.DecodeArgs, "enl_decode_args")])
+def test_ctypes_struct_layout_matches_c(cls, cname):
+    fields = [f for f, _ in cls._fields_]
+    size, offsets = _c_offsets(cname, fields)
+    assert ctypes.sizeof(cls) == size
+    for f, off in zip(fields, offsets):
+        assert getattr(cls, f).offset == off, f
+
+
+def test_validation_errors_raise_before_launch():
+    """Argument errors come back as a status (ValueError in Python) without
+    touching the device: NULL pointers and unsupported head dims."""
+    lib = _native.load()
+    a = _native.PrefillArgs()
+    with pytest.raises(ValueError, match="non-NULL"):
+        _native.check(lib.enl_attn_prefill(ctypes.byref(a), None), "enl_attn_prefill")
+    a.q = a.k = a.v = a.o = 16
+    a.batch = a.num_heads = a.num_kv_heads = a.seq_q = a.seq_kv = 1
+    a.head_dim = 96
+    with pytest.raises(ValueError, match="head_dim=96"):
+        _native.check(lib.enl_attn_prefill(ctypes.byref(a), None), "enl_attn_prefill")
+    a.head_dim = 64
+    a.num_kv_heads = 3
+    a.num_heads = 4
+    with pytest.raises(ValueError, match="must divide"):
+        _native.check(lib.enl_attn_prefill(ctypes.byref(a), None), "enl_attn_prefill")
+    d = _native.DecodeArgs()
+    with pytest.raises(ValueError):
+        _native.check(lib.enl_attn_decode(ctypes.byref(d), None), "enl_attn_decode")
+    with pytest.raises(ValueError, match="exceed capacity"):
+        _native.check(lib.enl_kv_append(16, 0, 0, 0, 16, 0, 0, 0, 1, 1, 4, 64, 0, 6, 8, None),
+                      "enl_kv_append")
+
+
+def test_decode_split_heuristic():
+    lib = _native.load()
+    assert lib.enl_decode_auto_splits(64, 32, 8193) == 3
+    assert lib.enl_decode_auto_splits(4, 32, 262145) == 37
+    assert lib.enl_decode_auto_splits(1, 1, 10) == 1
+    assert lib.enl_decode_workspace_bytes(2, 4, 128, 1) == 0
+    assert lib.enl_decode_workspace_bytes(2, 4, 128, 3) == 3 * 2 * 4 * 129 * 4
