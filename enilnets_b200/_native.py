@@ -74,6 +74,7 @@ class DecodeArgs(Structure):
 SIGNATURES = {
     "enl_attn_prefill": ([POINTER(PrefillArgs), c_void_p], c_int32),
     "enl_attn_decode": ([POINTER(DecodeArgs), c_void_p], c_int32),
+    "enl_attn_decode_noalloc": ([POINTER(DecodeArgs), c_void_p], c_int32),
     "enl_decode_auto_splits": ([c_int32, c_int32, c_int32], c_int32),
     "enl_decode_workspace_bytes": ([c_int32, c_int32, c_int32, c_int32], c_size_t),
     "enl_lse_merge": ([c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p,

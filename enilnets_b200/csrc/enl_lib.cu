@@ -5,3 +5,4 @@
 #include "enl_prefill.cu"
 #include "enl_decode.cu"
 #include "enl_kvcache.cu"
+#include "enl_decode_noalloc.cu"

@@ -104,6 +104,22 @@ typedef struct enl_decode_args {
  * {1, 2, 4, 8}. */
 int enl_attn_decode(const enl_decode_args* args, void* stream);
 
+/* Scratch held by enl_attn_decode_noalloc on every device that loads the library. */
+#define ENL_DECODE_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+/* enl_attn_decode for callers that cannot allocate device memory: a host
+ * that owns all device memory and gives plugins no allocation hook, or a
+ * token loop where a cudaMalloc (which may synchronise the device) is not
+ * allowed. Same arguments and results as enl_attn_decode; args->workspace is
+ * ignored and the split partials go to a fixed scratch array inside the
+ * library (ENL_DECODE_NOALLOC_SCRATCH_BYTES per device, kept until exit).
+ * Requests whose partials would not fit are rejected with ENL_ERR_INVALID.
+ * The first call on a device looks up the scratch address, so make it before
+ * any stream capture. All calls on a device share the scratch: calls whose
+ * kernels overlap on the GPU race and must be ordered on one stream.
+ * No counterpart in the reference, which never splits the key sequence. */
+int enl_attn_decode_noalloc(const enl_decode_args* args, void* stream);
+
 /* The split count enl_attn_decode uses for n_splits == 0. */
 int enl_decode_auto_splits(int32_t batch, int32_t num_kv_heads, int32_t n_slots);
 
