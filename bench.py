@@ -202,14 +202,15 @@ def timed(dist: Dist, clocks: ClockSampler, fn, steps: int) -> float:
 
 
 # ------------------------------------------------------------- workloads
-def bench_prefill(dist: Dist, clocks: ClockSampler, steps: int, warmup: int):
+def bench_prefill(dist: Dist, clocks: ClockSampler, steps: int, warmup: int, batch: int = 0,
+                  e2e_on: bool = True):
     import torch
     from enilnets_b200 import kernels, _native
-    B, S, H, D = CFG2["B"], CFG2["S"], CFG2["H"], CFG2["D"]
+    B, S, H, D = batch or CFG2["B"], CFG2["S"], CFG2["H"], CFG2["D"]
     g = torch.Generator(device=dist.device).manual_seed(1000 + dist.rank)
     q, k, v = (torch.randn((B, S, H, D), generator=g, device=dist.device).to(torch.bfloat16)
                for _ in range(3))
-    lengths = cfg2_lengths(dist.rank)
+    lengths = cfg2_lengths(dist.rank)[:B]
     lens = torch.tensor(lengths, dtype=torch.int32, device=dist.device)
     out = torch.empty((B, S, H, D), dtype=torch.bfloat16, device=dist.device)
 
@@ -227,6 +228,9 @@ def bench_prefill(dist: Dist, clocks: ClockSampler, steps: int, warmup: int):
     ms_step = ms / steps
     value = flops_total / (ms_step * 1e-3) / 1e12
 
+    if not e2e_on:
+        return dict(value=value, ms_step=ms_step, flops_rank=flops_rank, flops_total=flops_total,
+                    e2e=None, lengths=[int(x) for x in lengths], per_launch_ms=ms_step)
     # End to end: host (pinned) inputs -> H2D -> kernel -> D2H of the output,
     # through the same public call, every step.
     hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
@@ -253,11 +257,11 @@ def bench_prefill(dist: Dist, clocks: ClockSampler, steps: int, warmup: int):
                 e2e=e2e, lengths=[int(x) for x in lengths], per_launch_ms=ms_step)
 
 
-def bench_decode_cfg3(dist: Dist, clocks: ClockSampler, warmup: int):
+def bench_decode_cfg3(dist: Dist, clocks: ClockSampler, warmup: int, batch: int = 0):
     """Batch rows split across ranks (64 / N per GPU)."""
     import torch
     from enilnets_b200 import kernels, _native
-    Btot, H, D, ctx, T = CFG3["B"], CFG3["H"], CFG3["D"], CFG3["ctx"], CFG3["steps"]
+    Btot, H, D, ctx, T = batch or CFG3["B"], CFG3["H"], CFG3["D"], CFG3["ctx"], CFG3["steps"]
     if Btot % dist.world:
         return {"skipped": f"batch {Btot} not divisible by {dist.world} ranks"}
     B = Btot // dist.world
@@ -431,6 +435,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--skip-sub", action="store_true", help="headline only")
+    ap.add_argument("--only", choices=["all", "prefill", "decode", "longctx"], default="all",
+                    help="profiling: run one workload")
+    ap.add_argument("--batch", type=int, default=0, help="profiling: prefill batch override")
+    ap.add_argument("--decode-batch", type=int, default=0,
+                    help="profiling: cfg3 decode batch override")
+    ap.add_argument("--no-e2e", action="store_true", help="profiling: skip the e2e leg")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -444,10 +454,24 @@ def main():
     clocks = ClockSampler(dist.local_rank)
     clocks.start()
     try:
-        pre = bench_prefill(dist, clocks, args.steps, args.warmup)
+        if args.only != "all":
+            res = {}
+            if args.only == "prefill":
+                res = bench_prefill(dist, clocks, args.steps, args.warmup, args.batch,
+                                    e2e_on=False)
+            elif args.only == "decode":
+                res = bench_decode_cfg3(dist, clocks, args.warmup, args.decode_batch)
+            else:
+                res = bench_longctx_cfg5(dist, clocks, args.warmup)
+            if dist.rank == 0:
+                print(json.dumps({"profiling_only": args.only, **res}))
+            dist.close()
+            return 0
+        pre = bench_prefill(dist, clocks, args.steps, args.warmup, args.batch,
+                            e2e_on=not args.no_e2e)
         sub = {}
         if not args.skip_sub:
-            sub["decode_cfg3"] = bench_decode_cfg3(dist, clocks, args.warmup)
+            sub["decode_cfg3"] = bench_decode_cfg3(dist, clocks, args.warmup, args.decode_batch)
             sub["longctx_cfg5"] = bench_longctx_cfg5(dist, clocks, args.warmup)
     finally:
         clocks.stop()
