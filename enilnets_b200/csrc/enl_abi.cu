@@ -139,8 +139,9 @@ int enl_attn_prefill(const enl_prefill_args* a, void* stream) {
   if ((st = check_strides_16B("o", a->o_stride_b, a->o_stride_s, a->o_stride_h,
                               a->out_dtype == ENL_DTYPE_FP32 ? 4 : 2)))
     return st;
-  if ((long long)((a->seq_q + 255) / 256) > 65535)
-    return fail(ENL_ERR_UNSUPPORTED, "enl_attn_prefill: seq_q=%d too long", a->seq_q);
+  if ((long long)a->batch * a->num_heads > 65535)
+    return fail(ENL_ERR_UNSUPPORTED, "enl_attn_prefill: batch*num_heads=%lld exceeds 65535",
+                (long long)a->batch * a->num_heads);
 
   const int D = a->head_dim;
   CUtensorMap tq, tk, tv;

@@ -171,6 +171,53 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
       : "memory");
 }
 
+// MMAs issued from a warp-uniform loop: every lane of the MMA warp computes
+// the same descriptor words (so they stay in uniform registers) and
+// elect.sync picks the one lane that issues. The descriptor high word
+// (stride offset, version, swizzle) is loop-invariant and the low word
+// (start address, leading offset) advances by immediates.
+template <bool kAccumulate>
+__device__ __forceinline__ void umma_ss_elect(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo,
+                                              uint32_t desc_hi, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "mov.b64 da, {%1, %3};\n\t"
+      "mov.b64 db, {%2, %3};\n\t"
+      "@p tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, %5;\n\t}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(b_lo), "r"(desc_hi), "r"(idesc), "n"(kAccumulate ? 1 : 0)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_ts_elect(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo,
+                                              uint32_t desc_hi, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, acc;\n\t.reg .b64 db;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "mov.b64 db, {%2, %3};\n\t"
+      "setp.ne.b32 acc, %5, 0;\n\t"
+      "@p tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, acc;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(desc_hi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// tcgen05.commit by one elected lane of a converged warp.
+__device__ __forceinline__ void umma_commit_elect(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\t"
+      "@p tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+// High word of a SW128 descriptor with a 1024-byte stride offset.
+constexpr uint32_t kDescHiSw128 = (1024u >> 4) | (1u << 14) | (2u << 29);
+// Low word: start address and leading byte offset.
+__device__ __forceinline__ uint32_t desc_lo(uint32_t saddr, uint32_t lbo_bytes) {
+  return ((saddr >> 4) & 0x3FFFu) | ((lbo_bytes >> 4) << 16);
+}
+
 // Arrive on `bar` once every tcgen05.mma issued so far by this thread is done.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile(
@@ -219,6 +266,12 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
       "tcgen05.wait::ld.sync.aligned;"                                                       \
       : ENL_R32(a, 0), ENL_R32(a, 32), ENL_R32(a, 64), ENL_R32(a, 96)                        \
       : "r"(taddr)                                                                           \
+      : "memory")
+
+#define ENL_TMEM_ST64(taddr, a)                                                              \
+  asm volatile(                                                                              \
+      "tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63, %64};"                              \
+      ::"r"(taddr), ENL_W32(a, 0), ENL_W32(a, 32)                                           \
       : "memory")
 
 #define ENL_TMEM_ST32(taddr, a, o)                                                           \
@@ -270,6 +323,75 @@ __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Three-input maximum (sm_100 PTX).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Packed fp32 pairs on the FMA pipe (sm_100 f32x2 instructions).
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// 2^x on the FMA/ALU pipes, for x in (-inf, 8]: round-to-nearest range
+// reduction x = n + f, f in [-0.5, 0.5], via the 1.5 * 2^23 magic constant,
+// then a cubic for 2^f whose coefficients minimise the relative error on that
+// interval (Lawson-weighted least squares; max relative error 7.6e-5, well
+// under the 2^-9 of the bf16 P it feeds), then n is added to the exponent.
+// Inputs below -125 are clamped (results ~1e-38 instead of 0); only used on
+// tiles with no masked scores.
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -125.0f);
+  const float t = x + 12582912.0f;
+  const float f = x - (t - 12582912.0f);
+  float p = fmaf(0.05522262f, f, 0.24261537f);
+  p = fmaf(p, f, 0.6932516f);
+  p = fmaf(p, f, 0.9999276f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+// exp2_poly on a packed pair: the range reduction and the cubic run as f32x2
+// instructions (half the issue slots of the scalar form).
+__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float& y1) {
+  const uint64_t magic = f2_pack(12582912.0f, 12582912.0f);
+  const uint64_t neg_magic = f2_pack(-12582912.0f, -12582912.0f);
+  const uint64_t x = f2_pack(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
+  const uint64_t t = f2_add(x, magic);
+  float n0, n1;
+  f2_unpack(f2_add(t, neg_magic), n0, n1);
+  const uint64_t f = f2_add(x, f2_pack(-n0, -n1));
+  uint64_t p = f2_fma(f2_pack(0.05522262f, 0.05522262f), f, f2_pack(0.24261537f, 0.24261537f));
+  p = f2_fma(p, f, f2_pack(0.6932516f, 0.6932516f));
+  p = f2_fma(p, f, f2_pack(0.9999276f, 0.9999276f));
+  float p0, p1, t0, t1;
+  f2_unpack(p, p0, p1);
+  f2_unpack(t, t0, t1);
+  y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

@@ -5,18 +5,30 @@
 // (streaming softmax, the algorithmic spec followed here), nn/forward.py:578-586
 // (cross-attention) and the key-padding rule of graph/sequence.py:159-183.
 //
-// One CTA (three warpgroups, 384 threads) owns two 128-row query tiles (A, B)
-// of one (batch, head) and streams 128-key tiles of K and V through shared
-// memory:
-//   warp 8      TMA producer: Q tiles once, then K/V tiles into a ring of stages
-//   warp 9      MMA issuer: S = Q K^T (smem x smem) and O += P V (P from TMEM)
+// One CTA (three warpgroups, 384 threads) owns one 128-row query tile of one
+// (batch, head) and streams 128-key tiles of K and V through shared memory:
+//   warp 8      TMA producer: the Q tile once, then K/V tiles into a ring
+//   warp 9      MMA issuer (warp-uniform loop, elect.sync issue):
+//               S = Q K^T (smem x smem) into a double-buffered S in tensor
+//               memory, O += P V with P read from tensor memory
 //   warps 10-11 idle members of the producer warpgroup
-//   warps 0-3   softmax for tile A, warps 4-7 softmax for tile B: each thread
-//               owns one query row == one TMEM lane, so row max / row sum need
-//               no shuffles; P is written back into TMEM over the S columns.
-// Tensor memory per CTA: S_A | S_B | O_A | O_B (128 + 128 + D + D columns).
-// The online softmax rescales O lazily: only when a row max grows by more
-// than 2^8 does the thread pull O out of TMEM, scale and store it back.
+//   warps 0-3   softmax, key columns 0-63 of every key tile
+//   warps 4-7   softmax, key columns 64-127
+// Thread (warp w, lane l) owns query row 32*(w%4) + l == TMEM lane. The two
+// softmax warpgroups are independent online-softmax streams over the two
+// halves of every key tile, each with its own running max, sum and output
+// accumulator (O0 over keys 64t..64t+63, O1 over keys 64t+64..64t+127 of
+// tile t); the epilogue merges them by log-sum-exp. No per-tile exchange is
+// needed, so the two warps that share an SMSP drift apart and interleave
+// their MUFU-bound exponential phases with each other's other work.
+//
+// Tensor memory: S0 | S1 | O0 | O1 (128 + 128 + D + D columns). S is double
+// buffered, so the MMA warp computes S(j+1) while the softmax works on S(j);
+// each softmax half writes its bf16 P back over the first 32 columns of its
+// own half of S(j), and O_h += P_h V_h runs as soon as that half is
+// published. The online softmax rescales O lazily: only when a row max grows
+// by more than 2^8 does a thread pull its accumulator out of tensor memory,
+// scale and store it back.
 //
 // Masking semantics (see PrefillParams): causal / sliding window / per-batch
 // key-valid length / ALiBi, either with -inf exclusion (nn/ path) or with the
@@ -27,33 +39,36 @@
 
 namespace enl {
 
+// One in kEmuEvery score pairs of an unmasked tile takes its exponentials
+// from exp2_poly (FMA pipe) instead of MUFU ex2; 0 disables the split.
+#ifndef ENL_EXP_EMU_EVERY
+#define ENL_EXP_EMU_EVERY 4
+#endif
+constexpr int kEmuEvery = ENL_EXP_EMU_EVERY;
+
+#ifndef ENL_STAGGER
+#define ENL_STAGGER 0
+#endif
+
 template <int D>
 struct PrefillCfg {
   static constexpr int kThreads = 384;
-  // Register split (setmaxnreg): the launch holds kLaunchRegs * 384 registers;
-  // the producer warpgroup gives some up so the two softmax warpgroups can
-  // keep a full 128-score row in registers. 2*128*216 + 128*56 <= 168*384.
-  static constexpr int kLaunchRegs = 168;
-  static constexpr int kSoftmaxRegs = 216;
-  static constexpr int kProducerRegs = 56;
-  static_assert(2 * 128 * kSoftmaxRegs + 128 * kProducerRegs <= kLaunchRegs * kThreads,
-                "register split exceeds the launch allocation");
-  static constexpr int kBlockM = 128;
-  static constexpr int kBlockN = 128;
   static constexpr int kStages = (D == 128) ? 2 : 4;
   static constexpr int kAtoms = D / 64;  // 128-byte swizzle atoms along the head dim
-  static constexpr int kTileBytes = kBlockN * D * 2;
+  static constexpr int kTileBytes = 128 * D * 2;
   static constexpr int kAtomBytes = 128 * 128;  // 128 rows x 128 bytes
   static constexpr int kOffQ = 0;
-  static constexpr int kOffK = kOffQ + 2 * kTileBytes;
+  static constexpr int kOffK = kOffQ + kTileBytes;
   static constexpr int kOffV = kOffK + kStages * kTileBytes;
-  static constexpr int kOffBar = kOffV + kStages * kTileBytes;
-  static constexpr int kNumBars = 1 + 4 * kStages + 2 + 2 + 2 + 1;
+  static constexpr int kOffX = kOffV + kStages * kTileBytes;  // epilogue exchange
+  static constexpr int kXBytes = 3 * 2 * 128 * 4;              // m, l, tier [2 halves][128]
+  static constexpr int kOffBar = kOffX + kXBytes;
+  // q, k_full/empty, v_full/empty, s_full[2], p_ready[2 buf][2 half], o_prog[2], o_done, drain
+  static constexpr int kNumBars = 1 + 4 * kStages + 2 + 4 + 2 + 1 + 1;
   static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;  // +align slack
   static constexpr uint32_t kTmemCols = 512;
-  // Tensor-memory columns: S/P of tile x at 128*x, O of tile x at 256 + D*x.
-  __host__ __device__ static constexpr uint32_t col_s(int x) { return 128u * x; }
-  __host__ __device__ static constexpr uint32_t col_o(int x) { return 256u + D * x; }
+  __host__ __device__ static constexpr uint32_t col_s(int buf) { return 128u * buf; }
+  __host__ __device__ static constexpr uint32_t col_o(int half) { return 256u + D * half; }
 };
 
 struct RowBounds {
@@ -74,11 +89,6 @@ __device__ __forceinline__ RowBounds row_bounds(const PrefillParams& p, long lon
 // has at least one unmasked key (then -1e9 and -inf masking agree exactly).
 __device__ __forceinline__ void tile_range(const PrefillParams& p, int r0, int lkey, int n_ktiles,
                                            int& lo, int& hi, bool& safe) {
-  if (r0 >= p.Sq) {
-    lo = hi = 0;
-    safe = true;
-    return;
-  }
   const int r1 = min(r0 + 128, p.Sq) - 1;
   const RowBounds first = row_bounds(p, r0), last = row_bounds(p, r1);
   safe = (lkey > 0) && (first.jhi >= 0) && (last.jlo <= lkey - 1);
@@ -97,6 +107,10 @@ __device__ __forceinline__ void tile_range(const PrefillParams& p, int r0, int l
   hi = (int)(khi / 128) + 1;
 }
 
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 template <int D>
 __global__ void __launch_bounds__(384, 1)
     attn_prefill_sm100(const __grid_constant__ CUtensorMap tm_q,
@@ -106,48 +120,46 @@ __global__ void __launch_bounds__(384, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
+  float* x_m = reinterpret_cast<float*>(smem + Cfg::kOffX);  // [2 half][128]
+  float* x_l = x_m + 2 * 128;                                    // [2 half][128]
+  int* x_t = reinterpret_cast<int*>(x_l + 2 * 128);              // [2 half][128]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
   uint64_t* bar_q = bars + 0;
   uint64_t* bar_k_full = bars + 1;
   uint64_t* bar_k_empty = bar_k_full + Cfg::kStages;
   uint64_t* bar_v_full = bar_k_empty + Cfg::kStages;
   uint64_t* bar_v_empty = bar_v_full + Cfg::kStages;
-  uint64_t* bar_s_full = bar_v_empty + Cfg::kStages;  // [2]
-  uint64_t* bar_p_ready = bar_s_full + 2;             // [2]
-  uint64_t* bar_o_done = bar_p_ready + 2;             // [2]
-  uint64_t* bar_drain = bar_o_done + 2;               // [1]
+  uint64_t* bar_s_full = bar_v_empty + Cfg::kStages;  // [2 buffers]
+  uint64_t* bar_p_ready = bar_s_full + 2;             // [2 buffers][2 halves]
+  uint64_t* bar_o_prog = bar_p_ready + 4;             // [2 halves] one phase per P V
+  uint64_t* bar_o_done = bar_o_prog + 2;
+  uint64_t* bar_drain = bar_o_done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int bh = blockIdx.x;
+  // Query tiles of one (batch, head) are adjacent CTAs, heaviest first, so
+  // the K/V rows they all read are still in L2 when the next one runs.
+  const int bh = blockIdx.y;
+  const int qt = (int)gridDim.x - 1 - (int)blockIdx.x;
   const int b = bh / p.H;
   const int h = bh % p.H;
   const int hkv = h / (p.H / p.Hkv);
-  const int pair = (int)gridDim.y - 1 - (int)blockIdx.y;  // heaviest causal pairs first
-  const int r0_tile[2] = {pair * 256, pair * 256 + 128};
+  const int r0 = qt * 128;
 
   const int n_ktiles = (p.Skv + 127) / 128;
   int lkey = p.Skv;
   if (p.kv_len != nullptr) lkey = max(0, min(p.kv_len[b], p.Skv));
-  int lo_x[2], hi_x[2];
-  bool safe_x[2];
-  tile_range(p, r0_tile[0], lkey, n_ktiles, lo_x[0], hi_x[0], safe_x[0]);
-  tile_range(p, r0_tile[1], lkey, n_ktiles, lo_x[1], hi_x[1], safe_x[1]);
-  int lo = n_ktiles, hi = 0;
-  for (int x = 0; x < 2; ++x) {
-    if (lo_x[x] < hi_x[x]) {
-      lo = min(lo, lo_x[x]);
-      hi = max(hi, hi_x[x]);
-    }
-  }
+  int lo, hi;
+  bool safe;
+  tile_range(p, r0, lkey, n_ktiles, lo, hi, safe);
   const bool any_work = lo < hi;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < Cfg::kNumBars; ++i) {
       uint32_t count = 1;
-      if (bars + i == bar_p_ready || bars + i == bar_p_ready + 1) count = 4;
+      if (bars + i >= bar_p_ready && bars + i < bar_p_ready + 4) count = 4;  // one per warp
       mbar_init(bars + i, count);
     }
     *abort_flag = 0;
@@ -161,19 +173,15 @@ __global__ void __launch_bounds__(384, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp >= 8) {
-   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Cfg::kProducerRegs));
-   if (warp == 8) {
+  if (warp == 8) {
     // ------------------------------------------------------------------ TMA
     if (lane == 0 && any_work) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      mbar_arrive_expect_tx(bar_q, 2 * Cfg::kTileBytes);
-      for (int x = 0; x < 2; ++x)
-        for (int a = 0; a < Cfg::kAtoms; ++a)
-          tma_load_4d(smem + Cfg::kOffQ + x * Cfg::kTileBytes + a * Cfg::kAtomBytes, &tm_q, bar_q,
-                      a * 64, r0_tile[x], h, b);
+      mbar_arrive_expect_tx(bar_q, Cfg::kTileBytes);
+      for (int a = 0; a < Cfg::kAtoms; ++a)
+        tma_load_4d(smem + Cfg::kOffQ + a * Cfg::kAtomBytes, &tm_q, bar_q, a * 64, r0, h, b);
       int issued = 0, issued_v = 0;
       bool ok = true;
       for (int j = lo; j < hi && ok; ++j, ++issued) {
@@ -210,147 +218,158 @@ __global__ void __launch_bounds__(384, 1)
     __syncwarp();
   } else if (warp == 9) {
     // ------------------------------------------------------------------ MMA
-    if (lane == 0 && any_work) {
+    // The whole warp runs this loop with warp-uniform values; elect.sync
+    // inside the issue helpers picks the single lane that issues.
+    if (any_work) {
       const uint32_t idesc_s = idesc_bf16_f32(128, 128, false);
       const uint32_t idesc_o = idesc_bf16_f32(128, D, true);
-      const uint32_t sQ = smem_u32(smem + Cfg::kOffQ);
-      const uint32_t sK = smem_u32(smem + Cfg::kOffK);
-      const uint32_t sV = smem_u32(smem + Cfg::kOffV);
-      auto active = [&](int x, int j) { return j >= lo_x[x] && j < hi_x[x]; };
-      auto issue_s = [&](int x, int st) {
-        const uint32_t qa = sQ + x * Cfg::kTileBytes;
-        const uint32_t ka = sK + st * Cfg::kTileBytes;
+      // Descriptor low words, computed once; each MMA adds an immediate
+      // (16-byte units) for its K step.
+      const uint32_t q_lo = desc_lo(smem_u32(smem + Cfg::kOffQ), 16);
+      const uint32_t k_lo = desc_lo(smem_u32(smem + Cfg::kOffK), 16);
+      const uint32_t v_lo = desc_lo(smem_u32(smem + Cfg::kOffV), Cfg::kAtomBytes);
+      constexpr uint32_t kTileLo = Cfg::kTileBytes >> 4;
+      auto issue_s = [&](int buf, int st) {
+        const uint32_t ka = k_lo + st * kTileLo;
+        const uint32_t d = tmem_base + Cfg::col_s(buf);
+        umma_ss_elect<false>(d, q_lo, ka, kDescHiSw128, idesc_s);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk / 4) * Cfg::kAtomBytes + (kk % 4) * 32;
-          umma_ss(tmem_base + Cfg::col_s(x), smem_desc_sw128(qa + off, 16, 1024),
-                  smem_desc_sw128(ka + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+        for (int kk = 1; kk < D / 16; ++kk) {
+          const uint32_t off = (kk / 4) * (Cfg::kAtomBytes >> 4) + (kk % 4) * 2;
+          umma_ss_elect<true>(d, q_lo + off, ka + off, kDescHiSw128, idesc_s);
         }
       };
-      auto issue_pv = [&](int x, int st, bool acc) {
-        const uint32_t va = sV + st * Cfg::kTileBytes;
+      // O_hf += P_hf V_hf over one key half: P of half hf sits in columns
+      // [64*hf, 64*hf + 32) of the S buffer (two bf16 per column), V_hf is
+      // key rows [64*hf, 64*hf + 64) of the V tile.
+      auto issue_pv_half = [&](int buf, int st, int hf, bool acc) {
+        const uint32_t va = v_lo + st * kTileLo + hf * 4 * (2048 >> 4);
+        const uint32_t a = tmem_base + Cfg::col_s(buf) + hf * 64;
+        const uint32_t d = tmem_base + Cfg::col_o(hf);
+        umma_ts_elect(d, a, va, kDescHiSw128, idesc_o, acc ? 1u : 0u);
 #pragma unroll
-        for (int kk = 0; kk < 128 / 16; ++kk) {
-          umma_ts(tmem_base + Cfg::col_o(x), tmem_base + Cfg::col_s(x) + kk * 8,
-                  smem_desc_sw128(va + kk * 2048, Cfg::kAtomBytes, 1024), idesc_o,
-                  (acc || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 1; kk < 4; ++kk)
+          umma_ts_elect(d, a + kk * 8, va + kk * (2048 >> 4), kDescHiSw128, idesc_o, 1u);
       };
-      bool ok = mbar_wait(bar_q, 0, abort_flag, 20);
-      if (ok) ok = mbar_wait(bar_k_full + 0, 0, abort_flag, 21);
-      if (ok) {
-        tc_fence_after();
-        for (int x = 0; x < 2; ++x)
-          if (active(x, lo)) {
-            issue_s(x, 0);
-            umma_commit(bar_s_full + x);
-          }
-        umma_commit(bar_k_empty + 0);
-      }
-      uint32_t p_cnt[2] = {0, 0};
-      for (int n = 0; ok && lo + n < hi; ++n) {
-        const int j = lo + n;
-        const int st = n % Cfg::kStages;
-        const uint32_t ph = (n / Cfg::kStages) & 1;
-        const bool has_next = j + 1 < hi;
-        const int stn = (n + 1) % Cfg::kStages;
-        const uint32_t phn = ((n + 1) / Cfg::kStages) & 1;
-        ok = mbar_wait(bar_v_full + st, ph, abort_flag, 22);
+      auto wait = [&](uint64_t* bar, uint32_t parity, int site) {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, site));
+      };
+      bool ok = wait(bar_q, 0, 20);
+      // Prologue: S for the first two key tiles.
+      for (int t = 0; ok && t < 2 && lo + t < hi; ++t) {
+        ok = wait(bar_k_full + t % Cfg::kStages, (t / Cfg::kStages) & 1, 21);
         if (!ok) break;
-        if (active(0, j)) {
-          ok = mbar_wait(bar_p_ready + 0, p_cnt[0]++ & 1, abort_flag, 23);
+        tc_fence_after();
+        issue_s(t, t % Cfg::kStages);
+        umma_commit_elect(bar_s_full + t);
+        umma_commit_elect(bar_k_empty + t % Cfg::kStages);
+      }
+      for (int n = 0; ok && lo + n < hi; ++n) {
+        const int buf = n & 1;
+        const uint32_t use_par = (n >> 1) & 1;
+        const int st = n % Cfg::kStages;
+        ok = wait(bar_v_full + st, (n / Cfg::kStages) & 1, 22);
+        if (!ok) break;
+        for (int hf = 0; hf < 2 && ok; ++hf) {
+          ok = wait(bar_p_ready + 2 * buf + hf, use_par, 23);
           if (!ok) break;
           tc_fence_after();
-          issue_pv(0, st, j > lo_x[0]);
+          issue_pv_half(buf, st, hf, n > 0);
+          umma_commit_elect(bar_o_prog + hf);
         }
-        if (has_next) {
-          ok = mbar_wait(bar_k_full + stn, phn, abort_flag, 24);
+        if (!ok) break;
+        umma_commit_elect(bar_v_empty + st);
+        const int n2 = n + 2;  // S for two tiles ahead goes into this buffer
+        if (lo + n2 < hi) {
+          const int st2 = n2 % Cfg::kStages;
+          ok = wait(bar_k_full + st2, (n2 / Cfg::kStages) & 1, 24);
           if (!ok) break;
           tc_fence_after();
-          if (active(0, j + 1)) {
-            issue_s(0, stn);
-            umma_commit(bar_s_full + 0);
-          }
-        }
-        if (active(1, j)) {
-          ok = mbar_wait(bar_p_ready + 1, p_cnt[1]++ & 1, abort_flag, 25);
-          if (!ok) break;
-          tc_fence_after();
-          issue_pv(1, st, j > lo_x[1]);
-        }
-        umma_commit(bar_v_empty + st);
-        if (has_next) {
-          if (active(1, j + 1)) {
-            issue_s(1, stn);
-            umma_commit(bar_s_full + 1);
-          }
-          umma_commit(bar_k_empty + stn);
+          issue_s(buf, st2);
+          umma_commit_elect(bar_s_full + buf);
+          umma_commit_elect(bar_k_empty + st2);
         }
       }
-      umma_commit(bar_o_done + 0);
-      umma_commit(bar_o_done + 1);
+      umma_commit_elect(bar_o_done);
       // Drain: TMEM may only be released once every issued MMA has finished.
-      umma_commit(bar_drain);
+      umma_commit_elect(bar_drain);
       volatile int no_abort = 0;
       mbar_wait(bar_drain, 0, &no_abort, 26);
     }
-    __syncwarp();
-   }
-  } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(Cfg::kSoftmaxRegs));
+  } else if (warp < 8) {
     // -------------------------------------------------------------- softmax
-    const int x = warp / 4;  // query tile 0 (A) or 1 (B)
+    const int half = warp / 4;  // key columns [64*half, 64*half + 64)
     const int quarter = warp % 4;
-    const int row = r0_tile[x] + quarter * 32 + lane;
+    const int rloc = quarter * 32 + lane;
+    const int row = r0 + rloc;
     const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
-    const uint32_t col_s = Cfg::col_s(x);
-    const uint32_t col_o = Cfg::col_o(x);
+    const uint32_t col_h = 64 * half;
     const float sl2 = p.scale_log2;
     const float slope2 = (p.alibi != nullptr) ? p.alibi[h] * 1.4426950408889634f : 0.0f;
     const RowBounds rb = row_bounds(p, row);
     const long long row_lo = max(rb.jlo, 0ll);
     const long long row_hi = min(rb.jhi, (long long)lkey - 1);
     const long long diag = p.q_pos0 + row - p.k_pos0;
-    const bool tiers = p.additive && !safe_x[x];
-
-    float m_run = -INFINITY;
-    float l_run = 0.0f;
-    int tier = 3;
-    bool ok = true;
-    const int lo_t = lo_x[x], hi_t = hi_x[x];
-    // Key tiles wholly inside [row_lo, row_hi] for every row of this tile.
-    const int r_first = r0_tile[x], r_last = min(r0_tile[x] + 127, p.Sq - 1);
-    const RowBounds rb_first = row_bounds(p, r_first), rb_last = row_bounds(p, r_last);
+    const bool tiers = p.additive && !safe;
+    // Key tiles wholly inside [row_lo, row_hi] for every row of the tile.
+    const int r_last = min(r0 + 127, p.Sq - 1);
+    const RowBounds rb_first = row_bounds(p, r0), rb_last = row_bounds(p, r_last);
     const long long in_lo = max(rb_last.jlo, 0ll);
     const long long in_hi = min(rb_first.jhi, (long long)lkey - 1);
 
-    for (int j = lo_t; j < hi_t; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait(bar_s_full + x, (j - lo_t) & 1, abort_flag, 30 + x));
-      if (!ok) break;
+    float m_run = -INFINITY;  // this half's running max (log2 domain)
+    float l_run = 0.0f;       // this half's running sum
+    int tier = 3;             // fewest -1e9 terms seen by this half (tier mode)
+    bool failed = false;      // a wait ran out of time; skip the work
+
+#if ENL_STAGGER
+    // Start the second half one P-publish after the first, so the two warps
+    // that share an SMSP do not run their MUFU-bound phases in lockstep.
+    if (half == 1 && hi - lo >= 2)
+      failed = !__all_sync(0xffffffffu, mbar_wait(bar_p_ready + 0, 0, abort_flag, 29));
+#endif
+    for (int n = 0; lo + n < hi && !failed; ++n) {
+      const int j = lo + n;
+      const int buf = n & 1;
+      failed = !__all_sync(0xffffffffu,
+                           mbar_wait(bar_s_full + buf, (n >> 1) & 1, abort_flag, 30 + half));
+      if (failed) break;
       tc_fence_after();
-      uint32_t sr[128];
-      ENL_TMEM_LD128(lane_addr + col_s, sr);
-      float s[128];
+      const uint32_t s_addr = lane_addr + Cfg::col_s(buf) + col_h;
+      float s[64];
+      {
+        uint32_t sr[64];
+        ENL_TMEM_LD32(s_addr, sr, 0);
+        ENL_TMEM_LD32(s_addr + 32, sr, 32);
 #pragma unroll
-      for (int c = 0; c < 128; ++c) s[c] = __uint_as_float(sr[c]);
-      const long long j0 = (long long)j * 128;
-      const bool full_tile = (j0 >= in_lo) && (j0 + 127 <= in_hi) && !tiers && slope2 == 0.0f;
+        for (int c = 0; c < 64; ++c) s[c] = __uint_as_float(sr[c]);
+      }
+      const long long j0 = (long long)j * 128 + col_h;  // key index of this half's column 0
+      const bool full_tile = (j0 >= in_lo) && (j0 + 63 <= in_hi) && !tiers && slope2 == 0.0f;
       bool reset = false;
       float m_tile = -INFINITY;
       if (full_tile) {
+        float mx[8];
 #pragma unroll
-        for (int c = 0; c < 128; ++c) m_tile = fmaxf(m_tile, s[c]);
-        m_tile *= sl2;
+        for (int k = 0; k < 8; ++k) mx[k] = fmax3(s[k], s[8 + k], s[16 + k]);
+#pragma unroll
+        for (int c = 24; c < 56; c += 16)
+#pragma unroll
+          for (int k = 0; k < 8; ++k) mx[k] = fmax3(mx[k], s[c + k], s[c + 8 + k]);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx[k] = fmaxf(mx[k], s[56 + k]);
+        m_tile = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]),
+                       fmaxf(mx[6], mx[7])) * sl2;
       } else {
-        // Per-tile bounds relative to the tile start, clamped into int range:
-        // column c is key j0 + c.
-        auto rel = [&](long long v) { return (int)max(-1ll, min(129ll, v - j0)); };
-        const int c_lo = rel(row_lo), c_hi = rel(row_hi);  // unmasked columns [c_lo, c_hi]
+        // Bounds relative to this half's first column, clamped into int
+        // range: column c is key j0 + c.
+        auto rel = [&](long long v) { return (int)max(-1ll, min(65ll, v - j0)); };
         const float dbase = (float)(diag - j0);
         const bool alibi_abs = !p.causal;
         if (!tiers) {
+          const int c_lo = rel(row_lo), c_hi = rel(row_hi);  // unmasked columns [c_lo, c_hi]
 #pragma unroll
-          for (int c = 0; c < 128; ++c) {
+          for (int c = 0; c < 64; ++c) {
             float dist = dbase - (float)c;
             if (alibi_abs) dist = fabsf(dist);
             const float v = fmaf(s[c], sl2, -slope2 * dist);
@@ -359,27 +378,26 @@ __global__ void __launch_bounds__(384, 1)
           }
         } else {
           // -1e9 rule on rows without any unmasked key: only the scores with
-          // the fewest -1e9 terms survive (exp(-1e9) underflows to 0 in float64).
-          const int c_wlo = rel(rb.jlo), c_whi = rel(rb.jhi);  // causal/window bounds
-          const int c_pad = rel(lkey);                          // first padded column
-          const int cend = min(128, rel(p.Skv));                // columns [0, cend) exist
-          // Smallest tier present in this tile, from interval arithmetic:
-          // tier(c) = [c >= c_pad] + [c < c_wlo or c > c_whi].
+          // the fewest -1e9 terms survive (exp(-1e9) underflows to 0 in
+          // float64). tier(key) = [key >= lkey] + [key < jlo or key > jhi];
+          // the smallest tier of this half's 64 columns comes from interval
+          // arithmetic, the epilogue keeps the half with the smaller tier.
+          const int c_wlo = rel(rb.jlo), c_whi = rel(rb.jhi), c_pad = rel(lkey);
+          const int cend = min(64, rel(p.Skv));  // columns [0, cend) exist
           int tmin;
           if (max(0, c_wlo) <= min(min(c_whi, c_pad - 1), cend - 1)) {
             tmin = 0;
           } else {
             const int real_hi = min(c_pad, cend) - 1;  // real columns [0, real_hi]
             const bool real_blocked = real_hi >= 0 && (c_wlo > 0 || real_hi > c_whi);
-            const bool pad_open =
-                max(max(c_pad, 0), c_wlo) <= min(cend - 1, c_whi);  // padded, unblocked
+            const bool pad_open = max(max(c_pad, 0), c_wlo) <= min(cend - 1, c_whi);
             tmin = (real_blocked || pad_open) ? 1 : (cend > 0 ? 2 : 3);
           }
           const int new_tier = min(tier, tmin);
           reset = new_tier < tier;
           tier = new_tier;
 #pragma unroll
-          for (int c = 0; c < 128; ++c) {
+          for (int c = 0; c < 64; ++c) {
             const int t = (int)(c >= c_pad) + (int)(c < c_wlo || c > c_whi);
             float dist = dbase - (float)c;
             if (alibi_abs) dist = fabsf(dist);
@@ -401,20 +419,38 @@ __global__ void __launch_bounds__(384, 1)
       }
       const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
       float rowsum = 0.0f;
-      uint32_t pk[64];
+      uint32_t pk[32];
       if (full_tile) {
-        // Unmasked tile: s is still the raw dot product; fold the scale in.
-        const float neg_m = -m_use;
+        // Unmasked tile: s is still the raw dot product; fold the scale in
+        // with packed FMAs, accumulate the row sum in 4 packed lanes.
+        const uint64_t scale2 = f2_pack(sl2, sl2);
+        const uint64_t negm2 = f2_pack(-m_use, -m_use);
+        uint64_t acc[4];
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const float p0 = fast_exp2(fmaf(s[2 * c], sl2, neg_m));
-          const float p1 = fast_exp2(fmaf(s[2 * c + 1], sl2, neg_m));
-          rowsum += p0 + p1;
+        for (int k = 0; k < 4; ++k) acc[k] = f2_pack(0.0f, 0.0f);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(s[2 * c], s[2 * c + 1]), scale2, negm2), x0, x1);
+          float p0, p1;
+          if (kEmuEvery > 0 && (c % (kEmuEvery > 0 ? kEmuEvery : 1)) == kEmuEvery - 1) {
+            exp2_poly2(x0, x1, p0, p1);
+          } else {
+            p0 = fast_exp2(x0);
+            p1 = fast_exp2(x1);
+          }
+          acc[c % 4] = f2_add(acc[c % 4], f2_pack(p0, p1));
           pk[c] = pack_bf16x2(p0, p1);
         }
+        float a0, a1, a2, a3, a4, a5, a6, a7;
+        f2_unpack(acc[0], a0, a1);
+        f2_unpack(acc[1], a2, a3);
+        f2_unpack(acc[2], a4, a5);
+        f2_unpack(acc[3], a6, a7);
+        rowsum = ((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7));
       } else {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
+        for (int c = 0; c < 32; ++c) {
           const float p0 = fast_exp2(s[2 * c] - m_use);
           const float p1 = fast_exp2(s[2 * c + 1] - m_use);
           rowsum += p0 + p1;
@@ -422,50 +458,83 @@ __global__ void __launch_bounds__(384, 1)
         }
       }
       l_run = l_run * factor + rowsum;
-      // O correction (warp-collective): only once O holds earlier tiles.
-      const bool need_corr = (j > lo_t) && (factor != 1.0f);
+      // O_half correction, after this half's P V of the previous tile has
+      // finished (warp-collective; rare with the lazy threshold).
+      const bool need_corr = (n > 0) && (factor != 1.0f);
       if (__any_sync(0xffffffffu, need_corr)) {
+        failed = !__all_sync(0xffffffffu,
+                             mbar_wait(bar_o_prog + half, (n - 1) & 1, abort_flag, 32 + half));
+        if (failed) break;
+        tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
           uint32_t o[32];
-          ENL_TMEM_LD32(lane_addr + col_o + c * 32, o, 0);
+          const uint32_t oa = lane_addr + Cfg::col_o(half) + c * 32;
+          ENL_TMEM_LD32(oa, o, 0);
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
-          ENL_TMEM_ST32(lane_addr + col_o + c * 32, o, 0);
+          ENL_TMEM_ST32(oa, o, 0);
         }
       }
-      ENL_TMEM_ST32(lane_addr + col_s, pk, 0);
-      ENL_TMEM_ST32(lane_addr + col_s + 32, pk, 32);
+      // Publish this half of P over its own first 32 S columns.
+      ENL_TMEM_ST32(s_addr, pk, 0);
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar_p_ready + x);
+      if (lane == 0) mbar_arrive(bar_p_ready + 2 * buf + half);
     }
 
     // ------------------------------------------------------------- epilogue
+    // Merge the two halves by log-sum-exp: only the half(s) with the fewest
+    // -1e9 terms count (tier mode), scaled to a common maximum. Each thread
+    // then writes D/2 output columns of its row from both accumulators. All
+    // softmax threads reach this barrier (the loop above never exits early
+    // without every other exit path also arriving here).
+    x_m[half * 128 + rloc] = m_run;
+    x_l[half * 128 + rloc] = l_run;
+    x_t[half * 128 + rloc] = tier;
+    named_bar_sync(1, 256);
+    const float m0 = x_m[rloc], m1 = x_m[128 + rloc];
+    const float l0 = x_l[rloc], l1 = x_l[128 + rloc];
+    const int t0 = tiers ? x_t[rloc] : 0, t1 = tiers ? x_t[128 + rloc] : 0;
+    const int tfin = min(t0, t1);
+    const bool use0 = (t0 == tfin) && (m0 != -INFINITY);
+    const bool use1 = (t1 == tfin) && (m1 != -INFINITY);
+    const float mfin = fmaxf(use0 ? m0 : -INFINITY, use1 ? m1 : -INFINITY);
+    const float w0 = use0 ? exp2f(m0 - mfin) : 0.0f;
+    const float w1 = use1 ? exp2f(m1 - mfin) : 0.0f;
+    const float l_tot = w0 * l0 + w1 * l1;
     const bool row_valid = row < p.Sq;
-    ok = __all_sync(0xffffffffu, ok && !*abort_flag);
+    bool ok = __all_sync(0xffffffffu, !failed && !*abort_flag);
     const bool warp_has_rows = __any_sync(0xffffffffu, row_valid);
     if (ok && warp_has_rows) {
-      const bool have_o = lo_t < hi_t;
-      if (have_o)
-        ok = __all_sync(0xffffffffu, mbar_wait(bar_o_done + x, 0, abort_flag, 35 + x));
+      const bool have_o = lo < hi;
+      if (have_o) ok = __all_sync(0xffffffffu, mbar_wait(bar_o_done, 0, abort_flag, 35 + half));
       if (ok) {
         tc_fence_after();
-        const float inv_l = 1.0f / l_run;  // 0/0 -> NaN for rows with no key
+        const float inv_l = 1.0f / l_tot;  // 0/0 -> NaN for rows with no key
+        const float s0 = w0 * inv_l, s1 = w1 * inv_l;
+        const int c0 = half * (D / 2);  // this thread's output columns [c0, c0 + D/2)
         uint8_t* orow = reinterpret_cast<uint8_t*>(p.o) +
-                        ((long long)b * p.o_sb + (long long)row * p.o_ss + (long long)h * p.o_sh) *
+                        ((long long)b * p.o_sb + (long long)row * p.o_ss + (long long)h * p.o_sh +
+                         c0) *
                             (p.out_fp32 ? 4 : 2);
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
+        for (int c = 0; c < D / 64; ++c) {
+          uint32_t o0[32], o1[32];
           __syncwarp();  // the stores below diverge by row; reconverge for tcgen05.ld
           if (have_o) {
-            ENL_TMEM_LD32(lane_addr + col_o + c * 32, o, 0);
+            ENL_TMEM_LD32(lane_addr + Cfg::col_o(0) + c0 + c * 32, o0, 0);
+            ENL_TMEM_LD32(lane_addr + Cfg::col_o(1) + c0 + c * 32, o1, 0);
           }
           float v[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = have_o ? __uint_as_float(o[i]) * inv_l : NAN;
+          for (int i = 0; i < 32; ++i)
+            v[i] = have_o ? fmaf(__uint_as_float(o0[i]), s0, __uint_as_float(o1[i]) * s1) : NAN;
+          if (have_o && l_tot == 0.0f) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = NAN;
+          }
           if (row_valid && p.out_fp32) {
             float4* dst = reinterpret_cast<float4*>(orow + c * 32 * 4);
 #pragma unroll
@@ -481,9 +550,9 @@ __global__ void __launch_bounds__(384, 1)
                                   pack_bf16x2(v[8 * i + 6], v[8 * i + 7]));
           }
         }
-        if (p.lse != nullptr && row_valid) {
-          float lse = have_o ? (m_run + log2f(l_run)) * 0.6931471805599453f : NAN;
-          if (tiers && tier > 0) lse -= 1e9f * (float)tier;
+        if (p.lse != nullptr && row_valid && half == 0) {
+          float lse = have_o ? (mfin + log2f(l_tot)) * 0.6931471805599453f : NAN;
+          if (tiers && tfin > 0) lse -= 1e9f * (float)tfin;
           p.lse[((long long)b * p.H + h) * p.Sq + row] = lse;
         }
       }
@@ -501,11 +570,6 @@ __global__ void __launch_bounds__(384, 1)
 }
 
 template <int D>
-int prefill_smem_bytes() {
-  return PrefillCfg<D>::kSmemBytes;
-}
-
-template <int D>
 cudaError_t launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                            const PrefillParams& p, cudaStream_t stream) {
   using Cfg = PrefillCfg<D>;
@@ -518,8 +582,7 @@ cudaError_t launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const C
     configured = true;
   }
   const int q_tiles = (p.Sq + 127) / 128;
-  const int pairs = (q_tiles + 1) / 2;
-  dim3 grid(p.B * p.H, pairs);
+  dim3 grid(q_tiles, p.B * p.H);
   attn_prefill_sm100<D><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(tq, tk, tv, p);
   return cudaGetLastError();
 }
