@@ -1,0 +1,196 @@
+"""Layer-level attention on the B200 kernels.
+
+Mirrors the reference's attention branches layer by layer:
+  * self-attention           nn/forward.py:423-556 (projections, RoPE/ALiBi,
+                             GQA, causal/window masks, softmax, Wo)
+  * cross-attention          nn/forward.py:557-591
+  * key-padding (graph MHA)  graph/sequence.py:144-183 (additive -1e9 rule)
+The projections are plain bf16 GEMMs (cuBLAS through torch); Q/K/V are never
+copied or expanded: the prefill kernel (K1) reads them as strided head views
+of the fused QKV projection output and indexes K/V heads group-major
+(nn/forward.py:165-171) instead of repeating them.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import numpy as np
+
+from . import kernels
+from .backend import device, to_device
+
+SINUSOIDAL_BASE = 10000.0  # core/constants.py:70
+
+
+def check_supported(layer: dict, training: bool = False) -> None:
+    """Raise ValueError for options the B200 kernels do not implement, naming
+    the option, instead of falling back to another backend."""
+    kernel = layer.get("attention_kernel", "softmax")
+    if kernel != "softmax":
+        raise ValueError(f"attention_kernel={kernel!r} is not supported by the B200 attention "
+                         "path (softmax attention only).")
+    if layer.get("sparse_pattern") is not None:
+        raise ValueError("sparse_pattern is not supported by the B200 attention path.")
+    if training and layer.get("dropout", 0.0) > 0:
+        raise ValueError("attention dropout at training=True is not supported by the B200 "
+                         "attention path (inference only).")
+
+
+# --------------------------------------------------------------- caches
+class _LayerWeights:
+    """bf16 device copies of one layer's projections, rebuilt whenever an
+    array in the layer dict is replaced."""
+
+    def __init__(self):
+        self._store = {}
+
+    def get(self, layer: dict, names, kind):
+        import torch
+        arrays = tuple(layer[n] for n in names)
+        key = (kind,) + tuple(id(a) for a in arrays)
+        hit = self._store.get(key)
+        if hit is not None and all(x is y for x, y in zip(hit[0], arrays)):
+            return hit[1]
+        if kind == "w":
+            host = np.concatenate([np.asarray(a, np.float32) for a in arrays], axis=0)
+        else:
+            host = np.concatenate([np.asarray(a, np.float32).reshape(-1) for a in arrays])
+        t = to_device(host, torch.bfloat16)
+        self._store[key] = (arrays, t)
+        return t
+
+
+_WEIGHTS = _LayerWeights()
+_ALIBI: dict = {}
+_ROPE: dict = {}
+
+
+def alibi_slopes(num_heads: int) -> np.ndarray:
+    """Geometric ALiBi slopes, nn/forward.py:90-100."""
+    def pow2(n):
+        start = 2.0 ** (-8.0 / n)
+        return [start ** (i + 1) for i in range(n)]
+    if num_heads & (num_heads - 1) == 0:
+        return np.array(pow2(num_heads))
+    closest = 2 ** int(np.floor(np.log2(num_heads)))
+    return np.array(pow2(closest) + pow2(2 * closest)[0::2][: num_heads - closest])
+
+
+def alibi_tensor(num_heads: int):
+    import torch
+    key = (num_heads, device().index)
+    if key not in _ALIBI:
+        _ALIBI[key] = to_device(alibi_slopes(num_heads).astype(np.float32), torch.float32)
+    return _ALIBI[key]
+
+
+def rope_tables(n_rows: int, head_dim: int):
+    """(cos, sin) device tables of at least n_rows rows, computed in float64
+    exactly as nn/forward.py:46-55 computes the angles."""
+    import torch
+    key = (head_dim, device().index)
+    have = _ROPE.get(key)
+    if have is None or have[0].shape[0] < n_rows:
+        rows = max(n_rows, 2 * (have[0].shape[0] if have is not None else 0), 256)
+        half = head_dim // 2
+        theta = SINUSOIDAL_BASE ** (-2.0 * np.arange(half) / head_dim)
+        angles = np.arange(rows, dtype=np.float64)[:, None] * theta[None, :]
+        have = (to_device(np.cos(angles).astype(np.float32), torch.float32),
+                to_device(np.sin(angles).astype(np.float32), torch.float32))
+        _ROPE[key] = have
+    return have
+
+
+def apply_rope(t, pos0: int):
+    """Rotate (B, S, H, D) in place at absolute positions pos0.. (nn/forward.py:80-88)."""
+    cos, sin = rope_tables(pos0 + t.shape[1], t.shape[-1])
+    kernels.rope_(t, cos, sin, pos0)
+    return t
+
+
+# ---------------------------------------------------------- projections
+def project(x, layer: dict, which: str):
+    """x @ W.T + b for W in {"q", "kv", "qkv", "o"} as one bf16 GEMM
+    (nn/forward.py:428-430, :551)."""
+    import torch
+    import torch.nn.functional as F
+    names = {"q": (("Wq",), ("bq",)), "kv": (("Wk", "Wv"), ("bk", "bv")),
+             "qkv": (("Wq", "Wk", "Wv"), ("bq", "bk", "bv")), "o": (("Wo",), ("bo",))}[which]
+    w = _WEIGHTS.get(layer, names[0], "w")
+    b = _WEIGHTS.get(layer, names[1], "b")
+    return F.linear(x.to(torch.bfloat16), w, b)
+
+
+def split_heads(t, heads: int, head_dim: int, offset: int = 0):
+    """(B, S, *) -> strided (B, S, heads, head_dim) view at column offset."""
+    return t[..., offset:offset + heads * head_dim].unflatten(-1, (heads, head_dim))
+
+
+def lengths_from_mask(mask, B: int, S: int):
+    """Per-row valid lengths from a boolean key-padding mask (True = real
+    token, graph/sequence.py:23-29). The kernels take prefix lengths; a mask
+    whose real tokens do not form a prefix raises ValueError."""
+    m = np.asarray(mask if not hasattr(mask, "detach") else mask.detach().cpu().numpy())
+    if m.shape != (B, S):
+        raise ValueError(f"key_padding_mask shape {m.shape} must be (batch, seq) = {(B, S)}")
+    m = m.astype(bool)
+    lengths = m.sum(axis=1)
+    if not np.array_equal(m, np.arange(S)[None, :] < lengths[:, None]):
+        raise ValueError("key_padding_mask must mark a prefix of real tokens in every row "
+                         "(as lengths_to_mask builds); the B200 kernel takes valid lengths.")
+    return lengths.astype(np.int32)
+
+
+# ------------------------------------------------------------- forward
+def self_attention(layer: dict, x, key_padding_mask=None, mask_mode: Optional[str] = None):
+    """One multihead_attention layer on a (B, S, E) device tensor; returns
+    the (B, S, E) fp32 output. With key_padding_mask, masking follows the
+    graph layer's additive -1e9 rule (graph/sequence.py:162-176); without it,
+    the nn/ layer's -inf masks (nn/forward.py:539-543)."""
+    import torch
+    check_supported(layer)
+    B, S, E = x.shape
+    H, D = layer["num_heads"], layer["head_dim"]
+    Hkv = layer.get("num_kv_heads") or H
+    qkv = project(x, layer, "qkv")
+    q = split_heads(qkv, H, D, 0)
+    k = split_heads(qkv, Hkv, D, H * D)
+    v = split_heads(qkv, Hkv, D, H * D + Hkv * D)
+    scheme = layer.get("positional_scheme", "absolute")
+    if scheme == "rope":
+        apply_rope(q, 0)
+        apply_rope(k, 0)
+    lens = None
+    mode = mask_mode or "exclude"
+    if key_padding_mask is not None:
+        lens = to_device(lengths_from_mask(key_padding_mask, B, S), torch.int32)
+        mode = mask_mode or "additive"
+    ctx = kernels.attention_prefill(
+        q, k, v, causal=bool(layer.get("causal", False)), window=layer.get("window_size"),
+        kv_valid_len=lens, alibi_slopes=alibi_tensor(H) if scheme == "alibi" else None,
+        mask_mode=mode)
+    return project(ctx.flatten(-2), layer, "o").float()
+
+
+def cross_attention(layer: dict, x, memory, memory_key_padding_mask=None):
+    """One cross_attention layer (nn/forward.py:557-591): Q from x (B, Sq, E),
+    K/V from memory (B, Skv, E), non-causal. memory_key_padding_mask (True =
+    real) applies the graph layer's -1e9 key-padding rule to the memory keys."""
+    import torch
+    check_supported(layer)
+    B, Sq, E = x.shape
+    Skv = memory.shape[1]
+    H, D = layer["num_heads"], layer["head_dim"]
+    Hkv = layer.get("num_kv_heads") or H
+    q = split_heads(project(x, layer, "q"), H, D)
+    kv = project(memory, layer, "kv")
+    k = split_heads(kv, Hkv, D, 0)
+    v = split_heads(kv, Hkv, D, Hkv * D)
+    lens = None
+    mode = "exclude"
+    if memory_key_padding_mask is not None:
+        lens = to_device(lengths_from_mask(memory_key_padding_mask, B, Skv), torch.int32)
+        mode = "additive"
+    ctx = kernels.attention_prefill(q, k, v, causal=False, kv_valid_len=lens, mask_mode=mode)
+    return project(ctx.flatten(-2), layer, "o").float()

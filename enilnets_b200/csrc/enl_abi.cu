@@ -120,8 +120,9 @@ int enl_attn_prefill(const enl_prefill_args* a, void* stream) {
   if (a->num_heads % a->num_kv_heads != 0)
     return fail(ENL_ERR_INVALID, "enl_attn_prefill: num_kv_heads=%d must divide num_heads=%d",
                 a->num_kv_heads, a->num_heads);
-  if (a->head_dim != 64 && a->head_dim != 128)
-    return fail(ENL_ERR_UNSUPPORTED, "enl_attn_prefill: head_dim=%d (supported: 64, 128)",
+  if (a->head_dim < 8 || a->head_dim > 128 || a->head_dim % 8 != 0)
+    return fail(ENL_ERR_UNSUPPORTED,
+                "enl_attn_prefill: head_dim=%d (supported: multiples of 8 up to 128)",
                 a->head_dim);
   if (a->in_dtype != ENL_DTYPE_BF16)
     return fail(ENL_ERR_UNSUPPORTED, "enl_attn_prefill: in_dtype=%d (supported: bf16)",
@@ -143,19 +144,22 @@ int enl_attn_prefill(const enl_prefill_args* a, void* stream) {
     return fail(ENL_ERR_UNSUPPORTED, "enl_attn_prefill: batch*num_heads=%lld exceeds 65535",
                 (long long)a->batch * a->num_heads);
 
-  const int D = a->head_dim;
+  // The kernel runs at D = 64 or 128; smaller head dims are zero-filled by
+  // TMA (the tensor maps keep the real extent) and never stored.
+  const int D = a->head_dim <= 64 ? 64 : 128;
   CUtensorMap tq, tk, tv;
-  if ((st = make_qkv_map(&tq, a->q, D, a->seq_q, a->num_heads, a->batch, a->q_stride_s,
+  if ((st = make_qkv_map(&tq, a->q, a->head_dim, a->seq_q, a->num_heads, a->batch, a->q_stride_s,
                          a->q_stride_h, a->q_stride_b, "q")))
     return st;
-  if ((st = make_qkv_map(&tk, a->k, D, a->seq_kv, a->num_kv_heads, a->batch, a->k_stride_s,
+  if ((st = make_qkv_map(&tk, a->k, a->head_dim, a->seq_kv, a->num_kv_heads, a->batch, a->k_stride_s,
                          a->k_stride_h, a->k_stride_b, "k")))
     return st;
-  if ((st = make_qkv_map(&tv, a->v, D, a->seq_kv, a->num_kv_heads, a->batch, a->v_stride_s,
+  if ((st = make_qkv_map(&tv, a->v, a->head_dim, a->seq_kv, a->num_kv_heads, a->batch, a->v_stride_s,
                          a->v_stride_h, a->v_stride_b, "v")))
     return st;
 
   PrefillParams p;
+  p.d_real = a->head_dim;
   p.B = a->batch;
   p.H = a->num_heads;
   p.Hkv = a->num_kv_heads;
@@ -198,7 +202,8 @@ int enl_decode_auto_splits(int32_t batch, int32_t num_kv_heads, int32_t n_slots)
 size_t enl_decode_workspace_bytes(int32_t batch, int32_t num_heads, int32_t head_dim,
                                   int32_t n_splits) {
   if (n_splits <= 1) return 0;
-  return (size_t)n_splits * batch * num_heads * (head_dim + 1) * sizeof(float);
+  const int dk = head_dim <= 64 ? 64 : 128;  // the kernel's (zero-extended) head dim
+  return (size_t)n_splits * batch * num_heads * (dk + 1) * sizeof(float);
 }
 
 int enl_attn_decode(const enl_decode_args* a, void* stream) {
@@ -214,9 +219,11 @@ int enl_attn_decode(const enl_decode_args* a, void* stream) {
   if (G != 1 && G != 2 && G != 4 && G != 8)
     return fail(ENL_ERR_UNSUPPORTED,
                 "enl_attn_decode: num_heads/num_kv_heads=%d (supported: 1, 2, 4, 8)", G);
-  if (a->head_dim != 64 && a->head_dim != 128)
-    return fail(ENL_ERR_UNSUPPORTED, "enl_attn_decode: head_dim=%d (supported: 64, 128)",
+  if (a->head_dim < 8 || a->head_dim > 128 || a->head_dim % 8 != 0)
+    return fail(ENL_ERR_UNSUPPORTED,
+                "enl_attn_decode: head_dim=%d (supported: multiples of 8 up to 128)",
                 a->head_dim);
+  const int Dk = a->head_dim <= 64 ? 64 : 128;  // kernel head dim (zero-extended)
   if (a->in_dtype != ENL_DTYPE_BF16)
     return fail(ENL_ERR_UNSUPPORTED, "enl_attn_decode: in_dtype=%d (supported: bf16)",
                 a->in_dtype);
@@ -250,7 +257,7 @@ int enl_attn_decode(const enl_decode_args* a, void* stream) {
   splits = (n_slots + split_len - 1) / split_len;
   if (splits < 1) splits = 1;
   if (splits > 1) {
-    const size_t need = enl_decode_workspace_bytes(a->batch, a->num_heads, a->head_dim, splits);
+    const size_t need = enl_decode_workspace_bytes(a->batch, a->num_heads, Dk, splits);
     if (!a->workspace || a->workspace_bytes < need)
       return fail(ENL_ERR_INVALID,
                   "enl_attn_decode: %d splits need a %zu-byte workspace (got %zu)", splits, need,
@@ -258,6 +265,7 @@ int enl_attn_decode(const enl_decode_args* a, void* stream) {
   }
 
   DecodeParams p;
+  p.d_real = a->head_dim;
   p.B = a->batch;
   p.H = a->num_heads;
   p.Hkv = a->num_kv_heads;
@@ -282,10 +290,9 @@ int enl_attn_decode(const enl_decode_args* a, void* stream) {
   p.out_fp32 = a->out_dtype == ENL_DTYPE_FP32;
   p.lse = a->lse;
   p.part_o = reinterpret_cast<float*>(a->workspace);
-  p.part_lse = p.part_o ? p.part_o + (size_t)splits * a->batch * a->num_heads * a->head_dim
-                        : nullptr;
+  p.part_lse = p.part_o ? p.part_o + (size_t)splits * a->batch * a->num_heads * Dk : nullptr;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  cudaError_t e = (a->head_dim == 128) ? launch_decode<128>(p, s) : launch_decode<64>(p, s);
+  cudaError_t e = (Dk == 128) ? launch_decode<128>(p, s) : launch_decode<64>(p, s);
   if (e != cudaSuccess) return cuda_fail(e, "enl_attn_decode launch");
   return ENL_OK;
 }
@@ -300,8 +307,9 @@ int enl_lse_merge(const float* part_o, const float* part_lse, int32_t n_parts, i
   if (out_dtype != ENL_DTYPE_BF16 && out_dtype != ENL_DTYPE_FP32)
     return fail(ENL_ERR_INVALID, "enl_lse_merge: out_dtype=%d", out_dtype);
   cudaError_t e = launch_lse_merge(part_o, part_lse, n_parts, (long long)batch * num_heads * head_dim,
-                                   (long long)batch * num_heads, batch, num_heads, head_dim, o,
-                                   o_stride_b, o_stride_h, out_dtype == ENL_DTYPE_FP32, lse,
+                                   (long long)batch * num_heads, batch, num_heads, head_dim,
+                                   head_dim, o, o_stride_b, o_stride_h,
+                                   out_dtype == ENL_DTYPE_FP32, lse,
                                    reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "enl_lse_merge launch");
   return ENL_OK;

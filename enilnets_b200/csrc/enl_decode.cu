@@ -65,15 +65,18 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const DecodeParams p) 
   const int s_begin = p.slot_begin + split * p.split_len;
   const int s_end = min(p.slot_end, s_begin + p.split_len);
 
+  // Lanes whose 8-element slice lies past the tensors' head dim read zeros.
+  const bool lane_live = sub * 8 < p.d_real;
   // Queries of the GQA group, pre-scaled into the log2 domain.
   float q[G][8];
   float slope2[G];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     const int h = hkv * G + g;
-    const uint4 w = *reinterpret_cast<const uint4*>(
-        reinterpret_cast<const __nv_bfloat16*>(p.q) + (long long)b * p.q_sb +
-        (long long)h * p.q_sh + sub * 8);
+    const uint4 w = lane_live ? *reinterpret_cast<const uint4*>(
+                                    reinterpret_cast<const __nv_bfloat16*>(p.q) +
+                                    (long long)b * p.q_sb + (long long)h * p.q_sh + sub * 8)
+                              : make_uint4(0, 0, 0, 0);
     unpack8(w, q[g]);
 #pragma unroll
     for (int i = 0; i < 8; ++i) q[g][i] *= p.scale_log2;
@@ -105,7 +108,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const DecodeParams p) 
     for (int u = 0; u < U; ++u) {
       const int slot = s0 + u * NG;
       valid[u] = slot < s_end;
-      if (valid[u]) {
+      if (valid[u] && lane_live) {
         kr[u] = ld_stream(kbase + (long long)slot * p.k_ss);
         vr[u] = ld_stream(vbase + (long long)slot * p.v_ss);
       } else {
@@ -176,6 +179,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const DecodeParams p) 
   for (int idx = threadIdx.x; idx < G * D; idx += Cfg::kThreads) {
     const int g = idx / D;
     const int d = idx % D;
+    if (d >= p.d_real) continue;
     float M = -INFINITY;
 #pragma unroll
     for (int k = 0; k < NG; ++k) M = fmaxf(M, sm_m[g][k]);
@@ -227,8 +231,8 @@ cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream) {
   }
   if (e != cudaSuccess || p.n_splits == 1) return e;
   return launch_lse_merge(p.part_o, p.part_lse, p.n_splits, (long long)p.B * p.H * D,
-                          (long long)p.B * p.H, p.B, p.H, D, p.o, p.o_sb, p.o_sh, p.out_fp32,
-                          p.lse, stream);
+                          (long long)p.B * p.H, p.B, p.H, D, p.d_real, p.o, p.o_sb, p.o_sh,
+                          p.out_fp32, p.lse, stream);
 }
 
 template cudaError_t launch_decode<64>(const DecodeParams&, cudaStream_t);
@@ -239,7 +243,7 @@ template cudaError_t launch_decode<128>(const DecodeParams&, cudaStream_t);
 __global__ void lse_merge_kernel(const float* __restrict__ part_o,
                                  const float* __restrict__ part_lse, int n_parts,
                                  long long stride_o, long long stride_lse, int B, int H, int D,
-                                 void* o, long long o_sb, long long o_sh, int out_fp32,
+                                 int d_out, void* o, long long o_sb, long long o_sh, int out_fp32,
                                  float* lse_out) {
   const int bh = blockIdx.x;
   const int b = bh / H, h = bh % H;
@@ -248,7 +252,7 @@ __global__ void lse_merge_kernel(const float* __restrict__ part_o,
   float W = 0.0f;
   if (M != -INFINITY)
     for (int i = 0; i < n_parts; ++i) W += __expf(part_lse[i * stride_lse + bh] - M);
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+  for (int d = threadIdx.x; d < d_out; d += blockDim.x) {
     float acc = 0.0f;
     if (M != -INFINITY) {
       for (int i = 0; i < n_parts; ++i) {
@@ -268,11 +272,11 @@ __global__ void lse_merge_kernel(const float* __restrict__ part_o,
 
 cudaError_t launch_lse_merge(const float* part_o, const float* part_lse, int n_parts,
                              long long part_stride_o, long long part_stride_lse, int B, int H,
-                             int D, void* o, long long o_sb, long long o_sh, int out_fp32,
-                             float* lse, cudaStream_t stream) {
+                             int D, int d_out, void* o, long long o_sb, long long o_sh,
+                             int out_fp32, float* lse, cudaStream_t stream) {
   lse_merge_kernel<<<B * H, 128, 0, stream>>>(part_o, part_lse, n_parts, part_stride_o,
-                                              part_stride_lse, B, H, D, o, o_sb, o_sh, out_fp32,
-                                              lse);
+                                              part_stride_lse, B, H, D, d_out, o, o_sb, o_sh,
+                                              out_fp32, lse);
   return cudaGetLastError();
 }
 

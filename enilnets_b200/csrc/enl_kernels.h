@@ -14,6 +14,7 @@ namespace enl {
 // at k_pos0 + j.
 struct PrefillParams {
   int B, H, Hkv, Sq, Skv;
+  int d_real;                  // head dim of the tensors (<= the kernel's D; the rest is TMA zero fill)
   void* o;
   long long o_sb, o_ss, o_sh;  // element strides of O
   int out_fp32;                // 0: bf16 output, 1: fp32 output
@@ -34,6 +35,7 @@ cudaError_t launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const C
 // K2 split-KV decode: one query token per (b, h) against cached slots.
 struct DecodeParams {
   int B, H, Hkv;
+  int d_real;  // head dim of the tensors (<= the kernel's D); lanes past it read zeros
   const void* q;  // bf16 q[b, h, :]
   long long q_sb, q_sh;
   const void* k;  // bf16 cache[b, hkv, slot, :]
@@ -57,10 +59,11 @@ template <int D>
 cudaError_t launch_decode(const DecodeParams& p, cudaStream_t stream);
 
 // LSE merge of n_parts normalised partials (o_i, lse_i) into one output.
+// part_o rows hold D floats; the first d_out of them are written to o.
 cudaError_t launch_lse_merge(const float* part_o, const float* part_lse, int n_parts,
                              long long part_stride_o, long long part_stride_lse, int B, int H,
-                             int D, void* o, long long o_sb, long long o_sh, int out_fp32,
-                             float* lse, cudaStream_t stream);
+                             int D, int d_out, void* o, long long o_sb, long long o_sh,
+                             int out_fp32, float* lse, cudaStream_t stream);
 
 // K3 cache append: cache[b, h, slot0 + t, :] = src[b, t, h, :].
 cudaError_t launch_kv_append(void* cache, long long c_sb, long long c_sh, long long c_ss,

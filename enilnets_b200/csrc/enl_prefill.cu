@@ -535,19 +535,23 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = NAN;
           }
+          // Columns past the tensors' head dim are TMA zero fill: not stored.
+          const int col0 = c0 + c * 32;
           if (row_valid && p.out_fp32) {
             float4* dst = reinterpret_cast<float4*>(orow + c * 32 * 4);
 #pragma unroll
             for (int i = 0; i < 8; ++i)
-              dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+              if (col0 + 4 * i + 4 <= p.d_real)
+                dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
           } else if (row_valid) {
             uint4* dst = reinterpret_cast<uint4*>(orow + c * 32 * 2);
 #pragma unroll
             for (int i = 0; i < 4; ++i)
-              dst[i] = make_uint4(pack_bf16x2(v[8 * i], v[8 * i + 1]),
-                                  pack_bf16x2(v[8 * i + 2], v[8 * i + 3]),
-                                  pack_bf16x2(v[8 * i + 4], v[8 * i + 5]),
-                                  pack_bf16x2(v[8 * i + 6], v[8 * i + 7]));
+              if (col0 + 8 * i + 8 <= p.d_real)
+                dst[i] = make_uint4(pack_bf16x2(v[8 * i], v[8 * i + 1]),
+                                    pack_bf16x2(v[8 * i + 2], v[8 * i + 3]),
+                                    pack_bf16x2(v[8 * i + 4], v[8 * i + 5]),
+                                    pack_bf16x2(v[8 * i + 6], v[8 * i + 7]));
           }
         }
         if (p.lse != nullptr && row_valid && half == 0) {

@@ -72,7 +72,8 @@ typedef struct enl_prefill_args {
  * Replaces the score/softmax/context math of nn/forward.py:525-551 (MHA),
  * nn/flash_attention.py:42-80 (tiled softmax), nn/forward.py:578-586 (cross
  * attention), the cached multi-token step nn/kvcache.py:198-213, and the
- * key-padding rule of graph/sequence.py:159-183. head_dim 64 or 128. */
+ * key-padding rule of graph/sequence.py:159-183. head_dim: any multiple of 8
+ * up to 128 (the kernel runs at 64 or 128 with TMA zero fill). */
 int enl_attn_prefill(const enl_prefill_args* args, void* stream);
 
 /* ----------------------------------------------------------------- decode */
@@ -100,7 +101,8 @@ typedef struct enl_decode_args {
 
 /* Split-KV single-token decode with log-sum-exp merge of the splits.
  * Replaces the attention half of nn/kvcache.py:_attention_step (lines
- * 198-213) for one new token; head_dim 64 or 128, num_heads/num_kv_heads in
+ * 198-213) for one new token; head_dim a multiple of 8 up to 128,
+ * num_heads/num_kv_heads in
  * {1, 2, 4, 8}. */
 int enl_attn_decode(const enl_decode_args* args, void* stream);
 

@@ -273,6 +273,116 @@ def kvcache_cases():
     np.savez_compressed(HERE / "kvcache_stepping.npz", **out)
 
 
+def layer_b200_cases():
+    """Layer-level cases at head dims the kernels take (multiples of 8): full
+    MHA layers, graph padding, cross attention and KV-cache stepping, run by
+    the reference in float64 with its own seeded weights. Only outputs are
+    stored: the tests rebuild each model from the same seed with the
+    reference-order builders of enilnets_b200.layers (seeds: 1100+i for MHA
+    weights, 1200+i for its input; 1300+i / 1400+i graph; 1500+i / 1600+i
+    cross; 1700+i / 1800+i KV stepping)."""
+    out = {}
+    meta = {"mha": [], "graph": [], "cross": [], "kv": []}
+    configs = [
+        dict(embed_dim=64, num_heads=4, causal=True),
+        dict(embed_dim=64, num_heads=4, causal=False),
+        dict(embed_dim=64, num_heads=4, causal=True, window_size=5),
+        dict(embed_dim=64, num_heads=4, causal=True, positional_scheme="rope"),
+        dict(embed_dim=64, num_heads=4, causal=False, positional_scheme="alibi"),
+        dict(embed_dim=64, num_heads=4, causal=True, positional_scheme="alibi", window_size=9),
+        dict(embed_dim=64, num_heads=4, causal=True, num_kv_heads=2),
+        dict(embed_dim=64, num_heads=4, causal=True, num_kv_heads=1, positional_scheme="rope"),
+        dict(embed_dim=128, num_heads=2, causal=True),
+    ]
+    for i, cfg in enumerate(configs):
+        Enilnets.core.utils.set_seed(1100 + i)
+        m = NeuralNet()
+        m.add_multihead_attention(**cfg)
+        x = np.random.RandomState(1200 + i).standard_normal((2, 40, cfg["embed_dim"]))
+        y = m.Forward(x, training=False)
+        out[f"mha{i}_y"] = y.astype(np.float32)
+        meta["mha"].append(cfg)
+    i = 0
+    for causal in (False, True):
+        for window in (None, 3):
+            for lengths in ([33, 17, 1], [33, 20, 0]):
+                Enilnets.core.utils.set_seed(1300 + i)
+                g = MultiHeadAttention(64, 4, causal=causal, window_size=window)
+                x = np.random.RandomState(1400 + i).standard_normal((3, 33, 64))
+                mask = np.asarray(lengths_to_mask(lengths, 33))
+                y = g(Tensor(x), key_padding_mask=mask).data
+                out[f"graph{i}_y"] = y.astype(np.float32)
+                meta["graph"].append({"causal": causal, "window_size": window,
+                                      "embed_dim": 64, "num_heads": 4, "lengths": lengths})
+                i += 1
+    for i, hkv in enumerate((None, 2)):
+        Enilnets.core.utils.set_seed(1500 + i)
+        m = NeuralNet()
+        m.add_dense(64, 64, activation="linear")
+        m.add_cross_attention(kv_source_index=-1, embed_dim=64, num_heads=4, num_kv_heads=hkv)
+        x = np.random.RandomState(1600 + i).standard_normal((2, 24, 64))
+        y = m.Forward(x, training=False)
+        out[f"cross{i}_y"] = y.astype(np.float32)
+        meta["cross"].append({"num_kv_heads": hkv})
+    i = 0
+    for scheme in ("absolute", "rope", "alibi"):
+        for hkv, window in ((None, None), (2, 3)):
+            Enilnets.core.utils.set_seed(1700 + i)
+            m = NeuralNet()
+            m.add_embedding(vocab_size=17, embed_dim=64)
+            if scheme == "absolute":
+                m.add_positional_encoding(max_seq_len=32, learnable=False)
+            m.add_transformer_block(64, num_heads=4, causal=True, positional_scheme=scheme,
+                                    num_kv_heads=hkv, window_size=window)
+            m.add_layernorm()
+            m.add_dense(n_out=17, activation="linear")
+            toks = np.random.RandomState(1800 + i).randint(0, 17, size=(3, 9))
+            full = m.Forward(toks, training=False)
+            cache = kvc.KVCache()
+            pieces = [kvc.cached_forward_step(m, toks[:, :4], cache)]
+            pieces += [kvc.cached_forward_step(m, toks[:, j:j + 1], cache) for j in range(4, 9)]
+            out[f"kv{i}_full"] = full.astype(np.float32)
+            out[f"kv{i}_stepped"] = np.concatenate(pieces, axis=1).astype(np.float32)
+            attn_idx = [j for j, l in enumerate(m.layers) if l["type"] == "multihead_attention"][0]
+            out[f"kv{i}_kshape"] = np.array(cache.kv[attn_idx][0].shape)
+            out[f"kv{i}_start"] = np.array(cache.kv[attn_idx][2])
+            # reorder: expand row 0 to 3 beams, one step, gather by parents, one step
+            cache2 = kvc.KVCache()
+            kvc.cached_forward_step(m, toks[:1, :4], cache2)
+            cache2.expand(3)
+            kvc.cached_forward_step(m, np.array([[5], [6], [7]]), cache2)
+            cache2.reorder([2, 2, 0])
+            out[f"kv{i}_reordered"] = kvc.cached_forward_step(
+                m, np.array([[9], [9], [9]]), cache2).astype(np.float32)
+            meta["kv"].append({"scheme": scheme, "num_kv_heads": hkv, "window_size": window})
+            i += 1
+    out["meta"] = np.array(json.dumps(meta))
+    np.savez_compressed(HERE / "layer_b200.npz", **out)
+
+
+def config1_case():
+    """BASELINE config 1 exactly: set_seed(0), add_multihead_attention(256, 8,
+    causal=True) at the reference's default float32, x ~ RandomState(1);
+    the output of batch row 0 from the float64 path, plus SHA-256 digests of
+    the seeded float32 weights (to pin the builders' RNG order)."""
+    import hashlib
+    backend.use_float64(False)
+    Enilnets.core.utils.set_seed(0)
+    m = NeuralNet()
+    m.add_multihead_attention(embed_dim=256, num_heads=8, causal=True)
+    digests = {k: hashlib.sha256(np.ascontiguousarray(m.layers[0][k]).tobytes()).hexdigest()
+               for k in ("Wq", "bq", "Wk", "bk", "Wv", "bv", "Wo", "bo")}
+    layer = {k: np.asarray(v, np.float64) if isinstance(v, np.ndarray) else v
+             for k, v in m.layers[0].items()}
+    backend.use_float64(True)
+    m64 = NeuralNet()
+    m64.layers = [layer]
+    x = np.random.RandomState(1).standard_normal((4, 256, 256))
+    y = m64.Forward(x, training=False)
+    np.savez_compressed(HERE / "config1.npz", y0=y[0].astype(np.float32),
+                        digests=np.array(json.dumps(digests)))
+
+
 def main():
     flash_cases()
     mha_layer_cases()
@@ -281,6 +391,8 @@ def main():
     kernel_prefill_cases()
     kernel_decode_cases()
     kvcache_cases()
+    layer_b200_cases()
+    config1_case()
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size)
 

@@ -77,8 +77,8 @@ def test_validation_errors_raise_before_launch():
         _native.check(lib.enl_attn_prefill(ctypes.byref(a), None), "enl_attn_prefill")
     a.q = a.k = a.v = a.o = 16
     a.batch = a.num_heads = a.num_kv_heads = a.seq_q = a.seq_kv = 1
-    a.head_dim = 96
-    with pytest.raises(ValueError, match="head_dim=96"):
+    a.head_dim = 100
+    with pytest.raises(ValueError, match="head_dim=100"):
         _native.check(lib.enl_attn_prefill(ctypes.byref(a), None), "enl_attn_prefill")
     a.head_dim = 64
     a.num_kv_heads = 3
