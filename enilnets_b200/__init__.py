@@ -14,7 +14,8 @@ Python host side that mirrors the reference's layer interface:
 """
 __version__ = "0.2.0"
 
-from .backend import default_dtype, is_float64_enabled, set_seed, use_float64  # noqa: F401
+from .backend import (default_dtype, is_float64_enabled, precision, set_precision,  # noqa: F401
+                      set_seed, use_float64)
 from .graph import MultiHeadAttention, lengths_to_mask  # noqa: F401
 from .kvcache import KVCache, cached_forward_step  # noqa: F401
 from .layers import (add_cross_attention, add_multihead_attention,  # noqa: F401

@@ -32,6 +32,9 @@ DEVICE_ERRORS = {1: "an mbarrier wait exceeded its time budget",
                  3: "a launch-time shape invariant was violated"}
 
 
+ABI_VERSION = 2  # ENL_ABI_VERSION of include/enl_attn.h
+
+
 class PrefillArgs(Structure):
     """Mirror of enl_prefill_args (field order and types match the header)."""
     _fields_ = [
@@ -48,6 +51,7 @@ class PrefillArgs(Structure):
         ("kv_valid_len", c_void_p), ("alibi_slopes", c_void_p),
         ("q_pos0", c_int64), ("k_pos0", c_int64),
         ("scale", c_float),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t),
     ]
 
 
@@ -73,6 +77,7 @@ class DecodeArgs(Structure):
 # (a CPU test checks every declared symbol is exported and bound here).
 SIGNATURES = {
     "enl_attn_prefill": ([POINTER(PrefillArgs), c_void_p], c_int32),
+    "enl_prefill_workspace_bytes": ([POINTER(PrefillArgs)], c_size_t),
     "enl_attn_decode": ([POINTER(DecodeArgs), c_void_p], c_int32),
     "enl_attn_decode_noalloc": ([POINTER(DecodeArgs), c_void_p], c_int32),
     "enl_decode_auto_splits": ([c_int32, c_int32, c_int32], c_int32),
@@ -110,6 +115,10 @@ def load() -> ctypes.CDLL:
         fn = getattr(lib, name)
         fn.argtypes = argtypes
         fn.restype = restype
+    if lib.enl_abi_version() != ABI_VERSION:
+        raise RuntimeError(
+            f"{LIB_PATH.name} has ABI version {lib.enl_abi_version()}, these bindings expect "
+            f"{ABI_VERSION}: rebuild it with `python -m enilnets_b200.build --force`.")
     _lib = lib
     return lib
 

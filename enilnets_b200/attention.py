@@ -5,8 +5,9 @@ Mirrors the reference's attention branches layer by layer:
                              GQA, causal/window masks, softmax, Wo)
   * cross-attention          nn/forward.py:557-591
   * key-padding (graph MHA)  graph/sequence.py:144-183 (additive -1e9 rule)
-The projections are plain bf16 GEMMs (cuBLAS through torch); Q/K/V are never
-copied or expanded: the prefill kernel (K1) reads them as strided head views
+The projections are plain GEMMs (cuBLAS through torch) in the precision that
+backend.set_precision selects (fp32 or bf16); Q/K/V are never copied or
+expanded: the prefill kernel (K1) reads them as strided head views
 of the fused QKV projection output and indexes K/V heads group-major
 (nn/forward.py:165-171) instead of repeating them.
 """
@@ -18,7 +19,7 @@ from typing import Optional
 import numpy as np
 
 from . import kernels
-from .backend import device, to_device
+from .backend import compute_dtype, device, to_device
 
 SINUSOIDAL_BASE = 10000.0  # core/constants.py:70
 
@@ -39,16 +40,15 @@ def check_supported(layer: dict, training: bool = False) -> None:
 
 # --------------------------------------------------------------- caches
 class _LayerWeights:
-    """bf16 device copies of one layer's projections, rebuilt whenever an
-    array in the layer dict is replaced."""
+    """Device copies (in the compute dtype) of one layer's concatenated
+    projections, rebuilt whenever an array in the layer dict is replaced."""
 
     def __init__(self):
         self._store = {}
 
-    def get(self, layer: dict, names, kind):
-        import torch
+    def get(self, layer: dict, names, kind, dtype):
         arrays = tuple(layer[n] for n in names)
-        key = (kind,) + tuple(id(a) for a in arrays)
+        key = (kind, dtype) + tuple(id(a) for a in arrays)
         hit = self._store.get(key)
         if hit is not None and all(x is y for x, y in zip(hit[0], arrays)):
             return hit[1]
@@ -56,7 +56,7 @@ class _LayerWeights:
             host = np.concatenate([np.asarray(a, np.float32) for a in arrays], axis=0)
         else:
             host = np.concatenate([np.asarray(a, np.float32).reshape(-1) for a in arrays])
-        t = to_device(host, torch.bfloat16)
+        t = to_device(host, dtype)
         self._store[key] = (arrays, t)
         return t
 
@@ -111,15 +111,16 @@ def apply_rope(t, pos0: int):
 
 # ---------------------------------------------------------- projections
 def project(x, layer: dict, which: str):
-    """x @ W.T + b for W in {"q", "kv", "qkv", "o"} as one bf16 GEMM
-    (nn/forward.py:428-430, :551)."""
-    import torch
+    """x @ W.T + b for W in {"q", "kv", "qkv", "o"} as one GEMM in the compute
+    dtype (nn/forward.py:428-430, :551). fp32 GEMMs follow torch's matmul
+    precision setting, which is full fp32 unless the caller enabled TF32."""
     import torch.nn.functional as F
     names = {"q": (("Wq",), ("bq",)), "kv": (("Wk", "Wv"), ("bk", "bv")),
              "qkv": (("Wq", "Wk", "Wv"), ("bq", "bk", "bv")), "o": (("Wo",), ("bo",))}[which]
-    w = _WEIGHTS.get(layer, names[0], "w")
-    b = _WEIGHTS.get(layer, names[1], "b")
-    return F.linear(x.to(torch.bfloat16), w, b)
+    dt = compute_dtype()
+    w = _WEIGHTS.get(layer, names[0], "w", dt)
+    b = _WEIGHTS.get(layer, names[1], "b", dt)
+    return F.linear(x.to(dt), w, b)
 
 
 def split_heads(t, heads: int, head_dim: int, offset: int = 0):
@@ -169,7 +170,7 @@ def self_attention(layer: dict, x, key_padding_mask=None, mask_mode: Optional[st
     ctx = kernels.attention_prefill(
         q, k, v, causal=bool(layer.get("causal", False)), window=layer.get("window_size"),
         kv_valid_len=lens, alibi_slopes=alibi_tensor(H) if scheme == "alibi" else None,
-        mask_mode=mode)
+        mask_mode=mode, out_dtype=compute_dtype())
     return project(ctx.flatten(-2), layer, "o").float()
 
 
@@ -192,5 +193,6 @@ def cross_attention(layer: dict, x, memory, memory_key_padding_mask=None):
     if memory_key_padding_mask is not None:
         lens = to_device(lengths_from_mask(memory_key_padding_mask, B, Skv), torch.int32)
         mode = "additive"
-    ctx = kernels.attention_prefill(q, k, v, causal=False, kv_valid_len=lens, mask_mode=mode)
+    ctx = kernels.attention_prefill(q, k, v, causal=False, kv_valid_len=lens, mask_mode=mode,
+                                    out_dtype=compute_dtype())
     return project(ctx.flatten(-2), layer, "o").float()

@@ -10,15 +10,40 @@ from __future__ import annotations
 
 import numpy as np
 
-_STATE = {"float64": False}
+_STATE = {"float64": False, "precision": "fp32"}
+_PRECISIONS = ("fp32", "bf16")
 
 
 def use_float64(enabled: bool = True) -> None:
     """Default working precision of the NumPy side (weights built, arrays
     returned): float64 when enabled, else float32 (core/backend.py:126-130).
-    The attention core itself always runs the B200 kernels (bf16 tensor
-    cores with fp32 accumulation)."""
+    The device arithmetic is chosen by set_precision."""
     _STATE["float64"] = bool(enabled)
+
+
+def set_precision(mode: str) -> None:
+    """Device arithmetic of the attention layers.
+
+    "fp32" (default, the reference's float32 models): fp32 projection GEMMs,
+    attention on the split-bf16 tensor-core path (hi*hi + hi*lo + lo*hi per
+    product, about 2^-16 relative error), fp32 KV cache.
+    "bf16": bf16 projections, bf16 attention inputs with fp32 accumulation,
+    bf16 KV cache: the fast path, max abs error ~1e-2 per attention layer on
+    unit-variance activations.
+    """
+    if mode not in _PRECISIONS:
+        raise ValueError(f"precision must be one of {_PRECISIONS}, got {mode!r}")
+    _STATE["precision"] = mode
+
+
+def precision() -> str:
+    return _STATE["precision"]
+
+
+def compute_dtype():
+    """torch dtype of projections, attention inputs and the KV cache."""
+    import torch
+    return torch.float32 if _STATE["precision"] == "fp32" else torch.bfloat16
 
 
 def is_float64_enabled() -> bool:

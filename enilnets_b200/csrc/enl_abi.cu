@@ -124,9 +124,10 @@ int enl_attn_prefill(const enl_prefill_args* a, void* stream) {
     return fail(ENL_ERR_UNSUPPORTED,
                 "enl_attn_prefill: head_dim=%d (supported: multiples of 8 up to 128)",
                 a->head_dim);
-  if (a->in_dtype != ENL_DTYPE_BF16)
-    return fail(ENL_ERR_UNSUPPORTED, "enl_attn_prefill: in_dtype=%d (supported: bf16)",
-                a->in_dtype);
+  if (a->in_dtype != ENL_DTYPE_BF16 && a->in_dtype != ENL_DTYPE_FP32)
+    return fail(ENL_ERR_INVALID, "enl_attn_prefill: in_dtype=%d", a->in_dtype);
+  const bool split = a->in_dtype == ENL_DTYPE_FP32;
+  const int esz = split ? 4 : 2;
   if (a->out_dtype != ENL_DTYPE_BF16 && a->out_dtype != ENL_DTYPE_FP32)
     return fail(ENL_ERR_INVALID, "enl_attn_prefill: out_dtype=%d", a->out_dtype);
   if (a->mask_mode != ENL_MASK_EXCLUDE && a->mask_mode != ENL_MASK_ADDITIVE)
@@ -134,9 +135,9 @@ int enl_attn_prefill(const enl_prefill_args* a, void* stream) {
   if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->o))
     return fail(ENL_ERR_INVALID, "enl_attn_prefill: q, k, v, o must be 16-byte aligned");
   int st;
-  if ((st = check_strides_16B("q", a->q_stride_b, a->q_stride_s, a->q_stride_h, 2))) return st;
-  if ((st = check_strides_16B("k", a->k_stride_b, a->k_stride_s, a->k_stride_h, 2))) return st;
-  if ((st = check_strides_16B("v", a->v_stride_b, a->v_stride_s, a->v_stride_h, 2))) return st;
+  if ((st = check_strides_16B("q", a->q_stride_b, a->q_stride_s, a->q_stride_h, esz))) return st;
+  if ((st = check_strides_16B("k", a->k_stride_b, a->k_stride_s, a->k_stride_h, esz))) return st;
+  if ((st = check_strides_16B("v", a->v_stride_b, a->v_stride_s, a->v_stride_h, esz))) return st;
   if ((st = check_strides_16B("o", a->o_stride_b, a->o_stride_s, a->o_stride_h,
                               a->out_dtype == ENL_DTYPE_FP32 ? 4 : 2)))
     return st;
@@ -147,16 +148,49 @@ int enl_attn_prefill(const enl_prefill_args* a, void* stream) {
   // The kernel runs at D = 64 or 128; smaller head dims are zero-filled by
   // TMA (the tensor maps keep the real extent) and never stored.
   const int D = a->head_dim <= 64 ? 64 : 128;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   CUtensorMap tq, tk, tv;
-  if ((st = make_qkv_map(&tq, a->q, a->head_dim, a->seq_q, a->num_heads, a->batch, a->q_stride_s,
-                         a->q_stride_h, a->q_stride_b, "q")))
-    return st;
-  if ((st = make_qkv_map(&tk, a->k, a->head_dim, a->seq_kv, a->num_kv_heads, a->batch, a->k_stride_s,
-                         a->k_stride_h, a->k_stride_b, "k")))
-    return st;
-  if ((st = make_qkv_map(&tv, a->v, a->head_dim, a->seq_kv, a->num_kv_heads, a->batch, a->v_stride_s,
-                         a->v_stride_h, a->v_stride_b, "v")))
-    return st;
+  if (!split) {
+    if ((st = make_qkv_map(&tq, a->q, a->head_dim, a->seq_q, a->num_heads, a->batch,
+                           a->q_stride_s, a->q_stride_h, a->q_stride_b, "q")))
+      return st;
+    if ((st = make_qkv_map(&tk, a->k, a->head_dim, a->seq_kv, a->num_kv_heads, a->batch,
+                           a->k_stride_s, a->k_stride_h, a->k_stride_b, "k")))
+      return st;
+    if ((st = make_qkv_map(&tv, a->v, a->head_dim, a->seq_kv, a->num_kv_heads, a->batch,
+                           a->v_stride_s, a->v_stride_h, a->v_stride_b, "v")))
+      return st;
+  } else {
+    // fp32: (hi, lo) planes of q, k, v in the workspace, then tensor maps
+    // over them with the planes as 2 * heads "heads" of a contiguous tensor.
+    const size_t need = enl_prefill_workspace_bytes(a);
+    if (!a->workspace || a->workspace_bytes < need)
+      return fail(ENL_ERR_INVALID,
+                  "enl_attn_prefill: fp32 inputs need a %zu-byte workspace (got %zu)", need,
+                  a->workspace_bytes);
+    if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0)
+      return fail(ENL_ERR_INVALID, "enl_attn_prefill: workspace must be 256-byte aligned");
+    const int Dr = a->head_dim;
+    uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
+    struct Op {
+      const void* src;
+      int64_t sb, ss, sh;
+      int S, H;
+      CUtensorMap* map;
+      const char* name;
+    } ops[3] = {{a->q, a->q_stride_b, a->q_stride_s, a->q_stride_h, a->seq_q, a->num_heads, &tq, "q"},
+                {a->k, a->k_stride_b, a->k_stride_s, a->k_stride_h, a->seq_kv, a->num_kv_heads, &tk, "k"},
+                {a->v, a->v_stride_b, a->v_stride_s, a->v_stride_h, a->seq_kv, a->num_kv_heads, &tv, "v"}};
+    for (const Op& op : ops) {
+      const int64_t hs = Dr, ss = 2ll * op.H * Dr, bs = ss * op.S;  // plane tensor strides
+      cudaError_t e = launch_split_planes(reinterpret_cast<const float*>(op.src), op.sb, op.ss,
+                                          op.sh, a->batch, op.S, op.H, Dr, ws, s);
+      if (e != cudaSuccess) return cuda_fail(e, "enl_attn_prefill: split planes");
+      if ((st = make_qkv_map(op.map, ws, Dr, op.S, 2 * op.H, a->batch, ss, hs, bs, op.name)))
+        return st;
+      ws += (((size_t)a->batch * bs * 2) + 255) & ~size_t(255);
+    }
+  }
 
   PrefillParams p;
   p.d_real = a->head_dim;
@@ -180,11 +214,23 @@ int enl_attn_prefill(const enl_prefill_args* a, void* stream) {
   p.k_pos0 = a->k_pos0;
   p.scale_log2 = a->scale * 1.4426950408889634f;
 
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  cudaError_t e = (D == 128) ? launch_prefill<128>(tq, tk, tv, p, s)
-                             : launch_prefill<64>(tq, tk, tv, p, s);
+  cudaError_t e;
+  if (split)
+    e = (D == 128) ? launch_prefill<128, true>(tq, tk, tv, p, s)
+                   : launch_prefill<64, true>(tq, tk, tv, p, s);
+  else
+    e = (D == 128) ? launch_prefill<128, false>(tq, tk, tv, p, s)
+                   : launch_prefill<64, false>(tq, tk, tv, p, s);
   if (e != cudaSuccess) return cuda_fail(e, "enl_attn_prefill launch");
   return ENL_OK;
+}
+
+size_t enl_prefill_workspace_bytes(const enl_prefill_args* a) {
+  if (!a || a->in_dtype != ENL_DTYPE_FP32) return 0;
+  auto planes = [&](int S, int H) {
+    return (((size_t)a->batch * S * H * 2 * a->head_dim * 2) + 255) & ~size_t(255);
+  };
+  return planes(a->seq_q, a->num_heads) + 2 * planes(a->seq_kv, a->num_kv_heads);
 }
 
 int enl_decode_auto_splits(int32_t batch, int32_t num_kv_heads, int32_t n_slots) {
@@ -224,9 +270,9 @@ int enl_attn_decode(const enl_decode_args* a, void* stream) {
                 "enl_attn_decode: head_dim=%d (supported: multiples of 8 up to 128)",
                 a->head_dim);
   const int Dk = a->head_dim <= 64 ? 64 : 128;  // kernel head dim (zero-extended)
-  if (a->in_dtype != ENL_DTYPE_BF16)
-    return fail(ENL_ERR_UNSUPPORTED, "enl_attn_decode: in_dtype=%d (supported: bf16)",
-                a->in_dtype);
+  if (a->in_dtype != ENL_DTYPE_BF16 && a->in_dtype != ENL_DTYPE_FP32)
+    return fail(ENL_ERR_INVALID, "enl_attn_decode: in_dtype=%d", a->in_dtype);
+  const int esz = a->in_dtype == ENL_DTYPE_FP32 ? 4 : 2;
   if (a->out_dtype != ENL_DTYPE_BF16 && a->out_dtype != ENL_DTYPE_FP32)
     return fail(ENL_ERR_INVALID, "enl_attn_decode: out_dtype=%d", a->out_dtype);
   if (a->slot_begin < 0 || a->slot_end < a->slot_begin)
@@ -235,9 +281,9 @@ int enl_attn_decode(const enl_decode_args* a, void* stream) {
   if (!aligned16(a->q) || !aligned16(a->k_cache) || !aligned16(a->v_cache))
     return fail(ENL_ERR_INVALID, "enl_attn_decode: q and caches must be 16-byte aligned");
   int st;
-  if ((st = check_strides_16B("q", a->q_stride_b, 0, a->q_stride_h, 2))) return st;
+  if ((st = check_strides_16B("q", a->q_stride_b, 0, a->q_stride_h, esz))) return st;
   if ((st = check_strides_16B("cache", a->cache_stride_b, a->cache_stride_s, a->cache_stride_h,
-                              2)))
+                              esz)))
     return st;
 
   // Narrow the slot range by causality (keys after the query are invisible)
@@ -269,6 +315,7 @@ int enl_attn_decode(const enl_decode_args* a, void* stream) {
   p.B = a->batch;
   p.H = a->num_heads;
   p.Hkv = a->num_kv_heads;
+  p.in_fp32 = esz == 4;
   p.q = a->q;
   p.q_sb = a->q_stride_b;
   p.q_sh = a->q_stride_h;

@@ -26,6 +26,29 @@ __device__ __forceinline__ uint4 ld_stream(const void* p) {
   return r;
 }
 
+// Eight consecutive head-dim elements of one lane: one 16-byte load of bf16,
+// two of fp32 (raw words; unpack8 converts).
+template <bool kF32>
+struct Chunk {
+  uint4 w[kF32 ? 2 : 1];
+};
+
+template <bool kF32>
+__device__ __forceinline__ Chunk<kF32> ld_chunk(const uint8_t* p) {
+  Chunk<kF32> c;
+  c.w[0] = ld_stream(p);
+  if constexpr (kF32) c.w[1] = ld_stream(p + 16);
+  return c;
+}
+
+template <bool kF32>
+__device__ __forceinline__ Chunk<kF32> zero_chunk() {
+  Chunk<kF32> c;
+#pragma unroll
+  for (int i = 0; i < (kF32 ? 2 : 1); ++i) c.w[i] = make_uint4(0, 0, 0, 0);
+  return c;
+}
+
 __device__ __forceinline__ void unpack8(const uint4& w, float (&f)[8]) {
   f[0] = bf16lo_to_f32(w.x);
   f[1] = bf16hi_to_f32(w.x);
@@ -37,6 +60,22 @@ __device__ __forceinline__ void unpack8(const uint4& w, float (&f)[8]) {
   f[7] = bf16hi_to_f32(w.w);
 }
 
+template <bool kF32>
+__device__ __forceinline__ void unpack8(const Chunk<kF32>& c, float (&f)[8]) {
+  if constexpr (kF32) {
+    f[0] = __uint_as_float(c.w[0].x);
+    f[1] = __uint_as_float(c.w[0].y);
+    f[2] = __uint_as_float(c.w[0].z);
+    f[3] = __uint_as_float(c.w[0].w);
+    f[4] = __uint_as_float(c.w[1].x);
+    f[5] = __uint_as_float(c.w[1].y);
+    f[6] = __uint_as_float(c.w[1].z);
+    f[7] = __uint_as_float(c.w[1].w);
+  } else {
+    unpack8(c.w[0], f);
+  }
+}
+
 template <int D, int G>
 struct DecodeCfg {
   static constexpr int kThreads = 128;
@@ -46,8 +85,9 @@ struct DecodeCfg {
   static constexpr int kUnroll = (G >= 4) ? 2 : 4;  // bounded by registers at large G
 };
 
-template <int D, int G>
+template <int D, int G, bool kF32>
 __global__ void __launch_bounds__(128) attn_decode_kernel(const DecodeParams p) {
+  constexpr int kEsz = kF32 ? 4 : 2;  // element bytes
   using Cfg = DecodeCfg<D, G>;
   constexpr int LPK = Cfg::kLanesPerKey;
   constexpr int NG = Cfg::kGroups;
@@ -73,11 +113,9 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const DecodeParams p) 
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     const int h = hkv * G + g;
-    const uint4 w = lane_live ? *reinterpret_cast<const uint4*>(
-                                    reinterpret_cast<const __nv_bfloat16*>(p.q) +
-                                    (long long)b * p.q_sb + (long long)h * p.q_sh + sub * 8)
-                              : make_uint4(0, 0, 0, 0);
-    unpack8(w, q[g]);
+    const uint8_t* qp = reinterpret_cast<const uint8_t*>(p.q) +
+                        ((long long)b * p.q_sb + (long long)h * p.q_sh + sub * 8) * kEsz;
+    unpack8(lane_live ? ld_chunk<kF32>(qp) : zero_chunk<kF32>(), q[g]);
 #pragma unroll
     for (int i = 0; i < 8; ++i) q[g][i] *= p.scale_log2;
     slope2[g] = p.alibi ? p.alibi[h] * 1.4426950408889634f : 0.0f;
@@ -92,28 +130,29 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const DecodeParams p) 
     for (int i = 0; i < 8; ++i) acc[g][i] = 0.0f;
   }
 
-  const __nv_bfloat16* kbase = reinterpret_cast<const __nv_bfloat16*>(p.k) +
-                               (long long)b * p.k_sb + (long long)hkv * p.k_sh + sub * 8;
-  const __nv_bfloat16* vbase = reinterpret_cast<const __nv_bfloat16*>(p.v) +
-                               (long long)b * p.v_sb + (long long)hkv * p.v_sh + sub * 8;
+  const uint8_t* kbase = reinterpret_cast<const uint8_t*>(p.k) +
+                         ((long long)b * p.k_sb + (long long)hkv * p.k_sh + sub * 8) * kEsz;
+  const uint8_t* vbase = reinterpret_cast<const uint8_t*>(p.v) +
+                         ((long long)b * p.v_sb + (long long)hkv * p.v_sh + sub * 8) * kEsz;
+  const long long k_ss = p.k_ss * kEsz, v_ss = p.v_ss * kEsz;  // bytes per slot
 
   // The loop bound is warp-uniform (the shuffles below need the whole warp);
   // each lane group masks its own slots past the end of the split.
   const int group_in_warp = lane / LPK;
   for (int sw = s_begin + warp * Cfg::kKeysPerWarp; sw < s_end; sw += NG * U) {
     const int s0 = sw + group_in_warp;
-    uint4 kr[U], vr[U];
+    Chunk<kF32> kr[U], vr[U];
     bool valid[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int slot = s0 + u * NG;
       valid[u] = slot < s_end;
       if (valid[u] && lane_live) {
-        kr[u] = ld_stream(kbase + (long long)slot * p.k_ss);
-        vr[u] = ld_stream(vbase + (long long)slot * p.v_ss);
+        kr[u] = ld_chunk<kF32>(kbase + (long long)slot * k_ss);
+        vr[u] = ld_chunk<kF32>(vbase + (long long)slot * v_ss);
       } else {
-        kr[u] = make_uint4(0, 0, 0, 0);
-        vr[u] = make_uint4(0, 0, 0, 0);
+        kr[u] = zero_chunk<kF32>();
+        vr[u] = zero_chunk<kF32>();
       }
     }
     float kf[U][8], vf[U][8];
@@ -214,7 +253,10 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const DecodeParams p) 
 template <int D, int G>
 static cudaError_t launch_decode_g(const DecodeParams& p, cudaStream_t stream) {
   dim3 grid(p.n_splits, p.B * p.Hkv);
-  attn_decode_kernel<D, G><<<grid, DecodeCfg<D, G>::kThreads, 0, stream>>>(p);
+  if (p.in_fp32)
+    attn_decode_kernel<D, G, true><<<grid, DecodeCfg<D, G>::kThreads, 0, stream>>>(p);
+  else
+    attn_decode_kernel<D, G, false><<<grid, DecodeCfg<D, G>::kThreads, 0, stream>>>(p);
   return cudaGetLastError();
 }
 

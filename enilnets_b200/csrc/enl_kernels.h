@@ -28,17 +28,25 @@ struct PrefillParams {
   float scale_log2;            // softmax scale * log2(e)
 };
 
-template <int D>
+// kSplit: the tensor maps cover (hi, lo) bf16 planes of fp32 inputs
+// interleaved per head (head coordinate 2h + plane), see launch_split_planes.
+template <int D, bool kSplit>
 cudaError_t launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                            const PrefillParams& p, cudaStream_t stream);
+
+// fp32 src[b, s, h, :] (element strides, 16-byte aligned rows) ->
+// dst[b][s][h][plane][D] bf16 with plane 0 = bf16(x), plane 1 = bf16(x - hi).
+cudaError_t launch_split_planes(const float* src, long long sb, long long ss, long long sh, int B,
+                                int S, int H, int D, void* dst, cudaStream_t stream);
 
 // K2 split-KV decode: one query token per (b, h) against cached slots.
 struct DecodeParams {
   int B, H, Hkv;
   int d_real;  // head dim of the tensors (<= the kernel's D); lanes past it read zeros
-  const void* q;  // bf16 q[b, h, :]
+  int in_fp32;     // 0: bf16 q and cache, 1: fp32
+  const void* q;  // q[b, h, :]
   long long q_sb, q_sh;
-  const void* k;  // bf16 cache[b, hkv, slot, :]
+  const void* k;  // cache[b, hkv, slot, :]
   const void* v;
   long long k_sb, k_sh, k_ss;
   long long v_sb, v_sh, v_ss;

@@ -50,23 +50,33 @@ constexpr int kEmuEvery = ENL_EXP_EMU_EVERY;
 #define ENL_STAGGER 0
 #endif
 
-template <int D>
+// kSplit: fp32 inputs arrive as two bf16 planes, hi = bf16(x) and
+// lo = bf16(x - hi), and each product is formed from three bf16 MMAs
+// (hi*hi + hi*lo + lo*hi, fp32 accumulate), about 2^-16 relative error:
+// better than tf32 on the same tensor cores. P is split the same way in
+// tensor memory, its lo half over the second 32 columns of each key half.
+template <int D, bool kSplit>
 struct PrefillCfg {
   static constexpr int kThreads = 384;
-  static constexpr int kStages = (D == 128) ? 2 : 4;
+  static constexpr int kPlanes = kSplit ? 2 : 1;  // bf16 planes per operand tile
+  static constexpr int kStages = kSplit ? ((D == 128) ? 1 : 2) : ((D == 128) ? 2 : 4);
   static constexpr int kAtoms = D / 64;  // 128-byte swizzle atoms along the head dim
-  static constexpr int kTileBytes = 128 * D * 2;
+  static constexpr int kTileBytes = 128 * D * 2;          // one plane of a 128-row tile
+  static constexpr int kOpBytes = kPlanes * kTileBytes;   // all planes of one tile
   static constexpr int kAtomBytes = 128 * 128;  // 128 rows x 128 bytes
   static constexpr int kOffQ = 0;
-  static constexpr int kOffK = kOffQ + kTileBytes;
-  static constexpr int kOffV = kOffK + kStages * kTileBytes;
-  static constexpr int kOffX = kOffV + kStages * kTileBytes;  // epilogue exchange
-  static constexpr int kXBytes = 3 * 2 * 128 * 4;              // m, l, tier [2 halves][128]
+  static constexpr int kOffK = kOffQ + kOpBytes;
+  static constexpr int kOffV = kOffK + kStages * kOpBytes;
+  static constexpr int kOffX = kOffV + kStages * kOpBytes;  // epilogue exchange
+  static constexpr int kXBytes = 3 * 2 * 128 * 4;            // m, l, tier [2 halves][128]
   static constexpr int kOffBar = kOffX + kXBytes;
   // q, k_full/empty, v_full/empty, s_full[2], p_ready[2 buf][2 half], o_prog[2], o_done, drain
   static constexpr int kNumBars = 1 + 4 * kStages + 2 + 4 + 2 + 1 + 1;
   static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;  // +align slack
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
   static constexpr uint32_t kTmemCols = 512;
+  // Exponentials from the FMA-pipe polynomial are too coarse for the split path.
+  static constexpr int kEmu = kSplit ? 0 : kEmuEvery;
   __host__ __device__ static constexpr uint32_t col_s(int buf) { return 128u * buf; }
   __host__ __device__ static constexpr uint32_t col_o(int half) { return 256u + D * half; }
 };
@@ -111,12 +121,12 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-template <int D>
+template <int D, bool kSplit>
 __global__ void __launch_bounds__(384, 1)
     attn_prefill_sm100(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v, const PrefillParams p) {
-  using Cfg = PrefillCfg<D>;
+  using Cfg = PrefillCfg<D, kSplit>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -179,9 +189,13 @@ __global__ void __launch_bounds__(384, 1)
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      mbar_arrive_expect_tx(bar_q, Cfg::kTileBytes);
-      for (int a = 0; a < Cfg::kAtoms; ++a)
-        tma_load_4d(smem + Cfg::kOffQ + a * Cfg::kAtomBytes, &tm_q, bar_q, a * 64, r0, h, b);
+      // Split mode: the plane tensors interleave (hi, lo) per head, so plane
+      // pl of head h is "head" kPlanes * h + pl of the tensor map.
+      mbar_arrive_expect_tx(bar_q, Cfg::kOpBytes);
+      for (int pl = 0; pl < Cfg::kPlanes; ++pl)
+        for (int a = 0; a < Cfg::kAtoms; ++a)
+          tma_load_4d(smem + Cfg::kOffQ + pl * Cfg::kTileBytes + a * Cfg::kAtomBytes, &tm_q,
+                      bar_q, a * 64, r0, Cfg::kPlanes * h + pl, b);
       int issued = 0, issued_v = 0;
       bool ok = true;
       for (int j = lo; j < hi && ok; ++j, ++issued) {
@@ -189,19 +203,23 @@ __global__ void __launch_bounds__(384, 1)
         const uint32_t use = issued / Cfg::kStages;
         if (use > 0) ok = mbar_wait(bar_k_empty + st, (use - 1) & 1, abort_flag, 10);
         if (!ok) break;
-        mbar_arrive_expect_tx(bar_k_full + st, Cfg::kTileBytes);
-        for (int a = 0; a < Cfg::kAtoms; ++a)
-          tma_load_4d(smem + Cfg::kOffK + st * Cfg::kTileBytes + a * Cfg::kAtomBytes, &tm_k,
-                      bar_k_full + st, a * 64, j * 128, hkv, b);
+        mbar_arrive_expect_tx(bar_k_full + st, Cfg::kOpBytes);
+        for (int pl = 0; pl < Cfg::kPlanes; ++pl)
+          for (int a = 0; a < Cfg::kAtoms; ++a)
+            tma_load_4d(smem + Cfg::kOffK + st * Cfg::kOpBytes + pl * Cfg::kTileBytes +
+                            a * Cfg::kAtomBytes,
+                        &tm_k, bar_k_full + st, a * 64, j * 128, Cfg::kPlanes * hkv + pl, b);
         if (use > 0) ok = mbar_wait(bar_v_empty + st, (use - 1) & 1, abort_flag, 11);
         if (!ok) {
           ++issued;  // the K load of this iteration is in flight
           break;
         }
-        mbar_arrive_expect_tx(bar_v_full + st, Cfg::kTileBytes);
-        for (int a = 0; a < Cfg::kAtoms; ++a)
-          tma_load_4d(smem + Cfg::kOffV + st * Cfg::kTileBytes + a * Cfg::kAtomBytes, &tm_v,
-                      bar_v_full + st, a * 64, j * 128, hkv, b);
+        mbar_arrive_expect_tx(bar_v_full + st, Cfg::kOpBytes);
+        for (int pl = 0; pl < Cfg::kPlanes; ++pl)
+          for (int a = 0; a < Cfg::kAtoms; ++a)
+            tma_load_4d(smem + Cfg::kOffV + st * Cfg::kOpBytes + pl * Cfg::kTileBytes +
+                            a * Cfg::kAtomBytes,
+                        &tm_v, bar_v_full + st, a * 64, j * 128, Cfg::kPlanes * hkv + pl, b);
         ++issued_v;
       }
       if (*abort_flag) {
@@ -228,28 +246,43 @@ __global__ void __launch_bounds__(384, 1)
       const uint32_t q_lo = desc_lo(smem_u32(smem + Cfg::kOffQ), 16);
       const uint32_t k_lo = desc_lo(smem_u32(smem + Cfg::kOffK), 16);
       const uint32_t v_lo = desc_lo(smem_u32(smem + Cfg::kOffV), Cfg::kAtomBytes);
-      constexpr uint32_t kTileLo = Cfg::kTileBytes >> 4;
+      constexpr uint32_t kTileLo = Cfg::kTileBytes >> 4;  // one plane, 16-byte units
+      constexpr uint32_t kOpLo = Cfg::kOpBytes >> 4;
       auto issue_s = [&](int buf, int st) {
-        const uint32_t ka = k_lo + st * kTileLo;
+        const uint32_t ka = k_lo + st * kOpLo;
         const uint32_t d = tmem_base + Cfg::col_s(buf);
         umma_ss_elect<false>(d, q_lo, ka, kDescHiSw128, idesc_s);
+        if constexpr (kSplit) {
+          umma_ss_elect<true>(d, q_lo, ka + kTileLo, kDescHiSw128, idesc_s);  // Qhi Klo
+          umma_ss_elect<true>(d, q_lo + kTileLo, ka, kDescHiSw128, idesc_s);  // Qlo Khi
+        }
 #pragma unroll
         for (int kk = 1; kk < D / 16; ++kk) {
           const uint32_t off = (kk / 4) * (Cfg::kAtomBytes >> 4) + (kk % 4) * 2;
           umma_ss_elect<true>(d, q_lo + off, ka + off, kDescHiSw128, idesc_s);
+          if constexpr (kSplit) {
+            umma_ss_elect<true>(d, q_lo + off, ka + kTileLo + off, kDescHiSw128, idesc_s);
+            umma_ss_elect<true>(d, q_lo + kTileLo + off, ka + off, kDescHiSw128, idesc_s);
+          }
         }
       };
       // O_hf += P_hf V_hf over one key half: P of half hf sits in columns
       // [64*hf, 64*hf + 32) of the S buffer (two bf16 per column), V_hf is
       // key rows [64*hf, 64*hf + 64) of the V tile.
+      // Split mode adds Phi Vlo and Plo Vhi, Plo in columns [32, 64) of the half.
       auto issue_pv_half = [&](int buf, int st, int hf, bool acc) {
-        const uint32_t va = v_lo + st * kTileLo + hf * 4 * (2048 >> 4);
+        const uint32_t va = v_lo + st * kOpLo + hf * 4 * (2048 >> 4);
         const uint32_t a = tmem_base + Cfg::col_s(buf) + hf * 64;
         const uint32_t d = tmem_base + Cfg::col_o(hf);
-        umma_ts_elect(d, a, va, kDescHiSw128, idesc_o, acc ? 1u : 0u);
 #pragma unroll
-        for (int kk = 1; kk < 4; ++kk)
-          umma_ts_elect(d, a + kk * 8, va + kk * (2048 >> 4), kDescHiSw128, idesc_o, 1u);
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint32_t vk = va + kk * (2048 >> 4);
+          umma_ts_elect(d, a + kk * 8, vk, kDescHiSw128, idesc_o, (acc || kk > 0) ? 1u : 0u);
+          if constexpr (kSplit) {
+            umma_ts_elect(d, a + kk * 8, vk + kTileLo, kDescHiSw128, idesc_o, 1u);
+            umma_ts_elect(d, a + 32 + kk * 8, vk, kDescHiSw128, idesc_o, 1u);
+          }
+        }
       };
       auto wait = [&](uint64_t* bar, uint32_t parity, int site) {
         return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, site));
@@ -420,6 +453,7 @@ __global__ void __launch_bounds__(384, 1)
       const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
       float rowsum = 0.0f;
       uint32_t pk[32];
+      uint32_t pl[kSplit ? 32 : 1];  // split mode: bf16(p - bf16(p)) pairs
       if (full_tile) {
         // Unmasked tile: s is still the raw dot product; fold the scale in
         // with packed FMAs, accumulate the row sum in 4 packed lanes.
@@ -433,7 +467,7 @@ __global__ void __launch_bounds__(384, 1)
           float x0, x1;
           f2_unpack(f2_fma(f2_pack(s[2 * c], s[2 * c + 1]), scale2, negm2), x0, x1);
           float p0, p1;
-          if (kEmuEvery > 0 && (c % (kEmuEvery > 0 ? kEmuEvery : 1)) == kEmuEvery - 1) {
+          if (Cfg::kEmu > 0 && (c % (Cfg::kEmu > 0 ? Cfg::kEmu : 1)) == Cfg::kEmu - 1) {
             exp2_poly2(x0, x1, p0, p1);
           } else {
             p0 = fast_exp2(x0);
@@ -441,6 +475,8 @@ __global__ void __launch_bounds__(384, 1)
           }
           acc[c % 4] = f2_add(acc[c % 4], f2_pack(p0, p1));
           pk[c] = pack_bf16x2(p0, p1);
+          if constexpr (kSplit)
+            pl[c] = pack_bf16x2(p0 - bf16lo_to_f32(pk[c]), p1 - bf16hi_to_f32(pk[c]));
         }
         float a0, a1, a2, a3, a4, a5, a6, a7;
         f2_unpack(acc[0], a0, a1);
@@ -455,6 +491,8 @@ __global__ void __launch_bounds__(384, 1)
           const float p1 = fast_exp2(s[2 * c + 1] - m_use);
           rowsum += p0 + p1;
           pk[c] = pack_bf16x2(p0, p1);
+          if constexpr (kSplit)
+            pl[c] = pack_bf16x2(p0 - bf16lo_to_f32(pk[c]), p1 - bf16hi_to_f32(pk[c]));
         }
       }
       l_run = l_run * factor + rowsum;
@@ -478,6 +516,7 @@ __global__ void __launch_bounds__(384, 1)
       }
       // Publish this half of P over its own first 32 S columns.
       ENL_TMEM_ST32(s_addr, pk, 0);
+      if constexpr (kSplit) ENL_TMEM_ST32(s_addr + 32, pl, 0);
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
@@ -573,13 +612,13 @@ __global__ void __launch_bounds__(384, 1)
   }
 }
 
-template <int D>
+template <int D, bool kSplit>
 cudaError_t launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                            const PrefillParams& p, cudaStream_t stream) {
-  using Cfg = PrefillCfg<D>;
+  using Cfg = PrefillCfg<D, kSplit>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attn_prefill_sm100<D>,
+    cudaError_t e = cudaFuncSetAttribute(attn_prefill_sm100<D, kSplit>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Cfg::kSmemBytes);
     if (e != cudaSuccess) return e;
@@ -587,13 +626,55 @@ cudaError_t launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const C
   }
   const int q_tiles = (p.Sq + 127) / 128;
   dim3 grid(q_tiles, p.B * p.H);
-  attn_prefill_sm100<D><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(tq, tk, tv, p);
+  attn_prefill_sm100<D, kSplit><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(tq, tk, tv, p);
   return cudaGetLastError();
 }
 
-template cudaError_t launch_prefill<64>(const CUtensorMap&, const CUtensorMap&,
-                                        const CUtensorMap&, const PrefillParams&, cudaStream_t);
-template cudaError_t launch_prefill<128>(const CUtensorMap&, const CUtensorMap&,
-                                         const CUtensorMap&, const PrefillParams&, cudaStream_t);
+#define ENL_INST_PREFILL(D, S)                                                              \
+  template cudaError_t launch_prefill<D, S>(const CUtensorMap&, const CUtensorMap&,          \
+                                            const CUtensorMap&, const PrefillParams&,        \
+                                            cudaStream_t);
+ENL_INST_PREFILL(64, false)
+ENL_INST_PREFILL(128, false)
+ENL_INST_PREFILL(64, true)
+ENL_INST_PREFILL(128, true)
+#undef ENL_INST_PREFILL
+
+// fp32 -> (hi, lo) bf16 planes for the split path: dst[b][s][h][plane][d],
+// hi = bf16(x), lo = bf16(x - hi). Four elements per thread (16-byte load,
+// two 8-byte stores).
+__global__ void split_planes_kernel(const float* __restrict__ src, long long sb, long long ss,
+                                    long long sh, int B, int S, int H, int D,
+                                    uint16_t* __restrict__ dst) {
+  const int q4 = D / 4;
+  const long long total = (long long)B * S * H * q4;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i % q4);
+    long long r = i / q4;
+    const int h = (int)(r % H);
+    r /= H;
+    const int s = (int)(r % S);
+    const int b = (int)(r / S);
+    const float4 x = *reinterpret_cast<const float4*>(src + b * sb + s * ss + h * sh + 4 * c);
+    const uint32_t h01 = pack_bf16x2(x.x, x.y), h23 = pack_bf16x2(x.z, x.w);
+    const uint32_t l01 = pack_bf16x2(x.x - bf16lo_to_f32(h01), x.y - bf16hi_to_f32(h01));
+    const uint32_t l23 = pack_bf16x2(x.z - bf16lo_to_f32(h23), x.w - bf16hi_to_f32(h23));
+    uint16_t* row = dst + (((long long)b * S + s) * H + h) * 2 * D + 4 * c;
+    *reinterpret_cast<uint2*>(row) = make_uint2(h01, h23);
+    *reinterpret_cast<uint2*>(row + D) = make_uint2(l01, l23);
+  }
+}
+
+cudaError_t launch_split_planes(const float* src, long long sb, long long ss, long long sh, int B,
+                                int S, int H, int D, void* dst, cudaStream_t stream) {
+  const long long total = (long long)B * S * H * (D / 4);
+  if (total == 0) return cudaSuccess;
+  const int threads = 256;
+  const long long blocks = min((total + threads - 1) / threads, 148ll * 16);
+  split_planes_kernel<<<(int)blocks, threads, 0, stream>>>(src, sb, ss, sh, B, S, H, D,
+                                                           reinterpret_cast<uint16_t*>(dst));
+  return cudaGetLastError();
+}
 
 }  // namespace enl

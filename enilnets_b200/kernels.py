@@ -50,15 +50,19 @@ def attention_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
                       return_lse: bool = False):
     """softmax(q k^T * scale + alibi + mask) v via the K1 tcgen05 kernel.
 
-    q: (B, Sq, H, D) bf16; k, v: (B, Skv, Hkv, D) bf16; H % Hkv == 0 and query
-    head h reads kv head h // (H // Hkv) (nn/forward.py:165-171).
+    q: (B, Sq, H, D); k, v: (B, Skv, Hkv, D); all bf16, or all fp32 (the
+    split-bf16 path: three bf16 MMAs per product, about 2^-16 relative
+    error). H % Hkv == 0 and query head h reads kv head h // (H // Hkv)
+    (nn/forward.py:165-171).
     kv_valid_len: int32 (B,) -- keys [0, len_b) are real (graph/sequence.py:23-29).
     mask_mode: "exclude" (-inf, the nn/ path) or "additive" (-1e9 per violated
     mask term, graph/sequence.py:162-176).
     Returns out (B, Sq, H, D) [and lse (B, H, Sq) fp32].
     """
+    if q.dtype not in _DTYPES:
+        raise ValueError(f"q must be bfloat16 or float32 (got {q.dtype})")
     for name, t in (("q", q), ("k", k), ("v", v)):
-        _require_cuda(name, t, torch.bfloat16)
+        _require_cuda(name, t, q.dtype)
         if t.dim() != 4:
             raise ValueError(f"{name} must be 4-D (batch, seq, heads, head_dim)")
     B, Sq, H, D = q.shape
@@ -90,7 +94,7 @@ def attention_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     a.k_stride_b, a.k_stride_s, a.k_stride_h = k.stride(0), k.stride(1), k.stride(2)
     a.v_stride_b, a.v_stride_s, a.v_stride_h = v.stride(0), v.stride(1), v.stride(2)
     a.o_stride_b, a.o_stride_s, a.o_stride_h = out.stride(0), out.stride(1), out.stride(2)
-    a.in_dtype = nat.ENL_DTYPE_BF16
+    a.in_dtype = _DTYPES[q.dtype]
     a.out_dtype = _DTYPES[out.dtype]
     a.causal = int(bool(causal))
     a.window = -1 if window is None else int(window)
@@ -99,7 +103,14 @@ def attention_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     a.alibi_slopes = _ptr(alibi_slopes)
     a.q_pos0, a.k_pos0 = int(q_pos0), int(k_pos0)
     a.scale = 1.0 / math.sqrt(D) if scale is None else float(scale)
-    nat.check(nat.load().enl_attn_prefill(ctypes.byref(a), _stream()), "enl_attn_prefill")
+    lib = nat.load()
+    ws = None
+    need = int(lib.enl_prefill_workspace_bytes(ctypes.byref(a)))
+    if need > 0:
+        # Stream-ordered by torch's caching allocator, freed after the launch.
+        ws = torch.empty(need, dtype=torch.uint8, device=q.device)
+        a.workspace, a.workspace_bytes = ws.data_ptr(), need
+    nat.check(lib.enl_attn_prefill(ctypes.byref(a), _stream()), "enl_attn_prefill")
     return (out, lse) if return_lse else out
 
 
@@ -134,14 +145,16 @@ def attention_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
                      return_lse: bool = False):
     """One-token decode via the K2 split-KV kernel.
 
-    q: (B, H, D) bf16; k_cache/v_cache: (B, Hkv, capacity, D) bf16 with equal
-    strides; live slots [slot_begin, slot_end), slot s at absolute position
+    q: (B, H, D); k_cache/v_cache: (B, Hkv, capacity, D) with equal strides,
+    all bf16 or all fp32; live slots [slot_begin, slot_end), slot s at absolute position
     pos_slot0 + s; the query sits at q_pos (keys after it are invisible).
     Returns out (B, H, D) [and lse (B, H) fp32].
     """
-    _require_cuda("q", q, torch.bfloat16)
-    _require_cuda("k_cache", k_cache, torch.bfloat16)
-    _require_cuda("v_cache", v_cache, torch.bfloat16)
+    if q.dtype not in _DTYPES:
+        raise ValueError(f"q must be bfloat16 or float32 (got {q.dtype})")
+    _require_cuda("q", q, q.dtype)
+    _require_cuda("k_cache", k_cache, q.dtype)
+    _require_cuda("v_cache", v_cache, q.dtype)
     if q.dim() != 3 or k_cache.dim() != 4:
         raise ValueError("q must be (B, H, D) and caches (B, Hkv, capacity, D)")
     if k_cache.shape != v_cache.shape or k_cache.stride() != v_cache.stride():
@@ -178,7 +191,7 @@ def attention_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     a.window = -1 if window is None else int(window)
     a.alibi_slopes = _ptr(alibi_slopes)
     a.scale = 1.0 / math.sqrt(D) if scale is None else float(scale)
-    a.in_dtype, a.out_dtype = nat.ENL_DTYPE_BF16, _DTYPES[out.dtype]
+    a.in_dtype, a.out_dtype = _DTYPES[q.dtype], _DTYPES[out.dtype]
     a.n_splits = int(splits)
     a.workspace = _ptr(workspace)
     a.workspace_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()

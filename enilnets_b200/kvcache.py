@@ -30,10 +30,10 @@ class _LayerKV:
     """Device K/V of one attention layer: live slots [begin, end), slot s at
     absolute position base + s."""
 
-    def __init__(self, B: int, Hkv: int, D: int, base: int, need: int):
+    def __init__(self, B: int, Hkv: int, D: int, base: int, need: int, dtype):
         import torch
         cap = max(64, 1 << (max(need, 1) - 1).bit_length())
-        self.k = torch.zeros((B, Hkv, cap, D), dtype=torch.bfloat16, device=device())
+        self.k = torch.zeros((B, Hkv, cap, D), dtype=dtype, device=device())
         self.v = torch.zeros_like(self.k)
         self.begin = 0
         self.end = 0
@@ -174,8 +174,11 @@ def attention_step(layer: Dict[str, Any], x, idx: int, cache: KVCache, B: int, S
         attention.apply_rope(k_new, pos)
     lc = cache._kv.get(idx)
     if lc is None:
-        lc = _LayerKV(B, Hkv, D, base=pos, need=S_new)
+        lc = _LayerKV(B, Hkv, D, base=pos, need=S_new, dtype=qkv.dtype)
         cache._kv[idx] = lc
+    elif lc.k.dtype != qkv.dtype:
+        raise ValueError(f"the cache of layer {idx} holds {lc.k.dtype} K/V but the precision is "
+                         f"now {qkv.dtype}; start a new KVCache after set_precision")
     lc.reserve(S_new)
     kernels.kv_append(lc.k, k_new, lc.end)
     kernels.kv_append(lc.v, v_new, lc.end)
@@ -188,13 +191,14 @@ def attention_step(layer: Dict[str, Any], x, idx: int, cache: KVCache, B: int, S
     if S_new == 1:
         ctx = kernels.attention_decode(q[:, 0], lc.k, lc.v, slot_begin=lc.begin,
                                        slot_end=lc.end, pos_slot0=lc.base, q_pos=pos,
-                                       window=window, alibi_slopes=slopes).unsqueeze(1)
+                                       window=window, alibi_slopes=slopes,
+                                       out_dtype=qkv.dtype).unsqueeze(1)
     else:
         kv_k = lc.k[:, :, lc.begin:lc.end].permute(0, 2, 1, 3)
         kv_v = lc.v[:, :, lc.begin:lc.end].permute(0, 2, 1, 3)
         ctx = kernels.attention_prefill(q, kv_k, kv_v, causal=True, window=window,
                                         alibi_slopes=slopes, q_pos0=pos,
-                                        k_pos0=lc.base + lc.begin)
+                                        k_pos0=lc.base + lc.begin, out_dtype=qkv.dtype)
     return attention.project(ctx.flatten(-2), layer, "o").float()
 
 

@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define ENL_ABI_VERSION 1
+#define ENL_ABI_VERSION 2
 
 /* Status codes. The Python binding maps INVALID/UNSUPPORTED to ValueError
  * (the reference raises ValueError for bad layer configurations,
@@ -56,7 +56,7 @@ typedef struct enl_prefill_args {
   int64_t k_stride_b, k_stride_s, k_stride_h;
   int64_t v_stride_b, v_stride_s, v_stride_h;
   int64_t o_stride_b, o_stride_s, o_stride_h;
-  int32_t in_dtype;  /* ENL_DTYPE_BF16 */
+  int32_t in_dtype;  /* ENL_DTYPE_BF16, or ENL_DTYPE_FP32 (split-bf16 path, needs workspace) */
   int32_t out_dtype; /* ENL_DTYPE_BF16 or ENL_DTYPE_FP32 */
   int32_t causal;    /* key allowed only when pos_k <= pos_q */
   int32_t window;    /* < 0: none; else |pos_q - pos_k| <= window */
@@ -66,6 +66,8 @@ typedef struct enl_prefill_args {
   int64_t q_pos0;              /* absolute position of query row 0 */
   int64_t k_pos0;              /* absolute position of key row 0 */
   float scale;                 /* softmax scale, normally 1/sqrt(head_dim) */
+  void* workspace;             /* device scratch for fp32 inputs, >= enl_prefill_workspace_bytes() */
+  size_t workspace_bytes;
 } enl_prefill_args;
 
 /* Fused attention prefill: softmax(Q K^T * scale + bias + mask) V.
@@ -73,8 +75,18 @@ typedef struct enl_prefill_args {
  * nn/flash_attention.py:42-80 (tiled softmax), nn/forward.py:578-586 (cross
  * attention), the cached multi-token step nn/kvcache.py:198-213, and the
  * key-padding rule of graph/sequence.py:159-183. head_dim: any multiple of 8
- * up to 128 (the kernel runs at 64 or 128 with TMA zero fill). */
+ * up to 128 (the kernel runs at 64 or 128 with TMA zero fill).
+ *
+ * bf16 inputs: one bf16 MMA per product, fp32 accumulation.
+ * fp32 inputs (the reference's default float32 models): q, k, v are first
+ * split into bf16 planes hi = bf16(x), lo = bf16(x - hi) in the workspace,
+ * and every product is hi*hi + hi*lo + lo*hi on the bf16 tensor cores (the
+ * softmax probabilities are split the same way), for about 2^-16 relative
+ * error, tighter than tf32. fp32 rows must be 16-byte aligned. */
 int enl_attn_prefill(const enl_prefill_args* args, void* stream);
+
+/* Workspace bytes enl_attn_prefill needs for these arguments (0 for bf16 inputs). */
+size_t enl_prefill_workspace_bytes(const enl_prefill_args* args);
 
 /* ----------------------------------------------------------------- decode */
 typedef struct enl_decode_args {
@@ -102,8 +114,8 @@ typedef struct enl_decode_args {
 /* Split-KV single-token decode with log-sum-exp merge of the splits.
  * Replaces the attention half of nn/kvcache.py:_attention_step (lines
  * 198-213) for one new token; head_dim a multiple of 8 up to 128,
- * num_heads/num_kv_heads in
- * {1, 2, 4, 8}. */
+ * num_heads/num_kv_heads in {1, 2, 4, 8}. in_dtype (q and both caches):
+ * ENL_DTYPE_BF16 or ENL_DTYPE_FP32; the arithmetic is fp32 either way. */
 int enl_attn_decode(const enl_decode_args* args, void* stream);
 
 /* Scratch held by enl_attn_decode_noalloc on every device that loads the library. */

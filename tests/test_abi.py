@@ -33,7 +33,7 @@ def test_library_exports_every_declared_symbol():
     for name in declared_functions():
         assert hasattr(lib, name), f"{name} declared in enl_attn.h but not exported"
         assert name in _native.SIGNATURES, f"{name} has no ctypes signature"
-    assert lib.enl_abi_version() == 1
+    assert lib.enl_abi_version() == _native.ABI_VERSION == 2
 
 
 def test_nm_shows_c_linkage():
@@ -100,3 +100,19 @@ def test_decode_split_heuristic():
     assert lib.enl_decode_auto_splits(1, 1, 10) == 1
     assert lib.enl_decode_workspace_bytes(2, 4, 128, 1) == 0
     assert lib.enl_decode_workspace_bytes(2, 4, 128, 3) == 3 * 2 * 4 * 129 * 4
+
+
+def test_prefill_workspace_bytes_is_host_only_arithmetic():
+    """fp32 prefill needs (hi, lo) bf16 planes of q, k and v, each padded to
+    256 bytes; bf16 prefill needs none."""
+    lib = _native.load()
+    a = _native.PrefillArgs()
+    a.batch, a.num_heads, a.num_kv_heads, a.seq_q, a.seq_kv, a.head_dim = 2, 8, 2, 100, 300, 40
+    a.in_dtype = _native.ENL_DTYPE_BF16
+    assert lib.enl_prefill_workspace_bytes(ctypes.byref(a)) == 0
+    a.in_dtype = _native.ENL_DTYPE_FP32
+
+    def planes(S, H):
+        n = 2 * S * H * 2 * 40 * 2
+        return (n + 255) // 256 * 256
+    assert lib.enl_prefill_workspace_bytes(ctypes.byref(a)) == planes(100, 8) + 2 * planes(300, 2)

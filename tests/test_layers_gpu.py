@@ -3,8 +3,12 @@ from the reference's seeds run through AttentionNet.Forward,
 graph.MultiHeadAttention and cached_forward_step, against outputs the
 reference itself produced (tests/golden/layer_b200.npz, config1.npz).
 
-Tolerance: 2e-2 max abs (bf16 attention with fp32 accumulation against the
-float64 reference), as for the kernel tests."""
+Both device precisions run (enilnets_b200.set_precision):
+  fp32 (default): max abs error <= 1e-3, the north-star bar for fp32 inputs;
+  bf16:           max abs error <= 2e-2 per attention layer. Through a whole
+                  transformer block, layernorm and the logits projection the
+                  bf16 roundings compound, so those model-level outputs are
+                  held to 5e-2 in bf16 (and to 1e-3 in fp32)."""
 import json
 
 import numpy as np
@@ -14,7 +18,8 @@ import enilnets_b200 as enl
 from enilnets_b200.graph import MultiHeadAttention, lengths_to_mask
 
 pytestmark = pytest.mark.gpu
-TOL = 2e-2
+TOL = {"fp32": 1e-3, "bf16": 2e-2}
+TOL_MODEL = {"fp32": 1e-3, "bf16": 5e-2}
 
 
 @pytest.fixture
@@ -22,6 +27,13 @@ def float64():
     enl.use_float64(True)
     yield
     enl.use_float64(False)
+
+
+@pytest.fixture(params=["fp32", "bf16"])
+def precision(request):
+    enl.set_precision(request.param)
+    yield request.param
+    enl.set_precision("fp32")
 
 
 def _golden(golden_dir):
@@ -33,7 +45,7 @@ def _err(a, b):
     return float(np.max(np.abs(np.asarray(a, np.float64) - np.asarray(b, np.float64))))
 
 
-def test_mha_layers_forward(cuda, golden_dir, float64):
+def test_mha_layers_forward(cuda, golden_dir, float64, precision):
     data, meta = _golden(golden_dir)
     for i, cfg in enumerate(meta["mha"]):
         enl.set_seed(1100 + i)
@@ -41,10 +53,10 @@ def test_mha_layers_forward(cuda, golden_dir, float64):
         m.add_multihead_attention(**cfg)
         x = np.random.RandomState(1200 + i).standard_normal((2, 40, cfg["embed_dim"]))
         err = _err(m.Forward(x, training=False), data[f"mha{i}_y"])
-        assert err <= TOL, f"{cfg}: {err:.3e}"
+        assert err <= TOL[precision], f"{cfg}: {err:.3e}"
 
 
-def test_graph_padding_layers(cuda, golden_dir, float64):
+def test_graph_padding_layers(cuda, golden_dir, float64, precision):
     data, meta = _golden(golden_dir)
     for i, cfg in enumerate(meta["graph"]):
         enl.set_seed(1300 + i)
@@ -52,10 +64,10 @@ def test_graph_padding_layers(cuda, golden_dir, float64):
         x = np.random.RandomState(1400 + i).standard_normal((3, 33, 64))
         y = g(x, key_padding_mask=lengths_to_mask(cfg["lengths"], 33)).data
         err = _err(y, data[f"graph{i}_y"])
-        assert err <= TOL, f"{cfg}: {err:.3e}"
+        assert err <= TOL[precision], f"{cfg}: {err:.3e}"
 
 
-def test_graph_padding_garbage_invariance(cuda):
+def test_graph_padding_garbage_invariance(cuda, precision):
     """graph/sequence.py contract (reference test_enilnets.py:6791-6801):
     garbage in padded slots does not change real-token outputs."""
     enl.set_seed(0)
@@ -69,7 +81,7 @@ def test_graph_padding_garbage_invariance(cuda):
     assert np.allclose(clean[mask], dirty[mask], atol=1e-6)
 
 
-def test_cross_attention_layers(cuda, golden_dir, float64):
+def test_cross_attention_layers(cuda, golden_dir, float64, precision):
     data, meta = _golden(golden_dir)
     for i, cfg in enumerate(meta["cross"]):
         enl.set_seed(1500 + i)
@@ -79,7 +91,7 @@ def test_cross_attention_layers(cuda, golden_dir, float64):
                               num_kv_heads=cfg["num_kv_heads"])
         x = np.random.RandomState(1600 + i).standard_normal((2, 24, 64))
         err = _err(m.Forward(x, training=False), data[f"cross{i}_y"])
-        assert err <= TOL, f"{cfg}: {err:.3e}"
+        assert err <= TOL[precision], f"{cfg}: {err:.3e}"
 
 
 def _kv_model(i, cfg):
@@ -96,7 +108,7 @@ def _kv_model(i, cfg):
     return m, toks
 
 
-def test_kv_cache_stepping_matches_reference(cuda, golden_dir, float64):
+def test_kv_cache_stepping_matches_reference(cuda, golden_dir, float64, precision):
     """Primed 4-token step then 5 single-token steps (nn/kvcache.py:69-214)
     equal both the reference's stepped outputs and its full Forward; the
     cache stores the unexpanded Hkv heads and evicts outside the window."""
@@ -104,13 +116,13 @@ def test_kv_cache_stepping_matches_reference(cuda, golden_dir, float64):
     for i, cfg in enumerate(meta["kv"]):
         m, toks = _kv_model(i, cfg)
         full = m.Forward(toks, training=False)
-        assert _err(full, data[f"kv{i}_full"]) <= TOL, cfg
+        assert _err(full, data[f"kv{i}_full"]) <= TOL_MODEL[precision], cfg
         cache = enl.KVCache()
         pieces = [enl.cached_forward_step(m, toks[:, :4], cache)]
         pieces += [enl.cached_forward_step(m, toks[:, j:j + 1], cache) for j in range(4, 9)]
         stepped = np.concatenate(pieces, axis=1)
-        assert _err(stepped, data[f"kv{i}_stepped"]) <= TOL, cfg
-        assert _err(stepped, full) <= TOL, cfg
+        assert _err(stepped, data[f"kv{i}_stepped"]) <= TOL_MODEL[precision], cfg
+        assert _err(stepped, full) <= TOL_MODEL[precision], cfg
         attn_idx = [j for j, l in enumerate(m.layers) if l["type"] == "multihead_attention"][0]
         k, v, start = cache.kv[attn_idx]
         assert tuple(k.shape) == tuple(data[f"kv{i}_kshape"]), cfg
@@ -118,7 +130,7 @@ def test_kv_cache_stepping_matches_reference(cuda, golden_dir, float64):
         assert cache.position == 9
 
 
-def test_kv_cache_reorder_and_expand(cuda, golden_dir, float64):
+def test_kv_cache_reorder_and_expand(cuda, golden_dir, float64, precision):
     """KVCache.expand/reorder gather by parent on the device
     (nn/kvcache.py:42-66; reference test_enilnets.py:10539-10556)."""
     data, meta = _golden(golden_dir)
@@ -132,7 +144,7 @@ def test_kv_cache_reorder_and_expand(cuda, golden_dir, float64):
         enl.cached_forward_step(m, np.array([[5], [6], [7]]), cache)
         cache.reorder([2, 2, 0])
         out = enl.cached_forward_step(m, np.array([[9], [9], [9]]), cache)
-        assert _err(out, data[f"kv{i}_reordered"]) <= TOL, cfg
+        assert _err(out, data[f"kv{i}_reordered"]) <= TOL_MODEL[precision], cfg
         assert np.allclose(out[0], out[1], atol=1e-6)
 
 
@@ -144,9 +156,10 @@ def test_non_causal_layer_cannot_be_stepped(cuda):
         enl.cached_forward_step(m, np.array([[1, 2]]), enl.KVCache())
 
 
-def test_config1_layer_output(cuda, golden_dir):
+def test_config1_layer_output(cuda, golden_dir, precision):
     """set_seed(0), add_multihead_attention(256, 8,
-    causal=True), x ~ RandomState(1) (4, 256, 256), default float32."""
+    causal=True), x ~ RandomState(1) (4, 256, 256), default float32; <= 1e-3
+    on the fp32 path (the default), <= 2e-2 on the bf16 path."""
     data = np.load(golden_dir / "config1.npz")
     enl.use_float64(False)
     enl.set_seed(0)
@@ -156,4 +169,4 @@ def test_config1_layer_output(cuda, golden_dir):
     y = m.Forward(x, training=False)
     assert y.dtype == np.float32 and y.shape == (4, 256, 256)
     err = _err(y[0], data["y0"])
-    assert err <= TOL, err
+    assert err <= TOL[precision], err
