@@ -14,6 +14,13 @@ Also measured in the same run (sub-objects of the line):
   longctx_cfg5 -- split-KV decode B4 H32 D128 over a 262144-token cache
                   sharded by sequence across ranks; per-GPU (out, LSE)
                   partials all-gathered over NCCL and LSE-merged.
+  cross_cfg4   -- cross-attention prefill, decoder B16 x 1024 queries against
+                  2048 memory keys, H16 D64, non-causal, memory key padding
+                  L~U[1024, 2048], bf16 (per-GPU batch 16, no collective).
+  layer_cfg2   -- the whole graph.MultiHeadAttention layer on config 2 in
+                  bf16 precision (fused QKV GEMM, K1, output GEMM).
+  layer_cfg1   -- config 1 (B4 S256 E256 H8, causal, float32) through the
+                  NumPy-facing Forward on the fp32 split-bf16 path.
 
 Run: python bench.py [--gpus N --steps K --warmup W] [--impl reference]
 Multi-GPU: torchrun --nproc-per-node N bench.py --gpus N ...
@@ -41,6 +48,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 CFG2 = dict(B=8, S=4096, H=16, D=128, lo=2048, hi=4096)
 CFG3 = dict(B=64, H=32, D=128, ctx=8192, steps=128)
 CFG5 = dict(B=4, H=32, D=128, ctx=262144, steps=16)
+CFG4 = dict(B=16, Sq=1024, Skv=2048, H=16, D=64, lo=1024, hi=2048)
 
 
 def load_peaks():
@@ -365,6 +373,95 @@ def bench_longctx_cfg5(dist: Dist, clocks: ClockSampler, warmup: int):
             "collective": "none" if N == 1 else "ncclAllGather of fp32 (out, LSE) + LSE merge"}
 
 
+def bench_cross_cfg4(dist: Dist, clocks: ClockSampler, warmup: int, steps: int = 50):
+    """Cross-attention core: per-GPU batch 16, memory key padding."""
+    import numpy as np
+    import torch
+    from enilnets_b200 import kernels, _native
+    B, Sq, Skv, H, D = CFG4["B"], CFG4["Sq"], CFG4["Skv"], CFG4["H"], CFG4["D"]
+    g = torch.Generator(device=dist.device).manual_seed(4000 + dist.rank)
+    q = torch.randn((B, Sq, H, D), generator=g, device=dist.device).to(torch.bfloat16)
+    k, v = (torch.randn((B, Skv, H, D), generator=g, device=dist.device).to(torch.bfloat16)
+            for _ in range(2))
+    lengths = np.random.RandomState(4 + dist.rank).randint(CFG4["lo"], CFG4["hi"] + 1, size=B)
+    lens = torch.tensor(lengths, dtype=torch.int32, device=dist.device)
+    out = torch.empty_like(q)
+
+    def step():
+        kernels.attention_prefill(q, k, v, causal=False, kv_valid_len=lens,
+                                  mask_mode="additive", out=out)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    _native.raise_on_device_error()
+    ms = timed(dist, clocks, step, steps) / steps
+    flops = 4.0 * D * H * Sq * float(lengths.sum())
+    return {"TFLOP_s": dist.sum(flops) / (ms * 1e-3) / 1e12, "ms_per_step": ms,
+            "config": f"B{B}/GPU Sq{Sq} Skv{Skv} H{H} D{D} non-causal, memory key padding "
+                      f"L~U[{CFG4['lo']},{CFG4['hi']}], bf16"}
+
+
+def bench_layer_cfg2(dist: Dist, clocks: ClockSampler, warmup: int, steps: int = 10):
+    """graph.MultiHeadAttention(2048, 16, causal) forward with key padding on
+    device-resident x, bf16 precision: QKV GEMM + K1 + output GEMM."""
+    import numpy as np
+    import torch
+    import enilnets_b200 as enl
+    from enilnets_b200 import _native
+    from enilnets_b200.graph import MultiHeadAttention, lengths_to_mask
+    B, S, H, D = CFG2["B"], CFG2["S"], CFG2["H"], CFG2["D"]
+    E = H * D
+    enl.set_precision("bf16")
+    try:
+        enl.set_seed(0)
+        layer = MultiHeadAttention(E, H, causal=True)
+        g = torch.Generator(device=dist.device).manual_seed(2000 + dist.rank)
+        x = torch.randn((B, S, E), generator=g, device=dist.device)
+        lengths = cfg2_lengths(dist.rank)
+        mask = lengths_to_mask(lengths, S)
+
+        def step():
+            layer.forward_device(x, key_padding_mask=mask)
+
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        _native.raise_on_device_error()
+        ms = timed(dist, clocks, step, steps) / steps
+    finally:
+        enl.set_precision("fp32")
+    proj = 2.0 * B * S * E * (3 * E) + 2.0 * B * S * E * E
+    attn = cfg2_flops(lengths)
+    return {"TFLOP_s": dist.sum(proj + attn) / (ms * 1e-3) / 1e12, "ms_per_step": ms,
+            "attention_share_of_flops": attn / (proj + attn),
+            "config": "graph.MultiHeadAttention(2048, 16, causal) forward, x (8, 4096, 2048) "
+                      "on device, key padding as config 2, bf16 precision"}
+
+
+def bench_layer_cfg1(dist: Dist, warmup: int, steps: int = 20):
+    """Config 1 through the NumPy-facing API (host array in, host array out),
+    fp32 precision; host wall time per Forward, max over ranks."""
+    import numpy as np
+    import torch
+    import enilnets_b200 as enl
+    enl.set_seed(0)
+    m = enl.AttentionNet()
+    m.add_multihead_attention(embed_dim=256, num_heads=8, causal=True)
+    x = np.random.RandomState(1).standard_normal((4, 256, 256))
+    for _ in range(warmup):
+        m.Forward(x)
+    dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        m.Forward(x)
+    torch.cuda.synchronize()
+    ms = dist.max((time.perf_counter() - t0) * 1e3 / steps)
+    return {"ms_per_forward": ms, "precision": "fp32 (split-bf16 attention, fp32 GEMMs)",
+            "config": "set_seed(0), add_multihead_attention(256, 8, causal=True), "
+                      "x (4, 256, 256) float NumPy in/out"}
+
+
 # ------------------------------------------------------------- CPU baseline
 def cpu_sample_tflops(heads: int = 16, repeats: int = 1):
     """The reference's streaming softmax (oracle port of
@@ -435,7 +532,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--skip-sub", action="store_true", help="headline only")
-    ap.add_argument("--only", choices=["all", "prefill", "decode", "longctx"], default="all",
+    ap.add_argument("--only", choices=["all", "prefill", "decode", "longctx", "cross", "layer"],
+                    default="all",
                     help="profiling: run one workload")
     ap.add_argument("--batch", type=int, default=0, help="profiling: prefill batch override")
     ap.add_argument("--decode-batch", type=int, default=0,
@@ -461,6 +559,11 @@ def main():
                                     e2e_on=False)
             elif args.only == "decode":
                 res = bench_decode_cfg3(dist, clocks, args.warmup, args.decode_batch)
+            elif args.only == "cross":
+                res = bench_cross_cfg4(dist, clocks, args.warmup)
+            elif args.only == "layer":
+                res = {"layer_cfg2": bench_layer_cfg2(dist, clocks, args.warmup),
+                       "layer_cfg1": bench_layer_cfg1(dist, args.warmup)}
             else:
                 res = bench_longctx_cfg5(dist, clocks, args.warmup)
             if dist.rank == 0:
@@ -473,6 +576,9 @@ def main():
         if not args.skip_sub:
             sub["decode_cfg3"] = bench_decode_cfg3(dist, clocks, args.warmup, args.decode_batch)
             sub["longctx_cfg5"] = bench_longctx_cfg5(dist, clocks, args.warmup)
+            sub["cross_cfg4"] = bench_cross_cfg4(dist, clocks, args.warmup)
+            sub["layer_cfg2"] = bench_layer_cfg2(dist, clocks, args.warmup)
+            sub["layer_cfg1"] = bench_layer_cfg1(dist, args.warmup)
     finally:
         clocks.stop()
     peaks, peak_kind = load_peaks()
@@ -487,6 +593,9 @@ def main():
         if prof.exists():
             roofline["traffic"] = json.loads(prof.read_text()).get("bytes_per_launch")
         hbm = float(peaks["hbm_gbs"])
+        if "cross_cfg4" in sub:
+            sub["cross_cfg4"]["frac_of_bf16_peak_per_gpu"] = \
+                sub["cross_cfg4"]["TFLOP_s"] / dist.world / peak
         for key in ("decode_cfg3", "longctx_cfg5"):
             if key in sub and "GB_s" in sub[key]:
                 per_gpu = sub[key]["GB_s"] / dist.world

@@ -1,5 +1,6 @@
 // C-ABI entry points of libenl_b200.so (declared in include/enl_attn.h):
 // argument validation, TMA tensor-map construction and kernel launches.
+#include <algorithm>
 #include <cstdio>
 #include <cstdarg>
 #include <string>
@@ -68,6 +69,23 @@ int make_qkv_map(CUtensorMap* map, const void* base, int D, int S, int H, int B,
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// SM count of the current device, cached per device.
+int sm_count(int* out) {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(ENL_ERR_UNSUPPORTED, "device ordinal %d >= 64", dev);
+  if (cached[dev] == 0) {
+    int n = 0;
+    e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(multiProcessorCount)");
+    cached[dev] = n;
+  }
+  *out = cached[dev];
+  return ENL_OK;
+}
 
 int check_strides_16B(const char* name, int64_t sb, int64_t ss, int64_t sh, int elem_bytes) {
   const int64_t v[3] = {sb, ss, sh};
@@ -213,6 +231,26 @@ int enl_attn_prefill(const enl_prefill_args* a, void* stream) {
   p.q_pos0 = a->q_pos0;
   p.k_pos0 = a->k_pos0;
   p.scale_log2 = a->scale * 1.4426950408889634f;
+  // One persistent CTA per SM. Sections of (batch, head) pairs whose K/V
+  // fit in about a quarter of L2 keep the concurrently running items on
+  // shared keys.
+  {
+    const long long n_qt = (a->seq_q + 127) / 128;
+    const long long n_items = (long long)a->batch * a->num_heads * n_qt;
+    if (n_items > (1ll << 30))
+      return fail(ENL_ERR_UNSUPPORTED, "enl_attn_prefill: %lld query tiles exceed 2^30", n_items);
+    p.n_items = (int)n_items;
+    int sms = 0;
+    if ((st = sm_count(&sms))) return st;
+    p.n_ctas = sms;
+    const int G = a->num_heads / a->num_kv_heads;
+    const double kv_bytes_per_head =
+        4.0 * a->seq_kv * D * (split ? 2 : 1) / G;  // K and V, bf16, shared by G heads
+    const double budget = 32.0 * (1 << 20);
+    long long sec = (long long)(budget / kv_bytes_per_head);
+    const long long n_bh = (long long)a->batch * a->num_heads;
+    p.sec_bh = (int)std::max(1ll, std::min(n_bh, sec));
+  }
 
   cudaError_t e;
   if (split)

@@ -283,6 +283,27 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
       ENL_W32(a, o)                                                                          \
       : "memory")
 
+// 16 consecutive columns (load includes the wait), for low-register paths.
+#define ENL_TMEM_LD16(taddr, a)                                                              \
+  asm volatile(                                                                              \
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "  \
+      "%11, %12, %13, %14, %15}, [%16];\n\t"                                                  \
+      "tcgen05.wait::ld.sync.aligned;"                                                       \
+      : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]), "=r"(a[4]), "=r"(a[5]), "=r"(a[6]),   \
+        "=r"(a[7]), "=r"(a[8]), "=r"(a[9]), "=r"(a[10]), "=r"(a[11]), "=r"(a[12]),           \
+        "=r"(a[13]), "=r"(a[14]), "=r"(a[15])                                                \
+      : "r"(taddr)                                                                           \
+      : "memory")
+
+#define ENL_TMEM_ST16(taddr, a)                                                              \
+  asm volatile(                                                                              \
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "                                        \
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};"             \
+      ::"r"(taddr), "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(a[4]), "r"(a[5]),        \
+      "r"(a[6]), "r"(a[7]), "r"(a[8]), "r"(a[9]), "r"(a[10]), "r"(a[11]), "r"(a[12]),        \
+      "r"(a[13]), "r"(a[14]), "r"(a[15])                                                     \
+      : "memory")
+
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }

@@ -26,6 +26,9 @@ struct PrefillParams {
   const float* alibi;          // (H) ALiBi slopes (natural-log units), or null
   long long q_pos0, k_pos0;
   float scale_log2;            // softmax scale * log2(e)
+  // Persistent schedule: n_items = B * H * ceil(Sq / 128) work items over
+  // min(n_items, n_ctas) CTAs, in sections of sec_bh (batch, head) pairs.
+  int n_items, n_ctas, sec_bh;
 };
 
 // kSplit: the tensor maps cover (hi, lo) bf16 planes of fp32 inputs
