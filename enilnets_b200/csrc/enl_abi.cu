@@ -252,13 +252,20 @@ int enl_attn_prefill(const enl_prefill_args* a, void* stream) {
     p.sec_bh = (int)std::max(1ll, std::min(n_bh, sec));
   }
 
+  // O map for the kernel's TMA-store epilogue (bf16 output of bf16 inputs).
+  CUtensorMap to = tq;
+  if (!split && a->out_dtype == ENL_DTYPE_BF16 &&
+      (st = make_qkv_map(&to, a->o, a->head_dim, a->seq_q, a->num_heads, a->batch, a->o_stride_s,
+                         a->o_stride_h, a->o_stride_b, "o")))
+    return st;
+
   cudaError_t e;
   if (split)
-    e = (D == 128) ? launch_prefill<128, true>(tq, tk, tv, p, s)
-                   : launch_prefill<64, true>(tq, tk, tv, p, s);
+    e = (D == 128) ? launch_prefill<128, true>(tq, tk, tv, to, p, s)
+                   : launch_prefill<64, true>(tq, tk, tv, to, p, s);
   else
-    e = (D == 128) ? launch_prefill<128, false>(tq, tk, tv, p, s)
-                   : launch_prefill<64, false>(tq, tk, tv, p, s);
+    e = (D == 128) ? launch_prefill<128, false>(tq, tk, tv, to, p, s)
+                   : launch_prefill<64, false>(tq, tk, tv, to, p, s);
   if (e != cudaSuccess) return cuda_fail(e, "enl_attn_prefill launch");
   return ENL_OK;
 }

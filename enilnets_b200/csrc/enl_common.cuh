@@ -123,6 +123,34 @@ __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// shared -> global tensor store of one box (bulk-group completion). Its
+// coordinates start inside the tensor (TMA drops the parts of the box past
+// the tensor's extents).
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* smem_src, int c0,
+                                             int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];"
+      ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2),
+      "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until every committed bulk store has finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Wait until every committed bulk store has completed (writes visible).
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// Order this thread's generic-proxy shared-memory writes before later
+// async-proxy (TMA) reads of them.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // ---------------------------------------------------------------------------
 // tcgen05: tensor memory, MMA, loads and stores.
 // ---------------------------------------------------------------------------
@@ -402,9 +430,7 @@ __device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float&
   const uint64_t neg_magic = f2_pack(-12582912.0f, -12582912.0f);
   const uint64_t x = f2_pack(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
   const uint64_t t = f2_add(x, magic);
-  float n0, n1;
-  f2_unpack(f2_add(t, neg_magic), n0, n1);
-  const uint64_t f = f2_add(x, f2_pack(-n0, -n1));
+  const uint64_t f = f2_fma(f2_add(t, neg_magic), f2_pack(-1.0f, -1.0f), x);  // x - round(x)
   uint64_t p = f2_fma(f2_pack(0.05522262f, 0.05522262f), f, f2_pack(0.24261537f, 0.24261537f));
   p = f2_fma(p, f, f2_pack(0.6932516f, 0.6932516f));
   p = f2_fma(p, f, f2_pack(0.9999276f, 0.9999276f));

@@ -33,9 +33,11 @@ struct PrefillParams {
 
 // kSplit: the tensor maps cover (hi, lo) bf16 planes of fp32 inputs
 // interleaved per head (head coordinate 2h + plane), see launch_split_planes.
+// to: bf16 map over O with the Q maps' box and swizzle, used for bf16 output
+// of the bf16 path (otherwise ignored).
 template <int D, bool kSplit>
 cudaError_t launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                           const PrefillParams& p, cudaStream_t stream);
+                           const CUtensorMap& to, const PrefillParams& p, cudaStream_t stream);
 
 // fp32 src[b, s, h, :] (element strides, 16-byte aligned rows) ->
 // dst[b][s][h][plane][D] bf16 with plane 0 = bf16(x), plane 1 = bf16(x - hi).

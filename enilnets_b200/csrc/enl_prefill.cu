@@ -75,10 +75,12 @@ struct PrefillCfg {
   static constexpr int kOffV = kOffK + kStages * kOpBytes;
   static constexpr int kOffX = kOffV + kStages * kOpBytes;  // epilogue exchange
   static constexpr int kXBytes = 3 * 2 * 128 * 4;            // m, l, tier [2 halves][128]
-  static constexpr int kOffBar = kOffX + kXBytes;
+  static constexpr int kOffItems = kOffX + kXBytes;  // decoded items [8 softmax warps][2]
+  static constexpr int kOffBar = kOffItems + 8 * 2 * 32;
   // q_full/empty[kQBufs], k_full/empty, v_full/empty, s_full[2],
-  // p_ready[2 buf][2 half], o_prog[2], o_done, o_free, pv_done[2], drain[2]
-  static constexpr int kNumBars = 2 * kQBufs + 4 * kStages + 2 + 4 + 2 + 1 + 1 + 2 + 2;
+  // p_ready[2 buf][2 half], o_prog[2], o_done, o_free, pv_done[2], drain[2],
+  // stage_full
+  static constexpr int kNumBars = 2 * kQBufs + 4 * kStages + 2 + 4 + 2 + 1 + 1 + 2 + 2 + 1;
   static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;  // +align slack
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
   static constexpr uint32_t kTmemCols = 512;
@@ -133,8 +135,9 @@ struct WorkItem {
   int b, h, hkv, r0;
   int lo, hi;  // key tiles [lo, hi)
   int lkey;    // valid keys of this batch row
-  bool safe;
+  int safe;    // every row of the tile has an unmasked key
 };
+static_assert(sizeof(WorkItem) == 32, "softmax warps keep items in 32-byte slots");
 
 __device__ __forceinline__ WorkItem work_item(const PrefillParams& p, int t) {
   const int n_qt = (p.Sq + 127) / 128;
@@ -152,7 +155,9 @@ __device__ __forceinline__ WorkItem work_item(const PrefillParams& p, int t) {
   w.r0 = qt * 128;
   w.lkey = p.Skv;
   if (p.kv_len != nullptr) w.lkey = max(0, min(p.kv_len[w.b], p.Skv));
-  tile_range(p, w.r0, w.lkey, (p.Skv + 127) / 128, w.lo, w.hi, w.safe);
+  bool safe;
+  tile_range(p, w.r0, w.lkey, (p.Skv + 127) / 128, w.lo, w.hi, safe);
+  w.safe = safe;
   return w;
 }
 
@@ -195,8 +200,14 @@ template <int D, bool kSplit>
 __global__ void __launch_bounds__(384, 1)
     attn_prefill_sm100(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_k,
-                       const __grid_constant__ CUtensorMap tm_v, const PrefillParams p) {
+                       const __grid_constant__ CUtensorMap tm_v,
+                       const __grid_constant__ CUtensorMap tm_o, const PrefillParams p) {
   using Cfg = PrefillCfg<D, kSplit>;
+  // bf16 output of the bf16 path leaves through TMA stores: the epilogue
+  // stages O in the finished item's Q buffer and warp 11 stores it, then
+  // releases the buffer. Otherwise the epilogue stores rows directly and the
+  // last S of an item releases its Q buffer.
+  const bool tma_st = !kSplit && Cfg::kQBufs == 2 && !p.out_fp32;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -217,6 +228,7 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* bar_o_free = bar_o_done + 1;              // epilogue has read O; per item
   uint64_t* bar_pv_done = bar_o_free + 1;             // [2 buffers] P V of a tile complete
   uint64_t* bar_drain = bar_pv_done + 2;              // [2 issuing warps]
+  uint64_t* bar_stage_full = bar_drain + 2;           // O staged for the TMA store; per item
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -227,7 +239,7 @@ __global__ void __launch_bounds__(384, 1)
     for (int i = 0; i < Cfg::kNumBars; ++i) {
       uint32_t count = 1;
       if (bars + i >= bar_p_ready && bars + i < bar_p_ready + 4) count = 4;  // one per warp
-      if (bars + i == bar_o_free) count = 8;  // every softmax warp
+      if (bars + i == bar_o_free || bars + i == bar_stage_full) count = 8;  // every softmax warp
       mbar_init(bars + i, count);
     }
     *abort_flag = 0;
@@ -356,8 +368,9 @@ __global__ void __launch_bounds__(384, 1)
         }
         umma_commit_elect(bar_s_full + buf);
         umma_commit_elect(bar_k_empty + st);
-        // The item's last S: its Q buffer is free once this MMA completes.
-        if (cur.j == cur.hi - 1) umma_commit_elect(bar_q_empty + qb);
+        // The item's last S: its Q buffer is free once this MMA completes
+        // (unless the epilogue stages O there).
+        if (cur.j == cur.hi - 1 && !tma_st) umma_commit_elect(bar_q_empty + qb);
       }
     } else {
       // O_hf += P_hf V_hf over one key half: P of half hf sits in columns
@@ -406,6 +419,29 @@ __global__ void __launch_bounds__(384, 1)
     umma_commit_elect(drain);
     volatile int no_abort = 0;
     mbar_wait(drain, 0, &no_abort, 26);
+  } else if (warp == 11) {
+    // ------------------------------------------------------------- O stores
+    if (tma_st && lane == 0) {
+      tma_prefetch_desc(&tm_o);
+      int wi = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.n_items && ok; t += gridDim.x) {
+        const WorkItem w = work_item(p, t);
+        if (w.lo >= w.hi) continue;
+        const int qb = wi % Cfg::kQBufs;
+        ok = mbar_wait(bar_stage_full, wi & 1, abort_flag, 40);
+        if (!ok) break;
+        const uint8_t* stage = smem + Cfg::kOffQ + qb * Cfg::kOpBytes;
+        for (int a = 0; a < Cfg::kAtoms; ++a)
+          tma_store_4d(&tm_o, stage + a * Cfg::kAtomBytes, a * 64, w.r0, w.h, w.b);
+        bulk_commit_group();
+        bulk_wait_read_all();  // the buffer may now take the next Q tile
+        mbar_arrive(bar_q_empty + qb);
+        ++wi;
+      }
+      bulk_wait_all();  // the output is in global memory before the CTA exits
+    }
+    __syncwarp();
   } else if (warp < 8) {
     // -------------------------------------------------------------- softmax
     const int half = warp / 4;  // key columns [64*half, 64*half + 64)
@@ -417,8 +453,16 @@ __global__ void __launch_bounds__(384, 1)
     uint32_t g = 0;   // tiles of this CTA seen so far (S buffer and phase)
     int wi = 0;       // items with work seen so far (o_done / o_free phase)
     bool failed = false;  // a wait ran out of time; skip the remaining work
-    for (int t = blockIdx.x; t < p.n_items; t += gridDim.x) {
-      const WorkItem w = work_item(p, t);
+    // Each warp decodes the next item during the current one's epilogue
+    // (where the decode's latency overlaps the waits) and keeps it in its
+    // own shared-memory slot: nothing of it stays live in registers across
+    // the tile loop, which runs at the register limit.
+    WorkItem* slots = reinterpret_cast<WorkItem*>(smem + Cfg::kOffItems) + 2 * warp;
+    if (lane == 0) slots[0] = work_item(p, blockIdx.x);
+    int k = 0;  // this CTA's item ordinal
+    for (int t = blockIdx.x; t < p.n_items; t += gridDim.x, ++k) {
+      __syncwarp();
+      const WorkItem w = slots[k & 1];
       const int lo = w.lo, hi = w.hi, lkey = w.lkey;
       const int h = w.h;
       const int row = w.r0 + rloc;
@@ -607,9 +651,9 @@ __global__ void __launch_bounds__(384, 1)
       }
 
       // ----------------------------------------------------------- epilogue
-      // (The item is decoded again rather than kept live across the tile
-      // loop, which runs at the register limit.)
-      const WorkItem we = work_item(p, t);
+      if (lane == 0 && t + (int)gridDim.x < p.n_items)
+        slots[(k + 1) & 1] = work_item(p, t + gridDim.x);
+      const WorkItem we = slots[k & 1];
       const int erow = we.r0 + rloc;
       // Merge the two halves by log-sum-exp: only the half(s) with the
       // fewest -1e9 terms count (tier mode), scaled to a common maximum.
@@ -638,6 +682,7 @@ __global__ void __launch_bounds__(384, 1)
       const bool warp_has_rows = __any_sync(0xffffffffu, row_valid);
       if (ok && have_o)
         ok = __all_sync(0xffffffffu, mbar_wait(bar_o_done, wi & 1, abort_flag, 35 + half));
+      const bool staged = tma_st && have_o;
       if (ok && warp_has_rows) {
         if (have_o) tc_fence_after();
         const float inv_l = 1.0f / l_tot;  // 0/0 -> NaN for rows with no key
@@ -647,6 +692,9 @@ __global__ void __launch_bounds__(384, 1)
                         ((long long)we.b * p.o_sb + (long long)erow * p.o_ss +
                          (long long)we.h * p.o_sh + c0) *
                             (p.out_fp32 ? 4 : 2);
+        // Staging: the item's Q buffer in the Q tile's own 128-byte swizzled
+        // layout, which the O tensor map stores from.
+        uint8_t* stage = smem + Cfg::kOffQ + (wi % Cfg::kQBufs) * Cfg::kOpBytes;
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {  // 16-column chunks of this thread's D/2
           uint32_t o0[16], o1[16];
@@ -661,9 +709,21 @@ __global__ void __launch_bounds__(384, 1)
             v[i] = (have_o && l_tot != 0.0f)
                        ? fmaf(__uint_as_float(o0[i]), s0, __uint_as_float(o1[i]) * s1)
                        : NAN;
-          // Columns past the tensors' head dim are TMA zero fill: not stored.
           const int col0 = c0 + c * 16;
-          if (row_valid && p.out_fp32) {
+          if (staged) {
+            const int atom = col0 / 64;
+            const int chunk = (col0 % 64) / 8;  // 16-byte chunk within the 128-byte row
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+              uint4* dst = reinterpret_cast<uint4*>(
+                  stage + atom * Cfg::kAtomBytes + rloc * 128 + (((chunk + i) ^ (rloc & 7)) << 4));
+              *dst = make_uint4(pack_bf16x2(v[8 * i], v[8 * i + 1]),
+                                pack_bf16x2(v[8 * i + 2], v[8 * i + 3]),
+                                pack_bf16x2(v[8 * i + 4], v[8 * i + 5]),
+                                pack_bf16x2(v[8 * i + 6], v[8 * i + 7]));
+            }
+          } else if (row_valid && p.out_fp32) {
+            // Columns past the tensors' head dim are TMA zero fill: not stored.
             float4* dst = reinterpret_cast<float4*>(orow + c * 16 * 4);
 #pragma unroll
             for (int i = 0; i < 4; ++i)
@@ -685,6 +745,13 @@ __global__ void __launch_bounds__(384, 1)
           if (etiers && tfin > 0) lse -= 1e9f * (float)tfin;
           p.lse[((long long)we.b * p.H + we.h) * p.Sq + erow] = lse;
         }
+      }
+      if (staged) {
+        // Every softmax warp reports once per item, whether or not it had
+        // rows to write, so the store warp's count always completes.
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_stage_full);
       }
       if (have_o) {
         // O has been read (or will not be): the next item's first P V may
@@ -709,7 +776,7 @@ __global__ void __launch_bounds__(384, 1)
 
 template <int D, bool kSplit>
 cudaError_t launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                           const PrefillParams& p, cudaStream_t stream) {
+                           const CUtensorMap& to, const PrefillParams& p, cudaStream_t stream) {
   using Cfg = PrefillCfg<D, kSplit>;
   static bool configured[64] = {};  // per device
   int dev = 0;
@@ -724,14 +791,15 @@ cudaError_t launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const C
   }
   if (p.n_items <= 0) return cudaSuccess;
   const int grid = min(p.n_items, p.n_ctas);
-  attn_prefill_sm100<D, kSplit><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(tq, tk, tv, p);
+  attn_prefill_sm100<D, kSplit><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(tq, tk, tv, to,
+                                                                                  p);
   return cudaGetLastError();
 }
 
 #define ENL_INST_PREFILL(D, S)                                                              \
   template cudaError_t launch_prefill<D, S>(const CUtensorMap&, const CUtensorMap&,          \
-                                            const CUtensorMap&, const PrefillParams&,        \
-                                            cudaStream_t);
+                                            const CUtensorMap&, const CUtensorMap&,          \
+                                            const PrefillParams&, cudaStream_t);
 ENL_INST_PREFILL(64, false)
 ENL_INST_PREFILL(128, false)
 ENL_INST_PREFILL(64, true)
