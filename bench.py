@@ -269,10 +269,12 @@ def bench_decode_cfg3(dist: Dist, clocks: ClockSampler, warmup: int, batch: int 
     """Batch rows split across ranks (64 / N per GPU)."""
     import torch
     from enilnets_b200 import kernels, _native
+    from enilnets_b200 import sharding
     Btot, H, D, ctx, T = batch or CFG3["B"], CFG3["H"], CFG3["D"], CFG3["ctx"], CFG3["steps"]
-    if Btot % dist.world:
-        return {"skipped": f"batch {Btot} not divisible by {dist.world} ranks"}
-    B = Btot // dist.world
+    b0, b1 = sharding.batch_shard(Btot, dist.world, dist.rank)
+    B = b1 - b0
+    if B == 0:
+        return {"skipped": f"batch {Btot} has no rows for rank {dist.rank}"}
     cap = ctx + T
     g = torch.Generator(device=dist.device).manual_seed(3 + dist.rank)
     kc = torch.empty((B, H, cap, D), dtype=torch.bfloat16, device=dist.device)
@@ -321,10 +323,11 @@ def bench_decode_cfg3(dist: Dist, clocks: ClockSampler, warmup: int, batch: int 
 def bench_longctx_cfg5(dist: Dist, clocks: ClockSampler, warmup: int):
     """Sequence-sharded split-KV decode with an NCCL all-gather of (out, LSE)."""
     import torch
-    from enilnets_b200 import kernels, _native
+    from enilnets_b200 import kernels, sharding, _native
     B, H, D, ctx, T = CFG5["B"], CFG5["H"], CFG5["D"], CFG5["ctx"], CFG5["steps"]
     N = dist.world
-    shard = ctx // N
+    k0, k1 = sharding.kv_shard_range(ctx, N, dist.rank)
+    shard = k1 - k0
     tail = dist.rank == N - 1
     cap = shard + (T if tail else 0)
     g = torch.Generator(device=dist.device).manual_seed(5 + dist.rank)
@@ -336,9 +339,8 @@ def bench_longctx_cfg5(dist: Dist, clocks: ClockSampler, warmup: int):
     qs = torch.randn((T, B, H, D), generator=gq, device=dist.device).to(torch.bfloat16)
     kn = torch.randn((T, B, 1, H, D), generator=gq, device=dist.device).to(torch.bfloat16)
     vn = torch.randn((T, B, 1, H, D), generator=gq, device=dist.device).to(torch.bfloat16)
-    part = torch.empty((B, H, D + 1), dtype=torch.float32, device=dist.device)
-    gathered = torch.empty((N, B, H, D + 1), dtype=torch.float32, device=dist.device)
     out = torch.empty((B, H, D), dtype=torch.bfloat16, device=dist.device)
+    decode = sharding.SequenceShardedDecode()  # local split-KV decode, NCCL gather, LSE merge
     state = {"t": 0}
 
     def step():
@@ -348,17 +350,7 @@ def bench_longctx_cfg5(dist: Dist, clocks: ClockSampler, warmup: int):
             kernels.kv_append(kc, kn[t], shard + t)
             kernels.kv_append(vc, vn[t], shard + t)
         n_live = shard + (t + 1 if tail else 0)
-        o_loc, lse_loc = kernels.attention_decode(
-            qs[t], kc, vc, slot_begin=0, slot_end=n_live, pos_slot0=dist.rank * shard,
-            q_pos=pos, out_dtype=torch.float32, return_lse=True)
-        if N == 1:
-            out.copy_(o_loc)
-        else:
-            part[..., :D].copy_(o_loc)
-            part[..., D].copy_(lse_loc)
-            dist.pg.all_gather_into_tensor(gathered, part)
-            kernels.lse_merge(gathered[..., :D].contiguous(), gathered[..., D].contiguous(),
-                              out=out)
+        decode(qs[t], kc, vc, slot_begin=0, slot_end=n_live, pos_slot0=k0, q_pos=pos, out=out)
         state["t"] = (t + 1) % T
 
     for _ in range(max(warmup, 3)):

@@ -1,7 +1,7 @@
 // Shared device helpers for the Enilnets B200 attention kernels (sm_100a only).
 //
 // Everything here is a thin inline-PTX wrapper around one Blackwell feature:
-// mbarriers, TMA tensor/bulk copies (never with cluster multicast), tcgen05
+// mbarriers, TMA tensor/bulk copies (each CTA loads its own tiles), tcgen05
 // tensor-memory allocation / MMA / loads / stores, plus the device error word
 // that every bounded wait reports into instead of trapping.
 #pragma once
@@ -107,7 +107,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
 }
 
 // ---------------------------------------------------------------------------
-// TMA (tensor copies global -> shared, no multicast) and bulk copies.
+// TMA tensor copies (global <-> shared, one CTA each) and bulk groups.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

@@ -202,7 +202,9 @@ def decode_ref(q, k_cache, v_cache, *, slot_begin, slot_end, pos_slot0, q_pos,
             e = np.exp(s - m)
             den = np.sum(e, axis=-1, keepdims=True)
             o[:, h] = np.einsum("bs,bsd->bd", e, V[:, h // rep]) / den
-            lse[:, h] = (m + np.log(den))[:, 0]
+            # No visible key: lse = -inf (the partial carries no weight in a
+            # merge), the output stays NaN like the reference's 0/0.
+            lse[:, h] = np.where(np.isneginf(m), -np.inf, m + np.log(den))[:, 0]
     return o, lse
 
 
