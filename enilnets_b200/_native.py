@@ -96,6 +96,7 @@ SIGNATURES = {
     "enl_device_error": ([POINTER(c_int32), POINTER(c_int32), c_int32], c_int32),
     "enl_last_error": ([], c_char_p),
     "enl_abi_version": ([], c_int32),
+    "enl_selftest_wait_timeout": ([c_int64, c_void_p], c_int32),
 }
 
 _lib = None

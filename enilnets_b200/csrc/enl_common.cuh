@@ -91,19 +91,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait on `parity`. Returns false (after recording kDevWaitTimeout and
 // raising *abort) when the budget runs out or when another role already
 // aborted; the caller then stops issuing work and drains.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile int* abort_flag, int site) {
+__device__ __forceinline__ bool mbar_wait_budget(uint64_t* bar, uint32_t parity,
+                                                 volatile int* abort_flag, int site,
+                                                 uint64_t budget_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+    if (globaltimer_ns() - t0 > budget_ns) {
       report_error(kDevWaitTimeout, site);
       *abort_flag = 1;
       return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          volatile int* abort_flag, int site) {
+  return mbar_wait_budget(bar, parity, abort_flag, site, kWaitBudgetNs);
 }
 
 // ---------------------------------------------------------------------------

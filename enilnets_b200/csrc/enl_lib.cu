@@ -6,3 +6,4 @@
 #include "enl_decode.cu"
 #include "enl_kvcache.cu"
 #include "enl_decode_noalloc.cu"
+#include "enl_selftest.cu"

@@ -185,6 +185,16 @@ int enl_device_error(int32_t* code, int32_t* info, int32_t clear);
 /* Message for the last failing call on this thread ("" if none). */
 const char* enl_last_error(void);
 
+/* Site code that enl_selftest_wait_timeout records in the device error word. */
+#define ENL_SELFTEST_SITE 99
+
+/* Diagnostic of the failure path every kernel wait takes: launches one warp
+ * that waits on a barrier nothing arrives on, for budget_ns (1 us .. 100 ms),
+ * then records a wait timeout (code 1, info ENL_SELFTEST_SITE) in the device
+ * error word and returns. No trap and no hang: the context stays usable and
+ * enl_device_error() reports the status. */
+int enl_selftest_wait_timeout(int64_t budget_ns, void* stream);
+
 int enl_abi_version(void);
 
 #ifdef __cplusplus

@@ -168,3 +168,23 @@ def test_rope_kernel_matches_reference_rotation(cuda):
     torch.cuda.synchronize()
     expect = ref.rope_rotate(x.transpose(0, 2, 1, 3), cos[40:73], sin[40:73]).transpose(0, 2, 1, 3)
     np.testing.assert_allclose(_np(t), expect, atol=1e-5)
+
+
+def test_wait_timeout_is_reported_and_context_survives(cuda):
+    """Failure-detection path of every kernel wait: a barrier that nothing
+    arrives on runs out its (short) budget, the kernel records the timeout in
+    the device error word and returns; the next launch works normally."""
+    import torch
+    from enilnets_b200 import _native, kernels
+    lib = _native.load()
+    _native.device_error(clear=True)
+    _native.check(lib.enl_selftest_wait_timeout(2_000_000, None), "enl_selftest_wait_timeout")
+    code, info = _native.device_error(clear=True)
+    assert (code, info) == (1, 99)
+    q = torch.randn((1, 64, 2, 64), device="cuda").to(torch.bfloat16)
+    o = kernels.attention_prefill(q, q, q, causal=True)
+    torch.cuda.synchronize()
+    assert _native.device_error(clear=True) == (0, 0)
+    assert torch.isfinite(o.float()).all()
+    with pytest.raises(ValueError):
+        _native.check(lib.enl_selftest_wait_timeout(10 ** 9, None), "enl_selftest_wait_timeout")
