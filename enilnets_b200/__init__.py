@@ -21,5 +21,6 @@ from .kvcache import KVCache, cached_forward_step  # noqa: F401
 from .layers import (add_cross_attention, add_multihead_attention,  # noqa: F401
                      add_transformer_block, init_weights)
 from .network import AttentionNet  # noqa: F401
+from .generation import TextGenerator  # noqa: F401
 
 NeuralNet = AttentionNet

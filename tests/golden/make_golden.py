@@ -383,7 +383,68 @@ def config1_case():
                         digests=np.array(json.dumps(digests)))
 
 
+TEXTGEN_CORPUS = [
+    "attention reads keys and values; the cache keeps them close.",
+    "a small model writes one letter at a time, then looks back.",
+    "keys fade, values stay, and the window slides along.",
+]
+TEXTGEN_PROMPTS = ["the cache", "a small", "keys and", "values"]
+
+
+def textgen_case():
+    """The reference's TextGenerator (generative/text_generation.py) on a
+    char-level tokenizer, float64, seed 42: greedy ids with and without the
+    KV cache, beam-search ids, batched greedy ids, perplexity, and each
+    greedy step's top-1 / top-2 probability margin (for tie-aware
+    comparison). Also SHA-256 digests of every weight array, to pin the
+    builders' RNG order for the whole stack."""
+    import hashlib
+    from Enilnets.generative.text_generation import TextGenerator
+    from Enilnets.text.text_utils import Tokenizer
+    backend.use_float64(True)
+    tok = Tokenizer(level="char").fit(TEXTGEN_CORPUS)
+    Enilnets.core.utils.set_seed(42)
+    gen = TextGenerator(tok, embed_dim=32, num_heads=4, num_layers=2, max_seq_len=48)
+    digests = []
+    for layer in gen.network.layers:
+        for k in sorted(layer):
+            v = layer[k]
+            if isinstance(v, np.ndarray):
+                digests.append(hashlib.sha256(np.ascontiguousarray(v).tobytes()).hexdigest())
+    out = {"vocab": np.array(json.dumps(tok.word_to_idx)),
+           "digests": np.array(json.dumps(digests))}
+    start = tok.word_to_idx[tok.start_token]
+    for i, prompt in enumerate(TEXTGEN_PROMPTS[:2]):
+        ids = [start] + tok.encode(prompt, add_special_tokens=False).tolist()
+        # greedy path with margins, via the reference's own uncached loop
+        margins = []
+        cur = list(ids)
+        for _ in range(12):
+            probs = gen.network.Forward(np.array([cur[-48:]]), training=False)[0, -1]
+            top = np.sort(probs)[::-1]
+            margins.append(float(top[0] - top[1]))
+            nxt = int(np.argmax(probs))
+            if nxt == tok.word_to_idx[tok.end_token]:
+                break
+            cur.append(nxt)
+        out[f"greedy{i}_text"] = np.array(gen.generate(prompt, max_new_tokens=12, greedy=True))
+        out[f"greedy{i}_text_nocache"] = np.array(
+            gen.generate(prompt, max_new_tokens=12, greedy=True, use_cache=False))
+        out[f"greedy{i}_ids"] = np.array(cur)
+        out[f"greedy{i}_margins"] = np.array(margins)
+        out[f"beam{i}_text"] = np.array(
+            gen.generate_beam(prompt, beam_width=3, max_new_tokens=8))
+    out["batch_texts"] = np.array(json.dumps(
+        gen.generate_batch(TEXTGEN_PROMPTS, max_new_tokens=6, greedy=True)))
+    out["perplexity"] = np.array(gen.perplexity(TEXTGEN_CORPUS[0]))
+    np.savez_compressed(HERE / "textgen.npz", **out)
+
+
 def main():
+    if len(sys.argv) > 1:
+        for name in sys.argv[1:]:
+            globals()[name]()
+        return
     flash_cases()
     mha_layer_cases()
     graph_padding_cases()
@@ -393,6 +454,7 @@ def main():
     kvcache_cases()
     layer_b200_cases()
     config1_case()
+    textgen_case()
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size)
 
