@@ -88,6 +88,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// sleeps until it completes or `hint_ns` passes instead of polling, so
+// waiting warps leave the issue slots to the warps that have work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity,
+                                                    uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait on `parity`. Returns false (after recording kDevWaitTimeout and
 // raising *abort) when the budget runs out or when another role already
 // aborted; the caller then stops issuing work and drains.
@@ -97,7 +113,7 @@ __device__ __forceinline__ bool mbar_wait_budget(uint64_t* bar, uint32_t parity,
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 20000)) return true;
     if (*abort_flag) return false;
     if (globaltimer_ns() - t0 > budget_ns) {
       report_error(kDevWaitTimeout, site);
