@@ -1,0 +1,109 @@
+"""BASELINE configs 3, 4 and 5 at full size. The GPU runs the whole
+configuration, and the float64 oracle checks sampled (batch, head) slices
+against it. Tolerance is the bf16 bar, max abs error <= 2e-2. (Config 2 at
+full size is in test_prefill_gpu.py, config 1 in test_layers_gpu.py.)"""
+import numpy as np
+import pytest
+
+from oracle import attention_ref as ref
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+def _np(t):
+    return t.float().cpu().numpy().astype(np.float64)
+
+
+def test_config3_decode_full_size(cuda):
+    """B64 H32 D128, cache of 8192 bf16 tokens plus one appended token;
+    split-KV decode with the automatic split count."""
+    import torch
+    from enilnets_b200 import _native, kernels
+    B, H, D, ctx = 64, 32, 128, 8192
+    cap = ctx + 128
+    g = torch.Generator(device="cuda").manual_seed(3)
+    kc = torch.zeros((B, H, cap, D), dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    kc[:, :, :ctx].normal_(generator=g)
+    vc[:, :, :ctx].normal_(generator=g)
+    q = torch.randn((B, H, D), generator=g, device="cuda").to(torch.bfloat16)
+    kn = torch.randn((B, 1, H, D), generator=g, device="cuda").to(torch.bfloat16)
+    vn = torch.randn((B, 1, H, D), generator=g, device="cuda").to(torch.bfloat16)
+    kernels.kv_append(kc, kn, ctx)
+    kernels.kv_append(vc, vn, ctx)
+    o, lse = kernels.attention_decode(q, kc, vc, slot_begin=0, slot_end=ctx + 1, pos_slot0=0,
+                                      q_pos=ctx, out_dtype=torch.float32, return_lse=True)
+    torch.cuda.synchronize()
+    _native.raise_on_device_error()
+    on, ln = _np(o), _np(lse)
+    for b in (0, 17, 63):
+        for h in (0, 31):
+            oref, lref = ref.decode_ref(_np(q[b:b + 1, h:h + 1]), _np(kc[b:b + 1, h:h + 1]),
+                                        _np(vc[b:b + 1, h:h + 1]), slot_begin=0,
+                                        slot_end=ctx + 1, pos_slot0=0, q_pos=ctx)
+            assert np.max(np.abs(on[b, h] - oref[0, 0])) <= TOL, (b, h)
+            assert abs(ln[b, h] - lref[0, 0]) <= TOL, (b, h)
+
+
+def test_config4_cross_attention_full_size(cuda):
+    """Decoder B16 x 1024 queries against 2048 memory keys, H16 D64,
+    non-causal, memory key padding with valid lengths ~U[1024, 2048]."""
+    import torch
+    from enilnets_b200 import kernels
+    B, Sq, Skv, H, D = 16, 1024, 2048, 16, 64
+    g = torch.Generator(device="cuda").manual_seed(4)
+    q = torch.randn((B, Sq, H, D), generator=g, device="cuda").to(torch.bfloat16)
+    k = torch.randn((B, Skv, H, D), generator=g, device="cuda").to(torch.bfloat16)
+    v = torch.randn((B, Skv, H, D), generator=g, device="cuda").to(torch.bfloat16)
+    lens = np.random.RandomState(4).randint(1024, 2049, size=B)
+    out = kernels.attention_prefill(q, k, v, causal=False, mask_mode="additive",
+                                    kv_valid_len=torch.tensor(lens, dtype=torch.int32).cuda(),
+                                    out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    oh = _np(out)
+    rows = np.array([0, 511, 1023])
+    rows_t = torch.tensor(rows, device="cuda")
+    for b in (0, 7, 15):
+        for h in (0, 15):
+            o_r, _ = ref.attention_ref(_np(q[b:b + 1, rows_t][:, :, h:h + 1]),
+                                       _np(k[b:b + 1, :, h:h + 1]), _np(v[b:b + 1, :, h:h + 1]),
+                                       kv_valid_len=[lens[b]], mask_mode="additive")
+            err = np.max(np.abs(o_r[0, :, 0] - oh[b, rows, h]))
+            assert err <= TOL, (b, h, err)
+
+
+def test_config5_long_context_full_size(cuda):
+    """B4 H32 D128 over a 262144-token cache. The split-KV decode over the
+    whole sequence agrees with the oracle, and a decode over 8 contiguous
+    sequence shards merged by LSE (the multi-GPU path, run here on one GPU)
+    agrees with both."""
+    import torch
+    from enilnets_b200 import _native, kernels, sharding
+    B, H, D, ctx = 4, 32, 128, 262144
+    g = torch.Generator(device="cuda").manual_seed(5)
+    kc = torch.empty((B, H, ctx, D), dtype=torch.bfloat16, device="cuda").normal_(generator=g)
+    vc = torch.empty_like(kc).normal_(generator=g)
+    q = torch.randn((B, H, D), generator=g, device="cuda").to(torch.bfloat16)
+    o = kernels.attention_decode(q, kc, vc, slot_begin=0, slot_end=ctx, pos_slot0=0,
+                                 q_pos=ctx - 1, out_dtype=torch.float32)
+    parts_o, parts_l = [], []
+    for r in range(8):
+        s0, s1 = sharding.kv_shard_range(ctx, 8, r)
+        po, pl = kernels.attention_decode(q, kc[:, :, s0:s1], vc[:, :, s0:s1], slot_begin=0,
+                                          slot_end=s1 - s0, pos_slot0=s0, q_pos=ctx - 1,
+                                          out_dtype=torch.float32, return_lse=True)
+        parts_o.append(po)
+        parts_l.append(pl)
+    merged = kernels.lse_merge(torch.stack(parts_o), torch.stack(parts_l),
+                               out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    _native.raise_on_device_error()
+    on, mn = _np(o), _np(merged)
+    assert np.max(np.abs(on - mn)) <= 1e-3
+    for b, h in ((0, 0), (3, 31)):
+        oref, _ = ref.decode_ref(_np(q[b:b + 1, h:h + 1]), _np(kc[b:b + 1, h:h + 1]),
+                                 _np(vc[b:b + 1, h:h + 1]), slot_begin=0, slot_end=ctx,
+                                 pos_slot0=0, q_pos=ctx - 1)
+        assert np.max(np.abs(on[b, h] - oref[0, 0])) <= TOL, (b, h)
+        assert np.max(np.abs(mn[b, h] - oref[0, 0])) <= TOL, (b, h)
