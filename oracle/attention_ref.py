@@ -186,6 +186,8 @@ def decode_ref(q, k_cache, v_cache, *, slot_begin, slot_end, pos_slot0, q_pos,
     Hkv = k_cache.shape[1]
     rep = H // Hkv
     scale = 1.0 / math.sqrt(D) if scale is None else scale
+    if slot_end <= slot_begin:  # no key at all: 0/0 output, zero-weight partial
+        return np.full((B, H, D), np.nan), np.full((B, H), -np.inf)
     K = np.asarray(k_cache[:, :, slot_begin:slot_end], np.float64)
     V = np.asarray(v_cache[:, :, slot_begin:slot_end], np.float64)
     k_pos = pos_slot0 + np.arange(slot_begin, slot_end)
