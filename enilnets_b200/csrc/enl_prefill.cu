@@ -53,7 +53,11 @@ namespace enl {
 #ifndef ENL_EXP_EMU_EVERY
 #define ENL_EXP_EMU_EVERY 4
 #endif
+#ifndef ENL_EXP_EMU_EVERY_D64
+#define ENL_EXP_EMU_EVERY_D64 4
+#endif
 constexpr int kEmuEvery = ENL_EXP_EMU_EVERY;
+constexpr int kEmuEvery64 = ENL_EXP_EMU_EVERY_D64;  // head dim 64: half the tensor work per tile
 
 // kSplit: fp32 inputs arrive as two bf16 planes, hi = bf16(x) and
 // lo = bf16(x - hi), and each product is formed from three bf16 MMAs
@@ -85,7 +89,7 @@ struct PrefillCfg {
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
   static constexpr uint32_t kTmemCols = 512;
   // Exponentials from the FMA-pipe polynomial are too coarse for the split path.
-  static constexpr int kEmu = kSplit ? 0 : kEmuEvery;
+  static constexpr int kEmu = kSplit ? 0 : (D == 64 ? kEmuEvery64 : kEmuEvery);
   __host__ __device__ static constexpr uint32_t col_s(int buf) { return 128u * buf; }
   __host__ __device__ static constexpr uint32_t col_o(int half) { return 256u + D * half; }
 };
