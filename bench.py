@@ -486,6 +486,14 @@ def cpu_info():
     return model, os.cpu_count()
 
 
+def arm_config(n_gpus: int) -> dict:
+    """The headline workload's config, shared by both arms."""
+    return {"workload": "cfg2 causal prefill B8/GPU S4096 H16 D128, key padding L~U[2048,4096]",
+            "global_batch": CFG2["B"] * n_gpus, "seq_len": CFG2["S"],
+            "parallelism": f"batch x head over {n_gpus} GPU(s), no collective",
+            "l2": "inputs 402 MB per GPU > 126 MB L2 (no flush needed)"}
+
+
 def run_reference(args):
     """--impl reference: the reference algorithm (NumPy float64 port) on the
     host cores, rank 0 only."""
@@ -506,8 +514,9 @@ def run_reference(args):
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1000 * t_total / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": {"workload": "cfg2 causal prefill sample (reference flash path)",
-                       "cpu": model},
+            "config": {**arm_config(args.gpus), "cpu": model,
+                       "reference_sample": "the reference's streaming softmax on a bounded "
+                                           "sample of the workload, scaled by useful FLOPs"},
             "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port",
                              "sample": sample},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
@@ -606,12 +615,7 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": pre["ms_step"],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic N(0,1) activations, seeded",
-            "config": {"workload": "cfg2 causal prefill B8/GPU S4096 H16 D128, key padding "
-                                   "L~U[2048,4096]",
-                       "global_batch": CFG2["B"] * args.gpus, "seq_len": CFG2["S"],
-                       "parallelism": f"batch x head over {args.gpus} GPU(s), no collective",
-                       "l2": "inputs 402 MB per GPU > 126 MB L2 (no flush needed)",
-                       "lengths_rank0": pre["lengths"]},
+            "config": {**arm_config(args.gpus), "lengths_rank0": pre["lengths"]},
             "e2e": pre["e2e"],
             "roofline": roofline,
             "cpu_baseline": cpu,
