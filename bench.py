@@ -239,24 +239,62 @@ def bench_prefill(dist: Dist, clocks: ClockSampler, steps: int, warmup: int, bat
     if not e2e_on:
         return dict(value=value, ms_step=ms_step, flops_rank=flops_rank, flops_total=flops_total,
                     e2e=None, lengths=[int(x) for x in lengths], per_launch_ms=ms_step)
-    # End to end: host (pinned) inputs -> H2D -> kernel -> D2H of the output,
-    # through the same public call, every step.
+    # End to end through the same public call: every step copies its inputs
+    # from pinned host memory and reads its output back. Consecutive steps
+    # overlap (PCIe is full duplex): two device input/output sets on separate
+    # copy streams, so step i + 1's inputs go up while step i computes and
+    # step i - 1's output comes down. Events order each slot's reuse.
     hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
-    hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    dq, dk, dv = (torch.empty_like(t) for t in (q, k, v))
+    hout = [torch.empty(out.shape, dtype=out.dtype).pin_memory() for _ in range(2)]
+    dev_in = [tuple(torch.empty_like(t) for t in (q, k, v)) for _ in range(2)]
+    dev_out = [torch.empty_like(out) for _ in range(2)]
+    s_in, s_cmp, s_out = (torch.cuda.Stream(device=dist.device) for _ in range(3))
+    ev_in, ev_cmp, ev_out = ([torch.cuda.Event() for _ in range(2)] for _ in range(3))
+    used = [False, False]
 
-    def e2e_step():
-        dq.copy_(hq, non_blocking=True)
-        dk.copy_(hk, non_blocking=True)
-        dv.copy_(hv, non_blocking=True)
-        kernels.attention_prefill(dq, dk, dv, causal=True, kv_valid_len=lens,
-                                  mask_mode="additive", out=out)
-        hout.copy_(out, non_blocking=True)
+    def e2e_step(i):
+        slot = i % 2
+        dq, dk, dv = dev_in[slot]
+        with torch.cuda.stream(s_in):
+            if used[slot]:
+                s_in.wait_event(ev_cmp[slot])  # the slot's previous kernel read its inputs
+            dq.copy_(hq, non_blocking=True)
+            dk.copy_(hk, non_blocking=True)
+            dv.copy_(hv, non_blocking=True)
+            ev_in[slot].record(s_in)
+        with torch.cuda.stream(s_cmp):
+            s_cmp.wait_event(ev_in[slot])
+            if used[slot]:
+                s_cmp.wait_event(ev_out[slot])  # the slot's previous output is on the host
+            kernels.attention_prefill(dq, dk, dv, causal=True, kv_valid_len=lens,
+                                      mask_mode="additive", out=dev_out[slot])
+            ev_cmp[slot].record(s_cmp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_cmp[slot])
+            hout[slot].copy_(dev_out[slot], non_blocking=True)
+            ev_out[slot].record(s_out)
+        used[slot] = True
 
-    e2e_steps = max(3, min(steps, 20))
-    for _ in range(2):
-        e2e_step()
-    ms_e2e = timed(dist, clocks, e2e_step, e2e_steps) / e2e_steps
+    e2e_steps = max(4, min(steps, 20))
+    for i in range(2):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    cur = torch.cuda.current_stream()
+    dist.barrier()
+    t0 = time.time()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(cur)
+    for s_ in (s_in, s_cmp, s_out):
+        s_.wait_stream(cur)
+    for i in range(e2e_steps):
+        e2e_step(i)
+    cur.wait_stream(s_out)
+    end.record(cur)
+    torch.cuda.synchronize()
+    clocks.mark(t0, time.time())
+    dist.barrier()
+    ms_e2e = dist.max(start.elapsed_time(end)) / e2e_steps
     h2d = 3 * q.numel() * q.element_size()
     d2h = out.numel() * out.element_size()
     e2e = {"value": flops_total / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
