@@ -13,7 +13,10 @@
 //   warp 9      S issuer: S = Q K^T (smem x smem) into a double-buffered S
 //               in tensor memory
 //   warp 10     P V issuer: O += P V with P read from tensor memory
-//   warp 11     idle member of the producer warpgroup
+//   warp 11     output stores: for bf16 output the epilogue stages O in the
+//               finished item's Q buffer (the Q tile's swizzled layout) and
+//               this warp writes it with TMA bulk-tensor stores, then
+//               releases the buffer to the next Q load
 // The two issuers run independently (warp-uniform loops, elect.sync issue),
 // so a P V never queues behind the issue of an S that the tensor pipe is
 // still busy with; S(g + 2) waits only for P V(g) to finish with its buffer.
