@@ -244,8 +244,15 @@ def bench_prefill(dist: Dist, clocks: ClockSampler, steps: int, warmup: int, bat
     # overlap (PCIe is full duplex): two device input/output sets on separate
     # copy streams, so step i + 1's inputs go up while step i computes and
     # step i - 1's output comes down. Events order each slot's reuse.
-    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
-    hout = [torch.empty(out.shape, dtype=out.dtype).pin_memory() for _ in range(2)]
+    # The pinned buffers are allocated and first touched on the GPU's own
+    # NUMA node (enilnets_b200.hostmem): with eight ranks copying at once,
+    # buffers on the far socket make the socket link the bottleneck.
+    from enilnets_b200 import hostmem
+    with hostmem.local_to(dist.local_rank) as host_cpus:
+        hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+        hout = [torch.empty(out.shape, dtype=out.dtype).pin_memory() for _ in range(2)]
+        for h in hout:
+            h.zero_()
     dev_in = [tuple(torch.empty_like(t) for t in (q, k, v)) for _ in range(2)]
     dev_out = [torch.empty_like(out) for _ in range(2)]
     s_in, s_cmp, s_out = (torch.cuda.Stream(device=dist.device) for _ in range(3))
@@ -298,7 +305,9 @@ def bench_prefill(dist: Dist, clocks: ClockSampler, steps: int, warmup: int, bat
     h2d = 3 * q.numel() * q.element_size()
     d2h = out.numel() * out.element_size()
     e2e = {"value": flops_total / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
-           "ms_per_step": ms_e2e, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+           "ms_per_step": ms_e2e, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+           "pinned_host_memory": (f"GPU-local NUMA node ({len(host_cpus)} CPUs)" if host_cpus
+                                  else "unbound (NVML gave no CPU affinity)")}
     return dict(value=value, ms_step=ms_step, flops_rank=flops_rank, flops_total=flops_total,
                 e2e=e2e, lengths=[int(x) for x in lengths], per_launch_ms=ms_step)
 
