@@ -32,7 +32,7 @@ DEVICE_ERRORS = {1: "an mbarrier wait exceeded its time budget",
                  3: "a launch-time shape invariant was violated"}
 
 
-ABI_VERSION = 2  # ENL_ABI_VERSION of include/enl_attn.h
+ABI_VERSION = 3  # ENL_ABI_VERSION of include/enl_attn.h
 
 
 class PrefillArgs(Structure):
@@ -73,6 +73,38 @@ class DecodeArgs(Structure):
     ]
 
 
+class PhiArgs(Structure):
+    """Mirror of enl_phi_args."""
+    _fields_ = [
+        ("x", c_void_p), ("x_stride_b", c_int64), ("x_stride_s", c_int64),
+        ("x_stride_h", c_int64),
+        ("batch", c_int32), ("seq", c_int32), ("num_heads", c_int32), ("head_dim", c_int32),
+        ("in_dtype", c_int32), ("kernel", c_int32),
+        ("omega", c_void_p), ("num_features", c_int32), ("global_stab", c_int32),
+        ("stab_floor", c_void_p), ("stab", c_void_p), ("phi", c_void_p),
+    ]
+
+
+class LinearArgs(Structure):
+    """Mirror of enl_linear_args."""
+    _fields_ = [
+        ("phi_q", c_void_p), ("phi_k", c_void_p),
+        ("v", c_void_p), ("v_stride_b", c_int64), ("v_stride_s", c_int64),
+        ("v_stride_h", c_int64), ("v_dtype", c_int32),
+        ("o", c_void_p), ("o_stride_b", c_int64), ("o_stride_s", c_int64),
+        ("o_stride_h", c_int64), ("out_dtype", c_int32),
+        ("batch", c_int32), ("num_heads", c_int32), ("num_kv_heads", c_int32),
+        ("seq", c_int32), ("num_features", c_int32), ("head_dim", c_int32),
+        ("causal", c_int32),
+        ("kv_in", c_void_p), ("ksum_in", c_void_p), ("state_scale", c_void_p),
+        ("kv_out", c_void_p), ("ksum_out", c_void_p),
+        ("eps", c_float),
+    ]
+
+
+ENL_PHI_LINEAR = 0
+ENL_PHI_PERFORMER = 1
+
 # Exported symbol -> (argtypes, restype). Kept in sync with include/enl_attn.h
 # (a CPU test checks every declared symbol is exported and bound here).
 SIGNATURES = {
@@ -93,6 +125,9 @@ SIGNATURES = {
     "enl_rope_apply": ([c_void_p, c_int64, c_int64, c_int64, c_int32, c_int32, c_int32,
                         c_int32, c_int32, c_void_p, c_void_p, c_int64, c_int64, c_void_p],
                        c_int32),
+    "enl_linear_feature_map": ([POINTER(PhiArgs), c_void_p], c_int32),
+    "enl_linear_attention": ([POINTER(LinearArgs), c_void_p], c_int32),
+    "enl_linear_max_features": ([], c_int32),
     "enl_device_error": ([POINTER(c_int32), POINTER(c_int32), c_int32], c_int32),
     "enl_last_error": ([], c_char_p),
     "enl_abi_version": ([], c_int32),

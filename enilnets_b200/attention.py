@@ -24,13 +24,16 @@ from .backend import compute_dtype, device, to_device
 SINUSOIDAL_BASE = 10000.0  # core/constants.py:70
 
 
+LINEAR_KERNELS = ("linear", "performer")
+
+
 def check_supported(layer: dict, training: bool = False) -> None:
     """Raise ValueError for options the B200 kernels do not implement, naming
     the option, instead of falling back to another backend."""
     kernel = layer.get("attention_kernel", "softmax")
-    if kernel != "softmax":
+    if kernel != "softmax" and kernel not in LINEAR_KERNELS:
         raise ValueError(f"attention_kernel={kernel!r} is not supported by the B200 attention "
-                         "path (softmax attention only).")
+                         "path (softmax, linear and performer only).")
     if layer.get("sparse_pattern") is not None:
         raise ValueError("sparse_pattern is not supported by the B200 attention path.")
     if training and layer.get("dropout", 0.0) > 0:
@@ -143,6 +146,24 @@ def lengths_from_mask(mask, B: int, S: int):
     return lengths.astype(np.int32)
 
 
+def omega_tensor(layer: dict):
+    """The Performer projection of a layer as a device fp32 tensor."""
+    import torch
+    return _WEIGHTS.get(layer, ("omega",), "w", torch.float32)
+
+
+def linearized(layer: dict, q, k, v, causal: bool):
+    """phi(Q) (phi(K)^T V) / (phi(Q) . sum phi(K)) for a linear or performer
+    layer (nn/forward.py:456-478): queries take the row stabilizer, keys one
+    global stabilizer per (batch, kv head), the same as the reference's per
+    expanded head since a group's heads are copies."""
+    kernel = layer["attention_kernel"]
+    omega = omega_tensor(layer) if kernel == "performer" else None
+    qp, _ = kernels.linear_feature_map(q, kernel, omega)
+    kp, _ = kernels.linear_feature_map(k, kernel, omega, global_stab=True)
+    return kernels.linear_attention(qp, kp, v, causal=causal, out_dtype=compute_dtype())
+
+
 # ------------------------------------------------------------- forward
 def self_attention(layer: dict, x, key_padding_mask=None, mask_mode: Optional[str] = None):
     """One multihead_attention layer on a (B, S, E) device tensor; returns
@@ -162,6 +183,12 @@ def self_attention(layer: dict, x, key_padding_mask=None, mask_mode: Optional[st
     if scheme == "rope":
         apply_rope(q, 0)
         apply_rope(k, 0)
+    if layer.get("attention_kernel", "softmax") in LINEAR_KERNELS:
+        if key_padding_mask is not None:
+            raise ValueError("key_padding_mask is not supported with a linearized "
+                             "attention_kernel (it builds no score matrix to mask)")
+        ctx = linearized(layer, q, k, v, bool(layer.get("causal", False)))
+        return project(ctx.flatten(-2), layer, "o").float()
     lens = None
     mode = mask_mode or "exclude"
     if key_padding_mask is not None:

@@ -487,4 +487,97 @@ int enl_rope_apply(void* x, int64_t stride_b, int64_t stride_s, int64_t stride_h
   return ENL_OK;
 }
 
+int enl_linear_max_features(void) { return enl::linear_attn_max_features(); }
+
+int enl_linear_feature_map(const enl_phi_args* a, void* stream) {
+  if (!a || !a->x || !a->phi)
+    return fail(ENL_ERR_INVALID, "enl_linear_feature_map: args, x and phi must be non-NULL");
+  if (a->batch < 0 || a->seq < 0 || a->num_heads < 1 || a->head_dim < 1 || a->head_dim > 1024)
+    return fail(ENL_ERR_INVALID, "enl_linear_feature_map: bad sizes (batch %d, seq %d, heads %d, "
+                "head_dim %d)", a->batch, a->seq, a->num_heads, a->head_dim);
+  if (a->in_dtype != ENL_DTYPE_BF16 && a->in_dtype != ENL_DTYPE_FP32)
+    return fail(ENL_ERR_INVALID, "enl_linear_feature_map: in_dtype=%d", a->in_dtype);
+  if (a->kernel != ENL_PHI_LINEAR && a->kernel != ENL_PHI_PERFORMER)
+    return fail(ENL_ERR_INVALID, "enl_linear_feature_map: kernel=%d", a->kernel);
+  if (a->kernel == ENL_PHI_PERFORMER) {
+    if (!a->omega || a->num_features < 1 || a->num_features > 1024)
+      return fail(ENL_ERR_INVALID, "enl_linear_feature_map: performer needs omega and "
+                  "1 <= num_features <= 1024 (got %d)", a->num_features);
+    if (a->global_stab && !a->stab)
+      return fail(ENL_ERR_INVALID, "enl_linear_feature_map: a global stabilizer needs stab");
+  }
+  enl::PhiParams p{};
+  p.x = a->x;
+  p.sb = a->x_stride_b;
+  p.ss = a->x_stride_s;
+  p.sh = a->x_stride_h;
+  p.B = a->batch;
+  p.S = a->seq;
+  p.H = a->num_heads;
+  p.Dh = a->head_dim;
+  p.in_f32 = a->in_dtype == ENL_DTYPE_FP32;
+  p.kernel = a->kernel;
+  p.omega = a->omega;
+  p.Df = a->kernel == ENL_PHI_LINEAR ? a->head_dim : a->num_features;
+  p.global_stab = a->kernel == ENL_PHI_PERFORMER && a->global_stab;
+  p.stab_floor = a->stab_floor;
+  p.stab = a->stab;
+  p.phi = a->phi;
+  cudaError_t e = enl::launch_phi(p, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "enl_linear_feature_map launch");
+  return ENL_OK;
+}
+
+int enl_linear_attention(const enl_linear_args* a, void* stream) {
+  if (!a || !a->phi_q || !a->phi_k || !a->v || !a->o)
+    return fail(ENL_ERR_INVALID, "enl_linear_attention: args, phi_q, phi_k, v and o must be non-NULL");
+  if (a->batch < 0 || a->seq < 0 || a->num_heads < 1 || a->num_kv_heads < 1 || a->head_dim < 1 ||
+      a->num_features < 1)
+    return fail(ENL_ERR_INVALID, "enl_linear_attention: bad sizes");
+  if (a->num_heads % a->num_kv_heads != 0)
+    return fail(ENL_ERR_INVALID, "enl_linear_attention: num_heads %d is not a multiple of "
+                "num_kv_heads %d", a->num_heads, a->num_kv_heads);
+  if (a->num_features > enl::linear_attn_max_features())
+    return fail(ENL_ERR_UNSUPPORTED, "enl_linear_attention: num_features %d > %d",
+                a->num_features, enl::linear_attn_max_features());
+  if ((a->v_dtype != ENL_DTYPE_BF16 && a->v_dtype != ENL_DTYPE_FP32) ||
+      (a->out_dtype != ENL_DTYPE_BF16 && a->out_dtype != ENL_DTYPE_FP32))
+    return fail(ENL_ERR_INVALID, "enl_linear_attention: v_dtype=%d out_dtype=%d", a->v_dtype,
+                a->out_dtype);
+  if (!a->causal && (a->kv_in || a->ksum_in || a->kv_out || a->ksum_out))
+    return fail(ENL_ERR_INVALID, "enl_linear_attention: a carried state needs causal attention");
+  if ((a->kv_in == nullptr) != (a->ksum_in == nullptr) ||
+      (a->kv_out == nullptr) != (a->ksum_out == nullptr))
+    return fail(ENL_ERR_INVALID, "enl_linear_attention: kv and ksum come in pairs");
+  enl::LinearParams p{};
+  p.phi_q = a->phi_q;
+  p.phi_k = a->phi_k;
+  p.v = a->v;
+  p.v_sb = a->v_stride_b;
+  p.v_ss = a->v_stride_s;
+  p.v_sh = a->v_stride_h;
+  p.v_f32 = a->v_dtype == ENL_DTYPE_FP32;
+  p.o = a->o;
+  p.o_sb = a->o_stride_b;
+  p.o_ss = a->o_stride_s;
+  p.o_sh = a->o_stride_h;
+  p.o_f32 = a->out_dtype == ENL_DTYPE_FP32;
+  p.B = a->batch;
+  p.H = a->num_heads;
+  p.Hkv = a->num_kv_heads;
+  p.S = a->seq;
+  p.Df = a->num_features;
+  p.D = a->head_dim;
+  p.causal = a->causal;
+  p.kv_in = a->kv_in;
+  p.ks_in = a->ksum_in;
+  p.state_scale = a->state_scale;
+  p.kv_out = a->kv_out;
+  p.ks_out = a->ksum_out;
+  p.eps = a->eps;
+  cudaError_t e = enl::launch_linear_attn(p, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "enl_linear_attention launch");
+  return ENL_OK;
+}
+
 }  // extern "C"

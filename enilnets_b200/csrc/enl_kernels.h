@@ -97,4 +97,49 @@ cudaError_t launch_rope(void* x, long long x_sb, long long x_ss, long long x_sh,
                         int H, int D, int elem_bytes, const float* cos_t, const float* sin_t,
                         long long table_row0, long long n_rows, cudaStream_t stream);
 
+// Linearized attention feature map (enl_linear.cu): x[b, s, h, :] (strided,
+// bf16 or fp32) -> phi[b, h, s, :] fp32, Df = Dh for kernel 0 (elu + 1) or
+// the rows of omega for kernel 1 (Performer). With global_stab, stab[b*H + h]
+// receives the stabilizer (the max of w.x' over the call's rows, no lower
+// than stab_floor when given); otherwise each row uses its own max.
+struct PhiParams {
+  const void* x;
+  long long sb, ss, sh;
+  int B, S, H, Dh;
+  bool in_f32;
+  int kernel;
+  const float* omega;
+  int Df;
+  int global_stab;
+  const float* stab_floor;
+  float* stab;
+  float* phi;
+};
+cudaError_t launch_phi(const PhiParams& p, cudaStream_t stream);
+
+// Linear attention over phi(Q) (B, H, S, Df) and phi(K) (B, Hkv, S, Df) with
+// V[b, s, hkv, :] (strided); o[b, s, h, :]. Causal runs prefix sums starting
+// from the carried state (kv_in (B, Hkv, Df, D), ks_in (B, Hkv, Df), each
+// times state_scale[b*Hkv + hkv]) and returns the final sums in kv_out/ks_out.
+struct LinearParams {
+  const float* phi_q;
+  const float* phi_k;
+  const void* v;
+  long long v_sb, v_ss, v_sh;
+  bool v_f32;
+  void* o;
+  long long o_sb, o_ss, o_sh;
+  bool o_f32;
+  int B, H, Hkv, S, Df, D;
+  int causal;
+  const float* kv_in;
+  const float* ks_in;
+  const float* state_scale;
+  float* kv_out;
+  float* ks_out;
+  float eps;
+};
+cudaError_t launch_linear_attn(const LinearParams& p, cudaStream_t stream);
+int linear_attn_max_features();
+
 }  // namespace enl

@@ -7,3 +7,4 @@
 #include "enl_kvcache.cu"
 #include "enl_decode_noalloc.cu"
 #include "enl_selftest.cu"
+#include "enl_linear.cu"

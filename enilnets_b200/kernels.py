@@ -272,3 +272,111 @@ def rope_(x: torch.Tensor, cos_table: torch.Tensor, sin_table: torch.Tensor,
                                         _stream()),
               "enl_rope_apply")
     return x
+
+
+_PHI_KERNELS = {"linear": nat.ENL_PHI_LINEAR, "performer": nat.ENL_PHI_PERFORMER}
+
+
+def linear_feature_map(x: torch.Tensor, kernel: str, omega: Optional[torch.Tensor] = None, *,
+                       global_stab: bool = False, stab_floor: Optional[torch.Tensor] = None):
+    """phi(x) of the linearized attention kernels (nn/attention_kernels.py:58-74).
+
+    x: (B, S, H, Dh) bf16/fp32 head view. kernel "linear" (elu + 1) or
+    "performer" with omega (Df, Dh) fp32. Returns (phi (B, H, S, Df) fp32,
+    stab (B, H) fp32 or None): with global_stab (keys) one stabilizer per
+    (b, h), the max of w.x' over every row and stab_floor; otherwise (queries)
+    each row's own max."""
+    if kernel not in _PHI_KERNELS:
+        raise ValueError(f"Unknown attention feature map: {kernel!r}")
+    _require_cuda("x", x)
+    if x.dtype not in _DTYPES or x.dim() != 4:
+        raise ValueError("x must be a 4-D bf16 or fp32 tensor (batch, seq, heads, head_dim)")
+    B, S, H, Dh = x.shape
+    performer = kernel == "performer"
+    if performer:
+        _require_cuda("omega", omega, torch.float32)
+        if omega.dim() != 2 or omega.shape[1] != Dh or not omega.is_contiguous():
+            raise ValueError(f"omega must be a contiguous (num_features, {Dh}) fp32 tensor")
+    Df = omega.shape[0] if performer else Dh
+    phi = torch.empty((B, H, S, Df), device=x.device, dtype=torch.float32)
+    stab = None
+    if performer and global_stab:
+        stab = torch.empty((B, H), device=x.device, dtype=torch.float32)
+        if stab_floor is not None:
+            _require_cuda("stab_floor", stab_floor, torch.float32, last_contiguous=False)
+            stab_floor = stab_floor.reshape(B, H).contiguous()
+    a = nat.PhiArgs()
+    a.x = x.data_ptr()
+    a.x_stride_b, a.x_stride_s, a.x_stride_h = x.stride(0), x.stride(1), x.stride(2)
+    a.batch, a.seq, a.num_heads, a.head_dim = B, S, H, Dh
+    a.in_dtype = _DTYPES[x.dtype]
+    a.kernel = _PHI_KERNELS[kernel]
+    a.omega = _ptr(omega) if performer else None
+    a.num_features = Df if performer else 0
+    a.global_stab = int(performer and global_stab)
+    a.stab_floor = _ptr(stab_floor) if stab is not None else None
+    a.stab = _ptr(stab)
+    a.phi = phi.data_ptr()
+    nat.check(nat.load().enl_linear_feature_map(ctypes.byref(a), _stream()),
+              "enl_linear_feature_map")
+    return phi, stab
+
+
+def linear_attention(phi_q: torch.Tensor, phi_k: torch.Tensor, v: torch.Tensor, *,
+                     causal: bool, state=None, state_scale: Optional[torch.Tensor] = None,
+                     return_state: bool = False, out_dtype: torch.dtype = torch.float32,
+                     eps: float = 1e-20):
+    """Linear attention over feature-mapped queries/keys
+    (nn/attention_kernels.py:119-143). phi_q (B, H, S, Df), phi_k (B, Hkv, S, Df)
+    fp32; v (B, S, Hkv, D) bf16/fp32 head view. Causal: prefix sums, starting
+    from state = (kv (B, Hkv, Df, D), ksum (B, Hkv, Df)) times state_scale
+    (B, Hkv) when given; with return_state the sums after the last row are
+    returned too. Returns out (B, S, H, D) [, (kv, ksum)]."""
+    for name, t in (("phi_q", phi_q), ("phi_k", phi_k)):
+        _require_cuda(name, t, torch.float32)
+        if t.dim() != 4 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous 4-D fp32 tensor")
+    _require_cuda("v", v)
+    if v.dtype not in _DTYPES or v.dim() != 4:
+        raise ValueError("v must be a 4-D bf16 or fp32 tensor (batch, seq, kv_heads, head_dim)")
+    B, H, S, Df = phi_q.shape
+    _, Hkv, Sk, Dfk = phi_k.shape
+    D = v.shape[3]
+    if (phi_k.shape[0], Sk, Dfk) != (B, S, Df) or tuple(v.shape[:3]) != (B, S, Hkv):
+        raise ValueError(f"shape mismatch: phi_q {tuple(phi_q.shape)}, phi_k "
+                         f"{tuple(phi_k.shape)}, v {tuple(v.shape)}")
+    if (state is not None or return_state) and not causal:
+        raise ValueError("a carried state needs causal attention")
+    out = torch.empty((B, S, H, D), device=phi_q.device, dtype=out_dtype)
+    new_state = None
+    if return_state:
+        new_state = (torch.empty((B, Hkv, Df, D), device=phi_q.device, dtype=torch.float32),
+                     torch.empty((B, Hkv, Df), device=phi_q.device, dtype=torch.float32))
+    if state is not None:
+        for name, t, shape in (("kv", state[0], (B, Hkv, Df, D)), ("ksum", state[1], (B, Hkv, Df))):
+            _require_cuda(name, t, torch.float32)
+            if tuple(t.shape) != shape or not t.is_contiguous():
+                raise ValueError(f"state {name} must be a contiguous fp32 {shape} tensor")
+        if state_scale is not None:
+            _require_cuda("state_scale", state_scale, torch.float32, last_contiguous=False)
+            state_scale = state_scale.reshape(B, Hkv).contiguous()
+    a = nat.LinearArgs()
+    a.phi_q, a.phi_k = phi_q.data_ptr(), phi_k.data_ptr()
+    a.v = v.data_ptr()
+    a.v_stride_b, a.v_stride_s, a.v_stride_h = v.stride(0), v.stride(1), v.stride(2)
+    a.v_dtype = _DTYPES[v.dtype]
+    a.o = out.data_ptr()
+    a.o_stride_b, a.o_stride_s, a.o_stride_h = out.stride(0), out.stride(1), out.stride(2)
+    a.out_dtype = _DTYPES[out_dtype]
+    a.batch, a.num_heads, a.num_kv_heads, a.seq = B, H, Hkv, S
+    a.num_features, a.head_dim = Df, D
+    a.causal = int(bool(causal))
+    a.kv_in = _ptr(state[0]) if state is not None else None
+    a.ksum_in = _ptr(state[1]) if state is not None else None
+    a.state_scale = _ptr(state_scale) if state is not None else None
+    a.kv_out = _ptr(new_state[0]) if new_state is not None else None
+    a.ksum_out = _ptr(new_state[1]) if new_state is not None else None
+    a.eps = float(eps)
+    nat.check(nat.load().enl_linear_attention(ctypes.byref(a), _stream()),
+              "enl_linear_attention")
+    return (out, new_state) if return_state else out

@@ -142,6 +142,9 @@ class KVCache:
             self._kv[key] = self._kv[key].gather(idx)
         for key in list(self.residual):
             self.residual[key] = self.residual[key].index_select(0, idx)
+        for key in list(self.linear):
+            self.linear[key] = tuple(None if t is None else t.index_select(0, idx)
+                                     for t in self.linear[key])
 
     def expand(self, size: int) -> None:
         """Replicate a batch-1 cache to `size` rows (nn/kvcache.py:63-66)."""
@@ -172,6 +175,8 @@ def attention_step(layer: Dict[str, Any], x, idx: int, cache: KVCache, B: int, S
         # Rotate at absolute positions; the cache stores rotated K.
         attention.apply_rope(q, pos)
         attention.apply_rope(k_new, pos)
+    if layer.get("attention_kernel", "softmax") in attention.LINEAR_KERNELS:
+        return _linear_step(layer, q, k_new, v_new, idx, cache)
     lc = cache._kv.get(idx)
     if lc is None:
         lc = _LayerKV(B, Hkv, D, base=pos, need=S_new, dtype=qkv.dtype)
@@ -199,6 +204,36 @@ def attention_step(layer: Dict[str, Any], x, idx: int, cache: KVCache, B: int, S
         ctx = kernels.attention_prefill(q, kv_k, kv_v, causal=True, window=window,
                                         alibi_slopes=slopes, q_pos0=pos,
                                         k_pos0=lc.base + lc.begin, out_dtype=qkv.dtype)
+    return attention.project(ctx.flatten(-2), layer, "o").float()
+
+
+def _linear_step(layer: Dict[str, Any], q, k_new, v_new, idx: int, cache: KVCache):
+    """Cached step of a linearized layer (nn/kvcache.py:217-260): causal
+    linear attention is a linear RNN, so the whole history is the running
+    sums sum phi(k) v^T and sum phi(k), kept on the device in cache.linear[idx]
+    as (kv (B, Hkv, Df, D), ksum (B, Hkv, Df), stabilizer (B, Hkv) or None).
+    Performer keys share one stabilizer across steps: the larger of the
+    carried one and this step's, with the carried sums scaled down by
+    exp(old - new) (the ratio is scale-invariant)."""
+    import torch
+    kernel = layer["attention_kernel"]
+    prev = cache.linear.get(idx)
+    omega = attention.omega_tensor(layer) if kernel == "performer" else None
+    scale = None
+    stab = None
+    if kernel == "performer":
+        floor = prev[2] if prev is not None else None
+        kp, stab = kernels.linear_feature_map(k_new, kernel, omega, global_stab=True,
+                                              stab_floor=floor)
+        if prev is not None:
+            scale = torch.exp(prev[2] - stab)
+    else:
+        kp, _ = kernels.linear_feature_map(k_new, kernel)
+    qp, _ = kernels.linear_feature_map(q, kernel, omega)
+    ctx, (kv, ksum) = kernels.linear_attention(
+        qp, kp, v_new, causal=True, state=None if prev is None else (prev[0], prev[1]),
+        state_scale=scale, return_state=True, out_dtype=q.dtype)
+    cache.linear[idx] = (kv, ksum, stab)
     return attention.project(ctx.flatten(-2), layer, "o").float()
 
 

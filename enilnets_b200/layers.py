@@ -100,6 +100,44 @@ def _set_width(self: Any, width: int) -> None:
 
 
 # ----------------------------------------------------------- attention
+ATTENTION_KERNELS = ("softmax", "linear", "performer")  # nn/attention_kernels.py:20
+
+
+def make_projection(num_features: int, head_dim: int) -> np.ndarray:
+    """Performer random features (nn/attention_kernels.py:23-35): orthogonal
+    rows in blocks of head_dim (the transpose of a QR factor of a Gaussian
+    square), scaled to the norms of Gaussian rows. Draws from the global RNG
+    in the reference's order: one head_dim x head_dim Gaussian per block, then
+    one (num_features, head_dim) Gaussian for the norms."""
+    n_blocks = -(-num_features // head_dim)
+    rows = np.concatenate([np.linalg.qr(np.random.randn(head_dim, head_dim))[0].T
+                           for _ in range(n_blocks)], axis=0)[:num_features]
+    scale = np.linalg.norm(np.random.randn(num_features, head_dim), axis=1)
+    return (rows * scale[:, None]).astype(default_dtype())
+
+
+def _validate_attention_kernel(kernel: str, positional_scheme: str, window_size,
+                               dropout: float, head_dim: int, num_features) -> Optional[np.ndarray]:
+    """nn/layers.py:223-253: a linearized kernel builds no score matrix, so
+    ALiBi, a window and attention dropout are rejected; every linearized
+    kernel draws a projection (only the Performer uses it) before the layer's
+    weights, which keeps the RNG stream in the reference's order."""
+    if kernel not in ATTENTION_KERNELS:
+        raise ValueError(f"Unknown attention_kernel {kernel!r}. Expected one of {ATTENTION_KERNELS}.")
+    if kernel == "softmax":
+        return None
+    for name, bad, why in (
+            ("positional_scheme='alibi'", positional_scheme == "alibi",
+             "ALiBi is an additive bias on the score matrix"),
+            ("window_size", window_size is not None, "a sliding window is a mask on the score matrix"),
+            ("dropout", dropout > 0, "attention dropout is a mask on the softmax weights")):
+        if bad:
+            raise ValueError(
+                f"attention_kernel={kernel!r} is incompatible with {name}: {why}, and linearized "
+                "attention never materializes one. Use attention_kernel='softmax' if you need it.")
+    return make_projection(num_features or head_dim * 4, head_dim)
+
+
 def add_multihead_attention(self: Any, embed_dim: Optional[int] = None, num_heads: int = 4,
                             dropout: float = 0.0, init_method: str = "xavier_uniform",
                             causal: bool = False, positional_scheme: str = "absolute",
@@ -109,11 +147,12 @@ def add_multihead_attention(self: Any, embed_dim: Optional[int] = None, num_head
                             num_features: Optional[int] = None,
                             sparse_pattern: Optional[Dict[str, int]] = None,
                             tiled_block_size: Optional[int] = None) -> None:
-    """Multi-head self-attention, nn/layers.py:256-354. The B200 path runs
-    softmax attention only: the linearized kernels and block-sparse patterns
-    (nn/attention_kernels.py, nn/sparse_attention.py) raise ValueError here
-    rather than silently falling back. tiled_block_size is accepted (the
-    kernel always streams) and validated as the reference does."""
+    """Multi-head self-attention, nn/layers.py:256-354. attention_kernel
+    "softmax" runs the fused softmax kernels; "linear" (elu + 1) and
+    "performer" (FAVOR+) run the linearized-attention kernels. Block-sparse
+    patterns (nn/sparse_attention.py) raise ValueError here rather than
+    silently falling back. tiled_block_size is accepted (the softmax kernel
+    always streams) and validated as the reference does."""
     if embed_dim is None:
         embed_dim = _require_width(self, "add_multihead_attention")
     if embed_dim % num_heads != 0:
@@ -123,15 +162,22 @@ def add_multihead_attention(self: Any, embed_dim: Optional[int] = None, num_head
     kv_dim = num_kv_heads * head_dim
     if window_size is not None and window_size < 0:
         raise ValueError(f"window_size must be >= 0 or None, got {window_size}")
-    if attention_kernel != "softmax":
-        raise ValueError(
-            f"attention_kernel={attention_kernel!r} is not supported by the B200 attention "
-            "path, which implements softmax attention only.")
+    omega = _validate_attention_kernel(attention_kernel, positional_scheme, window_size,
+                                       dropout, head_dim, num_features)
     if sparse_pattern is not None:
+        if attention_kernel != "softmax":
+            raise ValueError(
+                f"sparse_pattern is incompatible with attention_kernel={attention_kernel!r}: a "
+                "linearized kernel never builds a score matrix, so there is nothing to sparsify.")
         raise ValueError("sparse_pattern is not supported by the B200 attention path.")
     if tiled_block_size is not None:
         if int(tiled_block_size) < 1:
             raise ValueError(f"tiled_block_size must be >= 1 or None, got {tiled_block_size}")
+        if attention_kernel != "softmax":
+            raise ValueError(
+                "tiled_block_size only applies to the plain softmax path; the linearized kernels "
+                "and sparse_pattern already avoid building a score matrix, so there is nothing "
+                "to tile.")
         if dropout > 0:
             raise ValueError(
                 "tiled_block_size is incompatible with attention dropout: the streaming path "
@@ -155,6 +201,8 @@ def add_multihead_attention(self: Any, embed_dim: Optional[int] = None, num_head
         "positional_scheme": positional_scheme,
         "Wq": Wq, "bq": bq, "Wk": Wk, "bk": bk, "Wv": Wv, "bv": bv, "Wo": Wo, "bo": bo,
     })
+    if omega is not None:
+        self.layers[-1]["omega"] = omega
     _set_width(self, embed_dim)
 
 

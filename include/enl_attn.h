@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define ENL_ABI_VERSION 2
+#define ENL_ABI_VERSION 3
 
 /* Status codes. The Python binding maps INVALID/UNSUPPORTED to ValueError
  * (the reference raises ValueError for bad layer configurations,
@@ -176,6 +176,63 @@ int enl_rope_apply(void* x, int64_t stride_b, int64_t stride_s, int64_t stride_h
                    int32_t seq, int32_t num_heads, int32_t head_dim, int32_t dtype,
                    const float* cos_table, const float* sin_table, int64_t table_row0,
                    int64_t table_rows, void* stream);
+
+/* ---------------------------------------------------- linearized attention */
+/* The reference's attention_kernel = "linear" (phi = elu + 1) and "performer"
+ * (FAVOR+) options: nn/attention_kernels.py:58-143, nn/forward.py:456-478 and
+ * the cached step of nn/kvcache.py:217-260. Arithmetic is fp32. */
+enum { ENL_PHI_LINEAR = 0, ENL_PHI_PERFORMER = 1 };
+
+typedef struct enl_phi_args {
+  const void* x; /* x[b, s, h, :], bf16 or fp32, strides in elements */
+  int64_t x_stride_b, x_stride_s, x_stride_h;
+  int32_t batch, seq, num_heads, head_dim;
+  int32_t in_dtype;        /* ENL_DTYPE_BF16 or ENL_DTYPE_FP32 */
+  int32_t kernel;          /* ENL_PHI_LINEAR or ENL_PHI_PERFORMER */
+  const float* omega;      /* performer: (num_features, head_dim) fp32, row-major */
+  int32_t num_features;    /* performer: rows of omega, 1..1024 */
+  int32_t global_stab;     /* performer: 1 = one stabilizer per (b, h) (keys),
+                              0 = one per row (queries) */
+  const float* stab_floor; /* global: optional lower bound per (b, h) */
+  float* stab;             /* global: receives the stabilizer per (b, h) */
+  float* phi;              /* out (batch, num_heads, seq, Df) fp32, contiguous;
+                              Df = head_dim (linear) or num_features */
+} enl_phi_args;
+
+/* phi(x) (nn/attention_kernels.py:58-74): elu(x) + 1, or
+ * exp(w.x' - |x'|^2 / 2 - stab) / sqrt(num_features) with x' = x / head_dim^(1/4)
+ * and stab the row max of w.x' (queries) or its max over every row of the
+ * call and stab_floor (keys, nn/attention_kernels.py:38-55). */
+int enl_linear_feature_map(const enl_phi_args* args, void* stream);
+
+typedef struct enl_linear_args {
+  const float* phi_q; /* (batch, num_heads, seq, num_features) fp32 */
+  const float* phi_k; /* (batch, num_kv_heads, seq, num_features) fp32 */
+  const void* v;      /* v[b, s, kv_head, :], strides in elements */
+  int64_t v_stride_b, v_stride_s, v_stride_h;
+  int32_t v_dtype;
+  void* o; /* o[b, s, h, :] */
+  int64_t o_stride_b, o_stride_s, o_stride_h;
+  int32_t out_dtype;
+  int32_t batch, num_heads, num_kv_heads, seq, num_features, head_dim;
+  int32_t causal;
+  /* Causal only, each nullable: a carried state added to every prefix,
+   * kv (batch, num_kv_heads, num_features, head_dim) and ksum (batch,
+   * num_kv_heads, num_features), both times state_scale[b * num_kv_heads +
+   * kv_head]; kv_out / ksum_out receive the sums after the last row. */
+  const float* kv_in;
+  const float* ksum_in;
+  const float* state_scale;
+  float* kv_out;
+  float* ksum_out;
+  float eps; /* denominator guard, 1e-20 in the reference */
+} enl_linear_args;
+
+/* o = phi(Q) S_kv / (phi(Q) . s_k + eps) with S_kv = sum phi(k) v^T and
+ * s_k = sum phi(k) over keys s <= t (causal, prefix sums) or all keys
+ * (nn/attention_kernels.py:119-143). num_features <= enl_linear_max_features(). */
+int enl_linear_attention(const enl_linear_args* args, void* stream);
+int enl_linear_max_features(void);
 
 /* ------------------------------------------------------------- utilities */
 /* Read (and with clear != 0 reset) the device error word of the current

@@ -440,6 +440,91 @@ def textgen_case():
     np.savez_compressed(HERE / "textgen.npz", **out)
 
 
+def linear_cases():
+    """Linearized attention kernels ("linear" elu+1 and "performer" FAVOR+),
+    run by the reference in float64 (nn/attention_kernels.py, nn/forward.py:
+    456-478, nn/kvcache.py:217-260).
+
+    core{i}: identity-weight layers, so the output is the attention context of
+        x itself; the Performer's projection matrix is stored as core{i}_omega
+        and the input regenerates from RandomState(2100 + i).
+    mha{i}: full layers with the reference's own seeded weights (set_seed
+        2200 + i, input RandomState(2300 + i)); the tests rebuild them with
+        enilnets_b200.layers, which draws the projection before the weights as
+        the reference does.
+    kv{i}: a transformer block with a linearized kernel stepped through the
+        cache (prime 4 tokens, then 5 single steps) against its full Forward,
+        and the step after expanding to 3 beams and reordering
+        (set_seed 2400 + i, tokens RandomState(2500 + i))."""
+    out = {}
+    meta = {"core": [], "mha": [], "kv": []}
+    core = [
+        dict(embed_dim=32, num_heads=2, causal=False, attention_kernel="linear"),
+        dict(embed_dim=32, num_heads=2, causal=True, attention_kernel="linear"),
+        dict(embed_dim=32, num_heads=2, causal=False, attention_kernel="performer"),
+        dict(embed_dim=32, num_heads=2, causal=True, attention_kernel="performer",
+             num_features=24),
+    ]
+    for i, cfg in enumerate(core):
+        Enilnets.core.utils.set_seed(2000 + i)
+        m = NeuralNet()
+        m.add_multihead_attention(**cfg)
+        identity_layer(m.layers[0])
+        x = np.random.RandomState(2100 + i).standard_normal((2, 21, cfg["embed_dim"]))
+        out[f"core{i}_y"] = m.Forward(x, training=False)
+        if "omega" in m.layers[0]:
+            out[f"core{i}_omega"] = np.asarray(m.layers[0]["omega"])
+        meta["core"].append(cfg)
+    mha = [
+        dict(embed_dim=64, num_heads=4, causal=True, attention_kernel="linear"),
+        dict(embed_dim=64, num_heads=4, causal=False, attention_kernel="linear", num_kv_heads=2),
+        dict(embed_dim=64, num_heads=4, causal=True, attention_kernel="performer"),
+        dict(embed_dim=64, num_heads=4, causal=False, attention_kernel="performer",
+             num_kv_heads=1, num_features=40),
+        dict(embed_dim=64, num_heads=4, causal=True, attention_kernel="linear",
+             positional_scheme="rope"),
+    ]
+    for i, cfg in enumerate(mha):
+        Enilnets.core.utils.set_seed(2200 + i)
+        m = NeuralNet()
+        m.add_multihead_attention(**cfg)
+        x = np.random.RandomState(2300 + i).standard_normal((2, 40, cfg["embed_dim"]))
+        out[f"mha{i}_y"] = m.Forward(x, training=False).astype(np.float32)
+        meta["mha"].append(cfg)
+    kv = [
+        dict(attention_kernel="linear", num_kv_heads=None, positional_scheme="absolute"),
+        dict(attention_kernel="performer", num_kv_heads=None, positional_scheme="absolute"),
+        dict(attention_kernel="performer", num_kv_heads=2, positional_scheme="rope"),
+        dict(attention_kernel="linear", num_kv_heads=2, positional_scheme="rope"),
+    ]
+    for i, cfg in enumerate(kv):
+        Enilnets.core.utils.set_seed(2400 + i)
+        m = NeuralNet()
+        m.add_embedding(vocab_size=17, embed_dim=64)
+        if cfg["positional_scheme"] == "absolute":
+            m.add_positional_encoding(max_seq_len=32, learnable=False)
+        m.add_transformer_block(64, num_heads=4, causal=True, **cfg)
+        m.add_layernorm()
+        m.add_dense(n_out=17, activation="linear")
+        toks = np.random.RandomState(2500 + i).randint(0, 17, size=(3, 9))
+        full = m.Forward(toks, training=False)
+        cache = kvc.KVCache()
+        pieces = [kvc.cached_forward_step(m, toks[:, :4], cache)]
+        pieces += [kvc.cached_forward_step(m, toks[:, j:j + 1], cache) for j in range(4, 9)]
+        out[f"kv{i}_full"] = full.astype(np.float32)
+        out[f"kv{i}_stepped"] = np.concatenate(pieces, axis=1).astype(np.float32)
+        cache2 = kvc.KVCache()
+        kvc.cached_forward_step(m, toks[:1, :4], cache2)
+        cache2.expand(3)
+        kvc.cached_forward_step(m, np.array([[5], [6], [7]]), cache2)
+        cache2.reorder([2, 2, 0])
+        out[f"kv{i}_reordered"] = kvc.cached_forward_step(
+            m, np.array([[9], [9], [9]]), cache2).astype(np.float32)
+        meta["kv"].append(cfg)
+    out["meta"] = np.array(json.dumps(meta))
+    np.savez_compressed(HERE / "linear_layers.npz", **out)
+
+
 def main():
     if len(sys.argv) > 1:
         for name in sys.argv[1:]:

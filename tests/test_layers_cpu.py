@@ -56,7 +56,17 @@ def test_layer_dict_contract():
     (dict(embed_dim=8, num_heads=2, positional_scheme="sinusoid"), "positional_scheme"),
     (dict(embed_dim=8, num_heads=2, tiled_block_size=0), "tiled_block_size"),
     (dict(embed_dim=8, num_heads=2, tiled_block_size=4, dropout=0.1), "dropout"),
-    (dict(embed_dim=8, num_heads=2, attention_kernel="linear"), "attention_kernel"),
+    (dict(embed_dim=8, num_heads=2, attention_kernel="cosine"), "Unknown attention_kernel"),
+    (dict(embed_dim=8, num_heads=2, attention_kernel="linear", positional_scheme="alibi"),
+     "incompatible with positional_scheme='alibi'"),
+    (dict(embed_dim=8, num_heads=2, attention_kernel="performer", window_size=2),
+     "incompatible with window_size"),
+    (dict(embed_dim=8, num_heads=2, attention_kernel="linear", dropout=0.1),
+     "incompatible with dropout"),
+    (dict(embed_dim=8, num_heads=2, attention_kernel="linear", sparse_pattern={"block_size": 2}),
+     "nothing to sparsify"),
+    (dict(embed_dim=8, num_heads=2, attention_kernel="linear", tiled_block_size=4),
+     "nothing to tile"),
     (dict(embed_dim=8, num_heads=2, sparse_pattern={"block_size": 2}), "sparse_pattern"),
 ])
 def test_builder_validation_matches_reference_errors(kwargs, match):
@@ -116,3 +126,23 @@ def test_transformer_block_layer_sequence():
                      "residual_add", "residual_save", "layernorm", "dense", "dense",
                      "residual_add"]
     assert m.layers[4]["save_index"] == 1 and m.layers[9]["save_index"] == 5
+
+
+def test_linearized_layers_draw_the_projection_before_the_weights():
+    """nn/layers.py:294: every linearized kernel draws its random-feature
+    matrix (head_dim * 4 rows unless num_features) before Wq..Wo, so the same
+    seed gives the reference's weights; only the Performer uses it."""
+    from oracle import linear_ref
+    for kernel, nf in (("linear", None), ("performer", 24)):
+        enl.set_seed(5)
+        m = enl.AttentionNet()
+        m.add_multihead_attention(embed_dim=32, num_heads=2, attention_kernel=kernel,
+                                  num_features=nf)
+        np.random.seed(5)
+        omega = linear_ref.make_projection(nf or 16 * 4, 16)
+        assert np.allclose(m.layers[0]["omega"], omega, atol=1e-6)
+        enl.set_seed(5)
+        ref = enl.AttentionNet()
+        ref.add_multihead_attention(embed_dim=32, num_heads=2)
+        # the softmax layer's Wq comes first in the stream, the linearized one after omega
+        assert not np.array_equal(m.layers[0]["Wq"], ref.layers[0]["Wq"])

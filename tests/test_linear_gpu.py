@@ -1,0 +1,190 @@
+"""Linearized attention kernels (K4, enl_linear.cu) on the GPU.
+
+Kernel level: the feature map and the linear-attention kernel against the
+float64 oracle (oracle/linear_ref.py) on the same inputs, including ragged
+chunk and column counts, GQA and a carried decode state. Layer level: models
+rebuilt from the reference's seeds against the reference's own outputs
+(tests/golden/linear_layers.npz), full forward and cached stepping.
+
+Arithmetic is fp32: max abs error <= 1e-3 (the north-star bar for fp32
+inputs); the kernel-level cases on fp32 inputs hold to 1e-4."""
+import json
+
+import numpy as np
+import pytest
+
+import enilnets_b200 as enl
+from oracle import linear_ref as lr
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+
+
+def _t(a, dtype=None):
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).cuda()
+    return t if dtype is None else t.to(dtype)
+
+
+def _np(t):
+    return t.float().cpu().numpy().astype(np.float64)
+
+
+@pytest.mark.parametrize("kernel", ["linear", "performer"])
+@pytest.mark.parametrize("Dh,Df", [(8, 24), (32, 128), (64, 256), (128, 512)])
+def test_feature_map_matches_oracle(cuda, kernel, Dh, Df):
+    from enilnets_b200 import _native, kernels
+    rng = np.random.RandomState(Dh + Df)
+    B, S, H = 2, 37, 3
+    x = rng.standard_normal((B, S, H, Dh))
+    omega = lr.make_projection(Df, Dh, np.random.RandomState(Dh))
+    xt = _t(x)
+    om = _t(omega) if kernel == "performer" else None
+    phi, _ = kernels.linear_feature_map(xt, kernel, om)
+    ref = lr.feature_map(x.transpose(0, 2, 1, 3), kernel, omega, "row")
+    assert np.max(np.abs(_np(phi) - ref)) <= 1e-4 * max(1.0, np.abs(ref).max())
+    if kernel == "performer":
+        phk, stab = kernels.linear_feature_map(xt, kernel, om, global_stab=True)
+        st = lr.performer_stab(x.transpose(0, 2, 1, 3), omega, "global")
+        assert np.max(np.abs(_np(stab) - st[..., 0, 0])) <= 1e-4 * max(1.0, np.abs(st).max())
+        refk = lr.feature_map(x.transpose(0, 2, 1, 3), kernel, omega, "global")
+        assert np.max(np.abs(_np(phk) - refk)) <= 1e-4 * max(1.0, np.abs(refk).max())
+        # a floor above the data's own maximum wins
+        floor = st[..., 0, 0] + 3.0
+        _, stab2 = kernels.linear_feature_map(xt, kernel, om, global_stab=True,
+                                              stab_floor=_t(floor))
+        assert np.allclose(_np(stab2), floor, atol=1e-5)
+    torch_sync()
+    _native.raise_on_device_error()
+
+
+def torch_sync():
+    import torch
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("S,D,Df,H,Hkv", [
+    (1, 8, 8, 2, 2), (5, 40, 40, 4, 2), (16, 32, 32, 2, 1), (37, 64, 256, 4, 4),
+    (300, 128, 128, 2, 2), (129, 72, 512, 4, 1)])
+def test_linear_attention_matches_oracle(cuda, causal, S, D, Df, H, Hkv):
+    from enilnets_b200 import _native, kernels
+    rng = np.random.RandomState(S + D + Df)
+    B = 2
+    qp = np.exp(rng.standard_normal((B, H, S, Df)) * 0.5)   # positive features
+    kp = np.exp(rng.standard_normal((B, Hkv, S, Df)) * 0.5)
+    v = rng.standard_normal((B, S, Hkv, D))
+    out = kernels.linear_attention(_t(qp), _t(kp), _t(v), causal=causal)
+    G = H // Hkv
+    kph = np.repeat(kp, G, axis=1)
+    vh = np.repeat(v.transpose(0, 2, 1, 3), G, axis=1)
+    ref, _, _ = lr.linear_attention(qp, kph, vh, causal)
+    torch_sync()
+    _native.raise_on_device_error()
+    assert np.max(np.abs(_np(out).transpose(0, 2, 1, 3) - ref)) <= 1e-4
+
+
+def test_linear_attention_bf16_values_and_output(cuda):
+    import torch
+    from enilnets_b200 import kernels
+    rng = np.random.RandomState(9)
+    B, S, H, D, Df = 2, 50, 2, 64, 64
+    qp = np.exp(rng.standard_normal((B, H, S, Df)) * 0.5)
+    kp = np.exp(rng.standard_normal((B, H, S, Df)) * 0.5)
+    v = rng.standard_normal((B, S, H, D))
+    vb = _t(v, torch.bfloat16)
+    out = kernels.linear_attention(_t(qp), _t(kp), vb, causal=True, out_dtype=torch.bfloat16)
+    ref, _, _ = lr.linear_attention(qp, kp, _np(vb).transpose(0, 2, 1, 3), True)
+    assert np.max(np.abs(_np(out).transpose(0, 2, 1, 3) - ref)) <= 2e-2
+
+
+def test_carried_state_equals_one_pass(cuda):
+    """Prefix sums split across calls (state out -> scaled state in) equal one
+    causal pass: the decode step's state algebra."""
+    from enilnets_b200 import kernels
+    rng = np.random.RandomState(4)
+    B, H, Hkv, S, D, Df = 2, 4, 2, 23, 48, 96
+    qp = np.exp(rng.standard_normal((B, H, S, Df)) * 0.5)
+    kp = np.exp(rng.standard_normal((B, Hkv, S, Df)) * 0.5)
+    v = rng.standard_normal((B, S, Hkv, D))
+    full = _np(kernels.linear_attention(_t(qp), _t(kp), _t(v), causal=True))
+    cut = 9
+    o1, st = kernels.linear_attention(_t(qp[:, :, :cut]), _t(kp[:, :, :cut]), _t(v[:, :cut]),
+                                      causal=True, return_state=True)
+    # a common scale on the carried sums and the new keys cancels in the ratio
+    scale = np.full((B, Hkv), 0.25)
+    o2, _ = kernels.linear_attention(_t(qp[:, :, cut:]), _t(kp[:, :, cut:] * 0.25),
+                                     _t(v[:, cut:]), causal=True, state=st,
+                                     state_scale=_t(scale), return_state=True)
+    stepped = np.concatenate([_np(o1), _np(o2)], axis=1)
+    assert np.max(np.abs(stepped - full)) <= 1e-4
+    kv_ref = np.einsum("bhsf,bshd->bhfd", kp, v)
+    assert np.max(np.abs(_np(st[0]) - np.einsum("bhsf,bshd->bhfd", kp[:, :, :cut],
+                                                 v[:, :cut]))) <= 1e-3
+    assert kv_ref.shape == tuple(st[0].shape)
+
+
+@pytest.fixture
+def float64():
+    enl.use_float64(True)
+    yield
+    enl.use_float64(False)
+
+
+def _golden(golden_dir):
+    data = np.load(golden_dir / "linear_layers.npz")
+    return data, json.loads(str(data["meta"]))
+
+
+def test_linear_layers_match_reference(cuda, golden_dir, float64):
+    data, meta = _golden(golden_dir)
+    for i, cfg in enumerate(meta["mha"]):
+        enl.set_seed(2200 + i)
+        m = enl.AttentionNet()
+        m.add_multihead_attention(**cfg)
+        x = np.random.RandomState(2300 + i).standard_normal((2, 40, cfg["embed_dim"]))
+        err = float(np.max(np.abs(m.Forward(x, training=False) - data[f"mha{i}_y"])))
+        assert err <= TOL, (cfg, err)
+
+
+def _kv_model(i, cfg):
+    enl.set_seed(2400 + i)
+    m = enl.AttentionNet()
+    m.add_embedding(vocab_size=17, embed_dim=64)
+    if cfg["positional_scheme"] == "absolute":
+        m.add_positional_encoding(max_seq_len=32, learnable=False)
+    m.add_transformer_block(64, num_heads=4, causal=True, **cfg)
+    m.add_layernorm()
+    m.add_dense(n_out=17, activation="linear")
+    return m, np.random.RandomState(2500 + i).randint(0, 17, size=(3, 9))
+
+
+def test_linear_kv_stepping_matches_reference(cuda, golden_dir, float64):
+    """Prime 4 tokens, then 5 single steps (nn/kvcache.py:217-260): equal to the
+    reference's stepped outputs and its full Forward; the state lives in
+    cache.linear, no K/V cache grows."""
+    data, meta = _golden(golden_dir)
+    for i, cfg in enumerate(meta["kv"]):
+        m, toks = _kv_model(i, cfg)
+        full = m.Forward(toks, training=False)
+        assert np.max(np.abs(full - data[f"kv{i}_full"])) <= TOL, cfg
+        cache = enl.KVCache()
+        pieces = [enl.cached_forward_step(m, toks[:, :4], cache)]
+        pieces += [enl.cached_forward_step(m, toks[:, j:j + 1], cache) for j in range(4, 9)]
+        stepped = np.concatenate(pieces, axis=1)
+        assert np.max(np.abs(stepped - data[f"kv{i}_stepped"])) <= TOL, cfg
+        assert len(cache.kv) == 0 and len(cache.linear) == 1
+
+
+def test_linear_kv_reorder_matches_reference(cuda, golden_dir, float64):
+    data, meta = _golden(golden_dir)
+    for i, cfg in enumerate(meta["kv"]):
+        m, toks = _kv_model(i, cfg)
+        cache = enl.KVCache()
+        enl.cached_forward_step(m, toks[:1, :4], cache)
+        cache.expand(3)
+        enl.cached_forward_step(m, np.array([[5], [6], [7]]), cache)
+        cache.reorder([2, 2, 0])
+        out = enl.cached_forward_step(m, np.array([[9], [9], [9]]), cache)
+        assert np.max(np.abs(out - data[f"kv{i}_reordered"])) <= TOL, cfg
+        assert np.allclose(out[0], out[1], atol=1e-6)
