@@ -21,6 +21,9 @@ Also measured in the same run (sub-objects of the line):
                   bf16 precision (fused QKV GEMM, K1, output GEMM).
   layer_cfg1   -- config 1 (B4 S256 E256 H8, causal, float32) through the
                   NumPy-facing Forward on the fp32 split-bf16 path.
+  linear_attention -- the attention_kernel="linear" and "performer" options
+                  (feature maps + causal linear attention, K4), B4 S4096 H16
+                  D64 per GPU, fp32 on the CUDA cores.
 
 Run: python bench.py [--gpus N --steps K --warmup W] [--impl reference]
 Multi-GPU: torchrun --nproc-per-node N bench.py --gpus N ...
@@ -441,6 +444,50 @@ def bench_cross_cfg4(dist: Dist, clocks: ClockSampler, warmup: int, steps: int =
                       f"L~U[{CFG4['lo']},{CFG4['hi']}], bf16"}
 
 
+FP32_CORE_TFLOPS = 148 * 128 * 2 * 1.965e-3  # nominal fp32 FMA TFLOP/s of the CUDA cores
+
+
+def bench_linear(dist: Dist, clocks: ClockSampler, warmup: int, steps: int = 10):
+    """Linearized attention (attention_kernel "linear" and "performer"):
+    feature maps plus causal linear attention on device fp32 head views, per
+    GPU B4 S4096 H16 D64 (Performer with 256 features). FLOPs count the
+    reference's reassociated form, 4 S Df D per query head, plus the
+    Performer projections (2 S Dh Df for queries, twice that for keys: the
+    stabilizer pass and the map)."""
+    import torch
+    from enilnets_b200 import kernels, _native
+    B, S, H, D, Df = 4, 4096, 16, 64, 256
+    g = torch.Generator(device=dist.device).manual_seed(6000 + dist.rank)
+    qkv = torch.randn((B, S, 3 * H * D), generator=g, device=dist.device) * 0.5
+    q, k, v = (qkv[..., i * H * D:(i + 1) * H * D].unflatten(-1, (H, D)) for i in range(3))
+    omega = torch.randn((Df, D), generator=g, device=dist.device)
+    res = {}
+    for kernel in ("linear", "performer"):
+        om = omega if kernel == "performer" else None
+        nf = Df if kernel == "performer" else D
+
+        def step():
+            qp, _ = kernels.linear_feature_map(q, kernel, om)
+            kp, _ = kernels.linear_feature_map(k, kernel, om, global_stab=True)
+            kernels.linear_attention(qp, kp, v, causal=True)
+
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        _native.raise_on_device_error()
+        ms = timed(dist, clocks, step, steps) / steps
+        flops = 4.0 * S * nf * D * B * H
+        if kernel == "performer":
+            flops += 3 * 2.0 * S * D * Df * B * H
+        tf = dist.sum(flops) / (ms * 1e-3) / 1e12
+        res[kernel] = {"ms_per_step": ms, "TFLOP_s": tf,
+                       "frac_of_fp32_core_peak_per_gpu": tf / dist.world / FP32_CORE_TFLOPS,
+                       "tokens_s": dist.sum(B * S) / (ms * 1e-3)}
+    res["config"] = (f"B{B}/GPU S{S} H{H} D{D} causal, fp32 arithmetic on CUDA cores; performer "
+                     f"with {Df} features; peak = nominal {FP32_CORE_TFLOPS:.1f} TFLOP/s fp32")
+    return res
+
+
 def bench_layer_cfg2(dist: Dist, clocks: ClockSampler, warmup: int, steps: int = 10):
     """graph.MultiHeadAttention(2048, 16, causal) forward with key padding on
     device-resident x, bf16 precision: QKV GEMM + K1 + output GEMM."""
@@ -580,7 +627,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--skip-sub", action="store_true", help="headline only")
-    ap.add_argument("--only", choices=["all", "prefill", "decode", "longctx", "cross", "layer"],
+    ap.add_argument("--only", choices=["all", "prefill", "decode", "longctx", "cross", "layer",
+                                       "linear"],
                     default="all",
                     help="profiling: run one workload")
     ap.add_argument("--batch", type=int, default=0, help="profiling: prefill batch override")
@@ -609,6 +657,8 @@ def main():
                 res = bench_decode_cfg3(dist, clocks, args.warmup, args.decode_batch)
             elif args.only == "cross":
                 res = bench_cross_cfg4(dist, clocks, args.warmup)
+            elif args.only == "linear":
+                res = bench_linear(dist, clocks, args.warmup)
             elif args.only == "layer":
                 res = {"layer_cfg2": bench_layer_cfg2(dist, clocks, args.warmup),
                        "layer_cfg1": bench_layer_cfg1(dist, args.warmup)}
@@ -625,6 +675,7 @@ def main():
             sub["decode_cfg3"] = bench_decode_cfg3(dist, clocks, args.warmup, args.decode_batch)
             sub["longctx_cfg5"] = bench_longctx_cfg5(dist, clocks, args.warmup)
             sub["cross_cfg4"] = bench_cross_cfg4(dist, clocks, args.warmup)
+            sub["linear_attention"] = bench_linear(dist, clocks, args.warmup)
             sub["layer_cfg2"] = bench_layer_cfg2(dist, clocks, args.warmup)
             sub["layer_cfg1"] = bench_layer_cfg1(dist, args.warmup)
     finally:

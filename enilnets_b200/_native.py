@@ -99,6 +99,7 @@ class LinearArgs(Structure):
         ("kv_in", c_void_p), ("ksum_in", c_void_p), ("state_scale", c_void_p),
         ("kv_out", c_void_p), ("ksum_out", c_void_p),
         ("eps", c_float),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t),
     ]
 
 
@@ -128,6 +129,7 @@ SIGNATURES = {
     "enl_linear_feature_map": ([POINTER(PhiArgs), c_void_p], c_int32),
     "enl_linear_attention": ([POINTER(LinearArgs), c_void_p], c_int32),
     "enl_linear_max_features": ([], c_int32),
+    "enl_linear_workspace_bytes": ([POINTER(LinearArgs)], c_size_t),
     "enl_device_error": ([POINTER(c_int32), POINTER(c_int32), c_int32], c_int32),
     "enl_last_error": ([], c_char_p),
     "enl_abi_version": ([], c_int32),

@@ -489,6 +489,12 @@ int enl_rope_apply(void* x, int64_t stride_b, int64_t stride_s, int64_t stride_h
 
 int enl_linear_max_features(void) { return enl::linear_attn_max_features(); }
 
+size_t enl_linear_workspace_bytes(const enl_linear_args* a) {
+  if (!a || a->batch < 1 || a->num_heads < 1 || a->num_kv_heads < 1 || a->seq < 1) return 0;
+  return enl::linear_workspace_bytes(a->batch, a->num_heads, a->num_kv_heads, a->seq,
+                                     a->num_features, a->head_dim, a->causal);
+}
+
 int enl_linear_feature_map(const enl_phi_args* a, void* stream) {
   if (!a || !a->x || !a->phi)
     return fail(ENL_ERR_INVALID, "enl_linear_feature_map: args, x and phi must be non-NULL");
@@ -505,6 +511,9 @@ int enl_linear_feature_map(const enl_phi_args* a, void* stream) {
                   "1 <= num_features <= 1024 (got %d)", a->num_features);
     if (a->global_stab && !a->stab)
       return fail(ENL_ERR_INVALID, "enl_linear_feature_map: a global stabilizer needs stab");
+    if (a->head_dim > enl::perf_max_head_dim())
+      return fail(ENL_ERR_UNSUPPORTED, "enl_linear_feature_map: performer head_dim %d > %d",
+                  a->head_dim, enl::perf_max_head_dim());
   }
   enl::PhiParams p{};
   p.x = a->x;
@@ -575,6 +584,18 @@ int enl_linear_attention(const enl_linear_args* a, void* stream) {
   p.kv_out = a->kv_out;
   p.ks_out = a->ksum_out;
   p.eps = a->eps;
+  const size_t need = enl_linear_workspace_bytes(a);
+  if (need > 0) {
+    if (!a->workspace || a->workspace_bytes < need)
+      return fail(ENL_ERR_INVALID, "enl_linear_attention: needs a workspace of %zu bytes "
+                  "(enl_linear_workspace_bytes), got %zu", need,
+                  a->workspace ? a->workspace_bytes : (size_t)0);
+    // (n_seg, B, Hkv, Df, D) partial S_kv, then (n_seg, B, Hkv, Df) partial s_k
+    const size_t per_seg = (size_t)a->batch * a->num_kv_heads * a->num_features;
+    const size_t n_seg = need / sizeof(float) / (per_seg * ((size_t)a->head_dim + 1));
+    p.carry_kv = reinterpret_cast<float*>(a->workspace);
+    p.carry_ks = p.carry_kv + n_seg * per_seg * a->head_dim;
+  }
   cudaError_t e = enl::launch_linear_attn(p, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "enl_linear_attention launch");
   return ENL_OK;

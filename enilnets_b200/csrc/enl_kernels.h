@@ -116,6 +116,7 @@ struct PhiParams {
   float* phi;
 };
 cudaError_t launch_phi(const PhiParams& p, cudaStream_t stream);
+int perf_max_head_dim();  // Performer feature maps take head_dim up to this
 
 // Linear attention over phi(Q) (B, H, S, Df) and phi(K) (B, Hkv, S, Df) with
 // V[b, s, hkv, :] (strided); o[b, s, h, :]. Causal runs prefix sums starting
@@ -138,8 +139,12 @@ struct LinearParams {
   float* kv_out;
   float* ks_out;
   float eps;
+  float* carry_kv;  // workspace: per-segment prefixes (n_seg, B, Hkv, Df, D)
+  float* carry_ks;  // (n_seg, B, Hkv, Df)
+  int n_seg, seg_len;  // set by launch_linear_attn
 };
 cudaError_t launch_linear_attn(const LinearParams& p, cudaStream_t stream);
+size_t linear_workspace_bytes(int B, int H, int Hkv, int S, int Df, int D, int causal);
 int linear_attn_max_features();
 
 }  // namespace enl

@@ -4,11 +4,13 @@
 //
 // Both kernels replace softmax(q.k) by phi(q).phi(k), so attention
 // reassociates into phi(Q) (phi(K)^T V) / (phi(Q) . sum phi(K)) and never
-// forms a score matrix. Two kernels, fp32 arithmetic throughout:
-//   phi_kernel          feature map of one head view into (B, H, S, Df) fp32:
-//                       elu(x) + 1, or exp(w.x' - |x'|^2/2 - stab)/sqrt(Df)
-//                       with x' = x / Dh^(1/4) and a row or per-(b, h) global
-//                       stabilizer (phi_max_kernel reduces the global one);
+// forms a score matrix. The kernels, fp32 arithmetic throughout:
+//   phi_linear_kernel   elu(x) + 1 of one head view into (B, H, S, Dh) fp32;
+//   phi_perf_kernel     exp(w.x' - |x'|^2/2 - stab)/sqrt(Df) with
+//                       x' = x / Dh^(1/4): the projections w.x' as a tiled
+//                       GEMM (64 rows x 64 features per step), with a row
+//                       stabilizer (queries) or one per (b, h) reduced by an
+//                       ordered-int atomic max over the rows (keys);
 //   linear_attn_kernel  per (b, query head, 32-column slice of V): causal
 //                       prefix sums over 16-row chunks (intra-chunk scores
 //                       phi(q_i).phi(k_j), j <= i, plus the carried state
@@ -16,6 +18,10 @@
 //                       two global sums when non-causal. A state can be
 //                       carried in (scaled) and returned, which is the decode
 //                       step: a fixed-size state instead of a growing cache.
+//   Long causal calls split the sequence into segments that run in
+//   parallel: linear_segsum_kernel sums each segment, linear_scan_kernel
+//   turns the sums into each segment's starting state (in the caller's
+//   workspace), and linear_attn_kernel runs one CTA per segment.
 // These options are O(S Df D) and small next to the softmax path; the
 // kernels favour simple, exact fp32 code over tensor cores.
 #include "enl_common.cuh"
@@ -35,30 +41,131 @@ __device__ __forceinline__ float load_elem(const void* base, long long idx, bool
              : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[idx]);
 }
 
-constexpr int kPhiMaxFeatPerLane = 32;  // Df <= 1024
-
-// One warp per (b, s, h) row. Performer: lane l owns features l, l + 32, ...
-__device__ __forceinline__ void performer_row(const PhiParams& p, long long xoff, float* xs,
-                                              int lane, float* proj, float& sq) {
-  const float inv = rsqrtf(sqrtf((float)p.Dh));  // Dh^(-1/4)
-  float s2 = 0.0f;
-  for (int d = lane; d < p.Dh; d += 32) {
-    const float v = load_elem(p.x, xoff + d, p.in_f32) * inv;
-    xs[d] = v;
-    s2 += v * v;
+// phi = elu(x) + 1: one warp per (b, s, h) row, elementwise.
+__global__ void __launch_bounds__(256) phi_linear_kernel(PhiParams p) {
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const long long rows = (long long)p.B * p.S * p.H;
+  for (long long r = (long long)blockIdx.x * 8 + warp; r < rows; r += (long long)gridDim.x * 8) {
+    const int h = (int)(r % p.H);
+    const long long bs = r / p.H;
+    const int s = (int)(bs % p.S), b = (int)(bs / p.S);
+    const long long xoff = b * p.sb + s * p.ss + h * p.sh;
+    float* out = p.phi + (((long long)b * p.H + h) * p.S + s) * p.Df;
+    for (int d = lane; d < p.Dh; d += 32) {
+      const float v = load_elem(p.x, xoff + d, p.in_f32);
+      out[d] = v > 0.0f ? v + 1.0f : expf(fminf(v, 0.0f));
+    }
   }
-  __syncwarp();
+}
+
+// Performer projections w.x' (x' = x / Dh^(1/4)) as a tiled fp32 GEMM: one
+// CTA per 64 rows of one (b, h), features in chunks of 64 staged in shared
+// memory with the rows; each thread accumulates a 4 x 4 tile.
+constexpr int kPtRows = 64, kPtFeat = 64, kPtThreads = 256;
+constexpr int kPerfMaxHeadDim = 256;
+
+__host__ __device__ inline int perf_smem_floats(int Dh) {
+  return (kPtRows + kPtFeat) * (Dh + 1) + 2 * kPtRows;
+}
+
+// kMode 0: global stabilizer, the max of w.x' over the tile's rows and all
+//          features, folded into stab[b*H + h] (ordered-int atomic max);
+//       1: phi with each row's own stabilizer (queries);
+//       2: phi with the global stabilizer in stab (keys).
+template <int kMode>
+__global__ void __launch_bounds__(kPtThreads) phi_perf_kernel(PhiParams p) {
+  extern __shared__ float sm[];
+  const int Dh = p.Dh, ld = Dh + 1;
+  float* xs = sm;                          // [64][Dh + 1] scaled rows
+  float* ws = xs + kPtRows * ld;           // [64][Dh + 1] feature chunk of omega
+  float* sq = ws + kPtFeat * ld;           // [64] |x'|^2 / 2
+  int* rmax = reinterpret_cast<int*>(sq + kPtRows);  // [64] row maxima, ordered ints
+  const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  const int s0 = blockIdx.x * kPtRows;
+  const int nrow = min(kPtRows, p.S - s0);
+  const int tid = threadIdx.x, ty = tid / 16, tx = tid % 16;
+  const float inv = rsqrtf(sqrtf((float)Dh));
+  for (int i = tid; i < kPtRows * Dh; i += kPtThreads) {
+    const int r = i / Dh, d = i % Dh;
+    xs[r * ld + d] = (r < nrow) ? load_elem(p.x, b * p.sb + (long long)(s0 + r) * p.ss +
+                                                   h * p.sh + d, p.in_f32) * inv
+                                : 0.0f;
+  }
+  __syncthreads();
+  if (tid < kPtRows) {
+    float a = 0.0f;
+    for (int d = 0; d < Dh; ++d) a = fmaf(xs[tid * ld + d], xs[tid * ld + d], a);
+    sq[tid] = 0.5f * a;
+    rmax[tid] = ord_enc(-INFINITY);
+  }
+  float acc[4][4];
+  auto chunk = [&](int f0) {
+    __syncthreads();  // the previous chunk's readers are done with ws
+    for (int i = tid; i < kPtFeat * Dh; i += kPtThreads) {
+      const int f = i / Dh, d = i % Dh;
+      ws[f * ld + d] = (f0 + f < p.Df) ? p.omega[(long long)(f0 + f) * Dh + d] : 0.0f;
+    }
+    __syncthreads();
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
-  sq = 0.5f * s2;
-#pragma unroll 1
-  for (int k = 0; k < kPhiMaxFeatPerLane; ++k) {
-    const int f = lane + 32 * k;
-    if (f >= p.Df) break;
-    const float* w = p.omega + (long long)f * p.Dh;
-    float acc = 0.0f;
-    for (int d = 0; d < p.Dh; ++d) acc = fmaf(xs[d], __ldg(w + d), acc);
-    proj[k] = acc;
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+    for (int d = 0; d < Dh; ++d) {
+      float xv[4], wv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) xv[i] = xs[(ty * 4 + i) * ld + d];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) wv[j] = ws[(tx * 4 + j) * ld + d];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xv[i], wv[j], acc[i][j]);
+    }
+  };
+  auto valid = [&](int f0, int i, int j) { return ty * 4 + i < nrow && f0 + tx * 4 + j < p.Df; };
+  if (kMode == 0) {
+    float m = -INFINITY;
+    for (int f0 = 0; f0 < p.Df; f0 += kPtFeat) {
+      chunk(f0);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (valid(f0, i, j) && acc[i][j] == acc[i][j]) m = fmaxf(m, acc[i][j]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((tid & 31) == 0 && m > -INFINITY)
+      atomicMax(reinterpret_cast<int*>(p.stab) + bh, ord_enc(m));
+    return;
+  }
+  if (kMode == 1) {  // row maxima first
+    for (int f0 = 0; f0 < p.Df; f0 += kPtFeat) {
+      chunk(f0);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float m = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (valid(f0, i, j) && acc[i][j] == acc[i][j]) m = fmaxf(m, acc[i][j]);
+        if (m > -INFINITY) atomicMax(rmax + ty * 4 + i, ord_enc(m));
+      }
+    }
+  }
+  const float gstab = (kMode == 2) ? ord_dec(reinterpret_cast<const int*>(p.stab)[bh]) : 0.0f;
+  const float norm = rsqrtf((float)p.Df);
+  float* out = p.phi + ((long long)bh * p.S + s0) * p.Df;
+  for (int f0 = 0; f0 < p.Df; f0 += kPtFeat) {
+    chunk(f0);  // its leading barrier also orders the row maxima above
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = ty * 4 + i;
+      const float st = (kMode == 2) ? gstab : ord_dec(rmax[r]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (valid(f0, i, j))
+          out[(long long)r * p.Df + f0 + tx * 4 + j] = expf(acc[i][j] - sq[r] - st) * norm;
+    }
   }
 }
 
@@ -66,66 +173,6 @@ __global__ void phi_init_kernel(PhiParams p) {
   const int n = p.B * p.H;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
     reinterpret_cast<int*>(p.stab)[i] = ord_enc(p.stab_floor ? p.stab_floor[i] : -INFINITY);
-}
-
-// Global stabilizer: max over rows and features of w.x' per (b, h).
-__global__ void __launch_bounds__(256) phi_max_kernel(PhiParams p) {
-  extern __shared__ float xs_all[];
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  float* xs = xs_all + warp * p.Dh;
-  const long long rows = (long long)p.B * p.S * p.H;
-  for (long long r = (long long)blockIdx.x * 8 + warp; r < rows; r += (long long)gridDim.x * 8) {
-    const int h = (int)(r % p.H);
-    const long long bs = r / p.H;
-    const int s = (int)(bs % p.S), b = (int)(bs / p.S);
-    float proj[kPhiMaxFeatPerLane];
-    float sq;
-    performer_row(p, b * p.sb + s * p.ss + h * p.sh, xs, lane, proj, sq);
-    float m = -INFINITY;
-    for (int k = 0; k < kPhiMaxFeatPerLane && lane + 32 * k < p.Df; ++k)
-      if (proj[k] == proj[k]) m = fmaxf(m, proj[k]);  // NaN rows do not vote
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0 && m > -INFINITY) atomicMax(reinterpret_cast<int*>(p.stab) + b * p.H + h, ord_enc(m));
-    __syncwarp();
-  }
-}
-
-__global__ void __launch_bounds__(256) phi_kernel(PhiParams p) {
-  extern __shared__ float xs_all[];
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  float* xs = xs_all + warp * p.Dh;
-  const long long rows = (long long)p.B * p.S * p.H;
-  const float norm = rsqrtf((float)p.Df);
-  for (long long r = (long long)blockIdx.x * 8 + warp; r < rows; r += (long long)gridDim.x * 8) {
-    const int h = (int)(r % p.H);
-    const long long bs = r / p.H;
-    const int s = (int)(bs % p.S), b = (int)(bs / p.S);
-    const long long xoff = b * p.sb + s * p.ss + h * p.sh;
-    float* out = p.phi + (((long long)b * p.H + h) * p.S + s) * p.Df;
-    if (p.kernel == 0) {
-      for (int d = lane; d < p.Dh; d += 32) {
-        const float v = load_elem(p.x, xoff + d, p.in_f32);
-        out[d] = v > 0.0f ? v + 1.0f : expf(fminf(v, 0.0f));  // elu(v) + 1
-      }
-      continue;
-    }
-    float proj[kPhiMaxFeatPerLane];
-    float sq;
-    performer_row(p, xoff, xs, lane, proj, sq);
-    float stab;
-    if (p.global_stab) {
-      stab = ord_dec(reinterpret_cast<const int*>(p.stab)[b * p.H + h]);
-    } else {
-      stab = -INFINITY;
-      for (int k = 0; k < kPhiMaxFeatPerLane && lane + 32 * k < p.Df; ++k) stab = fmaxf(stab, proj[k]);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) stab = fmaxf(stab, __shfl_xor_sync(0xffffffffu, stab, o));
-    }
-    for (int k = 0; k < kPhiMaxFeatPerLane && lane + 32 * k < p.Df; ++k)
-      out[lane + 32 * k] = expf(proj[k] - sq - stab) * norm;
-    __syncwarp();
-  }
 }
 
 __global__ void phi_decode_kernel(PhiParams p) {
@@ -136,17 +183,41 @@ __global__ void phi_decode_kernel(PhiParams p) {
   }
 }
 
+int perf_max_head_dim() { return kPerfMaxHeadDim; }
+
 cudaError_t launch_phi(const PhiParams& p, cudaStream_t stream) {
   const long long rows = (long long)p.B * p.S * p.H;
-  const int smem = 8 * p.Dh * (int)sizeof(float);
-  const int blocks = (int)min((rows + 7) / 8, 148ll * 16);
-  if (p.kernel == 1 && p.global_stab) {
-    phi_init_kernel<<<max(1, (p.B * p.H + 255) / 256), 256, 0, stream>>>(p);
-    if (rows > 0) phi_max_kernel<<<blocks, 256, smem, stream>>>(p);
+  if (p.kernel == 0) {
+    if (rows > 0)
+      phi_linear_kernel<<<(int)min((rows + 7) / 8, 148ll * 16), 256, 0, stream>>>(p);
+    return cudaGetLastError();
   }
-  if (rows > 0) phi_kernel<<<blocks, 256, smem, stream>>>(p);
-  if (p.kernel == 1 && p.global_stab)
+  const int smem = perf_smem_floats(p.Dh) * (int)sizeof(float);
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    const int most = perf_smem_floats(kPerfMaxHeadDim) * (int)sizeof(float);
+    e = cudaFuncSetAttribute(phi_perf_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(phi_perf_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(phi_perf_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  const dim3 grid((p.S + kPtRows - 1) / kPtRows, p.B * p.H);
+  if (p.global_stab) {
+    phi_init_kernel<<<max(1, (p.B * p.H + 255) / 256), 256, 0, stream>>>(p);
+    if (rows > 0) {
+      phi_perf_kernel<0><<<grid, kPtThreads, smem, stream>>>(p);
+      phi_perf_kernel<2><<<grid, kPtThreads, smem, stream>>>(p);
+    }
     phi_decode_kernel<<<max(1, (p.B * p.H + 255) / 256), 256, 0, stream>>>(p);
+  } else if (rows > 0) {
+    phi_perf_kernel<1><<<grid, kPtThreads, smem, stream>>>(p);
+  }
   return cudaGetLastError();
 }
 
@@ -179,16 +250,24 @@ __global__ void __launch_bounds__(kLinThreads) linear_attn_kernel(LinearParams p
   const int d0 = blockIdx.y * kLinCols;
   const int ncol = min(kLinCols, p.D - d0);
   const long long bk = (long long)b * p.Hkv + hkv;
+  // Causal with segments: this CTA covers rows [r0, r1) of one segment and
+  // starts from the segment's exclusive prefix in the workspace.
+  const int seg = blockIdx.z;
+  const int r0 = p.causal ? seg * p.seg_len : 0;
+  const int r1 = p.causal ? min(p.S, r0 + p.seg_len) : p.S;
   const float* phq = p.phi_q + ((long long)b * p.H + h) * p.S * Df;
   const float* phk = p.phi_k + bk * p.S * Df;
-  const float scale = p.state_scale ? p.state_scale[bk] : 1.0f;
+  const bool from_carry = p.causal && p.n_seg > 1;
+  const float* kv_src = from_carry ? p.carry_kv + (long long)seg * p.B * p.Hkv * Df * p.D : p.kv_in;
+  const float* ks_src = from_carry ? p.carry_ks + (long long)seg * p.B * p.Hkv * Df : p.ks_in;
+  const float scale = (!from_carry && p.state_scale) ? p.state_scale[bk] : 1.0f;
 
   // carried state (or zero)
   for (int i = tid; i < Df * kLinCols; i += kLinThreads) {
     const int f = i / kLinCols, c = i % kLinCols;
-    kv[i] = (p.kv_in && c < ncol) ? p.kv_in[(bk * Df + f) * p.D + d0 + c] * scale : 0.0f;
+    kv[i] = (kv_src && c < ncol) ? kv_src[(bk * Df + f) * p.D + d0 + c] * scale : 0.0f;
   }
-  for (int f = tid; f < Df; f += kLinThreads) ks[f] = p.ks_in ? p.ks_in[bk * Df + f] * scale : 0.0f;
+  for (int f = tid; f < Df; f += kLinThreads) ks[f] = ks_src ? ks_src[bk * Df + f] * scale : 0.0f;
   __syncthreads();
 
   auto load_rows = [&](const float* src, float* dst, int s0, int nrow) {
@@ -251,8 +330,8 @@ __global__ void __launch_bounds__(kLinThreads) linear_attn_kernel(LinearParams p
   };
 
   if (p.causal) {
-    for (int s0 = 0; s0 < p.S; s0 += kLinChunk) {
-      const int nrow = min(kLinChunk, p.S - s0);
+    for (int s0 = r0; s0 < r1; s0 += kLinChunk) {
+      const int nrow = min(kLinChunk, r1 - s0);
       load_rows(phq + (long long)s0 * Df, qc, 0, nrow);
       load_rows(phk + (long long)s0 * Df, kc, 0, nrow);
       load_v(s0, nrow);
@@ -287,8 +366,9 @@ __global__ void __launch_bounds__(kLinThreads) linear_attn_kernel(LinearParams p
       __syncthreads();
     }
   }
-  // state out: one query head per kv group writes it
-  if (h % (p.H / p.Hkv) == 0) {
+  // state out: one query head per kv group writes it (with segments the scan
+  // kernel writes the total instead)
+  if (h % (p.H / p.Hkv) == 0 && !from_carry) {
     if (p.kv_out)
       for (int i = tid; i < Df * kLinCols; i += kLinThreads) {
         const int f = i / kLinCols, c = i % kLinCols;
@@ -297,6 +377,103 @@ __global__ void __launch_bounds__(kLinThreads) linear_attn_kernel(LinearParams p
     if (p.ks_out && blockIdx.y == 0)
       for (int f = tid; f < Df; f += kLinThreads) p.ks_out[bk * Df + f] = ks[f];
   }
+}
+
+// Phase A of the segmented causal pass: per (segment, b, kv head, column
+// slice) the segment's sums of phi(k) v^T and phi(k) into the workspace.
+__global__ void __launch_bounds__(kLinThreads) linear_segsum_kernel(LinearParams p) {
+  extern __shared__ float sm[];
+  const int Df = p.Df, ld = Df + 1;
+  float* kv = sm;
+  float* ks = kv + Df * kLinCols;
+  float* kc = ks + Df;
+  float* vc = kc + kLinChunk * ld;
+  const int tid = threadIdx.x;
+  const int bk = blockIdx.x, b = bk / p.Hkv, hkv = bk % p.Hkv;
+  const int d0 = blockIdx.y * kLinCols;
+  const int ncol = min(kLinCols, p.D - d0);
+  const int seg = blockIdx.z;
+  const int r0 = seg * p.seg_len, r1 = min(p.S, r0 + p.seg_len);
+  const float* phk = p.phi_k + (long long)bk * p.S * Df;
+  for (int i = tid; i < Df * kLinCols; i += kLinThreads) kv[i] = 0.0f;
+  for (int f = tid; f < Df; f += kLinThreads) ks[f] = 0.0f;
+  for (int s0 = r0; s0 < r1; s0 += kLinChunk) {
+    const int nrow = min(kLinChunk, r1 - s0);
+    __syncthreads();
+    for (int i = tid; i < kLinChunk * Df; i += kLinThreads) {
+      const int r = i / Df, f = i % Df;
+      kc[r * ld + f] = (r < nrow) ? phk[(long long)(s0 + r) * Df + f] : 0.0f;
+    }
+    for (int i = tid; i < kLinChunk * kLinCols; i += kLinThreads) {
+      const int r = i / kLinCols, c = i % kLinCols;
+      vc[i] = (r < nrow && c < ncol)
+                  ? load_elem(p.v, b * p.v_sb + (long long)(s0 + r) * p.v_ss + hkv * p.v_sh + d0 + c,
+                              p.v_f32)
+                  : 0.0f;
+    }
+    __syncthreads();
+    for (int i = tid; i < Df * kLinCols; i += kLinThreads) {
+      const int f = i / kLinCols, c = i % kLinCols;
+      float acc = kv[i];
+#pragma unroll
+      for (int j = 0; j < kLinChunk; ++j) acc = fmaf(kc[j * ld + f], vc[j * kLinCols + c], acc);
+      kv[i] = acc;
+    }
+    for (int f = tid; f < Df; f += kLinThreads) {
+      float acc = ks[f];
+#pragma unroll
+      for (int j = 0; j < kLinChunk; ++j) acc += kc[j * ld + f];
+      ks[f] = acc;
+    }
+  }
+  __syncthreads();
+  float* okv = p.carry_kv + (long long)seg * p.B * p.Hkv * Df * p.D;
+  for (int i = tid; i < Df * kLinCols; i += kLinThreads) {
+    const int f = i / kLinCols, c = i % kLinCols;
+    if (c < ncol) okv[((long long)bk * Df + f) * p.D + d0 + c] = kv[i];
+  }
+  if (blockIdx.y == 0) {
+    float* oks = p.carry_ks + (long long)seg * p.B * p.Hkv * Df;
+    for (int f = tid; f < Df; f += kLinThreads) oks[(long long)bk * Df + f] = ks[f];
+  }
+}
+
+// Phase B: segment sums -> exclusive prefixes in place, starting from the
+// carried state (times its scale); the total goes to kv_out / ks_out.
+__global__ void linear_scan_kernel(LinearParams p) {
+  const long long nkv = (long long)p.B * p.Hkv * p.Df * p.D;
+  const long long nks = (long long)p.B * p.Hkv * p.Df;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nkv + nks;
+       i += (long long)gridDim.x * blockDim.x) {
+    const bool is_kv = i < nkv;
+    const long long e = is_kv ? i : i - nkv;
+    const long long bk = is_kv ? e / ((long long)p.Df * p.D) : e / p.Df;
+    float* buf = is_kv ? p.carry_kv : p.carry_ks;
+    const long long stride = is_kv ? nkv : nks;
+    const float* init = is_kv ? p.kv_in : p.ks_in;
+    float run = init ? init[e] * (p.state_scale ? p.state_scale[bk] : 1.0f) : 0.0f;
+    for (int z = 0; z < p.n_seg; ++z) {
+      const float t = buf[z * stride + e];
+      buf[z * stride + e] = run;
+      run += t;
+    }
+    float* out = is_kv ? p.kv_out : p.ks_out;
+    if (out) out[e] = run;
+  }
+}
+
+// Segments of the causal pass: enough CTAs for two waves, segments of at
+// least 256 rows.
+int linear_segments(int B, int H, int S, int D) {
+  const int ctas = B * H * ((D + kLinCols - 1) / kLinCols);
+  const int want = (2 * 148 + ctas - 1) / max(ctas, 1);
+  return max(1, min(want, S / 256));
+}
+
+size_t linear_workspace_bytes(int B, int H, int Hkv, int S, int Df, int D, int causal) {
+  const int n = causal ? linear_segments(B, H, S, D) : 1;
+  if (n <= 1) return 0;
+  return (size_t)n * B * Hkv * ((size_t)Df * D + Df) * sizeof(float);
 }
 
 int linear_attn_max_features() {
@@ -315,11 +492,24 @@ cudaError_t launch_linear_attn(const LinearParams& p, cudaStream_t stream) {
   if (dev >= 0 && dev < 64 && !configured[dev]) {
     e = cudaFuncSetAttribute(linear_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              227 * 1024);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(linear_segsum_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               227 * 1024);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  dim3 grid(p.B * p.H, (p.D + kLinCols - 1) / kLinCols);
-  linear_attn_kernel<<<grid, kLinThreads, smem, stream>>>(p);
+  const int nslice = (p.D + kLinCols - 1) / kLinCols;
+  LinearParams q = p;
+  q.n_seg = p.causal ? linear_segments(p.B, p.H, p.S, p.D) : 1;
+  q.seg_len = (p.S + q.n_seg - 1) / max(q.n_seg, 1);
+  if (q.n_seg > 1) {
+    if (!p.carry_kv || !p.carry_ks) return cudaErrorInvalidValue;  // the ABI checks the workspace
+    linear_segsum_kernel<<<dim3(p.B * p.Hkv, nslice, q.n_seg), kLinThreads, smem, stream>>>(q);
+    const long long n = (long long)p.B * p.Hkv * p.Df * (p.D + 1);
+    linear_scan_kernel<<<(int)min((n + 255) / 256, 148ll * 8), 256, 0, stream>>>(q);
+  }
+  dim3 grid(p.B * p.H, nslice, q.n_seg);
+  linear_attn_kernel<<<grid, kLinThreads, smem, stream>>>(q);
   return cudaGetLastError();
 }
 

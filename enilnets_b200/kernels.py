@@ -377,6 +377,10 @@ def linear_attention(phi_q: torch.Tensor, phi_k: torch.Tensor, v: torch.Tensor, 
     a.kv_out = _ptr(new_state[0]) if new_state is not None else None
     a.ksum_out = _ptr(new_state[1]) if new_state is not None else None
     a.eps = float(eps)
-    nat.check(nat.load().enl_linear_attention(ctypes.byref(a), _stream()),
-              "enl_linear_attention")
+    lib = nat.load()
+    ws_bytes = lib.enl_linear_workspace_bytes(ctypes.byref(a))
+    if ws_bytes:
+        ws = _workspace(phi_q.device, ws_bytes)
+        a.workspace, a.workspace_bytes = ws.data_ptr(), ws_bytes
+    nat.check(lib.enl_linear_attention(ctypes.byref(a), _stream()), "enl_linear_attention")
     return (out, new_state) if return_state else out

@@ -189,7 +189,8 @@ typedef struct enl_phi_args {
   int32_t batch, seq, num_heads, head_dim;
   int32_t in_dtype;        /* ENL_DTYPE_BF16 or ENL_DTYPE_FP32 */
   int32_t kernel;          /* ENL_PHI_LINEAR or ENL_PHI_PERFORMER */
-  const float* omega;      /* performer: (num_features, head_dim) fp32, row-major */
+  const float* omega;      /* performer: (num_features, head_dim) fp32, row-major;
+                              performer head_dim up to 256 */
   int32_t num_features;    /* performer: rows of omega, 1..1024 */
   int32_t global_stab;     /* performer: 1 = one stabilizer per (b, h) (keys),
                               0 = one per row (queries) */
@@ -226,6 +227,8 @@ typedef struct enl_linear_args {
   float* kv_out;
   float* ksum_out;
   float eps; /* denominator guard, 1e-20 in the reference */
+  void* workspace; /* device scratch for the segmented causal pass, */
+  size_t workspace_bytes; /* >= enl_linear_workspace_bytes() */
 } enl_linear_args;
 
 /* o = phi(Q) S_kv / (phi(Q) . s_k + eps) with S_kv = sum phi(k) v^T and
@@ -233,6 +236,11 @@ typedef struct enl_linear_args {
  * (nn/attention_kernels.py:119-143). num_features <= enl_linear_max_features(). */
 int enl_linear_attention(const enl_linear_args* args, void* stream);
 int enl_linear_max_features(void);
+
+/* Workspace bytes enl_linear_attention needs for these arguments: causal
+ * calls long enough to run in parallel sequence segments keep one partial
+ * state per segment; 0 otherwise. */
+size_t enl_linear_workspace_bytes(const enl_linear_args* args);
 
 /* ------------------------------------------------------------- utilities */
 /* Read (and with clear != 0 reset) the device error word of the current

@@ -66,7 +66,9 @@ def torch_sync():
 @pytest.mark.parametrize("causal", [False, True])
 @pytest.mark.parametrize("S,D,Df,H,Hkv", [
     (1, 8, 8, 2, 2), (5, 40, 40, 4, 2), (16, 32, 32, 2, 1), (37, 64, 256, 4, 4),
-    (300, 128, 128, 2, 2), (129, 72, 512, 4, 1)])
+    (300, 128, 128, 2, 2), (129, 72, 512, 4, 1),
+    # long enough for the causal pass to run in parallel sequence segments
+    (1500, 64, 96, 4, 2), (2048, 32, 32, 1, 1)])
 def test_linear_attention_matches_oracle(cuda, causal, S, D, Df, H, Hkv):
     from enilnets_b200 import _native, kernels
     rng = np.random.RandomState(S + D + Df)
@@ -188,3 +190,35 @@ def test_linear_kv_reorder_matches_reference(cuda, golden_dir, float64):
         out = enl.cached_forward_step(m, np.array([[9], [9], [9]]), cache)
         assert np.max(np.abs(out - data[f"kv{i}_reordered"])) <= TOL, cfg
         assert np.allclose(out[0], out[1], atol=1e-6)
+
+
+@pytest.mark.parametrize("S,cut", [(1500, 700), (2100, 1030)])
+def test_segmented_carried_state_equals_one_pass(cuda, S, cut):
+    """Long calls run in sequence segments (per-segment sums, a scan that
+    starts from the carried, scaled state, then the outputs): split at `cut`
+    with the state handed over, they equal one pass, and the returned state
+    is the total."""
+    from enilnets_b200 import _native, kernels
+    rng = np.random.RandomState(S)
+    B, H, Hkv, D, Df = 2, 4, 2, 64, 48
+    qp = np.exp(rng.standard_normal((B, H, S, Df)) * 0.5)
+    kp = np.exp(rng.standard_normal((B, Hkv, S, Df)) * 0.5)
+    v = rng.standard_normal((B, S, Hkv, D))
+    full, st_full = kernels.linear_attention(_t(qp), _t(kp), _t(v), causal=True,
+                                             return_state=True)
+    o1, st = kernels.linear_attention(_t(qp[:, :, :cut]), _t(kp[:, :, :cut]), _t(v[:, :cut]),
+                                      causal=True, return_state=True)
+    scale = np.full((B, Hkv), 0.5)
+    o2, st2 = kernels.linear_attention(_t(qp[:, :, cut:]), _t(kp[:, :, cut:] * 0.5),
+                                       _t(v[:, cut:]), causal=True, state=st,
+                                       state_scale=_t(scale), return_state=True)
+    torch_sync()
+    _native.raise_on_device_error()
+    stepped = np.concatenate([_np(o1), _np(o2)], axis=1)
+    assert np.max(np.abs(stepped - _np(full))) <= 1e-4
+    kv_ref = np.einsum("bhsf,bshd->bhfd", kp, v)
+    assert np.max(np.abs(_np(st_full[0]) - kv_ref)) <= 1e-3 * np.abs(kv_ref).max()
+    assert np.max(np.abs(_np(st2[0]) - 0.5 * kv_ref)) <= 1e-3 * np.abs(kv_ref).max()
+    ref, _, _ = lr.linear_attention(qp, np.repeat(kp, 2, axis=1),
+                                    np.repeat(v.transpose(0, 2, 1, 3), 2, axis=1), True)
+    assert np.max(np.abs(_np(full).transpose(0, 2, 1, 3) - ref)) <= 1e-4
