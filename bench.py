@@ -21,6 +21,8 @@ Also measured in the same run (sub-objects of the line):
                   bf16 precision (fused QKV GEMM, K1, output GEMM).
   layer_cfg1   -- config 1 (B4 S256 E256 H8, causal, float32) through the
                   NumPy-facing Forward on the fp32 split-bf16 path.
+  sparse_attention -- sparse_pattern (block-sparse, K1's sparse mode), B4
+                  S16384 H16 D128 causal bf16, beside the dense causal kernel
   linear_attention -- the attention_kernel="linear" and "performer" options
                   (feature maps + causal linear attention, K4), B4 S4096 H16
                   D64 per GPU, fp32 on the CUDA cores.
@@ -488,6 +490,49 @@ def bench_linear(dist: Dist, clocks: ClockSampler, warmup: int, steps: int = 10)
     return res
 
 
+SPARSE_PATTERNS = {
+    "bs128": {"block_size": 128, "local": 2, "global": 1, "random": 2},
+    "bs64": {"block_size": 64, "local": 3, "global": 2, "random": 3},
+}
+
+
+def bench_sparse(dist: Dist, clocks: ClockSampler, warmup: int, steps: int = 10):
+    """Block-sparse attention (sparse_pattern, local + global + random blocks)
+    on K1's sparse mode, per GPU B4 S16384 H16 D128 causal bf16, next to the
+    dense causal kernel on the same inputs. FLOPs count the pairs the pattern
+    allows (4 D per pair); tile_fill is that over the visited 128 x 128
+    tiles' area."""
+    import torch
+    from enilnets_b200 import kernels, _native, sparse
+    B, S, H, D = 4, 16384, 16, 128
+    g = torch.Generator(device=dist.device).manual_seed(7000 + dist.rank)
+    q, k, v = (torch.randn((B, S, H, D), generator=g, device=dist.device).to(torch.bfloat16)
+               for _ in range(3))
+    peak = float(load_peaks()[0]["bf16_tflops"])
+
+    def run(step):
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        _native.raise_on_device_error()
+        return timed(dist, clocks, step, steps) / steps
+
+    dense_ms = run(lambda: kernels.attention_prefill(q, k, v, causal=True))
+    res = {"dense_causal_ms": dense_ms}
+    for name, pat in SPARSE_PATTERNS.items():
+        spec = sparse.normalize_pattern(pat)
+        lay = sparse.build_layout(spec, S, S, causal=True, device=q.device)
+        ms = run(lambda: sparse.attention(q, k, v, spec, causal=True))
+        tf = dist.sum(4.0 * D * lay.pairs * B * H) / (ms * 1e-3) / 1e12
+        res[name] = {"pattern": pat, "ms_per_step": ms, "TFLOP_s": tf,
+                     "frac_of_bf16_peak_per_gpu": tf / dist.world / peak,
+                     "speedup_vs_dense_causal": dense_ms / ms,
+                     "allowed_fraction_of_causal": lay.pairs / (S * (S + 1) / 2),
+                     "tile_fill": lay.pairs / (lay.n_entries * 128.0 * 128.0)}
+    res["config"] = f"B{B}/GPU S{S} H{H} D{D} causal bf16; FLOPs over allowed pairs"
+    return res
+
+
 def bench_layer_cfg2(dist: Dist, clocks: ClockSampler, warmup: int, steps: int = 10):
     """graph.MultiHeadAttention(2048, 16, causal) forward with key padding on
     device-resident x, bf16 precision: QKV GEMM + K1 + output GEMM."""
@@ -628,7 +673,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--skip-sub", action="store_true", help="headline only")
     ap.add_argument("--only", choices=["all", "prefill", "decode", "longctx", "cross", "layer",
-                                       "linear"],
+                                       "linear", "sparse"],
                     default="all",
                     help="profiling: run one workload")
     ap.add_argument("--batch", type=int, default=0, help="profiling: prefill batch override")
@@ -659,6 +704,8 @@ def main():
                 res = bench_cross_cfg4(dist, clocks, args.warmup)
             elif args.only == "linear":
                 res = bench_linear(dist, clocks, args.warmup)
+            elif args.only == "sparse":
+                res = bench_sparse(dist, clocks, args.warmup)
             elif args.only == "layer":
                 res = {"layer_cfg2": bench_layer_cfg2(dist, clocks, args.warmup),
                        "layer_cfg1": bench_layer_cfg1(dist, args.warmup)}
@@ -676,6 +723,7 @@ def main():
             sub["longctx_cfg5"] = bench_longctx_cfg5(dist, clocks, args.warmup)
             sub["cross_cfg4"] = bench_cross_cfg4(dist, clocks, args.warmup)
             sub["linear_attention"] = bench_linear(dist, clocks, args.warmup)
+            sub["sparse_attention"] = bench_sparse(dist, clocks, args.warmup)
             sub["layer_cfg2"] = bench_layer_cfg2(dist, clocks, args.warmup)
             sub["layer_cfg1"] = bench_layer_cfg1(dist, args.warmup)
     finally:

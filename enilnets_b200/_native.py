@@ -32,7 +32,7 @@ DEVICE_ERRORS = {1: "an mbarrier wait exceeded its time budget",
                  3: "a launch-time shape invariant was violated"}
 
 
-ABI_VERSION = 3  # ENL_ABI_VERSION of include/enl_attn.h
+ABI_VERSION = 4  # ENL_ABI_VERSION of include/enl_attn.h
 
 
 class PrefillArgs(Structure):
@@ -106,6 +106,24 @@ class LinearArgs(Structure):
 ENL_PHI_LINEAR = 0
 ENL_PHI_PERFORMER = 1
 
+
+class SparseLayout(Structure):
+    """Mirror of enl_sparse_layout."""
+    _fields_ = [("tile_ptr", c_void_p), ("tile_kt", c_void_p), ("masks", c_void_p),
+                ("n_entries", c_int32)]
+
+
+class SparseMaskArgs(Structure):
+    """Mirror of enl_sparse_mask_args."""
+    _fields_ = [
+        ("tile_ptr", c_void_p), ("tile_kt", c_void_p), ("masks", c_void_p),
+        ("n_entries", c_int32),
+        ("sel_ptr", c_void_p), ("sel_kb", c_void_p),
+        ("n_qblocks", c_int32), ("n_sel", c_int32), ("qb0", c_int64),
+        ("block_size", c_int32), ("seq_q", c_int32), ("seq_kv", c_int32),
+        ("q_pos0", c_int64), ("k_pos0", c_int64), ("causal", c_int32),
+    ]
+
 # Exported symbol -> (argtypes, restype). Kept in sync with include/enl_attn.h
 # (a CPU test checks every declared symbol is exported and bound here).
 SIGNATURES = {
@@ -130,6 +148,9 @@ SIGNATURES = {
     "enl_linear_attention": ([POINTER(LinearArgs), c_void_p], c_int32),
     "enl_linear_max_features": ([], c_int32),
     "enl_linear_workspace_bytes": ([POINTER(LinearArgs)], c_size_t),
+    "enl_sparse_build_masks": ([POINTER(SparseMaskArgs), c_void_p], c_int32),
+    "enl_attn_prefill_sparse": ([POINTER(PrefillArgs), POINTER(SparseLayout), c_void_p],
+                                c_int32),
     "enl_device_error": ([POINTER(c_int32), POINTER(c_int32), c_int32], c_int32),
     "enl_last_error": ([], c_char_p),
     "enl_abi_version": ([], c_int32),

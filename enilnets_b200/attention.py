@@ -5,6 +5,8 @@ Mirrors the reference's attention branches layer by layer:
                              GQA, causal/window masks, softmax, Wo)
   * cross-attention          nn/forward.py:557-591
   * key-padding (graph MHA)  graph/sequence.py:144-183 (additive -1e9 rule)
+  * linearized kernels       nn/forward.py:456-480
+  * block-sparse patterns    nn/forward.py:482-502
 The projections are plain GEMMs (cuBLAS through torch) in the precision that
 backend.set_precision selects (fp32 or bf16); Q/K/V are never copied or
 expanded: the prefill kernel (K1) reads them as strided head views
@@ -18,7 +20,7 @@ from typing import Optional
 
 import numpy as np
 
-from . import kernels
+from . import kernels, sparse
 from .backend import compute_dtype, device, to_device
 
 SINUSOIDAL_BASE = 10000.0  # core/constants.py:70
@@ -34,8 +36,6 @@ def check_supported(layer: dict, training: bool = False) -> None:
     if kernel != "softmax" and kernel not in LINEAR_KERNELS:
         raise ValueError(f"attention_kernel={kernel!r} is not supported by the B200 attention "
                          "path (softmax, linear and performer only).")
-    if layer.get("sparse_pattern") is not None:
-        raise ValueError("sparse_pattern is not supported by the B200 attention path.")
     if training and layer.get("dropout", 0.0) > 0:
         raise ValueError("attention dropout at training=True is not supported by the B200 "
                          "attention path (inference only).")
@@ -188,6 +188,15 @@ def self_attention(layer: dict, x, key_padding_mask=None, mask_mode: Optional[st
             raise ValueError("key_padding_mask is not supported with a linearized "
                              "attention_kernel (it builds no score matrix to mask)")
         ctx = linearized(layer, q, k, v, bool(layer.get("causal", False)))
+        return project(ctx.flatten(-2), layer, "o").float()
+    if layer.get("sparse_pattern") is not None:
+        if key_padding_mask is not None:
+            raise ValueError("key_padding_mask is not supported with sparse_pattern (the "
+                             "pattern is the whole mask)")
+        ctx = sparse.attention(q, k, v, sparse.normalize_pattern(layer["sparse_pattern"]),
+                               causal=bool(layer.get("causal", False)),
+                               alibi_slopes=alibi_tensor(H) if scheme == "alibi" else None,
+                               out_dtype=compute_dtype())
         return project(ctx.flatten(-2), layer, "o").float()
     lens = None
     mode = mask_mode or "exclude"

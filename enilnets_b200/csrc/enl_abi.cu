@@ -126,7 +126,13 @@ int enl_device_error(int32_t* code, int32_t* info, int32_t clear) {
   return ENL_OK;
 }
 
-int enl_attn_prefill(const enl_prefill_args* a, void* stream) {
+}  // extern "C"
+
+namespace enl {
+namespace {
+
+// enl_attn_prefill, and enl_attn_prefill_sparse when layout is set.
+int prefill_impl(const enl_prefill_args* a, const enl_sparse_layout* layout, void* stream) {
   if (!a) return fail(ENL_ERR_INVALID, "enl_attn_prefill: args is NULL");
   if (!a->q || !a->k || !a->v || !a->o)
     return fail(ENL_ERR_INVALID, "enl_attn_prefill: q, k, v and o must be non-NULL");
@@ -231,6 +237,10 @@ int enl_attn_prefill(const enl_prefill_args* a, void* stream) {
   p.q_pos0 = a->q_pos0;
   p.k_pos0 = a->k_pos0;
   p.scale_log2 = a->scale * 1.4426950408889634f;
+  p.sp_ptr = layout ? layout->tile_ptr : nullptr;
+  p.sp_kt = layout ? layout->tile_kt : nullptr;
+  p.sp_mask = layout ? reinterpret_cast<const unsigned long long*>(layout->masks) : nullptr;
+  p.sp_entries = layout ? layout->n_entries : 0;
   // One persistent CTA per SM. Sections of (batch, head) pairs whose K/V
   // fit in about a quarter of L2 keep the concurrently running items on
   // shared keys.
@@ -267,6 +277,66 @@ int enl_attn_prefill(const enl_prefill_args* a, void* stream) {
     e = (D == 128) ? launch_prefill<128, false>(tq, tk, tv, to, p, s)
                    : launch_prefill<64, false>(tq, tk, tv, to, p, s);
   if (e != cudaSuccess) return cuda_fail(e, "enl_attn_prefill launch");
+  return ENL_OK;
+}
+
+}  // namespace
+}  // namespace enl
+
+extern "C" {
+
+int enl_attn_prefill(const enl_prefill_args* a, void* stream) {
+  return prefill_impl(a, nullptr, stream);
+}
+
+int enl_attn_prefill_sparse(const enl_prefill_args* a, const enl_sparse_layout* l,
+                            void* stream) {
+  if (!a || !l) return fail(ENL_ERR_INVALID, "enl_attn_prefill_sparse: args or layout is NULL");
+  if (!l->tile_ptr || !l->tile_kt || !l->masks || l->n_entries < 0)
+    return fail(ENL_ERR_INVALID,
+                "enl_attn_prefill_sparse: layout needs tile_ptr, tile_kt, masks and "
+                "n_entries >= 0");
+  if ((reinterpret_cast<uintptr_t>(l->masks) & 7u) != 0)
+    return fail(ENL_ERR_INVALID, "enl_attn_prefill_sparse: masks must be 8-byte aligned");
+  if (a->window >= 0 || a->mask_mode != ENL_MASK_EXCLUDE || a->kv_valid_len)
+    return fail(ENL_ERR_INVALID,
+                "enl_attn_prefill_sparse: the layout is the whole mask; window must be < 0, "
+                "mask_mode ENL_MASK_EXCLUDE and kv_valid_len NULL");
+  return prefill_impl(a, l, stream);
+}
+
+int enl_sparse_build_masks(const enl_sparse_mask_args* a, void* stream) {
+  if (!a) return fail(ENL_ERR_INVALID, "enl_sparse_build_masks: args is NULL");
+  if (!a->tile_ptr || !a->tile_kt || !a->masks || !a->sel_ptr || (!a->sel_kb && a->n_sel > 0))
+    return fail(ENL_ERR_INVALID, "enl_sparse_build_masks: NULL device pointer");
+  if (a->block_size < 1 || a->seq_q < 1 || a->seq_kv < 1 || a->n_entries < 0 ||
+      a->n_qblocks < 1 || a->n_sel < 0 || a->q_pos0 < 0 || a->k_pos0 < 0 || a->qb0 < 0)
+    return fail(ENL_ERR_INVALID,
+                "enl_sparse_build_masks: block_size=%d seq_q=%d seq_kv=%d n_entries=%d "
+                "n_qblocks=%d n_sel=%d q_pos0=%lld k_pos0=%lld qb0=%lld out of range",
+                a->block_size, a->seq_q, a->seq_kv, a->n_entries, a->n_qblocks, a->n_sel,
+                (long long)a->q_pos0, (long long)a->k_pos0, (long long)a->qb0);
+  if ((reinterpret_cast<uintptr_t>(a->masks) & 7u) != 0)
+    return fail(ENL_ERR_INVALID, "enl_sparse_build_masks: masks must be 8-byte aligned");
+  SparseMaskParams p;
+  p.tile_ptr = a->tile_ptr;
+  p.tile_kt = a->tile_kt;
+  p.masks = reinterpret_cast<unsigned long long*>(a->masks);
+  p.n_qtiles = (a->seq_q + 127) / 128;
+  p.n_entries = a->n_entries;
+  p.sel_ptr = a->sel_ptr;
+  p.sel_kb = a->sel_kb;
+  p.n_qblocks = a->n_qblocks;
+  p.n_sel = a->n_sel;
+  p.qb0 = a->qb0;
+  p.block_size = a->block_size;
+  p.seq_q = a->seq_q;
+  p.seq_kv = a->seq_kv;
+  p.causal = a->causal != 0;
+  p.q_pos0 = a->q_pos0;
+  p.k_pos0 = a->k_pos0;
+  cudaError_t e = launch_sparse_masks(p, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "enl_sparse_build_masks launch");
   return ENL_OK;
 }
 

@@ -29,6 +29,15 @@ struct PrefillParams {
   // Persistent schedule: n_items = B * H * ceil(Sq / 128) work items over
   // min(n_items, n_ctas) CTAs, in sections of sec_bh (batch, head) pairs.
   int n_items, n_ctas, sec_bh;
+  // Block-sparse mode (nn/sparse_attention.py:96-142), when sp_ptr is set:
+  // query tile qt visits the key tiles sp_kt[sp_ptr[qt] .. sp_ptr[qt + 1]),
+  // and row r of entry e sees key column c of half h (keys 64h + c of the
+  // tile) iff bit c of sp_mask[(2e + h) * 128 + r] is set. The masks carry
+  // causality and the sequence end; causal/window/kv_len do not apply.
+  const int* sp_ptr;
+  const int* sp_kt;
+  const unsigned long long* sp_mask;
+  int sp_entries;
 };
 
 // kSplit: the tensor maps cover (hi, lo) bf16 planes of fp32 inputs
@@ -43,6 +52,21 @@ cudaError_t launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const C
 // dst[b][s][h][plane][D] bf16 with plane 0 = bf16(x), plane 1 = bf16(x - hi).
 cudaError_t launch_split_planes(const float* src, long long sb, long long ss, long long sh, int B,
                                 int S, int H, int D, void* dst, cudaStream_t stream);
+
+// Column masks of a block-sparse layout (enl_sparse.cu).
+struct SparseMaskParams {
+  const int* tile_ptr;  // (n_qtiles + 1) entry ranges per query tile
+  const int* tile_kt;   // (n_entries) key tile of each entry
+  unsigned long long* masks;  // (n_entries, 2, 128) out
+  int n_qtiles, n_entries;
+  const int* sel_ptr;   // (n_qblocks + 1) selection ranges per query block
+  const int* sel_kb;    // (n_sel) selected key blocks
+  int n_qblocks, n_sel;
+  long long qb0;        // query block of sel_ptr[0]
+  int block_size, seq_q, seq_kv, causal;
+  long long q_pos0, k_pos0;
+};
+cudaError_t launch_sparse_masks(const SparseMaskParams& p, cudaStream_t stream);
 
 // K2 split-KV decode: one query token per (b, h) against cached slots.
 struct DecodeParams {

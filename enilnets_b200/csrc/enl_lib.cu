@@ -8,3 +8,4 @@
 #include "enl_decode_noalloc.cu"
 #include "enl_selftest.cu"
 #include "enl_linear.cu"
+#include "enl_sparse.cu"

@@ -146,6 +146,7 @@ struct WorkItem {
 };
 static_assert(sizeof(WorkItem) == 32, "softmax warps keep items in 32-byte slots");
 
+template <bool kSparse>
 __device__ __forceinline__ WorkItem work_item(const PrefillParams& p, int t) {
   const int n_qt = (p.Sq + 127) / 128;
   const int n_bh = p.B * p.H;
@@ -162,20 +163,41 @@ __device__ __forceinline__ WorkItem work_item(const PrefillParams& p, int t) {
   w.r0 = qt * 128;
   w.lkey = p.Skv;
   if (p.kv_len != nullptr) w.lkey = max(0, min(p.kv_len[w.b], p.Skv));
-  bool safe;
-  tile_range(p, w.r0, w.lkey, (p.Skv + 127) / 128, w.lo, w.hi, safe);
-  w.safe = safe;
+  if constexpr (kSparse) {
+    // Entries [sp_ptr[qt], sp_ptr[qt + 1]) of the layout; every row of a
+    // sparse tile sees at least its own key, so -inf exclusion is exact.
+    w.lo = p.sp_ptr[qt];
+    w.hi = p.sp_ptr[qt + 1];
+    if (w.lo < 0 || w.hi > p.sp_entries || w.lo > w.hi) {
+      report_error(kDevBadIndex, qt);
+      w.lo = w.hi = 0;
+    }
+    w.safe = 1;
+  } else {
+    bool safe;
+    tile_range(p, w.r0, w.lkey, (p.Skv + 127) / 128, w.lo, w.hi, safe);
+    w.safe = safe;
+  }
   return w;
 }
 
+// Key tile of the n-th visit of an item: the layout's entry in sparse mode,
+// otherwise the visit index itself.
+template <bool kSparse>
+__device__ __forceinline__ int key_tile(const PrefillParams& p, int j) {
+  if constexpr (kSparse) return p.sp_kt[j];
+  return j;
+}
+
 // Walks this CTA's (item, key tile) sequence, skipping items without keys.
+template <bool kSparse>
 struct TileCursor {
   int t;       // item id (>= n_items: done)
   int j, lo, hi;
   int wi;      // ordinal of the item among this CTA's items with work
   __device__ __forceinline__ void seek(const PrefillParams& p) {
     while (t < p.n_items) {
-      const WorkItem w = work_item(p, t);
+      const WorkItem w = work_item<kSparse>(p, t);
       if (w.lo < w.hi) {
         j = lo = w.lo;
         hi = w.hi;
@@ -203,7 +225,7 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-template <int D, bool kSplit>
+template <int D, bool kSplit, bool kSparse>
 __global__ void __launch_bounds__(384, 1)
     attn_prefill_sm100(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_k,
@@ -269,7 +291,7 @@ __global__ void __launch_bounds__(384, 1)
       int q_issued = 0, issued = 0, issued_v = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < p.n_items && ok; t += gridDim.x) {
-        const WorkItem w = work_item(p, t);
+        const WorkItem w = work_item<kSparse>(p, t);
         if (w.lo >= w.hi) continue;
         // Split mode: the plane tensors interleave (hi, lo) per head, so
         // plane pl of head h is "head" kPlanes * h + pl of the tensor map.
@@ -285,6 +307,7 @@ __global__ void __launch_bounds__(384, 1)
                         &tm_q, bar_q_full + qb, a * 64, w.r0, Cfg::kPlanes * w.h + pl, w.b);
         ++q_issued;
         for (int j = w.lo; j < w.hi && ok; ++j, ++issued) {
+          const int kt = key_tile<kSparse>(p, j);
           const int st = issued % Cfg::kStages;
           const uint32_t use = issued / Cfg::kStages;
           if (use > 0) ok = mbar_wait(bar_k_empty + st, (use - 1) & 1, abort_flag, 10);
@@ -294,7 +317,7 @@ __global__ void __launch_bounds__(384, 1)
             for (int a = 0; a < Cfg::kAtoms; ++a)
               tma_load_4d(smem + Cfg::kOffK + st * Cfg::kOpBytes + pl * Cfg::kTileBytes +
                               a * Cfg::kAtomBytes,
-                          &tm_k, bar_k_full + st, a * 64, j * 128, Cfg::kPlanes * w.hkv + pl,
+                          &tm_k, bar_k_full + st, a * 64, kt * 128, Cfg::kPlanes * w.hkv + pl,
                           w.b);
           if (use > 0) ok = mbar_wait(bar_v_empty + st, (use - 1) & 1, abort_flag, 11);
           if (!ok) {
@@ -306,7 +329,7 @@ __global__ void __launch_bounds__(384, 1)
             for (int a = 0; a < Cfg::kAtoms; ++a)
               tma_load_4d(smem + Cfg::kOffV + st * Cfg::kOpBytes + pl * Cfg::kTileBytes +
                               a * Cfg::kAtomBytes,
-                          &tm_v, bar_v_full + st, a * 64, j * 128, Cfg::kPlanes * w.hkv + pl,
+                          &tm_v, bar_v_full + st, a * 64, kt * 128, Cfg::kPlanes * w.hkv + pl,
                           w.b);
           ++issued_v;
         }
@@ -340,7 +363,7 @@ __global__ void __launch_bounds__(384, 1)
     auto wait = [&](uint64_t* bar, uint32_t parity, int site) {
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, site));
     };
-    TileCursor cur;
+    TileCursor<kSparse> cur;
     cur.start(p);
     uint32_t g = 0;  // tiles of this CTA issued so far
     bool ok = true;
@@ -433,7 +456,7 @@ __global__ void __launch_bounds__(384, 1)
       int wi = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < p.n_items && ok; t += gridDim.x) {
-        const WorkItem w = work_item(p, t);
+        const WorkItem w = work_item<kSparse>(p, t);
         if (w.lo >= w.hi) continue;
         const int qb = wi % Cfg::kQBufs;
         ok = mbar_wait(bar_stage_full, wi & 1, abort_flag, 40);
@@ -465,7 +488,7 @@ __global__ void __launch_bounds__(384, 1)
     // own shared-memory slot: nothing of it stays live in registers across
     // the tile loop, which runs at the register limit.
     WorkItem* slots = reinterpret_cast<WorkItem*>(smem + Cfg::kOffItems) + 2 * warp;
-    if (lane == 0) slots[0] = work_item(p, blockIdx.x);
+    if (lane == 0) slots[0] = work_item<kSparse>(p, blockIdx.x);
     int k = 0;  // this CTA's item ordinal
     for (int t = blockIdx.x; t < p.n_items; t += gridDim.x, ++k) {
       __syncwarp();
@@ -498,6 +521,14 @@ __global__ void __launch_bounds__(384, 1)
       for (int n = 0; lo + n < hi && !failed; ++n, ++g) {
         const int j = lo + n;
         const int buf = g & 1;
+        // Sparse mode: this row's allowed columns of this half, loaded before
+        // the wait so the load's latency hides behind it.
+        unsigned long long allow = ~0ull;
+        int kt = j;
+        if constexpr (kSparse) {
+          kt = p.sp_kt[j];
+          allow = p.sp_mask[((long long)j * 2 + half) * 128 + rloc];
+        }
         failed = !__all_sync(0xffffffffu,
                              mbar_wait(bar_s_full + buf, (g >> 1) & 1, abort_flag, 30 + half));
         if (failed) break;
@@ -511,8 +542,12 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
           for (int c = 0; c < 64; ++c) s[c] = __uint_as_float(sr[c]);
         }
-        const int j0 = j * 128 + (int)col_h;  // key index of this half's column 0
-        const bool full_tile = (j0 >= in_lo) && (j0 + 63 <= in_hi) && !tiers && slope2 == 0.0f;
+        const int j0 = kt * 128 + (int)col_h;  // key index of this half's column 0
+        bool full_tile;
+        if constexpr (kSparse)  // rows past Sq are never stored: they do not force masking
+          full_tile = __all_sync(0xffffffffu, allow == ~0ull || row >= p.Sq) && slope2 == 0.0f;
+        else
+          full_tile = (j0 >= in_lo) && (j0 + 63 <= in_hi) && !tiers && slope2 == 0.0f;
         bool reset = false;
         float m_tile = -INFINITY;
         if (full_tile) {
@@ -533,7 +568,16 @@ __global__ void __launch_bounds__(384, 1)
           auto rel = [&](int v) { return max(-1, min(65, v - j0)); };
           const float dbase = (float)(diag - j0);
           const bool alibi_abs = !p.causal;
-          if (!tiers) {
+          if constexpr (kSparse) {
+#pragma unroll
+            for (int c = 0; c < 64; ++c) {
+              float dist = dbase - (float)c;
+              if (alibi_abs) dist = fabsf(dist);
+              const float v = fmaf(s[c], sl2, -slope2 * dist);
+              s[c] = ((allow >> c) & 1ull) ? v : -INFINITY;
+              m_tile = fmaxf(m_tile, s[c]);
+            }
+          } else if (!tiers) {
             const int c_lo = rel(row_lo), c_hi = rel(row_hi);  // unmasked columns [c_lo, c_hi]
 #pragma unroll
             for (int c = 0; c < 64; ++c) {
@@ -659,7 +703,7 @@ __global__ void __launch_bounds__(384, 1)
 
       // ----------------------------------------------------------- epilogue
       if (lane == 0 && t + (int)gridDim.x < p.n_items)
-        slots[(k + 1) & 1] = work_item(p, t + gridDim.x);
+        slots[(k + 1) & 1] = work_item<kSparse>(p, t + gridDim.x);
       const WorkItem we = slots[k & 1];
       const int erow = we.r0 + rloc;
       // Merge the two halves by log-sum-exp: only the half(s) with the
@@ -791,15 +835,21 @@ cudaError_t launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const C
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
-    e = cudaFuncSetAttribute(attn_prefill_sm100<D, kSplit>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+    const cudaFuncAttribute a = cudaFuncAttributeMaxDynamicSharedMemorySize;
+    e = cudaFuncSetAttribute(attn_prefill_sm100<D, kSplit, false>, a, Cfg::kSmemBytes);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attn_prefill_sm100<D, kSplit, true>, a, Cfg::kSmemBytes);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
   if (p.n_items <= 0) return cudaSuccess;
   const int grid = min(p.n_items, p.n_ctas);
-  attn_prefill_sm100<D, kSplit><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(tq, tk, tv, to,
-                                                                                  p);
+  if (p.sp_ptr != nullptr)
+    attn_prefill_sm100<D, kSplit, true>
+        <<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(tq, tk, tv, to, p);
+  else
+    attn_prefill_sm100<D, kSplit, false>
+        <<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(tq, tk, tv, to, p);
   return cudaGetLastError();
 }
 

@@ -47,7 +47,7 @@ def attention_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
                       q_pos0: int = 0, k_pos0: int = 0, mask_mode: str = "exclude",
                       scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
                       out_dtype: torch.dtype = torch.bfloat16,
-                      return_lse: bool = False):
+                      return_lse: bool = False, sparse=None):
     """softmax(q k^T * scale + alibi + mask) v via the K1 tcgen05 kernel.
 
     q: (B, Sq, H, D); k, v: (B, Skv, Hkv, D); all bf16, or all fp32 (the
@@ -57,6 +57,9 @@ def attention_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     kv_valid_len: int32 (B,) -- keys [0, len_b) are real (graph/sequence.py:23-29).
     mask_mode: "exclude" (-inf, the nn/ path) or "additive" (-1e9 per violated
     mask term, graph/sequence.py:162-176).
+    sparse: a block-sparse layout (enilnets_b200.sparse.SparseLayout) built for
+    these Sq, Skv, q_pos0 and k_pos0; it is then the whole mask (causal only
+    picks the ALiBi distance), nn/sparse_attention.py:96-142.
     Returns out (B, Sq, H, D) [and lse (B, H, Sq) fp32].
     """
     if q.dtype not in _DTYPES:
@@ -110,8 +113,48 @@ def attention_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
         # Stream-ordered by torch's caching allocator, freed after the launch.
         ws = torch.empty(need, dtype=torch.uint8, device=q.device)
         a.workspace, a.workspace_bytes = ws.data_ptr(), need
-    nat.check(lib.enl_attn_prefill(ctypes.byref(a), _stream()), "enl_attn_prefill")
+    if sparse is None:
+        nat.check(lib.enl_attn_prefill(ctypes.byref(a), _stream()), "enl_attn_prefill")
+    else:
+        if (sparse.seq_q, sparse.seq_kv, sparse.q_pos0, sparse.k_pos0) != (Sq, Skv, int(q_pos0),
+                                                                           int(k_pos0)):
+            raise ValueError(
+                f"sparse layout is for seq_q={sparse.seq_q} seq_kv={sparse.seq_kv} "
+                f"q_pos0={sparse.q_pos0} k_pos0={sparse.k_pos0}, not {Sq}, {Skv}, {q_pos0}, "
+                f"{k_pos0}")
+        for name in ("tile_ptr", "tile_kt", "masks"):
+            if getattr(sparse, name).device != q.device:
+                raise ValueError(f"sparse layout {name} is on {getattr(sparse, name).device}, "
+                                 f"not {q.device}")
+        nat.check(lib.enl_attn_prefill_sparse(ctypes.byref(a), ctypes.byref(sparse.native()),
+                                              _stream()), "enl_attn_prefill_sparse")
     return (out, lse) if return_lse else out
+
+
+def sparse_build_masks(tile_ptr: torch.Tensor, tile_kt: torch.Tensor, masks: torch.Tensor,
+                       sel_ptr: torch.Tensor, sel_kb: torch.Tensor, *, qb0: int,
+                       block_size: int, seq_q: int, seq_kv: int, q_pos0: int, k_pos0: int,
+                       causal: bool) -> None:
+    """Fill a block-sparse layout's column masks on the device from the
+    per-query-block selection (nn/sparse_attention.py:48-84, :130-134)."""
+    for name, t, dt in (("tile_ptr", tile_ptr, torch.int32), ("tile_kt", tile_kt, torch.int32),
+                        ("masks", masks, torch.int64), ("sel_ptr", sel_ptr, torch.int32),
+                        ("sel_kb", sel_kb, torch.int32)):
+        _require_cuda(name, t, dt, last_contiguous=False)
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    n_entries = tile_kt.numel()
+    if masks.numel() != n_entries * 256:
+        raise ValueError(f"masks must hold {n_entries} x 2 x 128 words, got {masks.numel()}")
+    a = nat.SparseMaskArgs()
+    a.tile_ptr, a.tile_kt, a.masks = tile_ptr.data_ptr(), tile_kt.data_ptr(), masks.data_ptr()
+    a.n_entries = n_entries
+    a.sel_ptr, a.sel_kb = sel_ptr.data_ptr(), sel_kb.data_ptr()
+    a.n_qblocks, a.n_sel, a.qb0 = sel_ptr.numel() - 1, sel_kb.numel(), int(qb0)
+    a.block_size, a.seq_q, a.seq_kv = int(block_size), int(seq_q), int(seq_kv)
+    a.q_pos0, a.k_pos0, a.causal = int(q_pos0), int(k_pos0), int(bool(causal))
+    nat.check(nat.load().enl_sparse_build_masks(ctypes.byref(a), _stream()),
+              "enl_sparse_build_masks")
 
 
 _workspaces: dict = {}

@@ -21,7 +21,7 @@ from typing import Any, Dict
 
 import numpy as np
 
-from . import attention, kernels
+from . import attention, kernels, sparse
 from .backend import device, to_device, to_numpy
 from .network import dense, embed, layernorm, positional_table
 
@@ -193,7 +193,17 @@ def attention_step(layer: Dict[str, Any], x, idx: int, cache: KVCache, B: int, S
         drop = max(0, (pos - window) - (lc.base + lc.begin))
         lc.begin = min(lc.begin + drop, lc.end)
     slopes = attention.alibi_tensor(H) if scheme == "alibi" else None
-    if S_new == 1:
+    spec = layer.get("sparse_pattern")
+    if spec is not None:
+        # Block-sparse step (nn/kvcache.py:263-306): K1's sparse mode at the
+        # step's absolute positions, for one new token or several; the cache
+        # keeps every key since any earlier block may be selected.
+        kv_k = lc.k[:, :, lc.begin:lc.end].permute(0, 2, 1, 3)
+        kv_v = lc.v[:, :, lc.begin:lc.end].permute(0, 2, 1, 3)
+        ctx = sparse.attention(q, kv_k, kv_v, sparse.normalize_pattern(spec), causal=True,
+                               alibi_slopes=slopes, q_pos0=pos, k_pos0=lc.base + lc.begin,
+                               out_dtype=qkv.dtype)
+    elif S_new == 1:
         ctx = kernels.attention_decode(q[:, 0], lc.k, lc.v, slot_begin=lc.begin,
                                        slot_end=lc.end, pos_slot0=lc.base, q_pos=pos,
                                        window=window, alibi_slopes=slopes,

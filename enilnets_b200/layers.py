@@ -149,9 +149,9 @@ def add_multihead_attention(self: Any, embed_dim: Optional[int] = None, num_head
                             tiled_block_size: Optional[int] = None) -> None:
     """Multi-head self-attention, nn/layers.py:256-354. attention_kernel
     "softmax" runs the fused softmax kernels; "linear" (elu + 1) and
-    "performer" (FAVOR+) run the linearized-attention kernels. Block-sparse
-    patterns (nn/sparse_attention.py) raise ValueError here rather than
-    silently falling back. tiled_block_size is accepted (the softmax kernel
+    "performer" (FAVOR+) run the linearized-attention kernels; a
+    sparse_pattern (nn/sparse_attention.py) runs the softmax kernel over the
+    pattern's key tiles only. tiled_block_size is accepted (the softmax kernel
     always streams) and validated as the reference does."""
     if embed_dim is None:
         embed_dim = _require_width(self, "add_multihead_attention")
@@ -169,11 +169,17 @@ def add_multihead_attention(self: Any, embed_dim: Optional[int] = None, num_head
             raise ValueError(
                 f"sparse_pattern is incompatible with attention_kernel={attention_kernel!r}: a "
                 "linearized kernel never builds a score matrix, so there is nothing to sparsify.")
-        raise ValueError("sparse_pattern is not supported by the B200 attention path.")
+        if window_size is not None:
+            raise ValueError(
+                "sparse_pattern and window_size both restrict which keys a query sees; use "
+                "sparse_pattern's 'local' blocks for a windowed pattern rather than combining "
+                "the two.")
+        from .sparse import normalize_pattern
+        sparse_pattern = normalize_pattern(sparse_pattern)
     if tiled_block_size is not None:
         if int(tiled_block_size) < 1:
             raise ValueError(f"tiled_block_size must be >= 1 or None, got {tiled_block_size}")
-        if attention_kernel != "softmax":
+        if attention_kernel != "softmax" or sparse_pattern is not None:
             raise ValueError(
                 "tiled_block_size only applies to the plain softmax path; the linearized kernels "
                 "and sparse_pattern already avoid building a score matrix, so there is nothing "

@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define ENL_ABI_VERSION 3
+#define ENL_ABI_VERSION 4
 
 /* Status codes. The Python binding maps INVALID/UNSUPPORTED to ValueError
  * (the reference raises ValueError for bad layer configurations,
@@ -241,6 +241,52 @@ int enl_linear_max_features(void);
  * calls long enough to run in parallel sequence segments keep one partial
  * state per segment; 0 otherwise. */
 size_t enl_linear_workspace_bytes(const enl_linear_args* args);
+
+/* -------------------------------------------------- block-sparse attention */
+/* Which keys each query sees under a sparse_pattern, as 128 x 128 tiles.
+ * The gather of nn/sparse_attention.py:107-135 (block_selection's index and
+ * valid tables, the tail padding and the causal rule) becomes a per-query-
+ * tile list of key tiles plus a column mask per query row. Query tile t
+ * (rows [128t, 128t + 128)) visits the key tiles tile_kt[tile_ptr[t] ..
+ * tile_ptr[t + 1]); row r of entry e sees key 128*tile_kt[e] + 64h + c iff
+ * bit c of masks[(2e + h) * 128 + r] is set (h = 0, 1). All device memory. */
+typedef struct enl_sparse_layout {
+  const int32_t* tile_ptr;  /* (ceil(seq_q / 128) + 1) */
+  const int32_t* tile_kt;   /* (n_entries) */
+  const uint64_t* masks;    /* (n_entries, 2, 128) */
+  int32_t n_entries;
+} enl_sparse_layout;
+
+typedef struct enl_sparse_mask_args {
+  const int32_t* tile_ptr; /* device, as in enl_sparse_layout */
+  const int32_t* tile_kt;  /* device */
+  uint64_t* masks;         /* device out, (n_entries, 2, 128) */
+  int32_t n_entries;
+  /* block_selection's valid entries as a CSR over query blocks
+   * [qb0, qb0 + n_qblocks): query block qb0 + i selects the key blocks
+   * sel_kb[sel_ptr[i] .. sel_ptr[i + 1]) (absolute block numbers). */
+  const int32_t* sel_ptr;  /* device (n_qblocks + 1) */
+  const int32_t* sel_kb;   /* device (n_sel) */
+  int32_t n_qblocks, n_sel;
+  int64_t qb0;
+  int32_t block_size;
+  int32_t seq_q, seq_kv;
+  int64_t q_pos0, k_pos0;  /* absolute positions of query row 0 and key row 0 */
+  int32_t causal;          /* also drop keys after the query's position */
+} enl_sparse_mask_args;
+
+/* Fill the masks of a layout whose tile lists the caller built. */
+int enl_sparse_build_masks(const enl_sparse_mask_args* args, void* stream);
+
+/* Block-sparse attention: enl_attn_prefill with the keys of each query
+ * restricted to its layout. Replaces nn/sparse_attention.py:96-142 (forward)
+ * and the scores of nn/kvcache.py:263-306 (cached step, with q_pos0/k_pos0).
+ * The layout carries causality and the sequence end; args->causal only picks
+ * the ALiBi distance (signed when causal, absolute otherwise, :125-128).
+ * Needs window < 0, mask_mode ENL_MASK_EXCLUDE and kv_valid_len NULL: every
+ * row sees at least its own key, so there are no fully masked rows. */
+int enl_attn_prefill_sparse(const enl_prefill_args* args, const enl_sparse_layout* layout,
+                            void* stream);
 
 /* ------------------------------------------------------------- utilities */
 /* Read (and with clear != 0 reset) the device error word of the current

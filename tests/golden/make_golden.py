@@ -525,6 +525,114 @@ def linear_cases():
     np.savez_compressed(HERE / "linear_layers.npz", **out)
 
 
+def sparse_cases():
+    """Block-sparse attention (sparse_pattern), run by the reference in float64
+    (nn/sparse_attention.py:48-142, nn/forward.py:482-502,
+    nn/kvcache.py:263-306).
+
+    sel{i}: block_selection(index, valid) tables, random draws included.
+    core{i}: sparse_attention_forward on (B, H, S, Dh) inputs regenerated from
+        RandomState(3100 + i) (q, k, v drawn in that order), ALiBi slopes of
+        the reference's _alibi_slopes(H) when the case asks for them.
+    mha{i}: full layers with the reference's seeded weights (set_seed 3200 + i,
+        input RandomState(3300 + i)).
+    kv{i}: the reference test's stepping model (set_seed 3400 + i, tokens
+        RandomState(3500 + i)): full Forward, one-token steps, and a 5 + 4
+        split."""
+    from Enilnets.nn import sparse_attention as sa
+    from Enilnets.nn.forward import _alibi_slopes
+    out = {}
+    meta = {"sel": [], "core": [], "mha": [], "kv": []}
+    sel = [
+        ({"block_size": 3, "local": 1, "global": 1, "random": 1}, 12, True),
+        ({"block_size": 3, "local": 1, "global": 1, "random": 1}, 12, False),
+        ({"block_size": 2, "local": 1, "random": 2, "seed": 7}, 8, True),
+        ({"block_size": 16, "local": 2, "global": 2, "random": 3, "seed": 5}, 40, True),
+        ({"block_size": 16, "local": 2, "global": 2, "random": 3, "seed": 5}, 40, False),
+        ({"block_size": 4, "local": 0, "global": 0, "random": 2, "seed": 11}, 25, False),
+    ]
+    for i, (pat, nb, causal) in enumerate(sel):
+        index, valid = sa.block_selection(sa.normalize_pattern(pat), nb, causal)
+        out[f"sel{i}_index"], out[f"sel{i}_valid"] = index, valid
+        meta["sel"].append([pat, nb, causal])
+    core = [
+        dict(B=2, H=2, S=10, Dh=4, pattern={"block_size": 3, "local": 1, "global": 1,
+                                            "random": 1}, causal=False, alibi=False),
+        dict(B=2, H=2, S=10, Dh=4, pattern={"block_size": 4, "local": 1}, causal=True,
+             alibi=False),
+        dict(B=2, H=2, S=77, Dh=32, pattern={"block_size": 8, "local": 1, "global": 1,
+                                             "random": 2}, causal=True, alibi=False),
+        dict(B=1, H=3, S=300, Dh=64, pattern={"block_size": 16, "local": 2, "global": 1,
+                                              "random": 2, "seed": 4}, causal=False,
+             alibi=False),
+        dict(B=1, H=2, S=260, Dh=128, pattern={"block_size": 64, "local": 1, "global": 1},
+             causal=True, alibi=True),
+        dict(B=1, H=2, S=333, Dh=64, pattern={"block_size": 100, "local": 1, "random": 1},
+             causal=False, alibi=True),
+        dict(B=1, H=2, S=200, Dh=16, pattern={"block_size": 1, "local": 5, "global": 2},
+             causal=True, alibi=False),
+        dict(B=1, H=1, S=600, Dh=64, pattern={"block_size": 256, "local": 1}, causal=True,
+             alibi=False),
+    ]
+    for i, c in enumerate(core):
+        rs = np.random.RandomState(3100 + i)
+        shape = (c["B"], c["H"], c["S"], c["Dh"])
+        q, k, v = (rs.standard_normal(shape) for _ in range(3))
+        slopes = _alibi_slopes(c["H"]) if c["alibi"] else None
+        ctx, _ = sa.sparse_attention_forward(q, k, v, sa.normalize_pattern(c["pattern"]),
+                                             c["causal"], slopes)
+        out[f"core{i}_y"] = ctx.astype(np.float32)
+        meta["core"].append(c)
+    mha = [
+        dict(causal=True, positional_scheme="absolute", num_kv_heads=None,
+             sparse_pattern={"block_size": 8, "local": 1, "global": 1, "random": 1}),
+        dict(causal=False, positional_scheme="rope", num_kv_heads=2,
+             sparse_pattern={"block_size": 16, "local": 1, "random": 2, "seed": 3}),
+        dict(causal=True, positional_scheme="alibi", num_kv_heads=1,
+             sparse_pattern={"block_size": 5, "local": 2, "global": 1}),
+        dict(causal=False, positional_scheme="alibi", num_kv_heads=None,
+             sparse_pattern={"block_size": 12, "local": 1, "global": 2}),
+        dict(causal=True, positional_scheme="absolute", num_kv_heads=None,
+             sparse_pattern={"block_size": 40}),
+    ]
+    for i, cfg in enumerate(mha):
+        Enilnets.core.utils.set_seed(3200 + i)
+        m = NeuralNet()
+        m.add_multihead_attention(embed_dim=64, num_heads=4, **cfg)
+        x = np.random.RandomState(3300 + i).standard_normal((2, 40, 64))
+        out[f"mha{i}_y"] = m.Forward(x, training=False).astype(np.float32)
+        meta["mha"].append(cfg)
+    kv = [
+        dict(pattern={"block_size": 2, "local": 1}, scheme="absolute"),
+        dict(pattern={"block_size": 3, "local": 1, "global": 1, "random": 1}, scheme="rope"),
+        dict(pattern={"block_size": 3, "local": 1, "global": 1, "random": 1}, scheme="alibi"),
+        dict(pattern={"block_size": 4, "local": 1, "random": 2, "seed": 9}, scheme="absolute"),
+    ]
+    for i, cfg in enumerate(kv):
+        Enilnets.core.utils.set_seed(3400 + i)
+        m = NeuralNet()
+        m.add_embedding(vocab_size=13, embed_dim=32)
+        if cfg["scheme"] == "absolute":
+            m.add_positional_encoding(max_seq_len=16, learnable=False)
+        m.add_multihead_attention(embed_dim=32, num_heads=4, causal=True,
+                                  positional_scheme=cfg["scheme"],
+                                  sparse_pattern=cfg["pattern"])
+        m.add_dense(n_out=13, activation="linear")
+        toks = np.random.RandomState(3500 + i).randint(0, 13, size=(2, 9))
+        out[f"kv{i}_full"] = m.Forward(toks, training=False).astype(np.float32)
+        c1 = kvc.KVCache()
+        out[f"kv{i}_one"] = np.concatenate(
+            [kvc.cached_forward_step(m, toks[:, j:j + 1], c1) for j in range(9)],
+            axis=1).astype(np.float32)
+        c2 = kvc.KVCache()
+        out[f"kv{i}_multi"] = np.concatenate(
+            [kvc.cached_forward_step(m, toks[:, :5], c2),
+             kvc.cached_forward_step(m, toks[:, 5:], c2)], axis=1).astype(np.float32)
+        meta["kv"].append(cfg)
+    out["meta"] = np.array(json.dumps(meta))
+    np.savez_compressed(HERE / "sparse.npz", **out)
+
+
 def main():
     if len(sys.argv) > 1:
         for name in sys.argv[1:]:
@@ -540,6 +648,8 @@ def main():
     layer_b200_cases()
     config1_case()
     textgen_case()
+    linear_cases()
+    sparse_cases()
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size)
 

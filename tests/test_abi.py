@@ -23,7 +23,8 @@ def declared_functions():
 
 def test_header_declares_the_expected_entry_points():
     names = declared_functions()
-    for must in ("enl_attn_prefill", "enl_attn_decode", "enl_kv_append", "enl_kv_gather",
+    for must in ("enl_attn_prefill", "enl_attn_prefill_sparse", "enl_sparse_build_masks",
+                 "enl_attn_decode", "enl_kv_append", "enl_kv_gather",
                  "enl_lse_merge", "enl_rope_apply", "enl_last_error", "enl_device_error"):
         assert must in names
 
@@ -33,7 +34,7 @@ def test_library_exports_every_declared_symbol():
     for name in declared_functions():
         assert hasattr(lib, name), f"{name} declared in enl_attn.h but not exported"
         assert name in _native.SIGNATURES, f"{name} has no ctypes signature"
-    assert lib.enl_abi_version() == _native.ABI_VERSION == 3
+    assert lib.enl_abi_version() == _native.ABI_VERSION == 4
 
 
 def test_nm_shows_c_linkage():

@@ -67,7 +67,12 @@ def test_layer_dict_contract():
      "nothing to sparsify"),
     (dict(embed_dim=8, num_heads=2, attention_kernel="linear", tiled_block_size=4),
      "nothing to tile"),
-    (dict(embed_dim=8, num_heads=2, sparse_pattern={"block_size": 2}), "sparse_pattern"),
+    (dict(embed_dim=8, num_heads=2, sparse_pattern={"block_size": 2}, window_size=3),
+     "window_size"),
+    (dict(embed_dim=8, num_heads=2, sparse_pattern={"block_size": 2}, tiled_block_size=2),
+     "nothing to tile"),
+    (dict(embed_dim=8, num_heads=2, sparse_pattern={"block_size": 0}), "block_size >= 1"),
+    (dict(embed_dim=8, num_heads=2, sparse_pattern="local"), "must be a dict"),
 ])
 def test_builder_validation_matches_reference_errors(kwargs, match):
     with pytest.raises(ValueError, match=match):
