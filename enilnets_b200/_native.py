@@ -32,7 +32,7 @@ DEVICE_ERRORS = {1: "an mbarrier wait exceeded its time budget",
                  3: "a launch-time shape invariant was violated"}
 
 
-ABI_VERSION = 4  # ENL_ABI_VERSION of include/enl_attn.h
+ABI_VERSION = 5  # ENL_ABI_VERSION of include/enl_attn.h
 
 
 class PrefillArgs(Structure):
@@ -107,6 +107,21 @@ ENL_PHI_LINEAR = 0
 ENL_PHI_PERFORMER = 1
 
 
+class BackwardArgs(Structure):
+    """Mirror of enl_backward_args."""
+    _fields_ = [
+        ("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("o", c_void_p), ("dout", c_void_p),
+        ("lse", c_void_p), ("dq", c_void_p), ("dk", c_void_p), ("dv", c_void_p),
+        ("batch", c_int32), ("num_heads", c_int32), ("num_kv_heads", c_int32),
+        ("seq_q", c_int32), ("seq_kv", c_int32), ("head_dim", c_int32),
+    ] + [(f"{t}_stride_{d}", c_int64) for t in ("q", "k", "v", "o", "do", "dq", "dk", "dv")
+         for d in ("b", "s", "h")] + [
+        ("o_dtype", c_int32), ("causal", c_int32), ("window", c_int32),
+        ("alibi_slopes", c_void_p), ("scale", c_float),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+    ]
+
+
 class SparseLayout(Structure):
     """Mirror of enl_sparse_layout."""
     _fields_ = [("tile_ptr", c_void_p), ("tile_kt", c_void_p), ("masks", c_void_p),
@@ -149,6 +164,8 @@ SIGNATURES = {
     "enl_linear_max_features": ([], c_int32),
     "enl_linear_workspace_bytes": ([POINTER(LinearArgs)], c_size_t),
     "enl_sparse_build_masks": ([POINTER(SparseMaskArgs), c_void_p], c_int32),
+    "enl_attn_backward": ([POINTER(BackwardArgs), c_void_p], c_int32),
+    "enl_backward_workspace_bytes": ([POINTER(BackwardArgs)], c_size_t),
     "enl_attn_prefill_sparse": ([POINTER(PrefillArgs), POINTER(SparseLayout), c_void_p],
                                 c_int32),
     "enl_device_error": ([POINTER(c_int32), POINTER(c_int32), c_int32], c_int32),

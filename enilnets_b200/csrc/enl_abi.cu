@@ -305,6 +305,120 @@ int enl_attn_prefill_sparse(const enl_prefill_args* a, const enl_sparse_layout* 
   return prefill_impl(a, l, stream);
 }
 
+size_t enl_backward_workspace_bytes(const enl_backward_args* a) {
+  if (!a || a->batch < 1 || a->num_heads < 1 || a->seq_q < 1) return 0;
+  const size_t s_pad = ((size_t)a->seq_q + 127) / 128 * 128;
+  const size_t one = ((size_t)a->batch * a->num_heads * s_pad * sizeof(float) + 255) & ~size_t(255);
+  return 2 * one;
+}
+
+int enl_attn_backward(const enl_backward_args* a, void* stream) {
+  if (!a) return fail(ENL_ERR_INVALID, "enl_attn_backward: args is NULL");
+  if (!a->q || !a->k || !a->v || !a->o || !a->dout || !a->lse || !a->dq || !a->dk || !a->dv)
+    return fail(ENL_ERR_INVALID,
+                "enl_attn_backward: q, k, v, o, dout, lse, dq, dk and dv must be non-NULL");
+  if (a->batch < 1 || a->num_heads < 1 || a->num_kv_heads < 1 || a->seq_q < 1 || a->seq_kv < 1)
+    return fail(ENL_ERR_INVALID,
+                "enl_attn_backward: batch=%d num_heads=%d num_kv_heads=%d seq_q=%d seq_kv=%d "
+                "must all be >= 1",
+                a->batch, a->num_heads, a->num_kv_heads, a->seq_q, a->seq_kv);
+  if (a->num_heads % a->num_kv_heads != 0)
+    return fail(ENL_ERR_INVALID, "enl_attn_backward: num_kv_heads=%d must divide num_heads=%d",
+                a->num_kv_heads, a->num_heads);
+  if (a->head_dim < 8 || a->head_dim > 128 || a->head_dim % 8 != 0)
+    return fail(ENL_ERR_UNSUPPORTED,
+                "enl_attn_backward: head_dim=%d (supported: multiples of 8 up to 128)",
+                a->head_dim);
+  if (a->o_dtype != ENL_DTYPE_BF16 && a->o_dtype != ENL_DTYPE_FP32)
+    return fail(ENL_ERR_INVALID, "enl_attn_backward: o_dtype=%d", a->o_dtype);
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->dout))
+    return fail(ENL_ERR_INVALID, "enl_attn_backward: q, k, v, dout must be 16-byte aligned");
+  int st;
+  if ((st = check_strides_16B("q", a->q_stride_b, a->q_stride_s, a->q_stride_h, 2))) return st;
+  if ((st = check_strides_16B("k", a->k_stride_b, a->k_stride_s, a->k_stride_h, 2))) return st;
+  if ((st = check_strides_16B("v", a->v_stride_b, a->v_stride_s, a->v_stride_h, 2))) return st;
+  if ((st = check_strides_16B("dout", a->do_stride_b, a->do_stride_s, a->do_stride_h, 2)))
+    return st;
+  const long long n_kt = (a->seq_kv + 127) / 128, n_qt = (a->seq_q + 127) / 128;
+  if (n_kt * a->batch * a->num_kv_heads > (1ll << 31) - 1 ||
+      n_qt * a->batch * a->num_heads > (1ll << 31) - 1)
+    return fail(ENL_ERR_UNSUPPORTED, "enl_attn_backward: too many tiles for one launch");
+  const size_t need = enl_backward_workspace_bytes(a);
+  if (!a->workspace || a->workspace_bytes < need)
+    return fail(ENL_ERR_INVALID, "enl_attn_backward: needs a %zu-byte workspace (got %zu)", need,
+                a->workspace_bytes);
+  if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0)
+    return fail(ENL_ERR_INVALID, "enl_attn_backward: workspace must be 256-byte aligned");
+
+  CUtensorMap tq, tk, tv, tdo;
+  if ((st = make_qkv_map(&tq, a->q, a->head_dim, a->seq_q, a->num_heads, a->batch, a->q_stride_s,
+                         a->q_stride_h, a->q_stride_b, "q")))
+    return st;
+  if ((st = make_qkv_map(&tk, a->k, a->head_dim, a->seq_kv, a->num_kv_heads, a->batch,
+                         a->k_stride_s, a->k_stride_h, a->k_stride_b, "k")))
+    return st;
+  if ((st = make_qkv_map(&tv, a->v, a->head_dim, a->seq_kv, a->num_kv_heads, a->batch,
+                         a->v_stride_s, a->v_stride_h, a->v_stride_b, "v")))
+    return st;
+  if ((st = make_qkv_map(&tdo, a->dout, a->head_dim, a->seq_q, a->num_heads, a->batch,
+                         a->do_stride_s, a->do_stride_h, a->do_stride_b, "dout")))
+    return st;
+
+  const int s_pad = (int)(n_qt * 128);
+  float* lse2 = reinterpret_cast<float*>(a->workspace);
+  float* dsum = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a->workspace) + need / 2);
+  BwdPrepParams q;
+  q.B = a->batch;
+  q.H = a->num_heads;
+  q.Sq = a->seq_q;
+  q.s_pad = s_pad;
+  q.d_real = a->head_dim;
+  q.o = a->o;
+  q.o_sb = a->o_stride_b;
+  q.o_ss = a->o_stride_s;
+  q.o_sh = a->o_stride_h;
+  q.o_f32 = a->o_dtype == ENL_DTYPE_FP32;
+  q.dout = a->dout;
+  q.do_sb = a->do_stride_b;
+  q.do_ss = a->do_stride_s;
+  q.do_sh = a->do_stride_h;
+  q.lse = a->lse;
+  q.lse2 = lse2;
+  q.dsum = dsum;
+
+  BwdParams p;
+  p.B = a->batch;
+  p.H = a->num_heads;
+  p.Hkv = a->num_kv_heads;
+  p.Sq = a->seq_q;
+  p.Skv = a->seq_kv;
+  p.d_real = a->head_dim;
+  p.causal = a->causal != 0;
+  p.window = a->window < 0 ? -1 : a->window;
+  p.alibi = a->alibi_slopes;
+  p.scale = a->scale;
+  p.scale_log2 = a->scale * 1.4426950408889634f;
+  p.lse2 = lse2;
+  p.dsum = dsum;
+  p.s_pad = s_pad;
+  p.dq = a->dq;
+  p.dq_sb = a->dq_stride_b;
+  p.dq_ss = a->dq_stride_s;
+  p.dq_sh = a->dq_stride_h;
+  p.dk = a->dk;
+  p.dk_sb = a->dk_stride_b;
+  p.dk_ss = a->dk_stride_s;
+  p.dk_sh = a->dk_stride_h;
+  p.dv = a->dv;
+  p.dv_sb = a->dv_stride_b;
+  p.dv_ss = a->dv_stride_s;
+  p.dv_sh = a->dv_stride_h;
+  const int D = a->head_dim <= 64 ? 64 : 128;
+  cudaError_t e = launch_backward(tq, tk, tv, tdo, q, p, D, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "enl_attn_backward launch");
+  return ENL_OK;
+}
+
 int enl_sparse_build_masks(const enl_sparse_mask_args* a, void* stream) {
   if (!a) return fail(ENL_ERR_INVALID, "enl_sparse_build_masks: args is NULL");
   if (!a->tile_ptr || !a->tile_kt || !a->masks || !a->sel_ptr || (!a->sel_kb && a->n_sel > 0))

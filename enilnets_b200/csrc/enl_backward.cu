@@ -1,0 +1,606 @@
+// K5: attention backward on tcgen05 (nn/flash_attention.py:83-114).
+//
+// The reference recomputes each score block from Q and K, turns it into the
+// forward's probabilities with the saved row statistics, and accumulates
+//   dV += P^T dO,  dP = dO V^T,  dS = P * (dP - D) * scale,
+//   dQ += dS K,    dK += dS^T Q,  with D = rowsum(dO * O).
+// Here that is three launches:
+//   bwd_prep_kernel       D per query row and LSE in log2 units, padded to
+//                         whole 128-row tiles (pad rows: LSE +inf, so P = 0);
+//   attn_bwd_dkdv_sm100   one CTA per (batch, kv head, 128-key tile): K and V
+//                         stay in shared memory while the query tiles of
+//                         every query head of the group stream through;
+//                         S^T = K Q^T and dP^T = V dO^T in tensor memory,
+//                         P^T and dS^T written back over them as bf16, then
+//                         dV += P^T dO and dK += dS^T Q accumulate in tensor
+//                         memory (GQA sums the group's heads exactly there);
+//   attn_bwd_dq_sm100     one CTA per (batch, head, 128-query tile): Q and dO
+//                         stay, K and V stream; S and dP again, dS over S,
+//                         dQ += dS K in tensor memory.
+// Tensor memory per CTA: S (128 columns) + dP (128) + two D-column
+// accumulators, 512 columns at D = 128, so each tile's MMAs wait for the
+// previous tile's accumulation to read P and dS. Recomputing S and dP in the
+// dQ pass costs two GEMMs of seven but needs no atomics and no dQ staging.
+//
+// Warp roles (320 threads): 0-7 elementwise (warps w and w + 4 share TMEM
+// lanes 32 (w % 4) .. + 31 and split the 128 columns in halves), 8 TMA, 9 MMA.
+// Every wait is bounded (mbar_wait): on timeout a device error is recorded
+// and every role stops issuing and drains.
+#include "enl_common.cuh"
+#include "enl_kernels.h"
+
+namespace enl {
+
+// 1-D bulk copy global -> shared (no multicast), completing on an mbarrier.
+// Both addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_load_1d(void* smem_dst, const void* gsrc, uint32_t bytes,
+                                             uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+template <int D>
+struct BwdCfg {
+  static constexpr int kThreads = 320;
+  static constexpr int kAtoms = D / 64;
+  static constexpr int kAtomBytes = 128 * 128;
+  static constexpr int kTileBytes = 128 * D * 2;
+  static constexpr int kStages = 2;
+  static constexpr int kOffRes = 0;                          // resident pair of tiles
+  static constexpr int kOffStr = 2 * kTileBytes;             // streamed pairs [kStages][2]
+  static constexpr int kOffRow = kOffStr + kStages * 2 * kTileBytes;  // [kStages][2][128] f32
+  static constexpr int kOffBar = kOffRow + kStages * 2 * 128 * 4;
+  // res_full, full[kStages], empty[kStages], s_full, p_ready[2], mm_done, drain
+  static constexpr int kNumBars = 1 + 2 * kStages + 1 + 2 + 1 + 1;
+  static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+  static constexpr uint32_t kColS = 0, kColDP = 128, kColAcc0 = 256, kColAcc1 = 256 + D;
+};
+
+// Query-tile range [lo, hi) that can see key tile kt, and key-tile range that
+// query tile qt can see (causal: key <= query; window: |query - key| <= w).
+__device__ __forceinline__ void q_range_for_key_tile(const BwdParams& p, int kt, int& lo,
+                                                     int& hi) {
+  const int n_qt = (p.Sq + 127) / 128;
+  const long long j0 = (long long)kt * 128, j1 = min((long long)p.Skv, j0 + 128) - 1;
+  long long ilo = 0, ihi = (long long)p.Sq - 1;
+  if (p.causal) ilo = max(ilo, j0);
+  if (p.window >= 0) {
+    ilo = max(ilo, j0 - p.window);
+    ihi = min(ihi, j1 + p.window);
+  }
+  lo = (int)(ilo / 128);
+  hi = (ihi < ilo) ? lo : (int)min((long long)n_qt, ihi / 128 + 1);
+}
+
+__device__ __forceinline__ void k_range_for_query_tile(const BwdParams& p, int qt, int& lo,
+                                                       int& hi) {
+  const int n_kt = (p.Skv + 127) / 128;
+  const long long i0 = (long long)qt * 128, i1 = min((long long)p.Sq, i0 + 128) - 1;
+  long long jlo = 0, jhi = (long long)p.Skv - 1;
+  if (p.causal) jhi = min(jhi, i1);
+  if (p.window >= 0) {
+    jlo = max(jlo, i0 - p.window);
+    jhi = min(jhi, i1 + p.window);
+  }
+  lo = (int)(jlo / 128);
+  hi = (jhi < jlo) ? lo : (int)min((long long)n_kt, jhi / 128 + 1);
+}
+
+// P and dS of one (query i, key j) score, from the raw dot product s and the
+// raw dO.v product dp. lse2 and dsum belong to the query row.
+__device__ __forceinline__ void bwd_elem(const BwdParams& p, float s, float dp, long long i,
+                                         long long j, float slope2, float lse2, float dsum,
+                                         float& pr, float& ds) {
+  const long long diff = i - j;
+  bool ok = j < p.Skv && (!p.causal || diff >= 0);
+  if (p.window >= 0) ok = ok && (diff <= p.window && -diff <= p.window);
+  const float dist = p.causal ? (float)diff : fabsf((float)diff);
+  const float x = fmaf(s, p.scale_log2, -slope2 * dist) - lse2;
+  pr = ok ? fast_exp2(x) : 0.0f;
+  ds = pr * (dp - dsum);
+}
+
+__global__ void bwd_prep_kernel(BwdPrepParams q) {
+  const int lane = threadIdx.x % 32;
+  const long long warps = (long long)gridDim.x * (blockDim.x / 32);
+  const long long total = (long long)q.B * q.H * q.s_pad;
+  for (long long idx = blockIdx.x * (long long)(blockDim.x / 32) + threadIdx.x / 32; idx < total;
+       idx += warps) {
+    const long long bh = idx / q.s_pad;
+    const int i = (int)(idx % q.s_pad);
+    const int b = (int)(bh / q.H), h = (int)(bh % q.H);
+    if (i >= q.Sq) {
+      if (lane == 0) {
+        q.lse2[idx] = INFINITY;
+        q.dsum[idx] = 0.0f;
+      }
+      continue;
+    }
+    float acc = 0.0f;
+    const long long oo = b * q.o_sb + (long long)i * q.o_ss + h * q.o_sh;
+    const long long od = b * q.do_sb + (long long)i * q.do_ss + h * q.do_sh;
+    const __nv_bfloat16* dob = reinterpret_cast<const __nv_bfloat16*>(q.dout);
+    for (int d = lane; d < q.d_real; d += 32) {
+      const float o = q.o_f32 ? reinterpret_cast<const float*>(q.o)[oo + d]
+                              : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(q.o)[oo + d]);
+      acc = fmaf(o, __bfloat162float(dob[od + d]), acc);
+    }
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
+    if (lane == 0) {
+      q.dsum[idx] = acc;
+      q.lse2[idx] = q.lse[bh * q.Sq + i] * 1.4426950408889634f;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// dK, dV. CTA c -> key tile c / (B * Hkv) (small tiles first: under a causal
+// mask they see the most query tiles), (b, kv head) c % (B * Hkv).
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(320, 1)
+    attn_bwd_dkdv_sm100(const __grid_constant__ CUtensorMap tm_q,
+                        const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v,
+                        const __grid_constant__ CUtensorMap tm_do, const BwdParams p) {
+  using Cfg = BwdCfg<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  float* rows = reinterpret_cast<float*>(smem + Cfg::kOffRow);  // [stage][lse2 | dsum][128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
+  uint64_t* bar_res = bars;
+  uint64_t* bar_full = bar_res + 1;
+  uint64_t* bar_empty = bar_full + Cfg::kStages;
+  uint64_t* bar_s_full = bar_empty + Cfg::kStages;
+  uint64_t* bar_p_ready = bar_s_full + 1;  // [2 halves], 4 warps each
+  uint64_t* bar_mm_done = bar_p_ready + 2;
+  uint64_t* bar_drain = bar_mm_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int n_bk = p.B * p.Hkv;
+  const int kt = blockIdx.x / n_bk;
+  const int bk = blockIdx.x % n_bk;
+  const int b = bk / p.Hkv, hkv = bk % p.Hkv;
+  const int G = p.H / p.Hkv;
+  int qlo, qhi;
+  q_range_for_key_tile(p, kt, qlo, qhi);
+  const int nq = max(0, qhi - qlo);
+  const int n_units = G * nq;  // unit u: head hkv * G + u / nq, query tile qlo + u % nq
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < Cfg::kNumBars; ++i)
+      mbar_init(bars + i, (bars + i == bar_p_ready || bars + i == bar_p_ready + 1) ? 4u : 1u);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 9) {
+    tmem_alloc<512>(tmem_slot);
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------------ TMA
+    if (lane == 0 && n_units > 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_do);
+      mbar_arrive_expect_tx(bar_res, 2 * Cfg::kTileBytes);
+      for (int a = 0; a < Cfg::kAtoms; ++a) {
+        tma_load_4d(smem + Cfg::kOffRes + a * Cfg::kAtomBytes, &tm_k, bar_res, a * 64, kt * 128,
+                    hkv, b);
+        tma_load_4d(smem + Cfg::kOffRes + Cfg::kTileBytes + a * Cfg::kAtomBytes, &tm_v, bar_res,
+                    a * 64, kt * 128, hkv, b);
+      }
+      int issued = 0;
+      bool ok = true;
+      for (int u = 0; u < n_units; ++u) {
+        const int st = u % Cfg::kStages;
+        const int h = hkv * G + u / nq, qt = qlo + u % nq;
+        if (u >= Cfg::kStages) ok = mbar_wait(bar_empty + st, (u / Cfg::kStages - 1) & 1,
+                                              abort_flag, 80);
+        if (!ok) break;
+        uint8_t* dst = smem + Cfg::kOffStr + st * 2 * Cfg::kTileBytes;
+        mbar_arrive_expect_tx(bar_full + st, 2 * Cfg::kTileBytes + 2 * 512);
+        for (int a = 0; a < Cfg::kAtoms; ++a) {
+          tma_load_4d(dst + a * Cfg::kAtomBytes, &tm_q, bar_full + st, a * 64, qt * 128, h, b);
+          tma_load_4d(dst + Cfg::kTileBytes + a * Cfg::kAtomBytes, &tm_do, bar_full + st, a * 64,
+                      qt * 128, h, b);
+        }
+        const long long roff = ((long long)b * p.H + h) * p.s_pad + (long long)qt * 128;
+        bulk_load_1d(rows + st * 256, p.lse2 + roff, 512, bar_full + st);
+        bulk_load_1d(rows + st * 256 + 128, p.dsum + roff, 512, bar_full + st);
+        ++issued;
+      }
+      // Every issued load lands before the CTA may exit (bounded waits).
+      volatile int no_abort = 0;
+      mbar_wait(bar_res, 0, &no_abort, 81);
+      for (int n = max(0, issued - Cfg::kStages); n < issued; ++n)
+        mbar_wait(bar_full + n % Cfg::kStages, (n / Cfg::kStages) & 1, &no_abort, 82);
+    }
+    __syncwarp();
+  } else if (warp == 9) {
+    // ------------------------------------------------------------------ MMA
+    const uint32_t idesc_s = idesc_bf16_f32(128, 128, false);
+    const uint32_t idesc_o = idesc_bf16_f32(128, D, true);
+    const uint32_t k_lo = desc_lo(smem_u32(smem + Cfg::kOffRes), 16);
+    const uint32_t v_lo = k_lo + (Cfg::kTileBytes >> 4);
+    auto wait = [&](uint64_t* bar, uint32_t parity, int site) {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, site));
+    };
+    bool ok = n_units == 0 || wait(bar_res, 0, 83);
+    for (int u = 0; ok && u < n_units; ++u) {
+      const int st = u % Cfg::kStages;
+      ok = wait(bar_full + st, (u / Cfg::kStages) & 1, 84);
+      if (ok && u > 0) ok = wait(bar_mm_done, (u - 1) & 1, 85);  // P^T, dS^T consumed
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t sbase = smem_u32(smem + Cfg::kOffStr + st * 2 * Cfg::kTileBytes);
+      const uint32_t q_k = desc_lo(sbase, 16), o_k = q_k + (Cfg::kTileBytes >> 4);
+      const uint32_t q_mn = desc_lo(sbase, Cfg::kAtomBytes);
+      const uint32_t o_mn = q_mn + (Cfg::kTileBytes >> 4);
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint32_t off = (kk / 4) * (Cfg::kAtomBytes >> 4) + (kk % 4) * 2;
+        if (kk == 0) {
+          umma_ss_elect<false>(tmem + Cfg::kColS, k_lo + off, q_k + off, kDescHiSw128, idesc_s);
+          umma_ss_elect<false>(tmem + Cfg::kColDP, v_lo + off, o_k + off, kDescHiSw128, idesc_s);
+        } else {
+          umma_ss_elect<true>(tmem + Cfg::kColS, k_lo + off, q_k + off, kDescHiSw128, idesc_s);
+          umma_ss_elect<true>(tmem + Cfg::kColDP, v_lo + off, o_k + off, kDescHiSw128, idesc_s);
+        }
+      }
+      umma_commit_elect(bar_s_full);
+      for (int hf = 0; hf < 2 && ok; ++hf) {
+        ok = wait(bar_p_ready + hf, u & 1, 86 + hf);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint32_t boff = (hf * 4 + kk) * (2048 >> 4);  // 16 query rows per step
+          const uint32_t acc = (u > 0 || hf > 0 || kk > 0) ? 1u : 0u;
+          umma_ts_elect(tmem + Cfg::kColAcc0, tmem + Cfg::kColS + hf * 64 + kk * 8, o_mn + boff,
+                        kDescHiSw128, idesc_o, acc);  // dV += P^T dO
+          umma_ts_elect(tmem + Cfg::kColAcc1, tmem + Cfg::kColDP + hf * 64 + kk * 8,
+                        q_mn + boff, kDescHiSw128, idesc_o, acc);  // dK += dS^T Q
+        }
+      }
+      if (!ok) break;
+      umma_commit_elect(bar_empty + st);
+      umma_commit_elect(bar_mm_done);
+    }
+    umma_commit_elect(bar_drain);
+    volatile int no_abort = 0;
+    mbar_wait(bar_drain, 0, &no_abort, 88);
+  } else {
+    // ---------------------------------------------------------- elementwise
+    const int half = warp / 4, quarter = warp % 4;
+    const int rloc = quarter * 32 + lane;
+    const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+    const long long j = (long long)kt * 128 + rloc;  // this row's key
+    bool failed = false;
+    for (int u = 0; u < n_units && !failed; ++u) {
+      const int st = u % Cfg::kStages;
+      const int h = hkv * G + u / nq, qt = qlo + u % nq;
+      const float slope2 = p.alibi ? p.alibi[h] * 1.4426950408889634f : 0.0f;
+      failed = !__all_sync(0xffffffffu, mbar_wait(bar_full + st, (u / Cfg::kStages) & 1,
+                                                  abort_flag, 89));
+      if (!failed)
+        failed = !__all_sync(0xffffffffu, mbar_wait(bar_s_full, u & 1, abort_flag, 90 + half));
+      if (failed) break;
+      tc_fence_after();
+      const float* lse2 = rows + st * 256;
+      const float* dsum = lse2 + 128;
+#pragma unroll 1
+      for (int ch = 0; ch < 2; ++ch) {
+        const int c0 = 64 * half + 32 * ch;  // first query column of the chunk
+        uint32_t sr[32], dr[32], pk[16], dk[16];
+        ENL_TMEM_LD32(lane_addr + Cfg::kColS + c0, sr, 0);
+        ENL_TMEM_LD32(lane_addr + Cfg::kColDP + c0, dr, 0);
+        const long long i0 = (long long)qt * 128 + c0;
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          float p0, p1, d0, d1;
+          bwd_elem(p, __uint_as_float(sr[c]), __uint_as_float(dr[c]), i0 + c, j, slope2,
+                   lse2[c0 + c], dsum[c0 + c], p0, d0);
+          bwd_elem(p, __uint_as_float(sr[c + 1]), __uint_as_float(dr[c + 1]), i0 + c + 1, j,
+                   slope2, lse2[c0 + c + 1], dsum[c0 + c + 1], p1, d1);
+          pk[c / 2] = pack_bf16x2(p0, p1);
+          dk[c / 2] = pack_bf16x2(d0, d1);
+        }
+        // packed pairs over the chunk's own, already read, columns
+        ENL_TMEM_ST16(lane_addr + Cfg::kColS + 64 * half + 16 * ch, pk);
+        ENL_TMEM_ST16(lane_addr + Cfg::kColDP + 64 * half + 16 * ch, dk);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_p_ready + half);
+    }
+    // Epilogue: dV and dK rows of this key, this thread's half of the head dim.
+    bool ok = __all_sync(0xffffffffu, !failed && !*abort_flag);
+    if (ok && n_units > 0)
+      ok = __all_sync(0xffffffffu, mbar_wait(bar_mm_done, (n_units - 1) & 1, abort_flag, 92));
+    if (ok) {
+      tc_fence_after();
+      const bool row_ok = j < p.Skv;
+      float* dvr = p.dv + b * p.dv_sb + j * p.dv_ss + hkv * p.dv_sh;
+      float* dkr = p.dk + b * p.dk_sb + j * p.dk_ss + hkv * p.dk_sh;
+#pragma unroll 1
+      for (int c = 0; c < D / 2; c += 16) {
+        const int col0 = half * (D / 2) + c;
+        uint32_t av[16], ak[16];
+        __syncwarp();
+        if (n_units > 0) {
+          ENL_TMEM_LD16(lane_addr + Cfg::kColAcc0 + col0, av);
+          ENL_TMEM_LD16(lane_addr + Cfg::kColAcc1 + col0, ak);
+        }
+        if (row_ok)
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (col0 + e < p.d_real) {
+              dvr[col0 + e] = n_units > 0 ? __uint_as_float(av[e]) : 0.0f;
+              dkr[col0 + e] = n_units > 0 ? __uint_as_float(ak[e]) * p.scale : 0.0f;
+            }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc<512>(tmem);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// dQ. CTA c -> query tile (last first: under a causal mask it sees the most
+// key tiles), (b, head) c % (B * H).
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(320, 1)
+    attn_bwd_dq_sm100(const __grid_constant__ CUtensorMap tm_q,
+                      const __grid_constant__ CUtensorMap tm_k,
+                      const __grid_constant__ CUtensorMap tm_v,
+                      const __grid_constant__ CUtensorMap tm_do, const BwdParams p) {
+  using Cfg = BwdCfg<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
+  uint64_t* bar_res = bars;
+  uint64_t* bar_full = bar_res + 1;
+  uint64_t* bar_empty = bar_full + Cfg::kStages;
+  uint64_t* bar_s_full = bar_empty + Cfg::kStages;
+  uint64_t* bar_p_ready = bar_s_full + 1;
+  uint64_t* bar_mm_done = bar_p_ready + 2;
+  uint64_t* bar_drain = bar_mm_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int n_bh = p.B * p.H;
+  const int n_qt = (p.Sq + 127) / 128;
+  const int qt = n_qt - 1 - (int)(blockIdx.x / n_bh);
+  const int bh = blockIdx.x % n_bh;
+  const int b = bh / p.H, h = bh % p.H;
+  const int hkv = h / (p.H / p.Hkv);
+  int klo, khi;
+  k_range_for_query_tile(p, qt, klo, khi);
+  const int n_units = max(0, khi - klo);  // unit u: key tile klo + u
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < Cfg::kNumBars; ++i)
+      mbar_init(bars + i, (bars + i == bar_p_ready || bars + i == bar_p_ready + 1) ? 4u : 1u);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 9) {
+    tmem_alloc<512>(tmem_slot);
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    if (lane == 0 && n_units > 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_do);
+      mbar_arrive_expect_tx(bar_res, 2 * Cfg::kTileBytes);
+      for (int a = 0; a < Cfg::kAtoms; ++a) {
+        tma_load_4d(smem + Cfg::kOffRes + a * Cfg::kAtomBytes, &tm_q, bar_res, a * 64, qt * 128,
+                    h, b);
+        tma_load_4d(smem + Cfg::kOffRes + Cfg::kTileBytes + a * Cfg::kAtomBytes, &tm_do, bar_res,
+                    a * 64, qt * 128, h, b);
+      }
+      int issued = 0;
+      bool ok = true;
+      for (int u = 0; u < n_units; ++u) {
+        const int st = u % Cfg::kStages;
+        const int kt = klo + u;
+        if (u >= Cfg::kStages) ok = mbar_wait(bar_empty + st, (u / Cfg::kStages - 1) & 1,
+                                              abort_flag, 100);
+        if (!ok) break;
+        uint8_t* dst = smem + Cfg::kOffStr + st * 2 * Cfg::kTileBytes;
+        mbar_arrive_expect_tx(bar_full + st, 2 * Cfg::kTileBytes);
+        for (int a = 0; a < Cfg::kAtoms; ++a) {
+          tma_load_4d(dst + a * Cfg::kAtomBytes, &tm_k, bar_full + st, a * 64, kt * 128, hkv, b);
+          tma_load_4d(dst + Cfg::kTileBytes + a * Cfg::kAtomBytes, &tm_v, bar_full + st, a * 64,
+                      kt * 128, hkv, b);
+        }
+        ++issued;
+      }
+      volatile int no_abort = 0;
+      mbar_wait(bar_res, 0, &no_abort, 101);
+      for (int n = max(0, issued - Cfg::kStages); n < issued; ++n)
+        mbar_wait(bar_full + n % Cfg::kStages, (n / Cfg::kStages) & 1, &no_abort, 102);
+    }
+    __syncwarp();
+  } else if (warp == 9) {
+    const uint32_t idesc_s = idesc_bf16_f32(128, 128, false);
+    const uint32_t idesc_o = idesc_bf16_f32(128, D, true);
+    const uint32_t q_lo = desc_lo(smem_u32(smem + Cfg::kOffRes), 16);
+    const uint32_t o_lo = q_lo + (Cfg::kTileBytes >> 4);
+    auto wait = [&](uint64_t* bar, uint32_t parity, int site) {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, site));
+    };
+    bool ok = n_units == 0 || wait(bar_res, 0, 103);
+    for (int u = 0; ok && u < n_units; ++u) {
+      const int st = u % Cfg::kStages;
+      ok = wait(bar_full + st, (u / Cfg::kStages) & 1, 104);
+      if (ok && u > 0) ok = wait(bar_mm_done, (u - 1) & 1, 105);  // dS consumed
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t sbase = smem_u32(smem + Cfg::kOffStr + st * 2 * Cfg::kTileBytes);
+      const uint32_t k_k = desc_lo(sbase, 16), v_k = k_k + (Cfg::kTileBytes >> 4);
+      const uint32_t k_mn = desc_lo(sbase, Cfg::kAtomBytes);
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint32_t off = (kk / 4) * (Cfg::kAtomBytes >> 4) + (kk % 4) * 2;
+        if (kk == 0) {
+          umma_ss_elect<false>(tmem + Cfg::kColS, q_lo + off, k_k + off, kDescHiSw128, idesc_s);
+          umma_ss_elect<false>(tmem + Cfg::kColDP, o_lo + off, v_k + off, kDescHiSw128, idesc_s);
+        } else {
+          umma_ss_elect<true>(tmem + Cfg::kColS, q_lo + off, k_k + off, kDescHiSw128, idesc_s);
+          umma_ss_elect<true>(tmem + Cfg::kColDP, o_lo + off, v_k + off, kDescHiSw128, idesc_s);
+        }
+      }
+      umma_commit_elect(bar_s_full);
+      for (int hf = 0; hf < 2 && ok; ++hf) {
+        ok = wait(bar_p_ready + hf, u & 1, 106 + hf);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint32_t boff = (hf * 4 + kk) * (2048 >> 4);  // 16 key rows per step
+          const uint32_t acc = (u > 0 || hf > 0 || kk > 0) ? 1u : 0u;
+          umma_ts_elect(tmem + Cfg::kColAcc0, tmem + Cfg::kColS + hf * 64 + kk * 8, k_mn + boff,
+                        kDescHiSw128, idesc_o, acc);  // dQ += dS K
+        }
+      }
+      if (!ok) break;
+      umma_commit_elect(bar_empty + st);
+      umma_commit_elect(bar_mm_done);
+    }
+    umma_commit_elect(bar_drain);
+    volatile int no_abort = 0;
+    mbar_wait(bar_drain, 0, &no_abort, 108);
+  } else {
+    const int half = warp / 4, quarter = warp % 4;
+    const int rloc = quarter * 32 + lane;
+    const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+    const long long i = (long long)qt * 128 + rloc;  // this row's query
+    const long long roff = (long long)bh * p.s_pad + i;
+    const float lse2 = p.lse2[roff], dsum = p.dsum[roff];
+    const float slope2 = p.alibi ? p.alibi[h] * 1.4426950408889634f : 0.0f;
+    bool failed = false;
+    for (int u = 0; u < n_units && !failed; ++u) {
+      const int kt = klo + u;
+      failed = !__all_sync(0xffffffffu, mbar_wait(bar_s_full, u & 1, abort_flag, 110 + half));
+      if (failed) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int ch = 0; ch < 2; ++ch) {
+        const int c0 = 64 * half + 32 * ch;  // first key column of the chunk
+        uint32_t sr[32], dr[32], dk[16];
+        ENL_TMEM_LD32(lane_addr + Cfg::kColS + c0, sr, 0);
+        ENL_TMEM_LD32(lane_addr + Cfg::kColDP + c0, dr, 0);
+        const long long j0 = (long long)kt * 128 + c0;
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          float p0, p1, d0, d1;
+          bwd_elem(p, __uint_as_float(sr[c]), __uint_as_float(dr[c]), i, j0 + c, slope2, lse2,
+                   dsum, p0, d0);
+          bwd_elem(p, __uint_as_float(sr[c + 1]), __uint_as_float(dr[c + 1]), i, j0 + c + 1,
+                   slope2, lse2, dsum, p1, d1);
+          dk[c / 2] = pack_bf16x2(d0, d1);
+        }
+        ENL_TMEM_ST16(lane_addr + Cfg::kColS + 64 * half + 16 * ch, dk);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_p_ready + half);
+    }
+    bool ok = __all_sync(0xffffffffu, !failed && !*abort_flag);
+    if (ok && n_units > 0)
+      ok = __all_sync(0xffffffffu, mbar_wait(bar_mm_done, (n_units - 1) & 1, abort_flag, 112));
+    if (ok) {
+      tc_fence_after();
+      const bool row_ok = i < p.Sq;
+      float* dqr = p.dq + b * p.dq_sb + i * p.dq_ss + h * p.dq_sh;
+#pragma unroll 1
+      for (int c = 0; c < D / 2; c += 16) {
+        const int col0 = half * (D / 2) + c;
+        uint32_t aq[16];
+        __syncwarp();
+        if (n_units > 0) ENL_TMEM_LD16(lane_addr + Cfg::kColAcc0 + col0, aq);
+        if (row_ok)
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (col0 + e < p.d_real)
+              dqr[col0 + e] = n_units > 0 ? __uint_as_float(aq[e]) * p.scale : 0.0f;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc<512>(tmem);
+  }
+}
+
+template <int D>
+cudaError_t launch_bwd_main(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                            const CUtensorMap& tdo, const BwdParams& p, cudaStream_t stream) {
+  using Cfg = BwdCfg<D>;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    const cudaFuncAttribute a = cudaFuncAttributeMaxDynamicSharedMemorySize;
+    e = cudaFuncSetAttribute(attn_bwd_dkdv_sm100<D>, a, Cfg::kSmemBytes);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_bwd_dq_sm100<D>, a, Cfg::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  const long long n_kt = (p.Skv + 127) / 128, n_qt = (p.Sq + 127) / 128;
+  attn_bwd_dkdv_sm100<D><<<(unsigned)(n_kt * p.B * p.Hkv), Cfg::kThreads, Cfg::kSmemBytes,
+                           stream>>>(tq, tk, tv, tdo, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  attn_bwd_dq_sm100<D><<<(unsigned)(n_qt * p.B * p.H), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(
+      tq, tk, tv, tdo, p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_backward(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                            const CUtensorMap& tdo, const BwdPrepParams& prep, const BwdParams& p,
+                            int D, cudaStream_t stream) {
+  const long long rows = (long long)prep.B * prep.H * prep.s_pad;
+  const long long blocks = min((rows + 7) / 8, 148ll * 16);
+  bwd_prep_kernel<<<(int)blocks, 256, 0, stream>>>(prep);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  return D == 128 ? launch_bwd_main<128>(tq, tk, tv, tdo, p, stream)
+                  : launch_bwd_main<64>(tq, tk, tv, tdo, p, stream);
+}
+
+}  // namespace enl

@@ -53,6 +53,38 @@ cudaError_t launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const C
 cudaError_t launch_split_planes(const float* src, long long sb, long long ss, long long sh, int B,
                                 int S, int H, int D, void* dst, cudaStream_t stream);
 
+// K5 attention backward (enl_backward.cu).
+struct BwdPrepParams {
+  int B, H, Sq, s_pad, d_real;
+  const void* o;  // forward output (B, Sq, H, D), bf16 or fp32
+  long long o_sb, o_ss, o_sh;
+  int o_f32;
+  const void* dout;  // bf16 (B, Sq, H, D)
+  long long do_sb, do_ss, do_sh;
+  const float* lse;  // (B, H, Sq) natural-log LSE of the forward
+  float* lse2;       // out (B * H, s_pad): LSE * log2(e), +inf on pad rows
+  float* dsum;       // out (B * H, s_pad): rowsum(dO * O), 0 on pad rows
+};
+struct BwdParams {
+  int B, H, Hkv, Sq, Skv, d_real;
+  int causal;  // key j visible to query i only when j <= i
+  int window;  // < 0: none; else |i - j| <= window
+  const float* alibi;  // (H) slopes or null
+  float scale, scale_log2;
+  const float* lse2;
+  const float* dsum;
+  int s_pad;
+  float* dq;  // (B, Sq, H, D) fp32
+  long long dq_sb, dq_ss, dq_sh;
+  float* dk;  // (B, Skv, Hkv, D) fp32, summed over each kv head's query heads
+  long long dk_sb, dk_ss, dk_sh;
+  float* dv;
+  long long dv_sb, dv_ss, dv_sh;
+};
+cudaError_t launch_backward(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                            const CUtensorMap& tdo, const BwdPrepParams& prep, const BwdParams& p,
+                            int D, cudaStream_t stream);
+
 // Column masks of a block-sparse layout (enl_sparse.cu).
 struct SparseMaskParams {
   const int* tile_ptr;  // (n_qtiles + 1) entry ranges per query tile

@@ -9,3 +9,4 @@
 #include "enl_selftest.cu"
 #include "enl_linear.cu"
 #include "enl_sparse.cu"
+#include "enl_backward.cu"

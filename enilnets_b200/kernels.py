@@ -131,6 +131,65 @@ def attention_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     return (out, lse) if return_lse else out
 
 
+def attention_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor,
+                       lse: torch.Tensor, dout: torch.Tensor, *, causal: bool = False,
+                       window: Optional[int] = None,
+                       alibi_slopes: Optional[torch.Tensor] = None,
+                       scale: Optional[float] = None):
+    """dQ, dK, dV of attention_prefill (K5, nn/flash_attention.py:83-114).
+
+    q: (B, Sq, H, D), k, v: (B, Skv, Hkv, D), dout like o: bf16 (the forward's
+    operands); o: the forward output, bf16 or fp32; lse: (B, H, Sq) fp32 from
+    attention_prefill(..., return_lse=True). Returns fp32 dq (B, Sq, H, D) and
+    dk, dv (B, Skv, Hkv, D), dk/dv summed over each kv head's query heads.
+    """
+    for name, t in (("q", q), ("k", k), ("v", v), ("dout", dout)):
+        _require_cuda(name, t, torch.bfloat16)
+        if t.dim() != 4:
+            raise ValueError(f"{name} must be 4-D (batch, seq, heads, head_dim)")
+    _require_cuda("o", o)
+    if o.dtype not in _DTYPES:
+        raise ValueError(f"o must be bfloat16 or float32 (got {o.dtype})")
+    B, Sq, H, D = q.shape
+    Bk, Skv, Hkv, Dk = k.shape
+    if tuple(v.shape) != (Bk, Skv, Hkv, Dk) or Bk != B or Dk != D:
+        raise ValueError(f"shape mismatch: q {tuple(q.shape)}, k {tuple(k.shape)}, "
+                         f"v {tuple(v.shape)}")
+    if tuple(o.shape) != (B, Sq, H, D) or tuple(dout.shape) != (B, Sq, H, D):
+        raise ValueError(f"o and dout must be {(B, Sq, H, D)}")
+    _require_cuda("lse", lse, torch.float32, last_contiguous=False)
+    if tuple(lse.shape) != (B, H, Sq) or not lse.is_contiguous():
+        raise ValueError(f"lse must be a contiguous float32 {(B, H, Sq)} tensor")
+    if alibi_slopes is not None:
+        _require_cuda("alibi_slopes", alibi_slopes, torch.float32, last_contiguous=False)
+        if tuple(alibi_slopes.shape) != (H,) or not alibi_slopes.is_contiguous():
+            raise ValueError(f"alibi_slopes must be a contiguous float32 ({H},) tensor")
+    dq = torch.empty((B, Sq, H, D), device=q.device, dtype=torch.float32)
+    dk = torch.empty((B, Skv, Hkv, D), device=q.device, dtype=torch.float32)
+    dv = torch.empty((B, Skv, Hkv, D), device=q.device, dtype=torch.float32)
+    a = nat.BackwardArgs()
+    a.q, a.k, a.v, a.o, a.dout = (t.data_ptr() for t in (q, k, v, o, dout))
+    a.lse, a.dq, a.dk, a.dv = lse.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr()
+    a.batch, a.num_heads, a.num_kv_heads = B, H, Hkv
+    a.seq_q, a.seq_kv, a.head_dim = Sq, Skv, D
+    for name, t in (("q", q), ("k", k), ("v", v), ("o", o), ("do", dout), ("dq", dq),
+                    ("dk", dk), ("dv", dv)):
+        setattr(a, f"{name}_stride_b", t.stride(0))
+        setattr(a, f"{name}_stride_s", t.stride(1))
+        setattr(a, f"{name}_stride_h", t.stride(2))
+    a.o_dtype = _DTYPES[o.dtype]
+    a.causal = int(bool(causal))
+    a.window = -1 if window is None else int(window)
+    a.alibi_slopes = _ptr(alibi_slopes)
+    a.scale = 1.0 / math.sqrt(D) if scale is None else float(scale)
+    lib = nat.load()
+    need = int(lib.enl_backward_workspace_bytes(ctypes.byref(a)))
+    ws = torch.empty(need, dtype=torch.uint8, device=q.device)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), need
+    nat.check(lib.enl_attn_backward(ctypes.byref(a), _stream()), "enl_attn_backward")
+    return dq, dk, dv
+
+
 def sparse_build_masks(tile_ptr: torch.Tensor, tile_kt: torch.Tensor, masks: torch.Tensor,
                        sel_ptr: torch.Tensor, sel_kb: torch.Tensor, *, qb0: int,
                        block_size: int, seq_q: int, seq_kv: int, q_pos0: int, k_pos0: int,

@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define ENL_ABI_VERSION 4
+#define ENL_ABI_VERSION 5
 
 /* Status codes. The Python binding maps INVALID/UNSUPPORTED to ValueError
  * (the reference raises ValueError for bad layer configurations,
@@ -241,6 +241,47 @@ int enl_linear_max_features(void);
  * calls long enough to run in parallel sequence segments keep one partial
  * state per segment; 0 otherwise. */
 size_t enl_linear_workspace_bytes(const enl_linear_args* args);
+
+/* --------------------------------------------------------------- backward */
+typedef struct enl_backward_args {
+  const void* q;    /* bf16 (batch, seq_q, num_heads, head_dim), as given to the forward */
+  const void* k;    /* bf16 (batch, seq_kv, num_kv_heads, head_dim) */
+  const void* v;    /* bf16 (batch, seq_kv, num_kv_heads, head_dim) */
+  const void* o;    /* forward output (batch, seq_q, num_heads, head_dim), o_dtype */
+  const void* dout; /* bf16 gradient of o, same shape */
+  const float* lse; /* (batch, num_heads, seq_q) natural-log LSE from enl_attn_prefill */
+  float* dq;        /* fp32 (batch, seq_q, num_heads, head_dim) */
+  float* dk;        /* fp32 (batch, seq_kv, num_kv_heads, head_dim), summed over the group */
+  float* dv;        /* fp32, as dk */
+  int32_t batch, num_heads, num_kv_heads, seq_q, seq_kv, head_dim;
+  int64_t q_stride_b, q_stride_s, q_stride_h; /* element strides */
+  int64_t k_stride_b, k_stride_s, k_stride_h;
+  int64_t v_stride_b, v_stride_s, v_stride_h;
+  int64_t o_stride_b, o_stride_s, o_stride_h;
+  int64_t do_stride_b, do_stride_s, do_stride_h;
+  int64_t dq_stride_b, dq_stride_s, dq_stride_h;
+  int64_t dk_stride_b, dk_stride_s, dk_stride_h;
+  int64_t dv_stride_b, dv_stride_s, dv_stride_h;
+  int32_t o_dtype;           /* ENL_DTYPE_BF16 or ENL_DTYPE_FP32 */
+  int32_t causal;            /* as in the forward; query and key positions both start at 0 */
+  int32_t window;            /* < 0: none */
+  const float* alibi_slopes; /* device (num_heads,) or NULL */
+  float scale;               /* the forward's softmax scale */
+  void* workspace;           /* >= enl_backward_workspace_bytes(), 256-byte aligned */
+  size_t workspace_bytes;
+} enl_backward_args;
+
+/* Attention backward: dQ, dK, dV of softmax(Q K^T * scale + bias + mask) V
+ * from dO, recomputing the probabilities from the forward's LSE, as
+ * nn/flash_attention.py:83-114 does with its row statistics. bf16 operands,
+ * fp32 accumulation and outputs; head_dim a multiple of 8 up to 128. With
+ * GQA, dK and dV of a kv head sum its query heads (the adjoint of the
+ * reference's _repeat_kv, nn/forward.py:165-171). */
+int enl_attn_backward(const enl_backward_args* args, void* stream);
+
+/* Workspace bytes enl_attn_backward needs: two fp32 rows per query, padded
+ * to whole 128-row tiles. */
+size_t enl_backward_workspace_bytes(const enl_backward_args* args);
 
 /* -------------------------------------------------- block-sparse attention */
 /* Which keys each query sees under a sparse_pattern, as 128 x 128 tiles.

@@ -17,6 +17,7 @@ paths relative to the reference package):
 * cross attention                  nn/forward.py:557-591
 * one-token cached step            nn/kvcache.py:156-213
 * KVCache reorder                  nn/kvcache.py:42-66
+* attention backward (dQ, dK, dV)  nn/flash_attention.py:83-114
 
 Parity is pinned: tests/test_oracle_golden.py checks every function here
 against golden vectors produced by running the reference itself
@@ -173,6 +174,44 @@ def flash_attention_ref(Qh, Kh, Vh, block_size, causal=False, window=None, slope
         out = out * rescale + np.matmul(p, Vh[:, :, start:stop])
         row_max = new_max
     return out / row_sum, row_max, row_sum
+
+
+def attention_backward_ref(q, k, v, dout, *, causal=False, window=None, alibi=None,
+                           scale=None):
+    """Gradients of attention_ref's output in float64, as
+    nn/flash_attention.py:83-114 forms them: P from the -1e9-masked scores,
+    dV = P^T dO, dP = dO V^T, dS = P (dP - rowsum(dO * O)) scale,
+    dQ = dS K, dK = dS^T Q. q/dout (B, Sq, H, D), k/v (B, Skv, Hkv, D); dK and
+    dV of a kv head sum its query heads (the adjoint of the repeat,
+    nn/forward.py:165-171). Returns (dq, dk, dv) in the inputs' layouts."""
+    q, k, v, dout = (np.asarray(t, np.float64) for t in (q, k, v, dout))
+    B, Sq, H, D = q.shape
+    Skv, Hkv = k.shape[1], k.shape[2]
+    rep = H // Hkv
+    scale = 1.0 / math.sqrt(D) if scale is None else scale
+    q_pos, k_pos = np.arange(Sq), np.arange(Skv)
+    bias = np.where(_blocked(q_pos, k_pos, causal, window), MASK_VALUE, 0.0)
+    dist = q_pos[:, None] - k_pos[None, :]
+    dist = dist if causal else np.abs(dist)
+    dq = np.zeros_like(q)
+    dk = np.zeros_like(k)
+    dv = np.zeros_like(v)
+    for b in range(B):
+        for h in range(H):
+            kh, vh = k[b, :, h // rep], v[b, :, h // rep]
+            s = (q[b, :, h] @ kh.T) * scale + bias
+            if alibi is not None:
+                s = s - alibi[h] * dist
+            e = np.exp(s - s.max(axis=-1, keepdims=True))
+            pr = e / e.sum(axis=-1, keepdims=True)
+            o = pr @ vh
+            g = dout[b, :, h]
+            dv[b, :, h // rep] += pr.T @ g
+            dp = g @ vh.T
+            ds = pr * (dp - np.sum(g * o, axis=-1, keepdims=True)) * scale
+            dq[b, :, h] = ds @ kh
+            dk[b, :, h // rep] += ds.T @ q[b, :, h]
+    return dq, dk, dv
 
 
 def decode_ref(q, k_cache, v_cache, *, slot_begin, slot_end, pos_slot0, q_pos,

@@ -633,6 +633,35 @@ def sparse_cases():
     np.savez_compressed(HERE / "sparse.npz", **out)
 
 
+def flash_backward_cases():
+    """nn/flash_attention.py:83-114 (flash_attention_backward) after its
+    forward, on (B, H, S, Dh) inputs regenerated from RandomState(4000 + i)
+    (q, k, v, dout drawn in that order); dQ, dK, dV stored as float32."""
+    out = {}
+    meta = []
+    cases = []
+    for causal in (False, True):
+        for window in (None, 3):
+            for alibi in (False, True):
+                cases.append(dict(B=2, H=2, S=11, Dh=8, causal=causal, window=window,
+                                  alibi=alibi, block=4))
+    cases.append(dict(B=1, H=2, S=150, Dh=64, causal=True, window=None, alibi=True, block=32))
+    cases.append(dict(B=1, H=1, S=140, Dh=128, causal=False, window=40, alibi=False, block=64))
+    for i, c in enumerate(cases):
+        rs = np.random.RandomState(4000 + i)
+        shape = (c["B"], c["H"], c["S"], c["Dh"])
+        Q, K, V, dO = (rs.standard_normal(shape) for _ in range(4))
+        slopes = Enilnets.nn.forward._alibi_slopes(c["H"]) if c["alibi"] else None
+        _, cache = fa.flash_attention_forward(Q, K, V, c["block"], c["causal"], c["window"],
+                                              slopes)
+        dq, dk, dv = fa.flash_attention_backward(dO, cache)
+        out[f"dq{i}"], out[f"dk{i}"], out[f"dv{i}"] = (t.astype(np.float32)
+                                                       for t in (dq, dk, dv))
+        meta.append(c)
+    out["meta"] = np.array(json.dumps(meta))
+    np.savez_compressed(HERE / "flash_backward.npz", **out)
+
+
 def main():
     if len(sys.argv) > 1:
         for name in sys.argv[1:]:
@@ -650,6 +679,7 @@ def main():
     textgen_case()
     linear_cases()
     sparse_cases()
+    flash_backward_cases()
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size)
 

@@ -1,0 +1,87 @@
+"""Attention backward (K5, enl_backward.cu) on the GPU.
+
+dQ, dK, dV from the forward's LSE against the float64 oracle
+(oracle/attention_ref.attention_backward_ref) on the bf16 values the kernels
+read, and against the reference's own flash_attention_backward outputs
+(tests/golden/flash_backward.npz). bf16 operands with fp32 accumulation:
+max abs error <= 2e-2 relative to the gradient's largest magnitude (the
+north-star bar for bf16 inputs)."""
+import json
+
+import numpy as np
+import pytest
+
+from oracle import attention_ref as ar
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+def _np(t):
+    return t.float().cpu().numpy().astype(np.float64)
+
+
+def _run(cuda, q, k, v, do, causal, window, slopes):
+    import torch
+    from enilnets_b200 import kernels, _native
+    qt, kt, vt, dot = (torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+                       .to(torch.bfloat16) for a in (q, k, v, do))
+    sl = torch.tensor(slopes, dtype=torch.float32, device=cuda) if slopes is not None else None
+    o, lse = kernels.attention_prefill(qt, kt, vt, causal=causal, window=window,
+                                       alibi_slopes=sl, out_dtype=torch.float32,
+                                       return_lse=True)
+    dq, dk, dv = kernels.attention_backward(qt, kt, vt, o, lse, dot, causal=causal,
+                                            window=window, alibi_slopes=sl)
+    torch.cuda.synchronize()
+    _native.raise_on_device_error()
+    return (qt, kt, vt, dot), (dq, dk, dv)
+
+
+def _check(got, ref, what):
+    for name, g, r in zip(("dq", "dk", "dv"), got, ref):
+        err = np.max(np.abs(_np(g) - r))
+        assert err <= TOL * max(1.0, np.abs(r).max()), (what, name, err, np.abs(r).max())
+
+
+CASES = [
+    # B, S, H, Hkv, D, causal, window, alibi
+    (1, 128, 1, 1, 64, False, None, False),
+    (2, 300, 2, 2, 64, True, None, False),
+    (1, 517, 4, 2, 128, True, None, True),
+    (1, 700, 2, 1, 128, False, 100, False),
+    (2, 257, 3, 3, 32, False, None, True),
+    (1, 1024, 2, 2, 128, True, 300, False),
+    (1, 200, 8, 1, 16, True, None, False),
+]
+
+
+@pytest.mark.parametrize("B,S,H,Hkv,D,causal,window,alibi", CASES)
+def test_backward_matches_oracle(cuda, B, S, H, Hkv, D, causal, window, alibi):
+    rs = np.random.RandomState(S + D + H)
+    q = rs.standard_normal((B, S, H, D))
+    k = rs.standard_normal((B, S, Hkv, D))
+    v = rs.standard_normal((B, S, Hkv, D))
+    do = rs.standard_normal((B, S, H, D))
+    slopes = ar.alibi_slopes(H) if alibi else None
+    ins, got = _run(cuda, q, k, v, do, causal, window, slopes)
+    qn, kn, vn, don = (_np(t) for t in ins)  # the values the kernels saw
+    ref = ar.attention_backward_ref(qn, kn, vn, don, causal=causal, window=window,
+                                    alibi=slopes)
+    _check(got, ref, (B, S, H, Hkv, D, causal, window, alibi))
+
+
+def test_backward_matches_reference(cuda, golden_dir):
+    data = np.load(golden_dir / "flash_backward.npz")
+    meta = json.loads(str(data["meta"]))
+    for i, c in enumerate(meta):
+        rs = np.random.RandomState(4000 + i)
+        shape = (c["B"], c["H"], c["S"], c["Dh"])
+        q, k, v, do = (rs.standard_normal(shape).transpose(0, 2, 1, 3) for _ in range(4))
+        slopes = ar.alibi_slopes(c["H"]) if c["alibi"] else None
+        _, got = _run(cuda, q, k, v, do, c["causal"], c["window"], slopes)
+        ref = [data[f"{n}{i}"].transpose(0, 2, 1, 3).astype(np.float64)
+               for n in ("dq", "dk", "dv")]
+        # the reference ran on float64 inputs; the kernels read them as bf16
+        for name, g, r in zip(("dq", "dk", "dv"), got, ref):
+            err = np.max(np.abs(_np(g) - r))
+            assert err <= 3 * TOL * max(1.0, np.abs(r).max()), (c, name, err)
