@@ -23,6 +23,7 @@ Also measured in the same run (sub-objects of the line):
                   NumPy-facing Forward on the fp32 split-bf16 path.
   sparse_attention -- sparse_pattern (block-sparse, K1's sparse mode), B4
                   S16384 H16 D128 causal bf16, beside the dense causal kernel
+  backward     -- dQ, dK, dV (K5) of the causal B4 S4096 H16 D128 bf16 forward
   linear_attention -- the attention_kernel="linear" and "performer" options
                   (feature maps + causal linear attention, K4), B4 S4096 H16
                   D64 per GPU, fp32 on the CUDA cores.
@@ -490,6 +491,37 @@ def bench_linear(dist: Dist, clocks: ClockSampler, warmup: int, steps: int = 10)
     return res
 
 
+def bench_backward(dist: Dist, clocks: ClockSampler, warmup: int, steps: int = 10):
+    """Attention backward (K5): dQ, dK, dV of the causal cfg2-shaped forward
+    (B4 S4096 H16 D128 per GPU, bf16, no padding) from its LSE. FLOPs follow
+    the usual convention for a flash backward, 10 D per allowed pair (five
+    GEMMs); the kernels issue 14 D (S and dP are recomputed in the dQ pass),
+    reported as tensor_TFLOP_s."""
+    import torch
+    from enilnets_b200 import kernels, _native
+    B, S, H, D = 4, 4096, 16, 128
+    g = torch.Generator(device=dist.device).manual_seed(8000 + dist.rank)
+    q, k, v, do = (torch.randn((B, S, H, D), generator=g, device=dist.device)
+                   .to(torch.bfloat16) for _ in range(4))
+    o, lse = kernels.attention_prefill(q, k, v, causal=True, out_dtype=torch.bfloat16,
+                                       return_lse=True)
+
+    def step():
+        kernels.attention_backward(q, k, v, o, lse, do, causal=True)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    _native.raise_on_device_error()
+    ms = timed(dist, clocks, step, steps) / steps
+    pairs = B * H * S * (S + 1) / 2
+    tf = dist.sum(10.0 * D * pairs) / (ms * 1e-3) / 1e12
+    peak = float(load_peaks()[0]["bf16_tflops"])
+    return {"ms_per_step": ms, "TFLOP_s": tf, "frac_of_bf16_peak_per_gpu": tf / dist.world / peak,
+            "tensor_TFLOP_s": tf * 1.4,
+            "config": f"B{B}/GPU S{S} H{H} D{D} causal bf16; dQ, dK, dV (fp32) from dO and LSE"}
+
+
 SPARSE_PATTERNS = {
     "bs128": {"block_size": 128, "local": 2, "global": 1, "random": 2},
     "bs64": {"block_size": 64, "local": 3, "global": 2, "random": 3},
@@ -673,7 +705,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--skip-sub", action="store_true", help="headline only")
     ap.add_argument("--only", choices=["all", "prefill", "decode", "longctx", "cross", "layer",
-                                       "linear", "sparse"],
+                                       "linear", "sparse", "backward"],
                     default="all",
                     help="profiling: run one workload")
     ap.add_argument("--batch", type=int, default=0, help="profiling: prefill batch override")
@@ -706,6 +738,8 @@ def main():
                 res = bench_linear(dist, clocks, args.warmup)
             elif args.only == "sparse":
                 res = bench_sparse(dist, clocks, args.warmup)
+            elif args.only == "backward":
+                res = bench_backward(dist, clocks, args.warmup)
             elif args.only == "layer":
                 res = {"layer_cfg2": bench_layer_cfg2(dist, clocks, args.warmup),
                        "layer_cfg1": bench_layer_cfg1(dist, args.warmup)}
@@ -724,6 +758,7 @@ def main():
             sub["cross_cfg4"] = bench_cross_cfg4(dist, clocks, args.warmup)
             sub["linear_attention"] = bench_linear(dist, clocks, args.warmup)
             sub["sparse_attention"] = bench_sparse(dist, clocks, args.warmup)
+            sub["backward"] = bench_backward(dist, clocks, args.warmup)
             sub["layer_cfg2"] = bench_layer_cfg2(dist, clocks, args.warmup)
             sub["layer_cfg1"] = bench_layer_cfg1(dist, args.warmup)
     finally:

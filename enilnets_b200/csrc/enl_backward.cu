@@ -306,18 +306,40 @@ __global__ void __launch_bounds__(320, 1)
       for (int ch = 0; ch < 2; ++ch) {
         const int c0 = 64 * half + 32 * ch;  // first query column of the chunk
         uint32_t sr[32], dr[32], pk[16], dk[16];
-        ENL_TMEM_LD32(lane_addr + Cfg::kColS + c0, sr, 0);
-        ENL_TMEM_LD32(lane_addr + Cfg::kColDP + c0, dr, 0);
+        ENL_TMEM_LD32X2(lane_addr + Cfg::kColS + c0, sr, lane_addr + Cfg::kColDP + c0, dr);
         const long long i0 = (long long)qt * 128 + c0;
+        // Every (query, key) of the chunk visible and no bias: P needs only
+        // the column's LSE (queries past Sq carry +inf there, so P = 0).
+        const bool open = slope2 == 0.0f && j < p.Skv && (!p.causal || j <= i0) &&
+                          (p.window < 0 || (i0 + 31 - j <= p.window && j - i0 <= p.window));
+        if (open) {
+          const float4* l4 = reinterpret_cast<const float4*>(lse2 + c0);
+          const float4* d4 = reinterpret_cast<const float4*>(dsum + c0);
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          float p0, p1, d0, d1;
-          bwd_elem(p, __uint_as_float(sr[c]), __uint_as_float(dr[c]), i0 + c, j, slope2,
-                   lse2[c0 + c], dsum[c0 + c], p0, d0);
-          bwd_elem(p, __uint_as_float(sr[c + 1]), __uint_as_float(dr[c + 1]), i0 + c + 1, j,
-                   slope2, lse2[c0 + c + 1], dsum[c0 + c + 1], p1, d1);
-          pk[c / 2] = pack_bf16x2(p0, p1);
-          dk[c / 2] = pack_bf16x2(d0, d1);
+          for (int c = 0; c < 32; c += 4) {
+            const float4 L = l4[c / 4], Dd = d4[c / 4];
+            const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c]), p.scale_log2, -L.x));
+            const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c + 1]), p.scale_log2, -L.y));
+            const float p2 = fast_exp2(fmaf(__uint_as_float(sr[c + 2]), p.scale_log2, -L.z));
+            const float p3 = fast_exp2(fmaf(__uint_as_float(sr[c + 3]), p.scale_log2, -L.w));
+            pk[c / 2] = pack_bf16x2(p0, p1);
+            pk[c / 2 + 1] = pack_bf16x2(p2, p3);
+            dk[c / 2] = pack_bf16x2(p0 * (__uint_as_float(dr[c]) - Dd.x),
+                                    p1 * (__uint_as_float(dr[c + 1]) - Dd.y));
+            dk[c / 2 + 1] = pack_bf16x2(p2 * (__uint_as_float(dr[c + 2]) - Dd.z),
+                                        p3 * (__uint_as_float(dr[c + 3]) - Dd.w));
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            float p0, p1, d0, d1;
+            bwd_elem(p, __uint_as_float(sr[c]), __uint_as_float(dr[c]), i0 + c, j, slope2,
+                     lse2[c0 + c], dsum[c0 + c], p0, d0);
+            bwd_elem(p, __uint_as_float(sr[c + 1]), __uint_as_float(dr[c + 1]), i0 + c + 1, j,
+                     slope2, lse2[c0 + c + 1], dsum[c0 + c + 1], p1, d1);
+            pk[c / 2] = pack_bf16x2(p0, p1);
+            dk[c / 2] = pack_bf16x2(d0, d1);
+          }
         }
         // packed pairs over the chunk's own, already read, columns
         ENL_TMEM_ST16(lane_addr + Cfg::kColS + 64 * half + 16 * ch, pk);
@@ -517,17 +539,28 @@ __global__ void __launch_bounds__(320, 1)
       for (int ch = 0; ch < 2; ++ch) {
         const int c0 = 64 * half + 32 * ch;  // first key column of the chunk
         uint32_t sr[32], dr[32], dk[16];
-        ENL_TMEM_LD32(lane_addr + Cfg::kColS + c0, sr, 0);
-        ENL_TMEM_LD32(lane_addr + Cfg::kColDP + c0, dr, 0);
+        ENL_TMEM_LD32X2(lane_addr + Cfg::kColS + c0, sr, lane_addr + Cfg::kColDP + c0, dr);
         const long long j0 = (long long)kt * 128 + c0;
+        const bool open = slope2 == 0.0f && j0 + 31 < p.Skv && (!p.causal || j0 + 31 <= i) &&
+                          (p.window < 0 || (i - j0 <= p.window && j0 + 31 - i <= p.window));
+        if (open) {
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          float p0, p1, d0, d1;
-          bwd_elem(p, __uint_as_float(sr[c]), __uint_as_float(dr[c]), i, j0 + c, slope2, lse2,
-                   dsum, p0, d0);
-          bwd_elem(p, __uint_as_float(sr[c + 1]), __uint_as_float(dr[c + 1]), i, j0 + c + 1,
-                   slope2, lse2, dsum, p1, d1);
-          dk[c / 2] = pack_bf16x2(d0, d1);
+          for (int c = 0; c < 32; c += 2) {
+            const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c]), p.scale_log2, -lse2));
+            const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c + 1]), p.scale_log2, -lse2));
+            dk[c / 2] = pack_bf16x2(p0 * (__uint_as_float(dr[c]) - dsum),
+                                    p1 * (__uint_as_float(dr[c + 1]) - dsum));
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            float p0, p1, d0, d1;
+            bwd_elem(p, __uint_as_float(sr[c]), __uint_as_float(dr[c]), i, j0 + c, slope2, lse2,
+                     dsum, p0, d0);
+            bwd_elem(p, __uint_as_float(sr[c + 1]), __uint_as_float(dr[c + 1]), i, j0 + c + 1,
+                     slope2, lse2, dsum, p1, d1);
+            dk[c / 2] = pack_bf16x2(d0, d1);
+          }
         }
         ENL_TMEM_ST16(lane_addr + Cfg::kColS + 64 * half + 16 * ch, dk);
       }

@@ -309,6 +309,16 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
       : "r"(taddr)                                                                           \
       : "memory")
 
+// Two 32-column loads (from two addresses) under one wait.
+#define ENL_TMEM_LD32X2(ta, a, tb, b)                                                        \
+  asm volatile(                                                                              \
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%64];\n\t" \
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%65];\n\t" \
+      "tcgen05.wait::ld.sync.aligned;"                                                       \
+      : ENL_R32(a, 0), ENL_R32(b, 0)                                                         \
+      : "r"(ta), "r"(tb)                                                                     \
+      : "memory")
+
 // 128 consecutive columns in one instruction (a full 128-key score row).
 #define ENL_TMEM_LD128(taddr, a)                                                             \
   asm volatile(                                                                              \
