@@ -18,8 +18,11 @@
 //                         stay, K and V stream; S and dP again, dS over S,
 //                         dQ += dS K in tensor memory.
 // Tensor memory per CTA: S (128 columns) + dP (128) + two D-column
-// accumulators, 512 columns at D = 128, so each tile's MMAs wait for the
-// previous tile's accumulation to read P and dS. Recomputing S and dP in the
+// accumulators, 512 columns at D = 128: no room for a second S. Instead each
+// tile is split into two 64-column halves with their own barriers, and the
+// next tile's S and dP of half h are computed as soon as this tile's
+// accumulation of half h has read its P and dS, so the tensor pipe works
+// while the other half's elementwise warps run. Recomputing S and dP in the
 // dQ pass costs two GEMMs of seven but needs no atomics and no dQ staging.
 //
 // Warp roles (320 threads): 0-7 elementwise (warps w and w + 4 share TMEM
@@ -53,8 +56,8 @@ struct BwdCfg {
   static constexpr int kOffStr = 2 * kTileBytes;             // streamed pairs [kStages][2]
   static constexpr int kOffRow = kOffStr + kStages * 2 * kTileBytes;  // [kStages][2][128] f32
   static constexpr int kOffBar = kOffRow + kStages * 2 * 128 * 4;
-  // res_full, full[kStages], empty[kStages], s_full, p_ready[2], mm_done, drain
-  static constexpr int kNumBars = 1 + 2 * kStages + 1 + 2 + 1 + 1;
+  // res_full, full[kStages], empty[kStages], s_full[2], p_ready[2], done[2], drain
+  static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 2 + 1;
   static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
   static constexpr uint32_t kColS = 0, kColDP = 128, kColAcc0 = 256, kColAcc1 = 256 + D;
@@ -157,10 +160,10 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* bar_res = bars;
   uint64_t* bar_full = bar_res + 1;
   uint64_t* bar_empty = bar_full + Cfg::kStages;
-  uint64_t* bar_s_full = bar_empty + Cfg::kStages;
-  uint64_t* bar_p_ready = bar_s_full + 1;  // [2 halves], 4 warps each
-  uint64_t* bar_mm_done = bar_p_ready + 2;
-  uint64_t* bar_drain = bar_mm_done + 1;
+  uint64_t* bar_s_full = bar_empty + Cfg::kStages;  // [2 halves]
+  uint64_t* bar_p_ready = bar_s_full + 2;           // [2 halves], 4 warps each
+  uint64_t* bar_done = bar_p_ready + 2;             // [2 halves] accumulation read P, dS
+  uint64_t* bar_drain = bar_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -232,53 +235,76 @@ __global__ void __launch_bounds__(320, 1)
     __syncwarp();
   } else if (warp == 9) {
     // ------------------------------------------------------------------ MMA
-    const uint32_t idesc_s = idesc_bf16_f32(128, 128, false);
+    const uint32_t idesc_s = idesc_bf16_f32(128, 64, false);  // one 64-query half
     const uint32_t idesc_o = idesc_bf16_f32(128, D, true);
     const uint32_t k_lo = desc_lo(smem_u32(smem + Cfg::kOffRes), 16);
     const uint32_t v_lo = k_lo + (Cfg::kTileBytes >> 4);
     auto wait = [&](uint64_t* bar, uint32_t parity, int site) {
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, site));
     };
-    bool ok = n_units == 0 || wait(bar_res, 0, 83);
-    for (int u = 0; ok && u < n_units; ++u) {
-      const int st = u % Cfg::kStages;
-      ok = wait(bar_full + st, (u / Cfg::kStages) & 1, 84);
-      if (ok && u > 0) ok = wait(bar_mm_done, (u - 1) & 1, 85);  // P^T, dS^T consumed
-      if (!ok) break;
-      tc_fence_after();
-      const uint32_t sbase = smem_u32(smem + Cfg::kOffStr + st * 2 * Cfg::kTileBytes);
-      const uint32_t q_k = desc_lo(sbase, 16), o_k = q_k + (Cfg::kTileBytes >> 4);
-      const uint32_t q_mn = desc_lo(sbase, Cfg::kAtomBytes);
-      const uint32_t o_mn = q_mn + (Cfg::kTileBytes >> 4);
+    auto stage = [&](int u) {
+      return smem_u32(smem + Cfg::kOffStr + (u % Cfg::kStages) * 2 * Cfg::kTileBytes);
+    };
+    // S^T and dP^T of query half h of unit u: K Q_h^T and V dO_h^T, where
+    // Q_h / dO_h are rows 64h.. of the streamed tiles (64 rows x 128 bytes
+    // into each swizzle atom).
+    auto issue_sdp = [&](int u, int h) {
+      const uint32_t q_k = desc_lo(stage(u), 16) + h * (8192 >> 4);
+      const uint32_t o_k = q_k + (Cfg::kTileBytes >> 4);
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
         const uint32_t off = (kk / 4) * (Cfg::kAtomBytes >> 4) + (kk % 4) * 2;
+        const uint32_t ds = tmem + Cfg::kColS + 64 * h, dp = tmem + Cfg::kColDP + 64 * h;
         if (kk == 0) {
-          umma_ss_elect<false>(tmem + Cfg::kColS, k_lo + off, q_k + off, kDescHiSw128, idesc_s);
-          umma_ss_elect<false>(tmem + Cfg::kColDP, v_lo + off, o_k + off, kDescHiSw128, idesc_s);
+          umma_ss_elect<false>(ds, k_lo + off, q_k + off, kDescHiSw128, idesc_s);
+          umma_ss_elect<false>(dp, v_lo + off, o_k + off, kDescHiSw128, idesc_s);
         } else {
-          umma_ss_elect<true>(tmem + Cfg::kColS, k_lo + off, q_k + off, kDescHiSw128, idesc_s);
-          umma_ss_elect<true>(tmem + Cfg::kColDP, v_lo + off, o_k + off, kDescHiSw128, idesc_s);
+          umma_ss_elect<true>(ds, k_lo + off, q_k + off, kDescHiSw128, idesc_s);
+          umma_ss_elect<true>(dp, v_lo + off, o_k + off, kDescHiSw128, idesc_s);
         }
       }
-      umma_commit_elect(bar_s_full);
-      for (int hf = 0; hf < 2 && ok; ++hf) {
-        ok = wait(bar_p_ready + hf, u & 1, 86 + hf);
+      umma_commit_elect(bar_s_full + h);
+    };
+    // dV += P^T_h dO_h, dK += dS^T_h Q_h (K = the half's 64 queries).
+    auto issue_acc = [&](int u, int h) {
+      const uint32_t q_mn = desc_lo(stage(u), Cfg::kAtomBytes);
+      const uint32_t o_mn = q_mn + (Cfg::kTileBytes >> 4);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint32_t boff = (h * 4 + kk) * (2048 >> 4);  // 16 query rows per step
+        const uint32_t acc = (u > 0 || h > 0 || kk > 0) ? 1u : 0u;
+        umma_ts_elect(tmem + Cfg::kColAcc0, tmem + Cfg::kColS + h * 64 + kk * 8, o_mn + boff,
+                      kDescHiSw128, idesc_o, acc);
+        umma_ts_elect(tmem + Cfg::kColAcc1, tmem + Cfg::kColDP + h * 64 + kk * 8, q_mn + boff,
+                      kDescHiSw128, idesc_o, acc);
+      }
+      umma_commit_elect(bar_done + h);
+      if (h == 1) umma_commit_elect(bar_empty + u % Cfg::kStages);  // Q, dO of u read
+    };
+    bool ok = n_units == 0 || wait(bar_res, 0, 83);
+    if (ok && n_units > 0) {
+      ok = wait(bar_full, 0, 84);
+      if (ok) {
+        tc_fence_after();
+        issue_sdp(0, 0);
+        issue_sdp(0, 1);
+      }
+    }
+    for (int u = 0; ok && u < n_units; ++u) {
+      for (int h = 0; h < 2 && ok; ++h) {
+        ok = wait(bar_p_ready + h, u & 1, 86 + h);
         if (!ok) break;
         tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint32_t boff = (hf * 4 + kk) * (2048 >> 4);  // 16 query rows per step
-          const uint32_t acc = (u > 0 || hf > 0 || kk > 0) ? 1u : 0u;
-          umma_ts_elect(tmem + Cfg::kColAcc0, tmem + Cfg::kColS + hf * 64 + kk * 8, o_mn + boff,
-                        kDescHiSw128, idesc_o, acc);  // dV += P^T dO
-          umma_ts_elect(tmem + Cfg::kColAcc1, tmem + Cfg::kColDP + hf * 64 + kk * 8,
-                        q_mn + boff, kDescHiSw128, idesc_o, acc);  // dK += dS^T Q
+        issue_acc(u, h);
+        if (u + 1 < n_units) {
+          if (h == 0) ok = wait(bar_full + (u + 1) % Cfg::kStages,
+                                ((u + 1) / Cfg::kStages) & 1, 84);
+          if (ok) ok = wait(bar_done + h, u & 1, 85);  // half h's P^T, dS^T consumed
+          if (!ok) break;
+          tc_fence_after();
+          issue_sdp(u + 1, h);
         }
       }
-      if (!ok) break;
-      umma_commit_elect(bar_empty + st);
-      umma_commit_elect(bar_mm_done);
     }
     umma_commit_elect(bar_drain);
     volatile int no_abort = 0;
@@ -297,7 +323,8 @@ __global__ void __launch_bounds__(320, 1)
       failed = !__all_sync(0xffffffffu, mbar_wait(bar_full + st, (u / Cfg::kStages) & 1,
                                                   abort_flag, 89));
       if (!failed)
-        failed = !__all_sync(0xffffffffu, mbar_wait(bar_s_full, u & 1, abort_flag, 90 + half));
+        failed = !__all_sync(0xffffffffu,
+                             mbar_wait(bar_s_full + half, u & 1, abort_flag, 90 + half));
       if (failed) break;
       tc_fence_after();
       const float* lse2 = rows + st * 256;
@@ -353,7 +380,9 @@ __global__ void __launch_bounds__(320, 1)
     // Epilogue: dV and dK rows of this key, this thread's half of the head dim.
     bool ok = __all_sync(0xffffffffu, !failed && !*abort_flag);
     if (ok && n_units > 0)
-      ok = __all_sync(0xffffffffu, mbar_wait(bar_mm_done, (n_units - 1) & 1, abort_flag, 92));
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait(bar_done, (n_units - 1) & 1, abort_flag, 92) &&
+                          mbar_wait(bar_done + 1, (n_units - 1) & 1, abort_flag, 93));
     if (ok) {
       tc_fence_after();
       const bool row_ok = j < p.Skv;
@@ -404,10 +433,10 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* bar_res = bars;
   uint64_t* bar_full = bar_res + 1;
   uint64_t* bar_empty = bar_full + Cfg::kStages;
-  uint64_t* bar_s_full = bar_empty + Cfg::kStages;
-  uint64_t* bar_p_ready = bar_s_full + 1;
-  uint64_t* bar_mm_done = bar_p_ready + 2;
-  uint64_t* bar_drain = bar_mm_done + 1;
+  uint64_t* bar_s_full = bar_empty + Cfg::kStages;  // [2 halves]
+  uint64_t* bar_p_ready = bar_s_full + 2;
+  uint64_t* bar_done = bar_p_ready + 2;
+  uint64_t* bar_drain = bar_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -473,50 +502,71 @@ __global__ void __launch_bounds__(320, 1)
     }
     __syncwarp();
   } else if (warp == 9) {
-    const uint32_t idesc_s = idesc_bf16_f32(128, 128, false);
+    const uint32_t idesc_s = idesc_bf16_f32(128, 64, false);  // one 64-key half
     const uint32_t idesc_o = idesc_bf16_f32(128, D, true);
     const uint32_t q_lo = desc_lo(smem_u32(smem + Cfg::kOffRes), 16);
     const uint32_t o_lo = q_lo + (Cfg::kTileBytes >> 4);
     auto wait = [&](uint64_t* bar, uint32_t parity, int site) {
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, site));
     };
-    bool ok = n_units == 0 || wait(bar_res, 0, 103);
-    for (int u = 0; ok && u < n_units; ++u) {
-      const int st = u % Cfg::kStages;
-      ok = wait(bar_full + st, (u / Cfg::kStages) & 1, 104);
-      if (ok && u > 0) ok = wait(bar_mm_done, (u - 1) & 1, 105);  // dS consumed
-      if (!ok) break;
-      tc_fence_after();
-      const uint32_t sbase = smem_u32(smem + Cfg::kOffStr + st * 2 * Cfg::kTileBytes);
-      const uint32_t k_k = desc_lo(sbase, 16), v_k = k_k + (Cfg::kTileBytes >> 4);
-      const uint32_t k_mn = desc_lo(sbase, Cfg::kAtomBytes);
+    auto stage = [&](int u) {
+      return smem_u32(smem + Cfg::kOffStr + (u % Cfg::kStages) * 2 * Cfg::kTileBytes);
+    };
+    // S and dP of key half h of unit u: Q K_h^T and dO V_h^T.
+    auto issue_sdp = [&](int u, int h) {
+      const uint32_t k_k = desc_lo(stage(u), 16) + h * (8192 >> 4);
+      const uint32_t v_k = k_k + (Cfg::kTileBytes >> 4);
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
         const uint32_t off = (kk / 4) * (Cfg::kAtomBytes >> 4) + (kk % 4) * 2;
+        const uint32_t ds = tmem + Cfg::kColS + 64 * h, dp = tmem + Cfg::kColDP + 64 * h;
         if (kk == 0) {
-          umma_ss_elect<false>(tmem + Cfg::kColS, q_lo + off, k_k + off, kDescHiSw128, idesc_s);
-          umma_ss_elect<false>(tmem + Cfg::kColDP, o_lo + off, v_k + off, kDescHiSw128, idesc_s);
+          umma_ss_elect<false>(ds, q_lo + off, k_k + off, kDescHiSw128, idesc_s);
+          umma_ss_elect<false>(dp, o_lo + off, v_k + off, kDescHiSw128, idesc_s);
         } else {
-          umma_ss_elect<true>(tmem + Cfg::kColS, q_lo + off, k_k + off, kDescHiSw128, idesc_s);
-          umma_ss_elect<true>(tmem + Cfg::kColDP, o_lo + off, v_k + off, kDescHiSw128, idesc_s);
+          umma_ss_elect<true>(ds, q_lo + off, k_k + off, kDescHiSw128, idesc_s);
+          umma_ss_elect<true>(dp, o_lo + off, v_k + off, kDescHiSw128, idesc_s);
         }
       }
-      umma_commit_elect(bar_s_full);
-      for (int hf = 0; hf < 2 && ok; ++hf) {
-        ok = wait(bar_p_ready + hf, u & 1, 106 + hf);
+      umma_commit_elect(bar_s_full + h);
+    };
+    // dQ += dS_h K_h (K = the half's 64 keys).
+    auto issue_acc = [&](int u, int h) {
+      const uint32_t k_mn = desc_lo(stage(u), Cfg::kAtomBytes);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint32_t boff = (h * 4 + kk) * (2048 >> 4);  // 16 key rows per step
+        const uint32_t acc = (u > 0 || h > 0 || kk > 0) ? 1u : 0u;
+        umma_ts_elect(tmem + Cfg::kColAcc0, tmem + Cfg::kColS + h * 64 + kk * 8, k_mn + boff,
+                      kDescHiSw128, idesc_o, acc);
+      }
+      umma_commit_elect(bar_done + h);
+      if (h == 1) umma_commit_elect(bar_empty + u % Cfg::kStages);  // K, V of u read
+    };
+    bool ok = n_units == 0 || wait(bar_res, 0, 103);
+    if (ok && n_units > 0) {
+      ok = wait(bar_full, 0, 104);
+      if (ok) {
+        tc_fence_after();
+        issue_sdp(0, 0);
+        issue_sdp(0, 1);
+      }
+    }
+    for (int u = 0; ok && u < n_units; ++u) {
+      for (int h = 0; h < 2 && ok; ++h) {
+        ok = wait(bar_p_ready + h, u & 1, 106 + h);
         if (!ok) break;
         tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint32_t boff = (hf * 4 + kk) * (2048 >> 4);  // 16 key rows per step
-          const uint32_t acc = (u > 0 || hf > 0 || kk > 0) ? 1u : 0u;
-          umma_ts_elect(tmem + Cfg::kColAcc0, tmem + Cfg::kColS + hf * 64 + kk * 8, k_mn + boff,
-                        kDescHiSw128, idesc_o, acc);  // dQ += dS K
+        issue_acc(u, h);
+        if (u + 1 < n_units) {
+          if (h == 0) ok = wait(bar_full + (u + 1) % Cfg::kStages,
+                                ((u + 1) / Cfg::kStages) & 1, 104);
+          if (ok) ok = wait(bar_done + h, u & 1, 105);  // half h's dS consumed
+          if (!ok) break;
+          tc_fence_after();
+          issue_sdp(u + 1, h);
         }
       }
-      if (!ok) break;
-      umma_commit_elect(bar_empty + st);
-      umma_commit_elect(bar_mm_done);
     }
     umma_commit_elect(bar_drain);
     volatile int no_abort = 0;
@@ -532,7 +582,8 @@ __global__ void __launch_bounds__(320, 1)
     bool failed = false;
     for (int u = 0; u < n_units && !failed; ++u) {
       const int kt = klo + u;
-      failed = !__all_sync(0xffffffffu, mbar_wait(bar_s_full, u & 1, abort_flag, 110 + half));
+      failed = !__all_sync(0xffffffffu,
+                           mbar_wait(bar_s_full + half, u & 1, abort_flag, 110 + half));
       if (failed) break;
       tc_fence_after();
 #pragma unroll 1
@@ -571,7 +622,9 @@ __global__ void __launch_bounds__(320, 1)
     }
     bool ok = __all_sync(0xffffffffu, !failed && !*abort_flag);
     if (ok && n_units > 0)
-      ok = __all_sync(0xffffffffu, mbar_wait(bar_mm_done, (n_units - 1) & 1, abort_flag, 112));
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait(bar_done, (n_units - 1) & 1, abort_flag, 112) &&
+                          mbar_wait(bar_done + 1, (n_units - 1) & 1, abort_flag, 113));
     if (ok) {
       tc_fence_after();
       const bool row_ok = i < p.Sq;
