@@ -491,7 +491,8 @@ def bench_linear(dist: Dist, clocks: ClockSampler, warmup: int, steps: int = 10)
     return res
 
 
-def bench_backward(dist: Dist, clocks: ClockSampler, warmup: int, steps: int = 10):
+def bench_backward(dist: Dist, clocks: ClockSampler, warmup: int, steps: int = 10,
+                   batch: int = 0):
     """Attention backward (K5): dQ, dK, dV of the causal cfg2-shaped forward
     (B4 S4096 H16 D128 per GPU, bf16, no padding) from its LSE. FLOPs follow
     the usual convention for a flash backward, 10 D per allowed pair (five
@@ -499,7 +500,7 @@ def bench_backward(dist: Dist, clocks: ClockSampler, warmup: int, steps: int = 1
     reported as tensor_TFLOP_s."""
     import torch
     from enilnets_b200 import kernels, _native
-    B, S, H, D = 4, 4096, 16, 128
+    B, S, H, D = batch or 4, 4096, 16, 128
     g = torch.Generator(device=dist.device).manual_seed(8000 + dist.rank)
     q, k, v, do = (torch.randn((B, S, H, D), generator=g, device=dist.device)
                    .to(torch.bfloat16) for _ in range(4))
@@ -528,7 +529,8 @@ SPARSE_PATTERNS = {
 }
 
 
-def bench_sparse(dist: Dist, clocks: ClockSampler, warmup: int, steps: int = 10):
+def bench_sparse(dist: Dist, clocks: ClockSampler, warmup: int, steps: int = 10,
+                 batch: int = 0):
     """Block-sparse attention (sparse_pattern, local + global + random blocks)
     on K1's sparse mode, per GPU B4 S16384 H16 D128 causal bf16, next to the
     dense causal kernel on the same inputs. FLOPs count the pairs the pattern
@@ -536,7 +538,7 @@ def bench_sparse(dist: Dist, clocks: ClockSampler, warmup: int, steps: int = 10)
     tiles' area."""
     import torch
     from enilnets_b200 import kernels, _native, sparse
-    B, S, H, D = 4, 16384, 16, 128
+    B, S, H, D = batch or 4, 16384, 16, 128
     g = torch.Generator(device=dist.device).manual_seed(7000 + dist.rank)
     q, k, v = (torch.randn((B, S, H, D), generator=g, device=dist.device).to(torch.bfloat16)
                for _ in range(3))
@@ -708,7 +710,8 @@ def main():
                                        "linear", "sparse", "backward"],
                     default="all",
                     help="profiling: run one workload")
-    ap.add_argument("--batch", type=int, default=0, help="profiling: prefill batch override")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="profiling: batch override for prefill, sparse and backward")
     ap.add_argument("--decode-batch", type=int, default=0,
                     help="profiling: cfg3 decode batch override")
     ap.add_argument("--no-e2e", action="store_true", help="profiling: skip the e2e leg")
@@ -737,9 +740,9 @@ def main():
             elif args.only == "linear":
                 res = bench_linear(dist, clocks, args.warmup)
             elif args.only == "sparse":
-                res = bench_sparse(dist, clocks, args.warmup)
+                res = bench_sparse(dist, clocks, args.warmup, batch=args.batch)
             elif args.only == "backward":
-                res = bench_backward(dist, clocks, args.warmup)
+                res = bench_backward(dist, clocks, args.warmup, batch=args.batch)
             elif args.only == "layer":
                 res = {"layer_cfg2": bench_layer_cfg2(dist, clocks, args.warmup),
                        "layer_cfg1": bench_layer_cfg1(dist, args.warmup)}
