@@ -662,6 +662,40 @@ def flash_backward_cases():
     np.savez_compressed(HERE / "flash_backward.npz", **out)
 
 
+def mha_backward_cases():
+    """nn/backward.py:241-327 (multihead_attention_backward) after
+    Forward(training=True) on one-layer models (set_seed 4500 + i, input and
+    dout from RandomState(4600 + i), x first): dx and the eight parameter
+    gradients, float32."""
+    from Enilnets.nn import backward as bw
+    out = {}
+    meta = []
+    cfgs = [
+        dict(embed_dim=64, num_heads=4, causal=True),
+        dict(embed_dim=64, num_heads=4, causal=True, positional_scheme="rope", num_kv_heads=2),
+        dict(embed_dim=64, num_heads=4, causal=False, positional_scheme="alibi"),
+        dict(embed_dim=64, num_heads=2, causal=True, window_size=7, num_kv_heads=1),
+        dict(embed_dim=128, num_heads=2, causal=True, tiled_block_size=16,
+             positional_scheme="rope"),
+    ]
+    for i, cfg in enumerate(cfgs):
+        Enilnets.core.utils.set_seed(4500 + i)
+        m = NeuralNet()
+        m.add_multihead_attention(**cfg)
+        rs = np.random.RandomState(4600 + i)
+        x = rs.standard_normal((2, 37, cfg["embed_dim"]))
+        dout = rs.standard_normal((2, 37, cfg["embed_dim"]))
+        m.Forward(x, training=True)
+        layer = m.layers[0]
+        dx = bw.multihead_attention_backward(dout, layer, m.attention_cache[0])
+        out[f"dx{i}"] = dx.astype(np.float32)
+        for name in ("d_Wq", "d_bq", "d_Wk", "d_bk", "d_Wv", "d_bv", "d_Wo", "d_bo"):
+            out[f"{name}{i}"] = np.asarray(layer[name]).astype(np.float32)
+        meta.append(cfg)
+    out["meta"] = np.array(json.dumps(meta))
+    np.savez_compressed(HERE / "mha_backward.npz", **out)
+
+
 def main():
     if len(sys.argv) > 1:
         for name in sys.argv[1:]:
@@ -680,6 +714,7 @@ def main():
     linear_cases()
     sparse_cases()
     flash_backward_cases()
+    mha_backward_cases()
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size)
 
