@@ -377,34 +377,47 @@ __global__ void __launch_bounds__(320, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_p_ready + half);
     }
-    // Epilogue: dV and dK rows of this key, this thread's half of the head dim.
+    // Epilogue: dV, then dK (times the softmax scale). Each thread moves its
+    // row's half of the accumulator into shared memory (the streamed stages
+    // are free once the last accumulation completed; rows padded to D + 1
+    // floats, so the row-per-lane writes hit distinct banks), then each warp
+    // stores whole rows, 128 contiguous bytes per instruction. Every
+    // elementwise thread passes both barriers of both passes, failed or not.
     bool ok = __all_sync(0xffffffffu, !failed && !*abort_flag);
     if (ok && n_units > 0)
       ok = __all_sync(0xffffffffu,
                       mbar_wait(bar_done, (n_units - 1) & 1, abort_flag, 92) &&
                           mbar_wait(bar_done + 1, (n_units - 1) & 1, abort_flag, 93));
-    if (ok) {
-      tc_fence_after();
-      const bool row_ok = j < p.Skv;
-      float* dvr = p.dv + b * p.dv_sb + j * p.dv_ss + hkv * p.dv_sh;
-      float* dkr = p.dk + b * p.dk_sb + j * p.dk_ss + hkv * p.dk_sh;
+    float* stg = reinterpret_cast<float*>(smem + Cfg::kOffStr);  // [128][D + 1]
+    constexpr int ld = D + 1;
 #pragma unroll 1
-      for (int c = 0; c < D / 2; c += 16) {
-        const int col0 = half * (D / 2) + c;
-        uint32_t av[16], ak[16];
-        __syncwarp();
-        if (n_units > 0) {
-          ENL_TMEM_LD16(lane_addr + Cfg::kColAcc0 + col0, av);
-          ENL_TMEM_LD16(lane_addr + Cfg::kColAcc1 + col0, ak);
-        }
-        if (row_ok)
+    for (int arr = 0; arr < 2; ++arr) {
+      if (ok) {
+        tc_fence_after();
+        const uint32_t col_acc = arr ? Cfg::kColAcc1 : Cfg::kColAcc0;
+        const float mul = arr ? p.scale : 1.0f;
+#pragma unroll 1
+        for (int c = 0; c < D / 2; c += 16) {
+          const int col0 = half * (D / 2) + c;
+          uint32_t av[16];
+          __syncwarp();
+          if (n_units > 0) ENL_TMEM_LD16(lane_addr + col_acc + col0, av);
 #pragma unroll
           for (int e = 0; e < 16; ++e)
-            if (col0 + e < p.d_real) {
-              dvr[col0 + e] = n_units > 0 ? __uint_as_float(av[e]) : 0.0f;
-              dkr[col0 + e] = n_units > 0 ? __uint_as_float(ak[e]) * p.scale : 0.0f;
-            }
+            stg[rloc * ld + col0 + e] = n_units > 0 ? __uint_as_float(av[e]) * mul : 0.0f;
+        }
       }
+      named_bar_sync(1, 256);
+      if (ok) {
+        const long long ss = arr ? p.dk_ss : p.dv_ss;
+        float* base = arr ? p.dk + b * p.dk_sb + hkv * p.dk_sh : p.dv + b * p.dv_sb + hkv * p.dv_sh;
+        for (int r = warp; r < 128; r += 8) {
+          const long long jr = (long long)kt * 128 + r;
+          if (jr >= p.Skv) break;
+          for (int c = lane; c < p.d_real; c += 32) base[jr * ss + c] = stg[r * ld + c];
+        }
+      }
+      named_bar_sync(1, 256);
     }
   }
   tc_fence_before();
@@ -620,28 +633,37 @@ __global__ void __launch_bounds__(320, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_p_ready + half);
     }
+    // Epilogue through shared memory, as in the dK/dV kernel.
     bool ok = __all_sync(0xffffffffu, !failed && !*abort_flag);
     if (ok && n_units > 0)
       ok = __all_sync(0xffffffffu,
                       mbar_wait(bar_done, (n_units - 1) & 1, abort_flag, 112) &&
                           mbar_wait(bar_done + 1, (n_units - 1) & 1, abort_flag, 113));
+    float* stg = reinterpret_cast<float*>(smem + Cfg::kOffStr);  // [128][D + 1]
+    constexpr int ld = D + 1;
     if (ok) {
       tc_fence_after();
-      const bool row_ok = i < p.Sq;
-      float* dqr = p.dq + b * p.dq_sb + i * p.dq_ss + h * p.dq_sh;
 #pragma unroll 1
       for (int c = 0; c < D / 2; c += 16) {
         const int col0 = half * (D / 2) + c;
         uint32_t aq[16];
         __syncwarp();
         if (n_units > 0) ENL_TMEM_LD16(lane_addr + Cfg::kColAcc0 + col0, aq);
-        if (row_ok)
 #pragma unroll
-          for (int e = 0; e < 16; ++e)
-            if (col0 + e < p.d_real)
-              dqr[col0 + e] = n_units > 0 ? __uint_as_float(aq[e]) * p.scale : 0.0f;
+        for (int e = 0; e < 16; ++e)
+          stg[rloc * ld + col0 + e] = n_units > 0 ? __uint_as_float(aq[e]) * p.scale : 0.0f;
       }
     }
+    named_bar_sync(1, 256);
+    if (ok) {
+      float* base = p.dq + b * p.dq_sb + h * p.dq_sh;
+      for (int r = warp; r < 128; r += 8) {
+        const long long ir = (long long)qt * 128 + r;
+        if (ir >= p.Sq) break;
+        for (int c = lane; c < p.d_real; c += 32) base[ir * p.dq_ss + c] = stg[r * ld + c];
+      }
+    }
+    named_bar_sync(1, 256);
   }
   tc_fence_before();
   __syncthreads();

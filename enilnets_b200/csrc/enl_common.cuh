@@ -128,6 +128,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   return mbar_wait_budget(bar, parity, abort_flag, site, kWaitBudgetNs);
 }
 
+// Barrier over the first `threads` threads' warps that name barrier `id` (0 is
+// __syncthreads).
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // TMA tensor copies (global <-> shared, one CTA each) and bulk groups.
 // ---------------------------------------------------------------------------

@@ -221,10 +221,6 @@ struct TileCursor {
   __device__ __forceinline__ bool valid(const PrefillParams& p) const { return t < p.n_items; }
 };
 
-__device__ __forceinline__ void named_bar_sync(int id, int threads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
 template <int D, bool kSplit, bool kSparse>
 __global__ void __launch_bounds__(384, 1)
     attn_prefill_sm100(const __grid_constant__ CUtensorMap tm_q,
