@@ -107,36 +107,52 @@ __device__ __forceinline__ void bwd_elem(const BwdParams& p, float s, float dp, 
   ds = pr * (dp - dsum);
 }
 
+// One 16-lane group per query row. With bf16 O, 16-byte aligned rows and a
+// head dim that is a multiple of 8, each lane reads 8 elements of O and dO
+// per 16-byte load; otherwise one element at a time.
 __global__ void bwd_prep_kernel(BwdPrepParams q) {
-  const int lane = threadIdx.x % 32;
-  const long long warps = (long long)gridDim.x * (blockDim.x / 32);
+  const int sub = threadIdx.x % 16;
+  const long long groups = (long long)gridDim.x * (blockDim.x / 16);
   const long long total = (long long)q.B * q.H * q.s_pad;
-  for (long long idx = blockIdx.x * (long long)(blockDim.x / 32) + threadIdx.x / 32; idx < total;
-       idx += warps) {
+  const __nv_bfloat16* dob = reinterpret_cast<const __nv_bfloat16*>(q.dout);
+  const bool vec = !q.o_f32 && q.d_real % 8 == 0 && q.o_sb % 8 == 0 && q.o_ss % 8 == 0 &&
+                   q.o_sh % 8 == 0 && (reinterpret_cast<uintptr_t>(q.o) & 15u) == 0;
+  for (long long idx = blockIdx.x * (long long)(blockDim.x / 16) + threadIdx.x / 16; idx < total;
+       idx += groups) {
     const long long bh = idx / q.s_pad;
     const int i = (int)(idx % q.s_pad);
     const int b = (int)(bh / q.H), h = (int)(bh % q.H);
-    if (i >= q.Sq) {
-      if (lane == 0) {
-        q.lse2[idx] = INFINITY;
-        q.dsum[idx] = 0.0f;
-      }
-      continue;
-    }
     float acc = 0.0f;
-    const long long oo = b * q.o_sb + (long long)i * q.o_ss + h * q.o_sh;
-    const long long od = b * q.do_sb + (long long)i * q.do_ss + h * q.do_sh;
-    const __nv_bfloat16* dob = reinterpret_cast<const __nv_bfloat16*>(q.dout);
-    for (int d = lane; d < q.d_real; d += 32) {
-      const float o = q.o_f32 ? reinterpret_cast<const float*>(q.o)[oo + d]
-                              : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(q.o)[oo + d]);
-      acc = fmaf(o, __bfloat162float(dob[od + d]), acc);
-    }
+    if (i < q.Sq) {
+      const long long oo = b * q.o_sb + (long long)i * q.o_ss + h * q.o_sh;
+      const long long od = b * q.do_sb + (long long)i * q.do_ss + h * q.do_sh;
+      if (vec) {
+        const __nv_bfloat16* ob = reinterpret_cast<const __nv_bfloat16*>(q.o);
+        for (int d = 8 * sub; d < q.d_real; d += 128) {
+          const uint4 x = *reinterpret_cast<const uint4*>(ob + oo + d);
+          const uint4 y = *reinterpret_cast<const uint4*>(dob + od + d);
+          const uint32_t xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
 #pragma unroll
-    for (int m = 16; m > 0; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
-    if (lane == 0) {
-      q.dsum[idx] = acc;
-      q.lse2[idx] = q.lse[bh * q.Sq + i] * 1.4426950408889634f;
+          for (int k = 0; k < 4; ++k) {
+            acc = fmaf(bf16lo_to_f32(xs[k]), bf16lo_to_f32(ys[k]), acc);
+            acc = fmaf(bf16hi_to_f32(xs[k]), bf16hi_to_f32(ys[k]), acc);
+          }
+        }
+      } else {
+        for (int d = sub; d < q.d_real; d += 16) {
+          const float o = q.o_f32 ? reinterpret_cast<const float*>(q.o)[oo + d]
+                                  : __bfloat162float(
+                                        reinterpret_cast<const __nv_bfloat16*>(q.o)[oo + d]);
+          acc = fmaf(o, __bfloat162float(dob[od + d]), acc);
+        }
+      }
+    }
+    const unsigned group = 0xffffu << (16 * ((threadIdx.x % 32) / 16));  // this 16-lane half
+#pragma unroll
+    for (int m = 8; m > 0; m >>= 1) acc += __shfl_xor_sync(group, acc, m);
+    if (sub == 0) {
+      q.dsum[idx] = i < q.Sq ? acc : 0.0f;
+      q.lse2[idx] = i < q.Sq ? q.lse[bh * q.Sq + i] * 1.4426950408889634f : INFINITY;
     }
   }
 }
@@ -703,7 +719,7 @@ cudaError_t launch_backward(const CUtensorMap& tq, const CUtensorMap& tk, const 
                             const CUtensorMap& tdo, const BwdPrepParams& prep, const BwdParams& p,
                             int D, cudaStream_t stream) {
   const long long rows = (long long)prep.B * prep.H * prep.s_pad;
-  const long long blocks = min((rows + 7) / 8, 148ll * 16);
+  const long long blocks = min((rows + 15) / 16, 148ll * 32);  // 16 rows per 256-thread block
   bwd_prep_kernel<<<(int)blocks, 256, 0, stream>>>(prep);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
