@@ -19,10 +19,13 @@
 //                         dQ += dS K in tensor memory.
 // Tensor memory per CTA: S (128 columns) + dP (128) + two D-column
 // accumulators, 512 columns at D = 128: no room for a second S. Instead each
-// tile is split into two 64-column halves with their own barriers, and the
-// next tile's S and dP of half h are computed as soon as this tile's
-// accumulation of half h has read its P and dS, so the tensor pipe works
-// while the other half's elementwise warps run. Recomputing S and dP in the
+// tile is split into two 64-column halves with their own barriers. The
+// elementwise warps read a half's dP whole, then write the packed bf16 P and
+// dS of the half over its dP columns, so its S columns are free as soon as
+// they are done: the next tile's S of that half is issued right behind this
+// tile's accumulation, and only its dP waits for the accumulation to have
+// read P and dS. The tensor pipe works while the other half's elementwise
+// warps run. Recomputing S and dP in the
 // dQ pass costs two GEMMs of seven but needs no atomics and no dQ staging.
 //
 // Warp roles (320 threads): 0-7 elementwise (warps w and w + 4 share TMEM
@@ -264,24 +267,33 @@ __global__ void __launch_bounds__(320, 1)
     // S^T and dP^T of query half h of unit u: K Q_h^T and V dO_h^T, where
     // Q_h / dO_h are rows 64h.. of the streamed tiles (64 rows x 128 bytes
     // into each swizzle atom).
-    auto issue_sdp = [&](int u, int h) {
+    auto issue_s = [&](int u, int h) {
       const uint32_t q_k = desc_lo(stage(u), 16) + h * (8192 >> 4);
-      const uint32_t o_k = q_k + (Cfg::kTileBytes >> 4);
+      const uint32_t ds = tmem + Cfg::kColS + 64 * h;
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
         const uint32_t off = (kk / 4) * (Cfg::kAtomBytes >> 4) + (kk % 4) * 2;
-        const uint32_t ds = tmem + Cfg::kColS + 64 * h, dp = tmem + Cfg::kColDP + 64 * h;
-        if (kk == 0) {
+        if (kk == 0)
           umma_ss_elect<false>(ds, k_lo + off, q_k + off, kDescHiSw128, idesc_s);
-          umma_ss_elect<false>(dp, v_lo + off, o_k + off, kDescHiSw128, idesc_s);
-        } else {
+        else
           umma_ss_elect<true>(ds, k_lo + off, q_k + off, kDescHiSw128, idesc_s);
-          umma_ss_elect<true>(dp, v_lo + off, o_k + off, kDescHiSw128, idesc_s);
-        }
       }
-      umma_commit_elect(bar_s_full + h);
     };
-    // dV += P^T_h dO_h, dK += dS^T_h Q_h (K = the half's 64 queries).
+    auto issue_dp = [&](int u, int h) {
+      const uint32_t o_k = desc_lo(stage(u), 16) + h * (8192 >> 4) + (Cfg::kTileBytes >> 4);
+      const uint32_t dp = tmem + Cfg::kColDP + 64 * h;
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint32_t off = (kk / 4) * (Cfg::kAtomBytes >> 4) + (kk % 4) * 2;
+        if (kk == 0)
+          umma_ss_elect<false>(dp, v_lo + off, o_k + off, kDescHiSw128, idesc_s);
+        else
+          umma_ss_elect<true>(dp, v_lo + off, o_k + off, kDescHiSw128, idesc_s);
+      }
+      umma_commit_elect(bar_s_full + h);  // S and dP of the half
+    };
+    // dV += P^T_h dO_h, dK += dS^T_h Q_h (K = the half's 64 queries); P^T_h and
+    // dS^T_h are packed over the half's dP columns (first and second 32).
     auto issue_acc = [&](int u, int h) {
       const uint32_t q_mn = desc_lo(stage(u), Cfg::kAtomBytes);
       const uint32_t o_mn = q_mn + (Cfg::kTileBytes >> 4);
@@ -289,10 +301,10 @@ __global__ void __launch_bounds__(320, 1)
       for (int kk = 0; kk < 4; ++kk) {
         const uint32_t boff = (h * 4 + kk) * (2048 >> 4);  // 16 query rows per step
         const uint32_t acc = (u > 0 || h > 0 || kk > 0) ? 1u : 0u;
-        umma_ts_elect(tmem + Cfg::kColAcc0, tmem + Cfg::kColS + h * 64 + kk * 8, o_mn + boff,
+        umma_ts_elect(tmem + Cfg::kColAcc0, tmem + Cfg::kColDP + h * 64 + kk * 8, o_mn + boff,
                       kDescHiSw128, idesc_o, acc);
-        umma_ts_elect(tmem + Cfg::kColAcc1, tmem + Cfg::kColDP + h * 64 + kk * 8, q_mn + boff,
-                      kDescHiSw128, idesc_o, acc);
+        umma_ts_elect(tmem + Cfg::kColAcc1, tmem + Cfg::kColDP + h * 64 + 32 + kk * 8,
+                      q_mn + boff, kDescHiSw128, idesc_o, acc);
       }
       umma_commit_elect(bar_done + h);
       if (h == 1) umma_commit_elect(bar_empty + u % Cfg::kStages);  // Q, dO of u read
@@ -302,8 +314,10 @@ __global__ void __launch_bounds__(320, 1)
       ok = wait(bar_full, 0, 84);
       if (ok) {
         tc_fence_after();
-        issue_sdp(0, 0);
-        issue_sdp(0, 1);
+        for (int h = 0; h < 2; ++h) {
+          issue_s(0, h);
+          issue_dp(0, h);
+        }
       }
     }
     for (int u = 0; ok && u < n_units; ++u) {
@@ -315,10 +329,12 @@ __global__ void __launch_bounds__(320, 1)
         if (u + 1 < n_units) {
           if (h == 0) ok = wait(bar_full + (u + 1) % Cfg::kStages,
                                 ((u + 1) / Cfg::kStages) & 1, 84);
-          if (ok) ok = wait(bar_done + h, u & 1, 85);  // half h's P^T, dS^T consumed
+          if (!ok) break;
+          issue_s(u + 1, h);  // the half's S columns were read by the elementwise warps
+          ok = wait(bar_done + h, u & 1, 85);  // packed P^T_h, dS^T_h read
           if (!ok) break;
           tc_fence_after();
-          issue_sdp(u + 1, h);
+          issue_dp(u + 1, h);
         }
       }
     }
@@ -345,11 +361,17 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_after();
       const float* lse2 = rows + st * 256;
       const float* dsum = lse2 + 128;
-#pragma unroll 1
+      // The half's dP first (all 64 columns, so the packed P and dS can go
+      // over them), then S 32 columns at a time.
+      uint32_t dph[64];
+      ENL_TMEM_LD32X2(lane_addr + Cfg::kColDP + 64 * half, dph,
+                      lane_addr + Cfg::kColDP + 64 * half + 32, (dph + 32));
+#pragma unroll
       for (int ch = 0; ch < 2; ++ch) {
         const int c0 = 64 * half + 32 * ch;  // first query column of the chunk
-        uint32_t sr[32], dr[32], pk[16], dk[16];
-        ENL_TMEM_LD32X2(lane_addr + Cfg::kColS + c0, sr, lane_addr + Cfg::kColDP + c0, dr);
+        uint32_t sr[32], pk[16], dk[16];
+        const uint32_t* dr = dph + 32 * ch;
+        ENL_TMEM_LD32(lane_addr + Cfg::kColS + c0, sr, 0);
         const long long i0 = (long long)qt * 128 + c0;
         // Every (query, key) of the chunk visible and no bias: P needs only
         // the column's LSE (queries past Sq carry +inf there, so P = 0).
@@ -384,9 +406,9 @@ __global__ void __launch_bounds__(320, 1)
             dk[c / 2] = pack_bf16x2(d0, d1);
           }
         }
-        // packed pairs over the chunk's own, already read, columns
-        ENL_TMEM_ST16(lane_addr + Cfg::kColS + 64 * half + 16 * ch, pk);
-        ENL_TMEM_ST16(lane_addr + Cfg::kColDP + 64 * half + 16 * ch, dk);
+        // packed P^T over the half's first 32 dP columns, dS^T over the last 32
+        ENL_TMEM_ST16(lane_addr + Cfg::kColDP + 64 * half + 16 * ch, pk);
+        ENL_TMEM_ST16(lane_addr + Cfg::kColDP + 64 * half + 32 + 16 * ch, dk);
       }
       tmem_st_wait();
       tc_fence_before();
@@ -542,31 +564,40 @@ __global__ void __launch_bounds__(320, 1)
       return smem_u32(smem + Cfg::kOffStr + (u % Cfg::kStages) * 2 * Cfg::kTileBytes);
     };
     // S and dP of key half h of unit u: Q K_h^T and dO V_h^T.
-    auto issue_sdp = [&](int u, int h) {
+    auto issue_s = [&](int u, int h) {
       const uint32_t k_k = desc_lo(stage(u), 16) + h * (8192 >> 4);
-      const uint32_t v_k = k_k + (Cfg::kTileBytes >> 4);
+      const uint32_t ds = tmem + Cfg::kColS + 64 * h;
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
         const uint32_t off = (kk / 4) * (Cfg::kAtomBytes >> 4) + (kk % 4) * 2;
-        const uint32_t ds = tmem + Cfg::kColS + 64 * h, dp = tmem + Cfg::kColDP + 64 * h;
-        if (kk == 0) {
+        if (kk == 0)
           umma_ss_elect<false>(ds, q_lo + off, k_k + off, kDescHiSw128, idesc_s);
-          umma_ss_elect<false>(dp, o_lo + off, v_k + off, kDescHiSw128, idesc_s);
-        } else {
+        else
           umma_ss_elect<true>(ds, q_lo + off, k_k + off, kDescHiSw128, idesc_s);
+      }
+    };
+    auto issue_dp = [&](int u, int h) {
+      const uint32_t v_k = desc_lo(stage(u), 16) + h * (8192 >> 4) + (Cfg::kTileBytes >> 4);
+      const uint32_t dp = tmem + Cfg::kColDP + 64 * h;
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint32_t off = (kk / 4) * (Cfg::kAtomBytes >> 4) + (kk % 4) * 2;
+        if (kk == 0)
+          umma_ss_elect<false>(dp, o_lo + off, v_k + off, kDescHiSw128, idesc_s);
+        else
           umma_ss_elect<true>(dp, o_lo + off, v_k + off, kDescHiSw128, idesc_s);
-        }
       }
       umma_commit_elect(bar_s_full + h);
     };
-    // dQ += dS_h K_h (K = the half's 64 keys).
+    // dQ += dS_h K_h (K = the half's 64 keys); dS_h is packed over the half's
+    // first 32 dP columns.
     auto issue_acc = [&](int u, int h) {
       const uint32_t k_mn = desc_lo(stage(u), Cfg::kAtomBytes);
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         const uint32_t boff = (h * 4 + kk) * (2048 >> 4);  // 16 key rows per step
         const uint32_t acc = (u > 0 || h > 0 || kk > 0) ? 1u : 0u;
-        umma_ts_elect(tmem + Cfg::kColAcc0, tmem + Cfg::kColS + h * 64 + kk * 8, k_mn + boff,
+        umma_ts_elect(tmem + Cfg::kColAcc0, tmem + Cfg::kColDP + h * 64 + kk * 8, k_mn + boff,
                       kDescHiSw128, idesc_o, acc);
       }
       umma_commit_elect(bar_done + h);
@@ -577,8 +608,10 @@ __global__ void __launch_bounds__(320, 1)
       ok = wait(bar_full, 0, 104);
       if (ok) {
         tc_fence_after();
-        issue_sdp(0, 0);
-        issue_sdp(0, 1);
+        for (int h = 0; h < 2; ++h) {
+          issue_s(0, h);
+          issue_dp(0, h);
+        }
       }
     }
     for (int u = 0; ok && u < n_units; ++u) {
@@ -590,10 +623,12 @@ __global__ void __launch_bounds__(320, 1)
         if (u + 1 < n_units) {
           if (h == 0) ok = wait(bar_full + (u + 1) % Cfg::kStages,
                                 ((u + 1) / Cfg::kStages) & 1, 104);
-          if (ok) ok = wait(bar_done + h, u & 1, 105);  // half h's dS consumed
+          if (!ok) break;
+          issue_s(u + 1, h);  // the half's S columns were read by the elementwise warps
+          ok = wait(bar_done + h, u & 1, 105);  // packed dS_h read
           if (!ok) break;
           tc_fence_after();
-          issue_sdp(u + 1, h);
+          issue_dp(u + 1, h);
         }
       }
     }
@@ -615,11 +650,15 @@ __global__ void __launch_bounds__(320, 1)
                            mbar_wait(bar_s_full + half, u & 1, abort_flag, 110 + half));
       if (failed) break;
       tc_fence_after();
-#pragma unroll 1
+      uint32_t dph[64];  // the half's dP first, so the packed dS can go over it
+      ENL_TMEM_LD32X2(lane_addr + Cfg::kColDP + 64 * half, dph,
+                      lane_addr + Cfg::kColDP + 64 * half + 32, (dph + 32));
+#pragma unroll
       for (int ch = 0; ch < 2; ++ch) {
         const int c0 = 64 * half + 32 * ch;  // first key column of the chunk
-        uint32_t sr[32], dr[32], dk[16];
-        ENL_TMEM_LD32X2(lane_addr + Cfg::kColS + c0, sr, lane_addr + Cfg::kColDP + c0, dr);
+        uint32_t sr[32], dk[16];
+        const uint32_t* dr = dph + 32 * ch;
+        ENL_TMEM_LD32(lane_addr + Cfg::kColS + c0, sr, 0);
         const long long j0 = (long long)kt * 128 + c0;
         const bool open = slope2 == 0.0f && j0 + 31 < p.Skv && (!p.causal || j0 + 31 <= i) &&
                           (p.window < 0 || (i - j0 <= p.window && j0 + 31 - i <= p.window));
@@ -642,7 +681,7 @@ __global__ void __launch_bounds__(320, 1)
             dk[c / 2] = pack_bf16x2(d0, d1);
           }
         }
-        ENL_TMEM_ST16(lane_addr + Cfg::kColS + 64 * half + 16 * ch, dk);
+        ENL_TMEM_ST16(lane_addr + Cfg::kColDP + 64 * half + 16 * ch, dk);
       }
       tmem_st_wait();
       tc_fence_before();
