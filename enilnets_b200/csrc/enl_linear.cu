@@ -226,23 +226,92 @@ constexpr int kLinChunk = 16;   // rows per chunk
 constexpr int kLinCols = 32;    // V columns per CTA
 constexpr int kLinThreads = 256;
 
+// Shared-memory layout of both attention kernels, in floats. The S_kv slice
+// and the V chunk come first so their rows stay 16-byte aligned for float4
+// access; the phi chunks are padded to Df + 1 so column-wise walks avoid bank
+// conflicts.
+constexpr int kLinPart = kLinChunk * kLinCols + kLinChunk;  // emit's second-half partials
 __host__ __device__ inline int lin_smem_floats(int Df) {
-  // S_kv slice [Df][32], s_k [Df], phi(q) and phi(k) chunks [16][Df + 1],
-  // V chunk [16][32], scores [16][16], denominators [16]
-  return Df * kLinCols + Df + 2 * kLinChunk * (Df + 1) + kLinChunk * kLinCols +
-         kLinChunk * kLinChunk + kLinChunk;
+  // S_kv slice [Df][32], V chunk [16][32], partials [16][32] + [16],
+  // scores [16][16], s_k [Df], phi(q) and phi(k) chunks [16][Df + 1]
+  return Df * kLinCols + kLinChunk * kLinCols + kLinPart + kLinChunk * kLinChunk + Df +
+         2 * kLinChunk * (Df + 1);
 }
 
+// S_kv[f][c] += sum_j phi(k_j)[f] v_j[c] over a chunk, register-tiled: thread
+// t owns columns 4 (t % 8) .. + 3 of rows t / 8, t / 8 + 32, ..., two rows at
+// a time, so each step of j feeds eight independent FMAs from one float4 of V
+// and two phi values.
+__device__ __forceinline__ void lin_accumulate(float* kv, const float* vc, const float* kc, int ld,
+                                               int Df, int tid) {
+  const int cq = tid % 8, fg = tid / 8;
+  for (int f0 = fg; f0 < Df; f0 += 64) {
+    const int f1 = f0 + 32;
+    const bool has1 = f1 < Df;
+    float4 a0 = *reinterpret_cast<const float4*>(kv + f0 * kLinCols + 4 * cq);
+    float4 a1 = has1 ? *reinterpret_cast<const float4*>(kv + f1 * kLinCols + 4 * cq)
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < kLinChunk; ++j) {
+      const float4 v = *reinterpret_cast<const float4*>(vc + j * kLinCols + 4 * cq);
+      const float k0 = kc[j * ld + f0];
+      const float k1 = has1 ? kc[j * ld + f1] : 0.0f;
+      a0.x = fmaf(k0, v.x, a0.x);
+      a0.y = fmaf(k0, v.y, a0.y);
+      a0.z = fmaf(k0, v.z, a0.z);
+      a0.w = fmaf(k0, v.w, a0.w);
+      a1.x = fmaf(k1, v.x, a1.x);
+      a1.y = fmaf(k1, v.y, a1.y);
+      a1.z = fmaf(k1, v.z, a1.z);
+      a1.w = fmaf(k1, v.w, a1.w);
+    }
+    *reinterpret_cast<float4*>(kv + f0 * kLinCols + 4 * cq) = a0;
+    if (has1) *reinterpret_cast<float4*>(kv + f1 * kLinCols + 4 * cq) = a1;
+  }
+}
+
+// Next-chunk prefetch: with kPer > 0 (Df <= kPer * kLinThreads / kLinChunk)
+// each thread holds its kPer elements of the next chunk's phi rows, and its
+// share of the V slice, in registers while the current chunk computes, so a
+// chunk's global loads are in flight during the previous chunk's arithmetic.
+// kPer = 0: loads at the top of each chunk (feature counts above 256).
+constexpr int kLinVPer = kLinChunk * kLinCols / kLinThreads;  // V elements per thread
+
+template <int kPer>
+__device__ __forceinline__ void lin_fetch_rows(float (&dst)[kPer], const float* src, int nrow,
+                                               int Df, int tid) {
+#pragma unroll
+  for (int m = 0; m < kPer; ++m) {
+    const int i = tid + m * kLinThreads;
+    const int r = i / Df, f = i - r * Df;
+    dst[m] = (i < kLinChunk * Df && r < nrow) ? src[(long long)r * Df + f] : 0.0f;
+  }
+}
+
+template <int kPer>
+__device__ __forceinline__ void lin_commit_rows(const float (&src)[kPer], float* dst, int ld,
+                                                int Df, int tid) {
+#pragma unroll
+  for (int m = 0; m < kPer; ++m) {
+    const int i = tid + m * kLinThreads;
+    if (i < kLinChunk * Df) {
+      const int r = i / Df, f = i - r * Df;
+      dst[r * ld + f] = src[m];
+    }
+  }
+}
+
+template <int kPer>
 __global__ void __launch_bounds__(kLinThreads) linear_attn_kernel(LinearParams p) {
-  extern __shared__ float sm[];
+  extern __shared__ __align__(16) float sm[];
   const int Df = p.Df, ld = Df + 1;
-  float* kv = sm;                          // [Df][32]
-  float* ks = kv + Df * kLinCols;          // [Df]
-  float* qc = ks + Df;                     // [16][Df + 1]
-  float* kc = qc + kLinChunk * ld;         // [16][Df + 1]
-  float* vc = kc + kLinChunk * ld;         // [16][32]
-  float* sc = vc + kLinChunk * kLinCols;   // [16][16]
-  float* dn = sc + kLinChunk * kLinChunk;  // [16]
+  float* kv = sm;                            // [Df][32]
+  float* vc = kv + Df * kLinCols;            // [16][32]
+  float* part = vc + kLinChunk * kLinCols;   // [16][32] numerators + [16] denominators
+  float* sc = part + kLinPart;               // [16][16]
+  float* ks = sc + kLinChunk * kLinChunk;    // [Df]
+  float* qc = ks + Df;                       // [16][Df + 1]
+  float* kc = qc + kLinChunk * ld;           // [16][Df + 1]
   const int tid = threadIdx.x;
   const int bh = blockIdx.x;
   const int b = bh / p.H, h = bh % p.H;
@@ -287,13 +356,7 @@ __global__ void __launch_bounds__(kLinThreads) linear_attn_kernel(LinearParams p
   };
   // S_kv += phi(K_c)^T V_c, s_k += sum phi(K_c) (rows past nrow are zero)
   auto accumulate = [&]() {
-    for (int i = tid; i < Df * kLinCols; i += kLinThreads) {
-      const int f = i / kLinCols, c = i % kLinCols;
-      float acc = kv[i];
-#pragma unroll
-      for (int j = 0; j < kLinChunk; ++j) acc = fmaf(kc[j * ld + f], vc[j * kLinCols + c], acc);
-      kv[i] = acc;
-    }
+    lin_accumulate(kv, vc, kc, ld, Df, tid);
     for (int f = tid; f < Df; f += kLinThreads) {
       float acc = ks[f];
 #pragma unroll
@@ -301,47 +364,144 @@ __global__ void __launch_bounds__(kLinThreads) linear_attn_kernel(LinearParams p
       ks[f] = acc;
     }
   };
-  // out rows of the chunk: (causal part in sc) + phi(q) . state
+  // Out rows of the chunk: phi(q) . state (+ the causal part in sc), over
+  // the denominators phi(q) . s_k (+ the scores' row sums). Thread t takes
+  // row (t / 8) % 16, columns 4 (t % 8) .. + 3, and half kh = t / 128 of the
+  // features; the second half's partial sums meet the first's in shared
+  // memory. The denominator of a row is split over its 8 lanes.
   auto emit = [&](int s0, int nrow, bool with_scores) {
-    // denominators
-    if (tid < kLinChunk) {
-      const int r = tid;
-      float den = 0.0f;
-      for (int f = 0; f < Df; ++f) den = fmaf(qc[r * ld + f], ks[f], den);
-      if (with_scores)
-        for (int j = 0; j <= r; ++j) den += sc[r * kLinChunk + j];
-      dn[r] = den + p.eps;
+    const int cq = tid % 8, r = (tid / 8) % kLinChunk, kh = tid / 128;
+    const int fh = (Df + 1) / 2, fa = kh * fh, fb = min(Df, fa + fh);
+    const float* qr = qc + r * ld;
+    float4 n0 = make_float4(0.f, 0.f, 0.f, 0.f), n1 = n0;
+    int f = fa;
+    for (; f + 1 < fb; f += 2) {  // two interleaved partial sums
+      const float q0 = qr[f], q1 = qr[f + 1];
+      const float4 s0v = *reinterpret_cast<const float4*>(kv + f * kLinCols + 4 * cq);
+      const float4 s1v = *reinterpret_cast<const float4*>(kv + (f + 1) * kLinCols + 4 * cq);
+      n0.x = fmaf(q0, s0v.x, n0.x);
+      n0.y = fmaf(q0, s0v.y, n0.y);
+      n0.z = fmaf(q0, s0v.z, n0.z);
+      n0.w = fmaf(q0, s0v.w, n0.w);
+      n1.x = fmaf(q1, s1v.x, n1.x);
+      n1.y = fmaf(q1, s1v.y, n1.y);
+      n1.z = fmaf(q1, s1v.z, n1.z);
+      n1.w = fmaf(q1, s1v.w, n1.w);
+    }
+    if (f < fb) {
+      const float q0 = qr[f];
+      const float4 s0v = *reinterpret_cast<const float4*>(kv + f * kLinCols + 4 * cq);
+      n0.x = fmaf(q0, s0v.x, n0.x);
+      n0.y = fmaf(q0, s0v.y, n0.y);
+      n0.z = fmaf(q0, s0v.z, n0.z);
+      n0.w = fmaf(q0, s0v.w, n0.w);
+    }
+    float4 num = make_float4(n0.x + n1.x, n0.y + n1.y, n0.z + n1.z, n0.w + n1.w);
+    float den = 0.0f;
+    for (int g = fa + cq; g < fb; g += 8) den = fmaf(qr[g], ks[g], den);
+#pragma unroll
+    for (int m = 4; m > 0; m >>= 1) den += __shfl_xor_sync(0xffffffffu, den, m);
+    if (kh == 1) {
+      *reinterpret_cast<float4*>(part + r * kLinCols + 4 * cq) = num;
+      if (cq == 0) part[kLinChunk * kLinCols + r] = den;
     }
     __syncthreads();
-    for (int i = tid; i < kLinChunk * kLinCols; i += kLinThreads) {
-      const int r = i / kLinCols, c = i % kLinCols;
-      if (r >= nrow || c >= ncol) continue;
-      float num = 0.0f;
-      for (int f = 0; f < Df; ++f) num = fmaf(qc[r * ld + f], kv[f * kLinCols + c], num);
+    if (kh == 0) {
+      const float4 o2 = *reinterpret_cast<const float4*>(part + r * kLinCols + 4 * cq);
+      num.x += o2.x;
+      num.y += o2.y;
+      num.z += o2.z;
+      num.w += o2.w;
+      den += part[kLinChunk * kLinCols + r];
       if (with_scores)
-        for (int j = 0; j <= r; ++j) num = fmaf(sc[r * kLinChunk + j], vc[j * kLinCols + c], num);
-      const float o = num / dn[r];
-      const long long off = b * p.o_sb + (long long)(s0 + r) * p.o_ss + h * p.o_sh + d0 + c;
-      if (p.o_f32)
-        reinterpret_cast<float*>(p.o)[off] = o;
-      else
-        reinterpret_cast<__nv_bfloat16*>(p.o)[off] = __float2bfloat16(o);
+        for (int j = 0; j <= r; ++j) {
+          const float sv = sc[r * kLinChunk + j];
+          const float4 v = *reinterpret_cast<const float4*>(vc + j * kLinCols + 4 * cq);
+          num.x = fmaf(sv, v.x, num.x);
+          num.y = fmaf(sv, v.y, num.y);
+          num.z = fmaf(sv, v.z, num.z);
+          num.w = fmaf(sv, v.w, num.w);
+          den += sv;
+        }
+      den += p.eps;
+      if (r < nrow) {
+        const float vals[4] = {num.x / den, num.y / den, num.z / den, num.w / den};
+        const long long off = b * p.o_sb + (long long)(s0 + r) * p.o_ss + h * p.o_sh + d0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c = 4 * cq + e;
+          if (c >= ncol) continue;
+          if (p.o_f32)
+            reinterpret_cast<float*>(p.o)[off + c] = vals[e];
+          else
+            reinterpret_cast<__nv_bfloat16*>(p.o)[off + c] = __float2bfloat16(vals[e]);
+        }
+      }
     }
   };
 
+  constexpr int kP = kPer > 0 ? kPer : 1;
+  float rq[kP], rk[kP], rv[kLinVPer];
+  auto fetch_v = [&](int s0, int nrow) {
+#pragma unroll
+    for (int m = 0; m < kLinVPer; ++m) {
+      const int i = tid + m * kLinThreads, r = i / kLinCols, c = i % kLinCols;
+      rv[m] = (r < nrow && c < ncol)
+                  ? load_elem(p.v, b * p.v_sb + (long long)(s0 + r) * p.v_ss + hkv * p.v_sh + d0 + c,
+                              p.v_f32)
+                  : 0.0f;
+    }
+  };
+  auto commit_v = [&]() {
+#pragma unroll
+    for (int m = 0; m < kLinVPer; ++m) vc[tid + m * kLinThreads] = rv[m];
+  };
+
   if (p.causal) {
+    if constexpr (kPer > 0) {
+      if (r0 < r1) {
+        const int n0 = min(kLinChunk, r1 - r0);
+        lin_fetch_rows<kPer>(rq, phq + (long long)r0 * Df, n0, Df, tid);
+        lin_fetch_rows<kPer>(rk, phk + (long long)r0 * Df, n0, Df, tid);
+        fetch_v(r0, n0);
+      }
+    }
     for (int s0 = r0; s0 < r1; s0 += kLinChunk) {
       const int nrow = min(kLinChunk, r1 - s0);
-      load_rows(phq + (long long)s0 * Df, qc, 0, nrow);
-      load_rows(phk + (long long)s0 * Df, kc, 0, nrow);
-      load_v(s0, nrow);
-      __syncthreads();
-      {  // scores phi(q_i).phi(k_j) for j <= i inside the chunk
+      if constexpr (kPer > 0) {
+        lin_commit_rows<kPer>(rq, qc, ld, Df, tid);
+        lin_commit_rows<kPer>(rk, kc, ld, Df, tid);
+        commit_v();
+        __syncthreads();
+        const int s1 = s0 + kLinChunk;
+        if (s1 < r1) {
+          const int n1 = min(kLinChunk, r1 - s1);
+          lin_fetch_rows<kPer>(rq, phq + (long long)s1 * Df, n1, Df, tid);
+          lin_fetch_rows<kPer>(rk, phk + (long long)s1 * Df, n1, Df, tid);
+          fetch_v(s1, n1);
+        }
+      } else {
+        load_rows(phq + (long long)s0 * Df, qc, 0, nrow);
+        load_rows(phk + (long long)s0 * Df, kc, 0, nrow);
+        load_v(s0, nrow);
+        __syncthreads();
+      }
+      {  // scores phi(q_i).phi(k_j) for j <= i inside the chunk, four partial sums
         const int i = tid / kLinChunk, j = tid % kLinChunk;
-        float acc = 0.0f;
-        if (j <= i)
-          for (int f = 0; f < Df; ++f) acc = fmaf(qc[i * ld + f], kc[j * ld + f], acc);
-        sc[i * kLinChunk + j] = acc;
+        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+        if (j <= i) {
+          const float* qi = qc + i * ld;
+          const float* kj = kc + j * ld;
+          int f = 0;
+          for (; f + 3 < Df; f += 4) {
+            a0 = fmaf(qi[f], kj[f], a0);
+            a1 = fmaf(qi[f + 1], kj[f + 1], a1);
+            a2 = fmaf(qi[f + 2], kj[f + 2], a2);
+            a3 = fmaf(qi[f + 3], kj[f + 3], a3);
+          }
+          for (; f < Df; ++f) a0 = fmaf(qi[f], kj[f], a0);
+        }
+        sc[i * kLinChunk + j] = (a0 + a1) + (a2 + a3);
       }
       __syncthreads();
       emit(s0, nrow, true);  // uses the state before this chunk
@@ -350,18 +510,43 @@ __global__ void __launch_bounds__(kLinThreads) linear_attn_kernel(LinearParams p
       __syncthreads();
     }
   } else {
-    for (int s0 = 0; s0 < p.S; s0 += kLinChunk) {
-      const int nrow = min(kLinChunk, p.S - s0);
-      load_rows(phk + (long long)s0 * Df, kc, 0, nrow);
-      load_v(s0, nrow);
-      __syncthreads();
-      accumulate();
-      __syncthreads();
+    // keys and values into the state, then the queries against it
+    if constexpr (kPer > 0) {
+      lin_fetch_rows<kPer>(rk, phk, min(kLinChunk, p.S), Df, tid);
+      fetch_v(0, min(kLinChunk, p.S));
     }
     for (int s0 = 0; s0 < p.S; s0 += kLinChunk) {
       const int nrow = min(kLinChunk, p.S - s0);
-      load_rows(phq + (long long)s0 * Df, qc, 0, nrow);
+      if constexpr (kPer > 0) {
+        lin_commit_rows<kPer>(rk, kc, ld, Df, tid);
+        commit_v();
+        __syncthreads();
+        const int s1 = s0 + kLinChunk;
+        if (s1 < p.S) {
+          lin_fetch_rows<kPer>(rk, phk + (long long)s1 * Df, min(kLinChunk, p.S - s1), Df, tid);
+          fetch_v(s1, min(kLinChunk, p.S - s1));
+        }
+      } else {
+        load_rows(phk + (long long)s0 * Df, kc, 0, nrow);
+        load_v(s0, nrow);
+        __syncthreads();
+      }
+      accumulate();
       __syncthreads();
+    }
+    if constexpr (kPer > 0) lin_fetch_rows<kPer>(rq, phq, min(kLinChunk, p.S), Df, tid);
+    for (int s0 = 0; s0 < p.S; s0 += kLinChunk) {
+      const int nrow = min(kLinChunk, p.S - s0);
+      if constexpr (kPer > 0) {
+        lin_commit_rows<kPer>(rq, qc, ld, Df, tid);
+        __syncthreads();
+        const int s1 = s0 + kLinChunk;
+        if (s1 < p.S)
+          lin_fetch_rows<kPer>(rq, phq + (long long)s1 * Df, min(kLinChunk, p.S - s1), Df, tid);
+      } else {
+        load_rows(phq + (long long)s0 * Df, qc, 0, nrow);
+        __syncthreads();
+      }
       emit(s0, nrow, false);
       __syncthreads();
     }
@@ -381,13 +566,14 @@ __global__ void __launch_bounds__(kLinThreads) linear_attn_kernel(LinearParams p
 
 // Phase A of the segmented causal pass: per (segment, b, kv head, column
 // slice) the segment's sums of phi(k) v^T and phi(k) into the workspace.
+template <int kPer>
 __global__ void __launch_bounds__(kLinThreads) linear_segsum_kernel(LinearParams p) {
-  extern __shared__ float sm[];
+  extern __shared__ __align__(16) float sm[];
   const int Df = p.Df, ld = Df + 1;
-  float* kv = sm;
-  float* ks = kv + Df * kLinCols;
-  float* kc = ks + Df;
-  float* vc = kc + kLinChunk * ld;
+  float* kv = sm;                        // [Df][32]
+  float* vc = kv + Df * kLinCols;        // [16][32]
+  float* ks = vc + kLinChunk * kLinCols; // [Df]
+  float* kc = ks + Df;                   // [16][Df + 1]
   const int tid = threadIdx.x;
   const int bk = blockIdx.x, b = bk / p.Hkv, hkv = bk % p.Hkv;
   const int d0 = blockIdx.y * kLinCols;
@@ -397,28 +583,36 @@ __global__ void __launch_bounds__(kLinThreads) linear_segsum_kernel(LinearParams
   const float* phk = p.phi_k + (long long)bk * p.S * Df;
   for (int i = tid; i < Df * kLinCols; i += kLinThreads) kv[i] = 0.0f;
   for (int f = tid; f < Df; f += kLinThreads) ks[f] = 0.0f;
-  for (int s0 = r0; s0 < r1; s0 += kLinChunk) {
-    const int nrow = min(kLinChunk, r1 - s0);
-    __syncthreads();
-    for (int i = tid; i < kLinChunk * Df; i += kLinThreads) {
-      const int r = i / Df, f = i % Df;
-      kc[r * ld + f] = (r < nrow) ? phk[(long long)(s0 + r) * Df + f] : 0.0f;
-    }
-    for (int i = tid; i < kLinChunk * kLinCols; i += kLinThreads) {
-      const int r = i / kLinCols, c = i % kLinCols;
-      vc[i] = (r < nrow && c < ncol)
+  constexpr int kP = kPer > 0 ? kPer : 1;
+  float rk[kP], rv[kLinVPer];
+  auto fetch = [&](int s0, int nrow) {
+    if constexpr (kPer > 0) lin_fetch_rows<kPer>(rk, phk + (long long)s0 * Df, nrow, Df, tid);
+#pragma unroll
+    for (int m = 0; m < kLinVPer; ++m) {
+      const int i = tid + m * kLinThreads, r = i / kLinCols, c = i % kLinCols;
+      rv[m] = (r < nrow && c < ncol)
                   ? load_elem(p.v, b * p.v_sb + (long long)(s0 + r) * p.v_ss + hkv * p.v_sh + d0 + c,
                               p.v_f32)
                   : 0.0f;
     }
+  };
+  if (r0 < r1) fetch(r0, min(kLinChunk, r1 - r0));
+  for (int s0 = r0; s0 < r1; s0 += kLinChunk) {
+    const int nrow = min(kLinChunk, r1 - s0);
     __syncthreads();
-    for (int i = tid; i < Df * kLinCols; i += kLinThreads) {
-      const int f = i / kLinCols, c = i % kLinCols;
-      float acc = kv[i];
-#pragma unroll
-      for (int j = 0; j < kLinChunk; ++j) acc = fmaf(kc[j * ld + f], vc[j * kLinCols + c], acc);
-      kv[i] = acc;
+    if constexpr (kPer > 0) {
+      lin_commit_rows<kPer>(rk, kc, ld, Df, tid);
+    } else {
+      for (int i = tid; i < kLinChunk * Df; i += kLinThreads) {
+        const int r = i / Df, f = i % Df;
+        kc[r * ld + f] = (r < nrow) ? phk[(long long)(s0 + r) * Df + f] : 0.0f;
+      }
     }
+#pragma unroll
+    for (int m = 0; m < kLinVPer; ++m) vc[tid + m * kLinThreads] = rv[m];
+    __syncthreads();
+    if (s0 + kLinChunk < r1) fetch(s0 + kLinChunk, min(kLinChunk, r1 - s0 - kLinChunk));
+    lin_accumulate(kv, vc, kc, ld, Df, tid);
     for (int f = tid; f < Df; f += kLinThreads) {
       float acc = ks[f];
 #pragma unroll
@@ -477,9 +671,9 @@ size_t linear_workspace_bytes(int B, int H, int Hkv, int S, int Df, int D, int c
 }
 
 int linear_attn_max_features() {
-  return (227 * 1024 / (int)sizeof(float) - (kLinChunk * kLinCols + kLinChunk * kLinChunk +
-                                              kLinChunk + 2 * kLinChunk)) /
-         (kLinCols + 1 + 2 * kLinChunk);
+  // lin_smem_floats(Df) = (kLinCols + 1 + 2 kLinChunk) Df + the Df-free terms
+  const int fixed = kLinChunk * kLinCols + kLinPart + kLinChunk * kLinChunk + 2 * kLinChunk;
+  return (227 * 1024 / (int)sizeof(float) - fixed) / (kLinCols + 1 + 2 * kLinChunk);
 }
 
 cudaError_t launch_linear_attn(const LinearParams& p, cudaStream_t stream) {
@@ -490,26 +684,42 @@ cudaError_t launch_linear_attn(const LinearParams& p, cudaStream_t stream) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    e = cudaFuncSetAttribute(linear_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             227 * 1024);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(linear_segsum_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               227 * 1024);
+    const cudaFuncAttribute a = cudaFuncAttributeMaxDynamicSharedMemorySize;
+    const void* fns[8] = {(const void*)linear_attn_kernel<0>, (const void*)linear_attn_kernel<4>,
+                          (const void*)linear_attn_kernel<8>, (const void*)linear_attn_kernel<16>,
+                          (const void*)linear_segsum_kernel<0>,
+                          (const void*)linear_segsum_kernel<4>,
+                          (const void*)linear_segsum_kernel<8>,
+                          (const void*)linear_segsum_kernel<16>};
+    for (int i = 0; i < 8 && e == cudaSuccess; ++i) e = cudaFuncSetAttribute(fns[i], a, 227 * 1024);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
+  // prefetch width: phi elements per thread per chunk
+  const int per = p.Df <= 64 ? 4 : p.Df <= 128 ? 8 : p.Df <= 256 ? 16 : 0;
   const int nslice = (p.D + kLinCols - 1) / kLinCols;
   LinearParams q = p;
   q.n_seg = p.causal ? linear_segments(p.B, p.H, p.S, p.D) : 1;
   q.seg_len = (p.S + q.n_seg - 1) / max(q.n_seg, 1);
   if (q.n_seg > 1) {
     if (!p.carry_kv || !p.carry_ks) return cudaErrorInvalidValue;  // the ABI checks the workspace
-    linear_segsum_kernel<<<dim3(p.B * p.Hkv, nslice, q.n_seg), kLinThreads, smem, stream>>>(q);
+    const dim3 sg(p.B * p.Hkv, nslice, q.n_seg);
+    switch (per) {
+      case 4: linear_segsum_kernel<4><<<sg, kLinThreads, smem, stream>>>(q); break;
+      case 8: linear_segsum_kernel<8><<<sg, kLinThreads, smem, stream>>>(q); break;
+      case 16: linear_segsum_kernel<16><<<sg, kLinThreads, smem, stream>>>(q); break;
+      default: linear_segsum_kernel<0><<<sg, kLinThreads, smem, stream>>>(q); break;
+    }
     const long long n = (long long)p.B * p.Hkv * p.Df * (p.D + 1);
     linear_scan_kernel<<<(int)min((n + 255) / 256, 148ll * 8), 256, 0, stream>>>(q);
   }
   dim3 grid(p.B * p.H, nslice, q.n_seg);
-  linear_attn_kernel<<<grid, kLinThreads, smem, stream>>>(q);
+  switch (per) {
+    case 4: linear_attn_kernel<4><<<grid, kLinThreads, smem, stream>>>(q); break;
+    case 8: linear_attn_kernel<8><<<grid, kLinThreads, smem, stream>>>(q); break;
+    case 16: linear_attn_kernel<16><<<grid, kLinThreads, smem, stream>>>(q); break;
+    default: linear_attn_kernel<0><<<grid, kLinThreads, smem, stream>>>(q); break;
+  }
   return cudaGetLastError();
 }
 
