@@ -530,6 +530,24 @@ __global__ void __launch_bounds__(384, 1)
         if (failed) break;
         tc_fence_after();
         const uint32_t s_addr = lane_addr + Cfg::col_s(buf) + col_h;
+        if constexpr (kSparse) {
+          if (__all_sync(0xffffffffu, allow == 0ull)) {
+            // No key of this half is visible to any of the warp's rows (a
+            // half-tile between selected blocks): publish P = 0 without
+            // reading S or taking exponentials. The row statistics are
+            // unchanged, as a tile of -inf scores would leave them.
+            uint32_t z[32];
+#pragma unroll
+            for (int c = 0; c < 32; ++c) z[c] = 0u;
+            ENL_TMEM_ST32(s_addr, z, 0);
+            if constexpr (kSplit) ENL_TMEM_ST32(s_addr + 32, z, 0);
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_p_ready + 2 * buf + half);
+            continue;
+          }
+        }
         float s[64];
         {
           uint32_t sr[64];
