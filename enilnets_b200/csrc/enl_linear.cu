@@ -139,6 +139,44 @@ __global__ void __launch_bounds__(kPtThreads) phi_perf_kernel(PhiParams p) {
       atomicMax(reinterpret_cast<int*>(p.stab) + bh, ord_enc(m));
     return;
   }
+  if (kMode == 1 && p.Df <= 4 * kPtFeat) {
+    // Up to four feature chunks: keep every projection in registers, so the
+    // GEMM runs once (row maxima, then the features from the kept values).
+    float keep[4][4][4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      if (c * kPtFeat >= p.Df) break;
+      chunk(c * kPtFeat);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float m = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          keep[c][i][j] = acc[i][j];
+          if (valid(c * kPtFeat, i, j) && acc[i][j] == acc[i][j]) m = fmaxf(m, acc[i][j]);
+        }
+        if (m > -INFINITY) atomicMax(rmax + ty * 4 + i, ord_enc(m));
+      }
+    }
+    __syncthreads();  // row maxima complete
+    const float norm = rsqrtf((float)p.Df);
+    float* out = p.phi + ((long long)bh * p.S + s0) * p.Df;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      if (c * kPtFeat >= p.Df) break;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = ty * 4 + i;
+        const float st = ord_dec(rmax[r]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (valid(c * kPtFeat, i, j))
+            out[(long long)r * p.Df + c * kPtFeat + tx * 4 + j] =
+                expf(keep[c][i][j] - sq[r] - st) * norm;
+      }
+    }
+    return;
+  }
   if (kMode == 1) {  // row maxima first
     for (int f0 = 0; f0 < p.Df; f0 += kPtFeat) {
       chunk(f0);
