@@ -413,6 +413,14 @@ int enl_attn_backward(const enl_backward_args* a, void* stream) {
   p.dv_sb = a->dv_stride_b;
   p.dv_ss = a->dv_stride_s;
   p.dv_sh = a->dv_stride_h;
+  {
+    auto v4 = [](const void* ptr, int64_t x, int64_t y, int64_t z) {
+      return aligned16(ptr) && x % 4 == 0 && y % 4 == 0 && z % 4 == 0;
+    };
+    p.out_vec4 = v4(a->dq, a->dq_stride_b, a->dq_stride_s, a->dq_stride_h) &&
+                 v4(a->dk, a->dk_stride_b, a->dk_stride_s, a->dk_stride_h) &&
+                 v4(a->dv, a->dv_stride_b, a->dv_stride_s, a->dv_stride_h);
+  }
   const int D = a->head_dim <= 64 ? 64 : 128;
   cudaError_t e = launch_backward(tq, tk, tv, tdo, q, p, D, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "enl_attn_backward launch");

@@ -160,6 +160,39 @@ __global__ void bwd_prep_kernel(BwdPrepParams q) {
   }
 }
 
+// Epilogue staging: accumulator rows in shared memory at a stride of D + 4
+// floats, so rows stay 16-byte aligned and a warp's float4 writes (one row
+// per lane) are conflict-free per quarter warp.
+template <int D>
+__device__ __forceinline__ void stage_row16(float* stg, int rloc, int col0,
+                                            const uint32_t (&a)[16], float mul, bool have) {
+  float4* dst = reinterpret_cast<float4*>(stg + rloc * (D + 4) + col0);
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    dst[k] = have ? make_float4(__uint_as_float(a[4 * k]) * mul, __uint_as_float(a[4 * k + 1]) * mul,
+                                __uint_as_float(a[4 * k + 2]) * mul,
+                                __uint_as_float(a[4 * k + 3]) * mul)
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+// Staged rows [0, nrows) to base + r * ss, d_real columns each, one row per
+// warp step: float4 per lane when the outputs are 16-byte aligned (vec4),
+// else one float per lane.
+template <int D>
+__device__ __forceinline__ void store_rows(const float* stg, float* base, long long ss, int nrows,
+                                           int d_real, bool vec4, int warp, int lane) {
+  if (vec4) {
+#pragma unroll 4
+    for (int r = warp; r < nrows; r += 8)
+      for (int c4 = lane; c4 < d_real / 4; c4 += 32)
+        *reinterpret_cast<float4*>(base + r * ss + 4 * c4) =
+            *reinterpret_cast<const float4*>(stg + r * (D + 4) + 4 * c4);
+  } else {
+    for (int r = warp; r < nrows; r += 8)
+      for (int c = lane; c < d_real; c += 32) base[r * ss + c] = stg[r * (D + 4) + c];
+  }
+}
+
 // ---------------------------------------------------------------------------
 // dK, dV. CTA c -> key tile c / (B * Hkv) (small tiles first: under a causal
 // mask they see the most query tiles), (b, kv head) c % (B * Hkv).
@@ -426,8 +459,7 @@ __global__ void __launch_bounds__(320, 1)
       ok = __all_sync(0xffffffffu,
                       mbar_wait(bar_done, (n_units - 1) & 1, abort_flag, 92) &&
                           mbar_wait(bar_done + 1, (n_units - 1) & 1, abort_flag, 93));
-    float* stg = reinterpret_cast<float*>(smem + Cfg::kOffStr);  // [128][D + 1]
-    constexpr int ld = D + 1;
+    float* stg = reinterpret_cast<float*>(smem + Cfg::kOffStr);  // [128][D + 4]
 #pragma unroll 1
     for (int arr = 0; arr < 2; ++arr) {
       if (ok) {
@@ -440,20 +472,15 @@ __global__ void __launch_bounds__(320, 1)
           uint32_t av[16];
           __syncwarp();
           if (n_units > 0) ENL_TMEM_LD16(lane_addr + col_acc + col0, av);
-#pragma unroll
-          for (int e = 0; e < 16; ++e)
-            stg[rloc * ld + col0 + e] = n_units > 0 ? __uint_as_float(av[e]) * mul : 0.0f;
+          stage_row16<D>(stg, rloc, col0, av, mul, n_units > 0);
         }
       }
       named_bar_sync(1, 256);
       if (ok) {
         const long long ss = arr ? p.dk_ss : p.dv_ss;
         float* base = arr ? p.dk + b * p.dk_sb + hkv * p.dk_sh : p.dv + b * p.dv_sb + hkv * p.dv_sh;
-        for (int r = warp; r < 128; r += 8) {
-          const long long jr = (long long)kt * 128 + r;
-          if (jr >= p.Skv) break;
-          for (int c = lane; c < p.d_real; c += 32) base[jr * ss + c] = stg[r * ld + c];
-        }
+        store_rows<D>(stg, base + (long long)kt * 128 * ss, ss, min(128, p.Skv - kt * 128),
+                      p.d_real, p.out_vec4 != 0, warp, lane);
       }
       named_bar_sync(1, 256);
     }
@@ -694,8 +721,7 @@ __global__ void __launch_bounds__(320, 1)
       ok = __all_sync(0xffffffffu,
                       mbar_wait(bar_done, (n_units - 1) & 1, abort_flag, 112) &&
                           mbar_wait(bar_done + 1, (n_units - 1) & 1, abort_flag, 113));
-    float* stg = reinterpret_cast<float*>(smem + Cfg::kOffStr);  // [128][D + 1]
-    constexpr int ld = D + 1;
+    float* stg = reinterpret_cast<float*>(smem + Cfg::kOffStr);  // [128][D + 4]
     if (ok) {
       tc_fence_after();
 #pragma unroll 1
@@ -704,19 +730,14 @@ __global__ void __launch_bounds__(320, 1)
         uint32_t aq[16];
         __syncwarp();
         if (n_units > 0) ENL_TMEM_LD16(lane_addr + Cfg::kColAcc0 + col0, aq);
-#pragma unroll
-        for (int e = 0; e < 16; ++e)
-          stg[rloc * ld + col0 + e] = n_units > 0 ? __uint_as_float(aq[e]) * p.scale : 0.0f;
+        stage_row16<D>(stg, rloc, col0, aq, p.scale, n_units > 0);
       }
     }
     named_bar_sync(1, 256);
     if (ok) {
-      float* base = p.dq + b * p.dq_sb + h * p.dq_sh;
-      for (int r = warp; r < 128; r += 8) {
-        const long long ir = (long long)qt * 128 + r;
-        if (ir >= p.Sq) break;
-        for (int c = lane; c < p.d_real; c += 32) base[ir * p.dq_ss + c] = stg[r * ld + c];
-      }
+      float* base = p.dq + b * p.dq_sb + h * p.dq_sh + (long long)qt * 128 * p.dq_ss;
+      store_rows<D>(stg, base, p.dq_ss, min(128, p.Sq - qt * 128), p.d_real, p.out_vec4 != 0,
+                    warp, lane);
     }
     named_bar_sync(1, 256);
   }

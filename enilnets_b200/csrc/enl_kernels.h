@@ -80,6 +80,7 @@ struct BwdParams {
   long long dk_sb, dk_ss, dk_sh;
   float* dv;
   long long dv_sb, dv_ss, dv_sh;
+  int out_vec4;  // dq, dk, dv 16-byte aligned with strides multiple of 4: float4 stores
 };
 cudaError_t launch_backward(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                             const CUtensorMap& tdo, const BwdPrepParams& prep, const BwdParams& p,
