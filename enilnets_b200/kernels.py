@@ -135,13 +135,15 @@ def attention_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: tor
                        lse: torch.Tensor, dout: torch.Tensor, *, causal: bool = False,
                        window: Optional[int] = None,
                        alibi_slopes: Optional[torch.Tensor] = None,
-                       scale: Optional[float] = None):
+                       scale: Optional[float] = None, out=None):
     """dQ, dK, dV of attention_prefill (K5, nn/flash_attention.py:83-114).
 
     q: (B, Sq, H, D), k, v: (B, Skv, Hkv, D), dout like o: bf16 (the forward's
     operands); o: the forward output, bf16 or fp32; lse: (B, H, Sq) fp32 from
     attention_prefill(..., return_lse=True). Returns fp32 dq (B, Sq, H, D) and
-    dk, dv (B, Skv, Hkv, D), dk/dv summed over each kv head's query heads.
+    dk, dv (B, Skv, Hkv, D), dk/dv summed over each kv head's query heads;
+    out=(dq, dk, dv) writes into given fp32 views of those shapes instead
+    (any strides with a contiguous head dim).
     """
     for name, t in (("q", q), ("k", k), ("v", v), ("dout", dout)):
         _require_cuda(name, t, torch.bfloat16)
@@ -164,9 +166,17 @@ def attention_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: tor
         _require_cuda("alibi_slopes", alibi_slopes, torch.float32, last_contiguous=False)
         if tuple(alibi_slopes.shape) != (H,) or not alibi_slopes.is_contiguous():
             raise ValueError(f"alibi_slopes must be a contiguous float32 ({H},) tensor")
-    dq = torch.empty((B, Sq, H, D), device=q.device, dtype=torch.float32)
-    dk = torch.empty((B, Skv, Hkv, D), device=q.device, dtype=torch.float32)
-    dv = torch.empty((B, Skv, Hkv, D), device=q.device, dtype=torch.float32)
+    if out is None:
+        dq = torch.empty((B, Sq, H, D), device=q.device, dtype=torch.float32)
+        dk = torch.empty((B, Skv, Hkv, D), device=q.device, dtype=torch.float32)
+        dv = torch.empty((B, Skv, Hkv, D), device=q.device, dtype=torch.float32)
+    else:
+        dq, dk, dv = out
+        for name, t, shape in (("dq", dq, (B, Sq, H, D)), ("dk", dk, (B, Skv, Hkv, D)),
+                               ("dv", dv, (B, Skv, Hkv, D))):
+            _require_cuda(name, t, torch.float32)
+            if tuple(t.shape) != shape:
+                raise ValueError(f"{name} must be {shape}, got {tuple(t.shape)}")
     a = nat.BackwardArgs()
     a.q, a.k, a.v, a.o, a.dout = (t.data_ptr() for t in (q, k, v, o, dout))
     a.lse, a.dq, a.dk, a.dv = lse.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr()

@@ -85,3 +85,39 @@ def test_backward_matches_reference(cuda, golden_dir):
         for name, g, r in zip(("dq", "dk", "dv"), got, ref):
             err = np.max(np.abs(_np(g) - r))
             assert err <= 3 * TOL * max(1.0, np.abs(r).max()), (c, name, err)
+
+
+def test_backward_cross_shapes_match_oracle(cuda):
+    """Queries and keys of different lengths (positions both from 0), as a
+    cross-attention layer would call it; GQA and ALiBi on."""
+    rs = np.random.RandomState(11)
+    B, Sq, Skv, H, Hkv, D = 2, 200, 333, 4, 2, 64
+    q = rs.standard_normal((B, Sq, H, D))
+    k = rs.standard_normal((B, Skv, Hkv, D))
+    v = rs.standard_normal((B, Skv, Hkv, D))
+    do = rs.standard_normal((B, Sq, H, D))
+    slopes = ar.alibi_slopes(H)
+    ins, got = _run(cuda, q, k, v, do, False, None, slopes)
+    qn, kn, vn, don = (_np(t) for t in ins)
+    ref = ar.attention_backward_ref(qn, kn, vn, don, causal=False, window=None, alibi=slopes)
+    _check(got, ref, "cross")
+
+
+def test_backward_strided_outputs_equal_contiguous(cuda):
+    """Outputs written into views whose row strides are not multiples of four
+    floats take the scalar epilogue; they equal the contiguous outputs."""
+    import torch
+    from enilnets_b200 import kernels
+    rs = np.random.RandomState(12)
+    B, S, H, D = 1, 300, 2, 128
+    q, k, v, do = (torch.from_numpy(rs.standard_normal((B, S, H, D)).astype(np.float32))
+                   .cuda().to(torch.bfloat16) for _ in range(4))
+    o, lse = kernels.attention_prefill(q, k, v, causal=True, out_dtype=torch.float32,
+                                       return_lse=True)
+    ref = kernels.attention_backward(q, k, v, o, lse, do, causal=True)
+    wide = [torch.full((B, S, H, D + 2), float("nan"), device=cuda) for _ in range(3)]
+    views = tuple(w[..., :D] for w in wide)
+    got = kernels.attention_backward(q, k, v, o, lse, do, causal=True, out=views)
+    for a, b in zip(got, ref):
+        assert torch.equal(a, b)
+    torch.cuda.synchronize()
