@@ -11,12 +11,14 @@
 //                         stay in shared memory while the query tiles of
 //                         every query head of the group stream through;
 //                         S^T = K Q^T and dP^T = V dO^T in tensor memory,
-//                         P^T and dS^T written back over them as bf16, then
+//                         P^T and dS^T written back over dP^T as bf16, then
 //                         dV += P^T dO and dK += dS^T Q accumulate in tensor
 //                         memory (GQA sums the group's heads exactly there);
 //   attn_bwd_dq_sm100     one CTA per (batch, head, 128-query tile): Q and dO
-//                         stay, K and V stream; S and dP again, dS over S,
+//                         stay, K and V stream; S and dP again, dS over dP,
 //                         dQ += dS K in tensor memory.
+// Both kernels end by staging the accumulator rows in shared memory and
+// storing whole rows.
 // Tensor memory per CTA: S (128 columns) + dP (128) + two D-column
 // accumulators, 512 columns at D = 128: no room for a second S. Instead each
 // tile is split into two 64-column halves with their own barriers. The
@@ -25,8 +27,8 @@
 // they are done: the next tile's S of that half is issued right behind this
 // tile's accumulation, and only its dP waits for the accumulation to have
 // read P and dS. The tensor pipe works while the other half's elementwise
-// warps run. Recomputing S and dP in the
-// dQ pass costs two GEMMs of seven but needs no atomics and no dQ staging.
+// warps run. Recomputing S and dP in the dQ pass costs two GEMMs of seven but
+// needs no atomics and no dQ staging.
 //
 // Warp roles (320 threads): 0-7 elementwise (warps w and w + 4 share TMEM
 // lanes 32 (w % 4) .. + 31 and split the 128 columns in halves), 8 TMA, 9 MMA.
