@@ -696,14 +696,31 @@ __global__ void linear_scan_kernel(LinearParams p) {
 
 // Segments of the causal pass: enough CTAs for two waves, segments of at
 // least 256 rows.
-int linear_segments(int B, int H, int S, int D) {
-  const int ctas = B * H * ((D + kLinCols - 1) / kLinCols);
-  const int want = (2 * 148 + ctas - 1) / max(ctas, 1);
-  return max(1, min(want, S / 256));
+// Segments of the causal pass (segments of at least 256 rows): the count
+// whose CTAs best fill whole waves, taking the first that fills them to 95%.
+// A wave is 148 SMs times the CTAs one SM holds: two (the attention kernel's
+// registers allow two), fewer when shared memory does not.
+int linear_segments(int B, int H, int S, int D, int Df) {
+  const long long ctas = (long long)B * H * ((D + kLinCols - 1) / kLinCols);
+  const int smem = lin_smem_floats(Df) * (int)sizeof(float);
+  const long long slots = 148ll * max(1, min(2, (227 * 1024) / max(smem, 1)));
+  const int max_n = max(1, min(S / 256, 64));
+  int best = 1;
+  double best_util = 0.0;
+  for (int n = 1; n <= max_n; ++n) {
+    const long long c = ctas * n;
+    const double util = (double)c / (double)(((c + slots - 1) / slots) * slots);
+    if (util > best_util + 1e-9) {
+      best = n;
+      best_util = util;
+    }
+    if (util >= 0.95) break;
+  }
+  return best;
 }
 
 size_t linear_workspace_bytes(int B, int H, int Hkv, int S, int Df, int D, int causal) {
-  const int n = causal ? linear_segments(B, H, S, D) : 1;
+  const int n = causal ? linear_segments(B, H, S, D, Df) : 1;
   if (n <= 1) return 0;
   return (size_t)n * B * Hkv * ((size_t)Df * D + Df) * sizeof(float);
 }
@@ -737,7 +754,7 @@ cudaError_t launch_linear_attn(const LinearParams& p, cudaStream_t stream) {
   const int per = p.Df <= 64 ? 4 : p.Df <= 128 ? 8 : p.Df <= 256 ? 16 : 0;
   const int nslice = (p.D + kLinCols - 1) / kLinCols;
   LinearParams q = p;
-  q.n_seg = p.causal ? linear_segments(p.B, p.H, p.S, p.D) : 1;
+  q.n_seg = p.causal ? linear_segments(p.B, p.H, p.S, p.D, p.Df) : 1;
   q.seg_len = (p.S + q.n_seg - 1) / max(q.n_seg, 1);
   if (q.n_seg > 1) {
     if (!p.carry_kv || !p.carry_ks) return cudaErrorInvalidValue;  // the ABI checks the workspace
