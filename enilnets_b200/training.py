@@ -131,6 +131,7 @@ def self_attention_backward(layer: Dict[str, Any], cache: Dict[str, Any],
 def multihead_attention_forward_train(layer: Dict[str, Any], x) -> Tuple[np.ndarray, Dict]:
     """NumPy in, NumPy out: the layer's training forward and its cache."""
     import torch
+    _check_trainable(layer)  # before any device work
     y, cache = self_attention_forward_train(layer, to_device(np.asarray(x), torch.float32))
     return to_numpy(y), cache
 

@@ -117,3 +117,29 @@ def test_prefill_workspace_bytes_is_host_only_arithmetic():
         n = 2 * S * H * 2 * 40 * 2
         return (n + 255) // 256 * 256
     assert lib.enl_prefill_workspace_bytes(ctypes.byref(a)) == planes(100, 8) + 2 * planes(300, 2)
+
+
+def test_linear_workspace_fills_whole_waves():
+    """Host-only arithmetic: the causal linear pass splits a sequence into the
+    segment count whose CTAs best fill whole waves (148 SMs x 2 CTAs), first
+    count reaching 95%, segments of at least 256 rows; one partial state per
+    segment (num_features x head_dim + num_features floats per batch and kv
+    head). Short or non-causal calls need no workspace."""
+    lib = _native.load()
+
+    def ws(B, H, Hkv, S, Df, D, causal):
+        a = _native.LinearArgs()
+        a.batch, a.num_heads, a.num_kv_heads, a.seq = B, H, Hkv, S
+        a.num_features, a.head_dim, a.causal = Df, D, int(causal)
+        return lib.enl_linear_workspace_bytes(ctypes.byref(a))
+
+    def state(n, B, Hkv, Df, D):
+        return n * B * Hkv * (Df * D + Df) * 4
+
+    # 128 CTAs per segment: 9 segments = 1152 CTAs, 97% of four waves of 296
+    assert ws(4, 16, 16, 4096, 64, 64, True) == state(9, 4, 16, 64, 64)
+    assert ws(4, 16, 16, 4096, 256, 64, True) == state(9, 4, 16, 256, 64)
+    # few CTAs: as many segments as 256-row segments allow
+    assert ws(1, 2, 2, 1500, 64, 64, True) == state(5, 1, 2, 64, 64)
+    assert ws(4, 16, 16, 4096, 64, 64, False) == 0
+    assert ws(1, 2, 2, 255, 64, 64, True) == 0
