@@ -9,6 +9,12 @@
 #include "enl_common.cuh"
 #include "enl_kernels.h"
 
+// K1 work items come in sections of (batch, head) pairs whose K/V take about
+// this many MiB, a quarter of the 126 MB L2 by default.
+#ifndef ENL_PREFILL_SECTION_MB
+#define ENL_PREFILL_SECTION_MB 32
+#endif
+
 namespace enl {
 namespace {
 
@@ -256,7 +262,7 @@ int prefill_impl(const enl_prefill_args* a, const enl_sparse_layout* layout, voi
     const int G = a->num_heads / a->num_kv_heads;
     const double kv_bytes_per_head =
         4.0 * a->seq_kv * D * (split ? 2 : 1) / G;  // K and V, bf16, shared by G heads
-    const double budget = 32.0 * (1 << 20);
+    const double budget = ENL_PREFILL_SECTION_MB * double(1 << 20);
     long long sec = (long long)(budget / kv_bytes_per_head);
     const long long n_bh = (long long)a->batch * a->num_heads;
     p.sec_bh = (int)std::max(1ll, std::min(n_bh, sec));
