@@ -32,7 +32,7 @@ DEVICE_ERRORS = {1: "an mbarrier wait exceeded its time budget",
                  3: "a launch-time shape invariant was violated"}
 
 
-ABI_VERSION = 5  # ENL_ABI_VERSION of include/enl_attn.h
+ABI_VERSION = 6  # ENL_ABI_VERSION of include/enl_attn.h
 
 
 class PrefillArgs(Structure):
@@ -52,6 +52,7 @@ class PrefillArgs(Structure):
         ("q_pos0", c_int64), ("k_pos0", c_int64),
         ("scale", c_float),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+        ("kv_mask", c_void_p), ("kv_mask_stride_b", c_int64),
     ]
 
 

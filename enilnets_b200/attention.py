@@ -131,19 +131,32 @@ def split_heads(t, heads: int, head_dim: int, offset: int = 0):
     return t[..., offset:offset + heads * head_dim].unflatten(-1, (heads, head_dim))
 
 
-def lengths_from_mask(mask, B: int, S: int):
-    """Per-row valid lengths from a boolean key-padding mask (True = real
-    token, graph/sequence.py:23-29). The kernels take prefix lengths; a mask
-    whose real tokens do not form a prefix raises ValueError."""
+def classify_key_mask(mask, B: int, S: int):
+    """A boolean key-padding mask (True = real token) as the kernel takes it.
+
+    graph/sequence.py:162-168 adds -1e9 for any (batch, seq) mask. A mask
+    whose real tokens form a prefix in every row (what lengths_to_mask,
+    graph/sequence.py:23-29, builds) becomes ("lengths", int32 (B,)); any
+    other mask (left padding, holes) ("words", int64 (B, ceil(S/64)) packed
+    bits). Host arrays; raises ValueError for a wrong shape, as the
+    reference does."""
     m = np.asarray(mask if not hasattr(mask, "detach") else mask.detach().cpu().numpy())
     if m.shape != (B, S):
         raise ValueError(f"key_padding_mask shape {m.shape} must be (batch, seq) = {(B, S)}")
     m = m.astype(bool)
     lengths = m.sum(axis=1)
-    if not np.array_equal(m, np.arange(S)[None, :] < lengths[:, None]):
-        raise ValueError("key_padding_mask must mark a prefix of real tokens in every row "
-                         "(as lengths_to_mask builds); the B200 kernel takes valid lengths.")
-    return lengths.astype(np.int32)
+    if np.array_equal(m, np.arange(S)[None, :] < lengths[:, None]):
+        return "lengths", lengths.astype(np.int32)
+    return "words", kernels.key_mask_words(m)
+
+
+def key_mask_args(mask, B: int, S: int) -> dict:
+    """classify_key_mask as attention_prefill keyword arguments on the device."""
+    import torch
+    kind, arr = classify_key_mask(mask, B, S)
+    if kind == "lengths":
+        return {"kv_valid_len": to_device(arr, torch.int32)}
+    return {"kv_mask": torch.from_numpy(arr).to(device())}
 
 
 def omega_tensor(layer: dict):
@@ -198,15 +211,15 @@ def self_attention(layer: dict, x, key_padding_mask=None, mask_mode: Optional[st
                                alibi_slopes=alibi_tensor(H) if scheme == "alibi" else None,
                                out_dtype=compute_dtype())
         return project(ctx.flatten(-2), layer, "o").float()
-    lens = None
+    masks = {}
     mode = mask_mode or "exclude"
     if key_padding_mask is not None:
-        lens = to_device(lengths_from_mask(key_padding_mask, B, S), torch.int32)
+        masks = key_mask_args(key_padding_mask, B, S)
         mode = mask_mode or "additive"
     ctx = kernels.attention_prefill(
         q, k, v, causal=bool(layer.get("causal", False)), window=layer.get("window_size"),
-        kv_valid_len=lens, alibi_slopes=alibi_tensor(H) if scheme == "alibi" else None,
-        mask_mode=mode, out_dtype=compute_dtype())
+        alibi_slopes=alibi_tensor(H) if scheme == "alibi" else None,
+        mask_mode=mode, out_dtype=compute_dtype(), **masks)
     return project(ctx.flatten(-2), layer, "o").float()
 
 
@@ -224,11 +237,11 @@ def cross_attention(layer: dict, x, memory, memory_key_padding_mask=None):
     kv = project(memory, layer, "kv")
     k = split_heads(kv, Hkv, D, 0)
     v = split_heads(kv, Hkv, D, Hkv * D)
-    lens = None
+    masks = {}
     mode = "exclude"
     if memory_key_padding_mask is not None:
-        lens = to_device(lengths_from_mask(memory_key_padding_mask, B, Skv), torch.int32)
+        masks = key_mask_args(memory_key_padding_mask, B, Skv)
         mode = "additive"
-    ctx = kernels.attention_prefill(q, k, v, causal=False, kv_valid_len=lens, mask_mode=mode,
-                                    out_dtype=compute_dtype())
+    ctx = kernels.attention_prefill(q, k, v, causal=False, mask_mode=mode,
+                                    out_dtype=compute_dtype(), **masks)
     return project(ctx.flatten(-2), layer, "o").float()

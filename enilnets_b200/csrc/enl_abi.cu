@@ -171,6 +171,21 @@ int prefill_impl(const enl_prefill_args* a, const enl_sparse_layout* layout, voi
   if ((st = check_strides_16B("o", a->o_stride_b, a->o_stride_s, a->o_stride_h,
                               a->out_dtype == ENL_DTYPE_FP32 ? 4 : 2)))
     return st;
+  if (a->kv_mask) {
+    if ((reinterpret_cast<uintptr_t>(a->kv_mask) & 7u) != 0)
+      return fail(ENL_ERR_INVALID, "enl_attn_prefill: kv_mask must be 8-byte aligned");
+    if (a->kv_mask_stride_b < (a->seq_kv + 63) / 64)
+      return fail(ENL_ERR_INVALID,
+                  "enl_attn_prefill: kv_mask_stride_b=%lld words is less than ceil(seq_kv/64)=%d",
+                  (long long)a->kv_mask_stride_b, (a->seq_kv + 63) / 64);
+    const size_t need = enl_prefill_workspace_bytes(a);
+    if (!a->workspace || a->workspace_bytes < need)
+      return fail(ENL_ERR_INVALID,
+                  "enl_attn_prefill: kv_mask needs a %zu-byte workspace (got %zu)", need,
+                  a->workspace_bytes);
+    if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0)
+      return fail(ENL_ERR_INVALID, "enl_attn_prefill: workspace must be 256-byte aligned");
+  }
   if ((long long)a->batch * a->num_heads > 65535)
     return fail(ENL_ERR_UNSUPPORTED, "enl_attn_prefill: batch*num_heads=%lld exceeds 65535",
                 (long long)a->batch * a->num_heads);
@@ -247,6 +262,17 @@ int prefill_impl(const enl_prefill_args* a, const enl_sparse_layout* layout, voi
   p.sp_kt = layout ? layout->tile_kt : nullptr;
   p.sp_mask = layout ? reinterpret_cast<const unsigned long long*>(layout->masks) : nullptr;
   p.sp_entries = layout ? layout->n_entries : 0;
+  p.kv_mask = reinterpret_cast<const unsigned long long*>(a->kv_mask);
+  p.kv_mask_sb = a->kv_mask_stride_b;
+  p.mask_tiles = nullptr;
+  if (a->kv_mask) {
+    // The tile ranges sit after the fp32 planes (if any) in the workspace.
+    enl_prefill_args planes_only = *a;
+    planes_only.kv_mask = nullptr;
+    int4* tiles = reinterpret_cast<int4*>(reinterpret_cast<uint8_t*>(a->workspace) +
+                                          enl_prefill_workspace_bytes(&planes_only));
+    p.mask_tiles = tiles;
+  }
   // One persistent CTA per SM. Sections of (batch, head) pairs whose K/V
   // fit in about a quarter of L2 keep the concurrently running items on
   // shared keys.
@@ -266,6 +292,11 @@ int prefill_impl(const enl_prefill_args* a, const enl_sparse_layout* layout, voi
     long long sec = (long long)(budget / kv_bytes_per_head);
     const long long n_bh = (long long)a->batch * a->num_heads;
     p.sec_bh = (int)std::max(1ll, std::min(n_bh, sec));
+  }
+
+  if (p.mask_tiles) {
+    cudaError_t e = launch_mask_tiles(p, const_cast<int4*>(p.mask_tiles), s);
+    if (e != cudaSuccess) return cuda_fail(e, "enl_attn_prefill: mask tiles launch");
   }
 
   // O map for the kernel's TMA-store epilogue (bf16 output of bf16 inputs).
@@ -304,10 +335,10 @@ int enl_attn_prefill_sparse(const enl_prefill_args* a, const enl_sparse_layout* 
                 "n_entries >= 0");
   if ((reinterpret_cast<uintptr_t>(l->masks) & 7u) != 0)
     return fail(ENL_ERR_INVALID, "enl_attn_prefill_sparse: masks must be 8-byte aligned");
-  if (a->window >= 0 || a->mask_mode != ENL_MASK_EXCLUDE || a->kv_valid_len)
+  if (a->window >= 0 || a->mask_mode != ENL_MASK_EXCLUDE || a->kv_valid_len || a->kv_mask)
     return fail(ENL_ERR_INVALID,
                 "enl_attn_prefill_sparse: the layout is the whole mask; window must be < 0, "
-                "mask_mode ENL_MASK_EXCLUDE and kv_valid_len NULL");
+                "mask_mode ENL_MASK_EXCLUDE and kv_valid_len and kv_mask NULL");
   return prefill_impl(a, l, stream);
 }
 
@@ -469,17 +500,26 @@ int enl_sparse_build_masks(const enl_sparse_mask_args* a, void* stream) {
 }
 
 size_t enl_prefill_workspace_bytes(const enl_prefill_args* a) {
-  if (!a || a->in_dtype != ENL_DTYPE_FP32) return 0;
-  auto planes = [&](int S, int H) {
-    return (((size_t)a->batch * S * H * 2 * a->head_dim * 2) + 255) & ~size_t(255);
-  };
-  return planes(a->seq_q, a->num_heads) + 2 * planes(a->seq_kv, a->num_kv_heads);
+  if (!a || a->batch < 1 || a->seq_q < 1 || a->seq_kv < 1) return 0;
+  size_t total = 0;
+  if (a->in_dtype == ENL_DTYPE_FP32) {
+    auto planes = [&](int S, int H) {
+      return (((size_t)a->batch * S * H * 2 * a->head_dim * 2) + 255) & ~size_t(255);
+    };
+    total += planes(a->seq_q, a->num_heads) + 2 * planes(a->seq_kv, a->num_kv_heads);
+  }
+  if (a->kv_mask) total += (size_t)a->batch * ((a->seq_q + 127) / 128) * 16;
+  return total;
 }
 
 int enl_decode_auto_splits(int32_t batch, int32_t num_kv_heads, int32_t n_slots) {
   if (batch < 1 || num_kv_heads < 1 || n_slots < 1) return 1;
   const long long units = (long long)batch * num_kv_heads;
-  const long long target_ctas = 148ll * 32;  // enough CTAs to balance 148 SMs
+  int sms = 0;
+  const std::string saved = t_last_error;  // a query that fails here is not the caller's error
+  if (sm_count(&sms) != ENL_OK || sms < 1) sms = 148;  // no device: size for a B200
+  t_last_error = saved;
+  const long long target_ctas = (long long)sms * 32;  // enough CTAs to balance the SMs
   long long splits = (target_ctas + units - 1) / units;
   const long long max_splits = (n_slots + 511) / 512;  // keep >= ~512 slots per split
   if (splits > max_splits) splits = max_splits;
@@ -494,6 +534,32 @@ size_t enl_decode_workspace_bytes(int32_t batch, int32_t num_heads, int32_t head
   const int dk = head_dim <= 64 ? 64 : 128;  // the kernel's (zero-extended) head dim
   return (size_t)n_splits * batch * num_heads * (dk + 1) * sizeof(float);
 }
+
+namespace enl {
+// The slot range a decode actually streams -- [slot_begin, slot_end)
+// narrowed by causality (keys after the query are invisible) and by the
+// sliding window -- and the split count and length it runs with.
+void decode_plan(const enl_decode_args* a, long long* lo_out, long long* hi_out, int* splits_out,
+                 int* split_len_out) {
+  long long lo = a->slot_begin, hi = a->slot_end;
+  const long long q_slot = a->q_pos - a->pos_slot0;  // slot holding the query position
+  if (hi > q_slot + 1) hi = q_slot + 1;
+  if (a->window >= 0 && lo < q_slot - a->window) lo = q_slot - a->window;
+  if (hi < lo) hi = lo;
+  const int n_slots = (int)(hi - lo);
+  int splits = a->n_splits > 0 ? a->n_splits : enl_decode_auto_splits(a->batch, a->num_kv_heads,
+                                                                      n_slots > 0 ? n_slots : 1);
+  if (n_slots <= 1) splits = 1;
+  int split_len = (n_slots + splits - 1) / splits;
+  if (split_len < 1) split_len = 1;
+  splits = (n_slots + split_len - 1) / split_len;
+  if (splits < 1) splits = 1;
+  *lo_out = lo;
+  *hi_out = hi;
+  *splits_out = splits;
+  *split_len_out = split_len;
+}
+}  // namespace enl
 
 int enl_attn_decode(const enl_decode_args* a, void* stream) {
   if (!a) return fail(ENL_ERR_INVALID, "enl_attn_decode: args is NULL");
@@ -529,22 +595,12 @@ int enl_attn_decode(const enl_decode_args* a, void* stream) {
                               esz)))
     return st;
 
-  // Narrow the slot range by causality (keys after the query are invisible)
-  // and by the sliding window, so the kernel only streams what it attends.
-  long long lo = a->slot_begin, hi = a->slot_end;
-  const long long q_slot = a->q_pos - a->pos_slot0;  // slot holding the query position
-  if (hi > q_slot + 1) hi = q_slot + 1;
-  if (a->window >= 0 && lo < q_slot - a->window) lo = q_slot - a->window;
-  if (hi < lo) hi = lo;
-  const int n_slots = (int)(hi - lo);
-
-  int splits = a->n_splits > 0 ? a->n_splits : enl_decode_auto_splits(a->batch, a->num_kv_heads,
-                                                                      n_slots > 0 ? n_slots : 1);
-  if (n_slots <= 1) splits = 1;
-  int split_len = (n_slots + splits - 1) / splits;
-  if (split_len < 1) split_len = 1;
-  splits = (n_slots + split_len - 1) / split_len;
-  if (splits < 1) splits = 1;
+  // Narrow the slot range by causality and the window, so the kernel only
+  // streams what it attends.
+  long long lo, hi;
+  int splits, split_len;
+  decode_plan(a, &lo, &hi, &splits, &split_len);
+  const long long q_slot = a->q_pos - a->pos_slot0;
   if (splits > 1) {
     const size_t need = enl_decode_workspace_bytes(a->batch, a->num_heads, Dk, splits);
     if (!a->workspace || a->workspace_bytes < need)

@@ -11,7 +11,9 @@
 // Limits and sharing rules:
 //   * The scratch holds at most ENL_DECODE_NOALLOC_SCRATCH_BYTES (4 MiB).
 //     A request whose split partials (n_splits * batch * heads * (head_dim+1)
-//     floats) would not fit is rejected with ENL_ERR_INVALID.
+//     floats, for the split count the decode really runs with after the slot
+//     range is narrowed by causality and the window) would not fit is
+//     rejected with ENL_ERR_INVALID.
 //   * Every GPU that loads the library keeps its own copy of the array until
 //     the process exits.
 //   * All calls on a device share that one array and it keeps whatever the
@@ -22,6 +24,11 @@
 //   * The first call on a device looks up the array's device address (one
 //     cudaGetSymbolAddress, with that device current). Make that first call
 //     before any stream capture.
+//   * The address belongs to the CUDA context current at that first call.
+//     A call from a different context looks it up again, but a
+//     cudaDeviceReset destroys the context and a new one may reuse its
+//     handle, so keep the first call's context alive for as long as this
+//     entry point is used (do not reset the device in between).
 #include <mutex>
 
 #include "enl_attn.h"
@@ -39,8 +46,28 @@ static __device__ __align__(256) float g_noalloc_scratch[kNoallocScratchBytes / 
 
 std::mutex g_noalloc_mutex;
 void* g_noalloc_ptr[kMaxDevices] = {};
+CUcontext g_noalloc_ctx[kMaxDevices] = {};  // context the address was looked up in
 
-// Device address of the scratch on the current device, looked up once.
+// The driver's cuCtxGetCurrent, through the runtime's entry-point query (the
+// library does not link libcuda).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  }
+  return fn;
+}
+
+// Device address of the scratch on the current device: looked up once per
+// device, again only when the calling context differs from the one it was
+// looked up in.
 int noalloc_scratch(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -49,12 +76,17 @@ int noalloc_scratch(void** out) {
     return fail(ENL_ERR_UNSUPPORTED, "enl_attn_decode_noalloc: device %d >= %d", dev,
                 kMaxDevices);
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (!g_noalloc_ptr[dev]) {
+  CUcontext ctx = nullptr;
+  CtxGetCurrentFn get_ctx = ctx_get_current_fn();
+  if (get_ctx && g_noalloc_ptr[dev]) get_ctx(&ctx);
+  if (!g_noalloc_ptr[dev] || (get_ctx && ctx != g_noalloc_ctx[dev])) {
     void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);  // also makes the context current
     if (e != cudaSuccess)
       return cuda_fail(e, "enl_attn_decode_noalloc: cudaGetSymbolAddress(scratch)");
+    if (get_ctx) get_ctx(&ctx);
     g_noalloc_ptr[dev] = p;
+    g_noalloc_ctx[dev] = ctx;
   }
   *out = g_noalloc_ptr[dev];
   return ENL_OK;
@@ -66,12 +98,18 @@ int noalloc_scratch(void** out) {
 extern "C" int enl_attn_decode_noalloc(const enl_decode_args* a, void* stream) {
   using namespace enl;
   if (!a) return fail(ENL_ERR_INVALID, "enl_attn_decode_noalloc: args is NULL");
-  // Upper bound on the split partials: the split count enl_attn_decode would
-  // use for the full live range (narrowing by causality or the window never
-  // raises it).
-  const int n_slots = a->slot_end > a->slot_begin ? a->slot_end - a->slot_begin : 1;
-  const int splits = a->n_splits > 0 ? a->n_splits
-                                     : enl_decode_auto_splits(a->batch, a->num_kv_heads, n_slots);
+  // Sizes first, so a bad size is reported as itself rather than as an
+  // oversized scratch request; enl_attn_decode checks everything else.
+  if (a->batch < 1 || a->num_heads < 1 || a->num_kv_heads < 1 || a->head_dim < 1)
+    return fail(ENL_ERR_INVALID,
+                "enl_attn_decode_noalloc: batch/num_heads/num_kv_heads/head_dim must be >= 1");
+  if (a->slot_begin < 0 || a->slot_end < a->slot_begin)
+    return fail(ENL_ERR_INVALID, "enl_attn_decode_noalloc: slot range [%d, %d) is invalid",
+                a->slot_begin, a->slot_end);
+  // The split partials of the split count the decode will run with.
+  long long lo, hi;
+  int splits, split_len;
+  decode_plan(a, &lo, &hi, &splits, &split_len);
   const size_t need = enl_decode_workspace_bytes(a->batch, a->num_heads, a->head_dim, splits);
   if (need > kNoallocScratchBytes)
     return fail(ENL_ERR_INVALID,

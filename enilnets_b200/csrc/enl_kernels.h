@@ -38,7 +38,21 @@ struct PrefillParams {
   const int* sp_kt;
   const unsigned long long* sp_mask;
   int sp_entries;
+  // Arbitrary key-padding mask (graph/sequence.py:162-168 takes any boolean
+  // (B, S) mask), when kv_mask is set: bit c of kv_mask[b * kv_mask_sb + w]
+  // set = key 64 w + c of batch row b is real. A key must also lie below
+  // kv_len[b] when both are given. mask_tiles[b * n_qt + qt] = {lo, hi, safe,
+  // 0}: the key tiles [lo, hi) query tile qt of batch row b visits and
+  // whether each of its rows has an unmasked key (launch_mask_tiles).
+  const unsigned long long* kv_mask;
+  long long kv_mask_sb;
+  const int4* mask_tiles;
 };
+
+// Fill p.mask_tiles (B * ceil(Sq / 128) entries) from p.kv_mask, p.kv_len and
+// the causal/window bounds; must run before the prefill launch on the same
+// stream.
+cudaError_t launch_mask_tiles(const PrefillParams& p, int4* tiles, cudaStream_t stream);
 
 // kSplit: the tensor maps cover (hi, lo) bf16 planes of fp32 inputs
 // interleaved per head (head coordinate 2h + plane), see launch_split_planes.

@@ -46,6 +46,8 @@
 // key-valid length / ALiBi, either with -inf exclusion (nn/ path) or with the
 // graph path's additive -1e9 rule, which is applied exactly by tracking the
 // number of -1e9 terms ("tier") per score when a row has no unmasked key.
+#include <climits>
+
 #include "enl_common.cuh"
 #include "enl_kernels.h"
 
@@ -146,8 +148,13 @@ struct WorkItem {
 };
 static_assert(sizeof(WorkItem) == 32, "softmax warps keep items in 32-byte slots");
 
-template <bool kSparse>
+// Template modes of K1: dense masks, block-sparse layouts, and dense masks
+// with an arbitrary per-key mask.
+constexpr int kModeDense = 0, kModeSparse = 1, kModeKeyMask = 2;
+
+template <int kMode>
 __device__ __forceinline__ WorkItem work_item(const PrefillParams& p, int t) {
+  constexpr bool kSparse = kMode == kModeSparse;
   const int n_qt = (p.Sq + 127) / 128;
   const int n_bh = p.B * p.H;
   const int per_sec = p.sec_bh * n_qt;
@@ -173,6 +180,12 @@ __device__ __forceinline__ WorkItem work_item(const PrefillParams& p, int t) {
       w.lo = w.hi = 0;
     }
     w.safe = 1;
+  } else if constexpr (kMode == kModeKeyMask) {
+    // Ranges computed per (batch row, query tile) by mask_tiles_kernel.
+    const int4 mt = p.mask_tiles[(long long)w.b * n_qt + qt];
+    w.lo = mt.x;
+    w.hi = mt.y;
+    w.safe = mt.z;
   } else {
     bool safe;
     tile_range(p, w.r0, w.lkey, (p.Skv + 127) / 128, w.lo, w.hi, safe);
@@ -190,14 +203,14 @@ __device__ __forceinline__ int key_tile(const PrefillParams& p, int j) {
 }
 
 // Walks this CTA's (item, key tile) sequence, skipping items without keys.
-template <bool kSparse>
+template <int kMode>
 struct TileCursor {
   int t;       // item id (>= n_items: done)
   int j, lo, hi;
   int wi;      // ordinal of the item among this CTA's items with work
   __device__ __forceinline__ void seek(const PrefillParams& p) {
     while (t < p.n_items) {
-      const WorkItem w = work_item<kSparse>(p, t);
+      const WorkItem w = work_item<kMode>(p, t);
       if (w.lo < w.hi) {
         j = lo = w.lo;
         hi = w.hi;
@@ -221,13 +234,15 @@ struct TileCursor {
   __device__ __forceinline__ bool valid(const PrefillParams& p) const { return t < p.n_items; }
 };
 
-template <int D, bool kSplit, bool kSparse>
+template <int D, bool kSplit, int kMode>
 __global__ void __launch_bounds__(384, 1)
     attn_prefill_sm100(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v,
                        const __grid_constant__ CUtensorMap tm_o, const PrefillParams p) {
   using Cfg = PrefillCfg<D, kSplit>;
+  constexpr bool kSparse = kMode == kModeSparse;
+  constexpr bool kKeyMask = kMode == kModeKeyMask;
   // bf16 output of the bf16 path leaves through TMA stores: the epilogue
   // stages O in the finished item's Q buffer and warp 11 stores it, then
   // releases the buffer. Otherwise the epilogue stores rows directly and the
@@ -287,7 +302,7 @@ __global__ void __launch_bounds__(384, 1)
       int q_issued = 0, issued = 0, issued_v = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < p.n_items && ok; t += gridDim.x) {
-        const WorkItem w = work_item<kSparse>(p, t);
+        const WorkItem w = work_item<kMode>(p, t);
         if (w.lo >= w.hi) continue;
         // Split mode: the plane tensors interleave (hi, lo) per head, so
         // plane pl of head h is "head" kPlanes * h + pl of the tensor map.
@@ -359,7 +374,7 @@ __global__ void __launch_bounds__(384, 1)
     auto wait = [&](uint64_t* bar, uint32_t parity, int site) {
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, site));
     };
-    TileCursor<kSparse> cur;
+    TileCursor<kMode> cur;
     cur.start(p);
     uint32_t g = 0;  // tiles of this CTA issued so far
     bool ok = true;
@@ -452,7 +467,7 @@ __global__ void __launch_bounds__(384, 1)
       int wi = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < p.n_items && ok; t += gridDim.x) {
-        const WorkItem w = work_item<kSparse>(p, t);
+        const WorkItem w = work_item<kMode>(p, t);
         if (w.lo >= w.hi) continue;
         const int qb = wi % Cfg::kQBufs;
         ok = mbar_wait(bar_stage_full, wi & 1, abort_flag, 40);
@@ -484,7 +499,7 @@ __global__ void __launch_bounds__(384, 1)
     // own shared-memory slot: nothing of it stays live in registers across
     // the tile loop, which runs at the register limit.
     WorkItem* slots = reinterpret_cast<WorkItem*>(smem + Cfg::kOffItems) + 2 * warp;
-    if (lane == 0) slots[0] = work_item<kSparse>(p, blockIdx.x);
+    if (lane == 0) slots[0] = work_item<kMode>(p, blockIdx.x);
     int k = 0;  // this CTA's item ordinal
     for (int t = blockIdx.x; t < p.n_items; t += gridDim.x, ++k) {
       __syncwarp();
@@ -525,6 +540,13 @@ __global__ void __launch_bounds__(384, 1)
           kt = p.sp_kt[j];
           allow = p.sp_mask[((long long)j * 2 + half) * 128 + rloc];
         }
+        // Key-mask mode: which of this half's 64 keys are real (the same word
+        // for every row of the batch row; columns past Skv read as padding).
+        unsigned long long real = ~0ull;
+        if constexpr (kKeyMask) {
+          const int widx = kt * 2 + half;
+          real = (widx * 64 < p.Skv) ? p.kv_mask[(long long)w.b * p.kv_mask_sb + widx] : 0ull;
+        }
         failed = !__all_sync(0xffffffffu,
                              mbar_wait(bar_s_full + buf, (g >> 1) & 1, abort_flag, 30 + half));
         if (failed) break;
@@ -561,7 +583,8 @@ __global__ void __launch_bounds__(384, 1)
         if constexpr (kSparse)  // rows past Sq are never stored: they do not force masking
           full_tile = __all_sync(0xffffffffu, allow == ~0ull || row >= p.Sq) && slope2 == 0.0f;
         else
-          full_tile = (j0 >= in_lo) && (j0 + 63 <= in_hi) && !tiers && slope2 == 0.0f;
+          full_tile = (j0 >= in_lo) && (j0 + 63 <= in_hi) && !tiers && slope2 == 0.0f &&
+                      (!kKeyMask || real == ~0ull);
         bool reset = false;
         float m_tile = -INFINITY;
         if (full_tile) {
@@ -598,7 +621,8 @@ __global__ void __launch_bounds__(384, 1)
               float dist = dbase - (float)c;
               if (alibi_abs) dist = fabsf(dist);
               const float v = fmaf(s[c], sl2, -slope2 * dist);
-              s[c] = (c >= c_lo && c <= c_hi) ? v : -INFINITY;
+              const bool key_ok = !kKeyMask || ((real >> c) & 1ull);
+              s[c] = (c >= c_lo && c <= c_hi && key_ok) ? v : -INFINITY;
               m_tile = fmaxf(m_tile, s[c]);
             }
           } else {
@@ -610,7 +634,24 @@ __global__ void __launch_bounds__(384, 1)
             const int c_wlo = rel(jlo_c), c_whi = rel(jhi_c), c_pad = rel(lkey);
             const int cend = min(64, rel(p.Skv));  // columns [0, cend) exist
             int tmin;
-            if (max(0, c_wlo) <= min(min(c_whi, c_pad - 1), cend - 1)) {
+            unsigned long long realb = 0ull;  // key-mask mode: real columns
+            if constexpr (kKeyMask) {
+              // Same tiers from bit sets: real = mask word, below the valid
+              // length and inside the sequence; win = columns [c_wlo, c_whi].
+              auto below = [](int n) {  // bits [0, n)
+                return n >= 64 ? ~0ull : (n <= 0 ? 0ull : ((1ull << n) - 1ull));
+              };
+              const unsigned long long exist = below(cend);
+              realb = real & below(c_pad) & exist;
+              const int wa = max(0, c_wlo), wb = min(63, c_whi);
+              const unsigned long long win = wa > wb ? 0ull : (below(wb + 1) & ~below(wa));
+              if (realb & win)
+                tmin = 0;
+              else if ((realb & ~win) | (~realb & win & exist))
+                tmin = 1;
+              else
+                tmin = exist ? 2 : 3;
+            } else if (max(0, c_wlo) <= min(min(c_whi, c_pad - 1), cend - 1)) {
               tmin = 0;
             } else {
               const int real_hi = min(c_pad, cend) - 1;  // real columns [0, real_hi]
@@ -623,7 +664,8 @@ __global__ void __launch_bounds__(384, 1)
             tier = new_tier;
 #pragma unroll
             for (int c = 0; c < 64; ++c) {
-              const int tt = (int)(c >= c_pad) + (int)(c < c_wlo || c > c_whi);
+              const bool padded = kKeyMask ? !((realb >> c) & 1ull) : (c >= c_pad);
+              const int tt = (int)padded + (int)(c < c_wlo || c > c_whi);
               float dist = dbase - (float)c;
               if (alibi_abs) dist = fabsf(dist);
               const float v = fmaf(s[c], sl2, -slope2 * dist);
@@ -717,7 +759,7 @@ __global__ void __launch_bounds__(384, 1)
 
       // ----------------------------------------------------------- epilogue
       if (lane == 0 && t + (int)gridDim.x < p.n_items)
-        slots[(k + 1) & 1] = work_item<kSparse>(p, t + gridDim.x);
+        slots[(k + 1) & 1] = work_item<kMode>(p, t + gridDim.x);
       const WorkItem we = slots[k & 1];
       const int erow = we.r0 + rloc;
       // Merge the two halves by log-sum-exp: only the half(s) with the
@@ -850,20 +892,103 @@ cudaError_t launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const C
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
     const cudaFuncAttribute a = cudaFuncAttributeMaxDynamicSharedMemorySize;
-    e = cudaFuncSetAttribute(attn_prefill_sm100<D, kSplit, false>, a, Cfg::kSmemBytes);
+    e = cudaFuncSetAttribute(attn_prefill_sm100<D, kSplit, kModeDense>, a, Cfg::kSmemBytes);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(attn_prefill_sm100<D, kSplit, true>, a, Cfg::kSmemBytes);
+      e = cudaFuncSetAttribute(attn_prefill_sm100<D, kSplit, kModeSparse>, a, Cfg::kSmemBytes);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attn_prefill_sm100<D, kSplit, kModeKeyMask>, a, Cfg::kSmemBytes);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
   if (p.n_items <= 0) return cudaSuccess;
   const int grid = min(p.n_items, p.n_ctas);
   if (p.sp_ptr != nullptr)
-    attn_prefill_sm100<D, kSplit, true>
+    attn_prefill_sm100<D, kSplit, kModeSparse>
+        <<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(tq, tk, tv, to, p);
+  else if (p.kv_mask != nullptr)
+    attn_prefill_sm100<D, kSplit, kModeKeyMask>
         <<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(tq, tk, tv, to, p);
   else
-    attn_prefill_sm100<D, kSplit, false>
+    attn_prefill_sm100<D, kSplit, kModeDense>
         <<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(tq, tk, tv, to, p);
+  return cudaGetLastError();
+}
+
+// Per (batch row, query tile) key-tile range under an arbitrary key mask.
+// One thread per query row finds the first and last real key inside its
+// causal/window interval; the block reduces them to the tile's range
+// [lo, hi) and to `safe` (every row of the tile has an unmasked key). A tile
+// with a fully masked row under the additive rule visits every key tile: its
+// surviving scores (those with the fewest -1e9 terms) may lie anywhere.
+__global__ void __launch_bounds__(128) mask_tiles_kernel(const PrefillParams p, int4* tiles) {
+  const int qt = blockIdx.x, b = blockIdx.y;
+  const int row = qt * 128 + threadIdx.x;
+  const int lkey = p.kv_len != nullptr ? max(0, min(p.kv_len[b], p.Skv)) : p.Skv;
+  int first = INT_MAX, last = -1;
+  bool has = true;  // rows past Sq are never stored and do not count
+  if (row < p.Sq) {
+    const RowBounds rb = row_bounds(p, row);
+    const long long klo = max(rb.jlo, 0ll), khi = min(rb.jhi, (long long)lkey - 1);
+    has = false;
+    if (klo <= khi) {
+      const unsigned long long* m = p.kv_mask + (long long)b * p.kv_mask_sb;
+      const int w0 = (int)(klo / 64), w1 = (int)(khi / 64);
+      const unsigned long long lo_bits = ~0ull << (int)(klo % 64);
+      const unsigned long long hi_bits = (khi % 64 == 63) ? ~0ull : ((1ull << (khi % 64 + 1)) - 1);
+      for (int wd = w0; wd <= w1; ++wd) {
+        unsigned long long x = m[wd];
+        if (wd == w0) x &= lo_bits;
+        if (wd == w1) x &= hi_bits;
+        if (x) {
+          first = wd * 64 + __ffsll((long long)x) - 1;
+          break;
+        }
+      }
+      if (first != INT_MAX) {
+        has = true;
+        for (int wd = w1; wd >= w0; --wd) {
+          unsigned long long x = m[wd];
+          if (wd == w0) x &= lo_bits;
+          if (wd == w1) x &= hi_bits;
+          if (x) {
+            last = wd * 64 + 63 - __clzll((long long)x);
+            break;
+          }
+        }
+      }
+    }
+  }
+  __shared__ int s_first[4], s_last[4];
+  const int safe = __syncthreads_and(has);
+  first = __reduce_min_sync(0xffffffffu, first);
+  last = __reduce_max_sync(0xffffffffu, last);
+  if (threadIdx.x % 32 == 0) {
+    s_first[threadIdx.x / 32] = first;
+    s_last[threadIdx.x / 32] = last;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    first = min(min(s_first[0], s_first[1]), min(s_first[2], s_first[3]));
+    last = max(max(s_last[0], s_last[1]), max(s_last[2], s_last[3]));
+    int4 t;
+    if (!safe && p.additive) {
+      t.x = 0;
+      t.y = (p.Skv + 127) / 128;
+    } else if (last >= 0) {
+      t.x = first / 128;
+      t.y = last / 128 + 1;
+    } else {
+      t.x = t.y = 0;
+    }
+    t.z = safe;
+    t.w = 0;
+    tiles[(long long)b * gridDim.x + qt] = t;
+  }
+}
+
+cudaError_t launch_mask_tiles(const PrefillParams& p, int4* tiles, cudaStream_t stream) {
+  const int n_qt = (p.Sq + 127) / 128;
+  mask_tiles_kernel<<<dim3(n_qt, p.B), 128, 0, stream>>>(p, tiles);
   return cudaGetLastError();
 }
 

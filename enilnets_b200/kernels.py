@@ -47,7 +47,8 @@ def attention_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
                       q_pos0: int = 0, k_pos0: int = 0, mask_mode: str = "exclude",
                       scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
                       out_dtype: torch.dtype = torch.bfloat16,
-                      return_lse: bool = False, sparse=None):
+                      return_lse: bool = False, sparse=None,
+                      kv_mask: Optional[torch.Tensor] = None):
     """softmax(q k^T * scale + alibi + mask) v via the K1 tcgen05 kernel.
 
     q: (B, Sq, H, D); k, v: (B, Skv, Hkv, D); all bf16, or all fp32 (the
@@ -55,6 +56,9 @@ def attention_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     error). H % Hkv == 0 and query head h reads kv head h // (H // Hkv)
     (nn/forward.py:165-171).
     kv_valid_len: int32 (B,) -- keys [0, len_b) are real (graph/sequence.py:23-29).
+    kv_mask: int64 (B, W), W >= ceil(Skv / 64) -- any key-padding mask as
+    packed bits (pack_key_mask): bit c of word w set = key 64 w + c is real
+    (graph/sequence.py:162-168 accepts any boolean mask, not only prefixes).
     mask_mode: "exclude" (-inf, the nn/ path) or "additive" (-1e9 per violated
     mask term, graph/sequence.py:162-176).
     sparse: a block-sparse layout (enilnets_b200.sparse.SparseLayout) built for
@@ -89,6 +93,13 @@ def attention_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
         _require_cuda("alibi_slopes", alibi_slopes, torch.float32, last_contiguous=False)
         if tuple(alibi_slopes.shape) != (H,) or not alibi_slopes.is_contiguous():
             raise ValueError(f"alibi_slopes must be a contiguous float32 ({H},) tensor")
+    if kv_mask is not None:
+        _require_cuda("kv_mask", kv_mask, torch.int64)
+        if kv_mask.dim() != 2 or kv_mask.shape[0] != B or kv_mask.shape[1] * 64 < Skv:
+            raise ValueError(f"kv_mask must be int64 ({B}, >= {(Skv + 63) // 64}) packed words, "
+                             f"got {tuple(kv_mask.shape)}")
+        if sparse is not None:
+            raise ValueError("kv_mask cannot be combined with a sparse layout")
     a = nat.PrefillArgs()
     a.q, a.k, a.v, a.o, a.lse = q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), _ptr(lse)
     a.batch, a.num_heads, a.num_kv_heads = B, H, Hkv
@@ -106,6 +117,8 @@ def attention_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     a.alibi_slopes = _ptr(alibi_slopes)
     a.q_pos0, a.k_pos0 = int(q_pos0), int(k_pos0)
     a.scale = 1.0 / math.sqrt(D) if scale is None else float(scale)
+    if kv_mask is not None:
+        a.kv_mask, a.kv_mask_stride_b = kv_mask.data_ptr(), kv_mask.stride(0)
     lib = nat.load()
     ws = None
     need = int(lib.enl_prefill_workspace_bytes(ctypes.byref(a)))
@@ -224,6 +237,27 @@ def sparse_build_masks(tile_ptr: torch.Tensor, tile_kt: torch.Tensor, masks: tor
     a.q_pos0, a.k_pos0, a.causal = int(q_pos0), int(k_pos0), int(bool(causal))
     nat.check(nat.load().enl_sparse_build_masks(ctypes.byref(a), _stream()),
               "enl_sparse_build_masks")
+
+
+def key_mask_words(mask):
+    """Boolean (B, S) key-padding mask (True = real token) -> host int64
+    (B, ceil(S / 64)) words, bit c of word w = key 64 w + c, as the
+    prefill's kv_mask takes it."""
+    import numpy as np
+    m = np.ascontiguousarray(np.asarray(mask, dtype=bool))
+    if m.ndim != 2:
+        raise ValueError(f"key mask must be (batch, seq), got shape {m.shape}")
+    B, S = m.shape
+    W = max(1, (S + 63) // 64)
+    padded = np.zeros((B, W * 64), dtype=bool)
+    padded[:, :S] = m
+    words = np.packbits(padded.reshape(B, W, 8, 8), axis=-1, bitorder="little")
+    return words.reshape(B, W * 8).view("<i8").copy()
+
+
+def pack_key_mask(mask, device) -> torch.Tensor:
+    """key_mask_words(mask) as a device tensor."""
+    return torch.from_numpy(key_mask_words(mask)).to(device)
 
 
 _workspaces: dict = {}

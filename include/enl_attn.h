@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define ENL_ABI_VERSION 5
+#define ENL_ABI_VERSION 6
 
 /* Status codes. The Python binding maps INVALID/UNSUPPORTED to ValueError
  * (the reference raises ValueError for bad layer configurations,
@@ -66,8 +66,16 @@ typedef struct enl_prefill_args {
   int64_t q_pos0;              /* absolute position of query row 0 */
   int64_t k_pos0;              /* absolute position of key row 0 */
   float scale;                 /* softmax scale, normally 1/sqrt(head_dim) */
-  void* workspace;             /* device scratch for fp32 inputs, >= enl_prefill_workspace_bytes() */
-  size_t workspace_bytes;
+  void* workspace;             /* device scratch for fp32 inputs and kv_mask, */
+  size_t workspace_bytes;      /* >= enl_prefill_workspace_bytes(), 256-byte aligned */
+  /* Arbitrary key-padding mask, for masks that are not a prefix of real keys
+   * (left padding, holes): graph/sequence.py:162-168 adds -1e9 for any
+   * boolean (batch, seq) mask. Bit c of kv_mask[b * kv_mask_stride_b + w]
+   * set = key 64 w + c of batch row b is real. Device memory, NULL = none;
+   * with kv_valid_len also set a key must pass both. Bits past seq_kv are
+   * ignored. Needs the workspace (per-query-tile key ranges). */
+  const uint64_t* kv_mask;
+  int64_t kv_mask_stride_b; /* 64-bit words per batch row, >= ceil(seq_kv / 64) */
 } enl_prefill_args;
 
 /* Fused attention prefill: softmax(Q K^T * scale + bias + mask) V.
@@ -85,7 +93,9 @@ typedef struct enl_prefill_args {
  * error, tighter than tf32. fp32 rows must be 16-byte aligned. */
 int enl_attn_prefill(const enl_prefill_args* args, void* stream);
 
-/* Workspace bytes enl_attn_prefill needs for these arguments (0 for bf16 inputs). */
+/* Workspace bytes enl_attn_prefill needs for these arguments: the bf16
+ * planes of fp32 inputs, plus 16 bytes per (batch row, 128-row query tile)
+ * with kv_mask; 0 for bf16 inputs without kv_mask. */
 size_t enl_prefill_workspace_bytes(const enl_prefill_args* args);
 
 /* ----------------------------------------------------------------- decode */
@@ -127,10 +137,14 @@ int enl_attn_decode(const enl_decode_args* args, void* stream);
  * allowed. Same arguments and results as enl_attn_decode; args->workspace is
  * ignored and the split partials go to a fixed scratch array inside the
  * library (ENL_DECODE_NOALLOC_SCRATCH_BYTES per device, kept until exit).
- * Requests whose partials would not fit are rejected with ENL_ERR_INVALID.
- * The first call on a device looks up the scratch address, so make it before
- * any stream capture. All calls on a device share the scratch: calls whose
- * kernels overlap on the GPU race and must be ordered on one stream.
+ * Requests whose partials would not fit (for the split count actually run,
+ * after the slot range is narrowed by causality and the window) are
+ * rejected with ENL_ERR_INVALID. The first call on a device looks up the
+ * scratch address, so make it before any stream capture; the address
+ * belongs to that call's CUDA context, so keep that context alive (no
+ * cudaDeviceReset) while the entry point is in use. All calls on a device
+ * share the scratch: calls whose kernels overlap on the GPU race and must
+ * be ordered on one stream.
  * No counterpart in the reference, which never splits the key sequence. */
 int enl_attn_decode_noalloc(const enl_decode_args* args, void* stream);
 

@@ -98,7 +98,7 @@ def _blocked(q_pos, k_pos, causal, window):
 
 def attention_ref(q, k, v, *, causal=False, window=None, kv_valid_len=None,
                   alibi=None, q_pos0=0, k_pos0=0, mask_mode="exclude",
-                  scale=None) -> Tuple[np.ndarray, np.ndarray]:
+                  scale=None, key_mask=None) -> Tuple[np.ndarray, np.ndarray]:
     """Softmax attention in float64.
 
     q (B, Sq, H, D), k/v (B, Skv, Hkv, D); query head h reads kv head
@@ -106,6 +106,9 @@ def attention_ref(q, k, v, *, causal=False, window=None, kv_valid_len=None,
     mask_mode "exclude": masked scores are -inf (nn/forward.py:539-543).
     mask_mode "additive": padded keys add -1e9, and causal/window violations
     add another -1e9 (graph/sequence.py:162-176).
+    key_mask: (B, Skv) bool, True = real key; any pattern (left padding,
+    holes), the key_padding_mask of graph/sequence.py:162-168. A key is
+    padding when it is masked here or at/after kv_valid_len.
     alibi: (H,) slopes; bias -slope * (i - j) if causal else -slope * |i - j|
     (nn/forward.py:526-535, nn/kvcache.py:199-203).
     Returns (o (B, Sq, H, D), lse (B, H, Sq)).
@@ -128,6 +131,8 @@ def attention_ref(q, k, v, *, causal=False, window=None, kv_valid_len=None,
         for b in range(B):
             L = Skv if kv_valid_len is None else int(np.clip(kv_valid_len[b], 0, Skv))
             pad = np.arange(Skv) >= L
+            if key_mask is not None:
+                pad = pad | ~np.asarray(key_mask[b], dtype=bool)
             for h in range(H):
                 s = (q[b, :, h] @ k[b, :, h // rep].T) * scale
                 if alibi is not None:
@@ -300,24 +305,21 @@ def mha_layer_ref(layer: dict, x: np.ndarray, key_padding_mask: Optional[np.ndar
         Q = rope_rotate(Q.transpose(0, 2, 1, 3), cos, sin).transpose(0, 2, 1, 3)
         K = rope_rotate(K.transpose(0, 2, 1, 3), cos, sin).transpose(0, 2, 1, 3)
     slopes = alibi_slopes(H) if scheme == "alibi" else None
-    lengths = None
-    if key_padding_mask is not None:
-        mask = np.asarray(key_padding_mask, bool)
-        lengths = mask.sum(axis=1)
-        if not np.array_equal(mask, np.arange(S)[None, :] < lengths[:, None]):
-            raise ValueError("attention_ref models prefix (length) padding masks only")
+    mask = None if key_padding_mask is None else np.asarray(key_padding_mask, bool)
     mode = mask_mode or ("additive" if key_padding_mask is not None else "exclude")
     o, _ = attention_ref(Q, K, V, causal=layer.get("causal", False),
-                         window=layer.get("window_size"), kv_valid_len=lengths, alibi=slopes,
+                         window=layer.get("window_size"), key_mask=mask, alibi=slopes,
                          mask_mode=mode)
     return project(o.reshape(B, S, H * Dh), layer["Wo"], layer["bo"])
 
 
 def cross_layer_ref(layer: dict, x: np.ndarray, memory: np.ndarray,
-                    memory_valid_len: Optional[np.ndarray] = None) -> np.ndarray:
+                    memory_valid_len: Optional[np.ndarray] = None,
+                    memory_key_mask: Optional[np.ndarray] = None) -> np.ndarray:
     """Cross attention (nn/forward.py:557-591): Q from x, K/V from memory,
-    non-causal; memory_valid_len applies the graph path's -1e9 key-padding
-    rule to the memory keys."""
+    non-causal; memory_valid_len (prefix lengths) or memory_key_mask (any
+    boolean (B, Skv) mask, True = real) applies the graph path's -1e9
+    key-padding rule (graph/sequence.py:162-168) to the memory keys."""
     x = np.asarray(x, np.float64)
     mem = np.asarray(memory, np.float64)
     B, Sq, E = x.shape
@@ -327,6 +329,7 @@ def cross_layer_ref(layer: dict, x: np.ndarray, memory: np.ndarray,
     Q = project(x, layer["Wq"], layer["bq"]).reshape(B, Sq, H, Dh)
     K = project(mem, layer["Wk"], layer["bk"]).reshape(B, Skv, Hkv, Dh)
     V = project(mem, layer["Wv"], layer["bv"]).reshape(B, Skv, Hkv, Dh)
-    o, _ = attention_ref(Q, K, V, kv_valid_len=memory_valid_len,
-                         mask_mode="additive" if memory_valid_len is not None else "exclude")
+    masked = memory_valid_len is not None or memory_key_mask is not None
+    o, _ = attention_ref(Q, K, V, kv_valid_len=memory_valid_len, key_mask=memory_key_mask,
+                         mask_mode="additive" if masked else "exclude")
     return project(o.reshape(B, Sq, H * Dh), layer["Wo"], layer["bo"])

@@ -1,12 +1,12 @@
 """Generate the golden vectors that pin the oracle (and the kernels) to the
 reference, by running the reference itself.
 
-Run in a container that has the reference checked out:
+Run in a container that has the reference checked out, naming its source
+tree (the directory that holds the Enilnets package):
 
-    PYTHONPATH=/path/to/reference python tests/golden/make_golden.py
+    ENILNETS_REFERENCE=/path/to/reference python tests/golden/make_golden.py [case ...]
 
-(the default path is the reference mount of the build container). Writes
-tests/golden/*.npz. The reference must never be imported at test time; the
+Writes tests/golden/*.npz. The reference must never be imported at test time; the
 committed .npz files are all the tests use.
 
 Every case runs the reference in float64 (``use_float64(True)``). To expose
@@ -29,7 +29,10 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
 sys.path.insert(0, str(REPO))
-REF = os.environ.get("ENILNETS_REFERENCE", "/root/reference")
+REF = os.environ.get("ENILNETS_REFERENCE")
+if not REF:
+    raise SystemExit("set ENILNETS_REFERENCE to the reference source tree (the directory that "
+                     "holds the Enilnets package)")
 sys.path.insert(0, REF)
 
 from oracle.attention_ref import seeded_normal  # noqa: E402
@@ -128,6 +131,74 @@ def graph_padding_cases():
                 i += 1
     out["meta"] = np.array(json.dumps(meta))
     np.savez_compressed(HERE / "graph_padding.npz", **out)
+
+
+def _mask_patterns(B, S, rng):
+    """Key-padding masks that are not prefixes: left padding, random holes,
+    a fully masked row, and a row whose only real keys sit at the end."""
+    pats = []
+    left = np.ones((B, S), dtype=bool)
+    for b in range(B):
+        left[b, : (b * S) // (2 * B) + b] = False  # left padding of growing width
+    pats.append(("left", left))
+    holes = rng.rand(B, S) < 0.7
+    holes[:, 0] = rng.rand(B) < 0.5
+    pats.append(("holes", holes))
+    mixed = rng.rand(B, S) < 0.5
+    mixed[0] = False                      # every key of row 0 is padding
+    mixed[-1] = False
+    mixed[-1, S - max(1, S // 10):] = True  # row B-1: only its last keys are real
+    pats.append(("mixed", mixed))
+    return pats
+
+
+def graph_mask_cases():
+    """graph.MultiHeadAttention with key_padding_mask patterns that are not
+    prefixes (graph/sequence.py:162-168 adds -1e9 for any boolean mask).
+
+    layer{i}: MultiHeadAttention(64, 4) layers with the reference's own
+    seeded weights (set_seed 3600 + i; any builder that draws in the
+    reference's order rebuilds them), x = RandomState(3700 + i) (3, 33, 64);
+    mask and output (float32) stored. kernel{i}: identity projections at
+    kernel head dims, x = seeded_normal(seed, (B, S, E)) (not stored), mask
+    and output (float16) stored."""
+    out = {}
+    meta = {"layer": [], "kernel": []}
+    rng = np.random.RandomState(3500)
+    i = 0
+    for causal, window in ((False, None), (True, None), (True, 3), (False, 2)):
+        for name, mask in _mask_patterns(3, 33, rng):
+            Enilnets.core.utils.set_seed(3600 + i)
+            g = MultiHeadAttention(64, 4, causal=causal, window_size=window)
+            x = np.random.RandomState(3700 + i).standard_normal((3, 33, 64))
+            y = g(Tensor(x), key_padding_mask=mask).data
+            out[f"layer_y{i}"] = y.astype(np.float32)
+            out[f"layer_mask{i}"] = mask
+            meta["layer"].append({"causal": causal, "window_size": window, "embed_dim": 64,
+                                  "num_heads": 4, "pattern": name})
+            i += 1
+    cases = [dict(B=2, S=160, H=1, D=64, causal=True, window=None),
+             dict(B=2, S=160, H=1, D=64, causal=False, window=None),
+             dict(B=2, S=130, H=1, D=128, causal=True, window=None),
+             dict(B=2, S=160, H=1, D=64, causal=True, window=40),
+             dict(B=2, S=130, H=1, D=128, causal=False, window=25)]
+    j = 0
+    for c in cases:
+        for name, mask in _mask_patterns(c["B"], c["S"], rng):
+            seed = 3800 + j
+            E = c["H"] * c["D"]
+            x = seeded_normal(seed, (c["B"], c["S"], E))
+            g = MultiHeadAttention(E, c["H"], causal=c["causal"], window_size=c["window"])
+            for wname in ("Wq", "Wk", "Wv", "Wo"):
+                getattr(g, wname).data = np.eye(E)
+                getattr(g, "b" + wname[1:].lower()).data = np.zeros(E)
+            y = g(Tensor(x), key_padding_mask=mask).data
+            out[f"kernel_y{j}"] = y.astype(np.float16)  # kernel bar 2e-2; keeps the file small
+            out[f"kernel_mask{j}"] = mask
+            meta["kernel"].append(dict(c, seed=seed, pattern=name))
+            j += 1
+    out["meta"] = np.array(json.dumps(meta))
+    np.savez_compressed(HERE / "graph_mask.npz", **out)
 
 
 def cross_cases():
@@ -704,6 +775,7 @@ def main():
     flash_cases()
     mha_layer_cases()
     graph_padding_cases()
+    graph_mask_cases()
     cross_cases()
     kernel_prefill_cases()
     kernel_decode_cases()

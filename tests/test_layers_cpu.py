@@ -90,11 +90,29 @@ def test_lengths_to_mask_and_prefix_lengths():
     mask = lengths_to_mask([3, 1, 0], 4)
     assert mask.tolist() == [[True, True, True, False], [True, False, False, False],
                              [False] * 4]
-    assert attention.lengths_from_mask(mask, 3, 4).tolist() == [3, 1, 0]
-    with pytest.raises(ValueError, match="prefix"):
-        attention.lengths_from_mask(np.array([[True, False, True]]), 1, 3)
+    kind, lens = attention.classify_key_mask(mask, 3, 4)
+    assert kind == "lengths" and lens.tolist() == [3, 1, 0]
     with pytest.raises(ValueError, match="shape"):
-        attention.lengths_from_mask(mask, 3, 5)
+        attention.classify_key_mask(mask, 3, 5)
+
+
+def test_non_prefix_masks_become_packed_key_words():
+    """Left padding and holes (any boolean mask, graph/sequence.py:162-168)
+    go to the kernel as bits: bit c of word w = key 64 w + c."""
+    rng = np.random.RandomState(0)
+    for S in (3, 64, 65, 200):
+        m = rng.rand(3, S) < 0.6
+        m[0, : S // 2] = False  # left padding
+        m[0, S // 2:] = True
+        kind, words = attention.classify_key_mask(m, 3, S)
+        assert kind == "words" and words.dtype == np.int64
+        assert words.shape == (3, (S + 63) // 64)
+        u = words.view(np.uint64)
+        bits = np.array([[(int(u[b, j // 64]) >> (j % 64)) & 1 for j in range(S)]
+                         for b in range(3)], dtype=bool)
+        np.testing.assert_array_equal(bits, m)
+        pad = [(int(u[b, -1]) >> c) & 1 for b in range(3) for c in range(S % 64 or 64, 64)]
+        assert not any(pad), "bits past the sequence end must be clear"
 
 
 def _rebuild_mha(i, cfg):

@@ -80,6 +80,49 @@ def test_graph_padding_oracle_matches_reference(golden_dir):
         np.testing.assert_allclose(y, data[f"y{i}"], atol=1e-6, err_msg=str(cfg))
 
 
+def graph_mask_layer(i, cfg):
+    """Weights of graph_mask.npz layer case i, drawn in the reference's order
+    from its seed by enilnets_b200's graph builder (host-side NumPy)."""
+    import enilnets_b200 as enl
+    from enilnets_b200.graph import MultiHeadAttention
+    enl.set_seed(3600 + i)
+    g = MultiHeadAttention(cfg["embed_dim"], cfg["num_heads"], causal=cfg["causal"],
+                           window_size=cfg["window_size"])
+    layer = g._layer()
+    layer["window_size"] = cfg["window_size"]
+    return layer
+
+
+def test_graph_arbitrary_mask_oracle_matches_reference(golden_dir):
+    """Left padding, holes and fully masked rows (graph/sequence.py:162-168
+    accepts any boolean key_padding_mask), with and without causal/window."""
+    data, meta = _load(golden_dir, "graph_mask.npz")
+    for i, cfg in enumerate(meta["layer"]):
+        layer = graph_mask_layer(i, cfg)
+        mask = data[f"layer_mask{i}"]
+        assert not np.array_equal(mask, np.arange(mask.shape[1])[None, :] <
+                                  mask.sum(axis=1)[:, None]), "golden masks are not prefixes"
+        x = np.random.RandomState(3700 + i).standard_normal((3, 33, 64))
+        y = ref.mha_layer_ref(layer, x, key_padding_mask=mask)
+        np.testing.assert_allclose(y, data[f"layer_y{i}"], atol=1e-6, err_msg=str(cfg))
+    for j, c in enumerate(meta["kernel"]):
+        y = graph_mask_kernel_oracle(c, data[f"kernel_mask{j}"])
+        # stored as float16 (about 5e-4 relative)
+        np.testing.assert_allclose(y, data[f"kernel_y{j}"].astype(np.float64), atol=2e-3,
+                                   rtol=2e-3, err_msg=str(c))
+
+
+def graph_mask_kernel_oracle(c, mask):
+    """Oracle output of a graph_mask.npz kernel case (identity projections:
+    q = k = v = x split into heads)."""
+    E = c["H"] * c["D"]
+    x = ref.seeded_normal(c["seed"], (c["B"], c["S"], E))
+    qkv = x.reshape(c["B"], c["S"], c["H"], c["D"])
+    o, _ = ref.attention_ref(qkv, qkv, qkv, causal=c["causal"], window=c["window"],
+                             key_mask=mask, mask_mode="additive")
+    return o.reshape(c["B"], c["S"], E)
+
+
 def test_cross_attention_oracle_matches_reference(golden_dir):
     data, meta = _load(golden_dir, "cross_layer.npz")
     for i, cfg in enumerate(meta):
