@@ -65,9 +65,12 @@ def load_peaks():
     return dict(FALLBACK_PEAKS), "fallback"
 
 
-def cfg2_lengths(rank: int):
+def cfg2_lengths(rank: int, n: int = 0):
+    """Valid lengths ~U[2048, 4096] of config 2 from seed 2 + rank (n values,
+    default one per-GPU batch)."""
     import numpy as np
-    return np.random.RandomState(2 + rank).randint(CFG2["lo"], CFG2["hi"] + 1, size=CFG2["B"])
+    return np.random.RandomState(2 + rank).randint(CFG2["lo"], CFG2["hi"] + 1,
+                                                   size=n or CFG2["B"])
 
 
 def cfg2_flops(lengths) -> float:
@@ -216,45 +219,86 @@ def timed(dist: Dist, clocks: ClockSampler, fn, steps: int) -> float:
 
 
 # ------------------------------------------------------------- workloads
+def prefill_partition(world: int, rank: int, batch: int = 0):
+    """This rank's share of the global cfg2 batch (8 sequences per GPU, valid
+    lengths ~U[2048, 4096] from one seed): cost-balanced contiguous
+    (batch, head) units. Returns (global units, first row, end row, global
+    lengths)."""
+    from enilnets_b200 import sharding
+    S, H = CFG2["S"], CFG2["H"]
+    Bg = (batch or CFG2["B"]) * world
+    lengths = cfg2_lengths(0, Bg)
+    costs = sharding.prefill_unit_costs(lengths, S, H)
+    units = sharding.contiguous_partition(costs, world)[rank]
+    return units, units[0] // H, units[-1] // H + 1, lengths
+
+
 def bench_prefill(dist: Dist, clocks: ClockSampler, steps: int, warmup: int, batch: int = 0,
-                  e2e_on: bool = True):
+                  e2e_on: bool = True, e2e_policy: str = "local"):
+    """Weak scaling: a global batch of 8 sequences per GPU, partitioned into
+    cost-balanced contiguous (batch, head) units (sharding.contiguous_partition);
+    each rank holds only the sequences its units touch and K1 runs exactly
+    its units. Sequence b's q/k/v come from seed 1000 + b on every rank."""
     import torch
     from enilnets_b200 import kernels, _native
-    B, S, H, D = batch or CFG2["B"], CFG2["S"], CFG2["H"], CFG2["D"]
-    g = torch.Generator(device=dist.device).manual_seed(1000 + dist.rank)
-    q, k, v = (torch.randn((B, S, H, D), generator=g, device=dist.device).to(torch.bfloat16)
+    S, H, D = CFG2["S"], CFG2["H"], CFG2["D"]
+    units, b_lo, b_hi, lengths_g = prefill_partition(dist.world, dist.rank, batch)
+    B = b_hi - b_lo
+    q, k, v = (torch.empty((B, S, H, D), dtype=torch.bfloat16, device=dist.device)
                for _ in range(3))
-    lengths = cfg2_lengths(dist.rank)[:B]
+    for i in range(B):
+        g = torch.Generator(device=dist.device).manual_seed(1000 + b_lo + i)
+        for t in (q, k, v):
+            t[i] = torch.randn((S, H, D), generator=g, device=dist.device).to(torch.bfloat16)
+    lengths = lengths_g[b_lo:b_hi]
     lens = torch.tensor(lengths, dtype=torch.int32, device=dist.device)
     out = torch.empty((B, S, H, D), dtype=torch.bfloat16, device=dist.device)
+    local = [u - b_lo * H for u in units]
+    unit_t = None if local == list(range(B * H)) else \
+        torch.tensor(local, dtype=torch.int32, device=dist.device)
 
     def step():
         kernels.attention_prefill(q, k, v, causal=True, kv_valid_len=lens,
-                                  mask_mode="additive", out=out)
+                                  mask_mode="additive", out=out, units=unit_t)
 
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
     _native.raise_on_device_error()
     ms = timed(dist, clocks, step, steps)
-    flops_rank = cfg2_flops(lengths)
+    from enilnets_b200 import sharding
+    costs = sharding.prefill_unit_costs(lengths_g, S, H)
+    flops_rank = 4.0 * D * sum(costs[u] for u in units)
     flops_total = dist.sum(flops_rank)
     ms_step = ms / steps
     value = flops_total / (ms_step * 1e-3) / 1e12
 
+    info = dict(value=value, ms_step=ms_step, flops_rank=flops_rank, flops_total=flops_total,
+                lengths=[int(x) for x in lengths], per_launch_ms=ms_step,
+                rows=[b_lo, b_hi], n_units=len(units), e2e=None)
     if not e2e_on:
-        return dict(value=value, ms_step=ms_step, flops_rank=flops_rank, flops_total=flops_total,
-                    e2e=None, lengths=[int(x) for x in lengths], per_launch_ms=ms_step)
+        return info
     # End to end through the same public call: every step copies its inputs
     # from pinned host memory and reads its output back. Consecutive steps
     # overlap (PCIe is full duplex): two device input/output sets on separate
     # copy streams, so step i + 1's inputs go up while step i computes and
     # step i - 1's output comes down. Events order each slot's reuse.
-    # The pinned buffers are allocated and first touched on the GPU's own
-    # NUMA node (enilnets_b200.hostmem): with eight ranks copying at once,
-    # buffers on the far socket make the socket link the bottleneck.
-    from enilnets_b200 import hostmem
-    with hostmem.local_to(dist.local_rank) as host_cpus:
+    info["e2e"] = run_e2e(dist, clocks, q, k, v, out, lens, unit_t, steps, flops_total,
+                          e2e_policy)
+    return info
+
+
+def run_e2e(dist: Dist, clocks: ClockSampler, q, k, v, out, lens, unit_t, steps: int,
+            flops_total: float, policy: str = "local"):
+    """The e2e leg of the headline: host q/k/v in, host output back, every
+    step. policy "local" first-touches the pinned buffers on the CPUs NVML
+    reports as local to the GPU; "spread" on NUMA node rank % nodes. At N > 1
+    the leg runs twice: rank 0 alone (the other ranks idle), then every rank
+    at once, so that the line shows what concurrent copies cost."""
+    import torch
+    from enilnets_b200 import hostmem, kernels
+    cpus = hostmem.spread_cpus(dist.rank) if policy == "spread" else None
+    with hostmem.local_to(dist.local_rank, cpus) as host_cpus:
         hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
         hout = [torch.empty(out.shape, dtype=out.dtype).pin_memory() for _ in range(2)]
         for h in hout:
@@ -280,7 +324,7 @@ def bench_prefill(dist: Dist, clocks: ClockSampler, steps: int, warmup: int, bat
             if used[slot]:
                 s_cmp.wait_event(ev_out[slot])  # the slot's previous output is on the host
             kernels.attention_prefill(dq, dk, dv, causal=True, kv_valid_len=lens,
-                                      mask_mode="additive", out=dev_out[slot])
+                                      mask_mode="additive", out=dev_out[slot], units=unit_t)
             ev_cmp[slot].record(s_cmp)
         with torch.cuda.stream(s_out):
             s_out.wait_event(ev_cmp[slot])
@@ -292,34 +336,49 @@ def bench_prefill(dist: Dist, clocks: ClockSampler, steps: int, warmup: int, bat
     for i in range(2):
         e2e_step(i)
     torch.cuda.synchronize()
-    cur = torch.cuda.current_stream()
-    dist.barrier()
-    t0 = time.time()
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    start.record(cur)
-    for s_ in (s_in, s_cmp, s_out):
-        s_.wait_stream(cur)
-    for i in range(e2e_steps):
-        e2e_step(i)
-    cur.wait_stream(s_out)
-    end.record(cur)
-    torch.cuda.synchronize()
-    clocks.mark(t0, time.time())
-    dist.barrier()
-    ms_e2e = dist.max(start.elapsed_time(end)) / e2e_steps
+
+    def leg(active: bool) -> float:
+        cur = torch.cuda.current_stream()
+        dist.barrier()
+        ms = 0.0
+        if active:
+            t0 = time.time()
+            start = torch.cuda.Event(enable_timing=True)
+            end = torch.cuda.Event(enable_timing=True)
+            start.record(cur)
+            for s_ in (s_in, s_cmp, s_out):
+                s_.wait_stream(cur)
+            for i in range(e2e_steps):
+                e2e_step(i)
+            cur.wait_stream(s_out)
+            end.record(cur)
+            torch.cuda.synchronize()
+            clocks.mark(t0, time.time())
+            ms = start.elapsed_time(end) / e2e_steps
+        dist.barrier()
+        return dist.max(ms)
+
+    alone = leg(dist.rank == 0) if dist.world > 1 else None
+    ms_e2e = leg(True)
     h2d = 3 * q.numel() * q.element_size()
     d2h = out.numel() * out.element_size()
+    place = (f"{policy}: {len(host_cpus)} CPUs ({min(host_cpus)}-{max(host_cpus)})" if host_cpus
+             else f"{policy}: unbound (no CPU set available)")
     e2e = {"value": flops_total / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
            "ms_per_step": ms_e2e, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-           "pinned_host_memory": (f"GPU-local NUMA node ({len(host_cpus)} CPUs)" if host_cpus
-                                  else "unbound (NVML gave no CPU affinity)")}
-    return dict(value=value, ms_step=ms_step, flops_rank=flops_rank, flops_total=flops_total,
-                e2e=e2e, lengths=[int(x) for x in lengths], per_launch_ms=ms_step)
+           "h2d_GB_s_per_rank": h2d / (ms_e2e * 1e-3) / 1e9,
+           "d2h_GB_s_per_rank": d2h / (ms_e2e * 1e-3) / 1e9,
+           "pinned_host_memory": place, "numa_nodes": len(hostmem.numa_nodes())}
+    if alone is not None:
+        e2e["rank0_alone_ms_per_step"] = alone
+        e2e["rank0_alone_h2d_GB_s"] = h2d / (alone * 1e-3) / 1e9
+        e2e["host_copy_GB_s_all_ranks"] = dist.world * (h2d + d2h) / (ms_e2e * 1e-3) / 1e9
+    return e2e
 
 
 def bench_decode_cfg3(dist: Dist, clocks: ClockSampler, warmup: int, batch: int = 0):
-    """Batch rows split across ranks (64 / N per GPU)."""
+    """Batch rows split across ranks (64 / N per GPU). K and V live in one
+    (2, B, H, capacity, D) allocation, so one K3 launch appends both."""
     import torch
     from enilnets_b200 import kernels, _native
     from enilnets_b200 import sharding
@@ -330,20 +389,19 @@ def bench_decode_cfg3(dist: Dist, clocks: ClockSampler, warmup: int, batch: int 
         return {"skipped": f"batch {Btot} has no rows for rank {dist.rank}"}
     cap = ctx + T
     g = torch.Generator(device=dist.device).manual_seed(3 + dist.rank)
-    kc = torch.empty((B, H, cap, D), dtype=torch.bfloat16, device=dist.device)
-    vc = torch.empty_like(kc)
+    kv = torch.empty((2, B, H, cap, D), dtype=torch.bfloat16, device=dist.device)
+    kc, vc = kv[0], kv[1]
     kc[:, :, :ctx].normal_(generator=g)
     vc[:, :, :ctx].normal_(generator=g)
     qs = torch.randn((T, B, H, D), generator=g, device=dist.device).to(torch.bfloat16)
-    kn = torch.randn((T, B, 1, H, D), generator=g, device=dist.device).to(torch.bfloat16)
-    vn = torch.randn((T, B, 1, H, D), generator=g, device=dist.device).to(torch.bfloat16)
+    new = torch.randn((T, 2, B, 1, H, D), generator=g, device=dist.device).to(torch.bfloat16)
+    kv_rows = kv.view(2 * B, H, cap, D)  # K rows then V rows: one append covers both
     out = torch.empty((B, H, D), dtype=torch.bfloat16, device=dist.device)
     state = {"t": 0}
 
     def step():
         t = state["t"]
-        kernels.kv_append(kc, kn[t], ctx + t)
-        kernels.kv_append(vc, vn[t], ctx + t)
+        kernels.kv_append(kv_rows, new[t].view(2 * B, 1, H, D), ctx + t)
         kernels.attention_decode(qs[t], kc, vc, slot_begin=0, slot_end=ctx + t + 1,
                                  pos_slot0=0, q_pos=ctx + t, out=out)
         state["t"] = (t + 1) % T
@@ -353,7 +411,6 @@ def bench_decode_cfg3(dist: Dist, clocks: ClockSampler, warmup: int, batch: int 
     state["t"] = 0
     torch.cuda.synchronize()
     _native.raise_on_device_error()
-    # Decode-only timing of the same kernel on a fixed context, for the roofline.
     ms_all = timed(dist, clocks, step, T)
     bytes_rank = 0
     for t in range(T):
@@ -362,6 +419,7 @@ def bench_decode_cfg3(dist: Dist, clocks: ClockSampler, warmup: int, batch: int 
     bytes_total = dist.sum(bytes_rank)
     gbs = bytes_total / (ms_all * 1e-3) / 1e9
     state["t"] = 0
+    # Decode-only timing of the same kernel on a fixed context, for the roofline.
     ms_dec = timed(dist, clocks, lambda: kernels.attention_decode(
         qs[0], kc, vc, slot_begin=0, slot_end=ctx + 1, pos_slot0=0, q_pos=ctx, out=out), T)
     dec_bytes = 2 * B * H * D * 2 * (ctx + 1) + 2 * B * H * D * 2
@@ -369,25 +427,38 @@ def bench_decode_cfg3(dist: Dist, clocks: ClockSampler, warmup: int, batch: int 
     return {"GB_s": gbs, "tokens_s": Btot * T / (ms_all * 1e-3), "ms_per_step": ms_all / T,
             "decode_kernel_GB_s": dec_gbs, "decode_kernel_ms": ms_dec / T,
             "splits": kernels.decode_auto_splits(B, H, ctx + 1),
-            "config": f"B{Btot} H{H} D{D} ctx {ctx}+{T} steps, append each step, "
+            "config": f"B{Btot} H{H} D{D} ctx {ctx}+{T} steps, one K+V append each step, "
                       f"{B} rows per GPU"}
 
 
-def bench_longctx_cfg5(dist: Dist, clocks: ClockSampler, warmup: int):
-    """Sequence-sharded split-KV decode with an NCCL all-gather of (out, LSE)."""
+def _cfg5_shard(dist: "Dist", rank: int, B: int, H: int, D: int, ctx: int, T: int):
+    """Rank `rank`'s cfg5 cache shard on this device, generated exactly as
+    that rank generates it (same seed, same calls), and its slot range."""
     import torch
-    from enilnets_b200 import kernels, sharding, _native
-    B, H, D, ctx, T = CFG5["B"], CFG5["H"], CFG5["D"], CFG5["ctx"], CFG5["steps"]
-    N = dist.world
-    k0, k1 = sharding.kv_shard_range(ctx, N, dist.rank)
+    from enilnets_b200 import sharding
+    k0, k1 = sharding.kv_shard_range(ctx, dist.world, rank)
     shard = k1 - k0
-    tail = dist.rank == N - 1
-    cap = shard + (T if tail else 0)
-    g = torch.Generator(device=dist.device).manual_seed(5 + dist.rank)
+    cap = shard + (T if rank == dist.world - 1 else 0)
+    g = torch.Generator(device=dist.device).manual_seed(5 + rank)
     kc = torch.empty((B, H, cap, D), dtype=torch.bfloat16, device=dist.device)
     vc = torch.empty_like(kc)
     kc[:, :, :shard].normal_(generator=g)
     vc[:, :, :shard].normal_(generator=g)
+    return kc, vc, k0, shard
+
+
+def bench_longctx_cfg5(dist: Dist, clocks: ClockSampler, warmup: int):
+    """Sequence-sharded split-KV decode with an NCCL all-gather of (out, LSE).
+    After the timed steps: a split of the step into its parts, and a check of
+    the NCCL-merged output against the float64 oracle on sampled (b, h)."""
+    import numpy as np
+    import torch
+    from enilnets_b200 import kernels, sharding, _native
+    from oracle.attention_ref import decode_ref
+    B, H, D, ctx, T = CFG5["B"], CFG5["H"], CFG5["D"], CFG5["ctx"], CFG5["steps"]
+    N = dist.world
+    tail = dist.rank == N - 1
+    kc, vc, k0, shard = _cfg5_shard(dist, dist.rank, B, H, D, ctx, T)
     gq = torch.Generator(device=dist.device).manual_seed(55)  # same query on every rank
     qs = torch.randn((T, B, H, D), generator=gq, device=dist.device).to(torch.bfloat16)
     kn = torch.randn((T, B, 1, H, D), generator=gq, device=dist.device).to(torch.bfloat16)
@@ -396,14 +467,17 @@ def bench_longctx_cfg5(dist: Dist, clocks: ClockSampler, warmup: int):
     decode = sharding.SequenceShardedDecode()  # local split-KV decode, NCCL gather, LSE merge
     state = {"t": 0}
 
+    def n_live(t):
+        return shard + (t + 1 if tail else 0)
+
     def step():
         t = state["t"]
         pos = ctx + t
         if tail:
             kernels.kv_append(kc, kn[t], shard + t)
             kernels.kv_append(vc, vn[t], shard + t)
-        n_live = shard + (t + 1 if tail else 0)
-        decode(qs[t], kc, vc, slot_begin=0, slot_end=n_live, pos_slot0=k0, q_pos=pos, out=out)
+        decode(qs[t], kc, vc, slot_begin=0, slot_end=n_live(t), pos_slot0=k0, q_pos=pos,
+               out=out)
         state["t"] = (t + 1) % T
 
     for _ in range(max(warmup, 3)):
@@ -413,9 +487,60 @@ def bench_longctx_cfg5(dist: Dist, clocks: ClockSampler, warmup: int):
     _native.raise_on_device_error()
     ms = timed(dist, clocks, step, T)
     bytes_total = sum(2 * B * H * D * 2 * (ctx + t + 1) for t in range(T))
-    return {"GB_s": bytes_total / (ms * 1e-3) / 1e9, "tokens_s": B * T / (ms * 1e-3),
-            "ms_per_step": ms / T, "shard_tokens_per_gpu": shard,
-            "collective": "none" if N == 1 else "ncclAllGather of fp32 (out, LSE) + LSE merge"}
+    res = {"GB_s": bytes_total / (ms * 1e-3) / 1e9, "tokens_s": B * T / (ms * 1e-3),
+           "ms_per_step": ms / T, "shard_tokens_per_gpu": shard,
+           "collective": "none" if N == 1 else "ncclAllGather of fp32 (out, LSE) + LSE merge"}
+
+    # The step's parts, each timed alone over T repetitions (max over ranks).
+    t_last = T - 1
+    o_loc, lse_loc = kernels.attention_decode(
+        qs[t_last], kc, vc, slot_begin=0, slot_end=n_live(t_last), pos_slot0=k0,
+        q_pos=ctx + t_last, out_dtype=torch.float32, return_lse=True)
+    parts = {"local_decode_ms": timed(dist, clocks, lambda: kernels.attention_decode(
+        qs[t_last], kc, vc, slot_begin=0, slot_end=n_live(t_last), pos_slot0=k0,
+        q_pos=ctx + t_last, out=o_loc, return_lse=True), T) / T}
+    if N > 1:
+        packed = sharding.pack_partials(o_loc, lse_loc)
+        parts["all_gather_ms"] = timed(dist, clocks,
+                                       lambda: sharding.gather_partials(packed), T) / T
+        po, pl = sharding.split_partials(sharding.gather_partials(packed))
+        parts["merge_ms"] = timed(dist, clocks, lambda: kernels.lse_merge(po, pl, out=out), T) / T
+    res["step_parts"] = parts
+
+    # Correctness across ranks: one more step (t = 0, its tail token already
+    # in place) through the NCCL path, then rank 0 rebuilds every rank's
+    # shard from its seed and compares sampled (b, h) with the oracle.
+    state["t"] = 0
+    step()
+    torch.cuda.synchronize()
+    _native.raise_on_device_error()
+    if dist.rank == 0:
+        pairs = [(0, 0), (1, 17), (B - 1, H - 1)]
+        keys = {p: [] for p in pairs}
+        vals = {p: [] for p in pairs}
+        for r in range(N):
+            kr, vr, _, sr = _cfg5_shard(dist, r, B, H, D, ctx, T)
+            live = sr
+            if r == N - 1:  # the tail's slot sr holds token 0 of the appended ones
+                kr[:, :, sr:sr + T] = kn[:, :, 0].permute(1, 2, 0, 3)
+                vr[:, :, sr:sr + T] = vn[:, :, 0].permute(1, 2, 0, 3)
+                live = sr + 1
+            for (b, h) in pairs:
+                keys[(b, h)].append(kr[b, h, :live].float().cpu().numpy())
+                vals[(b, h)].append(vr[b, h, :live].float().cpu().numpy())
+            del kr, vr
+        got = out.float().cpu().numpy()
+        q0 = qs[0].float().cpu().numpy()
+        err = 0.0
+        for (b, h) in pairs:
+            K = np.concatenate(keys[(b, h)])[None, None]
+            V = np.concatenate(vals[(b, h)])[None, None]
+            o_ref, _ = decode_ref(q0[b:b + 1, h:h + 1], K, V, slot_begin=0,
+                                  slot_end=K.shape[2], pos_slot0=0, q_pos=ctx)
+            err = max(err, float(np.max(np.abs(got[b, h] - o_ref[0, 0]))))
+        res["check"] = {"max_abs_err": err, "pairs": [list(p) for p in pairs],
+                        "against": "float64 oracle over all ranks' shards (rebuilt from seeds)"}
+    return res
 
 
 def bench_cross_cfg4(dist: Dist, clocks: ClockSampler, warmup: int, steps: int = 50):
@@ -567,6 +692,51 @@ def bench_sparse(dist: Dist, clocks: ClockSampler, warmup: int, steps: int = 10,
     return res
 
 
+def bench_projections(dist: Dist, clocks: ClockSampler, warmup: int, steps: int = 20):
+    """The cfg2 layer's projections on K6 (tcgen05 CTA pairs): the fused QKV
+    GEMM (M = 8 x 4096, N = 3 x 2048, K = 2048) and the output GEMM (N = 2048),
+    bf16 in / bf16 out with bias, and the QKV GEMM with RoPE fused on the Q/K
+    columns; cuBLAS (torch.nn.functional.linear) on the same operands for
+    reference. Inputs 134 MB > L2."""
+    import torch
+    import torch.nn.functional as F
+    from enilnets_b200 import kernels, _native
+    from enilnets_b200.attention import rope_tables
+    M, E, H, D = CFG2["B"] * CFG2["S"], 2048, 16, 128
+    g = torch.Generator(device=dist.device).manual_seed(9000 + dist.rank)
+    x = torch.randn((M, E), generator=g, device=dist.device).to(torch.bfloat16)
+    peak = float(load_peaks()[0]["bf16_tflops"])
+    res = {}
+    for name, N in (("qkv", 3 * E), ("o", E)):
+        w = (torch.randn((N, E), generator=g, device=dist.device) / E ** 0.5).to(torch.bfloat16)
+        b = torch.randn(N, generator=g, device=dist.device)
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=dist.device)
+        fl = 2.0 * M * N * E
+
+        def run(fn):
+            for _ in range(warmup):
+                fn()
+            torch.cuda.synchronize()
+            _native.raise_on_device_error()
+            return timed(dist, clocks, fn, steps) / steps
+
+        ms = run(lambda: kernels.project(x, w, b, out=out))
+        bb = b.to(torch.bfloat16)
+        ms_cublas = run(lambda: F.linear(x, w, bb))
+        tf = dist.sum(fl) / (ms * 1e-3) / 1e12
+        res[name] = {"ms": ms, "TFLOP_s": tf, "frac_of_bf16_peak_per_gpu": tf / dist.world / peak,
+                     "cublas_ms": ms_cublas,
+                     "cublas_TFLOP_s": dist.sum(fl) / (ms_cublas * 1e-3) / 1e12,
+                     "shape": [M, N, E]}
+        if name == "qkv":
+            cos, sin = rope_tables(CFG2["S"], D)
+            ms_r = run(lambda: kernels.project(x, w, b, out=out,
+                                               rope=(cos, sin, 2 * E, D, CFG2["S"], 0)))
+            res["qkv_rope"] = {"ms": ms_r, "TFLOP_s": dist.sum(fl) / (ms_r * 1e-3) / 1e12}
+    res["config"] = "x (32768, 2048) bf16, W (N, 2048) bf16, fp32 bias, bf16 out"
+    return res
+
+
 def bench_layer_cfg2(dist: Dist, clocks: ClockSampler, warmup: int, steps: int = 10):
     """graph.MultiHeadAttention(2048, 16, causal) forward with key padding on
     device-resident x, bf16 precision: QKV GEMM + K1 + output GEMM."""
@@ -628,7 +798,24 @@ def bench_layer_cfg1(dist: Dist, warmup: int, steps: int = 20):
 
 
 # ------------------------------------------------------------- CPU baseline
-def cpu_sample_tflops(heads: int = 16, repeats: int = 1):
+CPU_SAMPLE_HEADS = 2  # one full-length causal sequence x 2 heads of config 2 per sample
+
+
+def host_blas_threads() -> int:
+    """Give NumPy's BLAS every host thread. torchrun sets OMP_NUM_THREADS=1
+    for its workers, which would otherwise leave the CPU baseline on one
+    core; returns the thread count BLAS reports afterwards."""
+    cores = os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_info, threadpool_limits
+        threadpool_limits(limits=cores, user_api="blas")
+        counts = [i["num_threads"] for i in threadpool_info() if i["user_api"] == "blas"]
+        return max(counts) if counts else cores
+    except ImportError:
+        return cores
+
+
+def cpu_sample_tflops(heads: int = CPU_SAMPLE_HEADS, repeats: int = 1):
     """The reference's streaming softmax (oracle port of
     nn/flash_attention.py:42-80, float64, block 512) on one full-length
     causal sequence x `heads` heads of config 2; useful causal FLOPs / s."""
@@ -647,6 +834,12 @@ def cpu_sample_tflops(heads: int = 16, repeats: int = 1):
     return flops / t / 1e12, t, f"1 sequence x {heads} heads, S={S}, D={D}, causal, float64"
 
 
+def cpu_sample_desc(model: str, threads: int) -> str:
+    return (f"the reference's streaming softmax (nn/flash_attention.py:42-80, float64, block "
+            f"512) on 1 full-length causal sequence x {CPU_SAMPLE_HEADS} heads of config 2 per "
+            f"sample, scaled by useful FLOPs; NumPy/OpenBLAS with {threads} threads on {model}")
+
+
 def cpu_info():
     model = platform.processor()
     try:
@@ -659,27 +852,53 @@ def cpu_info():
     return model, os.cpu_count()
 
 
+def decode_summary(sub: dict, world: int, hbm: float) -> dict:
+    """Compact record of the two decode workloads at this GPU count, last on
+    the line so that it survives a truncated tail: HBM GB/s (all GPUs),
+    fraction of the measured per-GPU copy bandwidth, tokens/s, the cfg5
+    step's parts and its multi-rank check."""
+    out = {"n_gpus": world, "hbm_peak_gbs": hbm}
+    c3 = sub.get("decode_cfg3", {})
+    if "GB_s" in c3:
+        out["cfg3"] = {"GB_s": round(c3["GB_s"], 1),
+                       "frac_per_gpu": round(c3["GB_s"] / world / hbm, 4),
+                       "tokens_s": round(c3["tokens_s"], 1),
+                       "ms_step": round(c3["ms_per_step"], 4),
+                       "kernel_frac_per_gpu": round(c3["decode_kernel_GB_s"] / world / hbm, 4)}
+    c5 = sub.get("longctx_cfg5", {})
+    if "GB_s" in c5:
+        out["cfg5"] = {"GB_s": round(c5["GB_s"], 1),
+                       "frac_per_gpu": round(c5["GB_s"] / world / hbm, 4),
+                       "tokens_s": round(c5["tokens_s"], 1),
+                       "ms_step": round(c5["ms_per_step"], 4),
+                       "parts_ms": {k: round(v, 4) for k, v in c5.get("step_parts", {}).items()},
+                       "max_abs_err": c5.get("check", {}).get("max_abs_err")}
+    return out
+
+
 def arm_config(n_gpus: int) -> dict:
     """The headline workload's config, shared by both arms."""
     return {"workload": "cfg2 causal prefill B8/GPU S4096 H16 D128, key padding L~U[2048,4096]",
             "global_batch": CFG2["B"] * n_gpus, "seq_len": CFG2["S"],
-            "parallelism": f"batch x head over {n_gpus} GPU(s), no collective",
+            "parallelism": f"batch x head over {n_gpus} GPU(s): cost-balanced contiguous "
+                           "(batch, head) units per GPU, no collective",
             "l2": "inputs 402 MB per GPU > 126 MB L2 (no flush needed)"}
 
 
 def run_reference(args):
     """--impl reference: the reference algorithm (NumPy float64 port) on the
-    host cores, rank 0 only."""
+    host cores, rank 0 only, BLAS on every host thread."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    model, cores = cpu_info()
+    model, _ = cpu_info()
+    threads = host_blas_threads()
     for _ in range(args.warmup):
-        cpu_sample_tflops(heads=2)
+        cpu_sample_tflops()
     vals = []
     t_total = 0.0
     for _ in range(args.steps):
-        v, t, sample = cpu_sample_tflops(heads=2)
+        v, t, _ = cpu_sample_tflops()
         vals.append(v)
         t_total += t
     value = statistics.mean(vals)
@@ -687,11 +906,9 @@ def run_reference(args):
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1000 * t_total / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": {**arm_config(args.gpus), "cpu": model,
-                       "reference_sample": "the reference's streaming softmax on a bounded "
-                                           "sample of the workload, scaled by useful FLOPs"},
-            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port",
-                             "sample": sample},
+            "config": arm_config(args.gpus),
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads,
+                             "kind": "port", "sample": cpu_sample_desc(model, threads)},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
@@ -707,7 +924,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--skip-sub", action="store_true", help="headline only")
     ap.add_argument("--only", choices=["all", "prefill", "decode", "longctx", "cross", "layer",
-                                       "linear", "sparse", "backward"],
+                                       "linear", "sparse", "backward", "e2e", "gemm"],
                     default="all",
                     help="profiling: run one workload")
     ap.add_argument("--batch", type=int, default=0,
@@ -733,6 +950,11 @@ def main():
             if args.only == "prefill":
                 res = bench_prefill(dist, clocks, args.steps, args.warmup, args.batch,
                                     e2e_on=False)
+            elif args.only == "gemm":
+                res = bench_projections(dist, clocks, args.warmup)
+            elif args.only == "e2e":
+                res = {pol: bench_prefill(dist, clocks, args.steps, args.warmup, args.batch,
+                                          e2e_policy=pol)["e2e"] for pol in ("local", "spread")}
             elif args.only == "decode":
                 res = bench_decode_cfg3(dist, clocks, args.warmup, args.decode_batch)
             elif args.only == "cross":
@@ -789,17 +1011,21 @@ def main():
             sub["decode_cfg3"]["decode_kernel_frac_of_hbm"] = \
                 sub["decode_cfg3"]["decode_kernel_GB_s"] / dist.world / hbm
         cpu = None
-        if not args.no_cpu_baseline:
-            model, cores = cpu_info()
-            v, t, sample = cpu_sample_tflops(heads=16)
-            cpu = {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port",
-                   "sample": sample + f" ({t:.1f} s, numpy/BLAS on all host threads, {model})"}
+        if not args.no_cpu_baseline and dist.world == 1:
+            model, _ = cpu_info()
+            threads = host_blas_threads()
+            cpu_sample_tflops()  # warm-up
+            v, t, _ = cpu_sample_tflops(repeats=8)
+            cpu = {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                   "sample": cpu_sample_desc(model, threads) + f"; 8 samples, {8 * t:.1f} s"}
         line = {
             "metric": METRIC, "value": pre["value"], "unit": "TFLOP/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": pre["ms_step"],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic N(0,1) activations, seeded",
-            "config": {**arm_config(args.gpus), "lengths_rank0": pre["lengths"]},
+            "config": arm_config(args.gpus),
+            "prefill_rank0": {"rows": pre["rows"], "n_units": pre["n_units"],
+                              "lengths": pre["lengths"]},
             "e2e": pre["e2e"],
             "roofline": roofline,
             "cpu_baseline": cpu,
@@ -807,6 +1033,7 @@ def main():
             "clocks": clocks.summary(),
             **sub,
         }
+        line["decode"] = decode_summary(sub, dist.world, hbm)
         print(json.dumps(line))
     dist.close()
     return 0

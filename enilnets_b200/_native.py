@@ -53,6 +53,22 @@ class PrefillArgs(Structure):
         ("scale", c_float),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t),
         ("kv_mask", c_void_p), ("kv_mask_stride_b", c_int64),
+        ("units", c_void_p), ("n_units", c_int32),
+    ]
+
+
+class ProjectArgs(Structure):
+    """Mirror of enl_project_args."""
+    _fields_ = [
+        ("x", c_void_p), ("x_stride_m", c_int64), ("x_dtype", c_int32),
+        ("w", c_void_p), ("w_lo", c_void_p), ("w_stride_n", c_int64),
+        ("bias", c_void_p),
+        ("y", c_void_p), ("y_stride_m", c_int64), ("y_dtype", c_int32),
+        ("M", c_int32), ("N", c_int32), ("K", c_int32),
+        ("rope_cols", c_int32), ("rope_head_dim", c_int32), ("rope_seq", c_int32),
+        ("rope_pos0", c_int64),
+        ("rope_cos", c_void_p), ("rope_sin", c_void_p), ("rope_rows", c_int64),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t),
     ]
 
 
@@ -173,6 +189,11 @@ SIGNATURES = {
     "enl_last_error": ([], c_char_p),
     "enl_abi_version": ([], c_int32),
     "enl_selftest_wait_timeout": ([c_int64, c_void_p], c_int32),
+    "enl_project": ([POINTER(ProjectArgs), c_void_p], c_int32),
+    "enl_project_workspace_bytes": ([POINTER(ProjectArgs)], c_size_t),
+    "enl_split_bf16": ([c_void_p, c_int64, c_int64, c_int32, c_void_p, c_void_p, c_void_p],
+                       c_int32),
+    "enl_selftest_exp2": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_void_p], c_int32),
 }
 
 _lib = None

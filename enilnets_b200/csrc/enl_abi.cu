@@ -76,6 +76,27 @@ int make_qkv_map(CUtensorMap* map, const void* base, int D, int S, int H, int B,
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// 2-D map over a row-major (rows, cols) matrix with a 128-byte swizzled box of
+// box_cols x box_rows elements (box_cols * element size = 128 bytes).
+int make_2d_map(CUtensorMap* map, const void* base, bool fp32, int64_t cols, int64_t rows,
+                int64_t ld, uint32_t box_cols, uint32_t box_rows, const char* name) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(ENL_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  const int esz = fp32 ? 4 : 2;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * esz)};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                  2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(ENL_ERR_INVALID, "cuTensorMapEncodeTiled(%s) failed with CUresult %d", name,
+                (int)r);
+  return ENL_OK;
+}
+
 // SM count of the current device, cached per device.
 int sm_count(int* out) {
   static int cached[64] = {0};
@@ -276,9 +297,15 @@ int prefill_impl(const enl_prefill_args* a, const enl_sparse_layout* layout, voi
   // One persistent CTA per SM. Sections of (batch, head) pairs whose K/V
   // fit in about a quarter of L2 keep the concurrently running items on
   // shared keys.
+  if (a->units && a->n_units < 0)
+    return fail(ENL_ERR_INVALID, "enl_attn_prefill: n_units=%d must be >= 0", a->n_units);
+  if (a->units && (reinterpret_cast<uintptr_t>(a->units) & 3u) != 0)
+    return fail(ENL_ERR_INVALID, "enl_attn_prefill: units must be 4-byte aligned");
+  p.units = a->units;
+  p.n_bh = a->units ? a->n_units : a->batch * a->num_heads;
   {
     const long long n_qt = (a->seq_q + 127) / 128;
-    const long long n_items = (long long)a->batch * a->num_heads * n_qt;
+    const long long n_items = (long long)p.n_bh * n_qt;
     if (n_items > (1ll << 30))
       return fail(ENL_ERR_UNSUPPORTED, "enl_attn_prefill: %lld query tiles exceed 2^30", n_items);
     p.n_items = (int)n_items;
@@ -290,7 +317,7 @@ int prefill_impl(const enl_prefill_args* a, const enl_sparse_layout* layout, voi
         4.0 * a->seq_kv * D * (split ? 2 : 1) / G;  // K and V, bf16, shared by G heads
     const double budget = ENL_PREFILL_SECTION_MB * double(1 << 20);
     long long sec = (long long)(budget / kv_bytes_per_head);
-    const long long n_bh = (long long)a->batch * a->num_heads;
+    const long long n_bh = std::max(1, p.n_bh);
     p.sec_bh = (int)std::max(1ll, std::min(n_bh, sec));
   }
 
@@ -340,6 +367,128 @@ int enl_attn_prefill_sparse(const enl_prefill_args* a, const enl_sparse_layout* 
                 "enl_attn_prefill_sparse: the layout is the whole mask; window must be < 0, "
                 "mask_mode ENL_MASK_EXCLUDE and kv_valid_len and kv_mask NULL");
   return prefill_impl(a, l, stream);
+}
+
+size_t enl_project_workspace_bytes(const enl_project_args* a) {
+  if (!a || a->x_dtype != ENL_DTYPE_FP32 || a->M < 1 || a->K < 1) return 0;
+  const size_t plane = ((size_t)a->M * a->K * 2 + 255) & ~size_t(255);
+  return 2 * plane;
+}
+
+int enl_project(const enl_project_args* a, void* stream) {
+  if (!a) return fail(ENL_ERR_INVALID, "enl_project: args is NULL");
+  if (!a->x || !a->w || !a->y)
+    return fail(ENL_ERR_INVALID, "enl_project: x, w and y must be non-NULL");
+  if (a->M < 0 || a->N < 1 || a->K < 1)
+    return fail(ENL_ERR_INVALID, "enl_project: M=%d N=%d K=%d (M >= 0, N and K >= 1)", a->M,
+                a->N, a->K);
+  if (a->K % 8 != 0 || a->N % 8 != 0)
+    return fail(ENL_ERR_UNSUPPORTED, "enl_project: K=%d and N=%d must be multiples of 8", a->K,
+                a->N);
+  if (a->x_dtype != ENL_DTYPE_BF16 && a->x_dtype != ENL_DTYPE_FP32)
+    return fail(ENL_ERR_INVALID, "enl_project: x_dtype=%d", a->x_dtype);
+  if (a->y_dtype != ENL_DTYPE_BF16 && a->y_dtype != ENL_DTYPE_FP32)
+    return fail(ENL_ERR_INVALID, "enl_project: y_dtype=%d", a->y_dtype);
+  const bool split = a->x_dtype == ENL_DTYPE_FP32;
+  if (split && !a->w_lo)
+    return fail(ENL_ERR_INVALID, "enl_project: fp32 x needs the weight's lo plane w_lo");
+  if (!split && a->w_lo)
+    return fail(ENL_ERR_INVALID, "enl_project: w_lo is only used with fp32 x");
+  const int xsz = split ? 4 : 2, ysz = a->y_dtype == ENL_DTYPE_FP32 ? 4 : 2;
+  if (!aligned16(a->x) || !aligned16(a->w) || !aligned16(a->y) || (a->w_lo && !aligned16(a->w_lo)))
+    return fail(ENL_ERR_INVALID, "enl_project: x, w, w_lo and y must be 16-byte aligned");
+  if (a->x_stride_m < a->K || (a->x_stride_m * xsz) % 16 != 0 || a->w_stride_n < a->K ||
+      (a->w_stride_n * 2) % 16 != 0 || a->y_stride_m < a->N || (a->y_stride_m * ysz) % 16 != 0)
+    return fail(ENL_ERR_INVALID,
+                "enl_project: row strides (x %lld, w %lld, y %lld) must cover a row and be "
+                "multiples of 16 bytes",
+                (long long)a->x_stride_m, (long long)a->w_stride_n, (long long)a->y_stride_m);
+  if (a->bias && (reinterpret_cast<uintptr_t>(a->bias) & 15u) != 0)
+    return fail(ENL_ERR_INVALID, "enl_project: bias must be 16-byte aligned");
+  if (a->rope_cols < 0 || a->rope_cols > a->N)
+    return fail(ENL_ERR_INVALID, "enl_project: rope_cols=%d outside [0, N=%d]", a->rope_cols,
+                a->N);
+  if (a->rope_cols > 0) {
+    const int d = a->rope_head_dim;
+    if (d != 8 && d != 16 && d != 32 && d != 64 && d != 128)
+      return fail(ENL_ERR_UNSUPPORTED,
+                  "enl_project: rope_head_dim=%d (fused RoPE: 8, 16, 32, 64 or 128)", d);
+    if (a->rope_cols % d != 0)
+      return fail(ENL_ERR_INVALID, "enl_project: rope_cols=%d is not whole heads of %d",
+                  a->rope_cols, d);
+    if (!a->rope_cos || !a->rope_sin || a->rope_seq < 1 || a->rope_pos0 < 0)
+      return fail(ENL_ERR_INVALID,
+                  "enl_project: RoPE needs cos/sin tables, rope_seq >= 1 and rope_pos0 >= 0");
+    const long long last = a->rope_pos0 + std::min<long long>(a->rope_seq, std::max(a->M, 1)) - 1;
+    if (last >= a->rope_rows)
+      return fail(ENL_ERR_INVALID, "enl_project: RoPE position %lld beyond the %lld table rows",
+                  last, (long long)a->rope_rows);
+    if ((reinterpret_cast<uintptr_t>(a->rope_cos) & 15u) ||
+        (reinterpret_cast<uintptr_t>(a->rope_sin) & 15u))
+      return fail(ENL_ERR_INVALID, "enl_project: RoPE tables must be 16-byte aligned");
+  }
+  if (a->M == 0) return ENL_OK;
+  int st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  CUtensorMap tx, txlo, tw, twlo, ty;
+  if (split) {
+    const size_t need = enl_project_workspace_bytes(a);
+    if (!a->workspace || a->workspace_bytes < need)
+      return fail(ENL_ERR_INVALID, "enl_project: fp32 x needs a %zu-byte workspace (got %zu)",
+                  need, a->workspace_bytes);
+    if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0)
+      return fail(ENL_ERR_INVALID, "enl_project: workspace must be 256-byte aligned");
+    uint8_t* hi = reinterpret_cast<uint8_t*>(a->workspace);
+    uint8_t* lo = hi + need / 2;
+    cudaError_t e = launch_split_matrix(reinterpret_cast<const float*>(a->x), a->x_stride_m, a->M,
+                                        a->K, hi, lo, s);
+    if (e != cudaSuccess) return cuda_fail(e, "enl_project: split x");
+    if ((st = make_2d_map(&tx, hi, false, a->K, a->M, a->K, 64, 128, "x hi"))) return st;
+    if ((st = make_2d_map(&txlo, lo, false, a->K, a->M, a->K, 64, 128, "x lo"))) return st;
+    if ((st = make_2d_map(&twlo, a->w_lo, false, a->K, a->N, a->w_stride_n, 64, 128, "w lo")))
+      return st;
+  } else {
+    if ((st = make_2d_map(&tx, a->x, false, a->K, a->M, a->x_stride_m, 64, 128, "x"))) return st;
+    txlo = tx;
+  }
+  if ((st = make_2d_map(&tw, a->w, false, a->K, a->N, a->w_stride_n, 64, 128, "w"))) return st;
+  if (!split) twlo = tw;
+  const bool yf32 = a->y_dtype == ENL_DTYPE_FP32;
+  if ((st = make_2d_map(&ty, a->y, yf32, a->N, a->M, a->y_stride_m, yf32 ? 32 : 64, 32, "y")))
+    return st;
+  ProjParams p;
+  p.M = a->M;
+  p.N = a->N;
+  p.K = a->K;
+  p.bias = a->bias;
+  p.out_fp32 = yf32;
+  p.rope_cols = a->rope_cols;
+  p.rope_d = a->rope_cols > 0 ? a->rope_head_dim : 128;
+  p.rope_seq = a->rope_cols > 0 ? a->rope_seq : 0;
+  p.rope_pos0 = a->rope_pos0;
+  p.rope_cos = a->rope_cos;
+  p.rope_sin = a->rope_sin;
+  int sms = 0;
+  if ((st = sm_count(&sms))) return st;
+  cudaError_t e = split ? launch_proj_gemm<true>(tx, txlo, tw, twlo, ty, p, sms, s)
+                        : launch_proj_gemm<false>(tx, txlo, tw, twlo, ty, p, sms, s);
+  if (e != cudaSuccess) return cuda_fail(e, "enl_project launch");
+  return ENL_OK;
+}
+
+int enl_split_bf16(const float* src, int64_t ld, int64_t rows, int32_t cols, void* hi, void* lo,
+                   void* stream) {
+  if (!src || !hi || !lo) return fail(ENL_ERR_INVALID, "enl_split_bf16: NULL pointer");
+  if (rows < 0 || cols < 0 || cols % 4 != 0 || ld < cols || ld % 4 != 0)
+    return fail(ENL_ERR_INVALID, "enl_split_bf16: rows=%lld cols=%d ld=%lld (cols, ld multiples "
+                "of 4, ld >= cols)", (long long)rows, cols, (long long)ld);
+  if (!aligned16(src) || (reinterpret_cast<uintptr_t>(hi) & 7u) ||
+      (reinterpret_cast<uintptr_t>(lo) & 7u))
+    return fail(ENL_ERR_INVALID, "enl_split_bf16: src must be 16-byte and planes 8-byte aligned");
+  cudaError_t e = launch_split_matrix(src, ld, rows, cols, hi, lo,
+                                      reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "enl_split_bf16 launch");
+  return ENL_OK;
 }
 
 size_t enl_backward_workspace_bytes(const enl_backward_args* a) {

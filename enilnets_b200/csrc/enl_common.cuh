@@ -447,8 +447,9 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
 // 2^x on the FMA/ALU pipes, for x in (-inf, 8]: round-to-nearest range
 // reduction x = n + f, f in [-0.5, 0.5], via the 1.5 * 2^23 magic constant,
 // then a cubic for 2^f whose coefficients minimise the relative error on that
-// interval (Lawson-weighted least squares; max relative error 7.6e-5, well
-// under the 2^-9 of the bf16 P it feeds), then n is added to the exponent.
+// interval (Lawson-weighted least squares), then n is added to the exponent.
+// Max relative error, fp32 rounding included: 7.64e-5 (measured over
+// [-125, 8] against exact 2^x), well under the 2^-9 of the bf16 P it feeds.
 // Inputs below -125 are clamped (results ~1e-38 instead of 0); only used on
 // tiles with no masked scores.
 __device__ __forceinline__ float exp2_poly(float x) {

@@ -26,9 +26,13 @@ struct PrefillParams {
   const float* alibi;          // (H) ALiBi slopes (natural-log units), or null
   long long q_pos0, k_pos0;
   float scale_log2;            // softmax scale * log2(e)
-  // Persistent schedule: n_items = B * H * ceil(Sq / 128) work items over
+  // Persistent schedule: n_items = n_bh * ceil(Sq / 128) work items over
   // min(n_items, n_ctas) CTAs, in sections of sec_bh (batch, head) pairs.
+  // The pairs are all B * H of them (units null) or units[0 .. n_bh), each
+  // b * H + h.
   int n_items, n_ctas, sec_bh;
+  int n_bh;
+  const int* units;
   // Block-sparse mode (nn/sparse_attention.py:96-142), when sp_ptr is set:
   // query tile qt visits the key tiles sp_kt[sp_ptr[qt] .. sp_ptr[qt + 1]),
   // and row r of entry e sees key column c of half h (keys 64h + c of the
@@ -48,6 +52,27 @@ struct PrefillParams {
   long long kv_mask_sb;
   const int4* mask_tiles;
 };
+
+// K6 projection GEMM (enl_gemm.cu): Y[m, n] = sum_k X[m, k] W[n, k] + bias[n],
+// then rotate-half RoPE on columns n < rope_cols in heads of rope_d columns at
+// position rope_pos0 + (m % rope_seq), with fp32 tables (rows, rope_d / 2).
+struct ProjParams {
+  int M, N, K;
+  const float* bias;  // (N) or null
+  int out_fp32;
+  int rope_cols, rope_d, rope_seq;
+  long long rope_pos0;
+  const float* rope_cos;
+  const float* rope_sin;
+};
+template <bool kSplit>
+cudaError_t launch_proj_gemm(const CUtensorMap& tx, const CUtensorMap& txlo,
+                             const CUtensorMap& tw, const CUtensorMap& twlo,
+                             const CUtensorMap& ty, const ProjParams& p, int n_sms,
+                             cudaStream_t stream);
+// fp32 (rows, cols) with row stride ld -> contiguous bf16 planes hi, lo.
+cudaError_t launch_split_matrix(const float* src, long long ld, long long rows, int cols,
+                                void* hi, void* lo, cudaStream_t stream);
 
 // Fill p.mask_tiles (B * ceil(Sq / 128) entries) from p.kv_mask, p.kv_len and
 // the causal/window bounds; must run before the prefill launch on the same

@@ -10,3 +10,4 @@
 #include "enl_linear.cu"
 #include "enl_sparse.cu"
 #include "enl_backward.cu"
+#include "enl_gemm.cu"

@@ -156,13 +156,20 @@ template <int kMode>
 __device__ __forceinline__ WorkItem work_item(const PrefillParams& p, int t) {
   constexpr bool kSparse = kMode == kModeSparse;
   const int n_qt = (p.Sq + 127) / 128;
-  const int n_bh = p.B * p.H;
+  const int n_bh = p.n_bh;
   const int per_sec = p.sec_bh * n_qt;
   const int s = t / per_sec;
   const int r = t - s * per_sec;
   const int sb = min(p.sec_bh, n_bh - s * p.sec_bh);
   const int qt = n_qt - 1 - r / sb;
-  const int bh = s * p.sec_bh + r % sb;
+  int bh = s * p.sec_bh + r % sb;
+  if (p.units != nullptr) {  // this call's (batch, head) units, b * H + h each
+    bh = p.units[bh];
+    if (bh < 0 || bh >= p.B * p.H) {
+      report_error(kDevBadIndex, bh);
+      bh = 0;
+    }
+  }
   WorkItem w;
   w.b = bh / p.H;
   w.h = bh % p.H;

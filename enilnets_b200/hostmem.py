@@ -49,10 +49,49 @@ def gpu_local_cpus(device: int) -> Optional[List[int]]:
     return cpus or None
 
 
+def numa_nodes() -> List[List[int]]:
+    """CPUs of each NUMA node of the host (from sysfs), restricted to the
+    CPUs this process may run on; [] when sysfs does not say."""
+    base = "/sys/devices/system/node"
+    nodes = []
+    try:
+        names = sorted((n for n in os.listdir(base) if n.startswith("node") and n[4:].isdigit()),
+                       key=lambda n: int(n[4:]))
+    except OSError:
+        return []
+    allowed = os.sched_getaffinity(0)
+    for name in names:
+        try:
+            with open(os.path.join(base, name, "cpulist")) as f:
+                text = f.read().strip()
+        except OSError:
+            continue
+        cpus = []
+        for part in filter(None, text.split(",")):
+            lo, _, hi = part.partition("-")
+            cpus.extend(range(int(lo), int(hi or lo) + 1))
+        cpus = [c for c in cpus if c in allowed]
+        if cpus:
+            nodes.append(cpus)
+    return nodes
+
+
+def spread_cpus(rank: int) -> Optional[List[int]]:
+    """CPUs of NUMA node rank % (number of nodes): spreads the ranks' pinned
+    buffers over every node's memory, for hosts where every GPU reports the
+    same local node; None on a single-node host."""
+    nodes = numa_nodes()
+    if len(nodes) < 2:
+        return None
+    return nodes[rank % len(nodes)]
+
+
 @contextlib.contextmanager
-def local_to(device: int) -> Iterator[Optional[List[int]]]:
-    """Run the block on the GPU's local CPUs; yield them (None: unbound)."""
-    cpus = gpu_local_cpus(device)
+def local_to(device: int, cpus: Optional[List[int]] = None) -> Iterator[Optional[List[int]]]:
+    """Run the block on the GPU's local CPUs (or on `cpus` when given); yield
+    the CPUs used (None: unbound)."""
+    if cpus is None:
+        cpus = gpu_local_cpus(device)
     before = os.sched_getaffinity(0)
     if cpus:
         os.sched_setaffinity(0, cpus)

@@ -48,7 +48,8 @@ def attention_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
                       scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
                       out_dtype: torch.dtype = torch.bfloat16,
                       return_lse: bool = False, sparse=None,
-                      kv_mask: Optional[torch.Tensor] = None):
+                      kv_mask: Optional[torch.Tensor] = None,
+                      units: Optional[torch.Tensor] = None):
     """softmax(q k^T * scale + alibi + mask) v via the K1 tcgen05 kernel.
 
     q: (B, Sq, H, D); k, v: (B, Skv, Hkv, D); all bf16, or all fp32 (the
@@ -61,6 +62,9 @@ def attention_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     (graph/sequence.py:162-168 accepts any boolean mask, not only prefixes).
     mask_mode: "exclude" (-inf, the nn/ path) or "additive" (-1e9 per violated
     mask term, graph/sequence.py:162-176).
+    units: int32 (n,) device list of the (batch, head) units b * H + h to
+    compute (a rank's share of sharding.partition_units); rows of other
+    units are left untouched. None = all.
     sparse: a block-sparse layout (enilnets_b200.sparse.SparseLayout) built for
     these Sq, Skv, q_pos0 and k_pos0; it is then the whole mask (causal only
     picks the ALiBi distance), nn/sparse_attention.py:96-142.
@@ -119,6 +123,11 @@ def attention_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     a.scale = 1.0 / math.sqrt(D) if scale is None else float(scale)
     if kv_mask is not None:
         a.kv_mask, a.kv_mask_stride_b = kv_mask.data_ptr(), kv_mask.stride(0)
+    if units is not None:
+        _require_cuda("units", units, torch.int32, last_contiguous=False)
+        if units.dim() != 1 or not units.is_contiguous():
+            raise ValueError("units must be a contiguous int32 1-D tensor")
+        a.units, a.n_units = units.data_ptr(), units.numel()
     lib = nat.load()
     ws = None
     need = int(lib.enl_prefill_workspace_bytes(ctypes.byref(a)))
@@ -142,6 +151,83 @@ def attention_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
         nat.check(lib.enl_attn_prefill_sparse(ctypes.byref(a), ctypes.byref(sparse.native()),
                                               _stream()), "enl_attn_prefill_sparse")
     return (out, lse) if return_lse else out
+
+
+def split_bf16(w: torch.Tensor):
+    """fp32 (rows, cols) -> contiguous bf16 planes (hi, lo), hi = bf16(w),
+    lo = bf16(w - hi): the weight operand of project() for fp32 inputs."""
+    _require_cuda("w", w, torch.float32)
+    if w.dim() != 2:
+        raise ValueError("w must be 2-D (rows, cols)")
+    rows, cols = w.shape
+    hi = torch.empty((rows, cols), dtype=torch.bfloat16, device=w.device)
+    lo = torch.empty_like(hi)
+    nat.check(nat.load().enl_split_bf16(w.data_ptr(), w.stride(0), rows, cols, hi.data_ptr(),
+                                        lo.data_ptr(), _stream()), "enl_split_bf16")
+    return hi, lo
+
+
+def project(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None, *,
+            w_lo: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+            out_dtype: Optional[torch.dtype] = None, rope=None) -> torch.Tensor:
+    """y = x @ w.T + bias on the K6 tcgen05 GEMM (nn/forward.py:428-430, :551).
+
+    x: (..., K) bf16, or fp32 with w_lo given (the split-bf16 path: w = the hi
+    plane, w_lo the lo plane from split_bf16). w: (N, K) bf16. bias: fp32 (N,).
+    rope: optional (cos, sin, rot_cols, head_dim, seq, pos0): rotate-half RoPE
+    (nn/forward.py:80-88) fused into the epilogue on columns < rot_cols, heads
+    of head_dim columns, row r of x at position pos0 + (r % seq); cos/sin fp32
+    (rows, head_dim / 2) tables. Returns y (..., N), out_dtype (default: x's).
+    """
+    _require_cuda("x", x)
+    _require_cuda("w", w, torch.bfloat16)
+    if x.dtype not in _DTYPES:
+        raise ValueError(f"x must be bfloat16 or float32 (got {x.dtype})")
+    if w.dim() != 2 or x.shape[-1] != w.shape[1]:
+        raise ValueError(f"shape mismatch: x {tuple(x.shape)}, w {tuple(w.shape)}")
+    lead = x.shape[:-1]
+    K, N = w.shape[1], w.shape[0]
+    x2 = x.reshape(-1, K)
+    if x2.stride(1) != 1:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    out_dtype = out_dtype or x.dtype
+    if out is None:
+        out = torch.empty(lead + (N,), dtype=out_dtype, device=x.device)
+    _require_cuda("out", out)
+    y2 = out.view(-1, N)
+    a = nat.ProjectArgs()
+    a.x, a.x_stride_m, a.x_dtype = x2.data_ptr(), x2.stride(0), _DTYPES[x.dtype]
+    a.w, a.w_stride_n = w.data_ptr(), w.stride(0)
+    if w_lo is not None:
+        _require_cuda("w_lo", w_lo, torch.bfloat16)
+        if w_lo.shape != w.shape or w_lo.stride() != w.stride():
+            raise ValueError("w_lo must match w's shape and strides")
+        a.w_lo = w_lo.data_ptr()
+    if bias is not None:
+        _require_cuda("bias", bias, torch.float32, last_contiguous=False)
+        if tuple(bias.shape) != (N,) or not bias.is_contiguous():
+            raise ValueError(f"bias must be a contiguous float32 ({N},) tensor")
+        a.bias = bias.data_ptr()
+    a.y, a.y_stride_m, a.y_dtype = y2.data_ptr(), y2.stride(0), _DTYPES[out.dtype]
+    a.M, a.N, a.K = M, N, K
+    if rope is not None:
+        cos, sin, cols, hd, seq, pos0 = rope
+        for name, t in (("cos", cos), ("sin", sin)):
+            _require_cuda(name, t, torch.float32)
+            if not t.is_contiguous() or t.dim() != 2 or t.shape[1] != hd // 2:
+                raise ValueError(f"rope {name} must be a contiguous fp32 (rows, {hd // 2}) table")
+        a.rope_cols, a.rope_head_dim, a.rope_seq, a.rope_pos0 = int(cols), int(hd), int(seq), \
+            int(pos0)
+        a.rope_cos, a.rope_sin, a.rope_rows = cos.data_ptr(), sin.data_ptr(), cos.shape[0]
+    lib = nat.load()
+    need = int(lib.enl_project_workspace_bytes(ctypes.byref(a)))
+    ws = None
+    if need > 0:
+        ws = torch.empty(need, dtype=torch.uint8, device=x.device)
+        a.workspace, a.workspace_bytes = ws.data_ptr(), need
+    nat.check(lib.enl_project(ctypes.byref(a), _stream()), "enl_project")
+    return out
 
 
 def attention_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor,
@@ -264,7 +350,14 @@ _workspaces: dict = {}
 
 
 def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    key = (device.index if device.index is not None else torch.cuda.current_device())
+    """Split-partial scratch of attention_decode and linear_attention, one per
+    (device, stream): calls on one stream run in order and may share it;
+    calls on different streams get their own, so they never race. A buffer
+    that grows is replaced under the same stream it was allocated on, so
+    torch's stream-ordered allocator reuses the old one only after the
+    kernels queued before it."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    key = (index, torch.cuda.current_stream(index).cuda_stream)
     ws = _workspaces.get(key)
     if ws is None or ws.numel() < nbytes:
         ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)

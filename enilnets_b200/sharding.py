@@ -6,8 +6,11 @@ Two shapes of sharding cover the attention path:
   collective. Key padding makes the units unequal: a causal row of valid
   length L has L(L+1)/2 + (S - L) * L visible (query, key) pairs (padded
   query rows still see all L real keys, the graph layer's rule,
-  graph/sequence.py:159-183). The units are balanced by that cost with the
-  longest-processing-time rule.
+  graph/sequence.py:159-183). The units are balanced by that cost, either
+  with the longest-processing-time rule (partition_units, any units) or as
+  cost-balanced contiguous ranges (contiguous_partition), so that a rank's
+  inputs are a run of consecutive sequences; K1 then runs exactly the
+  rank's units (the units argument of kernels.attention_prefill).
 * Long-context decode (K2) shards the KV sequence into contiguous slot
   ranges. Each rank runs the split-KV decode on its range and produces a
   normalised partial (out, lse). The partials are all-gathered (NCCL on GPUs,
@@ -61,6 +64,28 @@ def partition_units(costs: Sequence[int], world: int) -> List[List[int]]:
         parts[r].append(i)
         heapq.heappush(heap, (load + costs[i], r))
     return [sorted(p) for p in parts]
+
+
+def contiguous_partition(costs: Sequence[int], world: int) -> List[List[int]]:
+    """Cost-balanced partition of units into `world` contiguous index ranges.
+
+    Units are taken in index order (for (batch, head) units: batch-major,
+    so a rank's units cover a run of consecutive sequences and its inputs
+    are those sequences only). Unit i goes to the rank whose share of the
+    total cost contains the unit's cost midpoint, so every rank's load is
+    within one unit's cost of total / world. Deterministic: every rank
+    computes the same partition without communicating."""
+    if world < 1:
+        raise ValueError(f"world must be >= 1, got {world}")
+    total = float(sum(costs))
+    parts: List[List[int]] = [[] for _ in range(world)]
+    acc = 0.0
+    for i, c in enumerate(costs):
+        mid = acc + c / 2.0
+        r = min(world - 1, int(mid * world / total)) if total > 0 else i * world // len(costs)
+        parts[r].append(i)
+        acc += c
+    return parts
 
 
 def batch_shard(batch: int, world: int, rank: int) -> Tuple[int, int]:

@@ -76,6 +76,11 @@ typedef struct enl_prefill_args {
    * ignored. Needs the workspace (per-query-tile key ranges). */
   const uint64_t* kv_mask;
   int64_t kv_mask_stride_b; /* 64-bit words per batch row, >= ceil(seq_kv / 64) */
+  /* Which (batch, head) units to compute: device list of n_units entries
+   * b * num_heads + h (a rank's share of a batch x head partition); NULL =
+   * all batch * num_heads. Rows of units not listed are not written. */
+  const int32_t* units;
+  int32_t n_units;
 } enl_prefill_args;
 
 /* Fused attention prefill: softmax(Q K^T * scale + bias + mask) V.
@@ -190,6 +195,53 @@ int enl_rope_apply(void* x, int64_t stride_b, int64_t stride_s, int64_t stride_h
                    int32_t seq, int32_t num_heads, int32_t head_dim, int32_t dtype,
                    const float* cos_table, const float* sin_table, int64_t table_row0,
                    int64_t table_rows, void* stream);
+
+/* ------------------------------------------------------------ projections */
+typedef struct enl_project_args {
+  const void* x;       /* (M, K) rows, x_stride_m elements apart */
+  int64_t x_stride_m;
+  int32_t x_dtype;     /* ENL_DTYPE_BF16, or ENL_DTYPE_FP32 (split-bf16 path, needs w_lo
+                          and workspace) */
+  const void* w;       /* (N, K) bf16 weight of x @ W.T, rows w_stride_n elements apart;
+                          for fp32 x its hi plane bf16(W) */
+  const void* w_lo;    /* fp32 x: (N, K) bf16 lo plane bf16(W - bf16(W)), same strides */
+  int64_t w_stride_n;
+  const float* bias;   /* (N) fp32, or NULL */
+  void* y;             /* (M, N) rows, y_stride_m elements apart */
+  int64_t y_stride_m;
+  int32_t y_dtype;     /* ENL_DTYPE_BF16 or ENL_DTYPE_FP32 */
+  int32_t M, N, K;
+  /* RoPE fused into the epilogue (nn/forward.py:80-88): columns n < rope_cols,
+   * heads of rope_head_dim columns, rotate-half at position
+   * rope_pos0 + (m % rope_seq) with fp32 tables (rope_rows, rope_head_dim / 2)
+   * as nn/forward.py:46-55 computes them. rope_cols = 0: no rotation.
+   * rope_head_dim: 8, 16, 32, 64 or 128. */
+  int32_t rope_cols, rope_head_dim, rope_seq;
+  int64_t rope_pos0;
+  const float* rope_cos;
+  const float* rope_sin;
+  int64_t rope_rows;
+  void* workspace;     /* fp32 x: >= enl_project_workspace_bytes(), 256-byte aligned */
+  size_t workspace_bytes;
+} enl_project_args;
+
+/* y = x W^T + bias, then the RoPE rotation of the Q/K columns: the attention
+ * layers' projections (nn/forward.py:428-430 and :551, the cross-attention
+ * projections of nn/forward.py:567-586, the cached step's of
+ * nn/kvcache.py:148-154). tcgen05 MMAs on CTA pairs, fp32 accumulation.
+ * fp32 x: the split-bf16 path, x is split into hi/lo bf16 planes in the
+ * workspace and every product is hi*hi + hi*lo + lo*hi (about 2^-16
+ * relative error). K and N multiples of 8; rows 16-byte aligned. */
+int enl_project(const enl_project_args* args, void* stream);
+
+/* Workspace bytes enl_project needs (the bf16 planes of fp32 x; 0 for bf16). */
+size_t enl_project_workspace_bytes(const enl_project_args* args);
+
+/* fp32 (rows, cols) matrix with row stride ld elements -> contiguous bf16
+ * planes hi = bf16(x), lo = bf16(x - hi), for the weights of the split-bf16
+ * projections. cols a multiple of 4, rows 16-byte aligned. */
+int enl_split_bf16(const float* src, int64_t ld, int64_t rows, int32_t cols, void* hi, void* lo,
+                   void* stream);
 
 /* ---------------------------------------------------- linearized attention */
 /* The reference's attention_kernel = "linear" (phi = elu + 1) and "performer"
@@ -360,6 +412,14 @@ const char* enl_last_error(void);
  * error word and returns. No trap and no hang: the context stays usable and
  * enl_device_error() reports the status. */
 int enl_selftest_wait_timeout(int64_t budget_ns, void* stream);
+
+/* Diagnostic of the exponentials K1 computes on the FMA pipe (one pair in
+ * four of its softmax exponentials, on tiles without masked scores): for
+ * each x[i] (device fp32, n entries) writes the scalar cubic, the packed
+ * (f32x2) cubic and CUDA's exp2f of x[i]. Documented bound: relative error
+ * <= 7.7e-5 for x in [-125, 8]; inputs below -125 give 2^-125. */
+int enl_selftest_exp2(const float* x, float* y_poly, float* y_poly2, float* y_ref, int32_t n,
+                      void* stream);
 
 int enl_abi_version(void);
 

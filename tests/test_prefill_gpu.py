@@ -178,3 +178,28 @@ def test_config2_shape_sampled_rows(cuda):
                                            kv_valid_len=[lens[b]], mask_mode="additive")
                 err = np.max(np.abs(o_r[0, 0, 0] - oh[b, r, h]))
                 assert err <= TOL, (b, h, r, err)
+
+
+def test_unit_list_computes_exactly_those_units(cuda):
+    """K1 over a rank's (batch, head) units (sharding.contiguous_partition):
+    listed units equal the full run bit for bit; the rows of other units are
+    never written."""
+    import torch
+    from enilnets_b200 import kernels, _native
+    B, S, H, D = 3, 300, 4, 128
+    q, k, v = (_dev(ref.seeded_normal(70 + i, (B, S, H, D))) for i in range(3))
+    lens = torch.tensor([300, 170, 41], dtype=torch.int32).cuda()
+    full = kernels.attention_prefill(q, k, v, causal=True, kv_valid_len=lens,
+                                     mask_mode="additive")
+    units = [1, 6, 7, 11]
+    out = torch.full_like(full, 7.0)
+    kernels.attention_prefill(q, k, v, causal=True, kv_valid_len=lens, mask_mode="additive",
+                              out=out, units=torch.tensor(units, dtype=torch.int32).cuda())
+    torch.cuda.synchronize()
+    _native.raise_on_device_error()
+    for u in range(B * H):
+        b, h = divmod(u, H)
+        if u in units:
+            assert torch.equal(out[b, :, h], full[b, :, h]), f"unit {u}"
+        else:
+            assert bool((out[b, :, h] == 7.0).all()), f"unit {u} was written"

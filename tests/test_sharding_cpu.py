@@ -30,6 +30,25 @@ def test_partition_covers_every_unit_once_and_is_balanced():
         assert parts == sharding.partition_units(costs, world)  # deterministic
 
 
+def test_contiguous_partition_is_balanced_ranges():
+    """Contiguous (batch-major) unit ranges, every rank within one unit's
+    cost of the mean load; the bench's 8-sequences-per-GPU batches."""
+    rng = np.random.RandomState(2)
+    for world in (1, 2, 3, 4, 8):
+        lengths = rng.randint(2048, 4097, size=8 * world)
+        costs = sharding.prefill_unit_costs(lengths, 4096, 16)
+        parts = sharding.contiguous_partition(costs, world)
+        flat = [i for p in parts for i in p]
+        assert flat == list(range(len(costs))), "ranges in order, each unit once"
+        mean = sum(costs) / world
+        for p in parts:
+            assert p == list(range(p[0], p[-1] + 1))
+            assert abs(sum(costs[i] for i in p) - mean) <= max(costs)
+        assert parts == sharding.contiguous_partition(costs, world)
+    assert sharding.contiguous_partition([5, 5], 4) == [[], [0], [], [1]] or \
+        sum(len(p) for p in sharding.contiguous_partition([5, 5], 4)) == 2
+
+
 def test_causal_pairs_match_the_padding_rule():
     # padded query rows still see all L real keys (graph/sequence.py:159-183)
     assert sharding.causal_pairs(3, 5) == 3 * 4 // 2 + 2 * 3

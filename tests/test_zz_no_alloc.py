@@ -18,7 +18,7 @@ pytestmark = pytest.mark.gpu
 TOL = 2e-2  # the tolerance the other bf16 decode tests use
 
 
-def _noalloc_decode(q, kc, vc, out, *, slot_end, q_pos, n_splits):
+def _noalloc_decode(q, kc, vc, out, *, slot_end, q_pos, n_splits, **override):
     """Call the new entry point straight through the C ABI (no workspace)."""
     import torch
     from enilnets_b200 import _native as nat
@@ -38,6 +38,8 @@ def _noalloc_decode(q, kc, vc, out, *, slot_end, q_pos, n_splits):
     a.in_dtype, a.out_dtype = nat.ENL_DTYPE_BF16, nat.ENL_DTYPE_FP32
     a.n_splits = n_splits
     a.workspace, a.workspace_bytes = None, 0
+    for name, value in override.items():
+        setattr(a, name, value)
     status = nat.load().enl_attn_decode_noalloc(ctypes.byref(a),
                                                 torch.cuda.current_stream().cuda_stream)
     nat.check(status, "enl_attn_decode_noalloc")
@@ -53,13 +55,16 @@ def _case(seed, B, H, Hkv, D, ctx):
 
 
 def test_noalloc_decode_matches_workspace_decode_twice_in_a_row():
+    """Two calls in a row share (and overwrite) the scratch. Each must equal
+    enl_attn_decode bit for bit (same kernel, same split count) and the
+    float64 oracle within the bf16 bar."""
     import torch
     from enilnets_b200 import _native, kernels
     _native.load()
     cases = [dict(seed=31, B=4, H=8, Hkv=4, D=128, ctx=3000, n_splits=0),
              dict(seed=41, B=2, H=4, Hkv=4, D=64, ctx=1500, n_splits=5)]
     outs = []
-    for c in cases:  # two calls in a row share (and overwrite) the scratch
+    for c in cases:
         q, kc, vc = _case(c["seed"], c["B"], c["H"], c["Hkv"], c["D"], c["ctx"])
         out = torch.empty((c["B"], c["H"], c["D"]), dtype=torch.float32, device="cuda")
         _noalloc_decode(q, kc, vc, out, slot_end=c["ctx"], q_pos=c["ctx"] - 1,
@@ -72,8 +77,13 @@ def test_noalloc_decode_matches_workspace_decode_twice_in_a_row():
                                           pos_slot0=0, q_pos=c["ctx"] - 1,
                                           n_splits=c["n_splits"], out_dtype=torch.float32)
         torch.cuda.synchronize()
-        err = (out - expect).abs().max().item()
-        assert err <= TOL, f"{c}: max abs diff {err:.3e} vs enl_attn_decode"
+        assert torch.equal(out, expect), \
+            f"{c}: differs from enl_attn_decode by {(out - expect).abs().max().item():.3e}"
+        oref, _ = ref.decode_ref(q.float().cpu().numpy(), kc.float().cpu().numpy(),
+                                 vc.float().cpu().numpy(), slot_begin=0, slot_end=c["ctx"],
+                                 pos_slot0=0, q_pos=c["ctx"] - 1)
+        err = float(np.max(np.abs(out.cpu().numpy() - oref)))
+        assert err <= TOL, f"{c}: max abs err {err:.3e} vs the float64 oracle"
 
 
 def test_noalloc_decode_rejects_requests_beyond_its_scratch():
@@ -85,3 +95,11 @@ def test_noalloc_decode_rejects_requests_beyond_its_scratch():
     # 64 splits x 8 x 32 x 129 floats = 8.5 MB > 4 MiB of scratch.
     with pytest.raises(ValueError, match="bytes of scratch"):
         _noalloc_decode(q, kc, vc, out, slot_end=64, q_pos=63, n_splits=64)
+    # A bad size is reported as itself, not as an oversized scratch request.
+    with pytest.raises(ValueError, match="must be >= 1"):
+        _noalloc_decode(q, kc, vc, out, slot_end=64, q_pos=63, n_splits=8, batch=-1)
+    # The bound is on the splits actually run: a query at slot 3 sees 4 keys,
+    # which the decode runs as at most 4 splits, well inside the scratch.
+    _noalloc_decode(q, kc, vc, out, slot_end=64, q_pos=3, n_splits=64)
+    torch.cuda.synchronize()
+    _native.raise_on_device_error()
