@@ -7,10 +7,12 @@ Mirrors the reference's attention branches layer by layer:
   * key-padding (graph MHA)  graph/sequence.py:144-183 (additive -1e9 rule)
   * linearized kernels       nn/forward.py:456-480
   * block-sparse patterns    nn/forward.py:482-502
-The projections are plain GEMMs (cuBLAS through torch) in the precision that
-backend.set_precision selects (fp32 or bf16); Q/K/V are never copied or
-expanded: the prefill kernel (K1) reads them as strided head views
-of the fused QKV projection output and indexes K/V heads group-major
+The projections run on the K6 tcgen05 GEMM (kernels.project) in the
+precision that backend.set_precision selects: bf16 operands, or fp32 through
+split-bf16 planes (hi*hi + hi*lo + lo*hi). The bias and, for RoPE layers, the
+rotation of Q and K are fused into its epilogue. Q/K/V are never copied or
+expanded: the prefill kernel (K1) reads them as strided head views of the
+fused QKV projection output and indexes K/V heads group-major
 (nn/forward.py:165-171) instead of repeating them.
 """
 from __future__ import annotations
@@ -50,16 +52,23 @@ class _LayerWeights:
         self._store = {}
 
     def get(self, layer: dict, names, kind, dtype):
+        """kind "w": the weights stacked on their output axis, in dtype; "b":
+        the biases concatenated; "split": (hi, lo) bf16 planes of the fp32
+        weights, the operand of the split-bf16 projection."""
         arrays = tuple(layer[n] for n in names)
-        key = (kind, dtype) + tuple(id(a) for a in arrays)
+        key = (kind, dtype, device().index) + tuple(id(a) for a in arrays)
         hit = self._store.get(key)
         if hit is not None and all(x is y for x, y in zip(hit[0], arrays)):
             return hit[1]
-        if kind == "w":
+        import torch
+        if kind in ("w", "split"):
             host = np.concatenate([np.asarray(a, np.float32) for a in arrays], axis=0)
         else:
             host = np.concatenate([np.asarray(a, np.float32).reshape(-1) for a in arrays])
-        t = to_device(host, dtype)
+        if kind == "split":
+            t = kernels.split_bf16(to_device(host, torch.float32))
+        else:
+            t = to_device(host, dtype)
         self._store[key] = (arrays, t)
         return t
 
@@ -113,17 +122,39 @@ def apply_rope(t, pos0: int):
 
 
 # ---------------------------------------------------------- projections
-def project(x, layer: dict, which: str):
-    """x @ W.T + b for W in {"q", "kv", "qkv", "o"} as one GEMM in the compute
-    dtype (nn/forward.py:428-430, :551). fp32 GEMMs follow torch's matmul
-    precision setting, which is full fp32 unless the caller enabled TF32."""
-    import torch.nn.functional as F
+FUSED_ROPE_HEAD_DIMS = (8, 16, 32, 64, 128)
+
+
+def project(x, layer: dict, which: str, rope_pos0: Optional[int] = None, out_dtype=None):
+    """x @ W.T + b for W in {"q", "kv", "qkv", "o"} as one K6 GEMM in the
+    compute dtype (nn/forward.py:428-430, :551); fp32 runs the split-bf16
+    path. With rope_pos0 (a "qkv" projection of a RoPE layer) the Q and K
+    columns come out rotated at positions rope_pos0 + s (nn/forward.py:80-88),
+    fused into the GEMM's epilogue; returns (y, rotated) so that head dims the
+    epilogue does not cover fall back to apply_rope. out_dtype defaults to the
+    compute dtype; the layers' output projections ask for fp32, which the
+    epilogue writes directly (no bf16 rounding, no separate cast)."""
+    import torch
     names = {"q": (("Wq",), ("bq",)), "kv": (("Wk", "Wv"), ("bk", "bv")),
              "qkv": (("Wq", "Wk", "Wv"), ("bq", "bk", "bv")), "o": (("Wo",), ("bo",))}[which]
     dt = compute_dtype()
-    w = _WEIGHTS.get(layer, names[0], "w", dt)
-    b = _WEIGHTS.get(layer, names[1], "b", dt)
-    return F.linear(x.to(dt), w, b)
+    b = _WEIGHTS.get(layer, names[1], "b", torch.float32)
+    rope = None
+    if rope_pos0 is not None:
+        H, D = layer["num_heads"], layer["head_dim"]
+        Hkv = layer.get("num_kv_heads") or H
+        if D in FUSED_ROPE_HEAD_DIMS:
+            S = x.shape[-2]
+            cos, sin = rope_tables(rope_pos0 + S, D)
+            rope = (cos, sin, (H + Hkv) * D, D, S, rope_pos0)
+    out_dtype = out_dtype or dt
+    if dt == torch.float32:
+        hi, lo = _WEIGHTS.get(layer, names[0], "split", dt)
+        y = kernels.project(x.float(), hi, b, w_lo=lo, out_dtype=out_dtype, rope=rope)
+    else:
+        w = _WEIGHTS.get(layer, names[0], "w", dt)
+        y = kernels.project(x.to(dt), w, b, out_dtype=out_dtype, rope=rope)
+    return (y, rope is not None) if rope_pos0 is not None else y
 
 
 def split_heads(t, heads: int, head_dim: int, offset: int = 0):
@@ -188,12 +219,15 @@ def self_attention(layer: dict, x, key_padding_mask=None, mask_mode: Optional[st
     B, S, E = x.shape
     H, D = layer["num_heads"], layer["head_dim"]
     Hkv = layer.get("num_kv_heads") or H
-    qkv = project(x, layer, "qkv")
+    scheme = layer.get("positional_scheme", "absolute")
+    if scheme == "rope":
+        qkv, rotated = project(x, layer, "qkv", rope_pos0=0)
+    else:
+        qkv, rotated = project(x, layer, "qkv"), True
     q = split_heads(qkv, H, D, 0)
     k = split_heads(qkv, Hkv, D, H * D)
     v = split_heads(qkv, Hkv, D, H * D + Hkv * D)
-    scheme = layer.get("positional_scheme", "absolute")
-    if scheme == "rope":
+    if not rotated:
         apply_rope(q, 0)
         apply_rope(k, 0)
     if layer.get("attention_kernel", "softmax") in LINEAR_KERNELS:
@@ -201,7 +235,7 @@ def self_attention(layer: dict, x, key_padding_mask=None, mask_mode: Optional[st
             raise ValueError("key_padding_mask is not supported with a linearized "
                              "attention_kernel (it builds no score matrix to mask)")
         ctx = linearized(layer, q, k, v, bool(layer.get("causal", False)))
-        return project(ctx.flatten(-2), layer, "o").float()
+        return project(ctx.flatten(-2), layer, "o", out_dtype=torch.float32)
     if layer.get("sparse_pattern") is not None:
         if key_padding_mask is not None:
             raise ValueError("key_padding_mask is not supported with sparse_pattern (the "
@@ -210,7 +244,7 @@ def self_attention(layer: dict, x, key_padding_mask=None, mask_mode: Optional[st
                                causal=bool(layer.get("causal", False)),
                                alibi_slopes=alibi_tensor(H) if scheme == "alibi" else None,
                                out_dtype=compute_dtype())
-        return project(ctx.flatten(-2), layer, "o").float()
+        return project(ctx.flatten(-2), layer, "o", out_dtype=torch.float32)
     masks = {}
     mode = mask_mode or "exclude"
     if key_padding_mask is not None:
@@ -220,7 +254,7 @@ def self_attention(layer: dict, x, key_padding_mask=None, mask_mode: Optional[st
         q, k, v, causal=bool(layer.get("causal", False)), window=layer.get("window_size"),
         alibi_slopes=alibi_tensor(H) if scheme == "alibi" else None,
         mask_mode=mode, out_dtype=compute_dtype(), **masks)
-    return project(ctx.flatten(-2), layer, "o").float()
+    return project(ctx.flatten(-2), layer, "o", out_dtype=torch.float32)
 
 
 def cross_attention(layer: dict, x, memory, memory_key_padding_mask=None):
@@ -244,4 +278,4 @@ def cross_attention(layer: dict, x, memory, memory_key_padding_mask=None):
         mode = "additive"
     ctx = kernels.attention_prefill(q, k, v, causal=False, mask_mode=mode,
                                     out_dtype=compute_dtype(), **masks)
-    return project(ctx.flatten(-2), layer, "o").float()
+    return project(ctx.flatten(-2), layer, "o", out_dtype=torch.float32)

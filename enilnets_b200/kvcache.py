@@ -167,12 +167,16 @@ def attention_step(layer: Dict[str, Any], x, idx: int, cache: KVCache, B: int, S
     Hkv = layer.get("num_kv_heads") or H
     scheme = layer.get("positional_scheme", "absolute")
     window = layer.get("window_size")
-    qkv = attention.project(x, layer, "qkv")
+    if scheme == "rope":
+        # Rotated at absolute positions in the projection's epilogue; the
+        # cache stores rotated K.
+        qkv, rotated = attention.project(x, layer, "qkv", rope_pos0=pos)
+    else:
+        qkv, rotated = attention.project(x, layer, "qkv"), True
     q = attention.split_heads(qkv, H, D, 0)
     k_new = attention.split_heads(qkv, Hkv, D, H * D)
     v_new = attention.split_heads(qkv, Hkv, D, H * D + Hkv * D)
-    if scheme == "rope":
-        # Rotate at absolute positions; the cache stores rotated K.
+    if not rotated:
         attention.apply_rope(q, pos)
         attention.apply_rope(k_new, pos)
     if layer.get("attention_kernel", "softmax") in attention.LINEAR_KERNELS:
@@ -214,7 +218,7 @@ def attention_step(layer: Dict[str, Any], x, idx: int, cache: KVCache, B: int, S
         ctx = kernels.attention_prefill(q, kv_k, kv_v, causal=True, window=window,
                                         alibi_slopes=slopes, q_pos0=pos,
                                         k_pos0=lc.base + lc.begin, out_dtype=qkv.dtype)
-    return attention.project(ctx.flatten(-2), layer, "o").float()
+    return attention.project(ctx.flatten(-2), layer, "o", out_dtype=torch.float32)
 
 
 def _linear_step(layer: Dict[str, Any], q, k_new, v_new, idx: int, cache: KVCache):
@@ -244,7 +248,7 @@ def _linear_step(layer: Dict[str, Any], q, k_new, v_new, idx: int, cache: KVCach
         qp, kp, v_new, causal=True, state=None if prev is None else (prev[0], prev[1]),
         state_scale=scale, return_state=True, out_dtype=q.dtype)
     cache.linear[idx] = (kv, ksum, stab)
-    return attention.project(ctx.flatten(-2), layer, "o").float()
+    return attention.project(ctx.flatten(-2), layer, "o", out_dtype=torch.float32)
 
 
 def cached_forward_step_device(model: Any, token_ids, cache: KVCache,

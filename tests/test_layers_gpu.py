@@ -46,14 +46,30 @@ def _err(a, b):
 
 
 def test_mha_layers_forward(cuda, golden_dir, float64, precision):
+    """fp32: against the reference's own outputs at 1e-3. bf16: against the
+    float64 oracle (pinned to the reference, test_oracle_golden.py) run on the
+    bf16-rounded input and weights, so that 2e-2 measures the device path
+    rather than the quantisation of its inputs, and against the reference's
+    outputs at the model-level 5e-2."""
+    from oracle import attention_ref as ref
     data, meta = _golden(golden_dir)
     for i, cfg in enumerate(meta["mha"]):
         enl.set_seed(1100 + i)
         m = enl.AttentionNet()
         m.add_multihead_attention(**cfg)
         x = np.random.RandomState(1200 + i).standard_normal((2, 40, cfg["embed_dim"]))
-        err = _err(m.Forward(x, training=False), data[f"mha{i}_y"])
-        assert err <= TOL[precision], f"{cfg}: {err:.3e}"
+        y = m.Forward(x, training=False)
+        err = _err(y, data[f"mha{i}_y"])
+        if precision == "fp32":
+            assert err <= TOL["fp32"], f"{cfg}: {err:.3e}"
+            continue
+        assert err <= TOL_MODEL["bf16"], f"{cfg}: {err:.3e} against the reference"
+        layer = dict(m.layers[0])
+        for k in ("Wq", "Wk", "Wv", "Wo"):
+            layer[k] = ref.bf16_round(layer[k]).astype(np.float64)
+        y_ref = ref.mha_layer_ref(layer, ref.bf16_round(x).astype(np.float64))
+        err_q = _err(y, y_ref)
+        assert err_q <= TOL["bf16"], f"{cfg}: {err_q:.3e} against bf16-rounded inputs"
 
 
 def test_graph_padding_layers(cuda, golden_dir, float64, precision):
