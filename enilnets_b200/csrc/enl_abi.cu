@@ -76,6 +76,60 @@ int make_qkv_map(CUtensorMap* map, const void* base, int D, int S, int H, int B,
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// 3-D bf16 map (inner, rows, depth) with element strides row_ld and depth_ld,
+// 128-byte swizzled boxes of 64 x box_rows x 1.
+int make_3d_map(CUtensorMap* map, const void* base, int64_t inner, int64_t rows, int64_t depth,
+                int64_t row_ld, int64_t depth_ld, uint32_t box_rows, const char* name) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(ENL_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)rows, (cuuint64_t)depth};
+  cuuint64_t strides[2] = {(cuuint64_t)(row_ld * 2), (cuuint64_t)(depth_ld * 2)};
+  cuuint32_t box[3] = {64, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(ENL_ERR_INVALID, "cuTensorMapEncodeTiled(%s) failed with CUresult %d", name,
+                (int)r);
+  return ENL_OK;
+}
+
+// Sizes of the tensor-core linear-attention path (enl_linear_tc.cu): which
+// calls it takes (head_dim <= 128, at most 1024 features) and its workspace.
+struct LinTcPlan {
+  bool use;
+  int Dp, Dfp, Sp, n_chunks;
+  size_t off_qp, off_kp, off_kt, off_vt, off_u, off_st, total;
+};
+LinTcPlan lin_tc_plan(const enl_linear_args* a) {
+  LinTcPlan pl{};
+  pl.use = a->head_dim <= 128 && a->num_features <= 1024 && a->seq >= 1 && a->batch >= 1;
+  if (!pl.use) return pl;
+  const size_t B = a->batch, H = a->num_heads, Hk = a->num_kv_heads, S = a->seq;
+  const size_t Df = a->num_features;
+  pl.Dp = ((a->head_dim + 1 + 15) / 16) * 16;
+  pl.Dfp = (int)((Df + 7) / 8 * 8);
+  pl.Sp = (int)((S + 7) / 8 * 8);
+  pl.n_chunks = (int)((S + 127) / 128);
+  auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
+  size_t off = 0;
+  pl.off_qp = off;
+  off += al(2 * B * H * S * pl.Dfp * 2);
+  pl.off_kp = off;
+  off += a->causal ? al(2 * B * Hk * S * pl.Dfp * 2) : 0;
+  pl.off_kt = off;
+  off += al(2 * B * Hk * (size_t)pl.Dfp * pl.Sp * 2);
+  pl.off_vt = off;
+  off += al(2 * B * Hk * (size_t)pl.Dp * pl.Sp * 2);
+  pl.off_u = off;
+  off += al(B * Hk * (size_t)pl.n_chunks * Df * pl.Dp * 4);
+  pl.off_st = off;
+  off += al(2 * B * Hk * (size_t)pl.n_chunks * pl.Dp * pl.Dfp * 2);
+  pl.total = off;
+  return pl;
+}
+
 // 2-D map over a row-major (rows, cols) matrix with a 128-byte swizzled box of
 // box_cols x box_rows elements (box_cols * element size = 128 bytes).
 int make_2d_map(CUtensorMap* map, const void* base, bool fp32, int64_t cols, int64_t rows,
@@ -894,6 +948,8 @@ int enl_linear_max_features(void) { return enl::linear_attn_max_features(); }
 
 size_t enl_linear_workspace_bytes(const enl_linear_args* a) {
   if (!a || a->batch < 1 || a->num_heads < 1 || a->num_kv_heads < 1 || a->seq < 1) return 0;
+  const LinTcPlan pl = lin_tc_plan(a);
+  if (pl.use) return pl.total;
   return enl::linear_workspace_bytes(a->batch, a->num_heads, a->num_kv_heads, a->seq,
                                      a->num_features, a->head_dim, a->causal);
 }
@@ -993,6 +1049,71 @@ int enl_linear_attention(const enl_linear_args* a, void* stream) {
       return fail(ENL_ERR_INVALID, "enl_linear_attention: needs a workspace of %zu bytes "
                   "(enl_linear_workspace_bytes), got %zu", need,
                   a->workspace ? a->workspace_bytes : (size_t)0);
+  }
+  const LinTcPlan pl = lin_tc_plan(a);
+  if (pl.use) {
+    // Tensor-core path: bf16 hi/lo planes of phi(Q), phi(K) (both layouts)
+    // and V' in the workspace, chunk states, their scan, chunk outputs.
+    if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0)
+      return fail(ENL_ERR_INVALID, "enl_linear_attention: workspace must be 256-byte aligned");
+    uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
+    uint16_t* qp = reinterpret_cast<uint16_t*>(ws + pl.off_qp);
+    uint16_t* kp = reinterpret_cast<uint16_t*>(ws + pl.off_kp);
+    uint16_t* kt = reinterpret_cast<uint16_t*>(ws + pl.off_kt);
+    uint16_t* vt = reinterpret_cast<uint16_t*>(ws + pl.off_vt);
+    enl::LinTcParams t{};
+    t.B = a->batch;
+    t.H = a->num_heads;
+    t.Hkv = a->num_kv_heads;
+    t.S = a->seq;
+    t.Df = a->num_features;
+    t.D = a->head_dim;
+    t.Dp = pl.Dp;
+    t.Dfp = pl.Dfp;
+    t.Sp = pl.Sp;
+    t.n_chunks = pl.n_chunks;
+    t.causal = a->causal != 0;
+    t.tmem_cols = 128 + pl.Dp <= 256 ? 256 : 512;
+    t.u = reinterpret_cast<float*>(ws + pl.off_u);
+    t.st = reinterpret_cast<uint16_t*>(ws + pl.off_st);
+    t.kv_in = a->kv_in;
+    t.ks_in = a->ksum_in;
+    t.state_scale = a->state_scale;
+    t.kv_out = a->kv_out;
+    t.ks_out = a->ksum_out;
+    t.o = a->o;
+    t.o_sb = a->o_stride_b;
+    t.o_ss = a->o_stride_s;
+    t.o_sh = a->o_stride_h;
+    t.o_f32 = a->out_dtype == ENL_DTYPE_FP32;
+    t.eps = a->eps;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = enl::launch_lin_prep(a->phi_q, a->phi_k, a->v, a->v_stride_b, a->v_stride_s,
+                                         a->v_stride_h, a->v_dtype == ENL_DTYPE_FP32, t, qp, kp,
+                                         kt, vt, s);
+    if (e != cudaSuccess) return cuda_fail(e, "enl_linear_attention: prep launch");
+    const long long BHq = (long long)t.B * t.H, BHk = (long long)t.B * t.Hkv;
+    CUtensorMap tq, tk, tkt, tvt, tst;
+    int st;
+    if ((st = make_3d_map(&tq, qp, t.Df, t.S, 2 * BHq, t.Dfp, (int64_t)t.S * t.Dfp, 128, "phi_q")))
+      return st;
+    tk = tq;
+    if (t.causal &&
+        (st = make_3d_map(&tk, kp, t.Df, t.S, 2 * BHk, t.Dfp, (int64_t)t.S * t.Dfp, 128, "phi_k")))
+      return st;
+    if ((st = make_3d_map(&tkt, kt, t.S, t.Df, 2 * BHk, t.Sp, (int64_t)t.Dfp * t.Sp, 128,
+                          "phi_k^T")))
+      return st;
+    if ((st = make_3d_map(&tvt, vt, t.S, t.Dp, 2 * BHk, t.Sp, (int64_t)t.Dp * t.Sp, t.Dp, "v^T")))
+      return st;
+    if ((st = make_3d_map(&tst, t.st, t.Df, t.Dp, 2 * BHk * t.n_chunks, t.Dfp,
+                          (int64_t)t.Dp * t.Dfp, t.Dp, "state^T")))
+      return st;
+    e = enl::launch_lin_tc(tq, tk, tkt, tvt, tst, t, s);
+    if (e != cudaSuccess) return cuda_fail(e, "enl_linear_attention launch");
+    return ENL_OK;
+  }
+  if (need > 0) {
     // (n_seg, B, Hkv, Df, D) partial S_kv, then (n_seg, B, Hkv, Df) partial s_k
     const size_t per_seg = (size_t)a->batch * a->num_kv_heads * a->num_features;
     const size_t n_seg = need / sizeof(float) / (per_seg * ((size_t)a->head_dim + 1));

@@ -240,6 +240,31 @@ struct LinearParams {
   int n_seg, seg_len;  // set by launch_linear_attn
 };
 cudaError_t launch_linear_attn(const LinearParams& p, cudaStream_t stream);
+
+// K4 on tcgen05 (enl_linear_tc.cu): chunked linear attention over bf16 hi/lo
+// planes. Dp = V' columns (D + 1 rounded up to 16); Dfp, Sp: row strides of the
+// feature- and sequence-contiguous planes (multiples of 8).
+struct LinTcParams {
+  int B, H, Hkv, S, Df, D, Dp, Dfp, Sp, n_chunks, causal, tmem_cols;
+  float* u;      // (B * Hkv, n_chunks, Df, Dp) chunk states
+  uint16_t* st;  // [2][B * Hkv * n_chunks][Dp][Dfp] exclusive prefix states, transposed
+  const float* kv_in;
+  const float* ks_in;
+  const float* state_scale;
+  float* kv_out;
+  float* ks_out;
+  void* o;
+  long long o_sb, o_ss, o_sh;
+  int o_f32;
+  float eps;
+};
+cudaError_t launch_lin_prep(const float* phi_q, const float* phi_k, const void* v, long long v_sb,
+                            long long v_ss, long long v_sh, int v_f32, const LinTcParams& p,
+                            uint16_t* qp, uint16_t* kp, uint16_t* kt, uint16_t* vt,
+                            cudaStream_t stream);
+cudaError_t launch_lin_tc(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tkt,
+                          const CUtensorMap& tvt, const CUtensorMap& tst, const LinTcParams& p,
+                          cudaStream_t stream);
 size_t linear_workspace_bytes(int B, int H, int Hkv, int S, int Df, int D, int causal);
 int linear_attn_max_features();
 

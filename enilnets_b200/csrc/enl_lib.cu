@@ -8,6 +8,7 @@
 #include "enl_decode_noalloc.cu"
 #include "enl_selftest.cu"
 #include "enl_linear.cu"
+#include "enl_linear_tc.cu"
 #include "enl_sparse.cu"
 #include "enl_backward.cu"
 #include "enl_gemm.cu"
