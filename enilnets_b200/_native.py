@@ -99,6 +99,7 @@ class PhiArgs(Structure):
         ("in_dtype", c_int32), ("kernel", c_int32),
         ("omega", c_void_p), ("num_features", c_int32), ("global_stab", c_int32),
         ("stab_floor", c_void_p), ("stab", c_void_p), ("phi", c_void_p),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t),
     ]
 
 
@@ -167,6 +168,9 @@ SIGNATURES = {
     "enl_decode_workspace_bytes": ([c_int32, c_int32, c_int32, c_int32], c_size_t),
     "enl_lse_merge": ([c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p,
                        c_int64, c_int64, c_int32, c_void_p, c_void_p], c_int32),
+    "enl_lse_merge_strided": ([c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32, c_int32,
+                               c_int32, c_void_p, c_int64, c_int64, c_int32, c_void_p, c_void_p],
+                              c_int32),
     "enl_kv_append": ([c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64,
                        c_int64, c_int32, c_int32, c_int32, c_int32, c_int32, c_int64, c_int64,
                        c_void_p], c_int32),
@@ -177,6 +181,7 @@ SIGNATURES = {
                         c_int32, c_int32, c_void_p, c_void_p, c_int64, c_int64, c_void_p],
                        c_int32),
     "enl_linear_feature_map": ([POINTER(PhiArgs), c_void_p], c_int32),
+    "enl_phi_workspace_bytes": ([POINTER(PhiArgs)], c_size_t),
     "enl_linear_attention": ([POINTER(LinearArgs), c_void_p], c_int32),
     "enl_linear_max_features": ([], c_int32),
     "enl_linear_workspace_bytes": ([POINTER(LinearArgs)], c_size_t),

@@ -100,7 +100,7 @@ int make_3d_map(CUtensorMap* map, const void* base, int64_t inner, int64_t rows,
 struct LinTcPlan {
   bool use;
   int Dp, Dfp, Sp, n_chunks;
-  size_t off_qp, off_kp, off_kt, off_vt, off_u, off_st, total;
+  size_t off_qp, off_kp, off_vt, off_u, off_st, total;
 };
 LinTcPlan lin_tc_plan(const enl_linear_args* a) {
   LinTcPlan pl{};
@@ -117,9 +117,7 @@ LinTcPlan lin_tc_plan(const enl_linear_args* a) {
   pl.off_qp = off;
   off += al(2 * B * H * S * pl.Dfp * 2);
   pl.off_kp = off;
-  off += a->causal ? al(2 * B * Hk * S * pl.Dfp * 2) : 0;
-  pl.off_kt = off;
-  off += al(2 * B * Hk * (size_t)pl.Dfp * pl.Sp * 2);
+  off += al(2 * B * Hk * S * pl.Dfp * 2);
   pl.off_vt = off;
   off += al(2 * B * Hk * (size_t)pl.Dp * pl.Sp * 2);
   pl.off_u = off;
@@ -864,6 +862,29 @@ int enl_lse_merge(const float* part_o, const float* part_lse, int32_t n_parts, i
   return ENL_OK;
 }
 
+int enl_lse_merge_strided(const float* part_o, int64_t part_o_stride, const float* part_lse,
+                          int64_t part_lse_stride, int32_t n_parts, int32_t batch,
+                          int32_t num_heads, int32_t head_dim, void* o, int64_t o_stride_b,
+                          int64_t o_stride_h, int32_t out_dtype, float* lse, void* stream) {
+  if (!part_o || !part_lse || !o)
+    return fail(ENL_ERR_INVALID, "enl_lse_merge_strided: part_o, part_lse and o must be non-NULL");
+  if (n_parts < 1 || batch < 1 || num_heads < 1 || head_dim < 1)
+    return fail(ENL_ERR_INVALID, "enl_lse_merge_strided: sizes must be >= 1");
+  const long long bhd = (long long)batch * num_heads * head_dim, bh = (long long)batch * num_heads;
+  if ((n_parts > 1 && (part_o_stride < bhd || part_lse_stride < bh)) || part_o_stride < 0 ||
+      part_lse_stride < 0)
+    return fail(ENL_ERR_INVALID, "enl_lse_merge_strided: part strides (%lld, %lld) overlap the "
+                "parts", (long long)part_o_stride, (long long)part_lse_stride);
+  if (out_dtype != ENL_DTYPE_BF16 && out_dtype != ENL_DTYPE_FP32)
+    return fail(ENL_ERR_INVALID, "enl_lse_merge_strided: out_dtype=%d", out_dtype);
+  cudaError_t e = launch_lse_merge(part_o, part_lse, n_parts, part_o_stride, part_lse_stride,
+                                   batch, num_heads, head_dim, head_dim, o, o_stride_b, o_stride_h,
+                                   out_dtype == ENL_DTYPE_FP32, lse,
+                                   reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "enl_lse_merge_strided launch");
+  return ENL_OK;
+}
+
 int enl_kv_append(void* cache, int64_t cache_stride_b, int64_t cache_stride_h,
                   int64_t cache_stride_s, const void* src, int64_t src_stride_b,
                   int64_t src_stride_t, int64_t src_stride_h, int32_t batch,
@@ -954,6 +975,17 @@ size_t enl_linear_workspace_bytes(const enl_linear_args* a) {
                                      a->num_features, a->head_dim, a->causal);
 }
 
+size_t enl_phi_workspace_bytes(const enl_phi_args* a) {
+  if (!a || a->kernel != ENL_PHI_PERFORMER || a->batch < 1 || a->seq < 1 || a->num_heads < 1 ||
+      !enl::perf_tc_supported(a->head_dim, a->num_features) || a->num_features < 1 ||
+      a->num_features % 4 != 0)
+    return 0;
+  const size_t Dhp = (a->head_dim + 7) / 8 * 8;
+  auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
+  return al(2 * (size_t)a->batch * a->num_heads * a->seq * Dhp * 2) +
+         al(2 * (size_t)a->num_features * Dhp * 2);
+}
+
 int enl_linear_feature_map(const enl_phi_args* a, void* stream) {
   if (!a || !a->x || !a->phi)
     return fail(ENL_ERR_INVALID, "enl_linear_feature_map: args, x and phi must be non-NULL");
@@ -991,6 +1023,62 @@ int enl_linear_feature_map(const enl_phi_args* a, void* stream) {
   p.stab_floor = a->stab_floor;
   p.stab = a->stab;
   p.phi = a->phi;
+  const size_t need = enl_phi_workspace_bytes(a);
+  if (need > 0) {
+    // Tensor-core Performer map: planes of x and omega, then the projections
+    // on tcgen05 with the stabilizer in the epilogue.
+    if (!a->workspace || a->workspace_bytes < need ||
+        (reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0)
+      return fail(ENL_ERR_INVALID, "enl_linear_feature_map: the performer map needs a 256-byte "
+                  "aligned workspace of %zu bytes (enl_phi_workspace_bytes)", need);
+    const int Dhp = (a->head_dim + 7) / 8 * 8;
+    const size_t xbytes = ((2 * (size_t)a->batch * a->num_heads * a->seq * Dhp * 2) + 255) &
+                          ~size_t(255);
+    enl::PerfTcParams t{};
+    t.B = a->batch;
+    t.S = a->seq;
+    t.H = a->num_heads;
+    t.Dh = a->head_dim;
+    t.Dhp = Dhp;
+    t.Df = a->num_features;
+    t.xp = reinterpret_cast<uint16_t*>(a->workspace);
+    uint16_t* wp = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(a->workspace) + xbytes);
+    t.stab = a->stab;
+    t.phi = a->phi;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = enl::launch_perf_prep(a->x, a->x_stride_b, a->x_stride_s, a->x_stride_h,
+                                          a->in_dtype == ENL_DTYPE_FP32, a->omega, t, wp, s);
+    if (e != cudaSuccess) return cuda_fail(e, "enl_linear_feature_map: prep launch");
+    CUtensorMap tx, tw;
+    const long long BH = (long long)t.B * t.H;
+    const int Dfn = (t.Df + 15) / 16 * 16;
+    int st;
+    if ((st = make_3d_map(&tx, t.xp, t.Dh, t.S, 2 * BH, Dhp, (int64_t)t.S * Dhp, 128, "x")))
+      return st;
+    if ((st = make_3d_map(&tw, wp, t.Dh, t.Df, 2, Dhp, (int64_t)t.Df * Dhp, Dfn, "omega")))
+      return st;
+    // phi (B * H, S, Df) fp32, stored in 32-feature x 32-row boxes.
+    CUtensorMap tphi;
+    {
+      EncodeTiledFn fn = encode_fn();
+      if (!fn) return fail(ENL_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+      if ((t.Df * 4) % 16 != 0 || (reinterpret_cast<uintptr_t>(a->phi) & 15u) != 0)
+        return fail(ENL_ERR_INVALID, "enl_linear_feature_map: phi must be 16-byte aligned with "
+                    "num_features a multiple of 4 for the tensor-core map");
+      cuuint64_t dims[3] = {(cuuint64_t)t.Df, (cuuint64_t)t.S, (cuuint64_t)BH};
+      cuuint64_t strides[2] = {(cuuint64_t)t.Df * 4, (cuuint64_t)t.S * t.Df * 4};
+      cuuint32_t box[3] = {32, 32, 1};
+      cuuint32_t estr[3] = {1, 1, 1};
+      CUresult r = fn(&tphi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, a->phi, dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (r != CUDA_SUCCESS)
+        return fail(ENL_ERR_INVALID, "cuTensorMapEncodeTiled(phi) failed with CUresult %d", (int)r);
+    }
+    e = enl::launch_perf_tc_maps(tx, tw, tphi, t, p.global_stab, a->stab_floor, s);
+    if (e != cudaSuccess) return cuda_fail(e, "enl_linear_feature_map launch");
+    return ENL_OK;
+  }
   cudaError_t e = enl::launch_phi(p, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "enl_linear_feature_map launch");
   return ENL_OK;
@@ -1059,7 +1147,6 @@ int enl_linear_attention(const enl_linear_args* a, void* stream) {
     uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
     uint16_t* qp = reinterpret_cast<uint16_t*>(ws + pl.off_qp);
     uint16_t* kp = reinterpret_cast<uint16_t*>(ws + pl.off_kp);
-    uint16_t* kt = reinterpret_cast<uint16_t*>(ws + pl.off_kt);
     uint16_t* vt = reinterpret_cast<uint16_t*>(ws + pl.off_vt);
     enl::LinTcParams t{};
     t.B = a->batch;
@@ -1090,26 +1177,21 @@ int enl_linear_attention(const enl_linear_args* a, void* stream) {
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     cudaError_t e = enl::launch_lin_prep(a->phi_q, a->phi_k, a->v, a->v_stride_b, a->v_stride_s,
                                          a->v_stride_h, a->v_dtype == ENL_DTYPE_FP32, t, qp, kp,
-                                         kt, vt, s);
+                                         vt, s);
     if (e != cudaSuccess) return cuda_fail(e, "enl_linear_attention: prep launch");
     const long long BHq = (long long)t.B * t.H, BHk = (long long)t.B * t.Hkv;
-    CUtensorMap tq, tk, tkt, tvt, tst;
+    CUtensorMap tq, tk, tvt, tst;
     int st;
     if ((st = make_3d_map(&tq, qp, t.Df, t.S, 2 * BHq, t.Dfp, (int64_t)t.S * t.Dfp, 128, "phi_q")))
       return st;
-    tk = tq;
-    if (t.causal &&
-        (st = make_3d_map(&tk, kp, t.Df, t.S, 2 * BHk, t.Dfp, (int64_t)t.S * t.Dfp, 128, "phi_k")))
-      return st;
-    if ((st = make_3d_map(&tkt, kt, t.S, t.Df, 2 * BHk, t.Sp, (int64_t)t.Dfp * t.Sp, 128,
-                          "phi_k^T")))
+    if ((st = make_3d_map(&tk, kp, t.Df, t.S, 2 * BHk, t.Dfp, (int64_t)t.S * t.Dfp, 128, "phi_k")))
       return st;
     if ((st = make_3d_map(&tvt, vt, t.S, t.Dp, 2 * BHk, t.Sp, (int64_t)t.Dp * t.Sp, t.Dp, "v^T")))
       return st;
     if ((st = make_3d_map(&tst, t.st, t.Df, t.Dp, 2 * BHk * t.n_chunks, t.Dfp,
                           (int64_t)t.Dp * t.Dfp, t.Dp, "state^T")))
       return st;
-    e = enl::launch_lin_tc(tq, tk, tkt, tvt, tst, t, s);
+    e = enl::launch_lin_tc(tq, tk, tvt, tst, t, s);
     if (e != cudaSuccess) return cuda_fail(e, "enl_linear_attention launch");
     return ENL_OK;
   }

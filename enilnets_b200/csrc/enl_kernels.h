@@ -246,7 +246,7 @@ cudaError_t launch_linear_attn(const LinearParams& p, cudaStream_t stream);
 // feature- and sequence-contiguous planes (multiples of 8).
 struct LinTcParams {
   int B, H, Hkv, S, Df, D, Dp, Dfp, Sp, n_chunks, causal, tmem_cols;
-  float* u;      // (B * Hkv, n_chunks, Df, Dp) chunk states
+  float* u;      // (B * Hkv, n_chunks, Dp, Df) chunk states, transposed
   uint16_t* st;  // [2][B * Hkv * n_chunks][Dp][Dfp] exclusive prefix states, transposed
   const float* kv_in;
   const float* ks_in;
@@ -258,13 +258,29 @@ struct LinTcParams {
   int o_f32;
   float eps;
 };
+// Performer feature map on tcgen05 (enl_linear_tc.cu), Df <= 256.
+struct PerfTcParams {
+  int B, S, H, Dh, Dhp, Df;
+  uint16_t* xp;      // [2][B * H][S][Dhp] bf16 planes of x
+  float* stab;       // (B * H): mode 0 atomic-max target (ordered ints), mode 2 input
+  float* phi;        // (B, H, S, Df) fp32 out
+};
+bool perf_tc_supported(int Dh, int Df);
+cudaError_t launch_perf_prep(const void* x, long long sb, long long ss, long long sh, int f32,
+                             const float* omega, const PerfTcParams& p, uint16_t* wp,
+                             cudaStream_t stream);
+cudaError_t launch_perf_tc(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tphi,
+                           const PerfTcParams& p, int mode, cudaStream_t stream);
+// Queries (global_stab 0): one pass with row stabilizers. Keys: the
+// stabilizer (floored by stab_floor) as a max pass, then the map.
+cudaError_t launch_perf_tc_maps(const CUtensorMap& tx, const CUtensorMap& tw,
+                                const CUtensorMap& tphi, const PerfTcParams& p, int global_stab,
+                                const float* stab_floor, cudaStream_t stream);
 cudaError_t launch_lin_prep(const float* phi_q, const float* phi_k, const void* v, long long v_sb,
                             long long v_ss, long long v_sh, int v_f32, const LinTcParams& p,
-                            uint16_t* qp, uint16_t* kp, uint16_t* kt, uint16_t* vt,
-                            cudaStream_t stream);
-cudaError_t launch_lin_tc(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tkt,
-                          const CUtensorMap& tvt, const CUtensorMap& tst, const LinTcParams& p,
-                          cudaStream_t stream);
+                            uint16_t* qp, uint16_t* kp, uint16_t* vt, cudaStream_t stream);
+cudaError_t launch_lin_tc(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tvt,
+                          const CUtensorMap& tst, const LinTcParams& p, cudaStream_t stream);
 size_t linear_workspace_bytes(int B, int H, int Hkv, int S, int Df, int D, int causal);
 int linear_attn_max_features();
 

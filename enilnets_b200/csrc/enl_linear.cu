@@ -41,7 +41,37 @@ __device__ __forceinline__ float load_elem(const void* base, long long idx, bool
              : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[idx]);
 }
 
-// phi = elu(x) + 1: one warp per (b, s, h) row, elementwise.
+// phi = elu(x) + 1, four features per thread: one 16-byte (fp32) or 8-byte
+// (bf16) load and one 16-byte store, in output order (b, h, s, d).
+__global__ void __launch_bounds__(256) phi_linear_vec_kernel(PhiParams p) {
+  const int q4 = p.Dh / 4;
+  const long long n = (long long)p.B * p.H * p.S * q4;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i % q4) * 4;
+    long long r = i / q4;
+    const int s = (int)(r % p.S);
+    r /= p.S;
+    const int h = (int)(r % p.H), b = (int)(r / p.H);
+    const long long xoff = b * p.sb + s * p.ss + h * p.sh + c;
+    float v[4];
+    if (p.in_f32) {
+      const float4 x = __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) +
+                                                             xoff));
+      v[0] = x.x, v[1] = x.y, v[2] = x.z, v[3] = x.w;
+    } else {
+      const uint2 x = __ldg(reinterpret_cast<const uint2*>(
+          reinterpret_cast<const __nv_bfloat16*>(p.x) + xoff));
+      v[0] = bf16lo_to_f32(x.x), v[1] = bf16hi_to_f32(x.x);
+      v[2] = bf16lo_to_f32(x.y), v[3] = bf16hi_to_f32(x.y);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = v[e] > 0.0f ? v[e] + 1.0f : expf(fminf(v[e], 0.0f));
+    *reinterpret_cast<float4*>(p.phi + i * 4) = make_float4(v[0], v[1], v[2], v[3]);
+  }
+}
+
+// phi = elu(x) + 1: one warp per (b, s, h) row, elementwise (any alignment).
 __global__ void __launch_bounds__(256) phi_linear_kernel(PhiParams p) {
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const long long rows = (long long)p.B * p.S * p.H;
@@ -226,8 +256,17 @@ int perf_max_head_dim() { return kPerfMaxHeadDim; }
 cudaError_t launch_phi(const PhiParams& p, cudaStream_t stream) {
   const long long rows = (long long)p.B * p.S * p.H;
   if (p.kernel == 0) {
-    if (rows > 0)
+    const int esz = p.in_f32 ? 4 : 2;
+    const bool vec = p.Dh % 4 == 0 &&
+                     (reinterpret_cast<uintptr_t>(p.x) % (4 * esz)) == 0 &&
+                     ((p.sb | p.ss | p.sh) % 4) == 0 &&
+                     (reinterpret_cast<uintptr_t>(p.phi) % 16) == 0;
+    if (rows > 0 && vec) {
+      const long long n = rows * (p.Dh / 4);
+      phi_linear_vec_kernel<<<(int)min((n + 255) / 256, 148ll * 16), 256, 0, stream>>>(p);
+    } else if (rows > 0) {
       phi_linear_kernel<<<(int)min((rows + 7) / 8, 148ll * 16), 256, 0, stream>>>(p);
+    }
     return cudaGetLastError();
   }
   const int smem = perf_smem_floats(p.Dh) * (int)sizeof(float);

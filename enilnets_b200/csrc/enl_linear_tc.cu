@@ -6,7 +6,7 @@
 //   out_i = sum_{j <= i} (phi(q_i).phi(k_j)) v_j / (sum_{j <= i} phi(q_i).phi(k_j) + eps).
 // Appending a ones column to V (V' = [V | 1 | 0 ...], Dp columns) makes the
 // denominator column D of the same product. Over 128-row chunks c:
-//   U_c     = phi(K_c)^T V'_c                     (Df x Dp)  [lin_state_chunk]
+//   U_c     = phi(K_c)^T V'_c  (stored transposed, Dp x Df) [lin_state_chunk]
 //   S_{c-1} = S_in + sum_{c' < c} U_c'            (exclusive) [lin_scan_chunks]
 //   O'_c    = (phi(Q_c) phi(K_c)^T o mask) V'_c + phi(Q_c) S_{c-1}   [lin_out_chunk]
 //   out     = O'_c[:, :D] / (O'_c[:, D] + eps)
@@ -17,8 +17,8 @@
 // Every operand is staged K-major as bf16 planes hi = bf16(x), lo = bf16(x - hi)
 // and every product is hi*hi + hi*lo + lo*hi on kind::f16 MMAs with fp32
 // accumulation (about 2^-16 relative error, inside the fp32 bar). A prep pass
-// writes the planes: phi(Q) and phi(K) row-major (rows x features), phi(K)
-// and V' transposed (features / columns x rows), S^T by the scan.
+// writes the planes: phi(Q) and phi(K) row-major (rows x features), V'
+// transposed (columns x rows); the scan writes S^T.
 #include <climits>
 
 #include "enl_common.cuh"
@@ -36,6 +36,15 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* smem_src, int c0,
+                                             int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
 
@@ -69,8 +78,25 @@ __device__ __forceinline__ void split2(float x, uint16_t& hi, uint16_t& lo) {
 // Row-major planes: src (R, Df) fp32 -> dst[plane][R][Dfp] bf16.
 __global__ void lin_prep_rows(const float* __restrict__ src, long long R, int Df, int Dfp,
                               uint16_t* __restrict__ dst) {
-  const long long n = R * Df;
   const long long plane = R * Dfp;
+  if ((Df & 3) == 0) {
+    // Four features per thread: one 16-byte load, two 8-byte stores.
+    const int q4 = Df / 4;
+    const long long n = R * q4;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+      const long long r = i / q4;
+      const int f = (int)(i - r * q4) * 4;
+      const float4 x = __ldg(reinterpret_cast<const float4*>(src + r * Df + f));
+      const uint32_t h01 = pack_bf16x2(x.x, x.y), h23 = pack_bf16x2(x.z, x.w);
+      const uint32_t l01 = pack_bf16x2(x.x - bf16lo_to_f32(h01), x.y - bf16hi_to_f32(h01));
+      const uint32_t l23 = pack_bf16x2(x.z - bf16lo_to_f32(h23), x.w - bf16hi_to_f32(h23));
+      *reinterpret_cast<uint2*>(dst + r * Dfp + f) = make_uint2(h01, h23);
+      *reinterpret_cast<uint2*>(dst + plane + r * Dfp + f) = make_uint2(l01, l23);
+    }
+    return;
+  }
+  const long long n = R * Df;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
        i += (long long)gridDim.x * blockDim.x) {
     const long long r = i / Df;
@@ -79,32 +105,6 @@ __global__ void lin_prep_rows(const float* __restrict__ src, long long R, int Df
     split2(src[i], hi, lo);
     dst[r * Dfp + f] = hi;
     dst[plane + r * Dfp + f] = lo;
-  }
-}
-
-// Transposed planes of phi(K): src (BH, S, Df) -> dst[plane][BH][Dfp][Sp],
-// through 32 x 32 shared-memory tiles.
-__global__ void lin_prep_kt(const float* __restrict__ src, int S, int Df, int Sp, int Dfp,
-                            long long BH, uint16_t* __restrict__ dst) {
-  __shared__ float tile[32][33];
-  const long long bh = blockIdx.z;
-  const int s0 = blockIdx.x * 32, f0 = blockIdx.y * 32;
-  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
-  for (int r = ty; r < 32; r += 8) {
-    const int s = s0 + r, f = f0 + tx;
-    tile[r][tx] = (s < S && f < Df) ? src[(bh * S + s) * Df + f] : 0.0f;
-  }
-  __syncthreads();
-  const long long plane = BH * Dfp * Sp;
-  for (int r = ty; r < 32; r += 8) {
-    const int f = f0 + r, s = s0 + tx;
-    if (f < Df && s < Sp) {
-      uint16_t hi, lo;
-      split2(tile[tx][r], hi, lo);
-      const long long o = (bh * Dfp + f) * Sp + s;
-      dst[o] = hi;
-      dst[plane + o] = lo;
-    }
   }
 }
 
@@ -170,8 +170,10 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t addr, int n, float (&v)[kM
 
 // ---------------------------------------------------- A: chunk states
 // CTA (bh * n_chunks + c, m-tile): U[bh][c][f][d] for f in [128 mt, 128 mt + 128).
-// Operands: A = phi(K)^T rows f, chunk keys (two 64-key atoms per plane);
-// B = V'^T rows d, chunk keys. M = 128, N = Dp, K = 128 keys.
+// Operands: A = phi(K)^T, M = features, K = the chunk's keys, read from the
+// row-major phi(K) planes as an MN-major operand (two 64-feature atoms of 128
+// keys per plane, 16 KB apart); B = V'^T rows d, chunk keys (K-major).
+// M = 128, N = Dp, K = 128 keys.
 struct StateSmem {
   __host__ __device__ static int a_bytes() { return 2 * 2 * 128 * 128; }  // [plane][atom] 128 x 128 B
   __host__ __device__ static int b_bytes(int Dp) { return 2 * 2 * Dp * 128; }
@@ -179,7 +181,7 @@ struct StateSmem {
 };
 
 __global__ void __launch_bounds__(kThreads, 1)
-    lin_state_chunk(const __grid_constant__ CUtensorMap tm_kt,
+    lin_state_chunk(const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_vt, LinTcParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -217,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive_expect_tx(bar_full, 2 * 2 * (a_atom + b_atom));
       for (int pl = 0; pl < 2; ++pl)
         for (int a = 0; a < 2; ++a) {
-          tma_load_3d(sa + (pl * 2 + a) * a_atom, &tm_kt, bar_full, s0 + 64 * a, f0,
+          tma_load_3d(sa + (pl * 2 + a) * a_atom, &tm_k, bar_full, f0 + 64 * a, s0,
                       (int)(pl * BH + bh));
           tma_load_3d(sb + (pl * 2 + a) * b_atom, &tm_vt, bar_full, s0 + 64 * a, 0,
                       (int)(pl * BH + bh));
@@ -228,12 +230,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = warp_wait(bar_full, 0, abort_flag, 70);
     if (ok) {
       tc_fence_after();
-      const uint32_t idesc = idesc_bf16_f32(128, Dp, false);
-      const uint32_t a_lo = desc_lo(smem_u32(sa), 16), b_lo = desc_lo(smem_u32(sb), 16);
+      // A MN-major (bit 15 of the instruction descriptor): its 64-feature
+      // atoms lie a_atom bytes apart (leading byte offset), 16 keys are 2 KB.
+      const uint32_t idesc = idesc_bf16_f32(128, Dp, false) | (1u << 15);
+      const uint32_t a_lo = desc_lo(smem_u32(sa), a_atom), b_lo = desc_lo(smem_u32(sb), 16);
       const uint32_t a_pl = (2 * a_atom) >> 4, b_pl = (2 * b_atom) >> 4;
 #pragma unroll 1
       for (int kk = 0; kk < kC / 16; ++kk) {
-        const uint32_t ao = (kk / 4) * (a_atom >> 4) + (kk % 4) * 2;
+        const uint32_t ao = kk * (2048 >> 4);
         const uint32_t bo = (kk / 4) * (b_atom >> 4) + (kk % 4) * 2;
         const uint32_t acc = kk > 0 ? 1u : 0u;
         // hi*hi, hi*lo, lo*hi
@@ -249,18 +253,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool ok = warp_wait(bar_done, 0, abort_flag, 71);
     if (ok) {
       tc_fence_after();
+      // U^T[bh][c][d][f]: for each column d the warp's 32 lanes (consecutive
+      // features) store 128 contiguous bytes.
       const int f = f0 + 32 * q + lane;
-      float* urow = p.u + (((long long)bh * p.n_chunks + c) * p.Df + f) * Dp;
+      float* ut = p.u + ((long long)bh * p.n_chunks + c) * Dp * p.Df + f;
       const uint32_t addr = tmem + ((uint32_t)(32 * q) << 16);
       for (int c0 = 0; c0 < Dp; c0 += 16) {
         uint32_t r[16];
         ENL_TMEM_LD16(addr + c0, r);
         if (f < p.Df) {
 #pragma unroll
-          for (int i = 0; i < 16; i += 4)
-            *reinterpret_cast<float4*>(urow + c0 + i) =
-                make_float4(__uint_as_float(r[i]), __uint_as_float(r[i + 1]),
-                            __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+          for (int i = 0; i < 16; ++i) ut[(long long)(c0 + i) * p.Df] = __uint_as_float(r[i]);
         }
       }
     }
@@ -274,60 +277,53 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------ B: chunk scan
-// Per (b, kv head) and 32 x 32 tile of (feature, column): running sums over
-// the chunks, written before each chunk's own sum is added (exclusive) as
-// S^T planes st[plane][bh * n_chunks + c][d][f], starting from the carried
-// state (times its scale). Non-causal calls write only the total, at c = 0.
-// The total also goes to kv_out (d < D) / ks_out (d == D).
+// One thread per (b * kv head, column d, feature f), f fastest: the running
+// sum over the chunks of U^T, written before each chunk's own sum is added
+// (exclusive) as S^T planes st[plane][bh * n_chunks + c][d][f], starting
+// from the carried state (times its scale). Non-causal calls write only the
+// total, at c = 0. The total also goes to kv_out (d < D) / ks_out (d == D).
+// Chunk sums are loaded four chunks at a time so their loads overlap.
 __global__ void __launch_bounds__(256) lin_scan_chunks(LinTcParams p) {
-  __shared__ float tile[32][33];
-  const int bh = blockIdx.z;
-  const int f0 = blockIdx.y * 32, d0 = blockIdx.x * 32;
-  const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;  // 32 x 8
   const int Dp = p.Dp, Df = p.Df, D = p.D;
-  const float scale = p.state_scale ? p.state_scale[bh] : 1.0f;
-  // Thread (tx, ty) accumulates (f0 + ty + 8 j, d0 + tx), j < 4.
-  float run[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int f = f0 + ty + 8 * j, d = d0 + tx;
-    float x = 0.0f;
-    if (f < Df && d < D && p.kv_in) x = p.kv_in[((long long)bh * Df + f) * D + d] * scale;
-    if (f < Df && d == D && p.ks_in) x = p.ks_in[(long long)bh * Df + f] * scale;
-    run[j] = x;
-  }
+  const long long per_bh = (long long)Dp * Df;
+  const long long n = (long long)p.B * p.Hkv * per_bh;
   const long long plane = (long long)p.B * p.Hkv * p.n_chunks * Dp * p.Dfp;
-  auto emit = [&](int c) {
-    __syncthreads();  // previous readers of the tile are done
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long bh = i / per_bh;
+    const int e = (int)(i - bh * per_bh);
+    const int d = e / Df, f = e - d * Df;
+    const float scale = p.state_scale ? p.state_scale[bh] : 1.0f;
+    float run = 0.0f;
+    if (d < D && p.kv_in) run = p.kv_in[(bh * Df + f) * D + d] * scale;
+    if (d == D && p.ks_in) run = p.ks_in[bh * Df + f] * scale;
+    const float* u = p.u + bh * p.n_chunks * per_bh + e;
+    uint16_t* st = p.st + (bh * p.n_chunks * Dp + d) * p.Dfp + f;
+    const long long st_chunk = (long long)Dp * p.Dfp;
+    for (int cb = 0; cb < p.n_chunks; cb += 4) {
+      float x[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) tile[tx][ty + 8 * j] = run[j];  // tile[d][f]
-    __syncthreads();
+      for (int j = 0; j < 4; ++j) x[j] = cb + j < p.n_chunks ? u[(cb + j) * per_bh] : 0.0f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int d = d0 + ty + 8 * j, f = f0 + tx;
-      if (d < Dp && f < Df) {
-        uint16_t hi, lo;
-        split2(tile[ty + 8 * j][tx], hi, lo);
-        const long long o = (((long long)bh * p.n_chunks + c) * Dp + d) * p.Dfp + f;
-        p.st[o] = hi;
-        p.st[plane + o] = lo;
+      for (int j = 0; j < 4; ++j) {
+        if (cb + j >= p.n_chunks) break;
+        if (p.causal) {
+          uint16_t hi, lo;
+          split2(run, hi, lo);
+          st[(cb + j) * st_chunk] = hi;
+          st[plane + (cb + j) * st_chunk] = lo;
+        }
+        run += x[j];
       }
     }
-  };
-  for (int c = 0; c < p.n_chunks; ++c) {
-    if (p.causal) emit(c);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int f = f0 + ty + 8 * j, d = d0 + tx;
-      if (f < Df && d < Dp) run[j] += p.u[(((long long)bh * p.n_chunks + c) * Df + f) * Dp + d];
+    if (!p.causal) {
+      uint16_t hi, lo;
+      split2(run, hi, lo);
+      st[0] = hi;
+      st[plane] = lo;
     }
-  }
-  if (!p.causal) emit(0);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int f = f0 + ty + 8 * j, d = d0 + tx;
-    if (f < Df && d < D && p.kv_out) p.kv_out[((long long)bh * Df + f) * D + d] = run[j];
-    if (f < Df && d == D && p.ks_out) p.ks_out[(long long)bh * Df + f] = run[j];
+    if (d < D && p.kv_out) p.kv_out[(bh * Df + f) * D + d] = run;
+    if (d == D && p.ks_out) p.ks_out[bh * Df + f] = run;
   }
 }
 
@@ -348,7 +344,7 @@ struct OutSmem {
   __host__ __device__ static int total(int Dp) { return stage_bytes(Dp) + 128 + 1024; }
 };
 
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 2)
     lin_out_chunk(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_st,
                   const __grid_constant__ CUtensorMap tm_vt, LinTcParams p) {
@@ -509,24 +505,49 @@ __global__ void __launch_bounds__(kThreads)
     if (ok) ok = warp_wait(bar_o, 0, abort_flag, 87);
     if (ok) {
       tc_fence_after();
-      float v[160];
-      tmem_ld_cols<160>(t_o + lane_off, Dp, v);
+      // The denominator (column D) first, then the D output columns 16 at a time.
+      float den = 0.0f;
+      {
+        uint32_t r[16];
+        ENL_TMEM_LD16(t_o + lane_off + (uint32_t)(p.D & ~15), r);
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (i == (p.D & 15)) den = __uint_as_float(r[i]);
+      }
+      const float inv = 1.0f / (den + p.eps);
       const int s = s0 + row;
-      if (s < p.S) {
-        float den = 0.0f;
+      const long long off = (long long)b * p.o_sb + (long long)s * p.o_ss + (long long)h * p.o_sh;
+      const bool vec = p.o_f32 ? ((p.o_sh | p.o_ss | p.o_sb) & 3) == 0 &&
+                                     (reinterpret_cast<uintptr_t>(p.o) & 15) == 0
+                               : ((p.o_sh | p.o_ss | p.o_sb) & 7) == 0 &&
+                                     (reinterpret_cast<uintptr_t>(p.o) & 15) == 0;
+      for (int c0 = 0; c0 < p.D; c0 += 16) {
+        uint32_t r[16];
+        ENL_TMEM_LD16(t_o + lane_off + c0, r);
+        if (s >= p.S) continue;
+        float y[16];
 #pragma unroll
-        for (int i = 0; i < 160; ++i)
-          if (i == p.D) den = v[i];
-        const float inv = 1.0f / (den + p.eps);
-        const long long off = (long long)b * p.o_sb + (long long)s * p.o_ss + (long long)h * p.o_sh;
+        for (int i = 0; i < 16; ++i) y[i] = __uint_as_float(r[i]) * inv;
+        const int n = min(16, p.D - c0);
+        if (p.o_f32) {
+          float* dst = reinterpret_cast<float*>(p.o) + off + c0;
+          if (vec && n == 16) {
 #pragma unroll
-        for (int i = 0; i < 160; ++i) {
-          if (i < p.D) {
-            const float y = v[i] * inv;
-            if (p.o_f32)
-              reinterpret_cast<float*>(p.o)[off + i] = y;
-            else
-              reinterpret_cast<__nv_bfloat16*>(p.o)[off + i] = __float2bfloat16(y);
+            for (int i = 0; i < 16; i += 4)
+              *reinterpret_cast<float4*>(dst + i) = make_float4(y[i], y[i + 1], y[i + 2], y[i + 3]);
+          } else {
+            for (int i = 0; i < n; ++i) dst[i] = y[i];
+          }
+        } else {
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.o) + off + c0;
+          if (vec && n == 16) {
+#pragma unroll
+            for (int i = 0; i < 16; i += 8)
+              *reinterpret_cast<uint4*>(dst + i) =
+                  make_uint4(pack_bf16x2(y[i], y[i + 1]), pack_bf16x2(y[i + 2], y[i + 3]),
+                             pack_bf16x2(y[i + 4], y[i + 5]), pack_bf16x2(y[i + 6], y[i + 7]));
+          } else {
+            for (int i = 0; i < n; ++i) dst[i] = __float2bfloat16(y[i]);
           }
         }
       }
@@ -543,23 +564,333 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// ------------------------------------------- Performer feature map (tcgen05)
+// phi(x) = exp(x'.w - |x'|^2 / 2 - stab) / sqrt(Df), x' = x / Dh^(1/4)
+// (nn/attention_kernels.py:38-74), for Df <= 256: one CTA per (b * H + h,
+// 128-row block). The projections x.w run as split-bf16 MMAs (M = 128 rows,
+// N = Df, K = Dh in 64-wide steps through a two-stage ring) into tensor
+// memory; the epilogue threads (one row each) scale by Dh^(-1/4) and apply the
+// stabilizer. kMode 0: the tile's maximum into stab[b * H + h] (ordered-int
+// atomic max); 1: each row's own maximum (queries); 2: stab[b * H + h] (keys).
+// Operands: xp[plane][B * H][S][Dhp] (row planes of the head view), wp[plane][Df][Dhp].
+struct PerfSmem {
+  __host__ __device__ static int stage_bytes() { return 2 * 128 * 128 + 2 * 256 * 128; }
+  // Head dims up to 64 are one K step: one stage, so that two CTAs fit per SM.
+  __host__ __device__ static int stages(int Dh) { return Dh > 64 ? 2 : 1; }
+  static constexpr int kStageOut = 4 * 32 * 128;  // one 32-row x 128-byte buffer per epilogue warp
+  __host__ __device__ static int total(int Dh) {
+    return stages(Dh) * stage_bytes() + kStageOut + 128 + 1024;
+  }
+};
+
+template <int kMode>
+__global__ void __launch_bounds__(kThreads)
+    phi_perf_tc(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                const __grid_constant__ CUtensorMap tm_phi, PerfTcParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  constexpr int kX = 128 * 128;  // one plane of a 64-wide K step of x
+  const int n_st = PerfSmem::stages(p.Dh);
+  uint8_t* out_stage = smem + n_st * PerfSmem::stage_bytes();
+  uint64_t* bars = reinterpret_cast<uint64_t*>(out_stage + PerfSmem::kStageOut);
+  uint64_t* bar_full = bars;       // [2]
+  uint64_t* bar_empty = bars + 2;  // [2]
+  uint64_t* bar_acc = bars + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int bh = blockIdx.y, s0 = blockIdx.x * 128;
+  const int n_k = (p.Dh + 63) / 64;
+  const long long BH = (long long)p.B * p.H;
+  const int Dfn = (p.Df + 15) / 16 * 16;  // MMA N
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar_full + i, 1);
+      mbar_init(bar_empty + i, 1);
+    }
+    mbar_init(bar_acc, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc<256>(tmem_slot);
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      bool ok = true;
+      for (int kb = 0; kb < n_k && ok; ++kb) {
+        const int st = kb % n_st;
+        if (kb >= n_st) ok = mbar_wait(bar_empty + st, ((kb - n_st) / n_st) & 1, abort_flag, 90);
+        if (!ok) break;
+        uint8_t* base = smem + st * PerfSmem::stage_bytes();
+        mbar_arrive_expect_tx(bar_full + st, 2 * kX + 2 * Dfn * 128);
+        for (int pl = 0; pl < 2; ++pl) {
+          tma_load_3d(base + pl * kX, &tm_x, bar_full + st, 64 * kb, s0, (int)(pl * BH + bh));
+          tma_load_3d(base + 2 * kX + pl * Dfn * 128, &tm_w, bar_full + st, 64 * kb, 0, pl);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    const uint32_t idesc = idesc_bf16_f32(128, Dfn, false);
+    bool ok = true;
+    for (int kb = 0; kb < n_k && ok; ++kb) {
+      const int st = kb % n_st;
+      ok = warp_wait(bar_full + st, (kb / n_st) & 1, abort_flag, 91);
+      if (!ok) break;
+      tc_fence_after();
+      uint8_t* base = smem + st * PerfSmem::stage_bytes();
+      const uint32_t x_lo = desc_lo(smem_u32(base), 16);
+      const uint32_t w_lo = desc_lo(smem_u32(base + 2 * kX), 16);
+      const uint32_t x_pl = kX >> 4, w_pl = (Dfn * 128) >> 4;
+#pragma unroll 1
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint32_t off = kk * 2;
+        const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+        umma_ss_elect_acc(tmem, x_lo + off, w_lo + off, kDescHiSw128, idesc, acc);
+        umma_ss_elect_acc(tmem, x_lo + off, w_lo + w_pl + off, kDescHiSw128, idesc, 1u);
+        umma_ss_elect_acc(tmem, x_lo + x_pl + off, w_lo + off, kDescHiSw128, idesc, 1u);
+      }
+      umma_commit_elect(bar_empty + st);
+    }
+    umma_commit_elect(bar_acc);
+  } else {
+    const int q = warp % 4, row = 32 * q + lane, s = s0 + row;
+    const uint32_t addr = tmem + ((uint32_t)(32 * q) << 16);
+    const bool ok = warp_wait(bar_acc, 0, abort_flag, 92);
+    if (ok) {
+      tc_fence_after();
+      const float inv4 = rsqrtf(sqrtf((float)p.Dh));  // Dh^(-1/4)
+      // |x'|^2 / 2 from the row's own planes (hi + lo recovers x to 2^-16).
+      float sq = 0.0f;
+      if (s < p.S && kMode != 0) {
+        const uint16_t* xh = p.xp + ((long long)bh * p.S + s) * p.Dhp;
+        const uint16_t* xl = xh + BH * p.S * p.Dhp;
+        for (int d = 0; d < p.Dh; ++d) {
+          const float x = (bf16_val(xh[d]) + bf16_val(xl[d])) * inv4;
+          sq = fmaf(x, x, sq);
+        }
+        sq *= 0.5f;
+      }
+      // The row maximum (mode 0 and 1): one pass over the accumulator.
+      float m = -INFINITY;
+      if (kMode != 2) {
+        for (int c0 = 0; c0 < Dfn; c0 += 16) {
+          uint32_t r[16];
+          ENL_TMEM_LD16(addr + c0, r);
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (c0 + i < p.Df) m = fmaxf(m, __uint_as_float(r[i]) * inv4);
+        }
+        if (s >= p.S) m = -INFINITY;
+      }
+      if (kMode == 0) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0 && m > -INFINITY) atomicMax(reinterpret_cast<int*>(p.stab) + bh, ord_enc(m));
+      } else {
+        // 32 features at a time: the warp stages its 32 rows x 128 bytes in
+        // the TMA store's swizzled layout and stores them with one bulk copy
+        // (rows past S and features past Df are clipped by the tensor map).
+        const float stab = kMode == 1 ? m : p.stab[bh];
+        const float norm = rsqrtf((float)p.Df);
+        uint8_t* buf = out_stage + (warp - 2) * 32 * 128;
+        const int row0 = s0 + 32 * q;
+        for (int c0 = 0; c0 < Dfn && row0 < p.S; c0 += 32) {
+          uint32_t r[32];
+          ENL_TMEM_LD16(addr + c0, r);
+          if (c0 + 16 < Dfn) {
+            ENL_TMEM_LD16(addr + c0 + 16, (r + 16));
+          }
+          float y[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            y[i] = expf(__uint_as_float(r[i]) * inv4 - sq - stab) * norm;
+          if (lane == 0) bulk_wait_read_all();  // the previous store has read the buffer
+          __syncwarp();
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<float4*>(buf + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+                make_float4(y[4 * u], y[4 * u + 1], y[4 * u + 2], y[4 * u + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&tm_phi, buf, c0, row0, bh);
+            bulk_commit_group();
+          }
+        }
+        if (lane == 0) bulk_wait_all();
+        __syncwarp();
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<256>(tmem);
+  }
+}
+
+// x[b, s, h, :] (strided, bf16 or fp32) -> planes [plane][B * H][S][Dhp],
+// four elements per thread (Dh % 4 == 0, 8- or 16-byte aligned rows).
+__global__ void perf_prep_x4(const void* __restrict__ x, long long sb, long long ss,
+                             long long sh, int f32, int B, int S, int H, int Dh, int Dhp,
+                             uint16_t* __restrict__ dst) {
+  const int q4 = Dh / 4;
+  const long long n = (long long)B * H * S * q4;
+  const long long plane = (long long)B * H * S * Dhp;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int d = (int)(i % q4) * 4;
+    long long r = i / q4;
+    const int s = (int)(r % S);
+    r /= S;
+    const int h = (int)(r % H), b = (int)(r / H);
+    const long long off = b * sb + (long long)s * ss + (long long)h * sh + d;
+    float v[4];
+    if (f32) {
+      const float4 t = __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + off));
+      v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
+    } else {
+      const uint2 t = __ldg(reinterpret_cast<const uint2*>(
+          reinterpret_cast<const __nv_bfloat16*>(x) + off));
+      v[0] = bf16lo_to_f32(t.x), v[1] = bf16hi_to_f32(t.x);
+      v[2] = bf16lo_to_f32(t.y), v[3] = bf16hi_to_f32(t.y);
+    }
+    const uint32_t h01 = pack_bf16x2(v[0], v[1]), h23 = pack_bf16x2(v[2], v[3]);
+    const uint32_t l01 = pack_bf16x2(v[0] - bf16lo_to_f32(h01), v[1] - bf16hi_to_f32(h01));
+    const uint32_t l23 = pack_bf16x2(v[2] - bf16lo_to_f32(h23), v[3] - bf16hi_to_f32(h23));
+    const long long o = (((long long)b * H + h) * S + s) * Dhp + d;
+    *reinterpret_cast<uint2*>(dst + o) = make_uint2(h01, h23);
+    *reinterpret_cast<uint2*>(dst + plane + o) = make_uint2(l01, l23);
+  }
+}
+
+// Any alignment: one element per thread.
+__global__ void perf_prep_x(const void* __restrict__ x, long long sb, long long ss, long long sh,
+                            int f32, int B, int S, int H, int Dh, int Dhp,
+                            uint16_t* __restrict__ dst) {
+  const long long n = (long long)B * H * S * Dh;
+  const long long plane = (long long)B * H * S * Dhp;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int d = (int)(i % Dh);
+    long long r = i / Dh;
+    const int s = (int)(r % S);
+    r /= S;
+    const int h = (int)(r % H), b = (int)(r / H);
+    const long long off = b * sb + (long long)s * ss + (long long)h * sh + d;
+    const float v = f32 ? reinterpret_cast<const float*>(x)[off]
+                        : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(x)[off]);
+    uint16_t hi, lo;
+    split2(v, hi, lo);
+    const long long o = (((long long)b * H + h) * S + s) * Dhp + d;
+    dst[o] = hi;
+    dst[plane + o] = lo;
+  }
+}
+
+// omega (Df, Dh) fp32 -> planes [plane][Df][Dhp].
+__global__ void perf_prep_w(const float* __restrict__ w, int Df, int Dh, int Dhp,
+                            uint16_t* __restrict__ dst) {
+  const int n = Df * Dh;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int f = i / Dh, d = i % Dh;
+    uint16_t hi, lo;
+    split2(w[i], hi, lo);
+    dst[(long long)f * Dhp + d] = hi;
+    dst[(long long)Df * Dhp + (long long)f * Dhp + d] = lo;
+  }
+}
+
 }  // namespace lintc
+
+bool perf_tc_supported(int Dh, int Df) { return Df <= 256 && Dh <= 256; }
+
+cudaError_t launch_perf_prep(const void* x, long long sb, long long ss, long long sh, int f32,
+                             const float* omega, const PerfTcParams& p, uint16_t* wp,
+                             cudaStream_t stream) {
+  using namespace lintc;
+  const long long n = (long long)p.B * p.H * p.S * p.Dh;
+  const bool vec = p.Dh % 4 == 0 && ((sb | ss | sh) % 4) == 0 &&
+                   (reinterpret_cast<uintptr_t>(x) % (f32 ? 16 : 8)) == 0;
+  if (n > 0 && vec)
+    perf_prep_x4<<<(int)std::min<long long>((n / 4 + 255) / 256, 148ll * 16), 256, 0, stream>>>(
+        x, sb, ss, sh, f32, p.B, p.S, p.H, p.Dh, p.Dhp, p.xp);
+  else if (n > 0)
+    perf_prep_x<<<(int)std::min<long long>((n + 255) / 256, 148ll * 16), 256, 0, stream>>>(
+        x, sb, ss, sh, f32, p.B, p.S, p.H, p.Dh, p.Dhp, p.xp);
+  const int nw = p.Df * p.Dh;
+  perf_prep_w<<<std::max(1, std::min((nw + 255) / 256, 1024)), 256, 0, stream>>>(
+      omega, p.Df, p.Dh, p.Dhp, wp);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_perf_tc(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tphi,
+                           const PerfTcParams& p, int mode, cudaStream_t stream) {
+  using namespace lintc;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    const cudaFuncAttribute a = cudaFuncAttributeMaxDynamicSharedMemorySize;
+    e = cudaFuncSetAttribute(phi_perf_tc<0>, a, PerfSmem::total(256));
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(phi_perf_tc<1>, a, PerfSmem::total(256));
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(phi_perf_tc<2>, a, PerfSmem::total(256));
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  if (p.B * p.H == 0 || p.S == 0) return cudaSuccess;
+  const dim3 grid((p.S + 127) / 128, p.B * p.H);
+  const int smem = PerfSmem::total(p.Dh);
+  switch (mode) {
+    case 0: phi_perf_tc<0><<<grid, kThreads, smem, stream>>>(tx, tw, tphi, p); break;
+    case 1: phi_perf_tc<1><<<grid, kThreads, smem, stream>>>(tx, tw, tphi, p); break;
+    default: phi_perf_tc<2><<<grid, kThreads, smem, stream>>>(tx, tw, tphi, p); break;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_perf_tc_maps(const CUtensorMap& tx, const CUtensorMap& tw,
+                                const CUtensorMap& tphi, const PerfTcParams& p, int global_stab,
+                                const float* stab_floor, cudaStream_t stream) {
+  if (!global_stab) return launch_perf_tc(tx, tw, tphi, p, 1, stream);
+  // The CUDA-core kernels' stabilizer helpers: ordered-int init from the
+  // floor, and the conversion back to floats after the atomic-max pass.
+  PhiParams q{};
+  q.B = p.B;
+  q.H = p.H;
+  q.stab = p.stab;
+  q.stab_floor = stab_floor;
+  const int nb = std::max(1, (p.B * p.H + 255) / 256);
+  phi_init_kernel<<<nb, 256, 0, stream>>>(q);
+  cudaError_t e = launch_perf_tc(tx, tw, tphi, p, 0, stream);
+  if (e != cudaSuccess) return e;
+  phi_decode_kernel<<<nb, 256, 0, stream>>>(q);
+  return launch_perf_tc(tx, tw, tphi, p, 2, stream);
+}
 
 cudaError_t launch_lin_prep(const float* phi_q, const float* phi_k, const void* v, long long v_sb,
                             long long v_ss, long long v_sh, int v_f32, const LinTcParams& p,
-                            uint16_t* qp, uint16_t* kp, uint16_t* kt, uint16_t* vt,
-                            cudaStream_t stream) {
+                            uint16_t* qp, uint16_t* kp, uint16_t* vt, cudaStream_t stream) {
   using namespace lintc;
   const long long BHq = (long long)p.B * p.H, BHk = (long long)p.B * p.Hkv;
   const long long rq = BHq * p.S, rk = BHk * p.S;
   auto blocks = [](long long n) { return (int)std::min<long long>((n + 255) / 256, 148ll * 16); };
   if (rq * p.Df > 0) lin_prep_rows<<<blocks(rq * p.Df), 256, 0, stream>>>(phi_q, rq, p.Df, p.Dfp, qp);
-  if (p.causal && rk * p.Df > 0)
-    lin_prep_rows<<<blocks(rk * p.Df), 256, 0, stream>>>(phi_k, rk, p.Df, p.Dfp, kp);
+  if (rk * p.Df > 0) lin_prep_rows<<<blocks(rk * p.Df), 256, 0, stream>>>(phi_k, rk, p.Df, p.Dfp, kp);
   const dim3 tb(32, 8);
   if (BHk > 0 && p.S > 0) {
-    const dim3 gk((p.Sp + 31) / 32, (p.Df + 31) / 32, (unsigned)BHk);
-    lin_prep_kt<<<gk, tb, 0, stream>>>(phi_k, p.S, p.Df, p.Sp, p.Dfp, BHk, kt);
     const dim3 gv((p.Sp + 31) / 32, (p.Dp + 31) / 32, (unsigned)BHk);
     lin_prep_vt<<<gv, tb, 0, stream>>>(v, v_sb, v_ss, v_sh, v_f32, p.Hkv, p.S, p.D, p.Dp, p.Sp,
                                       BHk, vt);
@@ -567,9 +898,8 @@ cudaError_t launch_lin_prep(const float* phi_q, const float* phi_k, const void* 
   return cudaGetLastError();
 }
 
-cudaError_t launch_lin_tc(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tkt,
-                          const CUtensorMap& tvt, const CUtensorMap& tst, const LinTcParams& p,
-                          cudaStream_t stream) {
+cudaError_t launch_lin_tc(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tvt,
+                          const CUtensorMap& tst, const LinTcParams& p, cudaStream_t stream) {
   using namespace lintc;
   static bool configured[64] = {};
   int dev = 0;
@@ -586,11 +916,11 @@ cudaError_t launch_lin_tc(const CUtensorMap& tq, const CUtensorMap& tk, const CU
   const long long BHk = (long long)p.B * p.Hkv, BHq = (long long)p.B * p.H;
   if (p.n_chunks > 0 && BHk > 0) {
     const dim3 ga((unsigned)(BHk * p.n_chunks), (p.Df + 127) / 128);
-    lin_state_chunk<<<ga, kThreads, StateSmem::total(p.Dp), stream>>>(tkt, tvt, p);
+    lin_state_chunk<<<ga, kThreads, StateSmem::total(p.Dp), stream>>>(tk, tvt, p);
   }
   if (BHk > 0) {
-    const dim3 gs((p.Dp + 31) / 32, (p.Df + 31) / 32, (unsigned)BHk);
-    lin_scan_chunks<<<gs, 256, 0, stream>>>(p);
+    const long long n = BHk * p.Dp * p.Df;
+    lin_scan_chunks<<<(int)std::min<long long>((n + 255) / 256, 148ll * 32), 256, 0, stream>>>(p);
   }
   if (p.n_chunks > 0 && BHq > 0) {
     const dim3 gc((unsigned)BHq, p.n_chunks);

@@ -381,7 +381,7 @@ def attention_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
                      out: Optional[torch.Tensor] = None,
                      out_dtype: torch.dtype = torch.bfloat16,
                      workspace: Optional[torch.Tensor] = None,
-                     return_lse: bool = False):
+                     return_lse: bool = False, lse_out: Optional[torch.Tensor] = None):
     """One-token decode via the K2 split-KV kernel.
 
     q: (B, H, D); k_cache/v_cache: (B, Hkv, capacity, D) with equal strides,
@@ -410,6 +410,11 @@ def attention_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     if tuple(out.shape) != (B, H, D) or out.dtype not in _DTYPES:
         raise ValueError(f"out must be ({B}, {H}, {D}) bf16/fp32")
     lse = torch.empty((B, H), device=q.device, dtype=torch.float32) if return_lse else None
+    if lse_out is not None:
+        _require_cuda("lse_out", lse_out, torch.float32, last_contiguous=False)
+        if tuple(lse_out.shape) != (B, H) or lse_out.stride() != (H, 1):
+            raise ValueError(f"lse_out must be a contiguous float32 ({B}, {H}) tensor")
+        lse = lse_out
     if alibi_slopes is not None:
         _require_cuda("alibi_slopes", alibi_slopes, torch.float32, last_contiguous=False)
     n_slots = max(1, slot_end - slot_begin)
@@ -435,27 +440,29 @@ def attention_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     a.workspace = _ptr(workspace)
     a.workspace_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
     nat.check(nat.load().enl_attn_decode(ctypes.byref(a), _stream()), "enl_attn_decode")
-    return (out, lse) if return_lse else out
+    return (out, lse) if (return_lse or lse_out is not None) else out
 
 
 def lse_merge(part_o: torch.Tensor, part_lse: torch.Tensor, *,
               out: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.bfloat16,
               return_lse: bool = False):
-    """Merge (n_parts, B, H, D) fp32 partials by their (n_parts, B, H) LSEs."""
+    """Merge (n_parts, B, H, D) fp32 partials by their (n_parts, B, H) LSEs.
+    Each part must be contiguous; the parts may sit any distance apart (a
+    gathered buffer of packed [out | lse] parts is merged in place)."""
     _require_cuda("part_o", part_o, torch.float32)
     _require_cuda("part_lse", part_lse, torch.float32, last_contiguous=False)
-    if not part_o.is_contiguous() or not part_lse.is_contiguous():
-        raise ValueError("partials must be contiguous")
     P, B, H, D = part_o.shape
     if tuple(part_lse.shape) != (P, B, H):
         raise ValueError("part_lse must be (n_parts, B, H)")
+    if part_o[0].stride() != (H * D, D, 1) or part_lse[0].stride() != (H, 1):
+        raise ValueError("each part of part_o / part_lse must be contiguous")
     if out is None:
         out = torch.empty((B, H, D), device=part_o.device, dtype=out_dtype)
     lse = torch.empty((B, H), device=part_o.device, dtype=torch.float32) if return_lse else None
-    nat.check(nat.load().enl_lse_merge(part_o.data_ptr(), part_lse.data_ptr(), P, B, H, D,
-                                       out.data_ptr(), out.stride(0), out.stride(1),
-                                       _DTYPES[out.dtype], _ptr(lse), _stream()),
-              "enl_lse_merge")
+    nat.check(nat.load().enl_lse_merge_strided(
+        part_o.data_ptr(), part_o.stride(0), part_lse.data_ptr(), part_lse.stride(0), P, B, H,
+        D, out.data_ptr(), out.stride(0), out.stride(1), _DTYPES[out.dtype], _ptr(lse),
+        _stream()), "enl_lse_merge_strided")
     return (out, lse) if return_lse else out
 
 
@@ -556,8 +563,13 @@ def linear_feature_map(x: torch.Tensor, kernel: str, omega: Optional[torch.Tenso
     a.stab_floor = _ptr(stab_floor) if stab is not None else None
     a.stab = _ptr(stab)
     a.phi = phi.data_ptr()
-    nat.check(nat.load().enl_linear_feature_map(ctypes.byref(a), _stream()),
-              "enl_linear_feature_map")
+    lib = nat.load()
+    need = int(lib.enl_phi_workspace_bytes(ctypes.byref(a)))
+    ws = None
+    if need > 0:
+        ws = torch.empty(need, dtype=torch.uint8, device=x.device)
+        a.workspace, a.workspace_bytes = ws.data_ptr(), need
+    nat.check(lib.enl_linear_feature_map(ctypes.byref(a), _stream()), "enl_linear_feature_map")
     return phi, stab
 
 

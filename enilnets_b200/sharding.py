@@ -152,11 +152,39 @@ class SequenceShardedDecode:
         self.group = group
         self._local = local
         self._merge = merge
+        self._bufs = {}  # (shape, device) -> (packed, gathered) for the CUDA path
+
+    def _cuda_step(self, q, k_cache, v_cache, out, out_dtype, **kw):
+        """The CUDA path: K2 writes its (out, lse) straight into one packed
+        fp32 buffer [out (B*H*D) | lse (B*H)], a single all_gather_into_tensor
+        moves it, and the merge reads the gathered parts in place."""
+        import torch
+        import torch.distributed as dist
+        from . import kernels
+        B, H, D = q.shape
+        world = dist.get_world_size(self.group)
+        key = (B, H, D, world, q.device)
+        if key not in self._bufs:
+            n = B * H * (D + 1)
+            self._bufs[key] = (torch.empty(n, dtype=torch.float32, device=q.device),
+                               torch.empty((world, n), dtype=torch.float32, device=q.device))
+        packed, gathered = self._bufs[key]
+        kernels.attention_decode(q, k_cache, v_cache, out=packed[:B * H * D].view(B, H, D),
+                                 lse_out=packed[B * H * D:].view(B, H), **kw)
+        dist.all_gather_into_tensor(gathered, packed, group=self.group)
+        part_o = gathered[:, :B * H * D].unflatten(1, (B, H, D))
+        part_lse = gathered[:, B * H * D:].unflatten(1, (B, H))
+        return kernels.lse_merge(part_o, part_lse, out=out, out_dtype=out_dtype or torch.bfloat16)
 
     def __call__(self, q, k_cache, v_cache, *, slot_begin: int, slot_end: int,
                  pos_slot0: int, q_pos: int, window=None, alibi_slopes=None, scale=None,
                  out=None, out_dtype=None):
         import torch
+        import torch.distributed as dist
+        if self._local is None and self._merge is None and q.is_cuda and dist.is_initialized():
+            return self._cuda_step(q, k_cache, v_cache, out, out_dtype, slot_begin=slot_begin,
+                                   slot_end=slot_end, pos_slot0=pos_slot0, q_pos=q_pos,
+                                   window=window, alibi_slopes=alibi_slopes, scale=scale)
         if self._local is None:
             from . import kernels
             o, lse = kernels.attention_decode(

@@ -168,6 +168,14 @@ int enl_lse_merge(const float* part_o, const float* part_lse, int32_t n_parts, i
                   int32_t num_heads, int32_t head_dim, void* o, int64_t o_stride_b,
                   int64_t o_stride_h, int32_t out_dtype, float* lse, void* stream);
 
+/* enl_lse_merge with the parts part_o_stride / part_lse_stride floats apart
+ * (each part's (batch, heads, head_dim) and (batch, heads) contiguous), so a
+ * gathered buffer of packed [out | lse] parts is merged in place. */
+int enl_lse_merge_strided(const float* part_o, int64_t part_o_stride, const float* part_lse,
+                          int64_t part_lse_stride, int32_t n_parts, int32_t batch,
+                          int32_t num_heads, int32_t head_dim, void* o, int64_t o_stride_b,
+                          int64_t o_stride_h, int32_t out_dtype, float* lse, void* stream);
+
 /* -------------------------------------------------------------- KV cache */
 /* cache[b, h, slot0 + t, :] = src[b, t, h, :] for t < n_new. Replaces the
  * whole-cache np.concatenate of nn/kvcache.py:156-162. Fails with
@@ -264,12 +272,21 @@ typedef struct enl_phi_args {
   float* stab;             /* global: receives the stabilizer per (b, h) */
   float* phi;              /* out (batch, num_heads, seq, Df) fp32, contiguous;
                               Df = head_dim (linear) or num_features */
+  void* workspace;         /* performer: >= enl_phi_workspace_bytes(), 256-byte aligned */
+  size_t workspace_bytes;
 } enl_phi_args;
+
+/* Workspace bytes enl_linear_feature_map needs: the bf16 hi/lo planes of x
+ * and omega for the tensor-core Performer map (num_features <= 256); 0
+ * otherwise. */
+size_t enl_phi_workspace_bytes(const enl_phi_args* args);
 
 /* phi(x) (nn/attention_kernels.py:58-74): elu(x) + 1, or
  * exp(w.x' - |x'|^2 / 2 - stab) / sqrt(num_features) with x' = x / head_dim^(1/4)
  * and stab the row max of w.x' (queries) or its max over every row of the
- * call and stab_floor (keys, nn/attention_kernels.py:38-55). */
+ * call and stab_floor (keys, nn/attention_kernels.py:38-55). Performer maps
+ * with up to 256 features run the projections w.x as split-bf16 tcgen05 MMAs
+ * (needs the workspace); larger ones on the CUDA cores. */
 int enl_linear_feature_map(const enl_phi_args* args, void* stream);
 
 typedef struct enl_linear_args {

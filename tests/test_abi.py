@@ -119,12 +119,13 @@ def test_prefill_workspace_bytes_is_host_only_arithmetic():
     assert lib.enl_prefill_workspace_bytes(ctypes.byref(a)) == planes(100, 8) + 2 * planes(300, 2)
 
 
-def test_linear_workspace_fills_whole_waves():
-    """Host-only arithmetic: the causal linear pass splits a sequence into the
-    segment count whose CTAs best fill whole waves (148 SMs x 2 CTAs), first
-    count reaching 95%, segments of at least 256 rows; one partial state per
-    segment (num_features x head_dim + num_features floats per batch and kv
-    head). Short or non-causal calls need no workspace."""
+def test_linear_workspace_sizes():
+    """Host-only arithmetic of enl_linear_workspace_bytes. Head dims up to 128
+    take the tensor-core path: bf16 hi/lo planes of phi(Q) and phi(K)
+    (row-major) and V' = [V | 1] transposed, the per-chunk
+    states (128-row chunks) and their exclusive scan, each 256-byte aligned.
+    Larger head dims take the CUDA-core pass, whose causal calls split into
+    the segment count that best fills whole waves (one partial state each)."""
     lib = _native.load()
 
     def ws(B, H, Hkv, S, Df, D, causal):
@@ -133,13 +134,26 @@ def test_linear_workspace_fills_whole_waves():
         a.num_features, a.head_dim, a.causal = Df, D, int(causal)
         return lib.enl_linear_workspace_bytes(ctypes.byref(a))
 
+    def al(x):
+        return (x + 255) // 256 * 256
+
+    def tensor_path(B, H, Hkv, S, Df, D, causal):
+        Dp, Dfp, Sp, nc = (D + 1 + 15) // 16 * 16, (Df + 7) // 8 * 8, (S + 7) // 8 * 8, \
+            (S + 127) // 128
+        return (al(2 * B * H * S * Dfp * 2) + al(2 * B * Hkv * S * Dfp * 2)
+                + al(2 * B * Hkv * Dp * Sp * 2)
+                + al(B * Hkv * nc * Df * Dp * 4) + al(2 * B * Hkv * nc * Dp * Dfp * 2))
+
+    for args in [(4, 16, 16, 4096, 64, 64, True), (4, 16, 16, 4096, 256, 64, True),
+                 (1, 2, 2, 1500, 64, 64, True), (4, 16, 16, 4096, 64, 64, False),
+                 (2, 4, 1, 37, 100, 72, True), (1, 1, 1, 1, 8, 8, False)]:
+        assert ws(*args) == tensor_path(*args), args
+
     def state(n, B, Hkv, Df, D):
         return n * B * Hkv * (Df * D + Df) * 4
 
-    # 128 CTAs per segment: 9 segments = 1152 CTAs, 97% of four waves of 296
-    assert ws(4, 16, 16, 4096, 64, 64, True) == state(9, 4, 16, 64, 64)
-    assert ws(4, 16, 16, 4096, 256, 64, True) == state(9, 4, 16, 256, 64)
-    # few CTAs: as many segments as 256-row segments allow
-    assert ws(1, 2, 2, 1500, 64, 64, True) == state(5, 1, 2, 64, 64)
-    assert ws(4, 16, 16, 4096, 64, 64, False) == 0
-    assert ws(1, 2, 2, 255, 64, 64, True) == 0
+    # head_dim 256 (CUDA-core pass): 512 CTAs per segment; 4 segments = 2048
+    # CTAs, 98.8% of seven waves of 296
+    assert ws(4, 16, 16, 4096, 64, 256, True) == state(4, 4, 16, 64, 256)
+    assert ws(4, 16, 16, 4096, 64, 256, False) == 0
+    assert ws(1, 2, 2, 255, 64, 256, True) == 0
