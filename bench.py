@@ -218,6 +218,25 @@ def timed(dist: Dist, clocks: ClockSampler, fn, steps: int) -> float:
     return dist.max(start.elapsed_time(end))
 
 
+def timed_graph(dist: Dist, clocks: ClockSampler, steps_fn, n_steps: int):
+    """Capture `steps_fn` (which issues n_steps decode steps) as one CUDA
+    graph and time one replay (max over ranks); returns ms per step. The
+    graph removes the host's per-launch cost from steps of a fraction of a
+    millisecond; the kernels it replays are the eager steps' kernels."""
+    import torch
+    g = torch.cuda.CUDAGraph()
+    torch.cuda.synchronize()
+    with torch.cuda.graph(g):
+        steps_fn()
+    torch.cuda.synchronize()
+    g.replay()  # warm replay
+    torch.cuda.synchronize()
+    ms = timed(dist, clocks, g.replay, 1) / n_steps
+    del g
+    torch.cuda.synchronize()
+    return ms
+
+
 # ------------------------------------------------------------- workloads
 def prefill_partition(world: int, rank: int, batch: int = 0):
     """This rank's share of the global cfg2 batch (8 sequences per GPU, valid
@@ -411,7 +430,16 @@ def bench_decode_cfg3(dist: Dist, clocks: ClockSampler, warmup: int, batch: int 
     state["t"] = 0
     torch.cuda.synchronize()
     _native.raise_on_device_error()
-    ms_all = timed(dist, clocks, step, T)
+    ms_eager = timed(dist, clocks, step, T)
+    state["t"] = 0
+
+    def all_steps():
+        for _ in range(T):
+            step()
+
+    ms_all = timed_graph(dist, clocks, all_steps, T) * T
+    state["t"] = 0
+    _native.raise_on_device_error()
     bytes_rank = 0
     for t in range(T):
         n = ctx + t + 1
@@ -425,10 +453,11 @@ def bench_decode_cfg3(dist: Dist, clocks: ClockSampler, warmup: int, batch: int 
     dec_bytes = 2 * B * H * D * 2 * (ctx + 1) + 2 * B * H * D * 2
     dec_gbs = dist.sum(dec_bytes) / (ms_dec / T * 1e-3) / 1e9
     return {"GB_s": gbs, "tokens_s": Btot * T / (ms_all * 1e-3), "ms_per_step": ms_all / T,
+            "eager_ms_per_step": ms_eager / T,
             "decode_kernel_GB_s": dec_gbs, "decode_kernel_ms": ms_dec / T,
             "splits": kernels.decode_auto_splits(B, H, ctx + 1),
             "config": f"B{Btot} H{H} D{D} ctx {ctx}+{T} steps, one K+V append each step, "
-                      f"{B} rows per GPU"}
+                      f"{B} rows per GPU; the {T} steps replayed from one CUDA graph"}
 
 
 def _cfg5_shard(dist: "Dist", rank: int, B: int, H: int, D: int, ctx: int, T: int):
@@ -485,11 +514,22 @@ def bench_longctx_cfg5(dist: Dist, clocks: ClockSampler, warmup: int):
     state["t"] = 0
     torch.cuda.synchronize()
     _native.raise_on_device_error()
-    ms = timed(dist, clocks, step, T)
+    ms_eager = timed(dist, clocks, step, T)
+    state["t"] = 0
+
+    def all_steps():
+        for _ in range(T):
+            step()
+
+    ms = timed_graph(dist, clocks, all_steps, T) * T
+    state["t"] = 0
+    _native.raise_on_device_error()
     bytes_total = sum(2 * B * H * D * 2 * (ctx + t + 1) for t in range(T))
     res = {"GB_s": bytes_total / (ms * 1e-3) / 1e9, "tokens_s": B * T / (ms * 1e-3),
-           "ms_per_step": ms / T, "shard_tokens_per_gpu": shard,
-           "collective": "none" if N == 1 else "ncclAllGather of fp32 (out, LSE) + LSE merge"}
+           "ms_per_step": ms / T, "eager_ms_per_step": ms_eager / T,
+           "shard_tokens_per_gpu": shard,
+           "collective": "none" if N == 1 else "ncclAllGather of fp32 (out, LSE) + LSE merge",
+           "steps": f"the {T} steps replayed from one CUDA graph (collectives included)"}
 
     # The step's parts, each timed alone over T repetitions (max over ranks).
     t_last = T - 1
@@ -864,6 +904,7 @@ def decode_summary(sub: dict, world: int, hbm: float) -> dict:
                        "frac_per_gpu": round(c3["GB_s"] / world / hbm, 4),
                        "tokens_s": round(c3["tokens_s"], 1),
                        "ms_step": round(c3["ms_per_step"], 4),
+                       "eager_ms_step": round(c3["eager_ms_per_step"], 4),
                        "kernel_frac_per_gpu": round(c3["decode_kernel_GB_s"] / world / hbm, 4)}
     c5 = sub.get("longctx_cfg5", {})
     if "GB_s" in c5:
@@ -871,6 +912,7 @@ def decode_summary(sub: dict, world: int, hbm: float) -> dict:
                        "frac_per_gpu": round(c5["GB_s"] / world / hbm, 4),
                        "tokens_s": round(c5["tokens_s"], 1),
                        "ms_step": round(c5["ms_per_step"], 4),
+                       "eager_ms_step": round(c5["eager_ms_per_step"], 4),
                        "parts_ms": {k: round(v, 4) for k, v in c5.get("step_parts", {}).items()},
                        "max_abs_err": c5.get("check", {}).get("max_abs_err")}
     return out
