@@ -576,11 +576,9 @@ __global__ void __launch_bounds__(kThreads, 2)
 struct PerfSmem {
   __host__ __device__ static int stage_bytes() { return 2 * 128 * 128 + 2 * 256 * 128; }
   // Head dims up to 64 are one K step: one stage, so that two CTAs fit per SM.
+  // The epilogue stages its output in stage 0, free once the MMAs are done.
   __host__ __device__ static int stages(int Dh) { return Dh > 64 ? 2 : 1; }
-  static constexpr int kStageOut = 4 * 32 * 128;  // one 32-row x 128-byte buffer per epilogue warp
-  __host__ __device__ static int total(int Dh) {
-    return stages(Dh) * stage_bytes() + kStageOut + 128 + 1024;
-  }
+  __host__ __device__ static int total(int Dh) { return stages(Dh) * stage_bytes() + 128 + 1024; }
 };
 
 template <int kMode>
@@ -592,8 +590,8 @@ __global__ void __launch_bounds__(kThreads)
                                              ~uintptr_t(1023));
   constexpr int kX = 128 * 128;  // one plane of a 64-wide K step of x
   const int n_st = PerfSmem::stages(p.Dh);
-  uint8_t* out_stage = smem + n_st * PerfSmem::stage_bytes();
-  uint64_t* bars = reinterpret_cast<uint64_t*>(out_stage + PerfSmem::kStageOut);
+  uint8_t* out_stage = smem;  // stage 0, after the MMAs have read it
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + n_st * PerfSmem::stage_bytes());
   uint64_t* bar_full = bars;       // [2]
   uint64_t* bar_empty = bars + 2;  // [2]
   uint64_t* bar_acc = bars + 4;
@@ -696,9 +694,10 @@ __global__ void __launch_bounds__(kThreads)
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         if (lane == 0 && m > -INFINITY) atomicMax(reinterpret_cast<int*>(p.stab) + bh, ord_enc(m));
       } else {
-        // 32 features at a time: the warp stages its 32 rows x 128 bytes in
-        // the TMA store's swizzled layout and stores them with one bulk copy
-        // (rows past S and features past Df are clipped by the tensor map).
+        // 32 features at a time: each lane puts its row's 32 values in the
+        // warp's 32-row x 128-byte buffer (16-byte units XOR-swizzled by row
+        // against bank conflicts), then the warp stores 4 whole 128-byte row
+        // segments per instruction.
         const float stab = kMode == 1 ? m : p.stab[bh];
         const float norm = rsqrtf((float)p.Df);
         uint8_t* buf = out_stage + (warp - 2) * 32 * 128;
@@ -713,21 +712,24 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
           for (int i = 0; i < 32; ++i)
             y[i] = expf(__uint_as_float(r[i]) * inv4 - sq - stab) * norm;
-          if (lane == 0) bulk_wait_read_all();  // the previous store has read the buffer
-          __syncwarp();
+          __syncwarp();  // the previous chunk's reads of the buffer are done
 #pragma unroll
           for (int u = 0; u < 8; ++u)
             *reinterpret_cast<float4*>(buf + lane * 128 + ((u ^ (lane & 7)) << 4)) =
                 make_float4(y[4 * u], y[4 * u + 1], y[4 * u + 2], y[4 * u + 3]);
-          fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) {
-            tma_store_3d(&tm_phi, buf, c0, row0, bh);
-            bulk_commit_group();
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int piece = 32 * k + lane, rr = piece / 8, u = piece % 8;
+            const int col = c0 + 4 * u;
+            if (row0 + rr < p.S && col < p.Df) {
+              const float4 v4 =
+                  *reinterpret_cast<const float4*>(buf + rr * 128 + ((u ^ (rr & 7)) << 4));
+              *reinterpret_cast<float4*>(p.phi + ((long long)bh * p.S + row0 + rr) * p.Df + col) =
+                  v4;
+            }
           }
         }
-        if (lane == 0) bulk_wait_all();
-        __syncwarp();
       }
     }
   }
