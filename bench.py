@@ -612,16 +612,15 @@ def bench_cross_cfg4(dist: Dist, clocks: ClockSampler, warmup: int, steps: int =
                       f"L~U[{CFG4['lo']},{CFG4['hi']}], bf16"}
 
 
-FP32_CORE_TFLOPS = 148 * 128 * 2 * 1.965e-3  # nominal fp32 FMA TFLOP/s of the CUDA cores
-
-
 def bench_linear(dist: Dist, clocks: ClockSampler, warmup: int, steps: int = 10):
     """Linearized attention (attention_kernel "linear" and "performer"):
     feature maps plus causal linear attention on device fp32 head views, per
-    GPU B4 S4096 H16 D64 (Performer with 256 features). FLOPs count the
-    reference's reassociated form, 4 S Df D per query head, plus the
-    Performer projections (2 S Dh Df for queries, twice that for keys: the
-    stabilizer pass and the map)."""
+    GPU B4 S4096 H16 D64 (Performer with 256 features), as the layer runs them
+    (attention.linearized): the maps write phi as the bf16 hi/lo planes the
+    tensor-core attention reads. ms_fp32_phi times the same work through fp32
+    phi (the separate-call form). FLOPs count the reference's reassociated
+    form, 4 S Df D per query head, plus the Performer projections (2 S Dh Df
+    for queries, twice that for keys: the stabilizer pass and the map)."""
     import torch
     from enilnets_b200 import kernels, _native
     B, S, H, D, Df = 4, 4096, 16, 64, 256
@@ -633,26 +632,29 @@ def bench_linear(dist: Dist, clocks: ClockSampler, warmup: int, steps: int = 10)
     for kernel in ("linear", "performer"):
         om = omega if kernel == "performer" else None
         nf = Df if kernel == "performer" else D
+        planes = kernels.linear_planes_ok(D, nf)
 
-        def step():
-            qp, _ = kernels.linear_feature_map(q, kernel, om)
-            kp, _ = kernels.linear_feature_map(k, kernel, om, global_stab=True)
-            kernels.linear_attention(qp, kp, v, causal=True)
+        def step(pl=planes):
+            qp, _ = kernels.linear_feature_map(q, kernel, om, planes=pl)
+            kp, _ = kernels.linear_feature_map(k, kernel, om, global_stab=True, planes=pl)
+            kernels.linear_attention(qp, kp, v, causal=True, num_features=nf)
 
-        for _ in range(warmup):
-            step()
-        torch.cuda.synchronize()
-        _native.raise_on_device_error()
-        ms = timed(dist, clocks, step, steps) / steps
+        times = {}
+        for pl in (False, planes):
+            for _ in range(warmup):
+                step(pl)
+            torch.cuda.synchronize()
+            _native.raise_on_device_error()
+            times[pl] = timed(dist, clocks, lambda: step(pl), steps) / steps
+        ms = times[planes]
         flops = 4.0 * S * nf * D * B * H
         if kernel == "performer":
             flops += 3 * 2.0 * S * D * Df * B * H
         tf = dist.sum(flops) / (ms * 1e-3) / 1e12
-        res[kernel] = {"ms_per_step": ms, "TFLOP_s": tf,
-                       "frac_of_fp32_core_peak_per_gpu": tf / dist.world / FP32_CORE_TFLOPS,
-                       "tokens_s": dist.sum(B * S) / (ms * 1e-3)}
-    res["config"] = (f"B{B}/GPU S{S} H{H} D{D} causal, fp32 arithmetic on CUDA cores; performer "
-                     f"with {Df} features; peak = nominal {FP32_CORE_TFLOPS:.1f} TFLOP/s fp32")
+        res[kernel] = {"ms_per_step": ms, "TFLOP_s": tf, "ms_fp32_phi": times[False],
+                       "phi_planes": planes, "tokens_s": dist.sum(B * S) / (ms * 1e-3)}
+    res["config"] = (f"B{B}/GPU S{S} H{H} D{D} causal, fp32 inputs and outputs, split-bf16 "
+                     f"tcgen05 contractions (fp32-level accuracy); performer with {Df} features")
     return res
 
 

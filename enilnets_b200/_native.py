@@ -32,7 +32,7 @@ DEVICE_ERRORS = {1: "an mbarrier wait exceeded its time budget",
                  3: "a launch-time shape invariant was violated"}
 
 
-ABI_VERSION = 6  # ENL_ABI_VERSION of include/enl_attn.h
+ABI_VERSION = 7  # ENL_ABI_VERSION of include/enl_attn.h
 
 
 class PrefillArgs(Structure):
@@ -100,6 +100,7 @@ class PhiArgs(Structure):
         ("omega", c_void_p), ("num_features", c_int32), ("global_stab", c_int32),
         ("stab_floor", c_void_p), ("stab", c_void_p), ("phi", c_void_p),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+        ("phi_planes", c_void_p),
     ]
 
 
@@ -118,6 +119,7 @@ class LinearArgs(Structure):
         ("kv_out", c_void_p), ("ksum_out", c_void_p),
         ("eps", c_float),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+        ("phi_q_planes", c_void_p), ("phi_k_planes", c_void_p),
     ]
 
 
@@ -184,6 +186,7 @@ SIGNATURES = {
     "enl_phi_workspace_bytes": ([POINTER(PhiArgs)], c_size_t),
     "enl_linear_attention": ([POINTER(LinearArgs), c_void_p], c_int32),
     "enl_linear_max_features": ([], c_int32),
+    "enl_linear_planes_ok": ([c_int32, c_int32], c_int32),
     "enl_linear_workspace_bytes": ([POINTER(LinearArgs)], c_size_t),
     "enl_sparse_build_masks": ([POINTER(SparseMaskArgs), c_void_p], c_int32),
     "enl_attn_backward": ([POINTER(BackwardArgs), c_void_p], c_int32),

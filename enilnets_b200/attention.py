@@ -203,9 +203,14 @@ def linearized(layer: dict, q, k, v, causal: bool):
     expanded head since a group's heads are copies."""
     kernel = layer["attention_kernel"]
     omega = omega_tensor(layer) if kernel == "performer" else None
-    qp, _ = kernels.linear_feature_map(q, kernel, omega)
-    kp, _ = kernels.linear_feature_map(k, kernel, omega, global_stab=True)
-    return kernels.linear_attention(qp, kp, v, causal=causal, out_dtype=compute_dtype())
+    Df = omega.shape[0] if omega is not None else q.shape[3]
+    # On the tensor-core path the maps write phi as the bf16 planes the
+    # attention reads (no fp32 phi round trip).
+    planes = kernels.linear_planes_ok(v.shape[3], Df)
+    qp, _ = kernels.linear_feature_map(q, kernel, omega, planes=planes)
+    kp, _ = kernels.linear_feature_map(k, kernel, omega, global_stab=True, planes=planes)
+    return kernels.linear_attention(qp, kp, v, causal=causal, out_dtype=compute_dtype(),
+                                    num_features=Df)
 
 
 # ------------------------------------------------------------- forward

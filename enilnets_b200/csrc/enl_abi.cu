@@ -102,10 +102,17 @@ struct LinTcPlan {
   int Dp, Dfp, Sp, n_chunks;
   size_t off_qp, off_kp, off_vt, off_u, off_st, total;
 };
+bool lin_tc_sizes(int head_dim, int num_features) {
+  return head_dim >= 1 && head_dim <= 128 && num_features >= 1 && num_features <= 1024;
+}
+bool lin_planes_given(const enl_linear_args* a) { return a->phi_q_planes && a->phi_k_planes; }
+// With phi planes given, the qp / kp regions are empty and the caller's
+// planes are read in their place.
 LinTcPlan lin_tc_plan(const enl_linear_args* a) {
   LinTcPlan pl{};
-  pl.use = a->head_dim <= 128 && a->num_features <= 1024 && a->seq >= 1 && a->batch >= 1;
+  pl.use = lin_tc_sizes(a->head_dim, a->num_features) && a->seq >= 1 && a->batch >= 1;
   if (!pl.use) return pl;
+  const bool given = lin_planes_given(a);
   const size_t B = a->batch, H = a->num_heads, Hk = a->num_kv_heads, S = a->seq;
   const size_t Df = a->num_features;
   pl.Dp = ((a->head_dim + 1 + 15) / 16) * 16;
@@ -115,9 +122,9 @@ LinTcPlan lin_tc_plan(const enl_linear_args* a) {
   auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
   size_t off = 0;
   pl.off_qp = off;
-  off += al(2 * B * H * S * pl.Dfp * 2);
+  if (!given) off += al(2 * B * H * S * pl.Dfp * 2);
   pl.off_kp = off;
-  off += al(2 * B * Hk * S * pl.Dfp * 2);
+  if (!given) off += al(2 * B * Hk * S * pl.Dfp * 2);
   pl.off_vt = off;
   off += al(2 * B * Hk * (size_t)pl.Dp * pl.Sp * 2);
   pl.off_u = off;
@@ -967,6 +974,10 @@ int enl_rope_apply(void* x, int64_t stride_b, int64_t stride_s, int64_t stride_h
 
 int enl_linear_max_features(void) { return enl::linear_attn_max_features(); }
 
+int enl_linear_planes_ok(int32_t head_dim, int32_t num_features) {
+  return lin_tc_sizes(head_dim, num_features) ? 1 : 0;
+}
+
 size_t enl_linear_workspace_bytes(const enl_linear_args* a) {
   if (!a || a->batch < 1 || a->num_heads < 1 || a->num_kv_heads < 1 || a->seq < 1) return 0;
   const LinTcPlan pl = lin_tc_plan(a);
@@ -975,20 +986,68 @@ size_t enl_linear_workspace_bytes(const enl_linear_args* a) {
                                      a->num_features, a->head_dim, a->causal);
 }
 
+}  // extern "C"
+
+namespace {
+// The feature map's kernel parameters from the ABI arguments (phi / planes
+// pointers left for the caller to set).
+enl::PhiParams phi_params(const enl_phi_args* a) {
+  enl::PhiParams p{};
+  p.x = a->x;
+  p.sb = a->x_stride_b;
+  p.ss = a->x_stride_s;
+  p.sh = a->x_stride_h;
+  p.B = a->batch;
+  p.S = a->seq;
+  p.H = a->num_heads;
+  p.Dh = a->head_dim;
+  p.in_f32 = a->in_dtype == ENL_DTYPE_FP32;
+  p.kernel = a->kernel;
+  p.omega = a->omega;
+  p.Df = a->kernel == ENL_PHI_LINEAR ? a->head_dim : a->num_features;
+  p.Dfp = (p.Df + 7) / 8 * 8;
+  p.global_stab = a->kernel == ENL_PHI_PERFORMER && a->global_stab;
+  p.stab_floor = a->stab_floor;
+  p.stab = a->stab;
+  return p;
+}
+
+bool phi_on_tensor_cores(const enl_phi_args* a) {
+  return a->kernel == ENL_PHI_PERFORMER && enl::perf_tc_supported(a->head_dim, a->num_features) &&
+         a->num_features >= 1 && a->num_features % 4 == 0;
+}
+
+// Planes from a map that writes fp32 only: the map goes to an fp32 phi in the
+// workspace, then a split pass writes the planes.
+bool phi_planes_via_fp32(const enl_phi_args* a) {
+  if (!a->phi_planes || phi_on_tensor_cores(a)) return false;
+  enl::PhiParams p = phi_params(a);
+  p.planes = reinterpret_cast<uint16_t*>(a->phi_planes);
+  return !enl::phi_planes_direct(p);
+}
+}  // namespace
+
+extern "C" {
+
 size_t enl_phi_workspace_bytes(const enl_phi_args* a) {
-  if (!a || a->kernel != ENL_PHI_PERFORMER || a->batch < 1 || a->seq < 1 || a->num_heads < 1 ||
-      !enl::perf_tc_supported(a->head_dim, a->num_features) || a->num_features < 1 ||
-      a->num_features % 4 != 0)
-    return 0;
-  const size_t Dhp = (a->head_dim + 7) / 8 * 8;
+  if (!a || a->batch < 1 || a->seq < 1 || a->num_heads < 1) return 0;
   auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
-  return al(2 * (size_t)a->batch * a->num_heads * a->seq * Dhp * 2) +
-         al(2 * (size_t)a->num_features * Dhp * 2);
+  if (phi_on_tensor_cores(a)) {
+    const size_t Dhp = (a->head_dim + 7) / 8 * 8;
+    return al(2 * (size_t)a->batch * a->num_heads * a->seq * Dhp * 2) +
+           al(2 * (size_t)a->num_features * Dhp * 2);
+  }
+  if (phi_planes_via_fp32(a)) {
+    const size_t Df = a->kernel == ENL_PHI_LINEAR ? a->head_dim : a->num_features;
+    return al((size_t)a->batch * a->num_heads * a->seq * Df * 4);
+  }
+  return 0;
 }
 
 int enl_linear_feature_map(const enl_phi_args* a, void* stream) {
-  if (!a || !a->x || !a->phi)
-    return fail(ENL_ERR_INVALID, "enl_linear_feature_map: args, x and phi must be non-NULL");
+  if (!a || !a->x || (!a->phi && !a->phi_planes))
+    return fail(ENL_ERR_INVALID, "enl_linear_feature_map: args, x and phi (or phi_planes) must "
+                "be non-NULL");
   if (a->batch < 0 || a->seq < 0 || a->num_heads < 1 || a->head_dim < 1 || a->head_dim > 1024)
     return fail(ENL_ERR_INVALID, "enl_linear_feature_map: bad sizes (batch %d, seq %d, heads %d, "
                 "head_dim %d)", a->batch, a->seq, a->num_heads, a->head_dim);
@@ -1006,31 +1065,22 @@ int enl_linear_feature_map(const enl_phi_args* a, void* stream) {
       return fail(ENL_ERR_UNSUPPORTED, "enl_linear_feature_map: performer head_dim %d > %d",
                   a->head_dim, enl::perf_max_head_dim());
   }
-  enl::PhiParams p{};
-  p.x = a->x;
-  p.sb = a->x_stride_b;
-  p.ss = a->x_stride_s;
-  p.sh = a->x_stride_h;
-  p.B = a->batch;
-  p.S = a->seq;
-  p.H = a->num_heads;
-  p.Dh = a->head_dim;
-  p.in_f32 = a->in_dtype == ENL_DTYPE_FP32;
-  p.kernel = a->kernel;
-  p.omega = a->omega;
-  p.Df = a->kernel == ENL_PHI_LINEAR ? a->head_dim : a->num_features;
-  p.global_stab = a->kernel == ENL_PHI_PERFORMER && a->global_stab;
-  p.stab_floor = a->stab_floor;
-  p.stab = a->stab;
-  p.phi = a->phi;
+  if (a->phi_planes && (reinterpret_cast<uintptr_t>(a->phi_planes) & 15u) != 0)
+    return fail(ENL_ERR_INVALID, "enl_linear_feature_map: phi_planes must be 16-byte aligned");
+  enl::PhiParams p = phi_params(a);
   const size_t need = enl_phi_workspace_bytes(a);
-  if (need > 0) {
+  if (need > 0 && (!a->workspace || a->workspace_bytes < need ||
+                   (reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0))
+    return fail(ENL_ERR_INVALID, "enl_linear_feature_map: needs a 256-byte aligned workspace of "
+                "%zu bytes (enl_phi_workspace_bytes)", need);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (phi_on_tensor_cores(a)) {
     // Tensor-core Performer map: planes of x and omega, then the projections
-    // on tcgen05 with the stabilizer in the epilogue.
-    if (!a->workspace || a->workspace_bytes < need ||
-        (reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0)
-      return fail(ENL_ERR_INVALID, "enl_linear_feature_map: the performer map needs a 256-byte "
-                  "aligned workspace of %zu bytes (enl_phi_workspace_bytes)", need);
+    // on tcgen05 with the stabilizer in the epilogue, which writes fp32 phi or
+    // its planes.
+    if (!a->phi_planes && (reinterpret_cast<uintptr_t>(a->phi) & 15u) != 0)
+      return fail(ENL_ERR_INVALID, "enl_linear_feature_map: phi must be 16-byte aligned for the "
+                  "tensor-core map");
     const int Dhp = (a->head_dim + 7) / 8 * 8;
     const size_t xbytes = ((2 * (size_t)a->batch * a->num_heads * a->seq * Dhp * 2) + 255) &
                           ~size_t(255);
@@ -1041,11 +1091,12 @@ int enl_linear_feature_map(const enl_phi_args* a, void* stream) {
     t.Dh = a->head_dim;
     t.Dhp = Dhp;
     t.Df = a->num_features;
+    t.Dfp = p.Dfp;
     t.xp = reinterpret_cast<uint16_t*>(a->workspace);
     uint16_t* wp = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(a->workspace) + xbytes);
     t.stab = a->stab;
-    t.phi = a->phi;
-    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    t.phi = a->phi_planes ? nullptr : a->phi;
+    t.planes = reinterpret_cast<uint16_t*>(a->phi_planes);
     cudaError_t e = enl::launch_perf_prep(a->x, a->x_stride_b, a->x_stride_s, a->x_stride_h,
                                           a->in_dtype == ENL_DTYPE_FP32, a->omega, t, wp, s);
     if (e != cudaSuccess) return cuda_fail(e, "enl_linear_feature_map: prep launch");
@@ -1057,36 +1108,37 @@ int enl_linear_feature_map(const enl_phi_args* a, void* stream) {
       return st;
     if ((st = make_3d_map(&tw, wp, t.Dh, t.Df, 2, Dhp, (int64_t)t.Df * Dhp, Dfn, "omega")))
       return st;
-    // phi (B * H, S, Df) fp32, stored in 32-feature x 32-row boxes.
-    CUtensorMap tphi;
-    {
-      EncodeTiledFn fn = encode_fn();
-      if (!fn) return fail(ENL_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
-      if ((t.Df * 4) % 16 != 0 || (reinterpret_cast<uintptr_t>(a->phi) & 15u) != 0)
-        return fail(ENL_ERR_INVALID, "enl_linear_feature_map: phi must be 16-byte aligned with "
-                    "num_features a multiple of 4 for the tensor-core map");
-      cuuint64_t dims[3] = {(cuuint64_t)t.Df, (cuuint64_t)t.S, (cuuint64_t)BH};
-      cuuint64_t strides[2] = {(cuuint64_t)t.Df * 4, (cuuint64_t)t.S * t.Df * 4};
-      cuuint32_t box[3] = {32, 32, 1};
-      cuuint32_t estr[3] = {1, 1, 1};
-      CUresult r = fn(&tphi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, a->phi, dims, strides, box, estr,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-      if (r != CUDA_SUCCESS)
-        return fail(ENL_ERR_INVALID, "cuTensorMapEncodeTiled(phi) failed with CUresult %d", (int)r);
-    }
-    e = enl::launch_perf_tc_maps(tx, tw, tphi, t, p.global_stab, a->stab_floor, s);
+    e = enl::launch_perf_tc_maps(tx, tw, t, p.global_stab, a->stab_floor, s);
     if (e != cudaSuccess) return cuda_fail(e, "enl_linear_feature_map launch");
     return ENL_OK;
   }
-  cudaError_t e = enl::launch_phi(p, reinterpret_cast<cudaStream_t>(stream));
+  const bool via_fp32 = phi_planes_via_fp32(a);
+  p.phi = via_fp32 ? reinterpret_cast<float*>(a->workspace) : a->phi_planes ? nullptr : a->phi;
+  p.planes = via_fp32 ? nullptr : reinterpret_cast<uint16_t*>(a->phi_planes);
+  cudaError_t e = enl::launch_phi(p, s);
+  if (e == cudaSuccess && via_fp32)
+    e = enl::launch_rows_planes(p.phi, (long long)p.B * p.H * p.S, p.Df, p.Dfp,
+                                reinterpret_cast<uint16_t*>(a->phi_planes), s);
   if (e != cudaSuccess) return cuda_fail(e, "enl_linear_feature_map launch");
   return ENL_OK;
 }
 
 int enl_linear_attention(const enl_linear_args* a, void* stream) {
-  if (!a || !a->phi_q || !a->phi_k || !a->v || !a->o)
-    return fail(ENL_ERR_INVALID, "enl_linear_attention: args, phi_q, phi_k, v and o must be non-NULL");
+  if (!a || !a->v || !a->o)
+    return fail(ENL_ERR_INVALID, "enl_linear_attention: args, v and o must be non-NULL");
+  if ((a->phi_q_planes == nullptr) != (a->phi_k_planes == nullptr))
+    return fail(ENL_ERR_INVALID, "enl_linear_attention: phi_q_planes and phi_k_planes come in "
+                "pairs");
+  const bool given = lin_planes_given(a);
+  if (!given && (!a->phi_q || !a->phi_k))
+    return fail(ENL_ERR_INVALID, "enl_linear_attention: phi_q and phi_k (or their planes) must "
+                "be non-NULL");
+  if (given && !lin_tc_sizes(a->head_dim, a->num_features))
+    return fail(ENL_ERR_UNSUPPORTED, "enl_linear_attention: phi planes need head_dim <= 128 and "
+                "num_features <= 1024 (got %d, %d)", a->head_dim, a->num_features);
+  if (given && ((reinterpret_cast<uintptr_t>(a->phi_q_planes) |
+                 reinterpret_cast<uintptr_t>(a->phi_k_planes)) & 15u) != 0)
+    return fail(ENL_ERR_INVALID, "enl_linear_attention: phi planes must be 16-byte aligned");
   if (a->batch < 0 || a->seq < 0 || a->num_heads < 1 || a->num_kv_heads < 1 || a->head_dim < 1 ||
       a->num_features < 1)
     return fail(ENL_ERR_INVALID, "enl_linear_attention: bad sizes");
@@ -1145,8 +1197,10 @@ int enl_linear_attention(const enl_linear_args* a, void* stream) {
     if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0)
       return fail(ENL_ERR_INVALID, "enl_linear_attention: workspace must be 256-byte aligned");
     uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
-    uint16_t* qp = reinterpret_cast<uint16_t*>(ws + pl.off_qp);
-    uint16_t* kp = reinterpret_cast<uint16_t*>(ws + pl.off_kp);
+    const uint16_t* qp = given ? reinterpret_cast<const uint16_t*>(a->phi_q_planes)
+                               : reinterpret_cast<const uint16_t*>(ws + pl.off_qp);
+    const uint16_t* kp = given ? reinterpret_cast<const uint16_t*>(a->phi_k_planes)
+                               : reinterpret_cast<const uint16_t*>(ws + pl.off_kp);
     uint16_t* vt = reinterpret_cast<uint16_t*>(ws + pl.off_vt);
     enl::LinTcParams t{};
     t.B = a->batch;
@@ -1175,9 +1229,10 @@ int enl_linear_attention(const enl_linear_args* a, void* stream) {
     t.o_f32 = a->out_dtype == ENL_DTYPE_FP32;
     t.eps = a->eps;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    cudaError_t e = enl::launch_lin_prep(a->phi_q, a->phi_k, a->v, a->v_stride_b, a->v_stride_s,
-                                         a->v_stride_h, a->v_dtype == ENL_DTYPE_FP32, t, qp, kp,
-                                         vt, s);
+    cudaError_t e = enl::launch_lin_prep(
+        given ? nullptr : a->phi_q, given ? nullptr : a->phi_k, a->v, a->v_stride_b,
+        a->v_stride_s, a->v_stride_h, a->v_dtype == ENL_DTYPE_FP32, t,
+        const_cast<uint16_t*>(qp), const_cast<uint16_t*>(kp), vt, s);
     if (e != cudaSuccess) return cuda_fail(e, "enl_linear_attention: prep launch");
     const long long BHq = (long long)t.B * t.H, BHk = (long long)t.B * t.Hkv;
     CUtensorMap tq, tk, tvt, tst;

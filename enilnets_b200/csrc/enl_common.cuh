@@ -491,4 +491,24 @@ __device__ __forceinline__ float bf16hi_to_f32(uint32_t w) {
   return __uint_as_float(w & 0xFFFF0000u);
 }
 
+// Unsigned 32-bit division by a run-time invariant divisor d >= 1 as a
+// multiply-high, an add and a shift (Granlund and Montgomery, "Division by
+// invariant integers using multiplication", PLDI 1994, the N+1-bit multiplier
+// form): l = ceil(log2 d), m = floor(2^32 (2^l - d) / d) + 1, and
+// n / d = (mulhi(m, n) + n) >> l for every 0 <= n < 2^32 (the add is done in
+// 64 bits). Elementwise kernels use it for their index decomposition, where a
+// 64-bit division costs more than the element's own work.
+struct DivU32 {
+  uint32_t d, m, l;
+  static DivU32 make(uint32_t d) {
+    uint32_t l = 0;
+    while (l < 32 && (1ull << l) < d) ++l;
+    const uint64_t m = (((1ull << l) - d) << 32) / d + 1;
+    return DivU32{d, (uint32_t)m, l};
+  }
+  __device__ __forceinline__ uint32_t div(uint32_t n) const {
+    return (uint32_t)(((uint64_t)__umulhi(n, m) + n) >> l);
+  }
+};
+
 }  // namespace enl

@@ -209,9 +209,14 @@ struct PhiParams {
   int global_stab;
   const float* stab_floor;
   float* stab;
-  float* phi;
+  float* phi;        // (B, H, S, Df) fp32 out, or null when planes is set
+  uint16_t* planes;  // [2][B * H][S][Dfp] bf16 hi/lo planes out (elu + 1, vectorised path)
+  int Dfp;
 };
 cudaError_t launch_phi(const PhiParams& p, cudaStream_t stream);
+// Whether launch_phi writes planes directly for these arguments (else the
+// caller maps to fp32 and splits with launch_rows_planes).
+bool phi_planes_direct(const PhiParams& p);
 int perf_max_head_dim();  // Performer feature maps take head_dim up to this
 
 // Linear attention over phi(Q) (B, H, S, Df) and phi(K) (B, Hkv, S, Df) with
@@ -263,19 +268,24 @@ struct PerfTcParams {
   int B, S, H, Dh, Dhp, Df;
   uint16_t* xp;      // [2][B * H][S][Dhp] bf16 planes of x
   float* stab;       // (B * H): mode 0 atomic-max target (ordered ints), mode 2 input
-  float* phi;        // (B, H, S, Df) fp32 out
+  float* phi;        // (B, H, S, Df) fp32 out, or null when planes is set
+  uint16_t* planes;  // [2][B * H][S][Dfp] bf16 hi/lo planes out
+  int Dfp;
 };
 bool perf_tc_supported(int Dh, int Df);
 cudaError_t launch_perf_prep(const void* x, long long sb, long long ss, long long sh, int f32,
                              const float* omega, const PerfTcParams& p, uint16_t* wp,
                              cudaStream_t stream);
-cudaError_t launch_perf_tc(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tphi,
-                           const PerfTcParams& p, int mode, cudaStream_t stream);
+cudaError_t launch_perf_tc(const CUtensorMap& tx, const CUtensorMap& tw, const PerfTcParams& p,
+                           int mode, cudaStream_t stream);
 // Queries (global_stab 0): one pass with row stabilizers. Keys: the
 // stabilizer (floored by stab_floor) as a max pass, then the map.
 cudaError_t launch_perf_tc_maps(const CUtensorMap& tx, const CUtensorMap& tw,
-                                const CUtensorMap& tphi, const PerfTcParams& p, int global_stab,
-                                const float* stab_floor, cudaStream_t stream);
+                                const PerfTcParams& p, int global_stab, const float* stab_floor,
+                                cudaStream_t stream);
+// Row planes of an fp32 (R, Df) matrix: dst[plane][R][Dfp] bf16 hi/lo.
+cudaError_t launch_rows_planes(const float* src, long long R, int Df, int Dfp, uint16_t* dst,
+                               cudaStream_t stream);
 cudaError_t launch_lin_prep(const float* phi_q, const float* phi_k, const void* v, long long v_sb,
                             long long v_ss, long long v_sh, int v_f32, const LinTcParams& p,
                             uint16_t* qp, uint16_t* kp, uint16_t* vt, cudaStream_t stream);

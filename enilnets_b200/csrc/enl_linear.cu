@@ -42,32 +42,64 @@ __device__ __forceinline__ float load_elem(const void* base, long long idx, bool
 }
 
 // phi = elu(x) + 1, four features per thread: one 16-byte (fp32) or 8-byte
-// (bf16) load and one 16-byte store, in output order (b, h, s, d).
-__global__ void __launch_bounds__(256) phi_linear_vec_kernel(PhiParams p) {
-  const int q4 = p.Dh / 4;
-  const long long n = (long long)p.B * p.H * p.S * q4;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int c = (int)(i % q4) * 4;
-    long long r = i / q4;
-    const int s = (int)(r % p.S);
-    r /= p.S;
-    const int h = (int)(r % p.H), b = (int)(r / p.H);
-    const long long xoff = b * p.sb + s * p.ss + h * p.sh + c;
-    float v[4];
-    if (p.in_f32) {
-      const float4 x = __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) +
-                                                             xoff));
-      v[0] = x.x, v[1] = x.y, v[2] = x.z, v[3] = x.w;
-    } else {
-      const uint2 x = __ldg(reinterpret_cast<const uint2*>(
-          reinterpret_cast<const __nv_bfloat16*>(p.x) + xoff));
-      v[0] = bf16lo_to_f32(x.x), v[1] = bf16hi_to_f32(x.x);
-      v[2] = bf16lo_to_f32(x.y), v[3] = bf16hi_to_f32(x.y);
+// (bf16) load and one 16-byte store, in output order (b, h, s, d). At most
+// 2^31 groups of four, so that the flat index splits into (b, h, s, d) with
+// 32-bit multiply-high divisions. Each thread issues kPhiUnroll loads before
+// it stores anything, so that enough bytes are in flight to cover the DRAM
+// latency on inputs of a few tens of MB. With p.planes set the output is the
+// bf16 hi/lo planes [2][B * H][S][Dfp] that the tensor-core linear attention
+// reads, instead of fp32 phi.
+constexpr int kPhiUnroll = 4;
+
+__global__ void __launch_bounds__(256)
+    phi_linear_vec_kernel(PhiParams p, DivU32 dq4, DivU32 ds, DivU32 dh) {
+  const uint32_t n = (uint32_t)((long long)p.B * p.H * p.S * dq4.d);
+  const uint32_t stride = gridDim.x * blockDim.x;
+  const long long plane_elems = (long long)p.B * p.H * p.S * p.Dfp;
+  for (uint32_t i0 = blockIdx.x * blockDim.x + threadIdx.x; i0 < n; i0 += kPhiUnroll * stride) {
+    float v[kPhiUnroll][4];
+#pragma unroll
+    for (int u = 0; u < kPhiUnroll; ++u) {
+      const uint32_t i = i0 + u * stride;
+      if (i >= n) break;
+      const uint32_t r = dq4.div(i);
+      const int c = (int)(i - r * dq4.d) * 4;
+      const uint32_t bh = ds.div(r);
+      const int s = (int)(r - bh * ds.d);
+      const uint32_t b = dh.div(bh);
+      const int h = (int)(bh - b * dh.d);
+      const long long xoff = (long long)b * p.sb + (long long)s * p.ss + (long long)h * p.sh + c;
+      if (p.in_f32) {
+        const float4 x = __ldg(reinterpret_cast<const float4*>(
+            reinterpret_cast<const float*>(p.x) + xoff));
+        v[u][0] = x.x, v[u][1] = x.y, v[u][2] = x.z, v[u][3] = x.w;
+      } else {
+        const uint2 x = __ldg(reinterpret_cast<const uint2*>(
+            reinterpret_cast<const __nv_bfloat16*>(p.x) + xoff));
+        v[u][0] = bf16lo_to_f32(x.x), v[u][1] = bf16hi_to_f32(x.x);
+        v[u][2] = bf16lo_to_f32(x.y), v[u][3] = bf16hi_to_f32(x.y);
+      }
     }
 #pragma unroll
-    for (int e = 0; e < 4; ++e) v[e] = v[e] > 0.0f ? v[e] + 1.0f : expf(fminf(v[e], 0.0f));
-    *reinterpret_cast<float4*>(p.phi + i * 4) = make_float4(v[0], v[1], v[2], v[3]);
+    for (int u = 0; u < kPhiUnroll; ++u) {
+      const uint32_t i = i0 + u * stride;
+      if (i >= n) break;
+      float y[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) y[e] = v[u][e] > 0.0f ? v[u][e] + 1.0f : expf(fminf(v[u][e], 0.0f));
+      if (p.planes) {
+        // bf16 hi = bf16(y), lo = bf16(y - hi) at row r, columns c..c+3.
+        const uint32_t r = dq4.div(i);
+        const long long o = (long long)r * p.Dfp + (i - r * dq4.d) * 4;
+        const uint32_t h01 = pack_bf16x2(y[0], y[1]), h23 = pack_bf16x2(y[2], y[3]);
+        const uint32_t l01 = pack_bf16x2(y[0] - bf16lo_to_f32(h01), y[1] - bf16hi_to_f32(h01));
+        const uint32_t l23 = pack_bf16x2(y[2] - bf16lo_to_f32(h23), y[3] - bf16hi_to_f32(h23));
+        *reinterpret_cast<uint2*>(p.planes + o) = make_uint2(h01, h23);
+        *reinterpret_cast<uint2*>(p.planes + plane_elems + o) = make_uint2(l01, l23);
+      } else {
+        *reinterpret_cast<float4*>(p.phi + (long long)i * 4) = make_float4(y[0], y[1], y[2], y[3]);
+      }
+    }
   }
 }
 
@@ -253,17 +285,29 @@ __global__ void phi_decode_kernel(PhiParams p) {
 
 int perf_max_head_dim() { return kPerfMaxHeadDim; }
 
+// The elu + 1 map's vectorised kernel: four features per thread from aligned
+// rows, at most 2^31 groups of four.
+static bool phi_linear_vec_ok(const PhiParams& p) {
+  const int esz = p.in_f32 ? 4 : 2;
+  const long long n = (long long)p.B * p.S * p.H * (p.Dh / 4);
+  return p.Dh % 4 == 0 && (reinterpret_cast<uintptr_t>(p.x) % (4 * esz)) == 0 &&
+         ((p.sb | p.ss | p.sh) % 4) == 0 &&
+         (reinterpret_cast<uintptr_t>(p.planes ? static_cast<void*>(p.planes)
+                                               : static_cast<void*>(p.phi)) % 16) == 0 &&
+         n <= (1ll << 31) && (!p.planes || p.Dfp % 4 == 0);
+}
+
+bool phi_planes_direct(const PhiParams& p) { return p.kernel == 0 && phi_linear_vec_ok(p); }
+
 cudaError_t launch_phi(const PhiParams& p, cudaStream_t stream) {
   const long long rows = (long long)p.B * p.S * p.H;
+  if (p.planes && !phi_planes_direct(p)) return cudaErrorInvalidValue;
   if (p.kernel == 0) {
-    const int esz = p.in_f32 ? 4 : 2;
-    const bool vec = p.Dh % 4 == 0 &&
-                     (reinterpret_cast<uintptr_t>(p.x) % (4 * esz)) == 0 &&
-                     ((p.sb | p.ss | p.sh) % 4) == 0 &&
-                     (reinterpret_cast<uintptr_t>(p.phi) % 16) == 0;
-    if (rows > 0 && vec) {
-      const long long n = rows * (p.Dh / 4);
-      phi_linear_vec_kernel<<<(int)min((n + 255) / 256, 148ll * 16), 256, 0, stream>>>(p);
+    const long long n = rows * (p.Dh / 4);
+    if (rows > 0 && phi_linear_vec_ok(p)) {
+      phi_linear_vec_kernel<<<(int)min((n + 255) / 256, 148ll * 16), 256, 0, stream>>>(
+          p, DivU32::make((uint32_t)(p.Dh / 4)), DivU32::make((uint32_t)p.S),
+          DivU32::make((uint32_t)p.H));
     } else if (rows > 0) {
       phi_linear_kernel<<<(int)min((rows + 7) / 8, 148ll * 16), 256, 0, stream>>>(p);
     }

@@ -75,24 +75,57 @@ __device__ __forceinline__ void split2(float x, uint16_t& hi, uint16_t& lo) {
 }
 
 // ---------------------------------------------------------------- prep
+// Four fp32 values -> bf16 hi at dst[0..3] and lo at dst[plane + 0..3].
+__device__ __forceinline__ void store_split_quad(float4 x, uint16_t* dst, long long plane) {
+  const uint32_t h01 = pack_bf16x2(x.x, x.y), h23 = pack_bf16x2(x.z, x.w);
+  const uint32_t l01 = pack_bf16x2(x.x - bf16lo_to_f32(h01), x.y - bf16hi_to_f32(h01));
+  const uint32_t l23 = pack_bf16x2(x.z - bf16lo_to_f32(h23), x.w - bf16hi_to_f32(h23));
+  *reinterpret_cast<uint2*>(dst) = make_uint2(h01, h23);
+  *reinterpret_cast<uint2*>(dst + plane) = make_uint2(l01, l23);
+}
+
 // Row-major planes: src (R, Df) fp32 -> dst[plane][R][Dfp] bf16.
+__device__ __forceinline__ void prep_rows_quad(const float* __restrict__ src, long long r, int f,
+                                               int Df, int Dfp, long long plane,
+                                               uint16_t* __restrict__ dst) {
+  store_split_quad(__ldg(reinterpret_cast<const float4*>(src + r * Df + f)), dst + r * Dfp + f,
+                   plane);
+}
+
 __global__ void lin_prep_rows(const float* __restrict__ src, long long R, int Df, int Dfp,
-                              uint16_t* __restrict__ dst) {
+                              DivU32 dq4, uint16_t* __restrict__ dst) {
   const long long plane = R * Dfp;
   if ((Df & 3) == 0) {
     // Four features per thread: one 16-byte load, two 8-byte stores.
-    const int q4 = Df / 4;
-    const long long n = R * q4;
+    const long long n = R * dq4.d;
+    if (n <= (1ll << 31)) {
+      // Four loads in flight per thread before the first store.
+      const uint32_t stride = gridDim.x * blockDim.x;
+      for (uint32_t i0 = blockIdx.x * blockDim.x + threadIdx.x; i0 < (uint32_t)n;
+           i0 += 4 * stride) {
+        float4 x[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint32_t i = i0 + u * stride;
+          if (i >= (uint32_t)n) break;
+          const uint32_t r = dq4.div(i);
+          x[u] = __ldg(reinterpret_cast<const float4*>(src + (long long)r * Df) +
+                       (i - r * dq4.d));
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint32_t i = i0 + u * stride;
+          if (i >= (uint32_t)n) break;
+          const uint32_t r = dq4.div(i);
+          store_split_quad(x[u], dst + (long long)r * Dfp + (i - r * dq4.d) * 4, plane);
+        }
+      }
+      return;
+    }
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
          i += (long long)gridDim.x * blockDim.x) {
-      const long long r = i / q4;
-      const int f = (int)(i - r * q4) * 4;
-      const float4 x = __ldg(reinterpret_cast<const float4*>(src + r * Df + f));
-      const uint32_t h01 = pack_bf16x2(x.x, x.y), h23 = pack_bf16x2(x.z, x.w);
-      const uint32_t l01 = pack_bf16x2(x.x - bf16lo_to_f32(h01), x.y - bf16hi_to_f32(h01));
-      const uint32_t l23 = pack_bf16x2(x.z - bf16lo_to_f32(h23), x.w - bf16hi_to_f32(h23));
-      *reinterpret_cast<uint2*>(dst + r * Dfp + f) = make_uint2(h01, h23);
-      *reinterpret_cast<uint2*>(dst + plane + r * Dfp + f) = make_uint2(l01, l23);
+      const long long r = i / dq4.d;
+      prep_rows_quad(src, r, (int)(i - r * dq4.d) * 4, Df, Dfp, plane, dst);
     }
     return;
   }
@@ -109,40 +142,73 @@ __global__ void lin_prep_rows(const float* __restrict__ src, long long R, int Df
 }
 
 // Transposed planes of V' = [V | 1 | 0...]: v[b, s, hkv, d] (element strides,
-// bf16 or fp32) -> dst[plane][B * Hkv][Dp][Sp]; row D is 1 for s < S.
-__global__ void lin_prep_vt(const void* __restrict__ v, long long sb, long long ss, long long sh,
-                            int f32, int Hkv, int S, int D, int Dp, int Sp, long long BH,
-                            uint16_t* __restrict__ dst) {
-  __shared__ float tile[32][33];
-  const long long bh = blockIdx.z;
-  const int b = (int)(bh / Hkv), hkv = (int)(bh % Hkv);
-  const int s0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
-  const int tx = threadIdx.x, ty = threadIdx.y;
-  for (int r = ty; r < 32; r += 8) {
-    const int s = s0 + r, d = d0 + tx;
-    float x = 0.0f;
-    if (s < S) {
-      if (d < D) {
-        const long long off = b * sb + (long long)s * ss + hkv * sh + d;
+// bf16 or fp32) -> dst[plane][B * Hkv][Dp][Sp]; row D is 1 for s < S. One CTA
+// per (b * Hkv + hkv, 64 positions): the 64 rows of V go into shared memory
+// (an odd row stride, so that the column reads below are free of bank
+// conflicts), then every 16 threads write one 128-byte run of a row of V'^T,
+// four positions per thread, in both planes. D <= kVtMaxD, Sp a multiple of 4.
+constexpr int kVtRows = 64, kVtMaxD = 128;
+
+__global__ void __launch_bounds__(256)
+    lin_prep_vt(const void* __restrict__ v, long long sb, long long ss, long long sh, int f32,
+                int Hkv, int S, int D, int Dp, int Sp, long long BH, int vec, DivU32 dq4,
+                uint16_t* __restrict__ dst) {
+  __shared__ float tile[kVtRows * (kVtMaxD + 1)];
+  const int ld = D | 1;
+  const int bh = blockIdx.x;
+  const int b = bh / Hkv, hkv = bh - b * Hkv;
+  const int s0 = blockIdx.y * kVtRows;
+  const int t = threadIdx.x;
+  const long long base = (long long)b * sb + (long long)hkv * sh;
+  if (vec) {  // D % 4 == 0, 16-byte (fp32) or 8-byte (bf16) aligned rows
+    for (uint32_t k = t; k < kVtRows * dq4.d; k += 256) {
+      const uint32_t r = dq4.div(k);
+      const int c = (int)(k - r * dq4.d) * 4, s = s0 + (int)r;
+      float x[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      if (s < S) {
+        const long long off = base + (long long)s * ss + c;
+        if (f32) {
+          const float4 q = __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(v) + off));
+          x[0] = q.x, x[1] = q.y, x[2] = q.z, x[3] = q.w;
+        } else {
+          const uint2 q = __ldg(reinterpret_cast<const uint2*>(
+              reinterpret_cast<const __nv_bfloat16*>(v) + off));
+          x[0] = bf16lo_to_f32(q.x), x[1] = bf16hi_to_f32(q.x);
+          x[2] = bf16lo_to_f32(q.y), x[3] = bf16hi_to_f32(q.y);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) tile[r * ld + c + e] = x[e];
+    }
+  } else {
+    for (int k = t; k < kVtRows * D; k += 256) {
+      const int r = k / D, c = k - r * D, s = s0 + r;
+      float x = 0.0f;
+      if (s < S) {
+        const long long off = base + (long long)s * ss + c;
         x = f32 ? reinterpret_cast<const float*>(v)[off]
                 : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(v)[off]);
-      } else if (d == D) {
-        x = 1.0f;
       }
+      tile[r * ld + c] = x;
     }
-    tile[r][tx] = x;
   }
   __syncthreads();
   const long long plane = BH * Dp * Sp;
-  for (int r = ty; r < 32; r += 8) {
-    const int d = d0 + r, s = s0 + tx;
-    if (d < Dp && s < Sp) {
-      uint16_t hi, lo;
-      split2(tile[tx][r], hi, lo);
-      const long long o = (bh * Dp + d) * Sp + s;
-      dst[o] = hi;
-      dst[plane + o] = lo;
+  for (int k = t; k < Dp * (kVtRows / 4); k += 256) {
+    const int d = k >> 4, j = (k & 15) * 4;
+    if (s0 + j >= Sp) continue;
+    float x[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int s = s0 + j + e;
+      x[e] = s >= S ? 0.0f : d < D ? tile[(j + e) * ld + d] : d == D ? 1.0f : 0.0f;
     }
+    const uint32_t h01 = pack_bf16x2(x[0], x[1]), h23 = pack_bf16x2(x[2], x[3]);
+    const uint32_t l01 = pack_bf16x2(x[0] - bf16lo_to_f32(h01), x[1] - bf16hi_to_f32(h01));
+    const uint32_t l23 = pack_bf16x2(x[2] - bf16lo_to_f32(h23), x[3] - bf16hi_to_f32(h23));
+    const long long o = ((long long)bh * Dp + d) * Sp + s0 + j;
+    *reinterpret_cast<uint2*>(dst + o) = make_uint2(h01, h23);
+    *reinterpret_cast<uint2*>(dst + plane + o) = make_uint2(l01, l23);
   }
 }
 
@@ -277,53 +343,83 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------ B: chunk scan
-// One thread per (b * kv head, column d, feature f), f fastest: the running
-// sum over the chunks of U^T, written before each chunk's own sum is added
-// (exclusive) as S^T planes st[plane][bh * n_chunks + c][d][f], starting
-// from the carried state (times its scale). Non-causal calls write only the
-// total, at c = 0. The total also goes to kv_out (d < D) / ks_out (d == D).
-// Chunk sums are loaded four chunks at a time so their loads overlap.
-__global__ void __launch_bounds__(256) lin_scan_chunks(LinTcParams p) {
+// One thread per (b * kv head, column d, feature pair f, f + 1), f fastest:
+// the running sum over the chunks of U^T, written before each chunk's own sum
+// is added (exclusive) as S^T planes st[plane][bh * n_chunks + c][d][f],
+// starting from the carried state (times its scale). Non-causal calls write
+// only the total, at c = 0. The total also goes to kv_out (d < D) / ks_out
+// (d == D). Chunk sums are loaded four chunks at a time (8 bytes per thread
+// and chunk) so their loads overlap; the planes take 4-byte stores. An odd
+// feature count leaves the last pair's second feature out.
+__global__ void __launch_bounds__(256) lin_scan_chunks(LinTcParams p, DivU32 dpair, DivU32 dcol) {
   const int Dp = p.Dp, Df = p.Df, D = p.D;
+  const int n_pair = (int)dpair.d;  // (Df + 1) / 2
   const long long per_bh = (long long)Dp * Df;
-  const long long n = (long long)p.B * p.Hkv * per_bh;
+  const uint32_t n = (uint32_t)((long long)p.B * p.Hkv * Dp * n_pair);
   const long long plane = (long long)p.B * p.Hkv * p.n_chunks * Dp * p.Dfp;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
-       i += (long long)gridDim.x * blockDim.x) {
-    const long long bh = i / per_bh;
-    const int e = (int)(i - bh * per_bh);
-    const int d = e / Df, f = e - d * Df;
+  const long long st_chunk = (long long)Dp * p.Dfp;
+  const bool even = (Df & 1) == 0;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const uint32_t row = dpair.div(i);  // bh * Dp + d
+    const int f = (int)(i - row * dpair.d) * 2;
+    const uint32_t bh = dcol.div(row);
+    const int d = (int)(row - bh * dcol.d);
+    const bool two = f + 1 < Df;
     const float scale = p.state_scale ? p.state_scale[bh] : 1.0f;
-    float run = 0.0f;
-    if (d < D && p.kv_in) run = p.kv_in[(bh * Df + f) * D + d] * scale;
-    if (d == D && p.ks_in) run = p.ks_in[bh * Df + f] * scale;
-    const float* u = p.u + bh * p.n_chunks * per_bh + e;
-    uint16_t* st = p.st + (bh * p.n_chunks * Dp + d) * p.Dfp + f;
-    const long long st_chunk = (long long)Dp * p.Dfp;
+    float run0 = 0.0f, run1 = 0.0f;
+    if (d < D && p.kv_in) {
+      run0 = p.kv_in[((long long)bh * Df + f) * D + d] * scale;
+      if (two) run1 = p.kv_in[((long long)bh * Df + f + 1) * D + d] * scale;
+    }
+    if (d == D && p.ks_in) {
+      run0 = p.ks_in[(long long)bh * Df + f] * scale;
+      if (two) run1 = p.ks_in[(long long)bh * Df + f + 1] * scale;
+    }
+    const float* u = p.u + (long long)bh * p.n_chunks * per_bh + (long long)d * Df + f;
+    uint16_t* st = p.st + ((long long)bh * p.n_chunks * Dp + d) * p.Dfp + f;
     for (int cb = 0; cb < p.n_chunks; cb += 4) {
-      float x[4];
+      float x0[4], x1[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) x[j] = cb + j < p.n_chunks ? u[(cb + j) * per_bh] : 0.0f;
+      for (int j = 0; j < 4; ++j) {
+        x0[j] = x1[j] = 0.0f;
+        if (cb + j < p.n_chunks) {
+          const float* uj = u + (cb + j) * per_bh;
+          if (even) {
+            const float2 t = __ldg(reinterpret_cast<const float2*>(uj));
+            x0[j] = t.x, x1[j] = t.y;
+          } else {
+            x0[j] = uj[0];
+            if (two) x1[j] = uj[1];
+          }
+        }
+      }
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         if (cb + j >= p.n_chunks) break;
         if (p.causal) {
-          uint16_t hi, lo;
-          split2(run, hi, lo);
-          st[(cb + j) * st_chunk] = hi;
-          st[plane + (cb + j) * st_chunk] = lo;
+          const uint32_t hi = pack_bf16x2(run0, run1);
+          const uint32_t lo = pack_bf16x2(run0 - bf16lo_to_f32(hi), run1 - bf16hi_to_f32(hi));
+          *reinterpret_cast<uint32_t*>(st + (cb + j) * st_chunk) = hi;
+          *reinterpret_cast<uint32_t*>(st + plane + (cb + j) * st_chunk) = lo;
         }
-        run += x[j];
+        run0 += x0[j];
+        run1 += x1[j];
       }
     }
     if (!p.causal) {
-      uint16_t hi, lo;
-      split2(run, hi, lo);
-      st[0] = hi;
-      st[plane] = lo;
+      const uint32_t hi = pack_bf16x2(run0, run1);
+      const uint32_t lo = pack_bf16x2(run0 - bf16lo_to_f32(hi), run1 - bf16hi_to_f32(hi));
+      *reinterpret_cast<uint32_t*>(st) = hi;
+      *reinterpret_cast<uint32_t*>(st + plane) = lo;
     }
-    if (d < D && p.kv_out) p.kv_out[(bh * Df + f) * D + d] = run;
-    if (d == D && p.ks_out) p.ks_out[bh * Df + f] = run;
+    if (d < D && p.kv_out) {
+      p.kv_out[((long long)bh * Df + f) * D + d] = run0;
+      if (two) p.kv_out[((long long)bh * Df + f + 1) * D + d] = run1;
+    }
+    if (d == D && p.ks_out) {
+      p.ks_out[(long long)bh * Df + f] = run0;
+      if (two) p.ks_out[(long long)bh * Df + f + 1] = run1;
+    }
   }
 }
 
@@ -584,7 +680,7 @@ struct PerfSmem {
 template <int kMode>
 __global__ void __launch_bounds__(kThreads)
     phi_perf_tc(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-                const __grid_constant__ CUtensorMap tm_phi, PerfTcParams p) {
+                PerfTcParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -667,13 +763,43 @@ __global__ void __launch_bounds__(kThreads)
       tc_fence_after();
       const float inv4 = rsqrtf(sqrtf((float)p.Dh));  // Dh^(-1/4)
       // |x'|^2 / 2 from the row's own planes (hi + lo recovers x to 2^-16).
+      // While every K step still has its own stage (head dims up to 128), the
+      // row is read from the staged tiles: 128 bytes per plane and step, 16-
+      // byte units at (unit ^ row % 8) under the 128-byte swizzle. The stage's
+      // full barrier (one completed phase) orders the TMA's writes before the
+      // reads. Larger head dims read the planes from global memory.
       float sq = 0.0f;
+      bool staged = kMode != 0 && n_k <= n_st;
+      for (int kb = 0; kb < n_k && staged; ++kb)
+        staged = warp_wait(bar_full + kb, 0, abort_flag, 93);
       if (s < p.S && kMode != 0) {
-        const uint16_t* xh = p.xp + ((long long)bh * p.S + s) * p.Dhp;
-        const uint16_t* xl = xh + BH * p.S * p.Dhp;
-        for (int d = 0; d < p.Dh; ++d) {
-          const float x = (bf16_val(xh[d]) + bf16_val(xl[d])) * inv4;
-          sq = fmaf(x, x, sq);
+        if (staged) {
+          for (int kb = 0; kb < n_k; ++kb) {
+            const uint8_t* xs = smem + kb * PerfSmem::stage_bytes() + row * 128;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              if (64 * kb + 8 * j >= p.Dh) break;
+              const uint4 h = *reinterpret_cast<const uint4*>(xs + ((j ^ (row & 7)) << 4));
+              const uint4 l = *reinterpret_cast<const uint4*>(xs + kX + ((j ^ (row & 7)) << 4));
+              const uint32_t hw[4] = {h.x, h.y, h.z, h.w}, lw[4] = {l.x, l.y, l.z, l.w};
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                if (64 * kb + 8 * j + e < p.Dh) {
+                  const float hv = e & 1 ? bf16hi_to_f32(hw[e / 2]) : bf16lo_to_f32(hw[e / 2]);
+                  const float lv = e & 1 ? bf16hi_to_f32(lw[e / 2]) : bf16lo_to_f32(lw[e / 2]);
+                  const float x = (hv + lv) * inv4;
+                  sq = fmaf(x, x, sq);
+                }
+              }
+            }
+          }
+        } else {
+          const uint16_t* xh = p.xp + ((long long)bh * p.S + s) * p.Dhp;
+          const uint16_t* xl = xh + BH * p.S * p.Dhp;
+          for (int d = 0; d < p.Dh; ++d) {
+            const float x = (bf16_val(xh[d]) + bf16_val(xl[d])) * inv4;
+            sq = fmaf(x, x, sq);
+          }
         }
         sq *= 0.5f;
       }
@@ -697,36 +823,70 @@ __global__ void __launch_bounds__(kThreads)
         // 32 features at a time: each lane puts its row's 32 values in the
         // warp's 32-row x 128-byte buffer (16-byte units XOR-swizzled by row
         // against bank conflicts), then the warp stores 4 whole 128-byte row
-        // segments per instruction.
+        // segments per instruction. The buffer is where this warp's own rows
+        // of the x hi plane were staged, which only this warp has read. With
+        // p.planes a row's 128 bytes are its 32 bf16 hi values, then the 32
+        // lo values, and go to the two planes as 64-byte runs.
         const float stab = kMode == 1 ? m : p.stab[bh];
         const float norm = rsqrtf((float)p.Df);
-        uint8_t* buf = out_stage + (warp - 2) * 32 * 128;
+        const long long plane_elems = BH * p.S * p.Dfp;
+        uint8_t* buf = out_stage + q * 32 * 128;
         const int row0 = s0 + 32 * q;
         for (int c0 = 0; c0 < Dfn && row0 < p.S; c0 += 32) {
           uint32_t r[32];
           ENL_TMEM_LD16(addr + c0, r);
           if (c0 + 16 < Dfn) {
             ENL_TMEM_LD16(addr + c0 + 16, (r + 16));
+          } else {
+#pragma unroll
+            for (int i = 16; i < 32; ++i) r[i] = 0u;
           }
+          // All 32 exponentials independent (no branch between them), then
+          // the columns past Df are zeroed by a select.
+          const int n_valid = p.Df - c0;
           float y[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            y[i] = expf(__uint_as_float(r[i]) * inv4 - sq - stab) * norm;
+          for (int i = 0; i < 32; ++i) {
+            const float e = expf(__uint_as_float(r[i]) * inv4 - sq - stab) * norm;
+            y[i] = i < n_valid ? e : 0.0f;
+          }
           __syncwarp();  // the previous chunk's reads of the buffer are done
+          if (p.planes) {
+            uint32_t hw[16], lw[16];
 #pragma unroll
-          for (int u = 0; u < 8; ++u)
-            *reinterpret_cast<float4*>(buf + lane * 128 + ((u ^ (lane & 7)) << 4)) =
-                make_float4(y[4 * u], y[4 * u + 1], y[4 * u + 2], y[4 * u + 3]);
+            for (int i = 0; i < 16; ++i) {
+              hw[i] = pack_bf16x2(y[2 * i], y[2 * i + 1]);
+              lw[i] = pack_bf16x2(y[2 * i] - bf16lo_to_f32(hw[i]),
+                                  y[2 * i + 1] - bf16hi_to_f32(hw[i]));
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              *reinterpret_cast<uint4*>(buf + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+                  make_uint4(hw[4 * u], hw[4 * u + 1], hw[4 * u + 2], hw[4 * u + 3]);
+              *reinterpret_cast<uint4*>(buf + lane * 128 + (((u + 4) ^ (lane & 7)) << 4)) =
+                  make_uint4(lw[4 * u], lw[4 * u + 1], lw[4 * u + 2], lw[4 * u + 3]);
+            }
+          } else {
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              *reinterpret_cast<float4*>(buf + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+                  make_float4(y[4 * u], y[4 * u + 1], y[4 * u + 2], y[4 * u + 3]);
+          }
           __syncwarp();
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
             const int piece = 32 * k + lane, rr = piece / 8, u = piece % 8;
-            const int col = c0 + 4 * u;
-            if (row0 + rr < p.S && col < p.Df) {
-              const float4 v4 =
-                  *reinterpret_cast<const float4*>(buf + rr * 128 + ((u ^ (rr & 7)) << 4));
-              *reinterpret_cast<float4*>(p.phi + ((long long)bh * p.S + row0 + rr) * p.Df + col) =
-                  v4;
+            if (row0 + rr >= p.S) continue;
+            const uint4 v4 = *reinterpret_cast<const uint4*>(buf + rr * 128 + ((u ^ (rr & 7)) << 4));
+            const long long row = (long long)bh * p.S + row0 + rr;
+            if (p.planes) {
+              const int col = c0 + 8 * (u & 3);  // 8 features per 16-byte unit
+              if (col < p.Df)
+                *reinterpret_cast<uint4*>(p.planes + (u >> 2) * plane_elems + row * p.Dfp + col) =
+                    v4;
+            } else {
+              const int col = c0 + 4 * u;
+              if (col < p.Df) *reinterpret_cast<uint4*>(p.phi + row * p.Df + col) = v4;
             }
           }
         }
@@ -742,37 +902,45 @@ __global__ void __launch_bounds__(kThreads)
 }
 
 // x[b, s, h, :] (strided, bf16 or fp32) -> planes [plane][B * H][S][Dhp],
-// four elements per thread (Dh % 4 == 0, 8- or 16-byte aligned rows).
+// four elements per thread (Dh % 4 == 0, 8- or 16-byte aligned rows, at most
+// 2^31 groups of four: the flat index splits by multiply-high divisions),
+// four loads in flight per thread before the first store.
 __global__ void perf_prep_x4(const void* __restrict__ x, long long sb, long long ss,
-                             long long sh, int f32, int B, int S, int H, int Dh, int Dhp,
-                             uint16_t* __restrict__ dst) {
-  const int q4 = Dh / 4;
-  const long long n = (long long)B * H * S * q4;
+                             long long sh, int f32, DivU32 dq4, DivU32 ds, DivU32 dh, int B,
+                             int Dhp, uint16_t* __restrict__ dst) {
+  const int S = (int)ds.d, H = (int)dh.d;
+  const uint32_t n = (uint32_t)((long long)B * H * S * dq4.d);
   const long long plane = (long long)B * H * S * Dhp;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int d = (int)(i % q4) * 4;
-    long long r = i / q4;
-    const int s = (int)(r % S);
-    r /= S;
-    const int h = (int)(r % H), b = (int)(r / H);
-    const long long off = b * sb + (long long)s * ss + (long long)h * sh + d;
-    float v[4];
-    if (f32) {
-      const float4 t = __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + off));
-      v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
-    } else {
-      const uint2 t = __ldg(reinterpret_cast<const uint2*>(
-          reinterpret_cast<const __nv_bfloat16*>(x) + off));
-      v[0] = bf16lo_to_f32(t.x), v[1] = bf16hi_to_f32(t.x);
-      v[2] = bf16lo_to_f32(t.y), v[3] = bf16hi_to_f32(t.y);
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t i0 = blockIdx.x * blockDim.x + threadIdx.x; i0 < n; i0 += 4 * stride) {
+    float4 v[4];
+    long long o[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const uint32_t i = i0 + u * stride;
+      if (i >= n) break;
+      const uint32_t r = dq4.div(i);
+      const int d = (int)(i - r * dq4.d) * 4;
+      const uint32_t bh = ds.div(r);
+      const int s = (int)(r - bh * ds.d);
+      const uint32_t b = dh.div(bh);
+      const int h = (int)(bh - b * dh.d);
+      const long long off = (long long)b * sb + (long long)s * ss + (long long)h * sh + d;
+      o[u] = ((long long)bh * S + s) * Dhp + d;
+      if (f32) {
+        v[u] = __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + off));
+      } else {
+        const uint2 t = __ldg(reinterpret_cast<const uint2*>(
+            reinterpret_cast<const __nv_bfloat16*>(x) + off));
+        v[u] = make_float4(bf16lo_to_f32(t.x), bf16hi_to_f32(t.x), bf16lo_to_f32(t.y),
+                           bf16hi_to_f32(t.y));
+      }
     }
-    const uint32_t h01 = pack_bf16x2(v[0], v[1]), h23 = pack_bf16x2(v[2], v[3]);
-    const uint32_t l01 = pack_bf16x2(v[0] - bf16lo_to_f32(h01), v[1] - bf16hi_to_f32(h01));
-    const uint32_t l23 = pack_bf16x2(v[2] - bf16lo_to_f32(h23), v[3] - bf16hi_to_f32(h23));
-    const long long o = (((long long)b * H + h) * S + s) * Dhp + d;
-    *reinterpret_cast<uint2*>(dst + o) = make_uint2(h01, h23);
-    *reinterpret_cast<uint2*>(dst + plane + o) = make_uint2(l01, l23);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (i0 + u * stride >= n) break;
+      store_split_quad(v[u], dst + o[u], plane);
+    }
   }
 }
 
@@ -824,9 +992,10 @@ cudaError_t launch_perf_prep(const void* x, long long sb, long long ss, long lon
   const long long n = (long long)p.B * p.H * p.S * p.Dh;
   const bool vec = p.Dh % 4 == 0 && ((sb | ss | sh) % 4) == 0 &&
                    (reinterpret_cast<uintptr_t>(x) % (f32 ? 16 : 8)) == 0;
-  if (n > 0 && vec)
+  if (n > 0 && vec && n / 4 <= (1ll << 31))
     perf_prep_x4<<<(int)std::min<long long>((n / 4 + 255) / 256, 148ll * 16), 256, 0, stream>>>(
-        x, sb, ss, sh, f32, p.B, p.S, p.H, p.Dh, p.Dhp, p.xp);
+        x, sb, ss, sh, f32, DivU32::make((uint32_t)(p.Dh / 4)), DivU32::make((uint32_t)p.S),
+        DivU32::make((uint32_t)p.H), p.B, p.Dhp, p.xp);
   else if (n > 0)
     perf_prep_x<<<(int)std::min<long long>((n + 255) / 256, 148ll * 16), 256, 0, stream>>>(
         x, sb, ss, sh, f32, p.B, p.S, p.H, p.Dh, p.Dhp, p.xp);
@@ -836,8 +1005,8 @@ cudaError_t launch_perf_prep(const void* x, long long sb, long long ss, long lon
   return cudaGetLastError();
 }
 
-cudaError_t launch_perf_tc(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& tphi,
-                           const PerfTcParams& p, int mode, cudaStream_t stream) {
+cudaError_t launch_perf_tc(const CUtensorMap& tx, const CUtensorMap& tw, const PerfTcParams& p,
+                           int mode, cudaStream_t stream) {
   using namespace lintc;
   static bool configured[64] = {};
   int dev = 0;
@@ -856,17 +1025,17 @@ cudaError_t launch_perf_tc(const CUtensorMap& tx, const CUtensorMap& tw, const C
   const dim3 grid((p.S + 127) / 128, p.B * p.H);
   const int smem = PerfSmem::total(p.Dh);
   switch (mode) {
-    case 0: phi_perf_tc<0><<<grid, kThreads, smem, stream>>>(tx, tw, tphi, p); break;
-    case 1: phi_perf_tc<1><<<grid, kThreads, smem, stream>>>(tx, tw, tphi, p); break;
-    default: phi_perf_tc<2><<<grid, kThreads, smem, stream>>>(tx, tw, tphi, p); break;
+    case 0: phi_perf_tc<0><<<grid, kThreads, smem, stream>>>(tx, tw, p); break;
+    case 1: phi_perf_tc<1><<<grid, kThreads, smem, stream>>>(tx, tw, p); break;
+    default: phi_perf_tc<2><<<grid, kThreads, smem, stream>>>(tx, tw, p); break;
   }
   return cudaGetLastError();
 }
 
 cudaError_t launch_perf_tc_maps(const CUtensorMap& tx, const CUtensorMap& tw,
-                                const CUtensorMap& tphi, const PerfTcParams& p, int global_stab,
-                                const float* stab_floor, cudaStream_t stream) {
-  if (!global_stab) return launch_perf_tc(tx, tw, tphi, p, 1, stream);
+                                const PerfTcParams& p, int global_stab, const float* stab_floor,
+                                cudaStream_t stream) {
+  if (!global_stab) return launch_perf_tc(tx, tw, p, 1, stream);
   // The CUDA-core kernels' stabilizer helpers: ordered-int init from the
   // floor, and the conversion back to floats after the atomic-max pass.
   PhiParams q{};
@@ -876,26 +1045,42 @@ cudaError_t launch_perf_tc_maps(const CUtensorMap& tx, const CUtensorMap& tw,
   q.stab_floor = stab_floor;
   const int nb = std::max(1, (p.B * p.H + 255) / 256);
   phi_init_kernel<<<nb, 256, 0, stream>>>(q);
-  cudaError_t e = launch_perf_tc(tx, tw, tphi, p, 0, stream);
+  cudaError_t e = launch_perf_tc(tx, tw, p, 0, stream);
   if (e != cudaSuccess) return e;
   phi_decode_kernel<<<nb, 256, 0, stream>>>(q);
-  return launch_perf_tc(tx, tw, tphi, p, 2, stream);
+  return launch_perf_tc(tx, tw, p, 2, stream);
+}
+
+cudaError_t launch_rows_planes(const float* src, long long R, int Df, int Dfp, uint16_t* dst,
+                               cudaStream_t stream) {
+  using namespace lintc;
+  const long long n = (R * Df + 3) / 4;
+  if (n <= 0) return cudaSuccess;
+  lin_prep_rows<<<(int)std::min<long long>((n + 255) / 256, 148ll * 16), 256, 0, stream>>>(
+      src, R, Df, Dfp, DivU32::make((uint32_t)std::max(1, Df / 4)), dst);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_lin_prep(const float* phi_q, const float* phi_k, const void* v, long long v_sb,
                             long long v_ss, long long v_sh, int v_f32, const LinTcParams& p,
                             uint16_t* qp, uint16_t* kp, uint16_t* vt, cudaStream_t stream) {
   using namespace lintc;
-  const long long BHq = (long long)p.B * p.H, BHk = (long long)p.B * p.Hkv;
-  const long long rq = BHq * p.S, rk = BHk * p.S;
-  auto blocks = [](long long n) { return (int)std::min<long long>((n + 255) / 256, 148ll * 16); };
-  if (rq * p.Df > 0) lin_prep_rows<<<blocks(rq * p.Df), 256, 0, stream>>>(phi_q, rq, p.Df, p.Dfp, qp);
-  if (rk * p.Df > 0) lin_prep_rows<<<blocks(rk * p.Df), 256, 0, stream>>>(phi_k, rk, p.Df, p.Dfp, kp);
-  const dim3 tb(32, 8);
+  const long long BHk = (long long)p.B * p.Hkv;
+  // phi_q / phi_k are null when the caller passed planes already.
+  cudaError_t e = cudaSuccess;
+  if (phi_q) e = launch_rows_planes(phi_q, (long long)p.B * p.H * p.S, p.Df, p.Dfp, qp, stream);
+  if (e == cudaSuccess && phi_k) e = launch_rows_planes(phi_k, BHk * p.S, p.Df, p.Dfp, kp, stream);
+  if (e != cudaSuccess) return e;
   if (BHk > 0 && p.S > 0) {
-    const dim3 gv((p.Sp + 31) / 32, (p.Dp + 31) / 32, (unsigned)BHk);
-    lin_prep_vt<<<gv, tb, 0, stream>>>(v, v_sb, v_ss, v_sh, v_f32, p.Hkv, p.S, p.D, p.Dp, p.Sp,
-                                      BHk, vt);
+    const int n_sb = (p.Sp + kVtRows - 1) / kVtRows;
+    if (p.D > kVtMaxD || p.Sp % 4 != 0 || n_sb > 65535) return cudaErrorInvalidValue;
+    const int esz = v_f32 ? 4 : 2;
+    const int vec = p.D % 4 == 0 && ((v_sb | v_ss | v_sh) % 4) == 0 &&
+                    (reinterpret_cast<uintptr_t>(v) % (4 * esz)) == 0;
+    const dim3 gv((unsigned)BHk, n_sb);
+    lin_prep_vt<<<gv, 256, 0, stream>>>(v, v_sb, v_ss, v_sh, v_f32, p.Hkv, p.S, p.D, p.Dp, p.Sp,
+                                       BHk, vec, DivU32::make((uint32_t)std::max(1, p.D / 4)),
+                                       vt);
   }
   return cudaGetLastError();
 }
@@ -921,8 +1106,11 @@ cudaError_t launch_lin_tc(const CUtensorMap& tq, const CUtensorMap& tk, const CU
     lin_state_chunk<<<ga, kThreads, StateSmem::total(p.Dp), stream>>>(tk, tvt, p);
   }
   if (BHk > 0) {
-    const long long n = BHk * p.Dp * p.Df;
-    lin_scan_chunks<<<(int)std::min<long long>((n + 255) / 256, 148ll * 32), 256, 0, stream>>>(p);
+    const int n_pair = (p.Df + 1) / 2;
+    const long long n = BHk * p.Dp * n_pair;
+    if (n > (1ll << 31)) return cudaErrorInvalidValue;
+    lin_scan_chunks<<<(int)std::min<long long>((n + 255) / 256, 148ll * 32), 256, 0, stream>>>(
+        p, DivU32::make((uint32_t)n_pair), DivU32::make((uint32_t)p.Dp));
   }
   if (p.n_chunks > 0 && BHq > 0) {
     const dim3 gc((unsigned)BHq, p.n_chunks);

@@ -523,15 +523,25 @@ def rope_(x: torch.Tensor, cos_table: torch.Tensor, sin_table: torch.Tensor,
 _PHI_KERNELS = {"linear": nat.ENL_PHI_LINEAR, "performer": nat.ENL_PHI_PERFORMER}
 
 
+def linear_planes_ok(head_dim: int, num_features: int) -> bool:
+    """Whether linear_attention takes phi planes for these sizes (its
+    tensor-core path)."""
+    return bool(nat.load().enl_linear_planes_ok(int(head_dim), int(num_features)))
+
+
 def linear_feature_map(x: torch.Tensor, kernel: str, omega: Optional[torch.Tensor] = None, *,
-                       global_stab: bool = False, stab_floor: Optional[torch.Tensor] = None):
+                       global_stab: bool = False, stab_floor: Optional[torch.Tensor] = None,
+                       planes: bool = False):
     """phi(x) of the linearized attention kernels (nn/attention_kernels.py:58-74).
 
     x: (B, S, H, Dh) bf16/fp32 head view. kernel "linear" (elu + 1) or
     "performer" with omega (Df, Dh) fp32. Returns (phi (B, H, S, Df) fp32,
     stab (B, H) fp32 or None): with global_stab (keys) one stabilizer per
     (b, h), the max of w.x' over every row and stab_floor; otherwise (queries)
-    each row's own max."""
+    each row's own max. With planes, phi comes back as its bf16 hi/lo planes
+    (2, B, H, S, Dfp), Dfp = Df rounded up to 8, hi = bf16(phi) and
+    lo = bf16(phi - hi): the operand layout linear_attention reads on its
+    tensor-core path."""
     if kernel not in _PHI_KERNELS:
         raise ValueError(f"Unknown attention feature map: {kernel!r}")
     _require_cuda("x", x)
@@ -544,7 +554,10 @@ def linear_feature_map(x: torch.Tensor, kernel: str, omega: Optional[torch.Tenso
         if omega.dim() != 2 or omega.shape[1] != Dh or not omega.is_contiguous():
             raise ValueError(f"omega must be a contiguous (num_features, {Dh}) fp32 tensor")
     Df = omega.shape[0] if performer else Dh
-    phi = torch.empty((B, H, S, Df), device=x.device, dtype=torch.float32)
+    if planes:
+        phi = torch.empty((2, B, H, S, (Df + 7) // 8 * 8), device=x.device, dtype=torch.bfloat16)
+    else:
+        phi = torch.empty((B, H, S, Df), device=x.device, dtype=torch.float32)
     stab = None
     if performer and global_stab:
         stab = torch.empty((B, H), device=x.device, dtype=torch.float32)
@@ -562,7 +575,10 @@ def linear_feature_map(x: torch.Tensor, kernel: str, omega: Optional[torch.Tenso
     a.global_stab = int(performer and global_stab)
     a.stab_floor = _ptr(stab_floor) if stab is not None else None
     a.stab = _ptr(stab)
-    a.phi = phi.data_ptr()
+    if planes:
+        a.phi, a.phi_planes = None, phi.data_ptr()
+    else:
+        a.phi = phi.data_ptr()
     lib = nat.load()
     need = int(lib.enl_phi_workspace_bytes(ctypes.byref(a)))
     ws = None
@@ -576,24 +592,43 @@ def linear_feature_map(x: torch.Tensor, kernel: str, omega: Optional[torch.Tenso
 def linear_attention(phi_q: torch.Tensor, phi_k: torch.Tensor, v: torch.Tensor, *,
                      causal: bool, state=None, state_scale: Optional[torch.Tensor] = None,
                      return_state: bool = False, out_dtype: torch.dtype = torch.float32,
-                     eps: float = 1e-20):
+                     eps: float = 1e-20, num_features: Optional[int] = None):
     """Linear attention over feature-mapped queries/keys
     (nn/attention_kernels.py:119-143). phi_q (B, H, S, Df), phi_k (B, Hkv, S, Df)
-    fp32; v (B, S, Hkv, D) bf16/fp32 head view. Causal: prefix sums, starting
-    from state = (kv (B, Hkv, Df, D), ksum (B, Hkv, Df)) times state_scale
-    (B, Hkv) when given; with return_state the sums after the last row are
-    returned too. Returns out (B, S, H, D) [, (kv, ksum)]."""
+    fp32, or both as the bf16 planes linear_feature_map(planes=True) returns
+    (2, B, H, S, Dfp) / (2, B, Hkv, S, Dfp) with num_features=Df (sizes where
+    linear_planes_ok holds); v (B, S, Hkv, D) bf16/fp32 head view. Causal:
+    prefix sums, starting from state = (kv (B, Hkv, Df, D), ksum (B, Hkv, Df))
+    times state_scale (B, Hkv) when given; with return_state the sums after the
+    last row are returned too. Returns out (B, S, H, D) [, (kv, ksum)]."""
+    planes = phi_q.dim() == 5
     for name, t in (("phi_q", phi_q), ("phi_k", phi_k)):
-        _require_cuda(name, t, torch.float32)
-        if t.dim() != 4 or not t.is_contiguous():
-            raise ValueError(f"{name} must be a contiguous 4-D fp32 tensor")
+        if planes:
+            _require_cuda(name, t, torch.bfloat16)
+            if t.dim() != 5 or t.shape[0] != 2 or not t.is_contiguous():
+                raise ValueError(f"{name} planes must be a contiguous (2, B, H, S, Dfp) bf16 tensor")
+        else:
+            _require_cuda(name, t, torch.float32)
+            if t.dim() != 4 or not t.is_contiguous():
+                raise ValueError(f"{name} must be a contiguous 4-D fp32 tensor")
     _require_cuda("v", v)
     if v.dtype not in _DTYPES or v.dim() != 4:
         raise ValueError("v must be a 4-D bf16 or fp32 tensor (batch, seq, kv_heads, head_dim)")
-    B, H, S, Df = phi_q.shape
-    _, Hkv, Sk, Dfk = phi_k.shape
+    if planes:
+        if num_features is None:
+            raise ValueError("phi planes need num_features")
+        B, H, S, Dfp = phi_q.shape[1:]
+        _, _, Hkv, Sk, Dfpk = phi_k.shape
+        Df, Dfk = int(num_features), int(num_features)
+        if Dfp != (Df + 7) // 8 * 8 or Dfpk != Dfp:
+            raise ValueError(f"phi planes of width {Dfp}/{Dfpk} do not hold {Df} features")
+    else:
+        B, H, S, Df = phi_q.shape
+        _, Hkv, Sk, Dfk = phi_k.shape
     D = v.shape[3]
-    if (phi_k.shape[0], Sk, Dfk) != (B, S, Df) or tuple(v.shape[:3]) != (B, S, Hkv):
+    if planes and not linear_planes_ok(D, Df):
+        raise ValueError(f"phi planes need linear_planes_ok({D}, {Df})")
+    if (phi_k.shape[-4], Sk, Dfk) != (B, S, Df) or tuple(v.shape[:3]) != (B, S, Hkv):
         raise ValueError(f"shape mismatch: phi_q {tuple(phi_q.shape)}, phi_k "
                          f"{tuple(phi_k.shape)}, v {tuple(v.shape)}")
     if (state is not None or return_state) and not causal:
@@ -612,7 +647,10 @@ def linear_attention(phi_q: torch.Tensor, phi_k: torch.Tensor, v: torch.Tensor, 
             _require_cuda("state_scale", state_scale, torch.float32, last_contiguous=False)
             state_scale = state_scale.reshape(B, Hkv).contiguous()
     a = nat.LinearArgs()
-    a.phi_q, a.phi_k = phi_q.data_ptr(), phi_k.data_ptr()
+    if planes:
+        a.phi_q_planes, a.phi_k_planes = phi_q.data_ptr(), phi_k.data_ptr()
+    else:
+        a.phi_q, a.phi_k = phi_q.data_ptr(), phi_k.data_ptr()
     a.v = v.data_ptr()
     a.v_stride_b, a.v_stride_s, a.v_stride_h = v.stride(0), v.stride(1), v.stride(2)
     a.v_dtype = _DTYPES[v.dtype]

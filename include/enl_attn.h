@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define ENL_ABI_VERSION 6
+#define ENL_ABI_VERSION 7
 
 /* Status codes. The Python binding maps INVALID/UNSUPPORTED to ValueError
  * (the reference raises ValueError for bad layer configurations,
@@ -271,13 +271,21 @@ typedef struct enl_phi_args {
   const float* stab_floor; /* global: optional lower bound per (b, h) */
   float* stab;             /* global: receives the stabilizer per (b, h) */
   float* phi;              /* out (batch, num_heads, seq, Df) fp32, contiguous;
-                              Df = head_dim (linear) or num_features */
-  void* workspace;         /* performer: >= enl_phi_workspace_bytes(), 256-byte aligned */
+                              Df = head_dim (linear) or num_features; NULL when
+                              phi_planes is given */
+  void* workspace;         /* >= enl_phi_workspace_bytes(), 256-byte aligned */
   size_t workspace_bytes;
+  void* phi_planes;        /* optional out instead of phi: bf16 planes
+                              [2][batch * num_heads][seq][Dfp], hi = bf16(phi) then
+                              lo = bf16(phi - hi), Dfp = Df rounded up to 8,
+                              16-byte aligned: the operand layout of the
+                              tensor-core enl_linear_attention (phi_q_planes /
+                              phi_k_planes), so that phi makes no fp32 round trip */
 } enl_phi_args;
 
 /* Workspace bytes enl_linear_feature_map needs: the bf16 hi/lo planes of x
- * and omega for the tensor-core Performer map (num_features <= 256); 0
+ * and omega for the tensor-core Performer map (num_features <= 256), and an
+ * fp32 phi when planes are asked of a map that writes fp32 only; 0
  * otherwise. */
 size_t enl_phi_workspace_bytes(const enl_phi_args* args);
 
@@ -312,6 +320,12 @@ typedef struct enl_linear_args {
   float eps; /* denominator guard, 1e-20 in the reference */
   void* workspace; /* device scratch for the segmented causal pass, */
   size_t workspace_bytes; /* >= enl_linear_workspace_bytes() */
+  /* Optional, both or neither, instead of phi_q / phi_k (which may then be
+   * NULL): their bf16 hi/lo planes as enl_phi_args.phi_planes writes them,
+   * [2][batch * num_heads][seq][Dfp] and [2][batch * num_kv_heads][seq][Dfp].
+   * Only where enl_linear_planes_ok(head_dim, num_features). */
+  const void* phi_q_planes;
+  const void* phi_k_planes;
 } enl_linear_args;
 
 /* o = phi(Q) S_kv / (phi(Q) . s_k + eps) with S_kv = sum phi(k) v^T and
@@ -319,6 +333,9 @@ typedef struct enl_linear_args {
  * (nn/attention_kernels.py:119-143). num_features <= enl_linear_max_features(). */
 int enl_linear_attention(const enl_linear_args* args, void* stream);
 int enl_linear_max_features(void);
+/* 1 when enl_linear_attention runs these sizes on the tensor pipe and takes
+ * phi planes (head_dim <= 128, num_features <= 1024), else 0. */
+int enl_linear_planes_ok(int32_t head_dim, int32_t num_features);
 
 /* Workspace bytes enl_linear_attention needs for these arguments: causal
  * calls long enough to run in parallel sequence segments keep one partial

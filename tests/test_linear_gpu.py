@@ -31,7 +31,8 @@ def _np(t):
 
 
 @pytest.mark.parametrize("kernel", ["linear", "performer"])
-@pytest.mark.parametrize("Dh,Df", [(8, 24), (32, 128), (64, 256), (128, 512)])
+@pytest.mark.parametrize("Dh,Df", [(8, 24), (32, 128), (64, 256), (128, 256), (192, 256),
+                                   (128, 512)])
 def test_feature_map_matches_oracle(cuda, kernel, Dh, Df):
     from enilnets_b200 import _native, kernels
     rng = np.random.RandomState(Dh + Df)
@@ -67,6 +68,8 @@ def torch_sync():
 @pytest.mark.parametrize("S,D,Df,H,Hkv", [
     (1, 8, 8, 2, 2), (5, 40, 40, 4, 2), (16, 32, 32, 2, 1), (37, 64, 256, 4, 4),
     (300, 128, 128, 2, 2), (129, 72, 512, 4, 1),
+    # odd head dim (scalar V loads) and odd feature count (last feature pair half used)
+    (45, 37, 33, 2, 1),
     # long enough for the causal pass to run in parallel sequence segments
     (1500, 64, 96, 4, 2), (2048, 32, 32, 1, 1)])
 def test_linear_attention_matches_oracle(cuda, causal, S, D, Df, H, Hkv):
@@ -222,3 +225,57 @@ def test_segmented_carried_state_equals_one_pass(cuda, S, cut):
     ref, _, _ = lr.linear_attention(qp, np.repeat(kp, 2, axis=1),
                                     np.repeat(v.transpose(0, 2, 1, 3), 2, axis=1), True)
     assert np.max(np.abs(_np(full).transpose(0, 2, 1, 3) - ref)) <= 1e-4
+
+
+def _split_planes(phi):
+    """fp32 (B, H, S, Df) -> its bf16 (hi, lo) planes, as the kernels write them."""
+    import torch
+    hi = phi.to(torch.bfloat16)
+    return torch.stack([hi, (phi - hi.float()).to(torch.bfloat16)])
+
+
+@pytest.mark.parametrize("kernel,Dh,Df", [
+    ("linear", 64, 64), ("linear", 36, 36),        # vectorised map, planes written directly
+    ("linear", 6, 6),                              # scalar map: fp32 in the workspace, then split
+    ("performer", 64, 256), ("performer", 32, 36),  # tensor-core map (36: a half-used 16-byte unit)
+    ("performer", 64, 512)])                       # CUDA-core map, then split
+def test_feature_map_planes_equal_split_fp32(cuda, kernel, Dh, Df):
+    """The planes a map writes are exactly bf16(phi), bf16(phi - bf16(phi)) of
+    its fp32 phi, and linear attention over them is bit-identical to the fp32
+    call (the same planes reach the same kernels)."""
+    import torch
+    from enilnets_b200 import _native, kernels
+    rng = np.random.RandomState(Dh * 7 + Df)
+    B, S, H = 2, 133, 2
+    x, xk = _t(rng.standard_normal((B, S, H, Dh))), _t(rng.standard_normal((B, S, H, Dh)))
+    v = _t(rng.standard_normal((B, S, H, 40)))
+    om = _t(lr.make_projection(Df, Dh, np.random.RandomState(Dh))) if kernel == "performer" \
+        else None
+    q32, _ = kernels.linear_feature_map(x, kernel, om)
+    qpl, _ = kernels.linear_feature_map(x, kernel, om, planes=True)
+    k32, st32 = kernels.linear_feature_map(xk, kernel, om, global_stab=True)
+    kpl, stpl = kernels.linear_feature_map(xk, kernel, om, global_stab=True, planes=True)
+    Dfp = (Df + 7) // 8 * 8
+    assert tuple(qpl.shape) == (2, B, H, S, Dfp) and qpl.dtype == torch.bfloat16
+    assert torch.equal(qpl[..., :Df], _split_planes(q32))
+    assert torch.equal(kpl[..., :Df], _split_planes(k32))
+    if st32 is not None:
+        assert torch.equal(st32, stpl)
+    o32 = kernels.linear_attention(q32, k32, v, causal=True)
+    opl = kernels.linear_attention(qpl, kpl, v, causal=True, num_features=Df)
+    torch_sync()
+    _native.raise_on_device_error()
+    assert torch.equal(o32, opl)
+
+
+def test_linear_attention_planes_argument_errors(cuda):
+    import torch
+    from enilnets_b200 import kernels
+    x = _t(np.random.RandomState(0).standard_normal((1, 16, 2, 32)))
+    v = _t(np.random.RandomState(1).standard_normal((1, 16, 2, 32)))
+    qpl, _ = kernels.linear_feature_map(x, "linear", planes=True)
+    with pytest.raises(ValueError, match="num_features"):
+        kernels.linear_attention(qpl, qpl, v, causal=True)
+    with pytest.raises(ValueError, match="do not hold"):
+        kernels.linear_attention(qpl, qpl, v, causal=True, num_features=20)
+    assert not kernels.linear_planes_ok(160, 32) and kernels.linear_planes_ok(128, 1024)
