@@ -1097,6 +1097,7 @@ int enl_linear_feature_map(const enl_phi_args* a, void* stream) {
     t.stab = a->stab;
     t.phi = a->phi_planes ? nullptr : a->phi;
     t.planes = reinterpret_cast<uint16_t*>(a->phi_planes);
+    if (int st_sm = sm_count(&t.n_sm)) return st_sm;
     cudaError_t e = enl::launch_perf_prep(a->x, a->x_stride_b, a->x_stride_s, a->x_stride_h,
                                           a->in_dtype == ENL_DTYPE_FP32, a->omega, t, wp, s);
     if (e != cudaSuccess) return cuda_fail(e, "enl_linear_feature_map: prep launch");

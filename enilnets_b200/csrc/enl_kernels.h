@@ -271,6 +271,7 @@ struct PerfTcParams {
   float* phi;        // (B, H, S, Df) fp32 out, or null when planes is set
   uint16_t* planes;  // [2][B * H][S][Dfp] bf16 hi/lo planes out
   int Dfp;
+  int n_sm;          // SMs of the device (grid of the persistent form)
 };
 bool perf_tc_supported(int Dh, int Df);
 cudaError_t launch_perf_prep(const void* x, long long sb, long long ss, long long sh, int f32,

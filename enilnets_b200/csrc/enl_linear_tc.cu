@@ -669,6 +669,161 @@ __global__ void __launch_bounds__(kThreads, 2)
 // stabilizer. kMode 0: the tile's maximum into stab[b * H + h] (ordered-int
 // atomic max); 1: each row's own maximum (queries); 2: stab[b * H + h] (keys).
 // Operands: xp[plane][B * H][S][Dhp] (row planes of the head view), wp[plane][Df][Dhp].
+// One tile's epilogue for one warp: rows 32q..32q+31 of the 128-row tile at
+// s0 of head bh, accumulator columns at addr (this warp's lane quarter).
+// xs: the staged x tile (hi plane at 0, lo plane at kPerfX, one 64-wide K
+// step per xs_step bytes), or null to read the planes from global memory.
+// buf: the warp's 32-row x 128-byte staging buffer. xs_release (nullable):
+// a barrier the warp's lane 0 arrives on once the row norms are read.
+constexpr int kPerfX = 128 * 128;  // bytes of one plane of a 64-wide K step of x
+
+template <int kMode>
+__device__ __forceinline__ void perf_tile_epilogue(const PerfTcParams& p, uint32_t addr,
+                                                   const uint8_t* xs, int xs_step, int bh,
+                                                   int s0, int q, int lane, uint8_t* buf,
+                                                   uint64_t* xs_release = nullptr) {
+  const int row = 32 * q + lane, s = s0 + row;
+  const long long BH = (long long)p.B * p.H;
+  const int n_k = (p.Dh + 63) / 64;
+  const int Dfn = (p.Df + 15) / 16 * 16;
+  const float inv4 = rsqrtf(sqrtf((float)p.Dh));  // Dh^(-1/4)
+  // |x'|^2 / 2 from the row's own planes (hi + lo recovers x to 2^-16):
+  // 128 bytes per plane and K step, 16-byte units at (unit ^ row % 8) under
+  // the 128-byte swizzle.
+  float sq = 0.0f;
+  if (s < p.S && kMode != 0) {
+    if (xs) {
+      for (int kb = 0; kb < n_k; ++kb) {
+        const uint8_t* xr = xs + kb * xs_step + row * 128;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (64 * kb + 8 * j >= p.Dh) break;
+          const uint4 h = *reinterpret_cast<const uint4*>(xr + ((j ^ (row & 7)) << 4));
+          const uint4 l = *reinterpret_cast<const uint4*>(xr + kPerfX + ((j ^ (row & 7)) << 4));
+          const uint32_t hw[4] = {h.x, h.y, h.z, h.w}, lw[4] = {l.x, l.y, l.z, l.w};
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            if (64 * kb + 8 * j + e < p.Dh) {
+              const float hv = e & 1 ? bf16hi_to_f32(hw[e / 2]) : bf16lo_to_f32(hw[e / 2]);
+              const float lv = e & 1 ? bf16hi_to_f32(lw[e / 2]) : bf16lo_to_f32(lw[e / 2]);
+              const float x = (hv + lv) * inv4;
+              sq = fmaf(x, x, sq);
+            }
+          }
+        }
+      }
+    } else {
+      const uint16_t* xh = p.xp + ((long long)bh * p.S + s) * p.Dhp;
+      const uint16_t* xl = xh + BH * p.S * p.Dhp;
+      for (int d = 0; d < p.Dh; ++d) {
+        const float x = (bf16_val(xh[d]) + bf16_val(xl[d])) * inv4;
+        sq = fmaf(x, x, sq);
+      }
+    }
+    sq *= 0.5f;
+  }
+  if (xs_release) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(xs_release);
+  }
+  // The row maximum (mode 0 and 1): one pass over the accumulator.
+  float m = -INFINITY;
+  if (kMode != 2) {
+    for (int c0 = 0; c0 < Dfn; c0 += 32) {
+      uint32_t r[32];
+      if (c0 + 32 <= Dfn) {
+        ENL_TMEM_LD32(addr + c0, r, 0);
+      } else {
+        ENL_TMEM_LD16(addr + c0, r);
+#pragma unroll
+        for (int i = 16; i < 32; ++i) r[i] = __float_as_uint(-INFINITY);
+      }
+      const int n_valid = p.Df - c0;
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < n_valid) m = fmaxf(m, __uint_as_float(r[i]));
+    }
+    m *= inv4;
+    if (s >= p.S) m = -INFINITY;
+  }
+  if (kMode == 0) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0 && m > -INFINITY) atomicMax(reinterpret_cast<int*>(p.stab) + bh, ord_enc(m));
+    return;
+  }
+  // 32 features at a time: each lane puts its row's 32 values in the warp's
+  // 32-row x 128-byte buffer (16-byte units XOR-swizzled by row against bank
+  // conflicts), then the warp stores 4 whole 128-byte row segments per
+  // instruction. With p.planes a row's 128 bytes are its 32 bf16 hi values,
+  // then the 32 lo values, and go to the two planes as 64-byte runs.
+  // exp(a inv4 - sq - stab) / sqrt(Df) = 2^(a c1 - c2): one FMA and one ex2 per
+  // feature, c1 = inv4 log2(e), c2 = (sq + stab) log2(e) + log2(Df) / 2.
+  const float stab = kMode == 1 ? m : p.stab[bh];
+  constexpr float kLog2e = 1.4426950408889634f;
+  const float c1 = inv4 * kLog2e;
+  const float c2 = (sq + stab) * kLog2e + 0.5f * __log2f((float)p.Df);
+  const long long plane_elems = BH * p.S * p.Dfp;
+  const int row0 = s0 + 32 * q;
+  for (int c0 = 0; c0 < Dfn && row0 < p.S; c0 += 32) {
+    uint32_t r[32];
+    if (c0 + 32 <= Dfn) {
+      ENL_TMEM_LD32(addr + c0, r, 0);
+    } else {
+      ENL_TMEM_LD16(addr + c0, r);
+#pragma unroll
+      for (int i = 16; i < 32; ++i) r[i] = 0u;
+    }
+    // All 32 exponentials independent (no branch between them), then the
+    // columns past Df are zeroed by a select.
+    const int n_valid = p.Df - c0;
+    float y[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float e = fast_exp2(fmaf(__uint_as_float(r[i]), c1, -c2));
+      y[i] = i < n_valid ? e : 0.0f;
+    }
+    __syncwarp();  // the previous chunk's reads of the buffer are done
+    if (p.planes) {
+      uint32_t hw[16], lw[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        hw[i] = pack_bf16x2(y[2 * i], y[2 * i + 1]);
+        lw[i] = pack_bf16x2(y[2 * i] - bf16lo_to_f32(hw[i]), y[2 * i + 1] - bf16hi_to_f32(hw[i]));
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        *reinterpret_cast<uint4*>(buf + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+            make_uint4(hw[4 * u], hw[4 * u + 1], hw[4 * u + 2], hw[4 * u + 3]);
+        *reinterpret_cast<uint4*>(buf + lane * 128 + (((u + 4) ^ (lane & 7)) << 4)) =
+            make_uint4(lw[4 * u], lw[4 * u + 1], lw[4 * u + 2], lw[4 * u + 3]);
+      }
+    } else {
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        *reinterpret_cast<float4*>(buf + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+            make_float4(y[4 * u], y[4 * u + 1], y[4 * u + 2], y[4 * u + 3]);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int piece = 32 * k + lane, rr = piece / 8, u = piece % 8;
+      if (row0 + rr >= p.S) continue;
+      const uint4 v4 = *reinterpret_cast<const uint4*>(buf + rr * 128 + ((u ^ (rr & 7)) << 4));
+      const long long grow = (long long)bh * p.S + row0 + rr;
+      if (p.planes) {
+        const int col = c0 + 8 * (u & 3);  // 8 features per 16-byte unit
+        if (col < p.Df)
+          *reinterpret_cast<uint4*>(p.planes + (u >> 2) * plane_elems + grow * p.Dfp + col) = v4;
+      } else {
+        const int col = c0 + 4 * u;
+        if (col < p.Df) *reinterpret_cast<uint4*>(p.phi + grow * p.Df + col) = v4;
+      }
+    }
+  }
+  __syncwarp();  // the buffer is free for the warp's next tile
+}
+
 struct PerfSmem {
   __host__ __device__ static int stage_bytes() { return 2 * 128 * 128 + 2 * 256 * 128; }
   // Head dims up to 64 are one K step: one stage, so that two CTAs fit per SM.
@@ -684,7 +839,7 @@ __global__ void __launch_bounds__(kThreads)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  constexpr int kX = 128 * 128;  // one plane of a 64-wide K step of x
+  constexpr int kX = kPerfX;
   const int n_st = PerfSmem::stages(p.Dh);
   uint8_t* out_stage = smem;  // stage 0, after the MMAs have read it
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + n_st * PerfSmem::stage_bytes());
@@ -756,141 +911,19 @@ __global__ void __launch_bounds__(kThreads)
     }
     umma_commit_elect(bar_acc);
   } else {
-    const int q = warp % 4, row = 32 * q + lane, s = s0 + row;
-    const uint32_t addr = tmem + ((uint32_t)(32 * q) << 16);
+    const int q = warp % 4;
     const bool ok = warp_wait(bar_acc, 0, abort_flag, 92);
     if (ok) {
       tc_fence_after();
-      const float inv4 = rsqrtf(sqrtf((float)p.Dh));  // Dh^(-1/4)
-      // |x'|^2 / 2 from the row's own planes (hi + lo recovers x to 2^-16).
       // While every K step still has its own stage (head dims up to 128), the
-      // row is read from the staged tiles: 128 bytes per plane and step, 16-
-      // byte units at (unit ^ row % 8) under the 128-byte swizzle. The stage's
-      // full barrier (one completed phase) orders the TMA's writes before the
-      // reads. Larger head dims read the planes from global memory.
-      float sq = 0.0f;
+      // row norms are read from the staged tiles; the stage's full barrier (one
+      // completed phase) orders the TMA's writes before the reads.
       bool staged = kMode != 0 && n_k <= n_st;
       for (int kb = 0; kb < n_k && staged; ++kb)
         staged = warp_wait(bar_full + kb, 0, abort_flag, 93);
-      if (s < p.S && kMode != 0) {
-        if (staged) {
-          for (int kb = 0; kb < n_k; ++kb) {
-            const uint8_t* xs = smem + kb * PerfSmem::stage_bytes() + row * 128;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              if (64 * kb + 8 * j >= p.Dh) break;
-              const uint4 h = *reinterpret_cast<const uint4*>(xs + ((j ^ (row & 7)) << 4));
-              const uint4 l = *reinterpret_cast<const uint4*>(xs + kX + ((j ^ (row & 7)) << 4));
-              const uint32_t hw[4] = {h.x, h.y, h.z, h.w}, lw[4] = {l.x, l.y, l.z, l.w};
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                if (64 * kb + 8 * j + e < p.Dh) {
-                  const float hv = e & 1 ? bf16hi_to_f32(hw[e / 2]) : bf16lo_to_f32(hw[e / 2]);
-                  const float lv = e & 1 ? bf16hi_to_f32(lw[e / 2]) : bf16lo_to_f32(lw[e / 2]);
-                  const float x = (hv + lv) * inv4;
-                  sq = fmaf(x, x, sq);
-                }
-              }
-            }
-          }
-        } else {
-          const uint16_t* xh = p.xp + ((long long)bh * p.S + s) * p.Dhp;
-          const uint16_t* xl = xh + BH * p.S * p.Dhp;
-          for (int d = 0; d < p.Dh; ++d) {
-            const float x = (bf16_val(xh[d]) + bf16_val(xl[d])) * inv4;
-            sq = fmaf(x, x, sq);
-          }
-        }
-        sq *= 0.5f;
-      }
-      // The row maximum (mode 0 and 1): one pass over the accumulator.
-      float m = -INFINITY;
-      if (kMode != 2) {
-        for (int c0 = 0; c0 < Dfn; c0 += 16) {
-          uint32_t r[16];
-          ENL_TMEM_LD16(addr + c0, r);
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            if (c0 + i < p.Df) m = fmaxf(m, __uint_as_float(r[i]) * inv4);
-        }
-        if (s >= p.S) m = -INFINITY;
-      }
-      if (kMode == 0) {
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (lane == 0 && m > -INFINITY) atomicMax(reinterpret_cast<int*>(p.stab) + bh, ord_enc(m));
-      } else {
-        // 32 features at a time: each lane puts its row's 32 values in the
-        // warp's 32-row x 128-byte buffer (16-byte units XOR-swizzled by row
-        // against bank conflicts), then the warp stores 4 whole 128-byte row
-        // segments per instruction. The buffer is where this warp's own rows
-        // of the x hi plane were staged, which only this warp has read. With
-        // p.planes a row's 128 bytes are its 32 bf16 hi values, then the 32
-        // lo values, and go to the two planes as 64-byte runs.
-        const float stab = kMode == 1 ? m : p.stab[bh];
-        const float norm = rsqrtf((float)p.Df);
-        const long long plane_elems = BH * p.S * p.Dfp;
-        uint8_t* buf = out_stage + q * 32 * 128;
-        const int row0 = s0 + 32 * q;
-        for (int c0 = 0; c0 < Dfn && row0 < p.S; c0 += 32) {
-          uint32_t r[32];
-          ENL_TMEM_LD16(addr + c0, r);
-          if (c0 + 16 < Dfn) {
-            ENL_TMEM_LD16(addr + c0 + 16, (r + 16));
-          } else {
-#pragma unroll
-            for (int i = 16; i < 32; ++i) r[i] = 0u;
-          }
-          // All 32 exponentials independent (no branch between them), then
-          // the columns past Df are zeroed by a select.
-          const int n_valid = p.Df - c0;
-          float y[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float e = expf(__uint_as_float(r[i]) * inv4 - sq - stab) * norm;
-            y[i] = i < n_valid ? e : 0.0f;
-          }
-          __syncwarp();  // the previous chunk's reads of the buffer are done
-          if (p.planes) {
-            uint32_t hw[16], lw[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              hw[i] = pack_bf16x2(y[2 * i], y[2 * i + 1]);
-              lw[i] = pack_bf16x2(y[2 * i] - bf16lo_to_f32(hw[i]),
-                                  y[2 * i + 1] - bf16hi_to_f32(hw[i]));
-            }
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              *reinterpret_cast<uint4*>(buf + lane * 128 + ((u ^ (lane & 7)) << 4)) =
-                  make_uint4(hw[4 * u], hw[4 * u + 1], hw[4 * u + 2], hw[4 * u + 3]);
-              *reinterpret_cast<uint4*>(buf + lane * 128 + (((u + 4) ^ (lane & 7)) << 4)) =
-                  make_uint4(lw[4 * u], lw[4 * u + 1], lw[4 * u + 2], lw[4 * u + 3]);
-            }
-          } else {
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-              *reinterpret_cast<float4*>(buf + lane * 128 + ((u ^ (lane & 7)) << 4)) =
-                  make_float4(y[4 * u], y[4 * u + 1], y[4 * u + 2], y[4 * u + 3]);
-          }
-          __syncwarp();
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const int piece = 32 * k + lane, rr = piece / 8, u = piece % 8;
-            if (row0 + rr >= p.S) continue;
-            const uint4 v4 = *reinterpret_cast<const uint4*>(buf + rr * 128 + ((u ^ (rr & 7)) << 4));
-            const long long row = (long long)bh * p.S + row0 + rr;
-            if (p.planes) {
-              const int col = c0 + 8 * (u & 3);  // 8 features per 16-byte unit
-              if (col < p.Df)
-                *reinterpret_cast<uint4*>(p.planes + (u >> 2) * plane_elems + row * p.Dfp + col) =
-                    v4;
-            } else {
-              const int col = c0 + 4 * u;
-              if (col < p.Df) *reinterpret_cast<uint4*>(p.phi + row * p.Df + col) = v4;
-            }
-          }
-        }
-      }
+      perf_tile_epilogue<kMode>(p, tmem + ((uint32_t)(32 * q) << 16), staged ? smem : nullptr,
+                                PerfSmem::stage_bytes(), bh, s0, q, lane,
+                                out_stage + q * 32 * 128);
     }
   }
   tc_fence_before();
@@ -898,6 +931,147 @@ __global__ void __launch_bounds__(kThreads)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc<256>(tmem);
+  }
+}
+
+// Persistent form of the Performer map for head dims up to 64 (one K step):
+// one CTA per SM walks the (b * H + h, 128-row block) tiles c, c + grid, ...
+// The omega planes are loaded once and stay in shared memory; x tiles stream
+// through a 3-stage ring; the projections of a tile go to one of two 256-column
+// accumulators in tensor memory, so that a tile's MMAs and loads overlap the
+// epilogue of the one before. Two groups of four epilogue warps take
+// alternate tiles (group g always uses accumulator g). A ring stage is free
+// once the MMAs that read it completed and the group's four warps read its
+// row norms (five arrivals).
+constexpr int kPersistThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 two epilogue groups
+constexpr int kPersistStages = 3;
+struct PersistSmem {
+  static constexpr int kW = 2 * 256 * 128;      // omega, both planes, up to 256 features
+  static constexpr int kXStage = 2 * kPerfX;    // x tile, both planes
+  static constexpr int kOut = 8 * 32 * 128;     // eight warps' staging buffers
+  static constexpr int kBars = 256;
+  static constexpr int total() { return kW + kPersistStages * kXStage + kOut + kBars + 1024; }
+};
+
+template <int kMode>
+__global__ void __launch_bounds__(kPersistThreads, 1)
+    phi_perf_persist(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                     PerfTcParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* w_s = smem;
+  uint8_t* x_s = smem + PersistSmem::kW;
+  uint8_t* out_s = x_s + kPersistStages * PersistSmem::kXStage;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(out_s + PersistSmem::kOut);
+  uint64_t* w_full = bars;                            // [1]
+  uint64_t* x_full = bars + 1;                        // [kPersistStages]
+  uint64_t* x_empty = x_full + kPersistStages;        // [kPersistStages]
+  uint64_t* acc_full = x_empty + kPersistStages;      // [2]
+  uint64_t* acc_empty = acc_full + 2;                 // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const long long BH = (long long)p.B * p.H;
+  const int n_rb = (p.S + 127) / 128;
+  const long long n_tiles = BH * n_rb;
+  const int n_local =
+      blockIdx.x < n_tiles ? (int)((n_tiles - 1 - blockIdx.x) / gridDim.x + 1) : 0;
+  const int Dfn = (p.Df + 15) / 16 * 16;  // MMA N
+
+  if (threadIdx.x == 0) {
+    mbar_init(w_full, 1);
+    for (int i = 0; i < kPersistStages; ++i) {
+      mbar_init(x_full + i, 1);
+      mbar_init(x_empty + i, 5);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(acc_full + i, 1);
+      mbar_init(acc_empty + i, 4);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc<512>(tmem_slot);
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto tile_of = [&](int j, int& bh, int& s0) {
+    const long long t = blockIdx.x + (long long)j * gridDim.x;
+    bh = (int)(t / n_rb);
+    s0 = (int)(t - (long long)bh * n_rb) * 128;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      bool ok = true;
+      mbar_arrive_expect_tx(w_full, 2 * Dfn * 128);
+      for (int pl = 0; pl < 2; ++pl) tma_load_3d(w_s + pl * 256 * 128, &tm_w, w_full, 0, 0, pl);
+      for (int j = 0; j < n_local && ok; ++j) {
+        const int st = j % kPersistStages;
+        if (j >= kPersistStages)
+          ok = mbar_wait(x_empty + st, ((j / kPersistStages) - 1) & 1, abort_flag, 94);
+        if (!ok) break;
+        int bh, s0;
+        tile_of(j, bh, s0);
+        uint8_t* xb = x_s + st * PersistSmem::kXStage;
+        mbar_arrive_expect_tx(x_full + st, 2 * kPerfX);
+        for (int pl = 0; pl < 2; ++pl)
+          tma_load_3d(xb + pl * kPerfX, &tm_x, x_full + st, 0, s0, (int)(pl * BH + bh));
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    const uint32_t idesc = idesc_bf16_f32(128, Dfn, false);
+    bool ok = warp_wait(w_full, 0, abort_flag, 95);
+    const uint32_t w_lo = desc_lo(smem_u32(w_s), 16), w_pl = (256 * 128) >> 4;
+    for (int j = 0; j < n_local && ok; ++j) {
+      const int st = j % kPersistStages, a = j & 1;
+      if (j >= 2) ok = warp_wait(acc_empty + a, ((j >> 1) - 1) & 1, abort_flag, 96);
+      if (ok) ok = warp_wait(x_full + st, (j / kPersistStages) & 1, abort_flag, 97);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t x_lo = desc_lo(smem_u32(x_s + st * PersistSmem::kXStage), 16);
+      const uint32_t x_pl = kPerfX >> 4, d = tmem + (uint32_t)(a * 256);
+#pragma unroll 1
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint32_t off = kk * 2;
+        umma_ss_elect_acc(d, x_lo + off, w_lo + off, kDescHiSw128, idesc, kk > 0 ? 1u : 0u);
+        umma_ss_elect_acc(d, x_lo + off, w_lo + w_pl + off, kDescHiSw128, idesc, 1u);
+        umma_ss_elect_acc(d, x_lo + x_pl + off, w_lo + off, kDescHiSw128, idesc, 1u);
+      }
+      umma_commit_elect(x_empty + st);
+      umma_commit_elect(acc_full + a);
+    }
+  } else {
+    const int g = (warp - 2) / 4, q = warp % 4;
+    uint8_t* buf = out_s + (warp - 2) * 32 * 128;
+    bool ok = true;
+    for (int j = g; j < n_local && ok; j += 2) {
+      const int st = j % kPersistStages;
+      ok = warp_wait(acc_full + g, (j >> 1) & 1, abort_flag, 98);
+      if (ok) ok = warp_wait(x_full + st, (j / kPersistStages) & 1, abort_flag, 99);
+      if (!ok) break;
+      tc_fence_after();
+      int bh, s0;
+      tile_of(j, bh, s0);
+      // Row norms from the staged tile, then the stage goes back to the ring
+      // before the (longer) exponential and store pass.
+      const uint8_t* xb = x_s + st * PersistSmem::kXStage;
+      perf_tile_epilogue<kMode>(p, tmem + (uint32_t)(g * 256) + ((uint32_t)(32 * q) << 16), xb,
+                                0, bh, s0, q, lane, buf, x_empty + st);
+      tc_fence_before();
+      if (lane == 0) mbar_arrive(acc_empty + g);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<512>(tmem);
   }
 }
 
@@ -1018,10 +1192,24 @@ cudaError_t launch_perf_tc(const CUtensorMap& tx, const CUtensorMap& tw, const P
     e = cudaFuncSetAttribute(phi_perf_tc<0>, a, PerfSmem::total(256));
     if (e == cudaSuccess) e = cudaFuncSetAttribute(phi_perf_tc<1>, a, PerfSmem::total(256));
     if (e == cudaSuccess) e = cudaFuncSetAttribute(phi_perf_tc<2>, a, PerfSmem::total(256));
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(phi_perf_persist<0>, a, PersistSmem::total());
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(phi_perf_persist<1>, a, PersistSmem::total());
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(phi_perf_persist<2>, a, PersistSmem::total());
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
   if (p.B * p.H == 0 || p.S == 0) return cudaSuccess;
+  if (p.Dh <= 64 && p.Df <= 256) {
+    const long long n_tiles = (long long)p.B * p.H * ((p.S + 127) / 128);
+    const int grid = (int)std::min<long long>(n_tiles, p.n_sm > 0 ? p.n_sm : 148);
+    const int smem = PersistSmem::total();
+    switch (mode) {
+      case 0: phi_perf_persist<0><<<grid, kPersistThreads, smem, stream>>>(tx, tw, p); break;
+      case 1: phi_perf_persist<1><<<grid, kPersistThreads, smem, stream>>>(tx, tw, p); break;
+      default: phi_perf_persist<2><<<grid, kPersistThreads, smem, stream>>>(tx, tw, p); break;
+    }
+    return cudaGetLastError();
+  }
   const dim3 grid((p.S + 127) / 128, p.B * p.H);
   const int smem = PerfSmem::total(p.Dh);
   switch (mode) {
