@@ -309,52 +309,42 @@ def bench_prefill(dist: Dist, clocks: ClockSampler, steps: int, warmup: int, bat
 
 def run_e2e(dist: Dist, clocks: ClockSampler, q, k, v, out, lens, unit_t, steps: int,
             flops_total: float, policy: str = "local"):
-    """The e2e leg of the headline: host q/k/v in, host output back, every
-    step. policy "local" first-touches the pinned buffers on the CPUs NVML
-    reports as local to the GPU; "spread" on NUMA node rank % nodes. At N > 1
-    the leg runs twice: rank 0 alone (the other ranks idle), then every rank
-    at once, so that the line shows what concurrent copies cost."""
+    """The e2e leg of the headline through the host-buffer API
+    (hostprefill.HostPrefill): host q/k/v in, host output back, every step,
+    pipelined across steps. Key/value rows past each sequence's valid length
+    are not uploaded (no row can see them under this mask), so the upload is
+    the queries plus the valid K/V rows. policy "local" first-touches the
+    pinned buffers on the CPUs NVML reports as local to the GPU; "spread" on
+    NUMA node rank % nodes. At N > 1 the leg runs twice: rank 0 alone (the
+    other ranks idle), then every rank at once, so that the line shows what
+    concurrent copies cost."""
     import torch
-    from enilnets_b200 import hostmem, kernels
+    from enilnets_b200 import hostmem
+    from enilnets_b200.hostprefill import HostPrefill
     cpus = hostmem.spread_cpus(dist.rank) if policy == "spread" else None
     with hostmem.local_to(dist.local_rank, cpus) as host_cpus:
         hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
-        hout = [torch.empty(out.shape, dtype=out.dtype).pin_memory() for _ in range(2)]
-        for h in hout:
-            h.zero_()
-    dev_in = [tuple(torch.empty_like(t) for t in (q, k, v)) for _ in range(2)]
-    dev_out = [torch.empty_like(out) for _ in range(2)]
-    s_in, s_cmp, s_out = (torch.cuda.Stream(device=dist.device) for _ in range(3))
-    ev_in, ev_cmp, ev_out = ([torch.cuda.Event() for _ in range(2)] for _ in range(3))
-    used = [False, False]
+        hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        hout.zero_()
+    lengths = [int(x) for x in lens.cpu()]
+    pipe = HostPrefill(tuple(q.shape), dtype=q.dtype, device=q.device)
 
-    def e2e_step(i):
-        slot = i % 2
-        dq, dk, dv = dev_in[slot]
-        with torch.cuda.stream(s_in):
-            if used[slot]:
-                s_in.wait_event(ev_cmp[slot])  # the slot's previous kernel read its inputs
-            dq.copy_(hq, non_blocking=True)
-            dk.copy_(hk, non_blocking=True)
-            dv.copy_(hv, non_blocking=True)
-            ev_in[slot].record(s_in)
-        with torch.cuda.stream(s_cmp):
-            s_cmp.wait_event(ev_in[slot])
-            if used[slot]:
-                s_cmp.wait_event(ev_out[slot])  # the slot's previous output is on the host
-            kernels.attention_prefill(dq, dk, dv, causal=True, kv_valid_len=lens,
-                                      mask_mode="additive", out=dev_out[slot], units=unit_t)
-            ev_cmp[slot].record(s_cmp)
-        with torch.cuda.stream(s_out):
-            s_out.wait_event(ev_cmp[slot])
-            hout[slot].copy_(dev_out[slot], non_blocking=True)
-            ev_out[slot].record(s_out)
-        used[slot] = True
+    def e2e_step():
+        pipe.submit(hq, hk, hv, hout, lengths, causal=True, mask_mode="additive", units=unit_t)
 
     e2e_steps = max(4, min(steps, 20))
-    for i in range(2):
-        e2e_step(i)
-    torch.cuda.synchronize()
+    for _ in range(2):
+        e2e_step()
+    pipe.synchronize()
+    # The pipeline's output equals the device-resident call's (on the rank's
+    # own units: rows of other units are left untouched by both).
+    got = hout.to(out.device)
+    if unit_t is None:
+        check = bool(torch.equal(got, out))
+    else:
+        H = q.shape[2]
+        check = all(bool(torch.equal(got[u // H, :, u % H], out[u // H, :, u % H]))
+                    for u in unit_t.cpu().tolist())
 
     def leg(active: bool) -> float:
         cur = torch.cuda.current_stream()
@@ -365,11 +355,10 @@ def run_e2e(dist: Dist, clocks: ClockSampler, q, k, v, out, lens, unit_t, steps:
             start = torch.cuda.Event(enable_timing=True)
             end = torch.cuda.Event(enable_timing=True)
             start.record(cur)
-            for s_ in (s_in, s_cmp, s_out):
-                s_.wait_stream(cur)
-            for i in range(e2e_steps):
-                e2e_step(i)
-            cur.wait_stream(s_out)
+            pipe.wait_on(cur)
+            for _ in range(e2e_steps):
+                e2e_step()
+            pipe.join(cur)
             end.record(cur)
             torch.cuda.synchronize()
             clocks.mark(t0, time.time())
@@ -379,12 +368,15 @@ def run_e2e(dist: Dist, clocks: ClockSampler, q, k, v, out, lens, unit_t, steps:
 
     alone = leg(dist.rank == 0) if dist.world > 1 else None
     ms_e2e = leg(True)
-    h2d = 3 * q.numel() * q.element_size()
-    d2h = out.numel() * out.element_size()
+    h2d = pipe.h2d_bytes[-1]
+    d2h = pipe.d2h_bytes[-1]
     place = (f"{policy}: {len(host_cpus)} CPUs ({min(host_cpus)}-{max(host_cpus)})" if host_cpus
              else f"{policy}: unbound (no CPU set available)")
     e2e = {"value": flops_total / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
            "ms_per_step": ms_e2e, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+           "h2d_bytes_dense_inputs": 3 * q.numel() * q.element_size(),
+           "api": "hostprefill.HostPrefill.submit (pinned host q/k/v/out, valid K/V rows only)",
+           "output_equals_device_call": check,
            "h2d_GB_s_per_rank": h2d / (ms_e2e * 1e-3) / 1e9,
            "d2h_GB_s_per_rank": d2h / (ms_e2e * 1e-3) / 1e9,
            "pinned_host_memory": place, "numa_nodes": len(hostmem.numa_nodes())}
