@@ -436,7 +436,9 @@ size_t enl_project_workspace_bytes(const enl_project_args* a) {
 
 int enl_project(const enl_project_args* a, void* stream) {
   if (!a) return fail(ENL_ERR_INVALID, "enl_project: args is NULL");
-  if (!a->x || !a->w || !a->y)
+  // With M == 0 there are no rows: x and y may be NULL (an empty tensor's
+  // address); the call checks its other arguments and does nothing.
+  if ((a->M != 0 && (!a->x || !a->y)) || !a->w)
     return fail(ENL_ERR_INVALID, "enl_project: x, w and y must be non-NULL");
   if (a->M < 0 || a->N < 1 || a->K < 1)
     return fail(ENL_ERR_INVALID, "enl_project: M=%d N=%d K=%d (M >= 0, N and K >= 1)", a->M,
@@ -454,7 +456,8 @@ int enl_project(const enl_project_args* a, void* stream) {
   if (!split && a->w_lo)
     return fail(ENL_ERR_INVALID, "enl_project: w_lo is only used with fp32 x");
   const int xsz = split ? 4 : 2, ysz = a->y_dtype == ENL_DTYPE_FP32 ? 4 : 2;
-  if (!aligned16(a->x) || !aligned16(a->w) || !aligned16(a->y) || (a->w_lo && !aligned16(a->w_lo)))
+  if ((a->x && !aligned16(a->x)) || !aligned16(a->w) || (a->y && !aligned16(a->y)) ||
+      (a->w_lo && !aligned16(a->w_lo)))
     return fail(ENL_ERR_INVALID, "enl_project: x, w, w_lo and y must be 16-byte aligned");
   if (a->x_stride_m < a->K || (a->x_stride_m * xsz) % 16 != 0 || a->w_stride_n < a->K ||
       (a->w_stride_n * 2) % 16 != 0 || a->y_stride_m < a->N || (a->y_stride_m * ysz) % 16 != 0)

@@ -89,6 +89,13 @@ def attention_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     if tuple(out.shape) != (B, Sq, H, D) or out.dtype not in _DTYPES:
         raise ValueError(f"out must be ({B}, {Sq}, {H}, {D}) bf16/fp32")
     lse = torch.empty((B, H, Sq), device=q.device, dtype=torch.float32) if return_lse else None
+    if Skv == 0 and B * Sq > 0:
+        # A softmax over no keys: the reference's reduction over an empty key
+        # axis raises too.
+        raise ValueError("attention over no keys (seq_kv = 0)")
+    if B == 0 or Sq == 0:
+        # Nothing to compute: the reference returns the empty result as well.
+        return (out, lse) if return_lse else out
     if kv_valid_len is not None:
         _require_cuda("kv_valid_len", kv_valid_len, torch.int32, last_contiguous=False)
         if tuple(kv_valid_len.shape) != (B,) or not kv_valid_len.is_contiguous():
@@ -276,6 +283,11 @@ def attention_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: tor
             _require_cuda(name, t, torch.float32)
             if tuple(t.shape) != shape:
                 raise ValueError(f"{name} must be {shape}, got {tuple(t.shape)}")
+    if B == 0 or Sq == 0 or Skv == 0:
+        # No (query, key) pair: every gradient is zero (empty when B == 0).
+        for t in (dq, dk, dv):
+            t.zero_()
+        return dq, dk, dv
     a = nat.BackwardArgs()
     a.q, a.k, a.v, a.o, a.dout = (t.data_ptr() for t in (q, k, v, o, dout))
     a.lse, a.dq, a.dk, a.dv = lse.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr()
@@ -417,6 +429,8 @@ def attention_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
         lse = lse_out
     if alibi_slopes is not None:
         _require_cuda("alibi_slopes", alibi_slopes, torch.float32, last_contiguous=False)
+    if B == 0:
+        return (out, lse) if (return_lse or lse_out is not None) else out
     n_slots = max(1, slot_end - slot_begin)
     splits = n_splits if n_splits > 0 else decode_auto_splits(B, Hkv, n_slots)
     need = decode_workspace_bytes(B, H, D, splits)
@@ -554,6 +568,16 @@ def linear_feature_map(x: torch.Tensor, kernel: str, omega: Optional[torch.Tenso
         if omega.dim() != 2 or omega.shape[1] != Dh or not omega.is_contiguous():
             raise ValueError(f"omega must be a contiguous (num_features, {Dh}) fp32 tensor")
     Df = omega.shape[0] if performer else Dh
+    if B * S == 0:
+        # No rows: an empty map; a key stabilizer stays at its floor (-inf
+        # without one), as a carried decode state expects.
+        phi = torch.empty((2, B, H, S, (Df + 7) // 8 * 8) if planes else (B, H, S, Df),
+                          device=x.device, dtype=torch.bfloat16 if planes else torch.float32)
+        stab = None
+        if performer and global_stab:
+            stab = stab_floor.reshape(B, H).clone().float() if stab_floor is not None else \
+                torch.full((B, H), -math.inf, device=x.device, dtype=torch.float32)
+        return phi, stab
     if planes:
         phi = torch.empty((2, B, H, S, (Df + 7) // 8 * 8), device=x.device, dtype=torch.bfloat16)
     else:
@@ -646,6 +670,19 @@ def linear_attention(phi_q: torch.Tensor, phi_k: torch.Tensor, v: torch.Tensor, 
         if state_scale is not None:
             _require_cuda("state_scale", state_scale, torch.float32, last_contiguous=False)
             state_scale = state_scale.reshape(B, Hkv).contiguous()
+    if B == 0 or S == 0:
+        # No rows: the output is empty and the sums after the last row are
+        # the carried state (times its scale), or zero.
+        if new_state is not None:
+            if state is None:
+                new_state[0].zero_()
+                new_state[1].zero_()
+            else:
+                sc = state_scale if state_scale is not None else \
+                    torch.ones((B, Hkv), device=phi_q.device, dtype=torch.float32)
+                torch.mul(state[0], sc[:, :, None, None], out=new_state[0])
+                torch.mul(state[1], sc[:, :, None], out=new_state[1])
+        return (out, new_state) if return_state else out
     a = nat.LinearArgs()
     if planes:
         a.phi_q_planes, a.phi_k_planes = phi_q.data_ptr(), phi_k.data_ptr()
