@@ -15,7 +15,10 @@ what it can of it and moves no byte the kernel does not need:
   valid keys otherwise), so padded keys carry no weight under either mask
   rule. Rows [0, L_b) of sequence b go up as one copy per tensor; the rest of
   each device slot is zeroed once, so the kernel's partial last key tile
-  reads finite values. Otherwise K and V move whole.
+  reads finite values. Otherwise K and V move whole. One consequence: a
+  non-finite value in a padded host row is never read, where the reference
+  (and the device-resident call) would carry a NaN in a padded V row into
+  the output through 0 * NaN.
 * Queries (padded query rows still see every real key) and the output move
   whole.
 """
