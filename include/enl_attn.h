@@ -218,7 +218,7 @@ typedef struct enl_project_args {
   void* y;             /* (M, N) rows, y_stride_m elements apart */
   int64_t y_stride_m;
   int32_t y_dtype;     /* ENL_DTYPE_BF16 or ENL_DTYPE_FP32 */
-  int32_t M, N, K;
+  int32_t M, N, K;     /* M >= 0 (M == 0: nothing to do, x and y may be NULL) */
   /* RoPE fused into the epilogue (nn/forward.py:80-88): columns n < rope_cols,
    * heads of rope_head_dim columns, rotate-half at position
    * rope_pos0 + (m % rope_seq) with fp32 tables (rope_rows, rope_head_dim / 2)
