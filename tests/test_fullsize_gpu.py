@@ -46,6 +46,45 @@ def test_config3_decode_full_size(cuda):
             assert abs(ln[b, h] - lref[0, 0]) <= TOL, (b, h)
 
 
+def test_config3_consecutive_steps_full_size(cuda):
+    """Config 3's step loop: 128 steps, each appending one K/V token per row
+    and decoding the new query over the grown cache (the bench replays the
+    same loop from a CUDA graph). Every 32nd step and the last are checked
+    on sampled (batch, head) slices; the cache then holds exactly the
+    appended tokens after the original context (bit-exact appends)."""
+    import torch
+    from enilnets_b200 import _native, kernels
+    B, H, D, ctx, steps = 64, 32, 128, 8192, 128
+    cap = ctx + steps
+    g = torch.Generator(device="cuda").manual_seed(33)
+    kc = torch.zeros((B, H, cap, D), dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    kc[:, :, :ctx].normal_(generator=g)
+    vc[:, :, :ctx].normal_(generator=g)
+    qs = torch.randn((steps, B, H, D), generator=g, device="cuda").to(torch.bfloat16)
+    kn = torch.randn((steps, B, 1, H, D), generator=g, device="cuda").to(torch.bfloat16)
+    vn = torch.randn((steps, B, 1, H, D), generator=g, device="cuda").to(torch.bfloat16)
+    checked = {}
+    for t in range(steps):
+        kernels.kv_append(kc, kn[t], ctx + t)
+        kernels.kv_append(vc, vn[t], ctx + t)
+        o = kernels.attention_decode(qs[t], kc, vc, slot_begin=0, slot_end=ctx + t + 1,
+                                     pos_slot0=0, q_pos=ctx + t, out_dtype=torch.float32)
+        if t % 32 == 0 or t == steps - 1:
+            checked[t] = o.clone()
+    torch.cuda.synchronize()
+    _native.raise_on_device_error()
+    assert torch.equal(kc[:, :, ctx:], kn[:, :, 0].permute(1, 2, 0, 3))
+    assert torch.equal(vc[:, :, ctx:], vn[:, :, 0].permute(1, 2, 0, 3))
+    for t, o in checked.items():
+        on = _np(o)
+        for b, h in ((0, 0), (40, 31)):
+            oref, _ = ref.decode_ref(_np(qs[t, b:b + 1, h:h + 1]), _np(kc[b:b + 1, h:h + 1]),
+                                     _np(vc[b:b + 1, h:h + 1]), slot_begin=0,
+                                     slot_end=ctx + t + 1, pos_slot0=0, q_pos=ctx + t)
+            assert np.max(np.abs(on[b, h] - oref[0, 0])) <= TOL, (t, b, h)
+
+
 def test_config4_cross_attention_full_size(cuda):
     """Decoder B16 x 1024 queries against 2048 memory keys, H16 D64,
     non-causal, memory key padding with valid lengths ~U[1024, 2048]."""
