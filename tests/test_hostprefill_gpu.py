@@ -47,6 +47,28 @@ def test_host_prefill_equals_device_call(cuda, lengths, window, mode):
     assert pipe.d2h_bytes == [B * S * row] * 3
 
 
+def test_host_prefill_fp32_inputs(cuda):
+    """fp32 q/k/v (the split-bf16 path) with the partial K/V upload: equal to
+    the device-resident call bit for bit."""
+    import torch
+    from enilnets_b200 import kernels
+    from enilnets_b200.hostprefill import HostPrefill
+    B, S, H, D = 2, 200, 2, 64
+    rng = np.random.RandomState(11)
+    lengths = [200, 61]
+    host = [torch.from_numpy(rng.standard_normal((B, S, H, D)).astype(np.float32)).pin_memory()
+            for _ in range(3)]
+    hout = torch.empty((B, S, H, D), dtype=torch.float32).pin_memory()
+    pipe = HostPrefill((B, S, H, D), dtype=torch.float32)
+    pipe.submit(*host, hout, lengths, causal=True, mask_mode="additive")
+    pipe.synchronize()
+    ref = kernels.attention_prefill(*(t.cuda() for t in host), causal=True,
+                                    kv_valid_len=torch.tensor(lengths, dtype=torch.int32,
+                                                              device="cuda"),
+                                    mask_mode="additive", out_dtype=torch.float32)
+    assert torch.equal(hout, ref.cpu())
+
+
 def test_host_prefill_rejects_unpinned_and_bad_lengths(cuda):
     import torch
     from enilnets_b200.hostprefill import HostPrefill
