@@ -116,3 +116,48 @@ def test_decode_random_sweep(cuda, block):
         assert np.array_equal(lf, np.isfinite(ln)), ("lse pattern", seed)
         if lf.any():
             assert np.max(np.abs(ln[lf] - lref[lf])) <= 2e-2, seed
+
+
+@pytest.mark.parametrize("block", range(2))
+def test_linear_random_sweep(cuda, block):
+    """Feature map plus linear attention end to end (the layer's order: the
+    maps write planes when the attention takes them), elu + 1 and Performer,
+    head dims on both sides of the tensor-core limit (128), odd feature
+    counts, GQA, causal and not: fp32 inputs at the 1e-4 kernel bar."""
+    import torch
+    from enilnets_b200 import _native, kernels
+    from oracle import linear_ref as lr
+    for seed in range(2000 + 50 * block, 2000 + 50 * block + 10):
+        rng = np.random.RandomState(seed)
+        kernel = "performer" if rng.rand() < 0.5 else "linear"
+        Dh = int(rng.choice([8, 24, 32, 64, 96, 128, 160]))
+        Df = int(rng.choice([36, 64, 128, 256])) if kernel == "performer" else Dh
+        Hkv = int(rng.choice([1, 2]))
+        H = Hkv * int(rng.choice([1, 2]))
+        B, S = int(rng.randint(1, 3)), int(rng.randint(1, 300))
+        causal = bool(rng.rand() < 0.6)
+        D = Dh
+        x_q = rng.standard_normal((B, S, H, Dh)) * 0.5
+        x_k = rng.standard_normal((B, S, Hkv, Dh)) * 0.5
+        v = rng.standard_normal((B, S, Hkv, D))
+        omega = lr.make_projection(Df, Dh, np.random.RandomState(seed)) if kernel == "performer" \
+            else None
+
+        def dev(a):
+            return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).cuda()
+
+        om = dev(omega) if omega is not None else None
+        planes = kernels.linear_planes_ok(D, Df)
+        qp, _ = kernels.linear_feature_map(dev(x_q), kernel, om, planes=planes)
+        kp, _ = kernels.linear_feature_map(dev(x_k), kernel, om, global_stab=True, planes=planes)
+        out = kernels.linear_attention(qp, kp, dev(v), causal=causal, num_features=Df)
+        torch.cuda.synchronize()
+        _native.raise_on_device_error()
+        fq = lr.feature_map(x_q.transpose(0, 2, 1, 3), kernel, omega, "row")
+        fk = lr.feature_map(x_k.transpose(0, 2, 1, 3), kernel, omega, "global")
+        G = H // Hkv
+        oref, _, _ = lr.linear_attention(fq, np.repeat(fk, G, axis=1),
+                                         np.repeat(v.transpose(0, 2, 1, 3), G, axis=1), causal)
+        got = out.cpu().numpy().astype(np.float64).transpose(0, 2, 1, 3)
+        err = float(np.max(np.abs(got - oref)))
+        assert err <= 1e-4 * max(1.0, float(np.abs(oref).max())), (seed, kernel, Dh, Df, err)
