@@ -32,7 +32,7 @@ DEVICE_ERRORS = {1: "an mbarrier wait exceeded its time budget",
                  3: "a launch-time shape invariant was violated"}
 
 
-ABI_VERSION = 7  # ENL_ABI_VERSION of include/enl_attn.h
+ABI_VERSION = 8  # ENL_ABI_VERSION of include/enl_attn.h
 
 
 class PrefillArgs(Structure):
@@ -139,6 +139,7 @@ class BackwardArgs(Structure):
         ("o_dtype", c_int32), ("causal", c_int32), ("window", c_int32),
         ("alibi_slopes", c_void_p), ("scale", c_float),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+        ("in_dtype", c_int32),
     ]
 
 

@@ -553,11 +553,26 @@ int enl_split_bf16(const float* src, int64_t ld, int64_t rows, int32_t cols, voi
   return ENL_OK;
 }
 
+namespace {
+// Bytes of the row statistics (lse2, dsum), each rounded to 256.
+size_t bwd_rows_bytes(const enl_backward_args* a) {
+  const size_t s_pad = ((size_t)a->seq_q + 127) / 128 * 128;
+  return ((size_t)a->batch * a->num_heads * s_pad * sizeof(float) + 255) & ~size_t(255);
+}
+// Bytes of one operand's bf16 (hi, lo) planes, rounded to 256.
+size_t bwd_planes_bytes(const enl_backward_args* a, int S, int H) {
+  return ((size_t)a->batch * S * H * a->head_dim * 2 * sizeof(uint16_t) + 255) & ~size_t(255);
+}
+}  // namespace
+
 size_t enl_backward_workspace_bytes(const enl_backward_args* a) {
   if (!a || a->batch < 1 || a->num_heads < 1 || a->seq_q < 1) return 0;
-  const size_t s_pad = ((size_t)a->seq_q + 127) / 128 * 128;
-  const size_t one = ((size_t)a->batch * a->num_heads * s_pad * sizeof(float) + 255) & ~size_t(255);
-  return 2 * one;
+  size_t total = 2 * bwd_rows_bytes(a);
+  if (a->in_dtype == ENL_DTYPE_FP32 && a->seq_kv >= 1 && a->num_kv_heads >= 1 &&
+      a->head_dim >= 1)
+    total += 2 * bwd_planes_bytes(a, a->seq_q, a->num_heads) +
+             2 * bwd_planes_bytes(a, a->seq_kv, a->num_kv_heads);
+  return total;
 }
 
 int enl_attn_backward(const enl_backward_args* a, void* stream) {
@@ -579,13 +594,22 @@ int enl_attn_backward(const enl_backward_args* a, void* stream) {
                 a->head_dim);
   if (a->o_dtype != ENL_DTYPE_BF16 && a->o_dtype != ENL_DTYPE_FP32)
     return fail(ENL_ERR_INVALID, "enl_attn_backward: o_dtype=%d", a->o_dtype);
+  if (a->in_dtype != ENL_DTYPE_BF16 && a->in_dtype != ENL_DTYPE_FP32)
+    return fail(ENL_ERR_INVALID, "enl_attn_backward: in_dtype=%d", a->in_dtype);
+  const bool split = a->in_dtype == ENL_DTYPE_FP32;
+  if (split && a->head_dim > 64)
+    return fail(ENL_ERR_UNSUPPORTED,
+                "enl_attn_backward: fp32 inputs (split-bf16 operands) cover head_dim <= 64 "
+                "(got %d): the planes of a 128-wide head do not fit in shared memory",
+                a->head_dim);
   if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->dout))
     return fail(ENL_ERR_INVALID, "enl_attn_backward: q, k, v, dout must be 16-byte aligned");
   int st;
-  if ((st = check_strides_16B("q", a->q_stride_b, a->q_stride_s, a->q_stride_h, 2))) return st;
-  if ((st = check_strides_16B("k", a->k_stride_b, a->k_stride_s, a->k_stride_h, 2))) return st;
-  if ((st = check_strides_16B("v", a->v_stride_b, a->v_stride_s, a->v_stride_h, 2))) return st;
-  if ((st = check_strides_16B("dout", a->do_stride_b, a->do_stride_s, a->do_stride_h, 2)))
+  const int esz = split ? 4 : 2;
+  if ((st = check_strides_16B("q", a->q_stride_b, a->q_stride_s, a->q_stride_h, esz))) return st;
+  if ((st = check_strides_16B("k", a->k_stride_b, a->k_stride_s, a->k_stride_h, esz))) return st;
+  if ((st = check_strides_16B("v", a->v_stride_b, a->v_stride_s, a->v_stride_h, esz))) return st;
+  if ((st = check_strides_16B("dout", a->do_stride_b, a->do_stride_s, a->do_stride_h, esz)))
     return st;
   const long long n_kt = (a->seq_kv + 127) / 128, n_qt = (a->seq_q + 127) / 128;
   if (n_kt * a->batch * a->num_kv_heads > (1ll << 31) - 1 ||
@@ -598,23 +622,44 @@ int enl_attn_backward(const enl_backward_args* a, void* stream) {
   if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0)
     return fail(ENL_ERR_INVALID, "enl_attn_backward: workspace must be 256-byte aligned");
 
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const size_t rows_bytes = bwd_rows_bytes(a);
   CUtensorMap tq, tk, tv, tdo;
-  if ((st = make_qkv_map(&tq, a->q, a->head_dim, a->seq_q, a->num_heads, a->batch, a->q_stride_s,
-                         a->q_stride_h, a->q_stride_b, "q")))
-    return st;
-  if ((st = make_qkv_map(&tk, a->k, a->head_dim, a->seq_kv, a->num_kv_heads, a->batch,
-                         a->k_stride_s, a->k_stride_h, a->k_stride_b, "k")))
-    return st;
-  if ((st = make_qkv_map(&tv, a->v, a->head_dim, a->seq_kv, a->num_kv_heads, a->batch,
-                         a->v_stride_s, a->v_stride_h, a->v_stride_b, "v")))
-    return st;
-  if ((st = make_qkv_map(&tdo, a->dout, a->head_dim, a->seq_q, a->num_heads, a->batch,
-                         a->do_stride_s, a->do_stride_h, a->do_stride_b, "dout")))
-    return st;
+  struct Op {
+    const void* src;
+    int64_t sb, ss, sh;
+    int S, H;
+    CUtensorMap* map;
+    const char* name;
+  } ops[4] = {
+      {a->q, a->q_stride_b, a->q_stride_s, a->q_stride_h, a->seq_q, a->num_heads, &tq, "q"},
+      {a->k, a->k_stride_b, a->k_stride_s, a->k_stride_h, a->seq_kv, a->num_kv_heads, &tk, "k"},
+      {a->v, a->v_stride_b, a->v_stride_s, a->v_stride_h, a->seq_kv, a->num_kv_heads, &tv, "v"},
+      {a->dout, a->do_stride_b, a->do_stride_s, a->do_stride_h, a->seq_q, a->num_heads, &tdo,
+       "dout"}};
+  uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace) + 2 * rows_bytes;
+  for (const Op& op : ops) {
+    if (!split) {
+      if ((st = make_qkv_map(op.map, op.src, a->head_dim, op.S, op.H, a->batch, op.ss, op.sh,
+                             op.sb, op.name)))
+        return st;
+      continue;
+    }
+    // fp32: (hi, lo) planes in the workspace, mapped with the planes as
+    // 2 * heads "heads" of a contiguous tensor, as the fp32 prefill does.
+    const int Dr = a->head_dim;
+    const int64_t hs = Dr, ss = 2ll * op.H * Dr, bs = ss * op.S;
+    cudaError_t e = launch_split_planes(reinterpret_cast<const float*>(op.src), op.sb, op.ss,
+                                        op.sh, a->batch, op.S, op.H, Dr, ws, s);
+    if (e != cudaSuccess) return cuda_fail(e, "enl_attn_backward: split planes");
+    if ((st = make_qkv_map(op.map, ws, Dr, op.S, 2 * op.H, a->batch, ss, hs, bs, op.name)))
+      return st;
+    ws += bwd_planes_bytes(a, op.S, op.H);
+  }
 
   const int s_pad = (int)(n_qt * 128);
   float* lse2 = reinterpret_cast<float*>(a->workspace);
-  float* dsum = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a->workspace) + need / 2);
+  float* dsum = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a->workspace) + rows_bytes);
   BwdPrepParams q;
   q.B = a->batch;
   q.H = a->num_heads;
@@ -627,6 +672,7 @@ int enl_attn_backward(const enl_backward_args* a, void* stream) {
   q.o_sh = a->o_stride_h;
   q.o_f32 = a->o_dtype == ENL_DTYPE_FP32;
   q.dout = a->dout;
+  q.do_f32 = split;
   q.do_sb = a->do_stride_b;
   q.do_ss = a->do_stride_s;
   q.do_sh = a->do_stride_h;
@@ -670,7 +716,7 @@ int enl_attn_backward(const enl_backward_args* a, void* stream) {
                  v4(a->dv, a->dv_stride_b, a->dv_stride_s, a->dv_stride_h);
   }
   const int D = a->head_dim <= 64 ? 64 : 128;
-  cudaError_t e = launch_backward(tq, tk, tv, tdo, q, p, D, reinterpret_cast<cudaStream_t>(stream));
+  cudaError_t e = launch_backward(tq, tk, tv, tdo, q, p, D, split, s);
   if (e != cudaSuccess) return cuda_fail(e, "enl_attn_backward launch");
   return ENL_OK;
 }

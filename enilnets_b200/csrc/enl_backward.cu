@@ -30,6 +30,13 @@
 // warps run. Recomputing S and dP in the dQ pass costs two GEMMs of seven but
 // needs no atomics and no dQ staging.
 //
+// fp32 inputs (split mode, head dim <= 64): every operand arrives as bf16
+// hi and lo planes (x = hi + lo, lo = bf16(x - hi)) and every product takes
+// three MMAs, hi*hi + hi*lo + lo*hi, as K1's split mode does. P^T, dS^T (dS
+// in the dQ pass) are split the same way: their hi halves go over dP as in
+// the bf16 path, their lo halves into the 128 tensor-memory columns that a
+// 64-wide head leaves free. Shared memory holds twice the tiles (195 KB).
+//
 // Warp roles (320 threads): 0-7 elementwise (warps w and w + 4 share TMEM
 // lanes 32 (w % 4) .. + 31 and split the 128 columns in halves), 8 TMA, 9 MMA.
 // Every wait is bounded (mbar_wait): on timeout a device error is recorded
@@ -50,23 +57,37 @@ __device__ __forceinline__ void bulk_load_1d(void* smem_dst, const void* gsrc, u
       : "memory");
 }
 
-template <int D>
+template <int D, bool kSplit>
 struct BwdCfg {
   static constexpr int kThreads = 320;
+  static constexpr int kPlanes = kSplit ? 2 : 1;
   static constexpr int kAtoms = D / 64;
   static constexpr int kAtomBytes = 128 * 128;
-  static constexpr int kTileBytes = 128 * D * 2;
+  static constexpr int kTileBytes = 128 * D * 2;          // one plane of one operand tile
+  static constexpr int kOpBytes = kPlanes * kTileBytes;  // all planes of one operand tile
   static constexpr int kStages = 2;
-  static constexpr int kOffRes = 0;                          // resident pair of tiles
-  static constexpr int kOffStr = 2 * kTileBytes;             // streamed pairs [kStages][2]
-  static constexpr int kOffRow = kOffStr + kStages * 2 * kTileBytes;  // [kStages][2][128] f32
+  static constexpr int kOffRes = 0;                        // resident pair of operand tiles
+  static constexpr int kOffStr = 2 * kOpBytes;             // streamed pairs [kStages][2]
+  static constexpr int kOffRow = kOffStr + kStages * 2 * kOpBytes;  // [kStages][2][128] f32
   static constexpr int kOffBar = kOffRow + kStages * 2 * 128 * 4;
   // res_full, full[kStages], empty[kStages], s_full[2], p_ready[2], done[2], drain
   static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 2 + 1;
   static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
   static constexpr uint32_t kColS = 0, kColDP = 128, kColAcc0 = 256, kColAcc1 = 256 + D;
+  // Split mode: lo halves of the packed P^T / dS^T (dS) of half h at kColLo + 64 h.
+  static constexpr uint32_t kColLo = 256 + 2 * D;
+  static_assert(!kSplit || kColLo + 128 <= 512, "split mode needs 128 free TMEM columns");
+  static constexpr uint32_t kLoPlane = kTileBytes >> 4;  // lo plane, descriptor units
 };
+
+// bf16 pair (a0, a1) into hi[i]; split mode adds the remainders' pair to lo[i].
+template <bool kSplit>
+__device__ __forceinline__ void put_pair(uint32_t* hi, uint32_t* lo, int i, float a0, float a1) {
+  hi[i] = pack_bf16x2(a0, a1);
+  if constexpr (kSplit)
+    lo[i] = pack_bf16x2(a0 - bf16lo_to_f32(hi[i]), a1 - bf16hi_to_f32(hi[i]));
+}
 
 // Query-tile range [lo, hi) that can see key tile kt, and key-tile range that
 // query tile qt can see (causal: key <= query; window: |query - key| <= w).
@@ -120,7 +141,8 @@ __global__ void bwd_prep_kernel(BwdPrepParams q) {
   const long long groups = (long long)gridDim.x * (blockDim.x / 16);
   const long long total = (long long)q.B * q.H * q.s_pad;
   const __nv_bfloat16* dob = reinterpret_cast<const __nv_bfloat16*>(q.dout);
-  const bool vec = !q.o_f32 && q.d_real % 8 == 0 && q.o_sb % 8 == 0 && q.o_ss % 8 == 0 &&
+  const float* dof = reinterpret_cast<const float*>(q.dout);
+  const bool vec = !q.o_f32 && !q.do_f32 && q.d_real % 8 == 0 && q.o_sb % 8 == 0 && q.o_ss % 8 == 0 &&
                    q.o_sh % 8 == 0 && (reinterpret_cast<uintptr_t>(q.o) & 15u) == 0;
   for (long long idx = blockIdx.x * (long long)(blockDim.x / 16) + threadIdx.x / 16; idx < total;
        idx += groups) {
@@ -148,7 +170,7 @@ __global__ void bwd_prep_kernel(BwdPrepParams q) {
           const float o = q.o_f32 ? reinterpret_cast<const float*>(q.o)[oo + d]
                                   : __bfloat162float(
                                         reinterpret_cast<const __nv_bfloat16*>(q.o)[oo + d]);
-          acc = fmaf(o, __bfloat162float(dob[od + d]), acc);
+          acc = fmaf(o, q.do_f32 ? dof[od + d] : __bfloat162float(dob[od + d]), acc);
         }
       }
     }
@@ -199,13 +221,13 @@ __device__ __forceinline__ void store_rows(const float* stg, float* base, long l
 // dK, dV. CTA c -> key tile c / (B * Hkv) (small tiles first: under a causal
 // mask they see the most query tiles), (b, kv head) c % (B * Hkv).
 // ---------------------------------------------------------------------------
-template <int D>
+template <int D, bool kSplit>
 __global__ void __launch_bounds__(320, 1)
     attn_bwd_dkdv_sm100(const __grid_constant__ CUtensorMap tm_q,
                         const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v,
                         const __grid_constant__ CUtensorMap tm_do, const BwdParams p) {
-  using Cfg = BwdCfg<D>;
+  using Cfg = BwdCfg<D, kSplit>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -253,13 +275,15 @@ __global__ void __launch_bounds__(320, 1)
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       tma_prefetch_desc(&tm_do);
-      mbar_arrive_expect_tx(bar_res, 2 * Cfg::kTileBytes);
-      for (int a = 0; a < Cfg::kAtoms; ++a) {
-        tma_load_4d(smem + Cfg::kOffRes + a * Cfg::kAtomBytes, &tm_k, bar_res, a * 64, kt * 128,
-                    hkv, b);
-        tma_load_4d(smem + Cfg::kOffRes + Cfg::kTileBytes + a * Cfg::kAtomBytes, &tm_v, bar_res,
-                    a * 64, kt * 128, hkv, b);
-      }
+      // Split mode: plane pl of head h is "head" kPlanes * h + pl of the maps.
+      mbar_arrive_expect_tx(bar_res, 2 * Cfg::kOpBytes);
+      for (int pl = 0; pl < Cfg::kPlanes; ++pl)
+        for (int a = 0; a < Cfg::kAtoms; ++a) {
+          uint8_t* dst = smem + Cfg::kOffRes + pl * Cfg::kTileBytes + a * Cfg::kAtomBytes;
+          const int hp = Cfg::kPlanes * hkv + pl;
+          tma_load_4d(dst, &tm_k, bar_res, a * 64, kt * 128, hp, b);
+          tma_load_4d(dst + Cfg::kOpBytes, &tm_v, bar_res, a * 64, kt * 128, hp, b);
+        }
       int issued = 0;
       bool ok = true;
       for (int u = 0; u < n_units; ++u) {
@@ -268,13 +292,15 @@ __global__ void __launch_bounds__(320, 1)
         if (u >= Cfg::kStages) ok = mbar_wait(bar_empty + st, (u / Cfg::kStages - 1) & 1,
                                               abort_flag, 80);
         if (!ok) break;
-        uint8_t* dst = smem + Cfg::kOffStr + st * 2 * Cfg::kTileBytes;
-        mbar_arrive_expect_tx(bar_full + st, 2 * Cfg::kTileBytes + 2 * 512);
-        for (int a = 0; a < Cfg::kAtoms; ++a) {
-          tma_load_4d(dst + a * Cfg::kAtomBytes, &tm_q, bar_full + st, a * 64, qt * 128, h, b);
-          tma_load_4d(dst + Cfg::kTileBytes + a * Cfg::kAtomBytes, &tm_do, bar_full + st, a * 64,
-                      qt * 128, h, b);
-        }
+        uint8_t* dst = smem + Cfg::kOffStr + st * 2 * Cfg::kOpBytes;
+        mbar_arrive_expect_tx(bar_full + st, 2 * Cfg::kOpBytes + 2 * 512);
+        for (int pl = 0; pl < Cfg::kPlanes; ++pl)
+          for (int a = 0; a < Cfg::kAtoms; ++a) {
+            uint8_t* d2 = dst + pl * Cfg::kTileBytes + a * Cfg::kAtomBytes;
+            const int hp = Cfg::kPlanes * h + pl;
+            tma_load_4d(d2, &tm_q, bar_full + st, a * 64, qt * 128, hp, b);
+            tma_load_4d(d2 + Cfg::kOpBytes, &tm_do, bar_full + st, a * 64, qt * 128, hp, b);
+          }
         const long long roff = ((long long)b * p.H + h) * p.s_pad + (long long)qt * 128;
         bulk_load_1d(rows + st * 256, p.lse2 + roff, 512, bar_full + st);
         bulk_load_1d(rows + st * 256 + 128, p.dsum + roff, 512, bar_full + st);
@@ -292,12 +318,13 @@ __global__ void __launch_bounds__(320, 1)
     const uint32_t idesc_s = idesc_bf16_f32(128, 64, false);  // one 64-query half
     const uint32_t idesc_o = idesc_bf16_f32(128, D, true);
     const uint32_t k_lo = desc_lo(smem_u32(smem + Cfg::kOffRes), 16);
-    const uint32_t v_lo = k_lo + (Cfg::kTileBytes >> 4);
+    const uint32_t v_lo = k_lo + (Cfg::kOpBytes >> 4);
+    constexpr uint32_t kLo = Cfg::kLoPlane;
     auto wait = [&](uint64_t* bar, uint32_t parity, int site) {
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, site));
     };
     auto stage = [&](int u) {
-      return smem_u32(smem + Cfg::kOffStr + (u % Cfg::kStages) * 2 * Cfg::kTileBytes);
+      return smem_u32(smem + Cfg::kOffStr + (u % Cfg::kStages) * 2 * Cfg::kOpBytes);
     };
     // S^T and dP^T of query half h of unit u: K Q_h^T and V dO_h^T, where
     // Q_h / dO_h are rows 64h.. of the streamed tiles (64 rows x 128 bytes
@@ -312,10 +339,14 @@ __global__ void __launch_bounds__(320, 1)
           umma_ss_elect<false>(ds, k_lo + off, q_k + off, kDescHiSw128, idesc_s);
         else
           umma_ss_elect<true>(ds, k_lo + off, q_k + off, kDescHiSw128, idesc_s);
+        if constexpr (kSplit) {
+          umma_ss_elect<true>(ds, k_lo + off, q_k + kLo + off, kDescHiSw128, idesc_s);
+          umma_ss_elect<true>(ds, k_lo + kLo + off, q_k + off, kDescHiSw128, idesc_s);
+        }
       }
     };
     auto issue_dp = [&](int u, int h) {
-      const uint32_t o_k = desc_lo(stage(u), 16) + h * (8192 >> 4) + (Cfg::kTileBytes >> 4);
+      const uint32_t o_k = desc_lo(stage(u), 16) + h * (8192 >> 4) + (Cfg::kOpBytes >> 4);
       const uint32_t dp = tmem + Cfg::kColDP + 64 * h;
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
@@ -324,6 +355,10 @@ __global__ void __launch_bounds__(320, 1)
           umma_ss_elect<false>(dp, v_lo + off, o_k + off, kDescHiSw128, idesc_s);
         else
           umma_ss_elect<true>(dp, v_lo + off, o_k + off, kDescHiSw128, idesc_s);
+        if constexpr (kSplit) {
+          umma_ss_elect<true>(dp, v_lo + off, o_k + kLo + off, kDescHiSw128, idesc_s);
+          umma_ss_elect<true>(dp, v_lo + kLo + off, o_k + off, kDescHiSw128, idesc_s);
+        }
       }
       umma_commit_elect(bar_s_full + h);  // S and dP of the half
     };
@@ -331,15 +366,23 @@ __global__ void __launch_bounds__(320, 1)
     // dS^T_h are packed over the half's dP columns (first and second 32).
     auto issue_acc = [&](int u, int h) {
       const uint32_t q_mn = desc_lo(stage(u), Cfg::kAtomBytes);
-      const uint32_t o_mn = q_mn + (Cfg::kTileBytes >> 4);
+      const uint32_t o_mn = q_mn + (Cfg::kOpBytes >> 4);
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         const uint32_t boff = (h * 4 + kk) * (2048 >> 4);  // 16 query rows per step
         const uint32_t acc = (u > 0 || h > 0 || kk > 0) ? 1u : 0u;
-        umma_ts_elect(tmem + Cfg::kColAcc0, tmem + Cfg::kColDP + h * 64 + kk * 8, o_mn + boff,
-                      kDescHiSw128, idesc_o, acc);
-        umma_ts_elect(tmem + Cfg::kColAcc1, tmem + Cfg::kColDP + h * 64 + 32 + kk * 8,
-                      q_mn + boff, kDescHiSw128, idesc_o, acc);
+        const uint32_t p_hi = tmem + Cfg::kColDP + h * 64 + kk * 8;
+        const uint32_t s_hi = p_hi + 32;
+        umma_ts_elect(tmem + Cfg::kColAcc0, p_hi, o_mn + boff, kDescHiSw128, idesc_o, acc);
+        umma_ts_elect(tmem + Cfg::kColAcc1, s_hi, q_mn + boff, kDescHiSw128, idesc_o, acc);
+        if constexpr (kSplit) {
+          const uint32_t p_lo = tmem + Cfg::kColLo + h * 64 + kk * 8;
+          const uint32_t s_lo = p_lo + 32;
+          umma_ts_elect(tmem + Cfg::kColAcc0, p_hi, o_mn + kLo + boff, kDescHiSw128, idesc_o, 1u);
+          umma_ts_elect(tmem + Cfg::kColAcc0, p_lo, o_mn + boff, kDescHiSw128, idesc_o, 1u);
+          umma_ts_elect(tmem + Cfg::kColAcc1, s_hi, q_mn + kLo + boff, kDescHiSw128, idesc_o, 1u);
+          umma_ts_elect(tmem + Cfg::kColAcc1, s_lo, q_mn + boff, kDescHiSw128, idesc_o, 1u);
+        }
       }
       umma_commit_elect(bar_done + h);
       if (h == 1) umma_commit_elect(bar_empty + u % Cfg::kStages);  // Q, dO of u read
@@ -405,6 +448,7 @@ __global__ void __launch_bounds__(320, 1)
       for (int ch = 0; ch < 2; ++ch) {
         const int c0 = 64 * half + 32 * ch;  // first query column of the chunk
         uint32_t sr[32], pk[16], dk[16];
+        uint32_t pl[kSplit ? 16 : 1], dl[kSplit ? 16 : 1];  // split mode: lo halves
         const uint32_t* dr = dph + 32 * ch;
         ENL_TMEM_LD32(lane_addr + Cfg::kColS + c0, sr, 0);
         const long long i0 = (long long)qt * 128 + c0;
@@ -422,12 +466,12 @@ __global__ void __launch_bounds__(320, 1)
             const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c + 1]), p.scale_log2, -L.y));
             const float p2 = fast_exp2(fmaf(__uint_as_float(sr[c + 2]), p.scale_log2, -L.z));
             const float p3 = fast_exp2(fmaf(__uint_as_float(sr[c + 3]), p.scale_log2, -L.w));
-            pk[c / 2] = pack_bf16x2(p0, p1);
-            pk[c / 2 + 1] = pack_bf16x2(p2, p3);
-            dk[c / 2] = pack_bf16x2(p0 * (__uint_as_float(dr[c]) - Dd.x),
-                                    p1 * (__uint_as_float(dr[c + 1]) - Dd.y));
-            dk[c / 2 + 1] = pack_bf16x2(p2 * (__uint_as_float(dr[c + 2]) - Dd.z),
-                                        p3 * (__uint_as_float(dr[c + 3]) - Dd.w));
+            put_pair<kSplit>(pk, pl, c / 2, p0, p1);
+            put_pair<kSplit>(pk, pl, c / 2 + 1, p2, p3);
+            put_pair<kSplit>(dk, dl, c / 2, p0 * (__uint_as_float(dr[c]) - Dd.x),
+                             p1 * (__uint_as_float(dr[c + 1]) - Dd.y));
+            put_pair<kSplit>(dk, dl, c / 2 + 1, p2 * (__uint_as_float(dr[c + 2]) - Dd.z),
+                             p3 * (__uint_as_float(dr[c + 3]) - Dd.w));
           }
         } else {
 #pragma unroll
@@ -437,13 +481,17 @@ __global__ void __launch_bounds__(320, 1)
                      lse2[c0 + c], dsum[c0 + c], p0, d0);
             bwd_elem(p, __uint_as_float(sr[c + 1]), __uint_as_float(dr[c + 1]), i0 + c + 1, j,
                      slope2, lse2[c0 + c + 1], dsum[c0 + c + 1], p1, d1);
-            pk[c / 2] = pack_bf16x2(p0, p1);
-            dk[c / 2] = pack_bf16x2(d0, d1);
+            put_pair<kSplit>(pk, pl, c / 2, p0, p1);
+            put_pair<kSplit>(dk, dl, c / 2, d0, d1);
           }
         }
         // packed P^T over the half's first 32 dP columns, dS^T over the last 32
         ENL_TMEM_ST16(lane_addr + Cfg::kColDP + 64 * half + 16 * ch, pk);
         ENL_TMEM_ST16(lane_addr + Cfg::kColDP + 64 * half + 32 + 16 * ch, dk);
+        if constexpr (kSplit) {
+          ENL_TMEM_ST16(lane_addr + Cfg::kColLo + 64 * half + 16 * ch, pl);
+          ENL_TMEM_ST16(lane_addr + Cfg::kColLo + 64 * half + 32 + 16 * ch, dl);
+        }
       }
       tmem_st_wait();
       tc_fence_before();
@@ -499,13 +547,13 @@ __global__ void __launch_bounds__(320, 1)
 // dQ. CTA c -> query tile (last first: under a causal mask it sees the most
 // key tiles), (b, head) c % (B * H).
 // ---------------------------------------------------------------------------
-template <int D>
+template <int D, bool kSplit>
 __global__ void __launch_bounds__(320, 1)
     attn_bwd_dq_sm100(const __grid_constant__ CUtensorMap tm_q,
                       const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v,
                       const __grid_constant__ CUtensorMap tm_do, const BwdParams p) {
-  using Cfg = BwdCfg<D>;
+  using Cfg = BwdCfg<D, kSplit>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -551,13 +599,14 @@ __global__ void __launch_bounds__(320, 1)
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       tma_prefetch_desc(&tm_do);
-      mbar_arrive_expect_tx(bar_res, 2 * Cfg::kTileBytes);
-      for (int a = 0; a < Cfg::kAtoms; ++a) {
-        tma_load_4d(smem + Cfg::kOffRes + a * Cfg::kAtomBytes, &tm_q, bar_res, a * 64, qt * 128,
-                    h, b);
-        tma_load_4d(smem + Cfg::kOffRes + Cfg::kTileBytes + a * Cfg::kAtomBytes, &tm_do, bar_res,
-                    a * 64, qt * 128, h, b);
-      }
+      mbar_arrive_expect_tx(bar_res, 2 * Cfg::kOpBytes);
+      for (int pl = 0; pl < Cfg::kPlanes; ++pl)
+        for (int a = 0; a < Cfg::kAtoms; ++a) {
+          uint8_t* dst = smem + Cfg::kOffRes + pl * Cfg::kTileBytes + a * Cfg::kAtomBytes;
+          const int hp = Cfg::kPlanes * h + pl;
+          tma_load_4d(dst, &tm_q, bar_res, a * 64, qt * 128, hp, b);
+          tma_load_4d(dst + Cfg::kOpBytes, &tm_do, bar_res, a * 64, qt * 128, hp, b);
+        }
       int issued = 0;
       bool ok = true;
       for (int u = 0; u < n_units; ++u) {
@@ -566,13 +615,15 @@ __global__ void __launch_bounds__(320, 1)
         if (u >= Cfg::kStages) ok = mbar_wait(bar_empty + st, (u / Cfg::kStages - 1) & 1,
                                               abort_flag, 100);
         if (!ok) break;
-        uint8_t* dst = smem + Cfg::kOffStr + st * 2 * Cfg::kTileBytes;
-        mbar_arrive_expect_tx(bar_full + st, 2 * Cfg::kTileBytes);
-        for (int a = 0; a < Cfg::kAtoms; ++a) {
-          tma_load_4d(dst + a * Cfg::kAtomBytes, &tm_k, bar_full + st, a * 64, kt * 128, hkv, b);
-          tma_load_4d(dst + Cfg::kTileBytes + a * Cfg::kAtomBytes, &tm_v, bar_full + st, a * 64,
-                      kt * 128, hkv, b);
-        }
+        uint8_t* dst = smem + Cfg::kOffStr + st * 2 * Cfg::kOpBytes;
+        mbar_arrive_expect_tx(bar_full + st, 2 * Cfg::kOpBytes);
+        for (int pl = 0; pl < Cfg::kPlanes; ++pl)
+          for (int a = 0; a < Cfg::kAtoms; ++a) {
+            uint8_t* d2 = dst + pl * Cfg::kTileBytes + a * Cfg::kAtomBytes;
+            const int hp = Cfg::kPlanes * hkv + pl;
+            tma_load_4d(d2, &tm_k, bar_full + st, a * 64, kt * 128, hp, b);
+            tma_load_4d(d2 + Cfg::kOpBytes, &tm_v, bar_full + st, a * 64, kt * 128, hp, b);
+          }
         ++issued;
       }
       volatile int no_abort = 0;
@@ -585,12 +636,13 @@ __global__ void __launch_bounds__(320, 1)
     const uint32_t idesc_s = idesc_bf16_f32(128, 64, false);  // one 64-key half
     const uint32_t idesc_o = idesc_bf16_f32(128, D, true);
     const uint32_t q_lo = desc_lo(smem_u32(smem + Cfg::kOffRes), 16);
-    const uint32_t o_lo = q_lo + (Cfg::kTileBytes >> 4);
+    const uint32_t o_lo = q_lo + (Cfg::kOpBytes >> 4);
+    constexpr uint32_t kLo = Cfg::kLoPlane;
     auto wait = [&](uint64_t* bar, uint32_t parity, int site) {
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, site));
     };
     auto stage = [&](int u) {
-      return smem_u32(smem + Cfg::kOffStr + (u % Cfg::kStages) * 2 * Cfg::kTileBytes);
+      return smem_u32(smem + Cfg::kOffStr + (u % Cfg::kStages) * 2 * Cfg::kOpBytes);
     };
     // S and dP of key half h of unit u: Q K_h^T and dO V_h^T.
     auto issue_s = [&](int u, int h) {
@@ -603,10 +655,14 @@ __global__ void __launch_bounds__(320, 1)
           umma_ss_elect<false>(ds, q_lo + off, k_k + off, kDescHiSw128, idesc_s);
         else
           umma_ss_elect<true>(ds, q_lo + off, k_k + off, kDescHiSw128, idesc_s);
+        if constexpr (kSplit) {
+          umma_ss_elect<true>(ds, q_lo + off, k_k + kLo + off, kDescHiSw128, idesc_s);
+          umma_ss_elect<true>(ds, q_lo + kLo + off, k_k + off, kDescHiSw128, idesc_s);
+        }
       }
     };
     auto issue_dp = [&](int u, int h) {
-      const uint32_t v_k = desc_lo(stage(u), 16) + h * (8192 >> 4) + (Cfg::kTileBytes >> 4);
+      const uint32_t v_k = desc_lo(stage(u), 16) + h * (8192 >> 4) + (Cfg::kOpBytes >> 4);
       const uint32_t dp = tmem + Cfg::kColDP + 64 * h;
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
@@ -615,6 +671,10 @@ __global__ void __launch_bounds__(320, 1)
           umma_ss_elect<false>(dp, o_lo + off, v_k + off, kDescHiSw128, idesc_s);
         else
           umma_ss_elect<true>(dp, o_lo + off, v_k + off, kDescHiSw128, idesc_s);
+        if constexpr (kSplit) {
+          umma_ss_elect<true>(dp, o_lo + off, v_k + kLo + off, kDescHiSw128, idesc_s);
+          umma_ss_elect<true>(dp, o_lo + kLo + off, v_k + off, kDescHiSw128, idesc_s);
+        }
       }
       umma_commit_elect(bar_s_full + h);
     };
@@ -626,8 +686,13 @@ __global__ void __launch_bounds__(320, 1)
       for (int kk = 0; kk < 4; ++kk) {
         const uint32_t boff = (h * 4 + kk) * (2048 >> 4);  // 16 key rows per step
         const uint32_t acc = (u > 0 || h > 0 || kk > 0) ? 1u : 0u;
-        umma_ts_elect(tmem + Cfg::kColAcc0, tmem + Cfg::kColDP + h * 64 + kk * 8, k_mn + boff,
-                      kDescHiSw128, idesc_o, acc);
+        const uint32_t s_hi = tmem + Cfg::kColDP + h * 64 + kk * 8;
+        umma_ts_elect(tmem + Cfg::kColAcc0, s_hi, k_mn + boff, kDescHiSw128, idesc_o, acc);
+        if constexpr (kSplit) {
+          const uint32_t s_lo = tmem + Cfg::kColLo + h * 64 + kk * 8;
+          umma_ts_elect(tmem + Cfg::kColAcc0, s_hi, k_mn + kLo + boff, kDescHiSw128, idesc_o, 1u);
+          umma_ts_elect(tmem + Cfg::kColAcc0, s_lo, k_mn + boff, kDescHiSw128, idesc_o, 1u);
+        }
       }
       umma_commit_elect(bar_done + h);
       if (h == 1) umma_commit_elect(bar_empty + u % Cfg::kStages);  // K, V of u read
@@ -686,6 +751,7 @@ __global__ void __launch_bounds__(320, 1)
       for (int ch = 0; ch < 2; ++ch) {
         const int c0 = 64 * half + 32 * ch;  // first key column of the chunk
         uint32_t sr[32], dk[16];
+        uint32_t dl[kSplit ? 16 : 1];  // split mode: lo halves
         const uint32_t* dr = dph + 32 * ch;
         ENL_TMEM_LD32(lane_addr + Cfg::kColS + c0, sr, 0);
         const long long j0 = (long long)kt * 128 + c0;
@@ -696,8 +762,8 @@ __global__ void __launch_bounds__(320, 1)
           for (int c = 0; c < 32; c += 2) {
             const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c]), p.scale_log2, -lse2));
             const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c + 1]), p.scale_log2, -lse2));
-            dk[c / 2] = pack_bf16x2(p0 * (__uint_as_float(dr[c]) - dsum),
-                                    p1 * (__uint_as_float(dr[c + 1]) - dsum));
+            put_pair<kSplit>(dk, dl, c / 2, p0 * (__uint_as_float(dr[c]) - dsum),
+                             p1 * (__uint_as_float(dr[c + 1]) - dsum));
           }
         } else {
 #pragma unroll
@@ -707,10 +773,11 @@ __global__ void __launch_bounds__(320, 1)
                      dsum, p0, d0);
             bwd_elem(p, __uint_as_float(sr[c + 1]), __uint_as_float(dr[c + 1]), i, j0 + c + 1,
                      slope2, lse2, dsum, p1, d1);
-            dk[c / 2] = pack_bf16x2(d0, d1);
+            put_pair<kSplit>(dk, dl, c / 2, d0, d1);
           }
         }
         ENL_TMEM_ST16(lane_addr + Cfg::kColDP + 64 * half + 16 * ch, dk);
+        if constexpr (kSplit) ENL_TMEM_ST16(lane_addr + Cfg::kColLo + 64 * half + 16 * ch, dl);
       }
       tmem_st_wait();
       tc_fence_before();
@@ -751,10 +818,10 @@ __global__ void __launch_bounds__(320, 1)
   }
 }
 
-template <int D>
+template <int D, bool kSplit>
 cudaError_t launch_bwd_main(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                             const CUtensorMap& tdo, const BwdParams& p, cudaStream_t stream) {
-  using Cfg = BwdCfg<D>;
+  using Cfg = BwdCfg<D, kSplit>;
   static bool configured[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -762,31 +829,33 @@ cudaError_t launch_bwd_main(const CUtensorMap& tq, const CUtensorMap& tk, const 
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
     const cudaFuncAttribute a = cudaFuncAttributeMaxDynamicSharedMemorySize;
-    e = cudaFuncSetAttribute(attn_bwd_dkdv_sm100<D>, a, Cfg::kSmemBytes);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_bwd_dq_sm100<D>, a, Cfg::kSmemBytes);
+    e = cudaFuncSetAttribute(attn_bwd_dkdv_sm100<D, kSplit>, a, Cfg::kSmemBytes);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_bwd_dq_sm100<D, kSplit>, a, Cfg::kSmemBytes);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
   const long long n_kt = (p.Skv + 127) / 128, n_qt = (p.Sq + 127) / 128;
-  attn_bwd_dkdv_sm100<D><<<(unsigned)(n_kt * p.B * p.Hkv), Cfg::kThreads, Cfg::kSmemBytes,
+  attn_bwd_dkdv_sm100<D, kSplit><<<(unsigned)(n_kt * p.B * p.Hkv), Cfg::kThreads, Cfg::kSmemBytes,
                            stream>>>(tq, tk, tv, tdo, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  attn_bwd_dq_sm100<D><<<(unsigned)(n_qt * p.B * p.H), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(
+  attn_bwd_dq_sm100<D, kSplit><<<(unsigned)(n_qt * p.B * p.H), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(
       tq, tk, tv, tdo, p);
   return cudaGetLastError();
 }
 
 cudaError_t launch_backward(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                             const CUtensorMap& tdo, const BwdPrepParams& prep, const BwdParams& p,
-                            int D, cudaStream_t stream) {
+                            int D, bool split, cudaStream_t stream) {
   const long long rows = (long long)prep.B * prep.H * prep.s_pad;
   const long long blocks = min((rows + 15) / 16, 148ll * 32);  // 16 rows per 256-thread block
   bwd_prep_kernel<<<(int)blocks, 256, 0, stream>>>(prep);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  return D == 128 ? launch_bwd_main<128>(tq, tk, tv, tdo, p, stream)
-                  : launch_bwd_main<64>(tq, tk, tv, tdo, p, stream);
+  if (split)  // the ABI admits split mode only at head dims <= 64
+    return launch_bwd_main<64, true>(tq, tk, tv, tdo, p, stream);
+  return D == 128 ? launch_bwd_main<128, false>(tq, tk, tv, tdo, p, stream)
+                  : launch_bwd_main<64, false>(tq, tk, tv, tdo, p, stream);
 }
 
 }  // namespace enl

@@ -98,8 +98,9 @@ struct BwdPrepParams {
   const void* o;  // forward output (B, Sq, H, D), bf16 or fp32
   long long o_sb, o_ss, o_sh;
   int o_f32;
-  const void* dout;  // bf16 (B, Sq, H, D)
+  const void* dout;  // (B, Sq, H, D), bf16 or fp32
   long long do_sb, do_ss, do_sh;
+  int do_f32;
   const float* lse;  // (B, H, Sq) natural-log LSE of the forward
   float* lse2;       // out (B * H, s_pad): LSE * log2(e), +inf on pad rows
   float* dsum;       // out (B * H, s_pad): rowsum(dO * O), 0 on pad rows
@@ -123,7 +124,7 @@ struct BwdParams {
 };
 cudaError_t launch_backward(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                             const CUtensorMap& tdo, const BwdPrepParams& prep, const BwdParams& p,
-                            int D, cudaStream_t stream);
+                            int D, bool split, cudaStream_t stream);
 
 // Column masks of a block-sparse layout (enl_sparse.cu).
 struct SparseMaskParams {

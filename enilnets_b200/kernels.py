@@ -244,15 +244,20 @@ def attention_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: tor
                        scale: Optional[float] = None, out=None):
     """dQ, dK, dV of attention_prefill (K5, nn/flash_attention.py:83-114).
 
-    q: (B, Sq, H, D), k, v: (B, Skv, Hkv, D), dout like o: bf16 (the forward's
-    operands); o: the forward output, bf16 or fp32; lse: (B, H, Sq) fp32 from
+    q: (B, Sq, H, D), k, v: (B, Skv, Hkv, D), dout like o: one dtype, bf16
+    (the forward's operands) or fp32 (split into bf16 hi/lo planes, three
+    MMAs per product, as attention_prefill does for fp32; D <= 64); o: the
+    forward output, bf16 or fp32; lse: (B, H, Sq) fp32 from
     attention_prefill(..., return_lse=True). Returns fp32 dq (B, Sq, H, D) and
     dk, dv (B, Skv, Hkv, D), dk/dv summed over each kv head's query heads;
     out=(dq, dk, dv) writes into given fp32 views of those shapes instead
     (any strides with a contiguous head dim).
     """
+    in_dt = q.dtype if isinstance(q, torch.Tensor) else None
+    if in_dt not in _DTYPES:
+        raise ValueError(f"q must be bfloat16 or float32 (got {in_dt})")
     for name, t in (("q", q), ("k", k), ("v", v), ("dout", dout)):
-        _require_cuda(name, t, torch.bfloat16)
+        _require_cuda(name, t, in_dt)
         if t.dim() != 4:
             raise ValueError(f"{name} must be 4-D (batch, seq, heads, head_dim)")
     _require_cuda("o", o)
@@ -299,6 +304,7 @@ def attention_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: tor
         setattr(a, f"{name}_stride_s", t.stride(1))
         setattr(a, f"{name}_stride_h", t.stride(2))
     a.o_dtype = _DTYPES[o.dtype]
+    a.in_dtype = _DTYPES[in_dt]
     a.causal = int(bool(causal))
     a.window = -1 if window is None else int(window)
     a.alibi_slopes = _ptr(alibi_slopes)

@@ -13,10 +13,12 @@ attention core read, its output and LSE) and the backward runs K5
   RoPE layers: dQh, dKh rotated back by -angle     (nn/backward.py:300-308)
   d_Wq = dQ^T x_in, d_bq = sum dQ, ... ; dx = dQ Wq + dK Wk + dV Wv.
 
-The attention core runs on bf16 operands with fp32 accumulation in both
-directions, whatever set_precision chose for the projections (which run in
-fp32 GEMMs here): the backward kernels have no split-bf16 variant. Softmax
-layers only (plain and tiled_block_size, which compute the same function);
+The projections run in fp32 GEMMs. The attention core follows set_precision
+in both directions: under "fp32" (the reference's float32 models) Q, K, V,
+the output and dO stay fp32 and K1 / K5 split them into bf16 hi/lo planes
+(three MMAs per product), for head dims up to 64, where the split backward
+fits in shared memory; wider heads, and the "bf16" precision, run the core
+on bf16 operands with fp32 accumulation. Softmax layers only (plain and tiled_block_size, which compute the same function);
 linearized kernels, sparse patterns and attention dropout raise ValueError.
 """
 from __future__ import annotations
@@ -25,7 +27,7 @@ from typing import Any, Dict, Tuple
 
 import numpy as np
 
-from . import attention, kernels
+from . import attention, backend, kernels
 from .backend import to_device, to_numpy
 
 _NEG_SIN: dict = {}
@@ -58,6 +60,14 @@ def _unrotate(t, pos0: int = 0):
     return t
 
 
+def _core_dtype(head_dim: int):
+    """Operand dtype of the attention core for this precision and head dim."""
+    import torch
+    if backend.compute_dtype() == torch.float32 and head_dim <= 64:
+        return torch.float32
+    return torch.bfloat16
+
+
 def _weights_f32(layer, names):
     import torch
     return attention._WEIGHTS.get(layer, names, "w", torch.float32)
@@ -75,7 +85,8 @@ def self_attention_forward_train(layer: Dict[str, Any], x) -> Tuple[Any, Dict[st
     x = x.float()
     w = _weights_f32(layer, ("Wq", "Wk", "Wv"))
     b = attention._WEIGHTS.get(layer, ("bq", "bk", "bv"), "b", torch.float32)
-    qkv = F.linear(x, w, b).to(torch.bfloat16)
+    core = _core_dtype(D)
+    qkv = F.linear(x, w, b).to(core)
     q = attention.split_heads(qkv, H, D, 0)
     k = attention.split_heads(qkv, Hkv, D, H * D)
     v = attention.split_heads(qkv, Hkv, D, H * D + Hkv * D)
@@ -87,7 +98,7 @@ def self_attention_forward_train(layer: Dict[str, Any], x) -> Tuple[Any, Dict[st
     window = layer.get("window_size")
     slopes = attention.alibi_tensor(H) if scheme == "alibi" else None
     o, lse = kernels.attention_prefill(q, k, v, causal=causal, window=window,
-                                       alibi_slopes=slopes, out_dtype=torch.bfloat16,
+                                       alibi_slopes=slopes, out_dtype=core,
                                        return_lse=True)
     ctx = o.flatten(-2).float()
     wo = _weights_f32(layer, ("Wo",))
@@ -110,7 +121,7 @@ def self_attention_backward(layer: Dict[str, Any], cache: Dict[str, Any],
     dout = dout.float()
     d2 = dout.reshape(-1, E)
     grads = {"d_Wo": d2.T @ cache["ctx"].reshape(-1, E), "d_bo": d2.sum(0)}
-    dctx = (dout @ _weights_f32(layer, ("Wo",))).unflatten(-1, (H, D)).to(torch.bfloat16)
+    dctx = (dout @ _weights_f32(layer, ("Wo",))).unflatten(-1, (H, D)).to(cache["q"].dtype)
     dq, dk, dv = kernels.attention_backward(cache["q"], cache["k"], cache["v"], cache["o"],
                                             cache["lse"], dctx, causal=cache["causal"],
                                             window=cache["window"],

@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define ENL_ABI_VERSION 7
+#define ENL_ABI_VERSION 8
 
 /* Status codes. The Python binding maps INVALID/UNSUPPORTED to ValueError
  * (the reference raises ValueError for bad layer configurations,
@@ -344,11 +344,11 @@ size_t enl_linear_workspace_bytes(const enl_linear_args* args);
 
 /* --------------------------------------------------------------- backward */
 typedef struct enl_backward_args {
-  const void* q;    /* bf16 (batch, seq_q, num_heads, head_dim), as given to the forward */
-  const void* k;    /* bf16 (batch, seq_kv, num_kv_heads, head_dim) */
-  const void* v;    /* bf16 (batch, seq_kv, num_kv_heads, head_dim) */
+  const void* q;    /* in_dtype (batch, seq_q, num_heads, head_dim), as given to the forward */
+  const void* k;    /* in_dtype (batch, seq_kv, num_kv_heads, head_dim) */
+  const void* v;    /* in_dtype (batch, seq_kv, num_kv_heads, head_dim) */
   const void* o;    /* forward output (batch, seq_q, num_heads, head_dim), o_dtype */
-  const void* dout; /* bf16 gradient of o, same shape */
+  const void* dout; /* in_dtype gradient of o, same shape */
   const float* lse; /* (batch, num_heads, seq_q) natural-log LSE from enl_attn_prefill */
   float* dq;        /* fp32 (batch, seq_q, num_heads, head_dim) */
   float* dk;        /* fp32 (batch, seq_kv, num_kv_heads, head_dim), summed over the group */
@@ -369,18 +369,23 @@ typedef struct enl_backward_args {
   float scale;               /* the forward's softmax scale */
   void* workspace;           /* >= enl_backward_workspace_bytes(), 256-byte aligned */
   size_t workspace_bytes;
+  int32_t in_dtype; /* q, k, v, dout: ENL_DTYPE_BF16, or ENL_DTYPE_FP32 (split-bf16 operands,
+                       head_dim <= 64; 16-byte aligned, strides multiples of 4 elements) */
 } enl_backward_args;
 
 /* Attention backward: dQ, dK, dV of softmax(Q K^T * scale + bias + mask) V
  * from dO, recomputing the probabilities from the forward's LSE, as
  * nn/flash_attention.py:83-114 does with its row statistics. bf16 operands,
- * fp32 accumulation and outputs; head_dim a multiple of 8 up to 128. With
- * GQA, dK and dV of a kv head sum its query heads (the adjoint of the
- * reference's _repeat_kv, nn/forward.py:165-171). */
+ * or fp32 operands split into bf16 hi/lo planes (three MMAs per product, as
+ * the fp32 prefill), fp32 accumulation and outputs; head_dim a multiple of 8
+ * up to 128 (up to 64 for fp32). With GQA, dK and dV of a kv head sum its
+ * query heads (the adjoint of the reference's _repeat_kv,
+ * nn/forward.py:165-171). */
 int enl_attn_backward(const enl_backward_args* args, void* stream);
 
 /* Workspace bytes enl_attn_backward needs: two fp32 rows per query, padded
- * to whole 128-row tiles. */
+ * to whole 128-row tiles, plus (fp32 inputs) the bf16 hi/lo planes of q, k,
+ * v and dout. */
 size_t enl_backward_workspace_bytes(const enl_backward_args* args);
 
 /* -------------------------------------------------- block-sparse attention */

@@ -34,7 +34,7 @@ def test_library_exports_every_declared_symbol():
     for name in declared_functions():
         assert hasattr(lib, name), f"{name} declared in enl_attn.h but not exported"
         assert name in _native.SIGNATURES, f"{name} has no ctypes signature"
-    assert lib.enl_abi_version() == _native.ABI_VERSION == 7
+    assert lib.enl_abi_version() == _native.ABI_VERSION == 8
 
 
 def test_nm_shows_c_linkage():
