@@ -677,9 +677,31 @@ def bench_backward(dist: Dist, clocks: ClockSampler, warmup: int, steps: int = 1
     pairs = B * H * S * (S + 1) / 2
     tf = dist.sum(10.0 * D * pairs) / (ms * 1e-3) / 1e12
     peak = float(load_peaks()[0]["bf16_tflops"])
-    return {"ms_per_step": ms, "TFLOP_s": tf, "frac_of_bf16_peak_per_gpu": tf / dist.world / peak,
-            "tensor_TFLOP_s": tf * 1.4,
-            "config": f"B{B}/GPU S{S} H{H} D{D} causal bf16; dQ, dK, dV (fp32) from dO and LSE"}
+    out = {"ms_per_step": ms, "TFLOP_s": tf, "frac_of_bf16_peak_per_gpu": tf / dist.world / peak,
+           "tensor_TFLOP_s": tf * 1.4,
+           "config": f"B{B}/GPU S{S} H{H} D{D} causal bf16; dQ, dK, dV (fp32) from dO and LSE"}
+    # fp32 operands (split-bf16, three MMAs per product) at head dim 64, the
+    # widest the split mode takes, beside bf16 operands on the same shape.
+    D32 = 64
+    for name, dt in (("fp32_d64", torch.float32), ("bf16_d64", torch.bfloat16)):
+        q, k, v, do = (torch.randn((B, S, H, D32), generator=g, device=dist.device).to(dt)
+                       for _ in range(4))
+        o, lse = kernels.attention_prefill(q, k, v, causal=True, out_dtype=torch.float32,
+                                           return_lse=True)
+
+        def step32():
+            kernels.attention_backward(q, k, v, o, lse, do, causal=True)
+
+        for _ in range(warmup):
+            step32()
+        torch.cuda.synchronize()
+        _native.raise_on_device_error()
+        ms32 = timed(dist, clocks, step32, steps) / steps
+        out[name] = {"ms_per_step": ms32,
+                     "TFLOP_s": dist.sum(10.0 * D32 * pairs) / (ms32 * 1e-3) / 1e12,
+                     "config": f"B{B}/GPU S{S} H{H} D{D32} causal, {str(dt)[6:]} operands"}
+        del q, k, v, do, o, lse
+    return out
 
 
 SPARSE_PATTERNS = {
