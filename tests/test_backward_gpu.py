@@ -205,3 +205,36 @@ def test_backward_fp32_rejects_wide_heads_and_mixed_dtypes(cuda):
     xb = x[..., :64].contiguous()
     with pytest.raises(ValueError, match="dout must be"):
         kernels.attention_backward(xb, xb, xb, xb, lse, xb.to(torch.bfloat16))
+
+
+def test_backward_fp32_cross_shapes_and_strided_outputs(cuda):
+    """fp32 operands with queries and keys of different lengths, GQA and
+    ALiBi, at the fp32 bar; outputs written into strided views equal the
+    contiguous ones bit for bit."""
+    import torch
+    from enilnets_b200 import kernels
+    rs = np.random.RandomState(13)
+    B, Sq, Skv, H, Hkv, D = 2, 200, 333, 4, 2, 48
+    q = rs.standard_normal((B, Sq, H, D))
+    k = rs.standard_normal((B, Skv, Hkv, D))
+    v = rs.standard_normal((B, Skv, Hkv, D))
+    do = rs.standard_normal((B, Sq, H, D))
+    slopes = ar.alibi_slopes(H)
+    ins, got = _run32(cuda, q, k, v, do, False, None, slopes)
+    qn, kn, vn, don = (_np(t) for t in ins)
+    ref = ar.attention_backward_ref(qn, kn, vn, don, causal=False, window=None, alibi=slopes)
+    for name, g, r in zip(("dq", "dk", "dv"), got, ref):
+        err = np.max(np.abs(_np(g) - r))
+        assert err <= TOL32 * max(1.0, np.abs(r).max()), (name, err)
+    qt, kt, vt, dot = ins
+    sl = torch.tensor(slopes, dtype=torch.float32, device=cuda)
+    o, lse = kernels.attention_prefill(qt, kt, vt, alibi_slopes=sl, out_dtype=torch.float32,
+                                       return_lse=True)
+    base = kernels.attention_backward(qt, kt, vt, o, lse, dot, alibi_slopes=sl)
+    wide = [torch.full((B, S, Hh, D + 3), float("nan"), device=cuda)
+            for S, Hh in ((Sq, H), (Skv, Hkv), (Skv, Hkv))]
+    views = tuple(w[..., :D] for w in wide)
+    strided = kernels.attention_backward(qt, kt, vt, o, lse, dot, alibi_slopes=sl, out=views)
+    torch.cuda.synchronize()
+    for a, b in zip(strided, base):
+        assert torch.equal(a, b)
