@@ -370,6 +370,22 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
       "r"(a[13]), "r"(a[14]), "r"(a[15])                                                     \
       : "memory")
 
+// Two 16-column loads (from two addresses) under one wait.
+#define ENL_TMEM_LD16X2(ta, a, tb, b)                                                        \
+  asm volatile(                                                                              \
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "  \
+      "%11, %12, %13, %14, %15}, [%32];\n\t"                                                  \
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16, %17, %18, %19, %20, %21, %22, %23, %24, "  \
+      "%25, %26, %27, %28, %29, %30, %31}, [%33];\n\t"                                        \
+      "tcgen05.wait::ld.sync.aligned;"                                                       \
+      : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]), "=r"(a[4]), "=r"(a[5]), "=r"(a[6]),   \
+        "=r"(a[7]), "=r"(a[8]), "=r"(a[9]), "=r"(a[10]), "=r"(a[11]), "=r"(a[12]),           \
+        "=r"(a[13]), "=r"(a[14]), "=r"(a[15]), "=r"(b[0]), "=r"(b[1]), "=r"(b[2]),           \
+        "=r"(b[3]), "=r"(b[4]), "=r"(b[5]), "=r"(b[6]), "=r"(b[7]), "=r"(b[8]), "=r"(b[9]),   \
+        "=r"(b[10]), "=r"(b[11]), "=r"(b[12]), "=r"(b[13]), "=r"(b[14]), "=r"(b[15])         \
+      : "r"(ta), "r"(tb)                                                                     \
+      : "memory")
+
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }

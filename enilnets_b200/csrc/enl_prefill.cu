@@ -580,8 +580,7 @@ __global__ void __launch_bounds__(384, 1)
         float s[64];
         {
           uint32_t sr[64];
-          ENL_TMEM_LD32(s_addr, sr, 0);
-          ENL_TMEM_LD32(s_addr + 32, sr, 32);
+          ENL_TMEM_LD32X2(s_addr, sr, s_addr + 32, (sr + 32));  // both loads under one wait
 #pragma unroll
           for (int c = 0; c < 64; ++c) s[c] = __uint_as_float(sr[c]);
         }
@@ -813,10 +812,9 @@ __global__ void __launch_bounds__(384, 1)
         for (int c = 0; c < D / 32; ++c) {  // 16-column chunks of this thread's D/2
           uint32_t o0[16], o1[16];
           __syncwarp();  // the stores below diverge by row; reconverge for tcgen05.ld
-          if (have_o) {
-            ENL_TMEM_LD16(lane_addr + Cfg::col_o(0) + c0 + c * 16, o0);
-            ENL_TMEM_LD16(lane_addr + Cfg::col_o(1) + c0 + c * 16, o1);
-          }
+          if (have_o)
+            ENL_TMEM_LD16X2(lane_addr + Cfg::col_o(0) + c0 + c * 16, o0,
+                            lane_addr + Cfg::col_o(1) + c0 + c * 16, o1);
           float v[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i)
