@@ -729,7 +729,20 @@ __device__ __forceinline__ void perf_tile_epilogue(const PerfTcParams& p, uint32
   // The row maximum (mode 0 and 1): one pass over the accumulator.
   float m = -INFINITY;
   if (kMode != 2) {
-    for (int c0 = 0; c0 < Dfn; c0 += 32) {
+    int c0 = 0;
+    // 64 columns per wait while they last (two loads in flight), four
+    // independent maxima per pass.
+    for (; c0 + 64 <= Dfn; c0 += 64) {
+      uint32_t r[64];
+      ENL_TMEM_LD32X2(addr + c0, r, addr + c0 + 32, (r + 32));
+      const int n_valid = p.Df - c0;
+      float mx[4] = {m, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int i = 0; i < 64; ++i)
+        if (i < n_valid) mx[i % 4] = fmaxf(mx[i % 4], __uint_as_float(r[i]));
+      m = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+    }
+    for (; c0 < Dfn; c0 += 32) {
       uint32_t r[32];
       if (c0 + 32 <= Dfn) {
         ENL_TMEM_LD32(addr + c0, r, 0);
