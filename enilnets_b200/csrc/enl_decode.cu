@@ -281,42 +281,76 @@ template cudaError_t launch_decode<64>(const DecodeParams&, cudaStream_t);
 template cudaError_t launch_decode<128>(const DecodeParams&, cudaStream_t);
 
 // out = sum_i e^{lse_i - lse*} o_i / sum_i e^{lse_i - lse*}; parts whose
-// lse is -inf (no visible key) carry no weight.
-__global__ void lse_merge_kernel(const float* __restrict__ part_o,
-                                 const float* __restrict__ part_lse, int n_parts,
-                                 long long stride_o, long long stride_lse, int B, int H, int D,
-                                 int d_out, void* o, long long o_sb, long long o_sh, int out_fp32,
-                                 float* lse_out) {
+// lse is -inf (no visible key) carry no weight. One block of 128 threads per
+// (batch, head), one output column per thread. The parts' weights are
+// computed once per block, 128 parts at a time, into shared memory, so each
+// thread's pass over the parts is a stream of independent loads; the sums
+// keep the parts' order (the weight total is accumulated by one thread).
+constexpr int kMergeThreads = 128;
+__global__ void __launch_bounds__(kMergeThreads)
+    lse_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
+                     int n_parts, long long stride_o, long long stride_lse, int B, int H, int D,
+                     int d_out, void* o, long long o_sb, long long o_sh, int out_fp32,
+                     float* lse_out) {
+  __shared__ float s_red[kMergeThreads / 32];
+  __shared__ float s_w[kMergeThreads], s_l[kMergeThreads];
+  __shared__ float s_W;
   const int bh = blockIdx.x;
   const int b = bh / H, h = bh % H;
-  float M = -INFINITY;
-  for (int i = 0; i < n_parts; ++i) M = fmaxf(M, part_lse[i * stride_lse + bh]);
-  float W = 0.0f;
-  if (M != -INFINITY)
-    for (int i = 0; i < n_parts; ++i) W += __expf(part_lse[i * stride_lse + bh] - M);
-  for (int d = threadIdx.x; d < d_out; d += blockDim.x) {
+  const int tid = threadIdx.x;
+  float m = -INFINITY;
+  for (int i = tid; i < n_parts; i += kMergeThreads) m = fmaxf(m, part_lse[i * stride_lse + bh]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  if (tid % 32 == 0) s_red[tid / 32] = m;
+  __syncthreads();
+  float M = s_red[0];
+#pragma unroll
+  for (int k = 1; k < kMergeThreads / 32; ++k) M = fmaxf(M, s_red[k]);
+  float W = 0.0f;  // thread 0's running total, in part order
+  for (int d0 = 0; d0 < d_out; d0 += kMergeThreads) {
+    const int d = d0 + tid;
     float acc = 0.0f;
-    if (M != -INFINITY) {
-      for (int i = 0; i < n_parts; ++i) {
-        const float li = part_lse[i * stride_lse + bh];
-        if (li != -INFINITY) acc += __expf(li - M) * part_o[i * stride_o + (long long)bh * D + d];
+    for (int c0 = 0; c0 < n_parts; c0 += kMergeThreads) {
+      const int n = min(kMergeThreads, n_parts - c0);
+      __syncthreads();  // the previous chunk's weights have been read
+      if (tid < n) {
+        const float li = part_lse[(c0 + tid) * stride_lse + bh];
+        s_l[tid] = li;
+        s_w[tid] = (M != -INFINITY) ? __expf(li - M) : 0.0f;
+      }
+      __syncthreads();
+      if (d0 == 0 && tid == 0 && M != -INFINITY)
+        for (int k = 0; k < n; ++k) W += s_w[k];
+      if (d < d_out && M != -INFINITY) {
+        const float* po = part_o + (long long)c0 * stride_o + (long long)bh * D + d;
+#pragma unroll 8
+        for (int k = 0; k < n; ++k)
+          if (s_l[k] != -INFINITY) acc = fmaf(s_w[k], po[k * stride_o], acc);
       }
     }
-    const float val = acc / W;  // NaN when nothing was visible, like the reference
-    if (out_fp32)
-      reinterpret_cast<float*>(o)[(long long)b * o_sb + (long long)h * o_sh + d] = val;
-    else
-      reinterpret_cast<__nv_bfloat16*>(o)[(long long)b * o_sb + (long long)h * o_sh + d] =
-          __float2bfloat16_rn(val);
+    if (d0 == 0) {
+      if (tid == 0) s_W = W;
+      __syncthreads();
+      W = s_W;
+    }
+    if (d < d_out) {
+      const float val = acc / W;  // NaN when nothing was visible, like the reference
+      if (out_fp32)
+        reinterpret_cast<float*>(o)[(long long)b * o_sb + (long long)h * o_sh + d] = val;
+      else
+        reinterpret_cast<__nv_bfloat16*>(o)[(long long)b * o_sb + (long long)h * o_sh + d] =
+            __float2bfloat16_rn(val);
+    }
   }
-  if (threadIdx.x == 0 && lse_out) lse_out[bh] = (M == -INFINITY) ? M : M + logf(W);
+  if (tid == 0 && lse_out) lse_out[bh] = (M == -INFINITY) ? M : M + logf(W);
 }
 
 cudaError_t launch_lse_merge(const float* part_o, const float* part_lse, int n_parts,
                              long long part_stride_o, long long part_stride_lse, int B, int H,
                              int D, int d_out, void* o, long long o_sb, long long o_sh,
                              int out_fp32, float* lse, cudaStream_t stream) {
-  lse_merge_kernel<<<B * H, 128, 0, stream>>>(part_o, part_lse, n_parts, part_stride_o,
+  lse_merge_kernel<<<B * H, kMergeThreads, 0, stream>>>(part_o, part_lse, n_parts, part_stride_o,
                                               part_stride_lse, B, H, D, d_out, o, o_sb, o_sh,
                                               out_fp32, lse);
   return cudaGetLastError();
