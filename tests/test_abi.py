@@ -119,6 +119,36 @@ def test_prefill_workspace_bytes_is_host_only_arithmetic():
     assert lib.enl_prefill_workspace_bytes(ctypes.byref(a)) == planes(100, 8) + 2 * planes(300, 2)
 
 
+def test_backward_workspace_and_validation_are_host_only():
+    """The backward's workspace is two fp32 rows per padded query, plus the
+    bf16 (hi, lo) planes of q, k, v and dout for fp32 operands; fp32 operands
+    past head dim 64 and unknown dtypes are rejected before any launch."""
+    lib = _native.load()
+    a = _native.BackwardArgs()
+    a.batch, a.num_heads, a.num_kv_heads, a.seq_q, a.seq_kv, a.head_dim = 2, 4, 2, 100, 300, 32
+    rows = (2 * 4 * 128 * 4 + 255) // 256 * 256
+    a.in_dtype = _native.ENL_DTYPE_BF16
+    assert lib.enl_backward_workspace_bytes(ctypes.byref(a)) == 2 * rows
+
+    def planes(S, H):
+        return (2 * S * H * 32 * 2 * 2 + 255) // 256 * 256
+    a.in_dtype = _native.ENL_DTYPE_FP32
+    assert lib.enl_backward_workspace_bytes(ctypes.byref(a)) == \
+        2 * rows + 2 * planes(100, 4) + 2 * planes(300, 2)
+    a.q = a.k = a.v = a.o = a.dout = a.lse = a.dq = a.dk = a.dv = 256
+    a.head_dim = 128
+    with pytest.raises(ValueError, match="head_dim <= 64"):
+        _native.check(lib.enl_attn_backward(ctypes.byref(a), None), "enl_attn_backward")
+    a.head_dim = 32
+    a.in_dtype = 7
+    with pytest.raises(ValueError, match="in_dtype=7"):
+        _native.check(lib.enl_attn_backward(ctypes.byref(a), None), "enl_attn_backward")
+    a.in_dtype = _native.ENL_DTYPE_FP32
+    a.q_stride_b, a.q_stride_s, a.q_stride_h = 100 * 4 * 32, 4 * 32, 30  # not 16-byte in fp32
+    with pytest.raises(ValueError, match="multiples of 16 bytes"):
+        _native.check(lib.enl_attn_backward(ctypes.byref(a), None), "enl_attn_backward")
+
+
 def test_linear_workspace_sizes():
     """Host-only arithmetic of enl_linear_workspace_bytes. Head dims up to 128
     take the tensor-core path: bf16 hi/lo planes of phi(Q) and phi(K)
